@@ -1,0 +1,366 @@
+#!/usr/bin/env python
+"""bench.py -- Gemma 3 4B Q4_K batch-1 decode on B200.
+
+A "step" is one decode step of the 4B model (34 layers + LM head) for one
+sequence: prompt of 512 random token ids prefilled, then greedy steps at
+positions 512..767.  Timed steps cycle through that 256-position span (every
+span restarts at position 512 and overwrites the same cache rows), so every
+timed step is a config-1 step whatever --steps is.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank decoding its own
+sequence with its own weight replica (sequences are independent: no
+collective on the data path; the barrier and max-over-ranks timing use NCCL).
+value = total tokens / max-over-ranks device time.  `--impl reference` times
+the reference's CPU decode path (its restatement in oracle/, since the Rust
+crate cannot be built here) on the host cores.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Gemma-3 4B Q4_K decode tok/s (bs=1) and Q4_K GEMV HBM GB/s vs 8 TB/s peak"
+PROMPT = 512
+SPAN = 256
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2048)
+    p.add_argument("--warmup", type=int, default=16)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--layers", type=int, default=34, help="model depth (34 = Gemma 3 4B)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-steps", type=int, default=3)
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 8:
+                    continue
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), parts[4:8]))
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def argmax_last(v):
+    import numpy as np
+    return int(np.flatnonzero(v == v.max())[-1])
+
+
+def run_reference(args):
+    """Reference arm: the CPU decode step (oracle restatement of the reference's
+    x86 path) on all host threads, on config 1's shapes."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import oracle as orc
+    from rich_triplet_b200.model import Config4, synth_gemma3, synth_normal, synth_tokens
+
+    cfg = Config4.gemma3_4b(vocab_size=262144).with_layers(args.layers)
+    w = synth_gemma3(cfg, seed=args.seed)
+    cap = PROMPT + SPAN
+    om = orc.OracleModel(cfg, w, cap, nthreads=0)
+    kvd = cfg.num_key_value_heads * cfg.head_dim
+    # Positions 0..511 of every layer's f32 cache hold N(0,1) values: prefilling
+    # 512 tokens through the CPU path would take tens of minutes, and a decode
+    # step reads the same bytes whatever the cached values are.
+    for layer in range(cfg.num_hidden_layers):
+        kc = np.ctypeslib.as_array(orc.lib.or_model_kcache(om._h, layer), shape=(cap * kvd,))
+        vc = np.ctypeslib.as_array(orc.lib.or_model_vcache(om._h, layer), shape=(cap * kvd,))
+        kc[: PROMPT * kvd] = synth_normal(args.seed, 5000 + 2 * layer, PROMPT * kvd)
+        vc[: PROMPT * kvd] = synth_normal(args.seed, 5001 + 2 * layer, PROMPT * kvd)
+    tok = int(synth_tokens(args.seed, 100, 1, cfg.vocab_size)[0])
+    n_warm = min(args.warmup, 1)
+    n_steps = max(1, min(args.steps, args.cpu_steps))
+    om.set_seq_len(PROMPT)
+    for _ in range(n_warm):
+        tok = orc.sample_greedy(om.step(tok))
+    om.set_seq_len(PROMPT)
+    t0 = time.perf_counter()
+    for _ in range(n_steps):
+        tok = orc.sample_greedy(om.step(tok))
+    dt = time.perf_counter() - t0
+    value = n_steps / dt
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": n_steps, "warmup": n_warm, "ms_per_step": dt * 1e3 / n_steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"gemma3-4b decode bs=1 (layers={cfg.num_hidden_layers}), positions 512..",
+                   "prompt": PROMPT, "kv": "f32", "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{n_steps} CPU decode steps at positions 512.. (requested {args.steps}); "
+                                   "reference is Rust (no toolchain here): oracle/ C restatement of its x86 path, "
+                                   "row-parallel over all host threads; KV rows 0..511 synthetic"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    om.close()
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.cuda.current_device()
+
+    from rich_triplet_b200.decode import CudaDecodeContext
+    from rich_triplet_b200.model import Config4, synth_gemma3, synth_tokens
+    from rich_triplet_b200.ops import Context
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    cfg = Config4.gemma3_4b(vocab_size=262144).with_layers(args.layers)
+    w = synth_gemma3(cfg, seed=args.seed)
+    ctx = Context(device)
+    cap = PROMPT + SPAN
+    dec = CudaDecodeContext(w, cap, ctx)
+    ext = torch.cuda.ExternalStream(ctx.stream_ptr)
+    prompt = synth_tokens(args.seed, 100 + rank, PROMPT, cfg.vocab_size)
+    last = dec.prefill(prompt)
+    first = argmax_last(last)
+
+    def enqueue(n):
+        done = 0
+        while done < n:
+            m = min(SPAN, n - done)
+            dec.enqueue_generate(first, PROMPT, m)
+            done += m
+
+    # ---- warm-up ----
+    enqueue(max(3, args.warmup))
+    ctx.sync()
+    barrier()
+
+    # ---- timed decode (inputs resident in HBM) ----
+    clocks = ClockSampler(device)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    enqueue(args.steps)
+    e1.record(ext)
+    e1.synchronize()
+    ctx.sync()
+    ms = e0.elapsed_time(e1)
+    barrier()
+    clock_info = clocks.stop()
+    t = torch.tensor([ms], device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1e3)
+
+    # ---- dominant kernel: the Q4_K GEMVs of one step, timed alone ----
+    reps = 20
+    dec.enqueue_q4k_gemvs()
+    ctx.sync()
+    e0.record(ext)
+    for _ in range(reps):
+        n_launch, gbytes = dec.enqueue_q4k_gemvs()
+    e1.record(ext)
+    e1.synchronize()
+    gemv_ms = e0.elapsed_time(e1) / (reps * n_launch)
+    gemv_bytes = gbytes / n_launch
+    achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
+
+    # ---- whole-step bytes (weights + KV read), for the step roofline ----
+    H, D, NKV = cfg.hidden_size, cfg.head_dim, cfg.num_key_value_heads
+    q4k_bytes = w.q4k_bytes()
+    lm_bytes = cfg.vocab_size * H * 2
+    kv_per_pos = 2 * NKV * D * 4
+    kv_avg = sum(kv_per_pos * (p + 1) * cfg.num_hidden_layers for p in range(PROMPT, PROMPT + SPAN)) / SPAN
+    step_bytes = q4k_bytes + lm_bytes + kv_avg + H * 2
+    step_gbs = step_bytes * args.steps / (ms / 1e3) / 1e9
+
+    # ---- e2e through the public API: host token in, host logits out ----
+    e2e = None
+    if True:
+        pinned = torch.empty(cfg.vocab_size, dtype=torch.float32).pin_memory()
+        buf = pinned.numpy()
+        n_e2e = min(args.steps, SPAN)
+        tok, pos = first, PROMPT
+        for _ in range(3):
+            dec.decode_step(tok, pos, out=buf)
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(n_e2e):
+            dec.decode_step(tok, PROMPT + i, out=buf)
+            tok = int(buf.argmax())
+        dt = time.perf_counter() - t0
+        tt = torch.tensor([dt], device="cuda")
+        if dist is not None:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * n_e2e / float(tt.item()), "unit": "tok/s", "h2d_bytes_per_step": 8,
+               "d2h_bytes_per_step": cfg.vocab_size * 4 + 4}
+
+    # ---- standalone Q4_K GEMV, 16 rotating copies (> L2) ----
+    gemv0 = {}
+    if rank == 0:
+        from rich_triplet_b200._lib import RT_FMT_Q4K
+        from rich_triplet_b200.model import synth_normal, synth_q4k
+        from rich_triplet_b200.ops import DeviceWeight, gemv_device
+        for rows, cols in ((10240, 2560), (2560, 10240)):
+            copies = [DeviceWeight.upload(ctx, RT_FMT_Q4K, synth_q4k(args.seed, 9000 + c, rows, cols), rows, cols)
+                      for c in range(16)]
+            x = torch.from_numpy(synth_normal(args.seed, 9100, cols)).cuda()
+            y = torch.empty(rows, dtype=torch.float32, device="cuda")
+            torch.cuda.synchronize()
+            for c in copies:
+                gemv_device(ctx, c, x.data_ptr(), y.data_ptr())
+            ctx.sync()
+            n = 256
+            e0.record(ext)
+            for i in range(n):
+                gemv_device(ctx, copies[i % 16], x.data_ptr(), y.data_ptr())
+            e1.record(ext)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / n
+            b = rows * cols // 256 * 144 + cols * 4 + rows * 4
+            gemv0[f"{rows}x{cols}"] = {"us": us, "gbs": b / (us * 1e-6) / 1e9, "frac": b / (us * 1e-6) / 1e9 / hbm_peak,
+                                       "bytes": b, "rotation": "16 weight copies, 236 MB > L2"}
+            for c in copies:
+                c.free()
+
+    # ---- CPU baseline: the oracle decode step on host cores (rank 0, N=1) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        om = orc.OracleModel(cfg, w, cap, nthreads=0)
+        kvd = NKV * D
+        for layer in range(cfg.num_hidden_layers):
+            k, v = dec.read_kv(layer, PROMPT)
+            np.ctypeslib.as_array(orc.lib.or_model_kcache(om._h, layer), shape=(cap * kvd,))[: PROMPT * kvd] = k
+            np.ctypeslib.as_array(orc.lib.or_model_vcache(om._h, layer), shape=(cap * kvd,))[: PROMPT * kvd] = v
+        om.set_seq_len(PROMPT)
+        tok = first
+        t0 = time.perf_counter()
+        for _ in range(args.cpu_steps):
+            tok = orc.sample_greedy(om.step(tok))
+        dt = time.perf_counter() - t0
+        cpu = {"value": args.cpu_steps / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{args.cpu_steps} decode steps at positions 512..{511 + args.cpu_steps} of the same model, "
+                         "KV cache copied from the GPU prefill; oracle/ restatement of the reference's x86 path"}
+        om.close()
+
+    launches = dec.launches_per_step
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"gemma3-4b Q4_K decode bs=1 (BASELINE config 1), layers={cfg.num_hidden_layers}",
+                       "prompt": PROMPT, "decode_positions": [PROMPT, PROMPT + SPAN - 1], "kv": "f32",
+                       "vocab": cfg.vocab_size, "l2": "inputs larger than L2: 3.3 GB of weights + KV per step",
+                       "parallelism": f"dp{world} (one sequence and weight replica per GPU)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None, "kernel": "gemv_kernel<Q4K> (all Q4_K GEMVs of a step)",
+                         "launch_us": gemv_ms * 1e3, "bytes_per_launch": gemv_bytes, "peak_kind": peak_kind,
+                         "step_gbs": step_gbs, "step_frac": step_gbs / hbm_peak, "step_bytes": step_bytes},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches * args.steps,
+            "clocks": clock_info,
+            "q4k_gemv_config0": gemv0,
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,214 @@
+/*
+ * rt_cuda.h -- C ABI of the B200 (sm_100a) Q4_K decode library, librtcuda.so.
+ *
+ * This is the drop-in boundary for rich-triplet's GPU decode path: every
+ * entry point below replaces one function of the reference crate's Metal
+ * surface (paths are relative to the reference crate root).  The reference's
+ * own host language is Rust; its binding (an `extern "C"` block behind a
+ * `cuda` cargo feature) needs only the plain pointers and sizes used here.
+ *
+ * Conventions
+ *  - Every function returns RT_OK (0) or a negative RT_E_* status; nothing
+ *    aborts the process.  rt_last_error() gives a one-line reason.
+ *  - The caller owns host buffers; the library owns device buffers (rt_w,
+ *    rt_dec).  A context owns one CUDA stream; every call on it is ordered on
+ *    that stream.  A context is not thread-safe: use one per thread or GPU.
+ *  - Weight matrices are [rows = out_features, cols = in_features], row-major,
+ *    exactly as Q4KMat / MatBf16 hold them (src/autograd2.rs:1036-1042, 688-692).
+ *  - flags: RT_HOST means x / y (or the source blob) are host pointers and the
+ *    call returns when the result is in host memory; RT_DEVICE means they are
+ *    device pointers and the call only enqueues work on rt_stream(ctx).
+ */
+#ifndef RT_CUDA_H
+#define RT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------- */
+#define RT_OK 0
+#define RT_E_INVAL (-1)   /* bad argument (null pointer, unknown flag)      */
+#define RT_E_CUDA (-2)    /* a CUDA runtime call failed                      */
+#define RT_E_NOMEM (-3)   /* device or host allocation failed                */
+#define RT_E_SHAPE (-4)   /* dimension mismatch or unsupported size          */
+#define RT_E_FORMAT (-5)  /* weight format not accepted here                 */
+#define RT_E_IO (-6)      /* file could not be read / is malformed           */
+#define RT_E_STATE (-7)   /* call out of order (e.g. context full)           */
+#define RT_E_TIMEOUT (-8) /* a bounded device-side wait gave up              */
+
+/* ---- weight formats (values are GGUF tensor type ids, src/gguf_loader.rs:40-61;
+ *      BF16 is GGUF type 30) ------------------------------------------- */
+#define RT_FMT_F32 0
+#define RT_FMT_Q4_0 2
+#define RT_FMT_Q4K 12
+#define RT_FMT_Q6K 14
+#define RT_FMT_BF16 30
+
+/* ---- pointer location flags ----------------------------------------- */
+#define RT_HOST 0
+#define RT_DEVICE 1
+
+typedef struct rt_ctx rt_ctx; /* device + stream + last error          */
+typedef struct rt_w rt_w;     /* a weight matrix resident in HBM        */
+typedef struct rt_dec rt_dec; /* a Gemma 3 decode engine                */
+
+/* ---- context ---------------------------------------------------------- */
+
+/* Open `device` and create the context's stream.
+ * Replaces the thread-local METAL_CTX set-up (src/metal_ops.rs:404-428). */
+int rt_init(int device, rt_ctx** out);
+void rt_destroy(rt_ctx* ctx);
+/* Last error message of `ctx` ("" when none); never NULL. */
+const char* rt_last_error(const rt_ctx* ctx);
+const char* rt_version(void);
+/* The cudaStream_t every call on ctx is ordered on (as void*). */
+void* rt_stream(rt_ctx* ctx);
+int rt_sync(rt_ctx* ctx);
+
+/* ---- weights ---------------------------------------------------------- */
+
+/* Copy a weight matrix to HBM in `fmt` (RT_FMT_Q4K: rows*cols/256*144 bytes;
+ * RT_FMT_BF16: rows*cols*2; RT_FMT_F32: rows*cols*4).  Q4_K needs cols % 256 == 0,
+ * BF16 needs cols % 8 == 0.
+ * Replaces the weight upload + cache of metal_gemv_q4k_t / metal_gemv_bf16_t
+ * (src/metal_ops.rs:811-815, 899-903) and MetalDecodeContext::new's uploads
+ * (src/metal_decode.rs:1002-1121). */
+int rt_weight_upload(rt_ctx* ctx, int fmt, const void* host, uint64_t bytes, int64_t rows, int64_t cols,
+                     rt_w** out);
+/* Copy a weight's device bytes back (for bit-exact checks of conversions). */
+int rt_weight_download(rt_ctx* ctx, const rt_w* w, void* host, uint64_t bytes);
+int rt_weight_info(const rt_w* w, int* fmt, int64_t* rows, int64_t* cols, uint64_t* bytes);
+const void* rt_weight_device_ptr(const rt_w* w);
+void rt_weight_free(rt_ctx* ctx, rt_w* w);
+
+/* ---- GEMV ------------------------------------------------------------- */
+
+/* y[rows] = dequant(W[rows, cols]) . x[cols], f32 accumulation.
+ * Replaces metal_gemv_q4k_t (src/metal_ops.rs:799-860) and the CPU
+ * Q4KMat::gemv_mt it mirrors (src/autograd2.rs:1953-2035). */
+int rt_gemv_q4k(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags);
+/* y[rows] = bf16(W[rows, cols]) . x[cols], f32 accumulation.
+ * Replaces metal_gemv_bf16_t (src/metal_ops.rs:887-960) / MatBf16::gemv_mt
+ * (src/autograd2.rs:954-1000). */
+int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags);
+
+/* ---- load-time conversions (bit-exact with the reference CPU code) ---- */
+
+/* GGUF Q4_0 bytes of a [rows, cols] tensor -> Q4_K weight in HBM, as
+ * decode_q4_0_to_q4mat + Q4KMat::from_q4mat do on the CPU
+ * (src/gguf_loader.rs:282-350, src/autograd2.rs:1291-1320, 1171-1246).
+ * flags: RT_HOST or RT_DEVICE for `q4_0`. */
+int rt_convert_q4_0_to_q4k(rt_ctx* ctx, const void* q4_0, int64_t rows, int64_t cols, int flags, rt_w** out);
+/* GGUF Q6_K bytes -> BF16 weight in HBM, as decode_q6k_to_f32 +
+ * f32s_to_bf16_and_drop do (src/gguf_loader.rs:482-533, src/transformer4.rs:1084-1097). */
+int rt_convert_q6k_to_bf16(rt_ctx* ctx, const void* q6k, int64_t rows, int64_t cols, int flags, rt_w** out);
+
+/* ---- Gemma 3 decode engine -------------------------------------------- */
+
+/* Config4 (src/transformer4.rs:51-80).  Layer i is global iff i % 6 == 5
+ * (Config4::is_global_layer, :141-143). */
+typedef struct {
+    int32_t vocab_size;          /* rows of the tied embedding / LM head */
+    int32_t hidden_size;
+    int32_t num_hidden_layers;
+    int32_t num_attention_heads;
+    int32_t num_key_value_heads;
+    int32_t head_dim;
+    int32_t intermediate_size;
+    int32_t sliding_window;      /* 0 = no window on local layers */
+    float rope_theta_local;
+    float rope_theta_global;
+    float rope_freq_scale_local;
+    float rope_freq_scale_global;
+    float rms_norm_eps;
+    float query_pre_attn_scalar;
+} rt_gemma3_cfg;
+
+/* One Gemma3Block's weights (src/transformer4.rs:146-170, 290-300, 1936-1950).
+ * Projections are rt_w handles already in HBM (Q4_K); the decoder copies them
+ * into its own fused layout, so the handles may be freed afterwards.  Norm
+ * weights are host f32 arrays holding gamma as the kernels apply it,
+ * out = x_hat * (1 + gamma) (the value GGUF stores minus one, as the loader
+ * keeps it: src/transformer4.rs:870-968). */
+typedef struct {
+    const rt_w *q, *k, *v, *o, *gate, *up, *down;
+    const float *attn_norm, *post_attn_norm, *pre_ffn_norm, *post_ffn_norm; /* [hidden]   */
+    const float *q_norm, *k_norm;                                            /* [head_dim] */
+} rt_gemma3_layer;
+
+/* Build the decode engine: upload norms, fuse QKV and gate/up, allocate an f32
+ * KV cache of max_ctx positions and capture one decode step as a CUDA graph.
+ * `embed` is the BF16 [vocab, hidden] embedding, tied with the LM head.
+ * Replaces MetalDecodeContext::new (src/metal_decode.rs:971-1254). */
+int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_layer* layers, const rt_w* embed,
+                      const float* final_norm, int32_t max_ctx, rt_dec** out);
+void rt_decoder_destroy(rt_dec* dec);
+
+/* Load seq_len rows of one layer's K and V cache, host f32 in the CPU cache's
+ * layout [seq_len, n_kv_heads * head_dim] (Gemma3LayerKvCache,
+ * src/transformer4.rs:1794-1810).  Replaces sync_kv_from_cpu
+ * (src/metal_decode.rs:1366-1396), without the f16 narrowing. */
+int rt_decoder_load_kv(rt_dec* dec, int32_t layer, const float* k, const float* v, int32_t seq_len);
+/* Read seq_len rows of one layer's K and V cache back, same layout. */
+int rt_decoder_read_kv(rt_dec* dec, int32_t layer, float* k, float* v, int32_t seq_len);
+
+/* One token: embed `token` at absolute `position`, run every layer, append its
+ * K/V at `position`, and write vocab_size f32 logits to host `logits`.
+ * Replaces MetalDecodeContext::decode_step (src/metal_decode.rs:2028-2074). */
+int rt_decoder_step(rt_dec* dec, int32_t token, int32_t position, float* logits);
+
+/* Run `n` prompt tokens through the engine one position at a time starting at
+ * start_pos, filling the KV cache, and write the last token's logits (may be
+ * NULL).  Replaces the CPU prefill + sync_kv_from_cpu hand-off
+ * (src/transformer4.rs:2103-2164, 2190-2212). */
+int rt_decoder_prefill(rt_dec* dec, const int32_t* tokens, int32_t n, int32_t start_pos, float* last_logits);
+
+/* Greedy decode entirely on the device: step i feeds the argmax of step i-1
+ * (largest logit, ties to the higher index) back as its token.  Starts from
+ * `first_token` at `start_pos`.  tokens_out (host, may be NULL) receives the n
+ * argmax tokens.  With flags == RT_DEVICE the n graph launches are only
+ * enqueued on rt_stream() (tokens_out must be NULL); with RT_HOST the call
+ * waits.  The decode loop of generate_cached_streaming
+ * (src/transformer4.rs:2245-2439) with sample_token at temperature 0. */
+int rt_decoder_generate(rt_dec* dec, int32_t first_token, int32_t start_pos, int32_t n, int32_t* tokens_out,
+                        int flags);
+
+/* Enqueue, on rt_stream(), only the Q4_K GEMV launches of one decode step with
+ * the step's own shapes, layouts and inputs (one per projection group and
+ * layer), for timing the dominant kernel alone.  *n_launches and *bytes
+ * receive the launch count and the algorithmic bytes they move. */
+int rt_decoder_enqueue_q4k_gemvs(rt_dec* dec, int32_t* n_launches, uint64_t* bytes);
+
+/* Device bytes held by the engine (weights + KV cache + activations).
+ * Replaces print_metal_memory (src/metal_decode.rs:1285-1354). */
+int rt_decoder_memory(const rt_dec* dec, uint64_t* bytes);
+/* The engine's kernel launches per decode step. */
+int rt_decoder_launches_per_step(const rt_dec* dec, int32_t* n);
+/* Copy an internal activation vector of the last step to host (debugging and
+ * tests): which = 0 residual stream after the last layer, 1 logits.
+ * `count` is the number of f32 values to copy. */
+int rt_decoder_read_activation(rt_dec* dec, int32_t which, float* host, int64_t count);
+
+/* ---- synthetic inputs ---------------------------------------------------
+ * Deterministic, counter-based (SplitMix64) generators for benchmarks and
+ * tests; the same (seed, stream) always gives the same bytes, independent of
+ * thread count.  Host-side, no GPU needed. */
+
+/* Q4_K blocks: per block d = f16(U[1e-3,1e-2]), dmin = f16(U[0,5e-3]) (f16 by
+ * Q4KMat::f32_to_f16), 8 scales + 8 mins U{0..63} packed by pack_scales, 128
+ * quant bytes U{0..255}.  out: rows*cols/256*144 bytes. */
+void rt_synth_q4k(uint64_t seed, uint64_t stream, int64_t rows, int64_t cols, uint8_t* out);
+void rt_synth_normal_f32(uint64_t seed, uint64_t stream, int64_t n, float mean, float stddev, float* out);
+/* Normal values rounded to BF16 (round to nearest even). */
+void rt_synth_normal_bf16(uint64_t seed, uint64_t stream, int64_t n, float mean, float stddev, uint16_t* out);
+void rt_synth_tokens(uint64_t seed, uint64_t stream, int64_t n, int32_t vocab, int32_t* out);
+void rt_synth_bytes(uint64_t seed, uint64_t stream, int64_t n, uint8_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RT_CUDA_H */

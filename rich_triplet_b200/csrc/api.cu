@@ -1,0 +1,331 @@
+// api.cu -- C ABI (include/rt_cuda.h): context, weights, GEMV, conversions.
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "convert.cuh"
+#include "gemv.cuh"
+#include "rt_internal.h"
+
+namespace rt {
+
+int fail(rt_ctx* ctx, int code, const char* fmt, ...) {
+    if (ctx) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        ctx->err = buf;
+    }
+    return code;
+}
+
+static std::atomic<long> g_alloc_count{0};
+
+int dev_alloc(rt_ctx* ctx, void** p, size_t bytes, const char* what) {
+    *p = nullptr;
+    const long n = ++g_alloc_count;
+    const char* inj = getenv("RT_FAULT_INJECT_ALLOC");
+    if (inj && atol(inj) == n) return fail(ctx, RT_E_NOMEM, "injected allocation failure (%s, %zu bytes)", what, bytes);
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *p = nullptr;
+        return fail(ctx, e == cudaErrorMemoryAllocation ? RT_E_NOMEM : RT_E_CUDA, "cudaMalloc(%s, %zu bytes): %s", what,
+                    bytes, cudaGetErrorString(e));
+    }
+    return RT_OK;
+}
+
+uint64_t weight_bytes(int fmt, int64_t rows, int64_t cols) {
+    if (rows <= 0 || cols <= 0) return 0;
+    switch (fmt) {
+        case RT_FMT_Q4K: return cols % 256 ? 0 : static_cast<uint64_t>(rows) * (cols / 256) * 144;
+        case RT_FMT_BF16: return static_cast<uint64_t>(rows) * cols * 2;
+        case RT_FMT_F32: return static_cast<uint64_t>(rows) * cols * 4;
+        case RT_FMT_Q4_0: return cols % 32 ? 0 : static_cast<uint64_t>(rows) * (cols / 32) * 18;
+        case RT_FMT_Q6K: return cols % 256 ? 0 : static_cast<uint64_t>(rows) * (cols / 256) * 210;
+        default: return 0;
+    }
+}
+
+}  // namespace rt
+
+using rt::fail;
+
+extern "C" {
+
+const char* rt_version(void) { return "rich-triplet-b200 0.1 (sm_100a)"; }
+
+int rt_init(int device, rt_ctx** out) {
+    if (!out) return RT_E_INVAL;
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return RT_E_CUDA;
+    }
+    if (device < 0 || device >= n) return RT_E_INVAL;
+    rt_ctx* ctx = new rt_ctx();
+    ctx->device = device;
+    if (cudaSetDevice(device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        delete ctx;
+        return RT_E_CUDA;
+    }
+    if (rt::dev_alloc(ctx, reinterpret_cast<void**>(&ctx->d_err), sizeof(int) * 4, "error word") != RT_OK) {
+        cudaStreamDestroy(ctx->stream);
+        delete ctx;
+        return RT_E_NOMEM;
+    }
+    cudaMemset(ctx->d_err, 0, sizeof(int) * 4);
+    *out = ctx;
+    return RT_OK;
+}
+
+void rt_destroy(rt_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->scratch);
+    cudaFree(ctx->d_err);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+const char* rt_last_error(const rt_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+void* rt_stream(rt_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int rt_sync(rt_ctx* ctx) {
+    if (!ctx) return RT_E_INVAL;
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    int herr = 0;
+    RT_CHECK_CUDA(ctx, cudaMemcpy(&herr, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) {
+        cudaMemset(ctx->d_err, 0, sizeof(int));
+        return fail(ctx, RT_E_TIMEOUT, "a kernel reported error word %d (bounded wait gave up)", herr);
+    }
+    return RT_OK;
+}
+
+int rt_weight_upload(rt_ctx* ctx, int fmt, const void* host, uint64_t bytes, int64_t rows, int64_t cols, rt_w** out) {
+    if (!ctx || !host || !out) return fail(ctx, RT_E_INVAL, "rt_weight_upload: null argument");
+    *out = nullptr;
+    if (fmt != RT_FMT_Q4K && fmt != RT_FMT_BF16 && fmt != RT_FMT_F32)
+        return fail(ctx, RT_E_FORMAT, "rt_weight_upload: format %d is not a resident weight format", fmt);
+    const uint64_t need = rt::weight_bytes(fmt, rows, cols);
+    if (need == 0) return fail(ctx, RT_E_SHAPE, "rt_weight_upload: invalid shape [%lld, %lld] for format %d",
+                               static_cast<long long>(rows), static_cast<long long>(cols), fmt);
+    if (fmt == RT_FMT_BF16 && cols % 8) return fail(ctx, RT_E_SHAPE, "rt_weight_upload: BF16 needs cols %% 8 == 0");
+    if (bytes != need)
+        return fail(ctx, RT_E_SHAPE, "rt_weight_upload: %llu bytes given, [%lld, %lld] needs %llu",
+                    static_cast<unsigned long long>(bytes), static_cast<long long>(rows), static_cast<long long>(cols),
+                    static_cast<unsigned long long>(need));
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    rt_w* w = new rt_w();
+    w->fmt = fmt;
+    w->rows = rows;
+    w->cols = cols;
+    w->bytes = bytes;
+    int rc = rt::dev_alloc(ctx, &w->d, bytes, "weight");
+    if (rc != RT_OK) {
+        delete w;
+        return rc;
+    }
+    cudaError_t e = cudaMemcpyAsync(w->d, host, bytes, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        cudaFree(w->d);
+        delete w;
+        return fail(ctx, RT_E_CUDA, "rt_weight_upload: %s", cudaGetErrorString(e));
+    }
+    *out = w;
+    return RT_OK;
+}
+
+int rt_weight_download(rt_ctx* ctx, const rt_w* w, void* host, uint64_t bytes) {
+    if (!ctx || !w || !host) return fail(ctx, RT_E_INVAL, "rt_weight_download: null argument");
+    if (bytes != w->bytes) return fail(ctx, RT_E_SHAPE, "rt_weight_download: weight holds %llu bytes",
+                                       static_cast<unsigned long long>(w->bytes));
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(host, w->d, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return RT_OK;
+}
+
+int rt_weight_info(const rt_w* w, int* fmt, int64_t* rows, int64_t* cols, uint64_t* bytes) {
+    if (!w) return RT_E_INVAL;
+    if (fmt) *fmt = w->fmt;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (bytes) *bytes = w->bytes;
+    return RT_OK;
+}
+
+const void* rt_weight_device_ptr(const rt_w* w) { return w ? w->d : nullptr; }
+
+void rt_weight_free(rt_ctx* ctx, rt_w* w) {
+    if (!w) return;
+    if (ctx) {
+        cudaSetDevice(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    cudaFree(w->d);
+    delete w;
+}
+
+}  // extern "C"
+
+namespace {
+
+int ensure_scratch(rt_ctx* ctx, size_t floats) {
+    if (ctx->scratch_floats >= floats) return RT_OK;
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_floats = 0;
+    int rc = rt::dev_alloc(ctx, reinterpret_cast<void**>(&ctx->scratch), floats * sizeof(float), "gemv scratch");
+    if (rc != RT_OK) return rc;
+    ctx->scratch_floats = floats;
+    return RT_OK;
+}
+
+int gemv_common(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags, int kind) {
+    if (!ctx || !w || !x || !y) return fail(ctx, RT_E_INVAL, "gemv: null argument");
+    if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "gemv: flags must be RT_HOST or RT_DEVICE");
+    const int want = kind == rt::kQ4K ? RT_FMT_Q4K : RT_FMT_BF16;
+    if (w->fmt != want) return fail(ctx, RT_E_FORMAT, "gemv: weight format %d, this entry point takes %d", w->fmt, want);
+    if (w->cols > (1 << 20)) return fail(ctx, RT_E_SHAPE, "gemv: cols %lld too large", static_cast<long long>(w->cols));
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const int K = static_cast<int>(w->cols);
+    const rt::GemvPlan p = rt::gemv_plan(kind, w->rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 2);
+    if (p.warps == 0) return fail(ctx, RT_E_SHAPE, "gemv: no launch geometry for cols %d", K);
+    const float* dx = x;
+    float* dy = y;
+    if (flags == RT_HOST) {
+        int rc = ensure_scratch(ctx, static_cast<size_t>(K) + static_cast<size_t>(w->rows));
+        if (rc != RT_OK) return rc;
+        dx = ctx->scratch;
+        dy = ctx->scratch + K;
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(const_cast<float*>(dx), x, sizeof(float) * K, cudaMemcpyHostToDevice, ctx->stream));
+    }
+    rt::GemvArgs a = {};
+    a.w = static_cast<const uint8_t*>(w->d);
+    a.rows = w->rows;
+    a.K = K;
+    a.x = dx;
+    a.y = dy;
+    a.err = ctx->d_err;
+    RT_CHECK_CUDA(ctx, rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, p, ctx->stream, false));
+    if (flags == RT_HOST) {
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(y, dy, sizeof(float) * w->rows, cudaMemcpyDeviceToHost, ctx->stream));
+        return rt_sync(ctx);
+    }
+    return RT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rt_gemv_q4k(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags) {
+    return gemv_common(ctx, w, x, y, flags, rt::kQ4K);
+}
+
+int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags) {
+    return gemv_common(ctx, w, x, y, flags, rt::kBF16);
+}
+
+int rt_convert_q4_0_to_q4k(rt_ctx* ctx, const void* q4_0, int64_t rows, int64_t cols, int flags, rt_w** out) {
+    if (!ctx || !q4_0 || !out) return fail(ctx, RT_E_INVAL, "rt_convert_q4_0_to_q4k: null argument");
+    *out = nullptr;
+    if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "rt_convert_q4_0_to_q4k: bad flags");
+    if (rows <= 0 || cols <= 0 || cols % 256)
+        return fail(ctx, RT_E_SHAPE, "rt_convert_q4_0_to_q4k: cols must be a positive multiple of 256");
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const uint64_t in_bytes = rt::weight_bytes(RT_FMT_Q4_0, rows, cols);
+    const uint64_t out_bytes = rt::weight_bytes(RT_FMT_Q4K, rows, cols);
+    const uint8_t* src = static_cast<const uint8_t*>(q4_0);
+    void* staged = nullptr;
+    if (flags == RT_HOST) {
+        int rc = rt::dev_alloc(ctx, &staged, in_bytes, "q4_0 staging");
+        if (rc != RT_OK) return rc;
+        cudaError_t e = cudaMemcpyAsync(staged, q4_0, in_bytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) {
+            cudaFree(staged);
+            return fail(ctx, RT_E_CUDA, "rt_convert_q4_0_to_q4k: %s", cudaGetErrorString(e));
+        }
+        src = static_cast<const uint8_t*>(staged);
+    }
+    rt_w* w = new rt_w();
+    w->fmt = RT_FMT_Q4K;
+    w->rows = rows;
+    w->cols = cols;
+    w->bytes = out_bytes;
+    int rc = rt::dev_alloc(ctx, &w->d, out_bytes, "q4_k weight");
+    if (rc == RT_OK) {
+        cudaError_t e = rt::q4_0_to_q4k_launch(src, rows * (cols / 256), static_cast<uint8_t*>(w->d), ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) rc = fail(ctx, RT_E_CUDA, "rt_convert_q4_0_to_q4k: %s", cudaGetErrorString(e));
+    }
+    cudaFree(staged);
+    if (rc != RT_OK) {
+        cudaFree(w->d);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return RT_OK;
+}
+
+int rt_convert_q6k_to_bf16(rt_ctx* ctx, const void* q6k, int64_t rows, int64_t cols, int flags, rt_w** out) {
+    if (!ctx || !q6k || !out) return fail(ctx, RT_E_INVAL, "rt_convert_q6k_to_bf16: null argument");
+    *out = nullptr;
+    if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "rt_convert_q6k_to_bf16: bad flags");
+    if (rows <= 0 || cols <= 0 || cols % 256)
+        return fail(ctx, RT_E_SHAPE, "rt_convert_q6k_to_bf16: cols must be a positive multiple of 256");
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const uint64_t in_bytes = rt::weight_bytes(RT_FMT_Q6K, rows, cols);
+    const uint64_t out_bytes = rt::weight_bytes(RT_FMT_BF16, rows, cols);
+    const uint8_t* src = static_cast<const uint8_t*>(q6k);
+    void* staged = nullptr;
+    if (flags == RT_HOST) {
+        int rc = rt::dev_alloc(ctx, &staged, in_bytes, "q6_k staging");
+        if (rc != RT_OK) return rc;
+        cudaError_t e = cudaMemcpyAsync(staged, q6k, in_bytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) {
+            cudaFree(staged);
+            return fail(ctx, RT_E_CUDA, "rt_convert_q6k_to_bf16: %s", cudaGetErrorString(e));
+        }
+        src = static_cast<const uint8_t*>(staged);
+    }
+    rt_w* w = new rt_w();
+    w->fmt = RT_FMT_BF16;
+    w->rows = rows;
+    w->cols = cols;
+    w->bytes = out_bytes;
+    int rc = rt::dev_alloc(ctx, &w->d, out_bytes, "bf16 weight");
+    if (rc == RT_OK) {
+        cudaError_t e = rt::q6k_to_bf16_launch(src, rows * cols, static_cast<uint16_t*>(w->d), ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) rc = fail(ctx, RT_E_CUDA, "rt_convert_q6k_to_bf16: %s", cudaGetErrorString(e));
+    }
+    cudaFree(staged);
+    if (rc != RT_OK) {
+        cudaFree(w->d);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return RT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,41 @@
+// attention.cuh -- single-token GQA attention for the Gemma 3 decode step.
+#pragma once
+
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+namespace rt {
+
+struct AttnArgs {
+    const float* qkv;       // raw projections of this token: [nq*D | nkv*D | nkv*D]
+    const float* q_norm;    // [D]  gamma of the per-head q norm
+    const float* k_norm;    // [D]
+    float* kcache;          // this layer's K cache, [nkv][cap][D] f32
+    float* vcache;          // this layer's V cache
+    const float* rope_cos;  // [cap][D/2] cos for this layer's theta / scale
+    const float* rope_sin;  // [cap][D/2]
+    const int32_t* pos;     // absolute position of the token (device scalar)
+    int32_t cap;            // cache positions
+    int32_t nq, nkv, D;
+    int32_t window;         // sliding window (0 = attend to every cached position)
+    int32_t nsplit;         // context splits per KV head (gridDim.x)
+    float scale;            // 1 / sqrt(query_pre_attn_scalar)
+    float eps;              // RMSNorm epsilon
+    float* part;            // [nkv][nsplit][G][D + 2] per-split (m, l, unnormalised out)
+    uint32_t* counter;      // [nkv], zero before the launch; the combining CTA resets it
+    float* out;             // [nq*D]
+    int* err;
+};
+
+constexpr int kAttnTile = 32;     // cached positions per shared-memory tile
+constexpr int kAttnThreads = 256;
+
+size_t attention_smem_bytes(int D, int G);
+// Set kernel attributes; call once per device before the first launch / capture.
+cudaError_t attention_prepare();
+cudaError_t attention_launch(const AttnArgs& a, cudaStream_t s, bool pdl);
+// Algorithmic bytes at context length L (positions attended) for one layer.
+uint64_t attention_algorithmic_bytes(int nq, int nkv, int D, int64_t L);
+
+}  // namespace rt

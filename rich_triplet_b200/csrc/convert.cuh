@@ -1,0 +1,16 @@
+// convert.cuh -- load-time weight conversion kernels (bit-exact with the
+// reference CPU code; see convert.cu).
+#pragma once
+
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+namespace rt {
+
+// GGUF Q4_0 bytes (18 per 32 elements) -> Q4_K blocks (144 per 256 elements).
+cudaError_t q4_0_to_q4k_launch(const uint8_t* q40, int64_t n_q4k_blocks, uint8_t* out, cudaStream_t s);
+// GGUF Q6_K bytes (210 per 256 elements) -> BF16.
+cudaError_t q6k_to_bf16_launch(const uint8_t* q6, int64_t n_elem, uint16_t* out, cudaStream_t s);
+
+}  // namespace rt
