@@ -435,9 +435,16 @@ GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int ep
     smem = (smem + 127) & ~size_t(127);
     smem += static_cast<size_t>(best.nbuf) * best.stage_bytes;
     best.smem = smem;
+    // Raise the dynamic shared-memory limit of every instantiation here, outside
+    // any stream capture (a plan made for one prologue also serves the others).
+    for (int kd : {kQ4K, kBF16})
+        for (int pr : {kProPlain, kProResidNorm, kProEmbedNorm})
+            for (int ep : {kEpiPlain, kEpiGeluPair, kEpiArgmax})
+                dispatch(kd, pr, ep, [&](auto k) {
+                    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+                });
     int occ = 1;
     dispatch(kind, prologue, epilogue, [&](auto k) {
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, best.warps * 32, smem) != cudaSuccess) occ = 1;
     });
     cudaGetLastError();
