@@ -87,6 +87,7 @@ int rt_init(int device, rt_ctx** out) {
         return RT_E_NOMEM;
     }
     cudaMemset(ctx->d_err, 0, sizeof(int) * 4);
+    rt::gemv_prepare();
     *out = ctx;
     return RT_OK;
 }
@@ -198,7 +199,8 @@ int ensure_scratch(rt_ctx* ctx, size_t floats) {
     return RT_OK;
 }
 
-int gemv_common(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags, int kind) {
+int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags, int kind) {
+    rt_w* w = const_cast<rt_w*>(wc);  // caches its launch plan and TMA descriptor
     if (!ctx || !w || !x || !y) return fail(ctx, RT_E_INVAL, "gemv: null argument");
     if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "gemv: flags must be RT_HOST or RT_DEVICE");
     const int want = kind == rt::kQ4K ? RT_FMT_Q4K : RT_FMT_BF16;
@@ -206,10 +208,18 @@ int gemv_common(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags,
     if (w->cols > (1 << 20)) return fail(ctx, RT_E_SHAPE, "gemv: cols %lld too large", static_cast<long long>(w->cols));
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
     const int K = static_cast<int>(w->cols);
-    const rt::GemvPlan p = rt::gemv_plan(kind, w->rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 2);
-    if (p.warps == 0) return fail(ctx, RT_E_SHAPE, "gemv: no launch geometry for cols %d", K);
+    if (!w->gemv_ready) {
+        w->plan = rt::gemv_plan(kind, w->rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 2);
+        if (w->plan.warps == 0) return fail(ctx, RT_E_SHAPE, "gemv: no launch geometry for cols %d", K);
+        if (!rt::gemv_make_tmap(kind, w->d, w->rows, K, w->plan, &w->tmap))
+            return fail(ctx, RT_E_CUDA, "gemv: TMA descriptor rejected for [%lld, %d]", static_cast<long long>(w->rows), K);
+        w->gemv_ready = true;
+    }
+    const rt::GemvPlan& p = w->plan;
     const float* dx = x;
     float* dy = y;
+    if (flags == RT_DEVICE && (reinterpret_cast<uintptr_t>(x) & 15))
+        return fail(ctx, RT_E_INVAL, "gemv: device x must be 16-byte aligned");
     if (flags == RT_HOST) {
         int rc = ensure_scratch(ctx, static_cast<size_t>(K) + static_cast<size_t>(w->rows));
         if (rc != RT_OK) return rc;
@@ -224,7 +234,7 @@ int gemv_common(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags,
     a.x = dx;
     a.y = dy;
     a.err = ctx->d_err;
-    RT_CHECK_CUDA(ctx, rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, p, ctx->stream, false));
+    RT_CHECK_CUDA(ctx, rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, w->tmap, p, ctx->stream, false));
     if (flags == RT_HOST) {
         RT_CHECK_CUDA(ctx, cudaMemcpyAsync(y, dy, sizeof(float) * w->rows, cudaMemcpyDeviceToHost, ctx->stream));
         return rt_sync(ctx);

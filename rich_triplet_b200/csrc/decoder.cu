@@ -65,6 +65,8 @@ struct rt_dec {
     int* h_err = nullptr;          // pinned copy of the context's error word
     // launch geometry
     rt::GemvPlan p_qkv, p_o, p_gu, p_down, p_lm;
+    std::vector<CUtensorMap> t_qkv, t_o, t_gu, t_down;  // TMA descriptors of the weights
+    CUtensorMap t_lm;
     int nsplit = 0;
     int final_resid = 0;
     int launches = 0;
@@ -137,7 +139,7 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
                 a.g_post = norm_ptr(d, l - 1, 3);
                 p = 1 - p;
             }
-            e = rt::gemv_launch(rt::kQ4K, pro, rt::kEpiPlain, a, d->p_qkv, s, pdl);
+            e = rt::gemv_launch(rt::kQ4K, pro, rt::kEpiPlain, a, d->t_qkv[l], d->p_qkv, s, pdl);
             if (e != cudaSuccess) return e;
             ++n;
             b += rt::gemv_algorithmic_bytes(rt::kQ4K, d->qkv_rows, H, pro, rt::kEpiPlain);
@@ -180,7 +182,7 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
             a.x = d->attn;
             a.y = d->o_out;
             a.err = d->ctx->d_err;
-            e = rt::gemv_launch(rt::kQ4K, rt::kProPlain, rt::kEpiPlain, a, d->p_o, s, pdl);
+            e = rt::gemv_launch(rt::kQ4K, rt::kProPlain, rt::kEpiPlain, a, d->t_o[l], d->p_o, s, pdl);
             if (e != cudaSuccess) return e;
             ++n;
             b += rt::gemv_algorithmic_bytes(rt::kQ4K, H, d->NQ * D, rt::kProPlain, rt::kEpiPlain);
@@ -200,7 +202,7 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
             a.y = d->hbuf;
             a.err = d->ctx->d_err;
             p = 1 - p;
-            e = rt::gemv_launch(rt::kQ4K, rt::kProResidNorm, rt::kEpiGeluPair, a, d->p_gu, s, pdl);
+            e = rt::gemv_launch(rt::kQ4K, rt::kProResidNorm, rt::kEpiGeluPair, a, d->t_gu[l], d->p_gu, s, pdl);
             if (e != cudaSuccess) return e;
             ++n;
             b += rt::gemv_algorithmic_bytes(rt::kQ4K, 2LL * d->F, H, rt::kProResidNorm, rt::kEpiGeluPair);
@@ -214,7 +216,7 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
             a.x = d->hbuf;
             a.y = d->down;
             a.err = d->ctx->d_err;
-            e = rt::gemv_launch(rt::kQ4K, rt::kProPlain, rt::kEpiPlain, a, d->p_down, s, pdl);
+            e = rt::gemv_launch(rt::kQ4K, rt::kProPlain, rt::kEpiPlain, a, d->t_down[l], d->p_down, s, pdl);
             if (e != cudaSuccess) return e;
             ++n;
             b += rt::gemv_algorithmic_bytes(rt::kQ4K, H, d->F, rt::kProPlain, rt::kEpiPlain);
@@ -240,7 +242,7 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
         a.token_hist = d->ctl + 2;
         a.err = d->ctx->d_err;
         d->final_resid = 1 - p;
-        e = rt::gemv_launch(rt::kBF16, rt::kProResidNorm, rt::kEpiArgmax, a, d->p_lm, s, pdl);
+        e = rt::gemv_launch(rt::kBF16, rt::kProResidNorm, rt::kEpiArgmax, a, d->t_lm, d->p_lm, s, pdl);
         if (e != cudaSuccess) return e;
         ++n;
     }
@@ -426,6 +428,7 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
             return bail(fail(ctx, RT_E_CUDA, "upload rope tables"));
     }
     // --- plans ---
+    rt::gemv_prepare();
     d->p_qkv = rt::gemv_plan(rt::kQ4K, d->qkv_rows, H, 1, rt::kProResidNorm, rt::kEpiPlain, ctx->num_sms, 2);
     d->p_o = rt::gemv_plan(rt::kQ4K, H, d->NQ * D, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 2);
     d->p_gu = rt::gemv_plan(rt::kQ4K, 2LL * d->F, H, 2, rt::kProResidNorm, rt::kEpiGeluPair, ctx->num_sms, 2);
@@ -433,26 +436,46 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
     d->p_lm = rt::gemv_plan(rt::kBF16, d->V, H, 1, rt::kProResidNorm, rt::kEpiArgmax, ctx->num_sms, 2);
     if (!d->p_qkv.warps || !d->p_o.warps || !d->p_gu.warps || !d->p_down.warps || !d->p_lm.warps)
         return bail(fail(ctx, RT_E_SHAPE, "rt_decoder_create: no GEMV geometry for these shapes"));
+    d->t_qkv.resize(NL);
+    d->t_o.resize(NL);
+    d->t_gu.resize(NL);
+    d->t_down.resize(NL);
+    for (int l = 0; l < NL; ++l) {
+        if (!rt::gemv_make_tmap(rt::kQ4K, d->w_qkv[l], d->qkv_rows, H, d->p_qkv, &d->t_qkv[l]) ||
+            !rt::gemv_make_tmap(rt::kQ4K, d->w_o[l], H, d->NQ * D, d->p_o, &d->t_o[l]) ||
+            !rt::gemv_make_tmap(rt::kQ4K, d->w_gu[l], 2LL * d->F, H, d->p_gu, &d->t_gu[l]) ||
+            !rt::gemv_make_tmap(rt::kQ4K, d->w_down[l], H, d->F, d->p_down, &d->t_down[l]))
+            return bail(fail(ctx, RT_E_CUDA, "rt_decoder_create: TMA descriptor rejected (layer %d)", l));
+    }
+    if (!rt::gemv_make_tmap(rt::kBF16, d->embed, d->V, H, d->p_lm, &d->t_lm))
+        return bail(fail(ctx, RT_E_CUDA, "rt_decoder_create: TMA descriptor rejected (LM head)"));
     d->nsplit = std::max(1, std::min(64, (ctx->num_sms + d->NKV - 1) / d->NKV));
     if (rt::attention_prepare() != cudaSuccess) return bail(fail(ctx, RT_E_CUDA, "attention kernel attributes"));
     // --- activations ---
     {
         const size_t G_ = static_cast<size_t>(G);
         const size_t n_act = 2 * static_cast<size_t>(H) + d->qkv_rows + static_cast<size_t>(d->NQ) * D + H + d->F + H +
-                             d->V + static_cast<size_t>(d->NKV) * d->nsplit * G_ * (D + 2) + d->p_lm.grid;
+                             d->V + static_cast<size_t>(d->NKV) * d->nsplit * G_ * (D + 2) + d->p_lm.grid + 10 * 64;
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->act), n_act * 4 + 1024, "activations")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->act, 0, n_act * 4 + 1024, s);
+        // Every slice starts on a 256-byte boundary (the kernels move these
+        // vectors with TMA bulk copies, which need 16-byte alignment).
         float* p = d->act;
-        d->resid[0] = p; p += H;
-        d->resid[1] = p; p += H;
-        d->qkv = p; p += d->qkv_rows;
-        d->attn = p; p += static_cast<size_t>(d->NQ) * D;
-        d->o_out = p; p += H;
-        d->hbuf = p; p += d->F;
-        d->down = p; p += H;
-        d->logits = p; p += d->V;
-        d->attn_part = p; p += static_cast<size_t>(d->NKV) * d->nsplit * G_ * (D + 2);
-        d->am_val = p; p += d->p_lm.grid;
+        auto slice = [&](size_t n) {
+            float* q = p;
+            p += (n + 63) & ~size_t(63);
+            return q;
+        };
+        d->resid[0] = slice(H);
+        d->resid[1] = slice(H);
+        d->qkv = slice(d->qkv_rows);
+        d->attn = slice(static_cast<size_t>(d->NQ) * D);
+        d->o_out = slice(H);
+        d->hbuf = slice(d->F);
+        d->down = slice(H);
+        d->logits = slice(d->V);
+        d->attn_part = slice(static_cast<size_t>(d->NKV) * d->nsplit * G_ * (D + 2));
+        d->am_val = slice(d->p_lm.grid);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->am_idx), sizeof(int32_t) * d->p_lm.grid, "argmax idx")) != RT_OK) return bail(rc);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->counters), sizeof(uint32_t) * (d->NKV + 1), "counters")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->counters, 0, sizeof(uint32_t) * (d->NKV + 1), s);

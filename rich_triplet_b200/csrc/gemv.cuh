@@ -1,15 +1,16 @@
-// gemv.cuh -- row-streaming GEMV for Q4_K and BF16 weight matrices.
+// gemv.cuh -- row-streaming GEMV for Q4_K and BF16 weight matrices on the
+// tensor cores (mma.sync), for sm_100a.
 //
 // y[r] = sum_k W[r, k] * x[k] for a [rows, K] row-major matrix whose rows are
-// contiguous in HBM, with f32 accumulation.  One kernel serves the standalone
-// GEMV entry points (rt_gemv_q4k / rt_gemv_bf16) and every projection of the
-// fused decode step, where a prologue builds x in shared memory (RMSNorm of
-// the residual stream, embedding lookup) and an epilogue fuses the GELU gate
-// or the greedy argmax.
+// contiguous in HBM.  One kernel serves the standalone GEMV entry points
+// (rt_gemv_q4k / rt_gemv_bf16) and every projection of the fused decode step,
+// where a prologue builds x in shared memory (RMSNorm of the residual stream,
+// embedding lookup) and an epilogue fuses the GELU gate or the greedy argmax.
 #pragma once
 
 #include <stdint.h>
 
+#include <cuda.h>  // CUtensorMap (the encoder is fetched from the driver at run time)
 #include <cuda_runtime.h>
 
 namespace rt {
@@ -38,11 +39,12 @@ struct GemvArgs {
     int32_t seg_bytes;  // 144 (Q4_K block) or 512 (BF16)
     int32_t row_bytes;  // bytes of one row
     // geometry chosen by gemv_plan()
-    int32_t rl;              // row lanes: groups that share a segment index
-    int32_t rows_per_stage;  // rows moved by one bulk copy
-    int32_t nbuf;            // shared-memory stage buffers
-    int32_t stage_bytes;     // capacity of one stage buffer
-    int32_t pair;            // 2 for kEpiGeluPair (row ranges start on even rows)
+    int32_t spst;         // 256-column segments per stage (a stage is 16 rows x spst segments)
+    int32_t srow;         // shared-memory row stride of a stage, = 64 mod 128 bytes
+    int32_t nbuf;         // shared-memory stage buffers
+    int32_t stage_bytes;  // bytes of one stage buffer (16 * srow)
+    int32_t pair;         // 2 for kEpiGeluPair (row ranges start on even rows)
+    int32_t x_smem;       // plain prologue: 1 = copy x into shared memory first, 0 = read it in place
     // prologue inputs
     const float* x;
     const float* src;
@@ -67,22 +69,32 @@ struct GemvArgs {
 
 struct GemvPlan {
     int warps = 0;
-    int rl = 0;
-    int rows_per_stage = 0;
+    int spst = 0;
+    int srow = 0;
     int nbuf = 0;
     int stage_bytes = 0;
+    int x_smem = 1;
     int grid = 0;
     size_t smem = 0;
 };
+
+// Raise the dynamic shared-memory limit of every kernel instantiation on the
+// current device.  Call once per device before planning or capturing.
+void gemv_prepare();
 
 // Choose warps / stage geometry / grid for a [rows, K] GEMV.
 GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int epilogue, int num_sms,
                    int max_ctas_per_sm);
 
+// TMA descriptor of a [rows, K] weight matrix at `w` for plan `p`: 8-byte
+// elements, box = one stage (16 rows x srow bytes; bytes past the row end and
+// rows past the matrix read as zero).  Returns false if the driver refuses.
+bool gemv_make_tmap(int kind, const void* w, int64_t rows, int K, const GemvPlan& p, CUtensorMap* out);
+
 // Fill the geometry fields of `a` from `p` and launch.  `pdl` attaches the
 // programmatic-stream-serialization attribute (used inside the decode graph).
-cudaError_t gemv_launch(int kind, int prologue, int epilogue, GemvArgs a, const GemvPlan& p, cudaStream_t stream,
-                        bool pdl);
+cudaError_t gemv_launch(int kind, int prologue, int epilogue, GemvArgs a, const CUtensorMap& tmap, const GemvPlan& p,
+                        cudaStream_t stream, bool pdl);
 
 // Algorithmic bytes of one launch: weights + x + y (+ prologue vectors).
 uint64_t gemv_algorithmic_bytes(int kind, int64_t rows, int K, int prologue, int epilogue);

@@ -6,9 +6,12 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <map>
 #include <string>
+#include <tuple>
 
 #include "../../include/rt_cuda.h"
+#include "gemv.cuh"
 
 struct rt_ctx {
     int device = 0;
@@ -26,6 +29,10 @@ struct rt_w {
     int64_t rows = 0, cols = 0;
     uint64_t bytes = 0;
     void* d = nullptr;
+    // Launch plan and TMA descriptor of the standalone GEMV, made on first use.
+    bool gemv_ready = false;
+    rt::GemvPlan plan;
+    CUtensorMap tmap;
 };
 
 namespace rt {
