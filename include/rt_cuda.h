@@ -96,6 +96,34 @@ int rt_gemv_q4k(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags)
  * (src/autograd2.rs:954-1000). */
 int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags);
 
+/* Greedy LM-head step that allocates nothing.  No counterpart in the
+ * reference: its LM head and argmax run inside the decode context, whose
+ * buffers are created up front (src/metal_decode.rs:1002-1121).
+ *
+ * Enqueues, on `stream` (a cudaStream_t; NULL = the legacy default stream) of
+ * the CURRENT device: y_dev[r] = bf16(W[r, :]) . x_dev for the [rows, cols]
+ * row-major BF16 matrix at w_dev, then *token_dev = the row of the largest
+ * y_dev (ties to the higher row, as sample_greedy).  All four pointers are
+ * device memory the caller owns; w_dev and x_dev 16-byte aligned; cols a
+ * multiple of 8.  Returns once the work is enqueued.
+ *
+ * Scratch: no context, no cudaMalloc, no allocating library call.  The only
+ * scratch is a file-scope device array of RT_ARGMAX_STATIC_SLOTS per-CTA
+ * (value, row) slots plus an arrival counter (~8 KiB per device).  The counter
+ * must be zero when a launch starts: it is zero at module load and every
+ * launch that completes sets it back to zero.  A launch needing more CTA slots
+ * than RT_ARGMAX_STATIC_SLOTS is rejected with RT_E_SHAPE (and so are rows
+ * beyond 2^31 - 1 or cols beyond 2^20).
+ * Setup: the first call on each device (with that device current) looks up
+ * the scratch address (cudaGetSymbolAddress) and sets the kernel's
+ * shared-memory limit; make that first call before any stream capture.
+ * Overlapping calls on one device (two streams, or two threads) share the
+ * scratch and race: serialize them.
+ * errbuf (may be NULL) receives a one-line reason on failure. */
+#define RT_ARGMAX_STATIC_SLOTS 1024
+int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int cols, const float* x_dev, float* y_dev,
+                               int32_t* token_dev, void* stream, char* errbuf, size_t errlen);
+
 /* ---- load-time conversions (bit-exact with the reference CPU code) ---- */
 
 /* GGUF Q4_0 bytes of a [rows, cols] tensor -> Q4_K weight in HBM, as

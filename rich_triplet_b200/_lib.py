@@ -87,6 +87,10 @@ SIGNATURES = {
     "rt_weight_free": (None, [_vp, _vp]),
     "rt_gemv_q4k": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int]),
     "rt_gemv_bf16": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int]),
+    "rt_gemv_bf16_argmax_static": (
+        ctypes.c_int,
+        [_vp, ctypes.c_int64, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_char_p, ctypes.c_size_t],
+    ),
     "rt_convert_q4_0_to_q4k": (ctypes.c_int, [_vp, _vp, _i64, _i64, ctypes.c_int, _pp]),
     "rt_convert_q6k_to_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i64, ctypes.c_int, _pp]),
     "rt_decoder_create": (ctypes.c_int, [_vp, ctypes.POINTER(RtGemma3Cfg), ctypes.POINTER(RtGemma3Layer), _vp,
