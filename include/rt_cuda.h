@@ -108,19 +108,22 @@ int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags
  * multiple of 8.  Returns once the work is enqueued.
  *
  * Scratch: no context, no cudaMalloc, no allocating library call.  The only
- * scratch is a file-scope device array of RT_ARGMAX_STATIC_SLOTS per-CTA
- * (value, row) slots plus an arrival counter (~8 KiB per device).  The counter
- * must be zero when a launch starts: it is zero at module load and every
- * launch that completes sets it back to zero.  A launch needing more CTA slots
- * than RT_ARGMAX_STATIC_SLOTS is rejected with RT_E_SHAPE (and so are rows
- * beyond 2^31 - 1 or cols beyond 2^20).
+ * scratch is a file-scope device array (~1.3 MiB per device): for up to
+ * RT_ARGMAX_STATIC_SLOTS CTAs a (value, row) argmax slot each and an arrival
+ * counter, 32 partial row sums per warp, and a unit counter per 16-row tile
+ * for up to RT_ARGMAX_STATIC_MAX_ROWS rows.  The counters must be zero when a
+ * launch starts: they are zero at module load and every launch that completes
+ * sets them back to zero.  rows beyond RT_ARGMAX_STATIC_MAX_ROWS, cols beyond
+ * 2^20 and launches needing more than RT_ARGMAX_STATIC_SLOTS CTAs are
+ * rejected with RT_E_SHAPE.
  * Setup: the first call on each device (with that device current) looks up
  * the scratch address (cudaGetSymbolAddress) and sets the kernel's
  * shared-memory limit; make that first call before any stream capture.
  * Overlapping calls on one device (two streams, or two threads) share the
  * scratch and race: serialize them.
  * errbuf (may be NULL) receives a one-line reason on failure. */
-#define RT_ARGMAX_STATIC_SLOTS 1024
+#define RT_ARGMAX_STATIC_SLOTS 512
+#define RT_ARGMAX_STATIC_MAX_ROWS 1048576
 int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int cols, const float* x_dev, float* y_dev,
                                int32_t* token_dev, void* stream, char* errbuf, size_t errlen);
 

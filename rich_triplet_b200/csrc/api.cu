@@ -4,11 +4,13 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
 #include "convert.cuh"
 #include "gemv.cuh"
+
 #include "rt_internal.h"
 
 namespace rt {
@@ -97,6 +99,8 @@ void rt_destroy(rt_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->scratch);
+    cudaFree(ctx->gemv_part);
+    cudaFree(ctx->gemv_cnt);
     cudaFree(ctx->d_err);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -199,6 +203,26 @@ int ensure_scratch(rt_ctx* ctx, size_t floats) {
     return RT_OK;
 }
 
+int ensure_gemv_scratch(rt_ctx* ctx, const rt::GemvPlan& p) {
+    if (ctx->gemv_part_floats >= p.part_floats && ctx->gemv_cnt_words >= p.cnt_words) return RT_OK;
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    const int64_t pf = std::max(ctx->gemv_part_floats, p.part_floats);
+    const int64_t cw = std::max(ctx->gemv_cnt_words, p.cnt_words);
+    cudaFree(ctx->gemv_part);
+    cudaFree(ctx->gemv_cnt);
+    ctx->gemv_part = nullptr;
+    ctx->gemv_cnt = nullptr;
+    ctx->gemv_part_floats = ctx->gemv_cnt_words = 0;
+    int rc = rt::dev_alloc(ctx, reinterpret_cast<void**>(&ctx->gemv_part), sizeof(float) * pf, "gemv partials");
+    if (rc != RT_OK) return rc;
+    rc = rt::dev_alloc(ctx, reinterpret_cast<void**>(&ctx->gemv_cnt), sizeof(uint32_t) * cw, "gemv counters");
+    if (rc != RT_OK) return rc;
+    RT_CHECK_CUDA(ctx, cudaMemsetAsync(ctx->gemv_cnt, 0, sizeof(uint32_t) * cw, ctx->stream));
+    ctx->gemv_part_floats = pf;
+    ctx->gemv_cnt_words = cw;
+    return RT_OK;
+}
+
 int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags, int kind) {
     rt_w* w = const_cast<rt_w*>(wc);  // caches its launch plan and TMA descriptor
     if (!ctx || !w || !x || !y) return fail(ctx, RT_E_INVAL, "gemv: null argument");
@@ -209,13 +233,14 @@ int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
     const int K = static_cast<int>(w->cols);
     if (!w->gemv_ready) {
-        w->plan = rt::gemv_plan(kind, w->rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 2);
+        w->plan = rt::gemv_plan(kind, w->rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 1);
         if (w->plan.warps == 0) return fail(ctx, RT_E_SHAPE, "gemv: no launch geometry for cols %d", K);
         if (!rt::gemv_make_tmap(kind, w->d, w->rows, K, w->plan, &w->tmap))
             return fail(ctx, RT_E_CUDA, "gemv: TMA descriptor rejected for [%lld, %d]", static_cast<long long>(w->rows), K);
         w->gemv_ready = true;
     }
     const rt::GemvPlan& p = w->plan;
+    if (int rc = ensure_gemv_scratch(ctx, p); rc != RT_OK) return rc;
     const float* dx = x;
     float* dy = y;
     if (flags == RT_DEVICE && (reinterpret_cast<uintptr_t>(x) & 15))
@@ -233,6 +258,8 @@ int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags
     a.K = K;
     a.x = dx;
     a.y = dy;
+    a.part = ctx->gemv_part;
+    a.tile_cnt = ctx->gemv_cnt;
     a.err = ctx->d_err;
     RT_CHECK_CUDA(ctx, rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, w->tmap, p, ctx->stream, false));
     if (flags == RT_HOST) {

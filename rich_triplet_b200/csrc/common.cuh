@@ -98,6 +98,22 @@ __device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint
                  : "memory");
 }
 
+// Order this thread's earlier generic-proxy accesses of shared memory (plain
+// loads, ldmatrix) before later async-proxy (TMA) writes to the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Four 8x8 b16 matrices from shared memory; lane l gives the row address of
+// matrix l/8, row l%8 (16-byte aligned) and receives word (l%4) of row l/4 of
+// each matrix.
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p))
+                 : "memory");
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue now, and wait until every prerequisite grid has completed and its
 // memory is visible.

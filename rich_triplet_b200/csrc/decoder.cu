@@ -61,6 +61,8 @@ struct rt_dec {
           *down = nullptr, *logits = nullptr, *attn_part = nullptr, *am_val = nullptr;
     int32_t* am_idx = nullptr;
     uint32_t* counters = nullptr;  // [NKV] attention + [1] argmax
+    float* g_part = nullptr;       // GEMV split-tile partials (shared by the step's GEMVs, which run in order)
+    uint32_t* g_cnt = nullptr;     // GEMV split-tile counters, zero between launches
     int32_t* ctl = nullptr;        // [0] token, [1] position, [2..] token history [cap]
     int* h_err = nullptr;          // pinned copy of the context's error word
     // launch geometry
@@ -116,6 +118,8 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
         // 1. QKV
         {
             rt::GemvArgs a = {};
+            a.part = d->g_part;
+            a.tile_cnt = d->g_cnt;
             a.w = d->w_qkv[l];
             a.rows = d->qkv_rows;
             a.K = H;
@@ -176,6 +180,8 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
         // 3. o projection
         {
             rt::GemvArgs a = {};
+            a.part = d->g_part;
+            a.tile_cnt = d->g_cnt;
             a.w = d->w_o[l];
             a.rows = H;
             a.K = d->NQ * D;
@@ -190,6 +196,8 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
         // 4. gate / up with GELU gate
         {
             rt::GemvArgs a = {};
+            a.part = d->g_part;
+            a.tile_cnt = d->g_cnt;
             a.w = d->w_gu[l];
             a.rows = 2LL * d->F;
             a.K = H;
@@ -210,6 +218,8 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
         // 5. down projection
         {
             rt::GemvArgs a = {};
+            a.part = d->g_part;
+            a.tile_cnt = d->g_cnt;
             a.w = d->w_down[l];
             a.rows = H;
             a.K = d->F;
@@ -224,6 +234,8 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
     }
     if (!q4k_only) {
         rt::GemvArgs a = {};
+        a.part = d->g_part;
+        a.tile_cnt = d->g_cnt;
         a.w = reinterpret_cast<const uint8_t*>(d->embed);
         a.rows = d->V;
         a.K = H;
@@ -429,11 +441,11 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
     }
     // --- plans ---
     rt::gemv_prepare();
-    d->p_qkv = rt::gemv_plan(rt::kQ4K, d->qkv_rows, H, 1, rt::kProResidNorm, rt::kEpiPlain, ctx->num_sms, 2);
-    d->p_o = rt::gemv_plan(rt::kQ4K, H, d->NQ * D, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 2);
-    d->p_gu = rt::gemv_plan(rt::kQ4K, 2LL * d->F, H, 2, rt::kProResidNorm, rt::kEpiGeluPair, ctx->num_sms, 2);
-    d->p_down = rt::gemv_plan(rt::kQ4K, H, d->F, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 2);
-    d->p_lm = rt::gemv_plan(rt::kBF16, d->V, H, 1, rt::kProResidNorm, rt::kEpiArgmax, ctx->num_sms, 2);
+    d->p_qkv = rt::gemv_plan(rt::kQ4K, d->qkv_rows, H, 1, rt::kProResidNorm, rt::kEpiPlain, ctx->num_sms, 1);
+    d->p_o = rt::gemv_plan(rt::kQ4K, H, d->NQ * D, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 1);
+    d->p_gu = rt::gemv_plan(rt::kQ4K, 2LL * d->F, H, 2, rt::kProResidNorm, rt::kEpiGeluPair, ctx->num_sms, 1);
+    d->p_down = rt::gemv_plan(rt::kQ4K, H, d->F, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 1);
+    d->p_lm = rt::gemv_plan(rt::kBF16, d->V, H, 1, rt::kProResidNorm, rt::kEpiArgmax, ctx->num_sms, 1);
     if (!d->p_qkv.warps || !d->p_o.warps || !d->p_gu.warps || !d->p_down.warps || !d->p_lm.warps)
         return bail(fail(ctx, RT_E_SHAPE, "rt_decoder_create: no GEMV geometry for these shapes"));
     d->t_qkv.resize(NL);
@@ -479,6 +491,14 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->am_idx), sizeof(int32_t) * d->p_lm.grid, "argmax idx")) != RT_OK) return bail(rc);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->counters), sizeof(uint32_t) * (d->NKV + 1), "counters")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->counters, 0, sizeof(uint32_t) * (d->NKV + 1), s);
+        int64_t part_floats = 0, cnt_words = 0;
+        for (const rt::GemvPlan* gp : {&d->p_qkv, &d->p_o, &d->p_gu, &d->p_down, &d->p_lm}) {
+            part_floats = std::max(part_floats, gp->part_floats);
+            cnt_words = std::max(cnt_words, gp->cnt_words);
+        }
+        if ((rc = dalloc(d, reinterpret_cast<void**>(&d->g_part), sizeof(float) * part_floats, "gemv partials")) != RT_OK) return bail(rc);
+        if ((rc = dalloc(d, reinterpret_cast<void**>(&d->g_cnt), sizeof(uint32_t) * cnt_words, "gemv counters")) != RT_OK) return bail(rc);
+        cudaMemsetAsync(d->g_cnt, 0, sizeof(uint32_t) * cnt_words, s);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->ctl), sizeof(int32_t) * (2 + d->cap), "control")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->ctl, 0, sizeof(int32_t) * (2 + d->cap), s);
     }

@@ -1,37 +1,45 @@
-// gemv.cu -- Q4_K / BF16 GEMV on the sm_100a tensor cores (mma.sync).
+// gemv.cu -- Q4_K / BF16 GEMV on the sm_100a tensor cores (mma.sync), one
+// weight stream per warp.
 //
-// Streaming.  A CTA owns a contiguous range of 16-row tiles.  Each "stage" is
-// one tile restricted to `spst` consecutive 256-column segments, copied HBM ->
-// shared memory by one 2-D TMA tensor copy (8-byte elements, box = stage row
-// stride x 16 rows, no multicast) into a row stride of 64 mod 128 bytes, so the
-// fragment loads below are bank-conflict free.  The last warp of the CTA is the
-// copy producer; `nbuf` stage buffers are completed on mbarriers and released
-// by the compute warps on a second ring.  The first copies are issued before
-// griddepcontrol.wait, so under programmatic dependent launch the weight stream
-// starts while the previous kernel drains.  The 16 x 256 "units" of the stages
-// are dealt round-robin over the compute warps in flat (stage, segment) order.
+// Work split.  The matrix is cut into units of 16 rows x one column segment
+// (256 Q4_K columns = one 144-byte block per row, or 128 BF16 columns).  Units
+// are numbered tile-major (a tile is 16 rows) and every warp of the grid takes
+// one contiguous, equal share of that sequence, so all warps stream the same
+// number of bytes whatever the shape.  A warp copies its units HBM -> shared
+// memory itself: lane 0 issues one 2-D TMA tensor copy per unit (8-byte
+// elements, box = unit width x 16 rows, no multicast) into a private ring of
+// `nb` buffers, each completed on its own mbarrier (bounded waits).  The first
+// copies are issued before griddepcontrol.wait, so under programmatic dependent
+// launch the weight stream starts while the previous kernel drains.  No warp
+// ever waits for another warp inside the stream.
+//
+// Row sums.  A warp accumulates the units of one tile in registers.  A tile it
+// covers whole goes straight to the epilogue; a tile shared with neighbouring
+// warps (at most two per warp) leaves a 16-row partial in global scratch, and
+// the warp that brings the tile's unit count to a full row (an atomic counter
+// per split tile) adds the partials in warp order -- a fixed order, so results
+// are deterministic -- and runs the epilogue (store, GELU gate, greedy argmax).
 //
 // Q4_K (block layout src/autograd2.rs:1003-1042; Q4KMat::dot_row
 // src/autograd2.rs:1637-1702).  Per 32-column sub-block j of a row,
 //     dot_j = d * sc_j * sum(q * x) - dmin * m_j * sum(x).
-// The quants q (0..15) are the u8 A operand of mma.m16n8k32.u8.s8: a byte
-// mask (and a shift for the high nibbles) turns four packed quants into four
-// A bytes.  x is split once per launch, per sub-block, into three int8 planes
-// x = s * (p0 + p1/128 + p2/16384) (|error| <= s/32768, s = max|x|/127), the s8
-// B operand.  The MMA sums q * p exactly in s32; one k32 MMA covers 8 columns
-// of 4 sub-blocks, and B is zero outside a column pair per sub-block, so lane
-// t of every lane quad ends up holding the (p0, p1, p2) sums of one sub-block
-// for two rows and all 32 lanes share the per-sub-block scale epilogue.
+// ldmatrix hands each lane the A fragment of one 32-byte quant chunk c for 16
+// rows; a byte mask keeps the low nibbles (sub-block 2c) or the high nibbles
+// (sub-block 2c+1, as 16 q) as the u8 A operand of mma.m16n8k32.u8.s8.  x is
+// split once per launch, per sub-block, into three int8 planes
+// x = s * (p0 + p1/128 + p2/16384) (|error| <= s/32768, s = max|x|/127 over the
+// sub-block), the s8 B operand.  The MMA of sub-block j puts planes 0/1 in B
+// columns 2(j&3), 2(j&3)+1 (and plane 2 in column 2(j&3) of a second MMA), zero
+// elsewhere, so lane t of every lane quad ends up holding the three plane sums
+// of sub-blocks t and t+4 for two rows, and all 32 lanes share the scale
+// epilogue.
 //
-// BF16 (MatBf16::dot_row, src/autograd2.rs:861-888).  The weights are the A
-// operand of mma.m16n8k16.bf16 as they sit in shared memory; x is split exactly
-// into three bf16 planes x = hi + mid + lo (B columns 0..2), so the f32 sum of
-// the three product columns is the f32 dot product.
-//
-// Each unit leaves one partial sum per row in shared memory; the warp that
-// finishes the last unit of a tile (a shared-memory counter) adds the partials
-// in segment order (deterministic) and runs the epilogue (store, GELU gate,
-// greedy argmax).
+// BF16 (MatBf16::dot_row, src/autograd2.rs:861-888).  The weights, loaded by
+// ldmatrix, are the A operand of mma.m16n8k16.bf16; x is split exactly into
+// three bf16 planes x = hi + mid + lo (B columns 0..2), so the f32 sum of the
+// three product columns is the f32 dot product.  The unit box is 272 bytes wide
+// (128 columns + 16 bytes of the next unit), which puts consecutive rows 16
+// bytes apart modulo 128 and keeps ldmatrix free of bank conflicts.
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
 
 #include <algorithm>
@@ -44,8 +52,16 @@ namespace rt {
 
 namespace {
 
-constexpr int kMaxNbuf = 6;
 constexpr int kTile = 16;
+constexpr int kMaxWarps = 16;
+constexpr int kMaxNb = 8;
+constexpr int kMaxV8 = 4;  // 8-element chunks of x per thread held by the norm prologues
+constexpr int kQ4KSegCols = 256;
+constexpr int kBF16SegCols = 128;
+constexpr int kQ4KPitch = 144;   // one Q4_K block per row of a unit
+constexpr int kBF16Pitch = 272;  // 128 BF16 columns + 16 bytes
+constexpr int kQ4KUnit = kTile * kQ4KPitch;
+constexpr int kBF16Unit = kTile * kBF16Pitch;
 
 __device__ __forceinline__ float gelu_tanh_dev(float x) {
     // TensorNode::gelu_tanh (src/autograd2.rs:3082-3091): x*0.5*(1+tanh(s*(x+c*x^3))),
@@ -62,6 +78,7 @@ __device__ __forceinline__ float byte_to_float(uint32_t v, uint32_t sel) {
 }
 
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
 
 __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
@@ -75,87 +92,6 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
     asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
-constexpr int kSlots = kMaxNbuf + 2;  // tiles that can be in flight at once
-constexpr int kMaxV = 6;               // float4 chunks per thread in the norm prologues
-
-struct Smem {
-    uint64_t* full;    // [kMaxNbuf] stage data landed
-    uint64_t* empty;   // [kMaxNbuf] stage consumed by every compute warp
-    uint64_t* pbar;    // prologue vectors landed
-    float* red;        // [32]
-    int* flags;        // [8]: 0 = error, 1 = stages issued
-    uint32_t* tcnt;    // [kSlots] units finished per in-flight tile
-    float* part;       // [kSlots][16][nseg] per-(row, segment) partial sums
-    float* bv;         // [32] per-warp argmax value
-    long long* bi;     // [32] per-warp argmax row
-    uint8_t* zero;     // [16] zeros: B operand of columns a lane does not feed
-    float* xs;         // [K] x (copied in, or built by a norm prologue)
-    float* rs;         // [K] residual stream in (norm prologue) / embedding row (bf16)
-    uint8_t* planes;   // Q4_K: [3][Kp] int8; BF16: [3][Kp] bf16
-    float* sx;         // Q4_K: [Kp/32] sum of x over each sub-block
-    uint8_t* stage;    // [nbuf][stage_bytes]
-};
-
-__host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg, int nbuf, int stage_bytes,
-                                        bool need_xs, bool x_smem, Smem* S) {
-    size_t off = 0;
-    auto take = [&](size_t bytes, size_t align) -> uint8_t* {
-        off = (off + align - 1) / align * align;
-        uint8_t* p = base + off;
-        off += bytes;
-        return p;
-    };
-    const size_t Kp = static_cast<size_t>(nseg) * 256;
-    uint8_t* full = take(sizeof(uint64_t) * kMaxNbuf, 16);
-    uint8_t* empty = take(sizeof(uint64_t) * kMaxNbuf, 16);
-    uint8_t* pbar = take(sizeof(uint64_t), 16);
-    uint8_t* red = take(32 * 4, 16);
-    uint8_t* flags = take(8 * 4, 16);
-    uint8_t* tcnt = take(4 * kSlots, 16);
-    uint8_t* part = take(sizeof(float) * kSlots * kTile * nseg, 16);
-    uint8_t* bv = take(4 * 32, 16);
-    uint8_t* bi = take(8 * 32, 16);
-    uint8_t* zero = take(16, 16);
-    uint8_t* xs = take(need_xs || x_smem ? sizeof(float) * K : 0, 16);
-    uint8_t* rs = take(need_xs ? sizeof(float) * K : 0, 16);
-    uint8_t* planes = take(kind == kQ4K ? 3 * Kp : 3 * Kp * 2, 16);
-    uint8_t* sx = take(kind == kQ4K ? sizeof(float) * (Kp / 32) : 0, 16);
-    uint8_t* stage = take(static_cast<size_t>(nbuf) * stage_bytes, 128);
-    if (S) {
-        S->full = reinterpret_cast<uint64_t*>(full);
-        S->empty = reinterpret_cast<uint64_t*>(empty);
-        S->pbar = reinterpret_cast<uint64_t*>(pbar);
-        S->red = reinterpret_cast<float*>(red);
-        S->flags = reinterpret_cast<int*>(flags);
-        S->tcnt = reinterpret_cast<uint32_t*>(tcnt);
-        S->part = reinterpret_cast<float*>(part);
-        S->bv = reinterpret_cast<float*>(bv);
-        S->bi = reinterpret_cast<long long*>(bi);
-        S->zero = zero;
-        S->xs = reinterpret_cast<float*>(xs);
-        S->rs = reinterpret_cast<float*>(rs);
-        S->planes = planes;
-        S->sx = reinterpret_cast<float*>(sx);
-        S->stage = stage;
-    }
-    return off + 128;  // slack for the dynamic shared-memory base alignment
-}
-
-__device__ __forceinline__ float block_max(float v, float* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_max(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
-    return t;
 }
 
 // Round to the nearest integer (ties to even) without the XU pipe:
@@ -177,411 +113,576 @@ __device__ __forceinline__ uint32_t bf16_rne(float x) {
     return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
 }
 
-template <int KIND, int PRO, int EPI>
-__global__ void __launch_bounds__(544) gemv_kernel(const GemvArgs a, const __grid_constant__ CUtensorMap tmap) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    constexpr bool kNeedXs = PRO != kProPlain;
-    Smem S;
-    carve(smem, KIND, a.K, a.nseg, a.nbuf, a.stage_bytes, kNeedXs, a.x_smem != 0, &S);
+__device__ __forceinline__ float ldcg_f32(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
 
+// Shared-memory plane layout.
+//  Q4_K: plane p (0..2) at p * pstride bytes; per 256-column segment 256 bytes,
+//  ordered so that lane t of the quad feeding B column pair r gets, in one
+//  16-byte load, its MMA fragments of sub-blocks r and r+4:
+//      byte r*64 + t*16 + (j>>2)*8 + (e>=16)*4 + (e&3) holds element e of
+//      sub-block j (r = j&3, t = (e&15)>>2).
+//  BF16: plane p (hi, mid, lo) at p * pstride bytes, u16 elements; per 16
+//  columns, lane t's B fragment (columns 2t, 2t+1, 8+2t, 9+2t) is 8 bytes at 8t.
+__host__ __device__ inline int q4k_pstride(int Kp) { return Kp + 64; }       // = 64 mod 128: no bank conflicts
+__host__ __device__ inline int bf16_pstride(int Kp) { return Kp * 2 + 32; }  // = 32 mod 128
+
+struct Smem {
+    uint64_t* full;   // [warps][nb] unit landed
+    uint64_t* pbar;   // norm weights landed
+    float* red;       // [32]
+    int* flags;       // [4]: 0 = a wait gave up
+    float* bv;        // [32] per-warp argmax value
+    long long* bi;    // [32] per-warp argmax row
+    float* gpost;     // [K] post-norm weight (residual-norm prologue)
+    float* gpre;      // [K] pre-norm weight (norm prologues)
+    uint8_t* planes;  // x planes, layout above
+    float2* xsx;      // Q4_K: [Kp/32] {value of one unit of the plane integer (/16 for odd sub-blocks), sum of x}
+    uint8_t* ring;    // [warps][nb][unit_bytes]
+};
+
+__host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg, int warps, int nb, int unit_bytes,
+                                        int pro, Smem* S) {
+    size_t off = 0;
+    auto take = [&](size_t bytes, size_t align) -> uint8_t* {
+        off = (off + align - 1) / align * align;
+        uint8_t* p = base + off;
+        off += bytes;
+        return p;
+    };
+    const int Kp = nseg * (kind == kQ4K ? kQ4KSegCols : kBF16SegCols);
+    uint8_t* full = take(sizeof(uint64_t) * warps * nb, 16);
+    uint8_t* pbar = take(sizeof(uint64_t), 16);
+    uint8_t* red = take(32 * 4, 16);
+    uint8_t* flags = take(4 * 4, 16);
+    uint8_t* bv = take(4 * 32, 16);
+    uint8_t* bi = take(8 * 32, 16);
+    uint8_t* gpost = take(pro == kProResidNorm ? sizeof(float) * K : 0, 16);
+    uint8_t* gpre = take(pro != kProPlain ? sizeof(float) * K : 0, 16);
+    uint8_t* planes = take(kind == kQ4K ? 3 * static_cast<size_t>(q4k_pstride(Kp))
+                                        : 3 * static_cast<size_t>(bf16_pstride(Kp)),
+                           128);
+    uint8_t* xsx = take(kind == kQ4K ? sizeof(float2) * (Kp / 32) : 0, 16);
+    uint8_t* ring = take(static_cast<size_t>(warps) * nb * unit_bytes, 128);
+    if (S) {
+        S->full = reinterpret_cast<uint64_t*>(full);
+        S->pbar = reinterpret_cast<uint64_t*>(pbar);
+        S->red = reinterpret_cast<float*>(red);
+        S->flags = reinterpret_cast<int*>(flags);
+        S->bv = reinterpret_cast<float*>(bv);
+        S->bi = reinterpret_cast<long long*>(bi);
+        S->gpost = reinterpret_cast<float*>(gpost);
+        S->gpre = reinterpret_cast<float*>(gpre);
+        S->planes = planes;
+        S->xsx = reinterpret_cast<float2*>(xsx);
+        S->ring = ring;
+    }
+    return off;
+}
+
+// Q4_K planes of one 256-column segment: lane l of the calling warp holds
+// elements 8l..8l+7 of it (zeros past K).  Writes the three planes and the
+// per-sub-block {unit, sum}.
+__device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg, int lane, int pstride,
+                                                   uint8_t* planes, float2* xsx) {
+    float m = 0.f, sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        m = fmaxf(m, fabsf(xv[e]));
+        sum += xv[e];
+    }
+    // a sub-block is 4 lanes
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float s = m / 127.0f;
+    const float inv = m > 0.f ? 127.0f / m : 0.f;
+    const float s128 = s * (1.0f / 128.0f);
+    const float inv128 = inv * 128.0f, inv16k = inv * 16384.0f;
+    int q0[8], q1[8], q2[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        float f0, f1, f2;
+        q0[e] = round_magic(xv[e] * inv, &f0);
+        const float r1 = fmaf(-f0, s, xv[e]);
+        q1[e] = round_magic(r1 * inv128, &f1);
+        const float r2 = fmaf(-f1, s128, r1);
+        q2[e] = round_magic(r2 * inv16k, &f2);
+    }
+    const int j = lane >> 2;  // sub-block of this lane's elements
+    const int r = j & 3, half = j >> 2;
+    const int t0 = (lane & 1) ? 2 : 0;    // elements 8(l&3)..: t of the first four
+    const int posb = (lane & 2) ? 4 : 0;  // second 16 elements of the sub-block
+    const int o0 = seg * 256 + r * 64 + t0 * 16 + half * 8 + posb;
+    const int o1 = o0 + 16;
+    uint8_t* P0 = planes;
+    uint8_t* P1 = planes + pstride;
+    uint8_t* P2 = planes + 2 * pstride;
+    *reinterpret_cast<uint32_t*>(P0 + o0) = pack4(q0[0], q0[1], q0[2], q0[3]);
+    *reinterpret_cast<uint32_t*>(P0 + o1) = pack4(q0[4], q0[5], q0[6], q0[7]);
+    *reinterpret_cast<uint32_t*>(P1 + o0) = pack4(q1[0], q1[1], q1[2], q1[3]);
+    *reinterpret_cast<uint32_t*>(P1 + o1) = pack4(q1[4], q1[5], q1[6], q1[7]);
+    *reinterpret_cast<uint32_t*>(P2 + o0) = pack4(q2[0], q2[1], q2[2], q2[3]);
+    *reinterpret_cast<uint32_t*>(P2 + o1) = pack4(q2[4], q2[5], q2[6], q2[7]);
+    if ((lane & 3) == 0) {
+        // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
+        const float unit = s * (1.0f / 16384.0f) * ((j & 1) ? 0.0625f : 1.0f);
+        xsx[seg * 8 + j] = make_float2(unit, sum);
+    }
+}
+
+// BF16 planes of 8 consecutive columns 8q..8q+7 (zeros past K).
+__device__ __forceinline__ void bf16_chunk_planes(const float (&xv)[8], int q, int pstride, uint8_t* planes) {
+    uint32_t h[8], md[8], lo[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        h[e] = bf16_rne(xv[e]);
+        const float r = xv[e] - __uint_as_float(h[e] << 16);
+        md[e] = bf16_rne(r);
+        lo[e] = bf16_rne(r - __uint_as_float(md[e] << 16));
+    }
+    // 16-column block b = q >> 1, half hf = q & 1: element 8hf + i sits at slot
+    // 4(i >> 1) + 2hf + (i & 1), i.e. pair i>>1 is 32-bit word 2(i>>1) + hf.
+    const int b = q >> 1, hf = q & 1;
+    uint32_t* P0 = reinterpret_cast<uint32_t*>(planes) + b * 8 + hf;
+    uint32_t* P1 = reinterpret_cast<uint32_t*>(planes + pstride) + b * 8 + hf;
+    uint32_t* P2 = reinterpret_cast<uint32_t*>(planes + 2 * pstride) + b * 8 + hf;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        P0[2 * k] = h[2 * k] | (h[2 * k + 1] << 16);
+        P1[2 * k] = md[2 * k] | (md[2 * k + 1] << 16);
+        P2[2 * k] = lo[2 * k] | (lo[2 * k + 1] << 16);
+    }
+}
+
+// The unit split: warp w (grid-wide index) owns units [start(w), start(w+1))
+// with start(w) = floor(U * w / NW); U < 2^31 and NW < 2^16 keep all of it in
+// 32-bit arithmetic.
+struct Split {
+    uint32_t U;
+    uint32_t q;  // U / NW
+    uint32_t r;  // U % NW
+    uint32_t NW;
+    float w_per_u;  // NW / U
+    __device__ __forceinline__ uint32_t start(uint32_t w) const { return q * w + (r * w) / NW; }
+    // The warp whose range holds unit u (a float estimate, then exact steps).
+    __device__ __forceinline__ uint32_t owner(uint32_t u) const {
+        uint32_t w = min(NW - 1, static_cast<uint32_t>(static_cast<float>(u) * w_per_u));
+        while (w + 1 < NW && start(w + 1) <= u) ++w;
+        while (w > 0 && start(w) > u) --w;
+        return w;
+    }
+};
+
+template <int KIND, int PRO, int EPI>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1)
+    gemv_kernel(const GemvArgs a, const __grid_constant__ CUtensorMap tmap) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // TMA destinations need 128-byte alignment (the plan reserves the slack).
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t{127});
+    constexpr int kSegCols = KIND == kQ4K ? kQ4KSegCols : kBF16SegCols;
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
-    const int nwc = nw - 1;  // compute warps; the last warp is the copy producer
-    const bool producer = warp == nwc;
-    const int K = a.K, nseg = a.nseg, spst = a.spst;
-    const int Kp = nseg * 256;
-    const int nsc = (nseg + spst - 1) / spst;  // segment chunks (stages) per tile
+    const int g = lane >> 2, t = lane & 3;
+    const int K = a.K, nseg = a.nseg, NB = a.nb, ubytes = a.unit_bytes;
+    const int Kp = nseg * kSegCols;
+    const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
+    Smem S;
+    carve(smem, KIND, K, nseg, nw, NB, ubytes, PRO, &S);
 
-    // Contiguous, balanced range of 16-row tiles.
-    const int64_t ntiles_all = (a.rows + kTile - 1) / kTile;
-    const int64_t t_begin = ntiles_all * blockIdx.x / gridDim.x;
-    const int64_t t_end = ntiles_all * (blockIdx.x + 1) / gridDim.x;
-    const int64_t r_begin = t_begin * kTile;
-    const int64_t r_end = min(a.rows, t_end * kTile);
-    const int nst = static_cast<int>(t_end - t_begin) * nsc;
+    // This warp's share of the tile-major unit sequence.
+    const uint32_t ntiles = static_cast<uint32_t>((a.rows + kTile - 1) / kTile);
+    Split sp;
+    sp.U = ntiles * static_cast<uint32_t>(nseg);
+    sp.NW = gridDim.x * static_cast<uint32_t>(nw);
+    sp.q = sp.U / sp.NW;
+    sp.r = sp.U - sp.q * sp.NW;
+    sp.w_per_u = static_cast<float>(sp.NW) / static_cast<float>(sp.U);
+    const uint32_t gw = blockIdx.x * static_cast<uint32_t>(nw) + warp;
+    const uint32_t u_begin = sp.start(gw);
+    const int n = static_cast<int>(sp.start(gw + 1) - u_begin);
+    uint64_t* full = S.full + warp * NB;
+    uint8_t* ring = S.ring + static_cast<size_t>(warp) * NB * ubytes;
 
-    if (tid == 0) {
-        for (int b = 0; b < a.nbuf; ++b) {
-            mbar_init(&S.full[b], 1);
-            mbar_init(&S.empty[b], nwc);
-        }
-        mbar_init(S.pbar, 1);
+    if (lane == 0) {
+        for (int j = 0; j < NB; ++j) mbar_init(&full[j], 1);
+        if (warp == 0) mbar_init(S.pbar, 1);
         fence_mbar_init();
-        S.flags[0] = 0;
-        S.flags[1] = 0;
     }
-    if (tid < kSlots) S.tcnt[tid] = 0u;
-    if (tid < 4) reinterpret_cast<uint32_t*>(S.zero)[tid] = 0u;
+    if (tid == 0) S.flags[0] = 0;
     __syncthreads();
 
+    // ---- weight stream: lane 0 of each warp issues its own unit copies ----
     const uint64_t pol = l2_evict_first_policy();
-    // Producer: one 2-D tensor copy per stage (16 rows x one segment chunk);
-    // the box's inner extent is the padded row stride.
-    auto issue = [&](int st) {
-        if (lane == 0) {
-            const int tile = st / nsc, sc = st % nsc;
-            const int64_t r0 = r_begin + static_cast<int64_t>(tile) * kTile;
-            const int b = st % a.nbuf;
-            mbar_arrive_expect_tx(&S.full[b], static_cast<uint32_t>(a.stage_bytes));
-            tma_2d_g2s(S.stage + static_cast<size_t>(b) * a.stage_bytes, &tmap, sc * spst * a.seg_bytes / 8,
-                       static_cast<int>(r0), &S.full[b], pol);
-            S.flags[1] = st + 1;
+    constexpr int kBoxStep = KIND == kQ4K ? kQ4KPitch / 8 : kBF16SegCols * 2 / 8;  // x advance per segment
+    uint32_t is_tile = u_begin / nseg;
+    int is_seg = static_cast<int>(u_begin - is_tile * nseg);
+    int issued = 0;
+    auto issue = [&](int j) {
+        mbar_arrive_expect_tx(&full[j], static_cast<uint32_t>(ubytes));
+        tma_2d_g2s(ring + static_cast<size_t>(j) * ubytes, &tmap, is_seg * kBoxStep, static_cast<int>(is_tile * kTile),
+                   &full[j], pol);
+        if (++is_seg == nseg) {
+            is_seg = 0;
+            ++is_tile;
         }
-        __syncwarp();
+        ++issued;
     };
-    if (producer) {
-        for (int st = 0; st < min(a.nbuf, nst); ++st) issue(st);
+    if (lane == 0) {
+        const int np = min(NB, n);
+        for (int j = 0; j < np; ++j) issue(j);
     }
-    // The norm weights are constants: load this thread's float4 chunks now,
-    // before waiting for the previous kernel.
-    const int K4 = K / 4;
-    float4 gp[kMaxV], gq[kMaxV];
+    // Norm weights are constants: fetch them before waiting on the previous kernel.
     if constexpr (PRO != kProPlain) {
-#pragma unroll
-        for (int k = 0; k < kMaxV; ++k) {
-            const int i = tid + k * nthr;
-            if (i < K4) {
-                if constexpr (PRO == kProResidNorm) gp[k] = reinterpret_cast<const float4*>(a.g_post)[i];
-                gq[k] = reinterpret_cast<const float4*>(a.g_pre)[i];
-            }
+        if (tid == 0) {
+            const uint32_t kb = static_cast<uint32_t>(K) * 4u;
+            mbar_arrive_expect_tx(S.pbar, PRO == kProResidNorm ? 2u * kb : kb);
+            if constexpr (PRO == kProResidNorm) bulk_g2s_nohint(S.gpost, a.g_post, kb, S.pbar);
+            bulk_g2s_nohint(S.gpre, a.g_pre, kb, S.pbar);
         }
     }
     pdl_launch_dependents();
     pdl_wait();
 
-    // ---------------- prologue: the input vectors, one bulk round trip ----------------
-    const bool x_in_place = PRO == kProPlain && !a.x_smem;  // large K: planes read x from global
-    if (tid == 0 && !x_in_place) {
-        if constexpr (PRO == kProPlain) {
-            mbar_arrive_expect_tx(S.pbar, static_cast<uint32_t>(K) * 4u);
-            bulk_g2s_nohint(S.xs, a.x, static_cast<uint32_t>(K) * 4u, S.pbar);
-        } else if constexpr (PRO == kProResidNorm) {
-            mbar_arrive_expect_tx(S.pbar, static_cast<uint32_t>(K) * 8u);
-            bulk_g2s_nohint(S.xs, a.src, static_cast<uint32_t>(K) * 4u, S.pbar);
-            bulk_g2s_nohint(S.rs, a.resid_in, static_cast<uint32_t>(K) * 4u, S.pbar);
-        } else {
-            const int64_t tok = static_cast<int64_t>(*a.token);
-            mbar_arrive_expect_tx(S.pbar, static_cast<uint32_t>(K) * 2u);
-            bulk_g2s_nohint(S.rs, a.embed + tok * K, static_cast<uint32_t>(K) * 2u, S.pbar);
+    // ---------------- prologue: x -> planes ----------------
+    if constexpr (PRO == kProPlain) {
+        // 8-column chunks q = tid + i * nthr; for Q4_K a warp covers one segment
+        // per i.  All loads of a group of kMaxV8 chunks are in flight together.
+        const int nq = Kp / 8;
+        for (int base0 = 0; base0 < nq; base0 += kMaxV8 * nthr) {
+            float4 xl[kMaxV8][2];
+#pragma unroll
+            for (int i = 0; i < kMaxV8; ++i) {
+                const int c0 = (base0 + i * nthr + tid) * 8;
+                if (c0 + 8 <= K) {
+                    xl[i][0] = *reinterpret_cast<const float4*>(a.x + c0);
+                    xl[i][1] = *reinterpret_cast<const float4*>(a.x + c0 + 4);
+                } else {
+                    xl[i][0] = xl[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kMaxV8; ++i) {
+                const int base = base0 + i * nthr;
+                if (base >= nq) break;
+                const int qi = base + tid;
+                const float xv[8] = {xl[i][0].x, xl[i][0].y, xl[i][0].z, xl[i][0].w,
+                                     xl[i][1].x, xl[i][1].y, xl[i][1].z, xl[i][1].w};
+                if constexpr (KIND == kQ4K) {
+                    if (base + warp * 32 < nq) q4k_segment_planes(xv, (base >> 5) + warp, lane, pstride, S.planes, S.xsx);
+                } else {
+                    if (qi < nq) bf16_chunk_planes(xv, qi, pstride, S.planes);
+                }
+            }
         }
-    }
-    if (!x_in_place && !mbar_wait(S.pbar, 0u) && lane == 0) atomicExch(&S.flags[0], 1);
-    float4* xs4 = reinterpret_cast<float4*>(S.xs);
-    if constexpr (PRO == kProResidNorm || PRO == kProEmbedNorm) {
+    } else {
+        // Thread chunk i holds columns 8q..8q+7, q = tid + i * nthr.
         const float inv_d = 1.0f / static_cast<float>(K);
-        float4* out4 = reinterpret_cast<float4*>(a.resid_out);
+        float xr[kMaxV8][8];
         float ss = 0.f;
         if constexpr (PRO == kProResidNorm) {
             // post-norm of the sub-layer output, then the residual add
             // (Gemma3Block::forward_cached, src/transformer4.rs:1954-1964)
-            const float4* rs4 = reinterpret_cast<const float4*>(S.rs);
+            float v[kMaxV8][8];
 #pragma unroll
-            for (int k = 0; k < kMaxV; ++k) {
-                const int i = tid + k * nthr;
-                if (i < K4) {
-                    const float4 v = xs4[i];
-                    ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+            for (int i = 0; i < kMaxV8; ++i) {
+                const int c0 = (tid + i * nthr) * 8;
+                if (c0 < K) {
+                    const float4 s0 = *reinterpret_cast<const float4*>(a.src + c0);
+                    const float4 s1 = *reinterpret_cast<const float4*>(a.src + c0 + 4);
+                    const float4 r0 = *reinterpret_cast<const float4*>(a.resid_in + c0);
+                    const float4 r1 = *reinterpret_cast<const float4*>(a.resid_in + c0 + 4);
+                    v[i][0] = s0.x; v[i][1] = s0.y; v[i][2] = s0.z; v[i][3] = s0.w;
+                    v[i][4] = s1.x; v[i][5] = s1.y; v[i][6] = s1.z; v[i][7] = s1.w;
+                    xr[i][0] = r0.x; xr[i][1] = r0.y; xr[i][2] = r0.z; xr[i][3] = r0.w;
+                    xr[i][4] = r1.x; xr[i][5] = r1.y; xr[i][6] = r1.z; xr[i][7] = r1.w;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[i][e] = xr[i][e] = 0.f;
                 }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
             }
             ss = block_sum(ss, S.red);
+            if (!mbar_wait(S.pbar, 0u) && lane == 0) atomicExch(&S.flags[0], 1);
             const float r1 = 1.0f / sqrtf(ss * inv_d + a.eps);
             float ss2 = 0.f;
 #pragma unroll
-            for (int k = 0; k < kMaxV; ++k) {
-                const int i = tid + k * nthr;
-                if (i < K4) {
-                    const float4 v = xs4[i], r = rs4[i], g = gp[k];
-                    float4 n;
-                    n.x = __fadd_rn(r.x, __fmul_rn(__fmul_rn(v.x, r1), __fadd_rn(1.0f, g.x)));
-                    n.y = __fadd_rn(r.y, __fmul_rn(__fmul_rn(v.y, r1), __fadd_rn(1.0f, g.y)));
-                    n.z = __fadd_rn(r.z, __fmul_rn(__fmul_rn(v.z, r1), __fadd_rn(1.0f, g.z)));
-                    n.w = __fadd_rn(r.w, __fmul_rn(__fmul_rn(v.w, r1), __fadd_rn(1.0f, g.w)));
-                    xs4[i] = n;
-                    ss2 += (n.x * n.x + n.y * n.y) + (n.z * n.z + n.w * n.w);
-                    if (blockIdx.x == 0) out4[i] = n;
+            for (int i = 0; i < kMaxV8; ++i) {
+                const int c0 = (tid + i * nthr) * 8;
+                if (c0 < K) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float nv = __fadd_rn(xr[i][e], __fmul_rn(__fmul_rn(v[i][e], r1), __fadd_rn(1.0f, S.gpost[c0 + e])));
+                        xr[i][e] = nv;
+                        ss2 += nv * nv;
+                    }
+                    if (blockIdx.x == 0) {
+                        *reinterpret_cast<float4*>(a.resid_out + c0) = make_float4(xr[i][0], xr[i][1], xr[i][2], xr[i][3]);
+                        *reinterpret_cast<float4*>(a.resid_out + c0 + 4) = make_float4(xr[i][4], xr[i][5], xr[i][6], xr[i][7]);
+                    }
                 }
             }
             ss = block_sum(ss2, S.red);
         } else {
             // embedding row * sqrt(hidden) (src/transformer4.rs:2360-2364)
-            const uint2* e2 = reinterpret_cast<const uint2*>(S.rs);
+            const int64_t tok = static_cast<int64_t>(*a.token);
+            const uint16_t* er = a.embed + tok * K;
 #pragma unroll
-            for (int k = 0; k < kMaxV; ++k) {
-                const int i = tid + k * nthr;
-                if (i < K4) {
-                    const uint2 e = e2[i];
-                    float4 n;
-                    n.x = __fmul_rn(bf16_bits_to_f32(e.x & 0xFFFFu), a.embed_scale);
-                    n.y = __fmul_rn(bf16_bits_to_f32(e.x >> 16), a.embed_scale);
-                    n.z = __fmul_rn(bf16_bits_to_f32(e.y & 0xFFFFu), a.embed_scale);
-                    n.w = __fmul_rn(bf16_bits_to_f32(e.y >> 16), a.embed_scale);
-                    xs4[i] = n;
-                    ss += (n.x * n.x + n.y * n.y) + (n.z * n.z + n.w * n.w);
-                    if (blockIdx.x == 0) out4[i] = n;
+            for (int i = 0; i < kMaxV8; ++i) {
+                const int c0 = (tid + i * nthr) * 8;
+                if (c0 < K) {
+                    const uint4 e = *reinterpret_cast<const uint4*>(er + c0);
+                    const uint32_t ew[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        xr[i][2 * k] = __fmul_rn(bf16_bits_to_f32(ew[k] & 0xFFFFu), a.embed_scale);
+                        xr[i][2 * k + 1] = __fmul_rn(bf16_bits_to_f32(ew[k] >> 16), a.embed_scale);
+                    }
+#pragma unroll
+                    for (int e2 = 0; e2 < 8; ++e2) ss += xr[i][e2] * xr[i][e2];
+                    if (blockIdx.x == 0) {
+                        *reinterpret_cast<float4*>(a.resid_out + c0) = make_float4(xr[i][0], xr[i][1], xr[i][2], xr[i][3]);
+                        *reinterpret_cast<float4*>(a.resid_out + c0 + 4) = make_float4(xr[i][4], xr[i][5], xr[i][6], xr[i][7]);
+                    }
+                } else {
+#pragma unroll
+                    for (int e2 = 0; e2 < 8; ++e2) xr[i][e2] = 0.f;
                 }
             }
             ss = block_sum(ss, S.red);
+            if (!mbar_wait(S.pbar, 0u) && lane == 0) atomicExch(&S.flags[0], 1);
         }
         // pre-norm producing the projection input (rms_norm_gemma3,
-        // src/autograd2.rs:3477-3496)
+        // src/autograd2.rs:3477-3496), then the planes
         const float r2 = 1.0f / sqrtf(ss * inv_d + a.eps);
+        const int nq = Kp / 8;
 #pragma unroll
-        for (int k = 0; k < kMaxV; ++k) {
-            const int i = tid + k * nthr;
-            if (i < K4) {
-                const float4 n = xs4[i], g = gq[k];
-                float4 x;
-                x.x = __fmul_rn(__fmul_rn(n.x, r2), __fadd_rn(1.0f, g.x));
-                x.y = __fmul_rn(__fmul_rn(n.y, r2), __fadd_rn(1.0f, g.y));
-                x.z = __fmul_rn(__fmul_rn(n.z, r2), __fadd_rn(1.0f, g.z));
-                x.w = __fmul_rn(__fmul_rn(n.w, r2), __fadd_rn(1.0f, g.w));
-                xs4[i] = x;
+        for (int i = 0; i < kMaxV8; ++i) {
+            const int base = i * nthr;
+            if (base >= nq) break;
+            const int qi = base + tid;
+            const int c0 = qi * 8;
+            float xv[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                xv[e] = c0 < K ? __fmul_rn(__fmul_rn(xr[i][e], r2), __fadd_rn(1.0f, S.gpre[c0 + e])) : 0.f;
+            if constexpr (KIND == kQ4K) {
+                if (base + warp * 32 < nq) q4k_segment_planes(xv, (base >> 5) + warp, lane, pstride, S.planes, S.xsx);
+            } else {
+                if (qi < nq) bf16_chunk_planes(xv, qi, pstride, S.planes);
             }
         }
     }
     __syncthreads();
-    const float* xsrc = x_in_place ? a.x : S.xs;
 
-    // ---------------- x planes (the B operand) ----------------
-    float xsc = 0.f;  // Q4_K: value of one unit of the combined plane integer
-    if constexpr (KIND == kQ4K) {
-        // One scale for the whole vector: x = s * (p0 + p1/128 + p2/16384),
-        // |error| <= s / 32768 with s = max|x| / 127.
-        float m = 0.f;
-        for (int i = tid; i < K4; i += nthr) {
-            const float4 v = reinterpret_cast<const float4*>(xsrc)[i];
-            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        }
-        m = block_max(m, S.red);
-        const float s = m / 127.0f;
-        const float inv = m > 0.f ? 127.0f / m : 0.f;
-        const float s128 = s * (1.0f / 128.0f);
-        const float inv128 = inv * 128.0f, inv16k = inv * 16384.0f;
-        xsc = s * (1.0f / 16384.0f);
-        uint32_t* P = reinterpret_cast<uint32_t*>(S.planes);
-        for (int base = 0; base < K4; base += nthr) {
-            const int i = base + tid;
-            const bool valid = i < K4;
-            const float4 v = valid ? reinterpret_cast<const float4*>(xsrc)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float xv[4] = {v.x, v.y, v.z, v.w};
-            int q0[4], q1[4], q2[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float f0, f1, f2;
-                q0[e] = round_magic(xv[e] * inv, &f0);
-                const float r1 = fmaf(-f0, s, xv[e]);
-                q1[e] = round_magic(r1 * inv128, &f1);
-                const float r2 = fmaf(-f1, s128, r1);
-                q2[e] = round_magic(r2 * inv16k, &f2);
-            }
-            float sum = (v.x + v.y) + (v.z + v.w);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-            if (valid) {
-                P[i] = pack4(q0[0], q0[1], q0[2], q0[3]);
-                P[Kp / 4 + i] = pack4(q1[0], q1[1], q1[2], q1[3]);
-                P[Kp / 2 + i] = pack4(q2[0], q2[1], q2[2], q2[3]);
-                if ((i & 7) == 0) S.sx[i >> 3] = sum;
-            }
-        }
-    } else {
-        uint2* P = reinterpret_cast<uint2*>(S.planes);
-        for (int i = tid; i < Kp / 4; i += nthr) {
-            const float4 v = i < K4 ? reinterpret_cast<const float4*>(xsrc)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float xv[4] = {v.x, v.y, v.z, v.w};
-            uint32_t h[4], md[4], lo[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                h[e] = bf16_rne(xv[e]);
-                const float r = xv[e] - __uint_as_float(h[e] << 16);
-                md[e] = bf16_rne(r);
-                lo[e] = bf16_rne(r - __uint_as_float(md[e] << 16));
-            }
-            P[i] = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
-            P[Kp / 4 + i] = make_uint2(md[0] | (md[1] << 16), md[2] | (md[3] << 16));
-            P[Kp / 2 + i] = make_uint2(lo[0] | (lo[1] << 16), lo[2] | (lo[3] << 16));
-        }
-    }
-    __syncthreads();
-
+    // ---------------- the weight stream ----------------
     float best_v = -INFINITY;
     long long best_i = -1;
-    if (producer) {
-        // Refill each buffer once every compute warp has released it.
-        for (int st = a.nbuf; st < nst; ++st) {
-            const int b = st % a.nbuf;
-            const bool ok = mbar_wait(&S.empty[b], static_cast<uint32_t>(st / a.nbuf - 1) & 1u);
-            if (!ok) {
-                if (lane == 0) atomicExch(&S.flags[0], 1);
-                break;
+    // Row epilogue: lane L < 16 holds the sum of row r0 + L.
+    auto emit_rows = [&](int64_t r0, float v) {
+        const int64_t r = r0 + lane;
+        if constexpr (EPI == kEpiGeluPair) {
+            const float up = __shfl_down_sync(0xffffffffu, v, 1);
+            if (lane < kTile && !(lane & 1) && r < a.rows) a.y[r >> 1] = __fmul_rn(gelu_tanh_dev(v), up);
+        } else {
+            if (lane < kTile && r < a.rows) {
+                a.y[r] = v;
+                if constexpr (EPI == kEpiArgmax) {
+                    if (v > best_v || (v == best_v && r > best_i)) {
+                        best_v = v;
+                        best_i = r;
+                    }
+                }
             }
-            issue(st);
         }
-    } else {
-        const int g = lane >> 2, t = lane & 3;
-        // Q4_K: the B column this lane feeds (see the header comment).
-        const bool sel0 = (g >> 1) == (t >> 1);
-        const bool sel1 = (g >> 1) == 2 + (t >> 1);
-        const int j0 = 2 * (t & 1) + (t >> 1);  // sub-block (of each half block) whose sums this lane gets
-        const uint32_t jsel = 0x7540u | static_cast<uint32_t>(j0);
-        for (int st = 0; st < nst; ++st) {
-            const int b = st % a.nbuf;
-            if (!mbar_wait(&S.full[b], static_cast<uint32_t>(st / a.nbuf) & 1u)) {
-                if (lane == 0) atomicExch(&S.flags[0], 1);
-                break;
-            }
-            const int tile = st / nsc, sc = st % nsc;
-            const int64_t r0 = r_begin + static_cast<int64_t>(tile) * kTile;
-            const int nr = static_cast<int>(min(static_cast<int64_t>(kTile), r_end - r0));
-            const int s0 = sc * spst;
-            const int nus = min(nseg, s0 + spst) - s0;  // segments (units) in this stage
-            const uint8_t* sbuf = S.stage + static_cast<size_t>(b) * a.stage_bytes;
-            const int slot = tile % kSlots;
-            float* pb = S.part + static_cast<size_t>(slot) * kTile * nseg;
-            int mine = 0;
-            // Units are dealt round-robin over the flat (stage, segment) order, so
-            // the compute warps spread over every stage that has landed.
-            const int u0 = ((warp - (st * spst) % nwc) % nwc + nwc) % nwc;
-            for (int u = u0; u < nus; u += nwc) {
-                ++mine;
-                const int seg = s0 + u;
-                float vg = 0.f, vg8 = 0.f;
-                if constexpr (KIND == kQ4K) {
-                    const uint8_t* rg = sbuf + g * a.srow + u * 144;
-                    const uint8_t* rg8 = rg + 8 * a.srow;
-                    const uint4 h0 = lds128(rg), h1 = lds128(rg8);
-                    uint4 A0[2], A1[2], Ba0[2], Ba1[2], Bb0[2], Bb1[2];
+    };
+
+    const int q = g >> 1;  // Q4_K: the B column pair this lane feeds
+    const uint32_t jsel = 0x7540u | static_cast<uint32_t>(t);
+    // ldmatrix row address of this lane within a unit (matrix l/8: rows 0-7 or
+    // 8-15, first or second 16 bytes of the 32-byte k slice)
+    const int ldsm_off = KIND == kQ4K
+                             ? ((lane & 7) + ((lane >> 3) & 1) * 8) * kQ4KPitch + 16 + ((lane >> 4) & 1) * 16
+                             : ((lane & 7) + ((lane >> 3) & 1) * 8) * kBF16Pitch + ((lane >> 4) & 1) * 16;
+
+    float acc0 = 0.f, acc1 = 0.f;  // this lane's share of rows g and g+8 of the current tile
+    uint32_t tile = u_begin / nseg;
+    int seg = static_cast<int>(u_begin - tile * nseg);
+    const uint32_t first_tile = tile;
+    int pu = 0;  // units of the current tile piece
+    int jb = 0;
+    uint32_t ph = 0;
+    int done = 0;
+    bool failed = false;
+    for (int i = 0; i < n; ++i) {
+        const bool ok = mbar_wait(&full[jb], ph);
+        if (__any_sync(0xffffffffu, !ok)) {
+            failed = true;
+            break;
+        }
+        const uint8_t* ub = ring + static_cast<size_t>(jb) * ubytes;
+        if constexpr (KIND == kQ4K) {
+            // B fragments: planes 0/1 of sub-blocks q and q+4 (this lane's column
+            // pair) and, for even g, plane 2.
+            const uint8_t* pb = S.planes + seg * 256 + q * 64 + t * 16;
+            const uint4 B01 = lds128(pb + (g & 1) * pstride);
+            const uint4 B2 = (g & 1) ? make_uint4(0u, 0u, 0u, 0u) : lds128(pb + 2 * pstride);
+            const uint4 h0 = lds128(ub + g * kQ4KPitch), h1 = lds128(ub + (g + 8) * kQ4KPitch);
+            const float2 xa = S.xsx[seg * 8 + t], xb = S.xsx[seg * 8 + t + 4];
+            int c01[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, c2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 #pragma unroll
-                    for (int G = 0; G < 2; ++G) {
-                        // This lane's quants: chunk 2G + (t >> 1), bytes 16 (t & 1) .. +16;
-                        // low nibbles feed a0 / a1 (sub-block sb0), high nibbles a2 / a3 (sb0 + 1).
-                        const int aoff = 16 + 32 * (2 * G + (t >> 1)) + 16 * (t & 1);
-                        A0[G] = lds128(rg + aoff);
-                        A1[G] = lds128(rg8 + aoff);
-                        const int eoff = seg * 256 + 32 * (4 * G + 2 * (t >> 1)) + 16 * (t & 1);
-                        const uint8_t* zp = S.zero;
-                        Ba0[G] = lds128(sel0 ? S.planes + (g & 1) * Kp + eoff : zp);
-                        Ba1[G] = lds128(sel1 ? S.planes + (g & 1) * Kp + eoff + 32 : zp);
-                        Bb0[G] = lds128((sel0 && !(g & 1)) ? S.planes + 2 * Kp + eoff : zp);
-                        Bb1[G] = lds128((sel1 && !(g & 1)) ? S.planes + 2 * Kp + eoff + 32 : zp);
-                    }
-                    int ca[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, cbb[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+            for (int c = 0; c < 4; ++c) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(ub + ldsm_off + 32 * c, a0, a1, a2, a3);
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-#pragma unroll
-                        for (int G = 0; G < 2; ++G) {
-                            const uint32_t w0 = word(A0[G], s), w1 = word(A1[G], s);
-                            const uint32_t a0 = w0 & 0x0F0F0F0Fu, a2 = (w0 >> 4) & 0x0F0F0F0Fu;
-                            const uint32_t a1 = w1 & 0x0F0F0F0Fu, a3 = (w1 >> 4) & 0x0F0F0F0Fu;
-                            mma_u8s8(ca[G], a0, a1, a2, a3, word(Ba0[G], s), word(Ba1[G], s));
-                            mma_u8s8(cbb[G], a0, a1, a2, a3, word(Bb0[G], s), word(Bb1[G], s));
-                        }
-                    }
-                    // Lane (g, t) now holds sub-blocks j0 (G = 0) and j0 + 4 (G = 1):
-                    // ca[G] = {P0, P1} of row g (regs 0, 1) and row g+8 (regs 2, 3);
-                    // cbb[G][0] / cbb[G][2] = P2 of rows g / g+8.
-                    const float sx0 = S.sx[seg * 8 + j0], sx1 = S.sx[seg * 8 + j0 + 4];
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const uint4 h = half ? h1 : h0;
-                        const float d = f16_bits_to_f32(h.x & 0xFFFFu), dmin = f16_bits_to_f32(h.x >> 16);
-                        // scale_min (src/autograd2.rs:1075-1085), four 6-bit fields per word
-                        const uint32_t s_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
-                        const uint32_t s_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-                        const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-                        const float sc0 = byte_to_float(s_lo, jsel), mn0 = byte_to_float(m_lo, jsel);
-                        const float sc1 = byte_to_float(s_hi, jsel), mn1 = byte_to_float(m_hi, jsel);
-                        const int i0 = 2 * half;
-                        const float T0 = static_cast<float>(ca[0][i0] * 16384 + ca[0][i0 + 1] * 128 + cbb[0][i0]);
-                        const float T1 = static_cast<float>(ca[1][i0] * 16384 + ca[1][i0 + 1] * 128 + cbb[1][i0]);
-                        const float v = d * ((sc0 * T0 + sc1 * T1) * xsc) - dmin * (mn0 * sx0 + mn1 * sx1);
-                        if (half) vg8 = v;
-                        else vg = v;
-                    }
-                } else {
-                    const uint8_t* rg = sbuf + g * a.srow + u * 512 + 16 * t;
-                    const uint8_t* rg8 = rg + 8 * a.srow;
-                    const uint8_t* pbp = g < 3 ? S.planes + static_cast<size_t>(g) * Kp * 2 + seg * 512 + 16 * t : S.zero;
-                    const int pstep = g < 3 ? 64 : 0;
-                    const int valid = K - seg * 256;  // columns of this segment inside the row (multiple of 8)
-                    float c[4][4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) c[q][i] = 0.f;
-#pragma unroll
-                    for (int p = 0; p < 8; ++p) {
-                        uint4 A0 = lds128(rg + 64 * p), A1 = lds128(rg8 + 64 * p);
-                        const uint4 B = lds128(pbp + pstep * p);
-                        if (32 * p + 8 * t >= valid) A0 = A1 = make_uint4(0, 0, 0, 0);
-                        mma_bf16(c[(2 * p) & 3], A0.x, A1.x, A0.y, A1.y, B.x, B.y);
-                        mma_bf16(c[(2 * p + 1) & 3], A0.z, A1.z, A0.w, A1.w, B.z, B.w);
-                    }
-                    vg = ((c[0][0] + c[1][0]) + (c[2][0] + c[3][0])) + ((c[0][1] + c[1][1]) + (c[2][1] + c[3][1]));
-                    vg8 = ((c[0][2] + c[1][2]) + (c[2][2] + c[3][2])) + ((c[0][3] + c[1][3]) + (c[2][3] + c[3][3]));
-                }
-                vg += __shfl_xor_sync(0xffffffffu, vg, 1);
-                vg += __shfl_xor_sync(0xffffffffu, vg, 2);
-                vg8 += __shfl_xor_sync(0xffffffffu, vg8, 1);
-                vg8 += __shfl_xor_sync(0xffffffffu, vg8, 2);
-                if (t == 0) {
-                    pb[g * nseg + seg] = vg;
-                    pb[(g + 8) * nseg + seg] = vg8;
+                for (int hi = 0; hi < 2; ++hi) {
+                    const int j = 2 * c + hi;  // sub-block
+                    const int r = j & 3, set = j >> 2;
+                    const uint32_t m = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                    const bool own = q == r;
+                    const uint32_t b0 = own ? (set ? B01.z : B01.x) : 0u;
+                    const uint32_t b1 = own ? (set ? B01.w : B01.y) : 0u;
+                    const uint32_t e0 = own ? (set ? B2.z : B2.x) : 0u;
+                    const uint32_t e1 = own ? (set ? B2.w : B2.y) : 0u;
+                    mma_u8s8(c01[set], a0 & m, a1 & m, a2 & m, a3 & m, b0, b1);
+                    mma_u8s8(c2[set], a0 & m, a1 & m, a2 & m, a3 & m, e0, e1);
                 }
             }
-            // Count this warp's units of the tile; the warp that completes the
-            // tile sums its partials (fixed order) and runs the epilogue.
-            __syncwarp();
-            int last = 0;
-            if (lane == 0 && mine) {
-                __threadfence_block();
-                const uint32_t prev = atomicAdd(&S.tcnt[slot], static_cast<uint32_t>(mine));
-                last = prev + mine == static_cast<uint32_t>(nseg);
+            // Lane t: sub-blocks t (set 0) and t+4 (set 1); c01[.][0]/[1] = planes
+            // 0/1 of row g, [2]/[3] of row g+8; plane 2 sits in the even columns
+            // (c2[.][0] row g, c2[.][2] row g+8).
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const uint4 h = half ? h1 : h0;
+                const float d = f16_bits_to_f32(h.x & 0xFFFFu), dmin = f16_bits_to_f32(h.x >> 16);
+                // scale_min (src/autograd2.rs:1075-1085), four 6-bit fields per word
+                const uint32_t s_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
+                const uint32_t s_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+                const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+                const float sc0 = byte_to_float(s_lo, jsel), mn0 = byte_to_float(m_lo, jsel);
+                const float sc1 = byte_to_float(s_hi, jsel), mn1 = byte_to_float(m_hi, jsel);
+                const int i0 = 2 * half;
+                const float T0 = fmaf(static_cast<float>(c01[0][i0]), 16384.0f,
+                                      fmaf(static_cast<float>(c01[0][i0 + 1]), 128.0f, static_cast<float>(c2[0][i0])));
+                const float T1 = fmaf(static_cast<float>(c01[1][i0]), 16384.0f,
+                                      fmaf(static_cast<float>(c01[1][i0 + 1]), 128.0f, static_cast<float>(c2[1][i0])));
+                const float v = d * (sc0 * (T0 * xa.x) + sc1 * (T1 * xb.x)) - dmin * (mn0 * xa.y + mn1 * xb.y);
+                if (half) acc1 += v;
+                else acc0 += v;
             }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                __threadfence_block();
-                if constexpr (EPI == kEpiGeluPair) {
-                    if (lane < nr / 2) {
-                        float gsum = 0.f, usum = 0.f;
-                        for (int s2 = 0; s2 < nseg; ++s2) gsum += pb[(2 * lane) * nseg + s2];
-                        for (int s2 = 0; s2 < nseg; ++s2) usum += pb[(2 * lane + 1) * nseg + s2];
-                        a.y[(r0 >> 1) + lane] = __fmul_rn(gelu_tanh_dev(gsum), usum);
-                    }
-                } else {
-                    if (lane < nr) {
-                        float v = 0.f;
-                        for (int s2 = 0; s2 < nseg; ++s2) v += pb[lane * nseg + s2];
-                        a.y[r0 + lane] = v;
-                        if constexpr (EPI == kEpiArgmax) {
-                            if (v > best_v || (v == best_v && r0 + lane > best_i)) {
-                                best_v = v;
-                                best_i = r0 + lane;
-                            }
-                        }
-                    }
+        } else {
+            // BF16: lanes g < 3 feed B column g (plane g); the rest feed zeros.
+            const uint8_t* pb = S.planes + (g < 3 ? g : 0) * pstride + seg * (kBF16SegCols * 2) + t * 8;
+            float c[4][4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) c[k][e] = 0.f;
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(ub + ldsm_off + 32 * s, a0, a1, a2, a3);
+                const uint2 b = g < 3 ? lds64(pb + 32 * s) : make_uint2(0u, 0u);
+                mma_bf16(c[s & 3], a0, a1, a2, a3, b.x, b.y);
+            }
+            acc0 += ((c[0][0] + c[1][0]) + (c[2][0] + c[3][0])) + ((c[0][1] + c[1][1]) + (c[2][1] + c[3][1]));
+            acc1 += ((c[0][2] + c[1][2]) + (c[2][2] + c[3][2])) + ((c[0][3] + c[1][3]) + (c[2][3] + c[3][3]));
+        }
+        ++pu;
+        done = i + 1;
+        // Release the buffer to the next copy of this warp.
+        __syncwarp();
+        if (lane == 0 && issued < n) {
+            fence_proxy_async_smem();
+            issue(jb);
+        }
+        if (++jb == NB) {
+            jb = 0;
+            ph ^= 1u;
+        }
+        const bool tile_end = ++seg == nseg;
+        if (tile_end || i == n - 1) {
+            // Row sums of this piece: quad reduction, then lane L < 16 takes row L.
+            float s0 = acc0 + __shfl_xor_sync(0xffffffffu, acc0, 1);
+            s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+            float s1 = acc1 + __shfl_xor_sync(0xffffffffu, acc1, 1);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+            const float ra = __shfl_sync(0xffffffffu, s0, 4 * (lane & 7));
+            const float rb = __shfl_sync(0xffffffffu, s1, 4 * (lane & 7));
+            const float rowv = (lane & 8) ? rb : ra;
+            const int64_t r0 = static_cast<int64_t>(tile) * kTile;
+            if (pu == nseg) {
+                emit_rows(r0, rowv);
+            } else {
+                // Lanes 16..31 (row = lane - 16) publish the piece: lane 0 has this
+                // warp's copies in flight, and a fence there would wait for them.
+                const int slot = tile == first_tile ? 0 : 1;
+                const bool pub = lane >= kTile;
+                const float rv = __shfl_sync(0xffffffffu, rowv, lane & (kTile - 1));
+                if (pub) {
+                    a.part[(static_cast<int64_t>(gw) * 2 + slot) * kTile + (lane - kTile)] = rv;
+                    __threadfence();
                 }
                 __syncwarp();
-                if (lane == 0) S.tcnt[slot] = 0u;
+                int last = 0;
+                if (lane == kTile)
+                    last = atomicAdd(&a.tile_cnt[tile], static_cast<uint32_t>(pu)) + static_cast<uint32_t>(pu) ==
+                           static_cast<uint32_t>(nseg);
+                last = __shfl_sync(0xffffffffu, last, kTile);
+                if (last) {
+                    if (pub) __threadfence();
+                    const uint32_t u0 = tile * nseg;
+                    const uint32_t w_first = sp.owner(u0), w_last = sp.owner(u0 + nseg - 1);
+                    // Sum the pieces in warp order, eight loads in flight at a time.
+                    float v = 0.f;
+                    for (uint32_t wb = w_first; wb <= w_last; wb += 8) {
+                        float pv[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const uint32_t w = wb + k;
+                            pv[k] = 0.f;
+                            if (w <= w_last && pub) {
+                                const uint32_t s_w = sp.start(w);
+                                // a warp that began in an earlier tile keeps this one in slot 1
+                                if (sp.start(w + 1) > s_w)
+                                    pv[k] = ldcg_f32(a.part + (static_cast<int64_t>(w) * 2 + (s_w < u0 ? 1 : 0)) * kTile +
+                                                     (lane - kTile));
+                            }
+                        }
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) v += pv[k];
+                    }
+                    emit_rows(r0, __shfl_sync(0xffffffffu, v, (lane & (kTile - 1)) + kTile));
+                    if (lane == kTile) a.tile_cnt[tile] = 0u;
+                }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.empty[b]);
+            acc0 = acc1 = 0.f;
+            pu = 0;
+            if (tile_end) {
+                seg = 0;
+                ++tile;
+            }
         }
     }
-    __syncthreads();
 
-    if (S.flags[0]) {
-        // A bounded wait gave up: record it, then wait (bounded) for every copy
-        // this CTA issued before letting its shared memory go.
-        if (tid == 0) {
-            if (a.err) atomicExch(a.err, kErrMbarTimeout);
-            const int issued = S.flags[1];
-            for (int st = max(0, issued - a.nbuf); st < issued; ++st) {
-                if (!mbar_wait(&S.full[st % a.nbuf], static_cast<uint32_t>(st / a.nbuf) & 1u)) break;
-            }
+    if (failed) {
+        // A bounded wait gave up: record it, then wait (bounded) for the copies
+        // this warp still has in flight before its shared memory goes away.
+        if (lane == 0) {
+            atomicExch(&S.flags[0], 1);
+            for (int k = done; k < issued; ++k)
+                if (!mbar_wait(&full[k % NB], static_cast<uint32_t>(k / NB) & 1u)) break;
         }
-        __syncthreads();
+        __syncwarp();
+    }
+    __syncthreads();
+    if (S.flags[0]) {
+        if (tid == 0 && a.err) atomicExch(a.err, kErrMbarTimeout);
         return;
     }
 
@@ -622,9 +723,9 @@ __global__ void __launch_bounds__(544) gemv_kernel(const GemvArgs a, const __gri
             const volatile int32_t* vi = a.am_idx;
             float bv = vv[0];
             int32_t bi = vi[0];
-            for (unsigned q = 1; q < gridDim.x; ++q) {
-                const float v = vv[q];
-                const int32_t i = vi[q];
+            for (unsigned k = 1; k < gridDim.x; ++k) {
+                const float v = vv[k];
+                const int32_t i = vi[k];
                 if (v > bv || (v == bv && i > bi)) {
                     bv = v;
                     bi = i;
@@ -665,15 +766,9 @@ bool dispatch(int kind, int pro, int epi, F&& f) {
     return false;
 }
 
-// Largest divisor of n that is <= cap, or cap itself when that divisor would
-// leave stages less than half full.
-int pick_spst(int n, int cap) {
-    if (n <= cap) return n;
-    int best = 1;
-    for (int d = 1; d <= cap; ++d)
-        if (n % d == 0) best = d;
-    return best * 2 >= cap ? best : cap;
-}
+// Dynamic shared memory a CTA may take: the 227 KiB opt-in limit less 1 KiB,
+// which leaves room for the kernels' own static shared variables.
+constexpr size_t kSmemLimit = 226 * 1024;
 
 }  // namespace
 
@@ -684,52 +779,58 @@ void gemv_prepare() {
         for (int pr : {kProPlain, kProResidNorm, kProEmbedNorm})
             for (int ep : {kEpiPlain, kEpiGeluPair, kEpiArgmax})
                 dispatch(kd, pr, ep, [&](auto k) {
-                    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+                    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
                 });
-    cudaGetLastError();
+    cudaGetLastError();  // a failure here surfaces as a launch error
 }
 
-GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int epilogue, int num_sms,
-                   int max_ctas_per_sm) {
+GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int epilogue, int num_sms, int ctas_per_sm) {
     GemvPlan p;
-    const int nseg = (K + 255) / 256;
-    const int seg_bytes = kind == kQ4K ? 144 : 512;
-    // A stage row (plus padding) is one TMA box row: at most 256 8-byte elements.
-    const int spst = pick_spst(nseg, kind == kQ4K ? 10 : 3);
-    int srow = (spst * seg_bytes + 15) & ~15;
-    srow += ((64 - srow % 128) + 128) % 128;  // = 64 (mod 128): conflict-free fragment loads
-    p.spst = spst;
-    p.srow = srow;
-    p.stage_bytes = kTile * srow;
-    p.warps = 16 + 1;  // compute warps + the copy-producer warp
-    const bool need_xs = prologue != kProPlain;
-    if (need_xs && K / 4 > kMaxV * p.warps * 32) {
-        p.warps = 0;  // norm prologue holds at most kMaxV float4 per thread
+    (void)pair;  // tiles are 16 rows, so (gate, up) pairs never straddle tiles
+    (void)epilogue;
+    if (rows <= 0 || K <= 0 || num_sms <= 0) return p;
+    if (kind == kQ4K ? (K % 256) != 0 : (K % 8) != 0) return p;
+    const int seg_cols = kind == kQ4K ? kQ4KSegCols : kBF16SegCols;
+    const int nseg = (K + seg_cols - 1) / seg_cols;
+    const int cps = ctas_per_sm >= 2 ? 2 : 1;
+    p.unit_bytes = kind == kQ4K ? kQ4KUnit : kBF16Unit;
+    p.box_x = kind == kQ4K ? kQ4KPitch / 8 : kBF16Pitch / 8;
+    p.warps = cps == 2 ? kMaxWarps / 2 : kMaxWarps;
+    const int nthr = p.warps * 32;
+    if (prologue != kProPlain && nseg * seg_cols > kMaxV8 * 8 * nthr) {
+        p.warps = 0;  // the norm prologues hold at most kMaxV8 chunks of 8 per thread
         return p;
     }
-    // As many stage buffers as fit next to the rest (one CTA per SM).
-    const size_t budget = 200 * 1024;
-    p.x_smem = static_cast<size_t>(K) * 4 <= 48 * 1024 ? 1 : 0;
-    p.nbuf = 2;
-    size_t smem = carve(nullptr, kind, K, nseg, p.nbuf, p.stage_bytes, need_xs, p.x_smem, nullptr);
-    while (p.nbuf < kMaxNbuf && smem + p.stage_bytes <= budget) {
-        ++p.nbuf;
-        smem = carve(nullptr, kind, K, nseg, p.nbuf, p.stage_bytes, need_xs, p.x_smem, nullptr);
+    // Deepest ring that fits the CTA's share of shared memory.
+    const size_t budget = cps == 2 ? kSmemLimit / 2 : kSmemLimit;
+    p.nb = 0;
+    size_t smem = 0;
+    for (int nb = kMaxNb; nb >= 2; --nb) {
+        smem = carve(nullptr, kind, K, nseg, p.warps, nb, p.unit_bytes, prologue, nullptr) + 128;
+        if (smem <= budget) {
+            p.nb = nb;
+            break;
+        }
     }
-    if (smem > 220 * 1024) {
+    if (p.nb == 0) {
         p.warps = 0;  // does not fit: the caller reports RT_E_SHAPE
         return p;
     }
     p.smem = smem;
-    int occ = 1;
-    dispatch(kind, prologue, epilogue, [&](auto k) {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, p.warps * 32, smem) != cudaSuccess) occ = 1;
-    });
-    cudaGetLastError();
-    const int cps = std::max(1, std::min(occ, max_ctas_per_sm));
-    (void)pair;  // tiles are 16 rows, so (gate, up) pairs never straddle CTAs
-    const int64_t tiles = (rows + kTile - 1) / kTile;
-    p.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(num_sms) * cps, tiles)));
+    // Every warp gets at least one unit; the split indexes warps with 16 bits
+    // and units with 31.  One CTA per SM either way: a half-size CTA leaves the
+    // other half of the SM to the next kernel of a PDL chain.
+    const int64_t U = ((rows + kTile - 1) / kTile) * nseg;
+    if (U >= (int64_t{1} << 31)) {
+        p.warps = 0;
+        return p;
+    }
+    int64_t grid = num_sms;
+    grid = std::min<int64_t>(grid, (U + p.warps - 1) / p.warps);
+    grid = std::max<int64_t>(1, std::min<int64_t>(grid, 65535 / p.warps));
+    p.grid = static_cast<int>(grid);
+    p.part_floats = grid * p.warps * 2 * kTile;
+    p.cnt_words = (rows + kTile - 1) / kTile;
     return p;
 }
 
@@ -745,11 +846,10 @@ bool gemv_make_tmap(int kind, const void* w, int64_t rows, int K, const GemvPlan
         }
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
-    const int nseg = (K + 255) / 256;
-    const uint64_t row_bytes = kind == kQ4K ? static_cast<uint64_t>(nseg) * 144 : static_cast<uint64_t>(K) * 2;
+    const uint64_t row_bytes = kind == kQ4K ? static_cast<uint64_t>(K / 256) * 144 : static_cast<uint64_t>(K) * 2;
     const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(p.srow / 8), static_cast<cuuint32_t>(kTile)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(p.box_x), static_cast<cuuint32_t>(kTile)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -759,15 +859,10 @@ bool gemv_make_tmap(int kind, const void* w, int64_t rows, int K, const GemvPlan
 
 cudaError_t gemv_launch(int kind, int prologue, int epilogue, GemvArgs a, const CUtensorMap& tmap, const GemvPlan& p,
                         cudaStream_t s, bool pdl) {
-    a.nseg = (a.K + 255) / 256;
-    a.seg_bytes = kind == kQ4K ? 144 : 512;
-    a.row_bytes = kind == kQ4K ? a.nseg * 144 : a.K * 2;
-    a.spst = p.spst;
-    a.srow = p.srow;
-    a.nbuf = p.nbuf;
-    a.stage_bytes = p.stage_bytes;
-    a.pair = epilogue == kEpiGeluPair ? 2 : 1;
-    a.x_smem = p.x_smem;
+    const int seg_cols = kind == kQ4K ? kQ4KSegCols : kBF16SegCols;
+    a.nseg = (a.K + seg_cols - 1) / seg_cols;
+    a.nb = p.nb;
+    a.unit_bytes = p.unit_bytes;
     cudaError_t err = cudaErrorInvalidValue;
     // The dynamic shared-memory limit is raised by gemv_prepare (not here: this
     // function also runs under stream capture).

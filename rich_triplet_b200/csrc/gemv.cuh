@@ -1,11 +1,11 @@
-// gemv.cuh -- row-streaming GEMV for Q4_K and BF16 weight matrices on the
-// tensor cores (mma.sync), for sm_100a.
+// gemv.cuh -- weight-streaming GEMV for Q4_K and BF16 matrices on the sm_100a
+// tensor cores (mma.sync).
 //
 // y[r] = sum_k W[r, k] * x[k] for a [rows, K] row-major matrix whose rows are
 // contiguous in HBM.  One kernel serves the standalone GEMV entry points
 // (rt_gemv_q4k / rt_gemv_bf16) and every projection of the fused decode step,
-// where a prologue builds x in shared memory (RMSNorm of the residual stream,
-// embedding lookup) and an epilogue fuses the GELU gate or the greedy argmax.
+// where a prologue builds x (RMSNorm of the residual stream, embedding lookup)
+// and an epilogue fuses the GELU gate or the greedy argmax.
 #pragma once
 
 #include <stdint.h>
@@ -32,19 +32,16 @@ enum Epilogue : int {
 };
 
 struct GemvArgs {
-    const uint8_t* w;   // weight rows, row_bytes each, 16-byte aligned
-    int64_t rows;       // rows of W computed by this launch
-    int32_t K;          // columns
-    int32_t nseg;       // ceil(K / 256): 256-column segments per row
-    int32_t seg_bytes;  // 144 (Q4_K block) or 512 (BF16)
-    int32_t row_bytes;  // bytes of one row
-    // geometry chosen by gemv_plan()
-    int32_t spst;         // 256-column segments per stage (a stage is 16 rows x spst segments)
-    int32_t srow;         // shared-memory row stride of a stage, = 64 mod 128 bytes
-    int32_t nbuf;         // shared-memory stage buffers
-    int32_t stage_bytes;  // bytes of one stage buffer (16 * srow)
-    int32_t pair;         // 2 for kEpiGeluPair (row ranges start on even rows)
-    int32_t x_smem;       // plain prologue: 1 = copy x into shared memory first, 0 = read it in place
+    const uint8_t* w;  // weight rows, 16-byte aligned
+    int64_t rows;      // rows of W
+    int32_t K;         // columns
+    // geometry (filled by gemv_launch from the plan)
+    int32_t nseg;        // column segments per row (256 Q4_K / 128 BF16 columns each)
+    int32_t nb;          // copies in flight per warp
+    int32_t unit_bytes;  // shared-memory bytes of one unit (16 rows x one segment, padded)
+    // split-tile scratch: tiles shared by several warps are summed here
+    float* part;        // [gridDim.x * warps * 2 * 16] partial row sums
+    uint32_t* tile_cnt; // [ceil(rows / 16)] units arrived per split tile; zero before, zero after
     // prologue inputs
     const float* x;
     const float* src;
@@ -68,27 +65,29 @@ struct GemvArgs {
 };
 
 struct GemvPlan {
-    int warps = 0;
-    int spst = 0;
-    int srow = 0;
-    int nbuf = 0;
-    int stage_bytes = 0;
-    int x_smem = 1;
+    int warps = 0;       // warps per CTA (0: shape not supported)
+    int nb = 0;          // copies in flight per warp
+    int unit_bytes = 0;  // shared-memory bytes of one unit
+    int box_x = 0;       // TMA box inner extent, 8-byte elements
     int grid = 0;
     size_t smem = 0;
+    int64_t part_floats = 0;  // split-tile scratch this plan needs (GemvArgs::part)
+    int64_t cnt_words = 0;    // and GemvArgs::tile_cnt, zeroed once by the owner
 };
 
 // Raise the dynamic shared-memory limit of every kernel instantiation on the
 // current device.  Call once per device before planning or capturing.
 void gemv_prepare();
 
-// Choose warps / stage geometry / grid for a [rows, K] GEMV.
+// Choose warps / ring depth / grid for a [rows, K] GEMV: one CTA per SM.
+// ctas_per_sm is 1 (the CTA takes the whole SM) or 2 (a half-size CTA, so a
+// CTA of the next kernel in a PDL chain can be resident beside it).
 GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int epilogue, int num_sms,
-                   int max_ctas_per_sm);
+                   int ctas_per_sm);
 
 // TMA descriptor of a [rows, K] weight matrix at `w` for plan `p`: 8-byte
-// elements, box = one stage (16 rows x srow bytes; bytes past the row end and
-// rows past the matrix read as zero).  Returns false if the driver refuses.
+// elements, box = one unit (box_x elements x 16 rows; bytes past the row end
+// and rows past the matrix read as zero).  Returns false if the driver refuses.
 bool gemv_make_tmap(int kind, const void* w, int64_t rows, int K, const GemvPlan& p, CUtensorMap* out);
 
 // Fill the geometry fields of `a` from `p` and launch.  `pdl` attaches the

@@ -22,6 +22,11 @@ struct rt_ctx {
     float* scratch = nullptr;
     size_t scratch_floats = 0;
     int* d_err = nullptr;  // device error word written by kernels
+    // Split-tile scratch of the standalone GEMVs (counters zeroed on allocation;
+    // every completed launch leaves them at zero).
+    float* gemv_part = nullptr;
+    uint32_t* gemv_cnt = nullptr;
+    int64_t gemv_part_floats = 0, gemv_cnt_words = 0;
 };
 
 struct rt_w {

@@ -17,16 +17,20 @@
 namespace {
 
 constexpr int kSlots = RT_ARGMAX_STATIC_SLOTS;
+constexpr int kWarpsPerCta = 16;                             // the GEMV's largest CTA
+constexpr int64_t kMaxTiles = RT_ARGMAX_STATIC_MAX_ROWS / 16;  // 16-row tiles
 constexpr int kMaxDevices = 64;
 
 struct ArgmaxScratch {
-    float val[kSlots];    // per-CTA best logit
-    int32_t idx[kSlots];  // per-CTA best row
-    uint32_t counter;     // CTAs arrived; zero when a launch starts
+    float val[kSlots];                       // per-CTA best logit
+    int32_t idx[kSlots];                     // per-CTA best row
+    uint32_t counter;                        // CTAs arrived; zero when a launch starts
+    uint32_t tile_cnt[kMaxTiles];            // split-tile unit counters; zero when a launch starts
+    float part[kSlots * kWarpsPerCta * 32];  // split-tile partial row sums
 };
 
 // Zero-initialised at module load; every launch that completes leaves
-// `counter` at zero again.
+// `counter` and `tile_cnt` at zero again.
 static __device__ __align__(256) ArgmaxScratch g_argmax_scratch;
 
 struct DeviceSetup {
@@ -81,9 +85,9 @@ extern "C" int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int c
         return report(errbuf, errlen, RT_E_INVAL, "rt_gemv_bf16_argmax_static: null argument");
     if ((reinterpret_cast<uintptr_t>(w_dev) & 15) || (reinterpret_cast<uintptr_t>(x_dev) & 15))
         return report(errbuf, errlen, RT_E_INVAL, "rt_gemv_bf16_argmax_static: w and x must be 16-byte aligned");
-    if (rows <= 0 || rows > INT32_MAX)
-        return report(errbuf, errlen, RT_E_SHAPE, "rt_gemv_bf16_argmax_static: rows %lld outside [1, 2^31 - 1]",
-                      static_cast<long long>(rows));
+    if (rows <= 0 || rows > RT_ARGMAX_STATIC_MAX_ROWS)
+        return report(errbuf, errlen, RT_E_SHAPE, "rt_gemv_bf16_argmax_static: rows %lld outside [1, %d]",
+                      static_cast<long long>(rows), RT_ARGMAX_STATIC_MAX_ROWS);
     if (cols <= 0 || cols % 8 || cols > (1 << 20))
         return report(errbuf, errlen, RT_E_SHAPE,
                       "rt_gemv_bf16_argmax_static: cols %d must be a positive multiple of 8, at most 2^20", cols);
@@ -98,10 +102,11 @@ extern "C" int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int c
     int rc = setup_device(dev, &s, errbuf, errlen);
     if (rc != RT_OK) return rc;
 
-    const rt::GemvPlan p = rt::gemv_plan(rt::kBF16, rows, cols, 1, rt::kProPlain, rt::kEpiArgmax, s.num_sms, 2);
+    const rt::GemvPlan p = rt::gemv_plan(rt::kBF16, rows, cols, 1, rt::kProPlain, rt::kEpiArgmax, s.num_sms, 1);
     if (p.warps == 0)
         return report(errbuf, errlen, RT_E_SHAPE, "rt_gemv_bf16_argmax_static: no launch geometry for cols %d", cols);
-    if (p.grid > kSlots)
+    if (p.grid > kSlots || p.warps > kWarpsPerCta || p.cnt_words > kMaxTiles ||
+        p.part_floats > int64_t{kSlots} * kWarpsPerCta * 32)
         return report(errbuf, errlen, RT_E_SHAPE,
                       "rt_gemv_bf16_argmax_static: launch needs %d argmax slots, the static scratch holds %d", p.grid,
                       kSlots);
@@ -119,6 +124,8 @@ extern "C" int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int c
     a.am_val = reinterpret_cast<float*>(base + offsetof(ArgmaxScratch, val));
     a.am_idx = reinterpret_cast<int32_t*>(base + offsetof(ArgmaxScratch, idx));
     a.am_counter = reinterpret_cast<uint32_t*>(base + offsetof(ArgmaxScratch, counter));
+    a.tile_cnt = reinterpret_cast<uint32_t*>(base + offsetof(ArgmaxScratch, tile_cnt));
+    a.part = reinterpret_cast<float*>(base + offsetof(ArgmaxScratch, part));
     a.token_out = token_dev;
     e = rt::gemv_launch(rt::kBF16, rt::kProPlain, rt::kEpiArgmax, a, tmap, p, static_cast<cudaStream_t>(stream), false);
     if (e != cudaSuccess)

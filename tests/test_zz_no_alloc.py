@@ -76,7 +76,7 @@ def test_static_argmax_rejects_bad_arguments():
     assert rc == RT_E_INVAL and "null" in msg
     rc, msg = _static(w.data_ptr(), 16, 250, x, y, tok)
     assert rc == RT_E_SHAPE and "multiple of 8" in msg
-    rc, msg = _static(w.data_ptr(), 1 << 31, 256, x, y, tok)
+    rc, msg = _static(w.data_ptr(), (1 << 20) + 1, 256, x, y, tok)
     assert rc == RT_E_SHAPE and "rows" in msg
     rc, msg = _static(w.data_ptr() + 2, 16, 256, x, y, tok)
     assert rc == RT_E_INVAL and "aligned" in msg
