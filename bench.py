@@ -44,6 +44,9 @@ def parse():
     p.add_argument("--layers", type=int, default=34, help="model depth (34 = Gemma 3 4B)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-steps", type=int, default=3)
+    p.add_argument("--prompt", type=int, default=PROMPT,
+                   help="prompt tokens prefilled before the timed steps (512 = BASELINE config 1; "
+                        "shorter only for profiling)")
     return p.parse_args()
 
 
@@ -355,7 +358,9 @@ def run_ours(args):
 
 
 def main():
+    global PROMPT
     args = parse()
+    PROMPT = args.prompt
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -55,6 +55,7 @@ namespace {
 constexpr int kTile = 16;
 constexpr int kMaxWarps = 16;
 constexpr int kMaxNb = 8;
+constexpr int kCopiesInFlight = 32;  // per SM
 constexpr int kMaxV8 = 4;  // 8-element chunks of x per thread held by the norm prologues
 constexpr int kQ4KSegCols = 256;
 constexpr int kBF16SegCols = 128;
@@ -801,11 +802,13 @@ GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int ep
         p.warps = 0;  // the norm prologues hold at most kMaxV8 chunks of 8 per thread
         return p;
     }
-    // Deepest ring that fits the CTA's share of shared memory.
+    // Ring depth: about 32 TMA copies in flight per SM stream fastest (more
+    // outstanding copies slow the stream down), within the CTA's share of
+    // shared memory.
     const size_t budget = cps == 2 ? kSmemLimit / 2 : kSmemLimit;
     p.nb = 0;
     size_t smem = 0;
-    for (int nb = kMaxNb; nb >= 2; --nb) {
+    for (int nb = std::max(2, std::min(kMaxNb, kCopiesInFlight / p.warps)); nb >= 2; --nb) {
         smem = carve(nullptr, kind, K, nseg, p.warps, nb, p.unit_bytes, prologue, nullptr) + 128;
         if (smem <= budget) {
             p.nb = nb;
