@@ -1,45 +1,6 @@
-// gemv.cu -- Q4_K / BF16 GEMV on the sm_100a tensor cores (mma.sync), one
-// weight stream per warp.
-//
-// Work split.  The matrix is cut into units of 16 rows x one column segment
-// (256 Q4_K columns = one 144-byte block per row, or 128 BF16 columns).  Units
-// are numbered tile-major (a tile is 16 rows) and every warp of the grid takes
-// one contiguous, equal share of that sequence, so all warps stream the same
-// number of bytes whatever the shape.  A warp copies its units HBM -> shared
-// memory itself: lane 0 issues one 2-D TMA tensor copy per unit (8-byte
-// elements, box = unit width x 16 rows, no multicast) into a private ring of
-// `nb` buffers, each completed on its own mbarrier (bounded waits).  The first
-// copies are issued before griddepcontrol.wait, so under programmatic dependent
-// launch the weight stream starts while the previous kernel drains.  No warp
-// ever waits for another warp inside the stream.
-//
-// Row sums.  A warp accumulates the units of one tile in registers.  A tile it
-// covers whole goes straight to the epilogue; a tile shared with neighbouring
-// warps (at most two per warp) leaves a 16-row partial in global scratch, and
-// the warp that brings the tile's unit count to a full row (an atomic counter
-// per split tile) adds the partials in warp order -- a fixed order, so results
-// are deterministic -- and runs the epilogue (store, GELU gate, greedy argmax).
-//
-// Q4_K (block layout src/autograd2.rs:1003-1042; Q4KMat::dot_row
-// src/autograd2.rs:1637-1702).  Per 32-column sub-block j of a row,
-//     dot_j = d * sc_j * sum(q * x) - dmin * m_j * sum(x).
-// ldmatrix hands each lane the A fragment of one 32-byte quant chunk c for 16
-// rows; a byte mask keeps the low nibbles (sub-block 2c) or the high nibbles
-// (sub-block 2c+1, as 16 q) as the u8 A operand of mma.m16n8k32.u8.s8.  x is
-// split once per launch, per sub-block, into three int8 planes
-// x = s * (p0 + p1/128 + p2/16384) (|error| <= s/32768, s = max|x|/127 over the
-// sub-block), the s8 B operand.  The MMA of sub-block j puts planes 0/1 in B
-// columns 2(j&3), 2(j&3)+1 (and plane 2 in column 2(j&3) of a second MMA), zero
-// elsewhere, so lane t of every lane quad ends up holding the three plane sums
-// of sub-blocks t and t+4 for two rows, and all 32 lanes share the scale
-// epilogue.
-//
-// BF16 (MatBf16::dot_row, src/autograd2.rs:861-888).  The weights, loaded by
-// ldmatrix, are the A operand of mma.m16n8k16.bf16; x is split exactly into
-// three bf16 planes x = hi + mid + lo (B columns 0..2), so the f32 sum of the
-// three product columns is the f32 dot product.  The unit box is 272 bytes wide
-// (128 columns + 16 bytes of the next unit), which puts consecutive rows 16
-// bytes apart modulo 128 and keeps ldmatrix free of bank conflicts.
+// gemv.cu -- the standalone Q4_K / BF16 GEMV kernel (one job per launch) and
+// its host-side planning.  The streaming, the tensor-core arithmetic and the
+// epilogues live in gemv_core.cuh, shared with the decode-step kernel.
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
 
 #include <algorithm>
@@ -47,106 +8,33 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
+#include "gemv_core.cuh"
 
 namespace rt {
 
 namespace {
 
-constexpr int kTile = 16;
-constexpr int kMaxWarps = 16;
+using namespace gcore;
+
 constexpr int kMaxNb = 8;
 constexpr int kCopiesInFlight = 32;  // per SM
-constexpr int kMaxV8 = 4;  // 8-element chunks of x per thread held by the norm prologues
-constexpr int kQ4KSegCols = 256;
-constexpr int kBF16SegCols = 128;
-constexpr int kQ4KPitch = 144;   // one Q4_K block per row of a unit
-constexpr int kBF16Pitch = 272;  // 128 BF16 columns + 16 bytes
-constexpr int kQ4KUnit = kTile * kQ4KPitch;
-constexpr int kBF16Unit = kTile * kBF16Pitch;
-
-__device__ __forceinline__ float gelu_tanh_dev(float x) {
-    // TensorNode::gelu_tanh (src/autograd2.rs:3082-3091): x*0.5*(1+tanh(s*(x+c*x^3))),
-    // evaluated without FMA contraction in the reference's operation order.
-    const float kS = 0.7978845608028654f, kC = 0.044715f;
-    float x3 = __fmul_rn(__fmul_rn(__fmul_rn(kC, x), x), x);
-    float inner = __fmul_rn(kS, __fadd_rn(x, x3));
-    return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, tanhf(inner)));
-}
-
-// Byte selected by `sel` (0x7540 | b) of v, as an exact float.
-__device__ __forceinline__ float byte_to_float(uint32_t v, uint32_t sel) {
-    return __uint_as_float(__byte_perm(v, 0x4B000000u, sel)) - 8388608.0f;
-}
-
-__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
-__device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
-
-__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Round to the nearest integer (ties to even) without the XU pipe:
-// adding 1.5 * 2^23 leaves the integer in the low mantissa bits (|y| < 2^22).
-__device__ __forceinline__ int round_magic(float y, float* yr) {
-    const float m = __fadd_rn(y, 12582912.0f);
-    *yr = __fsub_rn(m, 12582912.0f);
-    return __float_as_int(m) - 0x4B400000;
-}
-
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-    return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
-           ((static_cast<uint32_t>(c) & 0xFFu) << 16) | (static_cast<uint32_t>(d) << 24);
-}
-
-// f32 -> bf16 bits, round to nearest even (finite inputs).
-__device__ __forceinline__ uint32_t bf16_rne(float x) {
-    const uint32_t u = __float_as_uint(x);
-    return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
-}
-
-__device__ __forceinline__ float ldcg_f32(const float* p) {
-    float v;
-    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Shared-memory plane layout.
-//  Q4_K: plane p (0..2) at p * pstride bytes; per 256-column segment 256 bytes,
-//  ordered so that lane t of the quad feeding B column pair r gets, in one
-//  16-byte load, its MMA fragments of sub-blocks r and r+4:
-//      byte r*64 + t*16 + (j>>2)*8 + (e>=16)*4 + (e&3) holds element e of
-//      sub-block j (r = j&3, t = (e&15)>>2).
-//  BF16: plane p (hi, mid, lo) at p * pstride bytes, u16 elements; per 16
-//  columns, lane t's B fragment (columns 2t, 2t+1, 8+2t, 9+2t) is 8 bytes at 8t.
-__host__ __device__ inline int q4k_pstride(int Kp) { return Kp + 64; }       // = 64 mod 128: no bank conflicts
-__host__ __device__ inline int bf16_pstride(int Kp) { return Kp * 2 + 32; }  // = 32 mod 128
 
 struct Smem {
-    uint64_t* full;   // [warps][nb] unit landed
-    uint64_t* pbar;   // norm weights landed
-    float* red;       // [32]
-    int* flags;       // [4]: 0 = a wait gave up
-    float* bv;        // [32] per-warp argmax value
-    long long* bi;    // [32] per-warp argmax row
-    float* gpost;     // [K] post-norm weight (residual-norm prologue)
-    float* gpre;      // [K] pre-norm weight (norm prologues)
-    uint8_t* planes;  // x planes, layout above
-    float2* xsx;      // Q4_K: [Kp/32] {value of one unit of the plane integer (/16 for odd sub-blocks), sum of x}
-    uint8_t* ring;    // [warps][nb][unit_bytes]
+    uint64_t* full;  // [warps][nb] unit landed
+    uint64_t* pbar;  // norm weights landed
+    float* red;      // [32]
+    int* flags;      // [4]: 0 = a wait gave up, 1 = last CTA (argmax)
+    float* bv;       // [32] per-warp argmax value
+    long long* bi;   // [32] per-warp argmax row
+    Job* job;
+    float* gpost;    // [K] post-norm weight (residual-norm prologue)
+    float* gpre;     // [K] pre-norm weight (norm prologues)
+    uint8_t* planes;
+    float2* xsx;
+    uint8_t* ring;   // [warps][nb][unit_bytes]
 };
 
-__host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg, int warps, int nb, int unit_bytes,
-                                        int pro, Smem* S) {
+__host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg, int warps, int nb, int pro, Smem* S) {
     size_t off = 0;
     auto take = [&](size_t bytes, size_t align) -> uint8_t* {
         off = (off + align - 1) / align * align;
@@ -154,20 +42,19 @@ __host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg
         off += bytes;
         return p;
     };
-    const int Kp = nseg * (kind == kQ4K ? kQ4KSegCols : kBF16SegCols);
+    const int Kp = nseg * seg_cols(kind);
     uint8_t* full = take(sizeof(uint64_t) * warps * nb, 16);
     uint8_t* pbar = take(sizeof(uint64_t), 16);
     uint8_t* red = take(32 * 4, 16);
     uint8_t* flags = take(4 * 4, 16);
     uint8_t* bv = take(4 * 32, 16);
     uint8_t* bi = take(8 * 32, 16);
+    uint8_t* job = take(sizeof(Job), 16);
     uint8_t* gpost = take(pro == kProResidNorm ? sizeof(float) * K : 0, 16);
     uint8_t* gpre = take(pro != kProPlain ? sizeof(float) * K : 0, 16);
-    uint8_t* planes = take(kind == kQ4K ? 3 * static_cast<size_t>(q4k_pstride(Kp))
-                                        : 3 * static_cast<size_t>(bf16_pstride(Kp)),
-                           128);
-    uint8_t* xsx = take(kind == kQ4K ? sizeof(float2) * (Kp / 32) : 0, 16);
-    uint8_t* ring = take(static_cast<size_t>(warps) * nb * unit_bytes, 128);
+    uint8_t* planes = take(planes_bytes(kind, Kp), 128);
+    uint8_t* xsx = take(xsx_bytes(kind, Kp), 16);
+    uint8_t* ring = take(static_cast<size_t>(warps) * nb * unit_bytes(kind), 128);
     if (S) {
         S->full = reinterpret_cast<uint64_t*>(full);
         S->pbar = reinterpret_cast<uint64_t*>(pbar);
@@ -175,6 +62,7 @@ __host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg
         S->flags = reinterpret_cast<int*>(flags);
         S->bv = reinterpret_cast<float*>(bv);
         S->bi = reinterpret_cast<long long*>(bi);
+        S->job = reinterpret_cast<Job*>(job);
         S->gpost = reinterpret_cast<float*>(gpost);
         S->gpre = reinterpret_cast<float*>(gpre);
         S->planes = planes;
@@ -184,500 +72,68 @@ __host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg
     return off;
 }
 
-// Q4_K planes of one 256-column segment: lane l of the calling warp holds
-// elements 8l..8l+7 of it (zeros past K).  Writes the three planes and the
-// per-sub-block {unit, sum}.
-__device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg, int lane, int pstride,
-                                                   uint8_t* planes, float2* xsx) {
-    float m = 0.f, sum = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        m = fmaxf(m, fabsf(xv[e]));
-        sum += xv[e];
-    }
-    // a sub-block is 4 lanes
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    const float s = m / 127.0f;
-    const float inv = m > 0.f ? 127.0f / m : 0.f;
-    const float s128 = s * (1.0f / 128.0f);
-    const float inv128 = inv * 128.0f, inv16k = inv * 16384.0f;
-    int q0[8], q1[8], q2[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        float f0, f1, f2;
-        q0[e] = round_magic(xv[e] * inv, &f0);
-        const float r1 = fmaf(-f0, s, xv[e]);
-        q1[e] = round_magic(r1 * inv128, &f1);
-        const float r2 = fmaf(-f1, s128, r1);
-        q2[e] = round_magic(r2 * inv16k, &f2);
-    }
-    const int j = lane >> 2;  // sub-block of this lane's elements
-    const int r = j & 3, half = j >> 2;
-    const int t0 = (lane & 1) ? 2 : 0;    // elements 8(l&3)..: t of the first four
-    const int posb = (lane & 2) ? 4 : 0;  // second 16 elements of the sub-block
-    const int o0 = seg * 256 + r * 64 + t0 * 16 + half * 8 + posb;
-    const int o1 = o0 + 16;
-    uint8_t* P0 = planes;
-    uint8_t* P1 = planes + pstride;
-    uint8_t* P2 = planes + 2 * pstride;
-    *reinterpret_cast<uint32_t*>(P0 + o0) = pack4(q0[0], q0[1], q0[2], q0[3]);
-    *reinterpret_cast<uint32_t*>(P0 + o1) = pack4(q0[4], q0[5], q0[6], q0[7]);
-    *reinterpret_cast<uint32_t*>(P1 + o0) = pack4(q1[0], q1[1], q1[2], q1[3]);
-    *reinterpret_cast<uint32_t*>(P1 + o1) = pack4(q1[4], q1[5], q1[6], q1[7]);
-    *reinterpret_cast<uint32_t*>(P2 + o0) = pack4(q2[0], q2[1], q2[2], q2[3]);
-    *reinterpret_cast<uint32_t*>(P2 + o1) = pack4(q2[4], q2[5], q2[6], q2[7]);
-    if ((lane & 3) == 0) {
-        // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
-        const float unit = s * (1.0f / 16384.0f) * ((j & 1) ? 0.0625f : 1.0f);
-        xsx[seg * 8 + j] = make_float2(unit, sum);
-    }
-}
-
-// BF16 planes of 8 consecutive columns 8q..8q+7 (zeros past K).
-__device__ __forceinline__ void bf16_chunk_planes(const float (&xv)[8], int q, int pstride, uint8_t* planes) {
-    uint32_t h[8], md[8], lo[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        h[e] = bf16_rne(xv[e]);
-        const float r = xv[e] - __uint_as_float(h[e] << 16);
-        md[e] = bf16_rne(r);
-        lo[e] = bf16_rne(r - __uint_as_float(md[e] << 16));
-    }
-    // 16-column block b = q >> 1, half hf = q & 1: element 8hf + i sits at slot
-    // 4(i >> 1) + 2hf + (i & 1), i.e. pair i>>1 is 32-bit word 2(i>>1) + hf.
-    const int b = q >> 1, hf = q & 1;
-    uint32_t* P0 = reinterpret_cast<uint32_t*>(planes) + b * 8 + hf;
-    uint32_t* P1 = reinterpret_cast<uint32_t*>(planes + pstride) + b * 8 + hf;
-    uint32_t* P2 = reinterpret_cast<uint32_t*>(planes + 2 * pstride) + b * 8 + hf;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        P0[2 * k] = h[2 * k] | (h[2 * k + 1] << 16);
-        P1[2 * k] = md[2 * k] | (md[2 * k + 1] << 16);
-        P2[2 * k] = lo[2 * k] | (lo[2 * k + 1] << 16);
-    }
-}
-
-// The unit split: warp w (grid-wide index) owns units [start(w), start(w+1))
-// with start(w) = floor(U * w / NW); U < 2^31 and NW < 2^16 keep all of it in
-// 32-bit arithmetic.
-struct Split {
-    uint32_t U;
-    uint32_t q;  // U / NW
-    uint32_t r;  // U % NW
-    uint32_t NW;
-    float w_per_u;  // NW / U
-    __device__ __forceinline__ uint32_t start(uint32_t w) const { return q * w + (r * w) / NW; }
-    // The warp whose range holds unit u (a float estimate, then exact steps).
-    __device__ __forceinline__ uint32_t owner(uint32_t u) const {
-        uint32_t w = min(NW - 1, static_cast<uint32_t>(static_cast<float>(u) * w_per_u));
-        while (w + 1 < NW && start(w + 1) <= u) ++w;
-        while (w > 0 && start(w) > u) --w;
-        return w;
-    }
-};
-
 template <int KIND, int PRO, int EPI>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     gemv_kernel(const GemvArgs a, const __grid_constant__ CUtensorMap tmap) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // TMA destinations need 128-byte alignment (the plan reserves the slack).
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t{127});
-    constexpr int kSegCols = KIND == kQ4K ? kQ4KSegCols : kBF16SegCols;
-    const int tid = threadIdx.x, nthr = blockDim.x;
-    const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int K = a.K, nseg = a.nseg, NB = a.nb, ubytes = a.unit_bytes;
-    const int Kp = nseg * kSegCols;
-    const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     Smem S;
-    carve(smem, KIND, K, nseg, nw, NB, ubytes, PRO, &S);
-
-    // This warp's share of the tile-major unit sequence.
-    const uint32_t ntiles = static_cast<uint32_t>((a.rows + kTile - 1) / kTile);
-    Split sp;
-    sp.U = ntiles * static_cast<uint32_t>(nseg);
-    sp.NW = gridDim.x * static_cast<uint32_t>(nw);
-    sp.q = sp.U / sp.NW;
-    sp.r = sp.U - sp.q * sp.NW;
-    sp.w_per_u = static_cast<float>(sp.NW) / static_cast<float>(sp.U);
-    const uint32_t gw = blockIdx.x * static_cast<uint32_t>(nw) + warp;
-    const uint32_t u_begin = sp.start(gw);
-    const int n = static_cast<int>(sp.start(gw + 1) - u_begin);
-    uint64_t* full = S.full + warp * NB;
-    uint8_t* ring = S.ring + static_cast<size_t>(warp) * NB * ubytes;
-
-    if (lane == 0) {
-        for (int j = 0; j < NB; ++j) mbar_init(&full[j], 1);
-        if (warp == 0) mbar_init(S.pbar, 1);
+    carve(smem, KIND, a.K, a.nseg, nw, a.nb, PRO, &S);
+    if (tid == 0) {
+        Job& j = *S.job;
+        j.tmap = &tmap;
+        j.kind = KIND;
+        j.K = a.K;
+        j.nseg = a.nseg;
+        j.rows = a.rows;
+        j.x = a.x;
+        j.src = a.src;
+        j.resid_in = a.resid_in;
+        j.resid_out = a.resid_out;
+        j.g_post = a.g_post;
+        j.g_pre = a.g_pre;
+        j.embed = a.embed;
+        j.token = a.token;
+        j.embed_scale = a.embed_scale;
+        j.eps = a.eps;
+        j.y = a.y;
+        j.am_val = a.am_val;
+        j.am_idx = a.am_idx;
+        j.am_counter = a.am_counter;
+        j.token_out = a.token_out;
+        j.pos_inout = a.pos_inout;
+        j.token_hist = a.token_hist;
+        mbar_init(S.pbar, 1);
         fence_mbar_init();
+        S.flags[0] = 0;
+        S.flags[1] = 0;
     }
-    if (tid == 0) S.flags[0] = 0;
     __syncthreads();
+    const Job& job = *S.job;
+    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx};
 
-    // ---- weight stream: lane 0 of each warp issues its own unit copies ----
-    const uint64_t pol = l2_evict_first_policy();
-    constexpr int kBoxStep = KIND == kQ4K ? kQ4KPitch / 8 : kBF16SegCols * 2 / 8;  // x advance per segment
-    uint32_t is_tile = u_begin / nseg;
-    int is_seg = static_cast<int>(u_begin - is_tile * nseg);
-    int issued = 0;
-    auto issue = [&](int j) {
-        mbar_arrive_expect_tx(&full[j], static_cast<uint32_t>(ubytes));
-        tma_2d_g2s(ring + static_cast<size_t>(j) * ubytes, &tmap, is_seg * kBoxStep, static_cast<int>(is_tile * kTile),
-                   &full[j], pol);
-        if (++is_seg == nseg) {
-            is_seg = 0;
-            ++is_tile;
-        }
-        ++issued;
-    };
-    if (lane == 0) {
-        const int np = min(NB, n);
-        for (int j = 0; j < np; ++j) issue(j);
-    }
-    // Norm weights are constants: fetch them before waiting on the previous kernel.
-    if constexpr (PRO != kProPlain) {
-        if (tid == 0) {
-            const uint32_t kb = static_cast<uint32_t>(K) * 4u;
-            mbar_arrive_expect_tx(S.pbar, PRO == kProResidNorm ? 2u * kb : kb);
-            if constexpr (PRO == kProResidNorm) bulk_g2s_nohint(S.gpost, a.g_post, kb, S.pbar);
-            bulk_g2s_nohint(S.gpre, a.g_pre, kb, S.pbar);
-        }
-    }
+    // Each warp's weight stream starts before the wait on the previous kernel
+    // (weights are constants), and so do the norm weights.
+    const int ubytes = unit_bytes(KIND);
+    Stream st;
+    stream_start(st, S.full + warp * a.nb, S.ring + static_cast<size_t>(warp) * a.nb * ubytes, a.nb, ubytes, S.job, 1,
+                 blockIdx.x * static_cast<uint32_t>(nw) + warp, gridDim.x * static_cast<uint32_t>(nw), lane);
+    if (tid == 0) prefetch_gammas(job, PRO, JS);
     pdl_launch_dependents();
     pdl_wait();
 
-    // ---------------- prologue: x -> planes ----------------
-    if constexpr (PRO == kProPlain) {
-        // 8-column chunks q = tid + i * nthr; for Q4_K a warp covers one segment
-        // per i.  All loads of a group of kMaxV8 chunks are in flight together.
-        const int nq = Kp / 8;
-        for (int base0 = 0; base0 < nq; base0 += kMaxV8 * nthr) {
-            float4 xl[kMaxV8][2];
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (base0 + i * nthr + tid) * 8;
-                if (c0 + 8 <= K) {
-                    xl[i][0] = *reinterpret_cast<const float4*>(a.x + c0);
-                    xl[i][1] = *reinterpret_cast<const float4*>(a.x + c0 + 4);
-                } else {
-                    xl[i][0] = xl[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int base = base0 + i * nthr;
-                if (base >= nq) break;
-                const int qi = base + tid;
-                const float xv[8] = {xl[i][0].x, xl[i][0].y, xl[i][0].z, xl[i][0].w,
-                                     xl[i][1].x, xl[i][1].y, xl[i][1].z, xl[i][1].w};
-                if constexpr (KIND == kQ4K) {
-                    if (base + warp * 32 < nq) q4k_segment_planes(xv, (base >> 5) + warp, lane, pstride, S.planes, S.xsx);
-                } else {
-                    if (qi < nq) bf16_chunk_planes(xv, qi, pstride, S.planes);
-                }
-            }
-        }
-    } else {
-        // Thread chunk i holds columns 8q..8q+7, q = tid + i * nthr.
-        const float inv_d = 1.0f / static_cast<float>(K);
-        float xr[kMaxV8][8];
-        float ss = 0.f;
-        if constexpr (PRO == kProResidNorm) {
-            // post-norm of the sub-layer output, then the residual add
-            // (Gemma3Block::forward_cached, src/transformer4.rs:1954-1964)
-            float v[kMaxV8][8];
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (tid + i * nthr) * 8;
-                if (c0 < K) {
-                    const float4 s0 = *reinterpret_cast<const float4*>(a.src + c0);
-                    const float4 s1 = *reinterpret_cast<const float4*>(a.src + c0 + 4);
-                    const float4 r0 = *reinterpret_cast<const float4*>(a.resid_in + c0);
-                    const float4 r1 = *reinterpret_cast<const float4*>(a.resid_in + c0 + 4);
-                    v[i][0] = s0.x; v[i][1] = s0.y; v[i][2] = s0.z; v[i][3] = s0.w;
-                    v[i][4] = s1.x; v[i][5] = s1.y; v[i][6] = s1.z; v[i][7] = s1.w;
-                    xr[i][0] = r0.x; xr[i][1] = r0.y; xr[i][2] = r0.z; xr[i][3] = r0.w;
-                    xr[i][4] = r1.x; xr[i][5] = r1.y; xr[i][6] = r1.z; xr[i][7] = r1.w;
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) v[i][e] = xr[i][e] = 0.f;
-                }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
-            }
-            ss = block_sum(ss, S.red);
-            if (!mbar_wait(S.pbar, 0u) && lane == 0) atomicExch(&S.flags[0], 1);
-            const float r1 = 1.0f / sqrtf(ss * inv_d + a.eps);
-            float ss2 = 0.f;
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (tid + i * nthr) * 8;
-                if (c0 < K) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float nv = __fadd_rn(xr[i][e], __fmul_rn(__fmul_rn(v[i][e], r1), __fadd_rn(1.0f, S.gpost[c0 + e])));
-                        xr[i][e] = nv;
-                        ss2 += nv * nv;
-                    }
-                    if (blockIdx.x == 0) {
-                        *reinterpret_cast<float4*>(a.resid_out + c0) = make_float4(xr[i][0], xr[i][1], xr[i][2], xr[i][3]);
-                        *reinterpret_cast<float4*>(a.resid_out + c0 + 4) = make_float4(xr[i][4], xr[i][5], xr[i][6], xr[i][7]);
-                    }
-                }
-            }
-            ss = block_sum(ss2, S.red);
-        } else {
-            // embedding row * sqrt(hidden) (src/transformer4.rs:2360-2364)
-            const int64_t tok = static_cast<int64_t>(*a.token);
-            const uint16_t* er = a.embed + tok * K;
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (tid + i * nthr) * 8;
-                if (c0 < K) {
-                    const uint4 e = *reinterpret_cast<const uint4*>(er + c0);
-                    const uint32_t ew[4] = {e.x, e.y, e.z, e.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        xr[i][2 * k] = __fmul_rn(bf16_bits_to_f32(ew[k] & 0xFFFFu), a.embed_scale);
-                        xr[i][2 * k + 1] = __fmul_rn(bf16_bits_to_f32(ew[k] >> 16), a.embed_scale);
-                    }
-#pragma unroll
-                    for (int e2 = 0; e2 < 8; ++e2) ss += xr[i][e2] * xr[i][e2];
-                    if (blockIdx.x == 0) {
-                        *reinterpret_cast<float4*>(a.resid_out + c0) = make_float4(xr[i][0], xr[i][1], xr[i][2], xr[i][3]);
-                        *reinterpret_cast<float4*>(a.resid_out + c0 + 4) = make_float4(xr[i][4], xr[i][5], xr[i][6], xr[i][7]);
-                    }
-                } else {
-#pragma unroll
-                    for (int e2 = 0; e2 < 8; ++e2) xr[i][e2] = 0.f;
-                }
-            }
-            ss = block_sum(ss, S.red);
-            if (!mbar_wait(S.pbar, 0u) && lane == 0) atomicExch(&S.flags[0], 1);
-        }
-        // pre-norm producing the projection input (rms_norm_gemma3,
-        // src/autograd2.rs:3477-3496), then the planes
-        const float r2 = 1.0f / sqrtf(ss * inv_d + a.eps);
-        const int nq = Kp / 8;
-#pragma unroll
-        for (int i = 0; i < kMaxV8; ++i) {
-            const int base = i * nthr;
-            if (base >= nq) break;
-            const int qi = base + tid;
-            const int c0 = qi * 8;
-            float xv[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-                xv[e] = c0 < K ? __fmul_rn(__fmul_rn(xr[i][e], r2), __fadd_rn(1.0f, S.gpre[c0 + e])) : 0.f;
-            if constexpr (KIND == kQ4K) {
-                if (base + warp * 32 < nq) q4k_segment_planes(xv, (base >> 5) + warp, lane, pstride, S.planes, S.xsx);
-            } else {
-                if (qi < nq) bf16_chunk_planes(xv, qi, pstride, S.planes);
-            }
-        }
-    }
-    __syncthreads();
-
-    // ---------------- the weight stream ----------------
+    job_prologue<KIND, PRO>(job, JS, 0u);
     float best_v = -INFINITY;
     long long best_i = -1;
-    // Row epilogue: lane L < 16 holds the sum of row r0 + L.
-    auto emit_rows = [&](int64_t r0, float v) {
-        const int64_t r = r0 + lane;
-        if constexpr (EPI == kEpiGeluPair) {
-            const float up = __shfl_down_sync(0xffffffffu, v, 1);
-            if (lane < kTile && !(lane & 1) && r < a.rows) a.y[r >> 1] = __fmul_rn(gelu_tanh_dev(v), up);
-        } else {
-            if (lane < kTile && r < a.rows) {
-                a.y[r] = v;
-                if constexpr (EPI == kEpiArgmax) {
-                    if (v > best_v || (v == best_v && r > best_i)) {
-                        best_v = v;
-                        best_i = r;
-                    }
-                }
-            }
-        }
-    };
-
-    const int q = g >> 1;  // Q4_K: the B column pair this lane feeds
-    const uint32_t jsel = 0x7540u | static_cast<uint32_t>(t);
-    // ldmatrix row address of this lane within a unit (matrix l/8: rows 0-7 or
-    // 8-15, first or second 16 bytes of the 32-byte k slice)
-    const int ldsm_off = KIND == kQ4K
-                             ? ((lane & 7) + ((lane >> 3) & 1) * 8) * kQ4KPitch + 16 + ((lane >> 4) & 1) * 16
-                             : ((lane & 7) + ((lane >> 3) & 1) * 8) * kBF16Pitch + ((lane >> 4) & 1) * 16;
-
-    float acc0 = 0.f, acc1 = 0.f;  // this lane's share of rows g and g+8 of the current tile
-    uint32_t tile = u_begin / nseg;
-    int seg = static_cast<int>(u_begin - tile * nseg);
-    const uint32_t first_tile = tile;
-    int pu = 0;  // units of the current tile piece
-    int jb = 0;
-    uint32_t ph = 0;
-    int done = 0;
-    bool failed = false;
-    for (int i = 0; i < n; ++i) {
-        const bool ok = mbar_wait(&full[jb], ph);
-        if (__any_sync(0xffffffffu, !ok)) {
-            failed = true;
-            break;
-        }
-        const uint8_t* ub = ring + static_cast<size_t>(jb) * ubytes;
-        if constexpr (KIND == kQ4K) {
-            // B fragments: planes 0/1 of sub-blocks q and q+4 (this lane's column
-            // pair) and, for even g, plane 2.
-            const uint8_t* pb = S.planes + seg * 256 + q * 64 + t * 16;
-            const uint4 B01 = lds128(pb + (g & 1) * pstride);
-            const uint4 B2 = (g & 1) ? make_uint4(0u, 0u, 0u, 0u) : lds128(pb + 2 * pstride);
-            const uint4 h0 = lds128(ub + g * kQ4KPitch), h1 = lds128(ub + (g + 8) * kQ4KPitch);
-            const float2 xa = S.xsx[seg * 8 + t], xb = S.xsx[seg * 8 + t + 4];
-            int c01[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, c2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(ub + ldsm_off + 32 * c, a0, a1, a2, a3);
-#pragma unroll
-                for (int hi = 0; hi < 2; ++hi) {
-                    const int j = 2 * c + hi;  // sub-block
-                    const int r = j & 3, set = j >> 2;
-                    const uint32_t m = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-                    const bool own = q == r;
-                    const uint32_t b0 = own ? (set ? B01.z : B01.x) : 0u;
-                    const uint32_t b1 = own ? (set ? B01.w : B01.y) : 0u;
-                    const uint32_t e0 = own ? (set ? B2.z : B2.x) : 0u;
-                    const uint32_t e1 = own ? (set ? B2.w : B2.y) : 0u;
-                    mma_u8s8(c01[set], a0 & m, a1 & m, a2 & m, a3 & m, b0, b1);
-                    mma_u8s8(c2[set], a0 & m, a1 & m, a2 & m, a3 & m, e0, e1);
-                }
-            }
-            // Lane t: sub-blocks t (set 0) and t+4 (set 1); c01[.][0]/[1] = planes
-            // 0/1 of row g, [2]/[3] of row g+8; plane 2 sits in the even columns
-            // (c2[.][0] row g, c2[.][2] row g+8).
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const uint4 h = half ? h1 : h0;
-                const float d = f16_bits_to_f32(h.x & 0xFFFFu), dmin = f16_bits_to_f32(h.x >> 16);
-                // scale_min (src/autograd2.rs:1075-1085), four 6-bit fields per word
-                const uint32_t s_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
-                const uint32_t s_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-                const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-                const float sc0 = byte_to_float(s_lo, jsel), mn0 = byte_to_float(m_lo, jsel);
-                const float sc1 = byte_to_float(s_hi, jsel), mn1 = byte_to_float(m_hi, jsel);
-                const int i0 = 2 * half;
-                const float T0 = fmaf(static_cast<float>(c01[0][i0]), 16384.0f,
-                                      fmaf(static_cast<float>(c01[0][i0 + 1]), 128.0f, static_cast<float>(c2[0][i0])));
-                const float T1 = fmaf(static_cast<float>(c01[1][i0]), 16384.0f,
-                                      fmaf(static_cast<float>(c01[1][i0 + 1]), 128.0f, static_cast<float>(c2[1][i0])));
-                const float v = d * (sc0 * (T0 * xa.x) + sc1 * (T1 * xb.x)) - dmin * (mn0 * xa.y + mn1 * xb.y);
-                if (half) acc1 += v;
-                else acc0 += v;
-            }
-        } else {
-            // BF16: lanes g < 3 feed B column g (plane g); the rest feed zeros.
-            const uint8_t* pb = S.planes + (g < 3 ? g : 0) * pstride + seg * (kBF16SegCols * 2) + t * 8;
-            float c[4][4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) c[k][e] = 0.f;
-#pragma unroll
-            for (int s = 0; s < 8; ++s) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(ub + ldsm_off + 32 * s, a0, a1, a2, a3);
-                const uint2 b = g < 3 ? lds64(pb + 32 * s) : make_uint2(0u, 0u);
-                mma_bf16(c[s & 3], a0, a1, a2, a3, b.x, b.y);
-            }
-            acc0 += ((c[0][0] + c[1][0]) + (c[2][0] + c[3][0])) + ((c[0][1] + c[1][1]) + (c[2][1] + c[3][1]));
-            acc1 += ((c[0][2] + c[1][2]) + (c[2][2] + c[3][2])) + ((c[0][3] + c[1][3]) + (c[2][3] + c[3][3]));
-        }
-        ++pu;
-        done = i + 1;
-        // Release the buffer to the next copy of this warp.
-        __syncwarp();
-        if (lane == 0 && issued < n) {
-            fence_proxy_async_smem();
-            issue(jb);
-        }
-        if (++jb == NB) {
-            jb = 0;
-            ph ^= 1u;
-        }
-        const bool tile_end = ++seg == nseg;
-        if (tile_end || i == n - 1) {
-            // Row sums of this piece: quad reduction, then lane L < 16 takes row L.
-            float s0 = acc0 + __shfl_xor_sync(0xffffffffu, acc0, 1);
-            s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-            float s1 = acc1 + __shfl_xor_sync(0xffffffffu, acc1, 1);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-            const float ra = __shfl_sync(0xffffffffu, s0, 4 * (lane & 7));
-            const float rb = __shfl_sync(0xffffffffu, s1, 4 * (lane & 7));
-            const float rowv = (lane & 8) ? rb : ra;
-            const int64_t r0 = static_cast<int64_t>(tile) * kTile;
-            if (pu == nseg) {
-                emit_rows(r0, rowv);
-            } else {
-                // Lanes 16..31 (row = lane - 16) publish the piece: lane 0 has this
-                // warp's copies in flight, and a fence there would wait for them.
-                const int slot = tile == first_tile ? 0 : 1;
-                const bool pub = lane >= kTile;
-                const float rv = __shfl_sync(0xffffffffu, rowv, lane & (kTile - 1));
-                if (pub) {
-                    a.part[(static_cast<int64_t>(gw) * 2 + slot) * kTile + (lane - kTile)] = rv;
-                    __threadfence();
-                }
-                __syncwarp();
-                int last = 0;
-                if (lane == kTile)
-                    last = atomicAdd(&a.tile_cnt[tile], static_cast<uint32_t>(pu)) + static_cast<uint32_t>(pu) ==
-                           static_cast<uint32_t>(nseg);
-                last = __shfl_sync(0xffffffffu, last, kTile);
-                if (last) {
-                    if (pub) __threadfence();
-                    const uint32_t u0 = tile * nseg;
-                    const uint32_t w_first = sp.owner(u0), w_last = sp.owner(u0 + nseg - 1);
-                    // Sum the pieces in warp order, eight loads in flight at a time.
-                    float v = 0.f;
-                    for (uint32_t wb = w_first; wb <= w_last; wb += 8) {
-                        float pv[8];
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) {
-                            const uint32_t w = wb + k;
-                            pv[k] = 0.f;
-                            if (w <= w_last && pub) {
-                                const uint32_t s_w = sp.start(w);
-                                // a warp that began in an earlier tile keeps this one in slot 1
-                                if (sp.start(w + 1) > s_w)
-                                    pv[k] = ldcg_f32(a.part + (static_cast<int64_t>(w) * 2 + (s_w < u0 ? 1 : 0)) * kTile +
-                                                     (lane - kTile));
-                            }
-                        }
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) v += pv[k];
-                    }
-                    emit_rows(r0, __shfl_sync(0xffffffffu, v, (lane & (kTile - 1)) + kTile));
-                    if (lane == kTile) a.tile_cnt[tile] = 0u;
-                }
-            }
-            acc0 = acc1 = 0.f;
-            pu = 0;
-            if (tile_end) {
-                seg = 0;
-                ++tile;
-            }
-        }
-    }
-
-    if (failed) {
+    const bool ok = job_units_run<KIND, EPI>(job, st, JS, SplitScratch{a.part, a.tile_cnt}, best_v, best_i);
+    if (!ok) {
         // A bounded wait gave up: record it, then wait (bounded) for the copies
         // this warp still has in flight before its shared memory goes away.
         if (lane == 0) {
             atomicExch(&S.flags[0], 1);
-            for (int k = done; k < issued; ++k)
-                if (!mbar_wait(&full[k % NB], static_cast<uint32_t>(k / NB) & 1u)) break;
+            stream_drain(st);
         }
         __syncwarp();
     }
@@ -686,61 +142,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         if (tid == 0 && a.err) atomicExch(a.err, kErrMbarTimeout);
         return;
     }
-
-    if constexpr (EPI == kEpiArgmax) {
-        // Block argmax (largest value; ties to the higher row index).
-        __shared__ bool is_last;
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-            const long long oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-            if (ov > best_v || (ov == best_v && oi > best_i)) {
-                best_v = ov;
-                best_i = oi;
-            }
-        }
-        if (lane == 0) {
-            S.bv[warp] = best_v;
-            S.bi[warp] = best_i;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float bv = S.bv[0];
-            long long bi = S.bi[0];
-            for (int w = 1; w < nw; ++w)
-                if (S.bv[w] > bv || (S.bv[w] == bv && S.bi[w] > bi)) {
-                    bv = S.bv[w];
-                    bi = S.bi[w];
-                }
-            a.am_val[blockIdx.x] = bv;
-            a.am_idx[blockIdx.x] = static_cast<int32_t>(bi);
-            __threadfence();
-            const uint32_t prev = atomicAdd(a.am_counter, 1u);
-            is_last = prev == gridDim.x - 1;
-        }
-        __syncthreads();
-        if (is_last && tid == 0) {
-            __threadfence();
-            const volatile float* vv = a.am_val;
-            const volatile int32_t* vi = a.am_idx;
-            float bv = vv[0];
-            int32_t bi = vi[0];
-            for (unsigned k = 1; k < gridDim.x; ++k) {
-                const float v = vv[k];
-                const int32_t i = vi[k];
-                if (v > bv || (v == bv && i > bi)) {
-                    bv = v;
-                    bi = i;
-                }
-            }
-            if (a.token_out) *a.token_out = bi;
-            if (a.pos_inout) {
-                const int32_t p = *a.pos_inout;
-                if (a.token_hist) a.token_hist[p] = bi;
-                *a.pos_inout = p + 1;
-            }
-            *a.am_counter = 0u;
-        }
-    }
+    if constexpr (EPI == kEpiArgmax) argmax_finish(job, JS, best_v, best_i);
 }
 
 // Calls f(kernel) for the instantiation matching (kind, prologue, epilogue).
@@ -809,7 +211,7 @@ GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int ep
     p.nb = 0;
     size_t smem = 0;
     for (int nb = std::max(2, std::min(kMaxNb, kCopiesInFlight / p.warps)); nb >= 2; --nb) {
-        smem = carve(nullptr, kind, K, nseg, p.warps, nb, p.unit_bytes, prologue, nullptr) + 128;
+        smem = carve(nullptr, kind, K, nseg, p.warps, nb, prologue, nullptr) + 128;
         if (smem <= budget) {
             p.nb = nb;
             break;
