@@ -220,8 +220,12 @@ int rt_decoder_memory(const rt_dec* dec, uint64_t* bytes);
 /* The engine's kernel launches per decode step. */
 int rt_decoder_launches_per_step(const rt_dec* dec, int32_t* n);
 /* Copy an internal activation vector of the last step to host (debugging and
- * tests): which = 0 residual stream after the last layer, 1 logits.
- * `count` is the number of f32 values to copy. */
+ * tests): which = 0 residual stream after the last layer, 1 logits, 2 the
+ * phase timeline of the last persistent step kernel (1024 u64 globaltimer
+ * stamps of CTA 0, read as 2048 f32 words; RT_E_INVAL when the engine runs
+ * per-projection kernels), 3..7 the last layer's qkv, attention output, O
+ * projection, gated FFN hidden and down projection.  `count` is the number of
+ * f32 values to copy. */
 int rt_decoder_read_activation(rt_dec* dec, int32_t which, float* host, int64_t count);
 
 /* ---- synthetic inputs ---------------------------------------------------

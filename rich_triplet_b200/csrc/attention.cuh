@@ -5,6 +5,8 @@
 
 #include <cuda_runtime.h>
 
+#include "gemv.cuh"
+
 namespace rt {
 
 struct AttnArgs {

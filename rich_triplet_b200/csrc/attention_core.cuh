@@ -1,0 +1,342 @@
+// attention_core.cuh -- device side of the fused per-head QK-norm + NeoX RoPE +
+// KV append + split-context flash-decode attention for one query token
+// (Gemma 3, GQA), shared by the standalone attention kernel (attention.cu) and
+// the persistent decode-step kernel (step.cu).
+//
+// Reference semantics (paths relative to the reference crate root):
+//   apply_per_head_norm      src/transformer4.rs:2485-2510 (rms_norm_gemma3 per head)
+//   apply_rope_at_offset     src/transformer4.rs:2742-2772 (pairs (i, i + D/2))
+//   Gemma3LayerKvCache::append + window selection  src/transformer4.rs:1813-1823, 1923-1929
+//   gqa_attention_cached (t_q == 1)  src/transformer4.rs:2806-2880
+//
+// Work item (h, s): the s-th slice of the attended positions [k_start, pos] of
+// KV head h, for all G query heads that share it.  Cached positions (< pos) do
+// not depend on this step, so their first tile can be copied into shared
+// memory (TMA bulk copy) before the projections of this step exist.  The item
+// whose slice contains `pos` normalises and rotates the new K row, appends K
+// and V to the cache and uses them from shared memory.  Each item keeps an
+// online softmax (max m, sum l, unnormalised output) per query head and writes
+// it to `part`; the last item of each KV head to finish (atomic counter, no
+// waiting) merges the slices.  RoPE cos/sin come from host-built tables that
+// evaluate the reference formula with the host libm, so the rotation matches
+// it exactly.  All threads of the CTA take part (any multiple of 32 >= D).
+#pragma once
+
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace rt {
+namespace acore {
+
+struct AttnSmem {
+    uint64_t* bar;
+    float* red;    // [32]
+    float* m_run;  // [G]
+    float* l_run;  // [G]
+    float* corr;   // [G]
+    int* flag;     // [4]
+    float* qv;     // [G][D]
+    float* sc;     // [G][T]
+    float* knew;   // [D]
+    float* vnew;   // [D]
+    float* kt;     // [T][D]
+    float* vt;     // [T][D]
+};
+
+// Shared-memory layout for G query heads per KV head and tiles of T positions.
+__host__ __device__ inline size_t attn_carve(uint8_t* base, int D, int G, int T, AttnSmem* S) {
+    size_t off = 0;
+    auto take = [&](size_t bytes, size_t align) -> uint8_t* {
+        off = (off + align - 1) / align * align;
+        uint8_t* p = base + off;
+        off += bytes;
+        return p;
+    };
+    uint8_t* bar = take(16, 16);
+    uint8_t* red = take(32 * 4, 16);
+    uint8_t* m = take(G * 4, 16);
+    uint8_t* l = take(G * 4, 16);
+    uint8_t* cr = take(G * 4, 16);
+    uint8_t* fl = take(16, 16);
+    uint8_t* qv = take(static_cast<size_t>(G) * D * 4, 16);
+    uint8_t* sc = take(static_cast<size_t>(G) * T * 4, 16);
+    uint8_t* kn = take(static_cast<size_t>(D) * 4, 16);
+    uint8_t* vn = take(static_cast<size_t>(D) * 4, 16);
+    uint8_t* kt = take(static_cast<size_t>(T) * D * 4, 128);
+    uint8_t* vt = take(static_cast<size_t>(T) * D * 4, 128);
+    if (S) {
+        S->bar = reinterpret_cast<uint64_t*>(bar);
+        S->red = reinterpret_cast<float*>(red);
+        S->m_run = reinterpret_cast<float*>(m);
+        S->l_run = reinterpret_cast<float*>(l);
+        S->corr = reinterpret_cast<float*>(cr);
+        S->flag = reinterpret_cast<int*>(fl);
+        S->qv = reinterpret_cast<float*>(qv);
+        S->sc = reinterpret_cast<float*>(sc);
+        S->knew = reinterpret_cast<float*>(kn);
+        S->vnew = reinterpret_cast<float*>(vn);
+        S->kt = reinterpret_cast<float*>(kt);
+        S->vt = reinterpret_cast<float*>(vt);
+    }
+    return off;
+}
+
+// In-place per-head RMSNorm (1 + gamma) of `v[D]` in shared memory.
+__device__ __forceinline__ void head_norm(float* v, const float* gamma, int D, float eps, float* red) {
+    float ss = 0.f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) ss += v[d] * v[d];
+    ss = block_sum(ss, red);
+    const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(D)) + eps);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) v[d] = __fmul_rn(__fmul_rn(v[d], r), __fadd_rn(1.0f, gamma[d]));
+    __syncthreads();
+}
+
+// In-place NeoX rotation of `v[D]`: (x0, x1) = (v[j], v[j + D/2]).
+__device__ __forceinline__ void head_rope(float* v, const float* cs, const float* sn, int D) {
+    const int half = D / 2;
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+        const float x0 = v[j], x1 = v[j + half], c = cs[j], s = sn[j];
+        v[j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        v[j + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    }
+    __syncthreads();
+}
+
+template <int G, int T>
+__device__ __forceinline__ void attend_tile(const AttnSmem& S, const float* K, const float* V, int nt, int D,
+                                            float scale, float (&acc)[G]) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    for (int j = warp; j < nt; j += nw) {
+        const float* kr = K + static_cast<size_t>(j) * D;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float* q = S.qv + g * D;
+            float dot = 0.f;
+            for (int d = lane; d < D; d += 32) dot += q[d] * kr[d];
+            dot = warp_sum(dot);
+            if (lane == 0) S.sc[g * T + j] = dot * scale;
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float v = lane < nt ? S.sc[g * T + lane] : -INFINITY;
+            const float tmax = warp_max(v);
+            const float mold = S.m_run[g];
+            const float mnew = fmaxf(mold, tmax);
+            const float p = lane < nt ? expf(v - mnew) : 0.f;
+            const float psum = warp_sum(p);
+            if (lane < T) S.sc[g * T + lane] = p;
+            __syncwarp();
+            if (lane == 0) {
+                const float cr = expf(mold - mnew);
+                S.corr[g] = cr;
+                S.l_run[g] = S.l_run[g] * cr + psum;
+                S.m_run[g] = mnew;
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    if (tid < D) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float v = acc[g] * S.corr[g];
+            const float* p = S.sc + g * T;
+            for (int j = 0; j < nt; ++j) v += p[j] * V[static_cast<size_t>(j) * D + tid];
+            acc[g] = v;
+        }
+    }
+    __syncthreads();
+}
+
+// Positions per split below which the context uses fewer splits: the merge
+// reads every split's partial, so splits cost more than they save when short.
+constexpr int kMinPerSplit = 16;
+
+// Attended positions of item (h, s) (window selection, src/transformer4.rs:1923-1929).
+struct AttnRange {
+    int pos;
+    int nsplit;   // splits in use at this context length (<= a.nsplit)
+    bool active;  // s < nsplit
+    int p0;
+    int ncached;  // cached positions of the slice (excluding the new one)
+    int ntiles;
+    bool has_new;
+    size_t head_base;
+};
+
+__device__ __forceinline__ AttnRange attn_range(const AttnArgs& a, int h, int s, int T) {
+    AttnRange R;
+    R.pos = *a.pos;
+    const int L = R.pos + 1;
+    const int kstart = a.window > 0 ? max(0, L - a.window) : 0;
+    const int n = L - kstart;
+    R.nsplit = max(1, min(a.nsplit, (n + kMinPerSplit - 1) / kMinPerSplit));
+    R.active = s < R.nsplit;
+    const int chunk = (n + R.nsplit - 1) / R.nsplit;
+    R.p0 = min(L, kstart + s * chunk);
+    const int p1 = min(L, R.p0 + chunk);
+    R.has_new = R.p0 <= R.pos && R.pos < p1;
+    R.ncached = max(0, (R.has_new ? R.pos : p1) - R.p0);
+    R.ntiles = (R.ncached + T - 1) / T;
+    R.head_base = static_cast<size_t>(h) * a.cap;
+    return R;
+}
+
+// Thread 0: copy cached tile t of the item into shared memory, completing on S.bar.
+__device__ __forceinline__ void attn_issue(const AttnArgs& a, const AttnRange& R, const AttnSmem& S, int t, int T) {
+    const int r0 = R.p0 + t * T;
+    const int nt = min(T, R.p0 + R.ncached - r0);
+    const uint32_t bytes = static_cast<uint32_t>(nt) * a.D * 4;
+    mbar_arrive_expect_tx(S.bar, 2 * bytes);
+    bulk_g2s_nohint(S.kt, a.kcache + (R.head_base + r0) * a.D, bytes, S.bar);
+    bulk_g2s_nohint(S.vt, a.vcache + (R.head_base + r0) * a.D, bytes, S.bar);
+}
+
+// Thread 0: initialise the tile barrier.  An initialised mbarrier owns its 8
+// bytes until it is invalidated: ordinary stores to them are undefined (on
+// B200 they do not stick), so the barrier must not live in memory that other
+// phases of the same kernel reuse.
+__device__ __forceinline__ void attn_bar_init(const AttnSmem& S) {
+    mbar_init(S.bar, 1);
+    fence_mbar_init();
+}
+
+// Thread 0, before the projections of this step exist: start the first cached
+// tile (S.bar initialised; its next phase is the one attn_run waits on first).
+__device__ __forceinline__ void attn_prefetch(const AttnArgs& a, const AttnRange& R, const AttnSmem& S, int T) {
+    fence_proxy_async_smem();  // the region may have been written by ordinary stores before
+    if (R.active && R.ntiles > 0) attn_issue(a, R, S, 0, T);
+}
+
+// The item itself, once q/k/v of this step are in a.qkv (all threads).  `ph0`:
+// parity of the barrier's next phase (phases it completed before, mod 2); the
+// item completes R.ntiles phases.  Returns false if a bounded wait gave up
+// (after waiting, bounded, for the copy in flight); `a.err` is then set.
+template <int G, int T>
+__device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const AttnRange& R, const AttnSmem& S,
+                                         uint32_t ph0) {
+    if (!R.active) return true;
+    const int D = a.D;
+    const int tid = threadIdx.x;
+    // Query heads h*G .. h*G+G-1 (kvh = qh / group, src/transformer4.rs:2819).
+    const float* qraw = a.qkv + static_cast<size_t>(h) * G * D;
+    for (int i = tid; i < G * D; i += blockDim.x) S.qv[i] = qraw[i];
+    if (tid < G) {
+        S.m_run[tid] = -INFINITY;
+        S.l_run[tid] = 0.f;
+    }
+    __syncthreads();
+    const float* cs = a.rope_cos + static_cast<size_t>(R.pos) * (D / 2);
+    const float* sn = a.rope_sin + static_cast<size_t>(R.pos) * (D / 2);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        head_norm(S.qv + g * D, a.q_norm, D, a.eps, S.red);
+        head_rope(S.qv + g * D, cs, sn, D);
+    }
+    if (R.has_new) {
+        const float* kraw = a.qkv + static_cast<size_t>(a.nq) * D + static_cast<size_t>(h) * D;
+        const float* vraw = a.qkv + static_cast<size_t>(a.nq + a.nkv) * D + static_cast<size_t>(h) * D;
+        for (int d = tid; d < D; d += blockDim.x) {
+            S.knew[d] = kraw[d];
+            S.vnew[d] = vraw[d];
+        }
+        __syncthreads();
+        head_norm(S.knew, a.k_norm, D, a.eps, S.red);
+        head_rope(S.knew, cs, sn, D);
+        float* kdst = a.kcache + (R.head_base + R.pos) * D;
+        float* vdst = a.vcache + (R.head_base + R.pos) * D;
+        for (int d = tid; d < D; d += blockDim.x) {
+            kdst[d] = S.knew[d];
+            vdst[d] = S.vnew[d];
+        }
+    }
+
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    for (int t = 0; t < R.ntiles; ++t) {
+        const bool ok = mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                if (a.err) atomicExch(a.err, kErrMbarTimeout);
+                // the one outstanding copy must land (bounded) before shared memory is reused
+                (void)mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
+            }
+            __syncthreads();
+            return false;
+        }
+        const int nt = min(T, R.ncached - t * T);
+        attend_tile<G, T>(S, S.kt, S.vt, nt, D, a.scale, acc);
+        if (tid == 0 && t + 1 < R.ntiles) {
+            fence_proxy_async_smem();
+            attn_issue(a, R, S, t + 1, T);
+        }
+    }
+    if (R.has_new) attend_tile<G, T>(S, S.knew, S.vnew, 1, D, a.scale, acc);
+
+    // Per-split partial state.
+    const int stride = D + 2;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float* pp = a.part + (static_cast<size_t>(h * a.nsplit + s) * G + g) * stride;
+        if (tid < D) pp[tid] = acc[g];
+        if (tid == 0) {
+            pp[D] = S.m_run[g];
+            pp[D + 1] = S.l_run[g];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(&a.counter[h], 1u);
+        S.flag[0] = prev == static_cast<uint32_t>(R.nsplit - 1);
+    }
+    __syncthreads();
+    if (!S.flag[0]) return true;
+    __threadfence();
+    // Merge the splits of head h (this CTA finished last).  Per query head:
+    // M = max m_q, w_q = exp(m_q - M), out = sum w_q acc_q / sum w_q l_q, the
+    // sums in split order.  The (m, l) pairs are staged in shared memory (the
+    // score buffer, G * T floats >= 2 * nsplit * G is not guaranteed, so the K
+    // tile buffer is used), and every thread keeps eight loads in flight.
+    float* ml = S.kt;  // [G][nsplit][2]
+    for (int i = tid; i < G * R.nsplit; i += blockDim.x) {
+        const int g = i / R.nsplit, q = i - g * R.nsplit;
+        const float* pp = a.part + (static_cast<size_t>(h * a.nsplit + q) * G + g) * stride;
+        ml[2 * i] = __ldcg(pp + D);
+        ml[2 * i + 1] = __ldcg(pp + D + 1);
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += blockDim.x) {
+        const int g = i / D, d = i - g * D;
+        const float* mlg = ml + 2 * g * R.nsplit;
+        float M = -INFINITY;
+        for (int q = 0; q < R.nsplit; ++q) M = fmaxf(M, mlg[2 * q]);
+        float num = 0.f, den = 0.f;
+        for (int q0 = 0; q0 < R.nsplit; q0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                v[k] = q0 + k < R.nsplit
+                           ? __ldcg(a.part + (static_cast<size_t>(h * a.nsplit + q0 + k) * G + g) * stride + d)
+                           : 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                if (q0 + k < R.nsplit) {
+                    const float w = expf(mlg[2 * (q0 + k)] - M);
+                    den += w * mlg[2 * (q0 + k) + 1];
+                    num += w * v[k];
+                }
+            }
+        }
+        a.out[static_cast<size_t>(h * G + g) * D + d] = num / den;
+    }
+    if (tid == 0) a.counter[h] = 0u;
+    return true;
+}
+
+}  // namespace acore
+}  // namespace rt

@@ -16,6 +16,7 @@ enum : int {
     kErrNone = 0,
     kErrMbarTimeout = 1,  // an mbarrier wait exceeded its iteration limit
     kErrShape = 2,        // a kernel saw an argument it cannot handle
+    kErrGridTimeout = 3,  // a grid-wide barrier of a persistent kernel timed out
 };
 
 // Iteration limit of every spin on an mbarrier.  Each try_wait may suspend the

@@ -219,4 +219,32 @@ cudaError_t q6k_to_bf16_launch(const uint8_t* q6, int64_t n_elem, uint16_t* out,
     return cudaGetLastError();
 }
 
+namespace {
+
+// One warp per 16-row x 144-byte unit, 16-byte words.
+__global__ void q4k_tile_major_kernel(const uint4* in, int64_t rows, int nseg, uint4* out, int64_t nunits) {
+    const int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (u >= nunits) return;
+    const int64_t t = u / nseg;
+    const int s = static_cast<int>(u - t * nseg);
+    for (int k = lane; k < 16 * 9; k += 32) {
+        const int i = k / 9, c = k - 9 * (k / 9);
+        const int64_t r = t * 16 + i;
+        out[u * 144 + k] = r < rows ? in[(r * nseg + s) * 9 + c] : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+}  // namespace
+
+cudaError_t q4k_tile_major_launch(const uint8_t* in, int64_t rows, int nseg, uint8_t* out, cudaStream_t s) {
+    const int64_t nunits = (rows + 15) / 16 * nseg;
+    if (nunits <= 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t blocks = (nunits * 32 + threads - 1) / threads;
+    q4k_tile_major_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(reinterpret_cast<const uint4*>(in), rows, nseg,
+                                                                          reinterpret_cast<uint4*>(out), nunits);
+    return cudaGetLastError();
+}
+
 }  // namespace rt

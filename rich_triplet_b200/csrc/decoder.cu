@@ -36,8 +36,10 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "convert.cuh"
 #include "gemv.cuh"
 #include "rt_internal.h"
+#include "step.cuh"
 
 using rt::fail;
 
@@ -74,6 +76,12 @@ struct rt_dec {
     int launches = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    // The persistent step kernel (one cooperative launch per step), when the
+    // shapes fit it; otherwise the captured graph of per-projection kernels.
+    bool use_step = false;
+    int step_grid = 0;
+    rt::StepGeom step_geom;
+    rt::StepParams step_params{};
     uint64_t dev_bytes = 0;
     std::vector<void*> allocs;
 };
@@ -287,6 +295,186 @@ int check_layer(rt_ctx* ctx, const rt_gemma3_cfg& c, const rt_gemma3_layer& L, i
     return RT_OK;
 }
 
+// Job and attention tables of the persistent step kernel, mirroring the
+// per-projection launches of enqueue_step (same buffers, same residual ping-pong).
+int build_step(rt_dec* d) {
+    rt_ctx* ctx = d->ctx;
+    const int H = d->H, D = d->D, NL = d->NL;
+    const int G = d->NQ / d->NKV;
+    const int kp_max = std::max({H, d->NQ * D, d->F});
+    d->step_geom = rt::step_geometry(H, kp_max, D, G);
+    if (!d->step_geom.warps) return RT_OK;  // shapes outside the step kernel: keep the graph
+    if (rt::step_prepare(d->step_geom) != cudaSuccess) {
+        cudaGetLastError();
+        return RT_OK;
+    }
+    const int grid = rt::step_max_grid(d->step_geom);
+    const int nsplit = std::min(grid / d->NKV, d->nsplit);  // the partials buffer holds d->nsplit slices
+    if (grid < ctx->num_sms || nsplit < 1) return RT_OK;
+    const int njobs = 4 * NL + 1;
+    std::vector<CUtensorMap> tm(njobs);
+    for (int l = 0; l < NL; ++l) {
+        tm[4 * l] = d->t_qkv[l];
+        tm[4 * l + 1] = d->t_o[l];
+        tm[4 * l + 2] = d->t_gu[l];
+        tm[4 * l + 3] = d->t_down[l];
+    }
+    tm[4 * NL] = d->t_lm;
+    CUtensorMap* d_tm = nullptr;
+    rt::gcore::Job* d_jobs = nullptr;
+    rt::AttnArgs* d_attn = nullptr;
+    uint32_t* d_sync = nullptr;
+    // Scratch indexed by CTA or by warp must cover the step kernel's own grid
+    // (the per-projection plans may use fewer CTAs).
+    float* s_part = nullptr;
+    float* s_am_val = nullptr;
+    int32_t* s_am_idx = nullptr;
+    const int64_t part_floats = static_cast<int64_t>(grid) * d->step_geom.warps * 2 * 16;
+    int rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&s_part), sizeof(float) * part_floats, "step partials")) != RT_OK) return rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&s_am_val), sizeof(float) * grid, "step argmax values")) != RT_OK) return rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&s_am_idx), sizeof(int32_t) * grid, "step argmax rows")) != RT_OK) return rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&d_tm), sizeof(CUtensorMap) * njobs, "step tensor maps")) != RT_OK) return rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&d_jobs), sizeof(rt::gcore::Job) * njobs, "step jobs")) != RT_OK) return rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&d_attn), sizeof(rt::AttnArgs) * NL, "step attention")) != RT_OK) return rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&d_sync), 4 * sizeof(uint32_t), "step sync")) != RT_OK) return rc;
+    // Tile-major copies of the Q4_K projections: each warp's share of a
+    // projection is then one contiguous byte range (1-D bulk copies).
+    auto tile_major = [&](const uint8_t* w, int64_t rows, int K, const uint8_t** out) -> int {
+        uint8_t* t = nullptr;
+        const size_t bytes = static_cast<size_t>((rows + 15) / 16) * (K / 256) * 2304;
+        int r = dalloc(d, reinterpret_cast<void**>(&t), bytes, "tile-major weight");
+        if (r != RT_OK) return r;
+        if (rt::q4k_tile_major_launch(w, rows, K / 256, t, ctx->stream) != cudaSuccess)
+            return fail(ctx, RT_E_CUDA, "tile-major weight copy");
+        *out = t;
+        return RT_OK;
+    };
+    std::vector<rt::gcore::Job> jobs(njobs);
+    std::vector<rt::AttnArgs> attn(NL);
+    const float eps = d->cfg.rms_norm_eps;
+    auto q4k = [&](int idx, int64_t rows, int K) -> rt::gcore::Job& {
+        rt::gcore::Job& j = jobs[idx];
+        j = rt::gcore::Job{};
+        j.tmap = d_tm + idx;
+        j.kind = rt::kQ4K;
+        j.K = K;
+        j.nseg = K / 256;
+        j.rows = rows;
+        j.eps = eps;
+        return j;
+    };
+    int p = 0;
+    for (int l = 0; l < NL; ++l) {
+        rt::gcore::Job& jq = q4k(4 * l, d->qkv_rows, H);
+        jq.tile_split = 1;
+        jq.g_pre = norm_ptr(d, l, 0);
+        jq.y = d->qkv;
+        if (l == 0) {
+            jq.embed = d->embed;
+            jq.token = d->ctl;
+            jq.embed_scale = sqrtf(static_cast<float>(H));
+            jq.resid_out = d->resid[0];
+            p = 0;
+        } else {
+            jq.src = d->down;
+            jq.resid_in = d->resid[p];
+            jq.resid_out = d->resid[1 - p];
+            jq.g_post = norm_ptr(d, l - 1, 3);
+            p = 1 - p;
+        }
+        rt::gcore::Job& jo = q4k(4 * l + 1, H, d->NQ * D);
+        jo.x = d->attn;
+        jo.y = d->o_out;
+        jo.tile_split = 1;
+        rt::gcore::Job& jg = q4k(4 * l + 2, 2LL * d->F, H);
+        jg.src = d->o_out;
+        jg.resid_in = d->resid[p];
+        jg.resid_out = d->resid[1 - p];
+        jg.g_post = norm_ptr(d, l, 1);
+        jg.g_pre = norm_ptr(d, l, 2);
+        jg.y = d->hbuf;
+        jg.tile_split = 1;
+        p = 1 - p;
+        rt::gcore::Job& jd = q4k(4 * l + 3, H, d->F);
+        jd.x = d->hbuf;
+        jd.y = d->down;
+        jd.tile_split = 1;
+        if ((rc = tile_major(d->w_qkv[l], d->qkv_rows, H, &jq.wt)) != RT_OK ||
+            (rc = tile_major(d->w_o[l], H, d->NQ * D, &jo.wt)) != RT_OK ||
+            (rc = tile_major(d->w_gu[l], 2LL * d->F, H, &jg.wt)) != RT_OK ||
+            (rc = tile_major(d->w_down[l], H, d->F, &jd.wt)) != RT_OK)
+            return rc;
+        rt::AttnArgs& a = attn[l];
+        a = rt::AttnArgs{};
+        a.qkv = d->qkv;
+        a.q_norm = d->qk_norms + static_cast<size_t>(l) * 2 * D;
+        a.k_norm = a.q_norm + D;
+        a.kcache = kc_layer(d, l);
+        a.vcache = vc_layer(d, l);
+        const int gsel = is_global(l) ? 1 : 0;
+        const size_t tab = static_cast<size_t>(d->cap) * (D / 2);
+        a.rope_cos = d->rope + (static_cast<size_t>(gsel) * 2 + 0) * tab;
+        a.rope_sin = d->rope + (static_cast<size_t>(gsel) * 2 + 1) * tab;
+        a.pos = d->ctl + 1;
+        a.cap = d->cap;
+        a.nq = d->NQ;
+        a.nkv = d->NKV;
+        a.D = D;
+        a.window = is_global(l) ? 0 : d->cfg.sliding_window;
+        a.nsplit = nsplit;
+        a.scale = 1.0f / sqrtf(d->cfg.query_pre_attn_scalar);
+        a.eps = eps;
+        a.part = d->attn_part;
+        a.counter = d->counters;
+        a.out = d->attn;
+        a.err = ctx->d_err;
+    }
+    rt::gcore::Job& jl = jobs[4 * NL];
+    jl = rt::gcore::Job{};
+    jl.tmap = d_tm + 4 * NL;
+    jl.kind = rt::kBF16;
+    jl.K = H;
+    jl.nseg = (H + 127) / 128;
+    jl.rows = d->V;
+    jl.eps = eps;
+    jl.src = d->down;
+    jl.resid_in = d->resid[p];
+    jl.resid_out = d->resid[1 - p];
+    jl.g_post = norm_ptr(d, NL - 1, 3);
+    jl.g_pre = d->final_norm;
+    jl.tile_split = 1;
+    jl.y = d->logits;
+    jl.am_val = s_am_val;
+    jl.am_idx = s_am_idx;
+    jl.am_counter = d->counters + d->NKV;
+    jl.token_out = d->ctl;
+    jl.pos_inout = d->ctl + 1;
+    jl.token_hist = d->ctl + 2;
+    cudaStream_t s = ctx->stream;
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(d_tm, tm.data(), sizeof(CUtensorMap) * njobs, cudaMemcpyHostToDevice, s));
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(d_jobs, jobs.data(), sizeof(rt::gcore::Job) * njobs, cudaMemcpyHostToDevice, s));
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(d_attn, attn.data(), sizeof(rt::AttnArgs) * NL, cudaMemcpyHostToDevice, s));
+    RT_CHECK_CUDA(ctx, cudaMemsetAsync(d_sync, 0, 4 * sizeof(uint32_t), s));
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(s));
+    rt::StepParams& P = d->step_params;
+    P.geom = d->step_geom;
+    P.jobs = d_jobs;
+    P.attn = d_attn;
+    P.nlayers = NL;
+    P.sync = d_sync;
+    P.abort = reinterpret_cast<int*>(d_sync + 2);
+    P.scratch = rt::gcore::SplitScratch{s_part, d->g_cnt};
+    P.err = ctx->d_err;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&P.trace), sizeof(uint64_t) * rt::kStepTraceLen, "step trace")) != RT_OK)
+        return rc;
+    RT_CHECK_CUDA(ctx, cudaMemset(P.trace, 0, sizeof(uint64_t) * rt::kStepTraceLen));
+    d->step_grid = grid;
+    d->use_step = getenv("RT_DECODER_GRAPH") == nullptr;
+    if (d->use_step) d->launches = 1;
+    return RT_OK;
+}
+
 int build_graph(rt_dec* d) {
     cudaStream_t s = d->ctx->stream;
     RT_CHECK_CUDA(d->ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
@@ -305,6 +493,11 @@ int build_graph(rt_dec* d) {
     return RT_OK;
 }
 
+cudaError_t launch_one_step(rt_dec* d, cudaStream_t s) {
+    if (d->use_step) return rt::step_launch(d->step_params, d->step_geom, d->step_grid, s);
+    return cudaGraphLaunch(d->exec, s);
+}
+
 cudaError_t set_ctl(rt_dec* d, int32_t token, int32_t pos) {
     set_ctl_kernel<<<1, 1, 0, d->ctx->stream>>>(d->ctl, token, pos);
     return cudaGetLastError();
@@ -315,6 +508,11 @@ int post_launch_check(rt_dec* d) {
         const int w = *d->h_err;
         *d->h_err = 0;
         cudaMemsetAsync(d->ctx->d_err, 0, sizeof(int), d->ctx->stream);
+        if (d->use_step) {
+            // an aborted step kernel leaves its barrier counters behind
+            cudaMemsetAsync(d->step_params.sync, 0, 2 * sizeof(uint32_t), d->ctx->stream);
+            cudaMemsetAsync(d->step_params.abort, 0, sizeof(int), d->ctx->stream);
+        }
         cudaStreamSynchronize(d->ctx->stream);
         return fail(d->ctx, RT_E_TIMEOUT, "decode step: a kernel reported error word %d", w);
     }
@@ -507,6 +705,7 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
     *d->h_err = 0;
     if (cudaStreamSynchronize(s) != cudaSuccess) return bail(fail(ctx, RT_E_CUDA, "rt_decoder_create: set-up failed"));
     if ((rc = build_graph(d)) != RT_OK) return bail(rc);
+    if ((rc = build_step(d)) != RT_OK) return bail(rc);
     *out = d;
     return RT_OK;
 }
@@ -550,7 +749,7 @@ int rt_decoder_step(rt_dec* d, int32_t token, int32_t position, float* logits) {
         return fail(d->ctx, RT_E_STATE, "rt_decoder_step: position %d outside the %d-position cache", position, d->cap);
     cudaStream_t s = d->ctx->stream;
     RT_CHECK_CUDA(d->ctx, set_ctl(d, token, position));
-    RT_CHECK_CUDA(d->ctx, cudaGraphLaunch(d->exec, s));
+    RT_CHECK_CUDA(d->ctx, launch_one_step(d, s));
     if (logits) RT_CHECK_CUDA(d->ctx, cudaMemcpyAsync(logits, d->logits, sizeof(float) * d->V, cudaMemcpyDeviceToHost, s));
     RT_CHECK_CUDA(d->ctx, cudaMemcpyAsync(d->h_err, d->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     RT_CHECK_CUDA(d->ctx, cudaStreamSynchronize(s));
@@ -567,7 +766,7 @@ int rt_decoder_prefill(rt_dec* d, const int32_t* tokens, int32_t n, int32_t star
     cudaStream_t s = d->ctx->stream;
     for (int i = 0; i < n; ++i) {
         RT_CHECK_CUDA(d->ctx, set_ctl(d, tokens[i], start_pos + i));
-        RT_CHECK_CUDA(d->ctx, cudaGraphLaunch(d->exec, s));
+        RT_CHECK_CUDA(d->ctx, launch_one_step(d, s));
     }
     if (last_logits) RT_CHECK_CUDA(d->ctx, cudaMemcpyAsync(last_logits, d->logits, sizeof(float) * d->V, cudaMemcpyDeviceToHost, s));
     RT_CHECK_CUDA(d->ctx, cudaMemcpyAsync(d->h_err, d->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -585,7 +784,7 @@ int rt_decoder_generate(rt_dec* d, int32_t first_token, int32_t start_pos, int32
         return fail(d->ctx, RT_E_STATE, "rt_decoder_generate: positions %d..%d outside the cache", start_pos, start_pos + n - 1);
     cudaStream_t s = d->ctx->stream;
     RT_CHECK_CUDA(d->ctx, set_ctl(d, first_token, start_pos));
-    for (int i = 0; i < n; ++i) RT_CHECK_CUDA(d->ctx, cudaGraphLaunch(d->exec, s));
+    for (int i = 0; i < n; ++i) RT_CHECK_CUDA(d->ctx, launch_one_step(d, s));
     if (flags == RT_DEVICE) return RT_OK;
     if (tokens_out)
         RT_CHECK_CUDA(d->ctx, cudaMemcpyAsync(tokens_out, d->ctl + 2 + start_pos, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
@@ -622,6 +821,17 @@ int rt_decoder_read_activation(rt_dec* d, int32_t which, float* host, int64_t co
     } else if (which == 1) {
         src = d->logits;
         n = d->V;
+    } else if (which >= 3 && which <= 7) {
+        // the last layer's intermediate vectors: qkv, attention output, O
+        // projection, GELU-gated FFN hidden, down projection
+        const float* v[5] = {d->qkv, d->attn, d->o_out, d->hbuf, d->down};
+        const int64_t nv[5] = {d->qkv_rows, static_cast<int64_t>(d->NQ) * d->D, d->H, d->F, d->H};
+        src = v[which - 3];
+        n = nv[which - 3];
+    } else if (which == 2 && d->use_step) {
+        // phase timeline of the last step kernel: kStepTraceLen u64 as 2x f32 each
+        src = reinterpret_cast<const float*>(d->step_params.trace);
+        n = 2 * rt::kStepTraceLen;
     } else {
         return fail(d->ctx, RT_E_INVAL, "rt_decoder_read_activation: unknown vector %d", which);
     }

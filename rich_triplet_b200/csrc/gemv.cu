@@ -83,7 +83,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     carve(smem, KIND, a.K, a.nseg, nw, a.nb, PRO, &S);
     if (tid == 0) {
         Job& j = *S.job;
+        j = Job{};
         j.tmap = &tmap;
+        j.wt = nullptr;  // row-major W, 2-D tensor copies
         j.kind = KIND;
         j.K = a.K;
         j.nseg = a.nseg;
@@ -112,14 +114,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     }
     __syncthreads();
     const Job& job = *S.job;
-    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx};
+    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx, nullptr};
 
     // Each warp's weight stream starts before the wait on the previous kernel
     // (weights are constants), and so do the norm weights.
     const int ubytes = unit_bytes(KIND);
     Stream st;
     stream_start(st, S.full + warp * a.nb, S.ring + static_cast<size_t>(warp) * a.nb * ubytes, a.nb, ubytes, S.job, 1,
-                 blockIdx.x * static_cast<uint32_t>(nw) + warp, gridDim.x * static_cast<uint32_t>(nw), lane);
+                 lane);
     if (tid == 0) prefetch_gammas(job, PRO, JS);
     pdl_launch_dependents();
     pdl_wait();

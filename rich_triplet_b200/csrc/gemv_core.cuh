@@ -29,8 +29,8 @@
 // rows; a byte mask keeps the low nibbles (sub-block 2c) or the high nibbles
 // (sub-block 2c+1, as 16 q) as the u8 A operand of mma.m16n8k32.u8.s8.  x is
 // split once per job, per sub-block, into three int8 planes
-// x = s * (p0 + p1/128 + p2/16384) (|error| <= s/32768, s = max|x|/127 over the
-// sub-block), the s8 B operand.  The MMA of sub-block j puts planes 0/1 in B
+// x = s * (p0 + p1/254 + p2/254^2) (|error| <= s/129032, s = max|x|/127 over
+// the sub-block), the s8 B operand.  The MMA of sub-block j puts planes 0/1 in B
 // columns 2(j&3), 2(j&3)+1 (and plane 2 in column 2(j&3) of a second MMA), zero
 // elsewhere, so lane t of every lane quad ends up holding the three plane sums
 // of sub-blocks t and t+4 for two rows, and all 32 lanes share the scale
@@ -156,19 +156,23 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    // x = s (p0 + p1/254 + p2/254^2): each residual spans the full int8 range,
+    // |error| <= s / (2 * 254^2).  The clamps only guard the rounding edge.
     const float s = m / 127.0f;
     const float inv = m > 0.f ? 127.0f / m : 0.f;
-    const float s128 = s * (1.0f / 128.0f);
-    const float inv128 = inv * 128.0f, inv16k = inv * 16384.0f;
+    const float s254 = s * (1.0f / 254.0f);
+    const float inv254 = inv * 254.0f, inv254sq = inv * 64516.0f;
     int q0[8], q1[8], q2[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
         float f0, f1, f2;
-        q0[e] = round_magic(xv[e] * inv, &f0);
+        q0[e] = min(127, max(-127, round_magic(xv[e] * inv, &f0)));
+        f0 = static_cast<float>(q0[e]);
         const float r1 = fmaf(-f0, s, xv[e]);
-        q1[e] = round_magic(r1 * inv128, &f1);
-        const float r2 = fmaf(-f1, s128, r1);
-        q2[e] = round_magic(r2 * inv16k, &f2);
+        q1[e] = min(127, max(-127, round_magic(r1 * inv254, &f1)));
+        f1 = static_cast<float>(q1[e]);
+        const float r2 = fmaf(-f1, s254, r1);
+        q2[e] = min(127, max(-127, round_magic(r2 * inv254sq, &f2)));
     }
     const int j = lane >> 2;  // sub-block of this lane's elements
     const int r = j & 3, half = j >> 2;
@@ -187,7 +191,7 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
     *reinterpret_cast<uint32_t*>(P2 + o1) = pack4(q2[4], q2[5], q2[6], q2[7]);
     if ((lane & 3) == 0) {
         // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
-        const float unit = s * (1.0f / 16384.0f) * ((j & 1) ? 0.0625f : 1.0f);
+        const float unit = s * (1.0f / 64516.0f) * ((j & 1) ? 0.0625f : 1.0f);
         xsx[seg * 8 + j] = make_float2(unit, sum);
     }
 }
@@ -242,14 +246,22 @@ struct Split {
     }
 };
 
+// Q4_K units per copy when W is stored tile-major (see Job::wt).
+constexpr int kTileMajorUnitsPerCopy = 2;
+
 // One GEMV as the kernels see it.
 struct Job {
-    const void* tmap;  // CUtensorMap of W (parameter or global memory)
-    int32_t kind;      // kQ4K / kBF16
+    const void* tmap;   // CUtensorMap of W (parameter or global memory), row-major W
+    const uint8_t* wt;  // Q4_K only, or null: W stored tile-major, unit (t, s) at
+                        // ((t * nseg) + s) * 2304 bytes (16 rows x 144 bytes, rows
+                        // past the matrix zero), so a warp's share of units is one
+                        // contiguous byte range, copied by 1-D bulk copies
+    int32_t kind;       // kQ4K / kBF16
     int32_t K;
     int32_t nseg;      // column segments per row
     int32_t pad;
     int64_t rows;
+    int32_t tile_split;  // 1: each CTA takes whole tiles, its warps split them (combined by cta_combine)
     // prologue
     const float* x;
     const float* src;
@@ -275,6 +287,35 @@ __device__ __forceinline__ uint32_t job_units(const Job& j) {
     return static_cast<uint32_t>((j.rows + kTile - 1) / kTile) * static_cast<uint32_t>(j.nseg);
 }
 
+// A warp's units [s, e) of a job.
+struct Share {
+    uint32_t s, e;
+};
+
+// Whole-grid split (tile_split == 0): every warp of the grid an equal,
+// contiguous share of the tile-major unit sequence; tiles may straddle warps
+// of different CTAs.  Tile split: CTA c takes whole tiles
+// [floor(T c / G), floor(T (c+1) / G)) and its warps share those tiles' units
+// equally, so no tile ever straddles CTAs.
+__device__ __forceinline__ Share warp_share(const Job& j, uint32_t cta, uint32_t ncta, uint32_t warp, uint32_t nw) {
+    const uint32_t nseg = static_cast<uint32_t>(j.nseg);
+    const uint32_t ntiles = static_cast<uint32_t>((j.rows + kTile - 1) / kTile);
+    if (j.tile_split) {
+        Split ct;
+        ct.init(ntiles, ncta);
+        const uint32_t tb = ct.start(cta), te = ct.start(cta + 1);
+        const uint32_t n = (te - tb) * nseg;
+        if (n == 0) return Share{0, 0};
+        Split wt;
+        wt.init(n, nw);
+        return Share{tb * nseg + wt.start(warp), tb * nseg + wt.start(warp + 1)};
+    }
+    Split sp;
+    sp.init(ntiles * nseg, ncta * nw);
+    const uint32_t gw = cta * nw + warp;
+    return Share{sp.start(gw), sp.start(gw + 1)};
+}
+
 // Grid-wide scratch of the split tiles.
 struct SplitScratch {
     float* part;         // [NW][2][16]
@@ -293,7 +334,7 @@ struct Stream {
     uint64_t pol;
     const Job* jobs;
     int njobs;
-    uint32_t gw, NW;
+    uint32_t cta, ncta, warp, nw;  // this warp's place in the grid
     // issue cursor
     int ij;              // job being issued (njobs: done)
     uint32_t iu, iend;   // next unit, end of this warp's share of job ij
@@ -301,15 +342,14 @@ struct Stream {
     int iseg;
     int islot;           // slot the next copy goes to
     int issued;          // copies issued, all jobs
-    int consumed;        // units consumed, all jobs
+    int consumed;        // copies consumed, all jobs
 
     // Move the cursor to the next job in which this warp has units.
     __device__ __forceinline__ void seek(int j) {
         for (ij = j; ij < njobs; ++ij) {
-            Split sp;
-            sp.init(job_units(jobs[ij]), NW);
-            iu = sp.start(gw);
-            iend = sp.start(gw + 1);
+            const Share sh = warp_share(jobs[ij], cta, ncta, warp, nw);
+            iu = sh.s;
+            iend = sh.e;
             if (iu < iend) {
                 const uint32_t ns = static_cast<uint32_t>(jobs[ij].nseg);
                 itile = iu / ns;
@@ -318,22 +358,33 @@ struct Stream {
             }
         }
     }
-    // lane 0: issue the next unit into slot `islot`, if any is left.
+    // lane 0: issue the next copy (one unit, or up to kTileMajorUnitsPerCopy
+    // consecutive units of a tile-major W) into slot `islot`, if any is left.
     __device__ __forceinline__ bool issue() {
         if (ij >= njobs) return false;
         const Job& jo = jobs[ij];
         const int kind = jo.kind;
         uint64_t* bar = &full[islot];
-        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(unit_bytes(kind)));
-        tma_2d_g2s(ring + static_cast<size_t>(islot) * slot_bytes, jo.tmap, iseg * box_step(kind),
-                   static_cast<int>(itile * kTile), bar, pol);
+        uint8_t* dst = ring + static_cast<size_t>(islot) * slot_bytes;
+        int k = 1;
+        if (jo.wt) {
+            k = min(static_cast<uint32_t>(kTileMajorUnitsPerCopy), iend - iu);
+            const uint32_t bytes = static_cast<uint32_t>(k) * kQ4KUnit;
+            mbar_arrive_expect_tx(bar, bytes);
+            bulk_g2s(dst, jo.wt + static_cast<size_t>(iu) * kQ4KUnit, bytes, bar, pol);
+        } else {
+            mbar_arrive_expect_tx(bar, static_cast<uint32_t>(unit_bytes(kind)));
+            tma_2d_g2s(dst, jo.tmap, iseg * box_step(kind), static_cast<int>(itile * kTile), bar, pol);
+        }
         if (++islot == nb) islot = 0;
         ++issued;
-        if (++iseg == jo.nseg) {
-            iseg = 0;
-            ++itile;
-        }
-        if (++iu == iend) seek(ij + 1);
+        for (int u = 0; u < k; ++u)
+            if (++iseg == jo.nseg) {
+                iseg = 0;
+                ++itile;
+            }
+        iu += static_cast<uint32_t>(k);
+        if (iu == iend) seek(ij + 1);
         return true;
     }
 };
@@ -342,7 +393,7 @@ struct Stream {
 // issues the first copies.  The caller makes the barrier init visible
 // (__syncthreads or __syncwarp) before any other lane waits on them.
 __device__ __forceinline__ void stream_start(Stream& s, uint64_t* full, uint8_t* ring, int nb, int slot_bytes,
-                                             const Job* jobs, int njobs, uint32_t gw, uint32_t NW, int lane) {
+                                             const Job* jobs, int njobs, int lane) {
     s.full = full;
     s.ring = ring;
     s.nb = nb;
@@ -352,8 +403,10 @@ __device__ __forceinline__ void stream_start(Stream& s, uint64_t* full, uint8_t*
     s.pol = l2_evict_first_policy();
     s.jobs = jobs;
     s.njobs = njobs;
-    s.gw = gw;
-    s.NW = NW;
+    s.cta = blockIdx.x;
+    s.ncta = gridDim.x;
+    s.warp = threadIdx.x >> 5;
+    s.nw = blockDim.x >> 5;
     s.islot = 0;
     s.issued = 0;
     s.consumed = 0;
@@ -383,6 +436,7 @@ struct JobSmem {
     float* gpre;     // [K]
     uint8_t* planes;
     float2* xsx;
+    float* wpart;    // [warps][2][16] per-warp pieces of tiles shared within the CTA (cta_combine)
 };
 
 // Thread 0: fetch the norm weights of `j` (prologue `pro`) into gpost / gpre,
@@ -449,10 +503,10 @@ __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uin
                 if (c0 < K) {
                     const float4 s0 = *reinterpret_cast<const float4*>(a.src + c0);
                     const float4 s1 = *reinterpret_cast<const float4*>(a.src + c0 + 4);
-                    const float4 r0 = *reinterpret_cast<const float4*>(a.resid_in + c0);
-                    const float4 r1 = *reinterpret_cast<const float4*>(a.resid_in + c0 + 4);
                     v[i][0] = s0.x; v[i][1] = s0.y; v[i][2] = s0.z; v[i][3] = s0.w;
                     v[i][4] = s1.x; v[i][5] = s1.y; v[i][6] = s1.z; v[i][7] = s1.w;
+                    const float4 r0 = *reinterpret_cast<const float4*>(a.resid_in + c0);
+                    const float4 r1 = *reinterpret_cast<const float4*>(a.resid_in + c0 + 4);
                     xr[i][0] = r0.x; xr[i][1] = r0.y; xr[i][2] = r0.z; xr[i][3] = r0.w;
                     xr[i][4] = r1.x; xr[i][5] = r1.y; xr[i][6] = r1.z; xr[i][7] = r1.w;
                 } else {
@@ -548,10 +602,12 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     const int nseg = a.nseg;
     const int Kp = nseg * seg_cols(KIND);
     const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
-    Split sp;
-    sp.init(job_units(a), st.NW);
-    const uint32_t u_begin = sp.start(st.gw);
-    const int n = static_cast<int>(sp.start(st.gw + 1) - u_begin);
+    const uint32_t gw = st.cta * st.nw + st.warp;
+    Split sp;  // the whole-grid split (owner lookups of the per-warp combine)
+    sp.init(job_units(a), st.ncta * st.nw);
+    const Share sh = warp_share(a, st.cta, st.ncta, st.warp, st.nw);
+    const uint32_t u_begin = sh.s;
+    const int n = static_cast<int>(sh.e - sh.s);
 
     // Row epilogue: lane L < 16 holds the sum of row r0 + L.
     auto emit_rows = [&](int64_t r0, float v) {
@@ -585,10 +641,16 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     int seg = static_cast<int>(u_begin - tile * nseg);
     const uint32_t first_tile = tile;
     int pu = 0;  // units of the current tile piece
+    const int upc = a.wt ? kTileMajorUnitsPerCopy : 1;
+    int in_copy = 0, uic = 0;  // units left in / consumed from the current copy
     for (int i = 0; i < n; ++i) {
-        const bool ok = mbar_wait(&st.full[st.jb], st.ph);
-        if (__any_sync(0xffffffffu, !ok)) return false;
-        const uint8_t* ub = st.ring + static_cast<size_t>(st.jb) * st.slot_bytes;
+        if (in_copy == 0) {
+            const bool ok = mbar_wait(&st.full[st.jb], st.ph);
+            if (__any_sync(0xffffffffu, !ok)) return false;
+            in_copy = min(upc, n - i);
+            uic = 0;
+        }
+        const uint8_t* ub = st.ring + static_cast<size_t>(st.jb) * st.slot_bytes + uic * unit_bytes(KIND);
         if constexpr (KIND == kQ4K) {
             // B fragments: planes 0/1 of sub-blocks q and q+4 (this lane's column
             // pair) and, for even g, plane 2.
@@ -630,10 +692,10 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
                 const float sc0 = byte_to_float(s_lo, jsel), mn0 = byte_to_float(m_lo, jsel);
                 const float sc1 = byte_to_float(s_hi, jsel), mn1 = byte_to_float(m_hi, jsel);
                 const int i0 = 2 * half;
-                const float T0 = fmaf(static_cast<float>(c01[0][i0]), 16384.0f,
-                                      fmaf(static_cast<float>(c01[0][i0 + 1]), 128.0f, static_cast<float>(c2[0][i0])));
-                const float T1 = fmaf(static_cast<float>(c01[1][i0]), 16384.0f,
-                                      fmaf(static_cast<float>(c01[1][i0 + 1]), 128.0f, static_cast<float>(c2[1][i0])));
+                const float T0 = fmaf(static_cast<float>(c01[0][i0]), 64516.0f,
+                                      fmaf(static_cast<float>(c01[0][i0 + 1]), 254.0f, static_cast<float>(c2[0][i0])));
+                const float T1 = fmaf(static_cast<float>(c01[1][i0]), 64516.0f,
+                                      fmaf(static_cast<float>(c01[1][i0 + 1]), 254.0f, static_cast<float>(c2[1][i0])));
                 const float v = d * (sc0 * (T0 * xa.x) + sc1 * (T1 * xb.x)) - dmin * (mn0 * xa.y + mn1 * xb.y);
                 if (half) acc1 += v;
                 else acc0 += v;
@@ -657,16 +719,19 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
             acc1 += ((c[0][2] + c[1][2]) + (c[2][2] + c[3][2])) + ((c[0][3] + c[1][3]) + (c[2][3] + c[3][3]));
         }
         ++pu;
-        ++st.consumed;
-        // Release the slot to the next copy of this warp's stream (any job).
-        __syncwarp();
-        if (lane == 0) {
-            fence_proxy_async_smem();
-            st.issue();
-        }
-        if (++st.jb == st.nb) {
-            st.jb = 0;
-            st.ph ^= 1u;
+        ++uic;
+        if (--in_copy == 0) {
+            // Release the slot to the next copy of this warp's stream (any job).
+            ++st.consumed;
+            __syncwarp();
+            if (lane == 0) {
+                fence_proxy_async_smem();
+                st.issue();
+            }
+            if (++st.jb == st.nb) {
+                st.jb = 0;
+                st.ph ^= 1u;
+            }
         }
         const bool tile_end = ++seg == nseg;
         if (tile_end || i == n - 1) {
@@ -681,13 +746,17 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
             const int64_t r0 = static_cast<int64_t>(tile) * kTile;
             if (pu == nseg) {
                 emit_rows(r0, rowv);
+            } else if (a.tile_split) {
+                // Combined later by the CTA (cta_combine), in shared memory.
+                const int slot = tile == first_tile ? 0 : 1;
+                if (lane < kTile) S.wpart[((threadIdx.x >> 5) * 2 + slot) * kTile + lane] = rowv;
             } else {
                 // Lanes 16..31 (row = lane - 16) publish the piece.
                 const int slot = tile == first_tile ? 0 : 1;
                 const bool pub = lane >= kTile;
                 const float rv = __shfl_sync(0xffffffffu, rowv, lane & (kTile - 1));
                 if (pub) {
-                    sc.part[(static_cast<int64_t>(st.gw) * 2 + slot) * kTile + (lane - kTile)] = rv;
+                    sc.part[(static_cast<int64_t>(gw) * 2 + slot) * kTile + (lane - kTile)] = rv;
                     __threadfence();
                 }
                 __syncwarp();
@@ -732,6 +801,56 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
         }
     }
     return true;
+}
+
+// After every warp of the CTA ran job_units_run on a job with tile_split set:
+// add, in warp order, the pieces of the tiles this CTA's warps shared (one
+// warp per tile, from shared memory) and run the epilogue on them.  All
+// threads call it; it starts with __syncthreads.
+template <int EPI>
+__device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, float& best_v, long long& best_i) {
+    __syncthreads();
+    const uint32_t nw = blockDim.x >> 5, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t nseg = static_cast<uint32_t>(a.nseg);
+    const uint32_t ntiles = static_cast<uint32_t>((a.rows + kTile - 1) / kTile);
+    Split ct;
+    ct.init(ntiles, gridDim.x);
+    const uint32_t tb = ct.start(blockIdx.x), te = ct.start(blockIdx.x + 1);
+    if (tb >= te) return;
+    Split wt;  // the warps' split of this CTA's units, numbered from the CTA's first unit
+    wt.init((te - tb) * nseg, nw);
+    // lane -> row (or the first row of a GELU pair)
+    constexpr int kPer = EPI == kEpiGeluPair ? kTile / 2 : kTile;
+    const int row = EPI == kEpiGeluPair ? 2 * lane : lane;
+    for (uint32_t T = tb + warp; T < te; T += nw) {
+        const uint32_t u0 = (T - tb) * nseg;
+        const uint32_t wa = wt.owner(u0), wb = wt.owner(u0 + nseg - 1);
+        if (wa == wb) continue;  // one warp had it all: already through the epilogue
+        if (lane >= kPer) continue;
+        float v0 = 0.f, v1 = 0.f;
+        for (uint32_t w = wa; w <= wb; ++w) {
+            const uint32_t s_w = wt.start(w);
+            if (wt.start(w + 1) <= s_w) continue;
+            // a warp that began in an earlier tile keeps this one in slot 1
+            const float* pw = S.wpart + (w * 2 + (s_w < u0 ? 1 : 0)) * kTile;
+            v0 += pw[row];
+            if constexpr (EPI == kEpiGeluPair) v1 += pw[row + 1];
+        }
+        const int64_t r = static_cast<int64_t>(T) * kTile + row;
+        if (r >= a.rows) continue;
+        if constexpr (EPI == kEpiGeluPair) {
+            a.y[r >> 1] = __fmul_rn(gelu_tanh_dev(v0), v1);
+        } else {
+            a.y[r] = v0;
+            if constexpr (EPI == kEpiArgmax) {
+                if (v0 > best_v || (v0 == best_v && r > best_i)) {
+                    best_v = v0;
+                    best_i = r;
+                }
+            }
+        }
+    }
 }
 
 // Greedy argmax over the grid (largest value; ties to the higher row index),

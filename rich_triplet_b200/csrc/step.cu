@@ -1,0 +1,361 @@
+// step.cu -- the persistent Gemma 3 decode-step kernel.
+//
+// One cooperative launch runs a whole decode step: for every layer the QKV
+// projection (with the fused residual/RMSNorm prologue), attention, the O
+// projection, gate/up with the GELU gate and the down projection, then the LM
+// head with the greedy argmax (Gemma3Block::forward_cached,
+// src/transformer4.rs:1954-1964, and MetalDecodeContext::decode_step,
+// src/metal_decode.rs:1930-2074).  One CTA per SM, all resident at once; a
+// grid-wide barrier separates phases whose inputs are the previous phase's
+// outputs.
+//
+// What this buys over one launch per projection: every warp's weight stream
+// (gemv_core.cuh) runs through all the step's projections back to back, so
+// the copies of the next projection's weights are already in flight, or in
+// shared memory, while the grid waits at a barrier; and there is no kernel
+// launch, no first-copy latency and no drain between projections.  The GEMV
+// and attention arithmetic is the same code the standalone kernels run.
+//
+// Every wait is bounded: mbarrier waits by iteration count, grid barriers by
+// time (globaltimer).  A CTA that gives up raises `abort`; the others see it
+// at their next barrier, wait (bounded) for their own copies in flight, and
+// leave.
+#include <algorithm>
+
+#include "attention_core.cuh"
+#include "common.cuh"
+#include "gemv_core.cuh"
+#include "step.cuh"
+
+namespace rt {
+
+namespace {
+
+using namespace gcore;
+
+constexpr int kStepWarps = 16;
+constexpr int kStepNb = 2;           // 32 copies in flight per SM
+constexpr int kSlotBytes =  // a ring slot holds a BF16 unit or a copy of tile-major Q4_K units
+    kBF16Unit > kTileMajorUnitsPerCopy * kQ4KUnit ? kBF16Unit : kTileMajorUnitsPerCopy * kQ4KUnit;
+constexpr int kAttnT = 16;           // cached positions per attention tile
+constexpr uint64_t kBarrierTimeoutNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct StepSmem {
+    uint64_t* full;  // [warps][nb]
+    uint64_t* pbar;
+    uint64_t* abar;  // attention tile barrier (kept out of `uni`: see attn_bar_init)
+    float* red;
+    int* flags;      // 0: this CTA failed, 1: last CTA (argmax), 2: barrier result, 3: attention copy pending
+    float* bv;
+    long long* bi;
+    float* gpost;    // [hidden]
+    float* gpre;     // [hidden]
+    float* wpart;    // [warps][2][16]
+    uint8_t* uni;    // planes + xsx of a projection, or an attention item
+    float2* xsx;
+    uint8_t* ring;   // [warps][nb][kSlotBytes]
+};
+
+__host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, StepSmem* S) {
+    size_t off = 0;
+    auto take = [&](size_t bytes, size_t align) -> uint8_t* {
+        off = (off + align - 1) / align * align;
+        uint8_t* p = base + off;
+        off += bytes;
+        return p;
+    };
+    uint8_t* full = take(sizeof(uint64_t) * g.warps * g.nb, 16);
+    uint8_t* pbar = take(sizeof(uint64_t), 16);
+    uint8_t* abar = take(sizeof(uint64_t), 16);
+    uint8_t* red = take(32 * 4, 16);
+    uint8_t* flags = take(4 * 4, 16);
+    uint8_t* bv = take(4 * 32, 16);
+    uint8_t* bi = take(8 * 32, 16);
+    uint8_t* gpost = take(sizeof(float) * g.hidden, 16);
+    uint8_t* gpre = take(sizeof(float) * g.hidden, 16);
+    uint8_t* wpart = take(sizeof(float) * g.warps * 2 * 16, 16);
+    const size_t q4 = (planes_bytes(kQ4K, g.kp_max) + 127) / 128 * 128;
+    const size_t q4all = q4 + xsx_bytes(kQ4K, g.kp_max), bf = planes_bytes(kBF16, g.kp_lm);
+    const size_t proj = q4all > bf ? q4all : bf;
+    const size_t att = acore::attn_carve(nullptr, g.head_dim, g.group, kAttnT, nullptr);
+    uint8_t* uni = take(proj > att ? proj : att, 128);
+    uint8_t* ring = take(static_cast<size_t>(g.warps) * g.nb * kSlotBytes, 128);
+    if (S) {
+        S->full = reinterpret_cast<uint64_t*>(full);
+        S->pbar = reinterpret_cast<uint64_t*>(pbar);
+        S->abar = reinterpret_cast<uint64_t*>(abar);
+        S->red = reinterpret_cast<float*>(red);
+        S->flags = reinterpret_cast<int*>(flags);
+        S->bv = reinterpret_cast<float*>(bv);
+        S->bi = reinterpret_cast<long long*>(bi);
+        S->gpost = reinterpret_cast<float*>(gpost);
+        S->gpre = reinterpret_cast<float*>(gpre);
+        S->wpart = reinterpret_cast<float*>(wpart);
+        S->uni = uni;
+        S->xsx = reinterpret_cast<float2*>(uni + q4);
+        S->ring = ring;
+    }
+    return off;
+}
+
+// Grid-wide barrier (all threads call it).  Returns false when the grid must
+// stop: this CTA failed, another CTA raised `abort`, or the wait timed out.
+__device__ __forceinline__ bool grid_sync(const StepParams& P, uint32_t& nsync, int* flags) {
+    __syncthreads();
+    ++nsync;
+    if (threadIdx.x == 0) {
+        bool ok = flags[0] == 0;
+        if (!ok) atomicExch(P.abort, 1);
+        __threadfence();
+        atomicAdd(&P.sync[0], 1u);
+        const uint32_t target = nsync * gridDim.x;
+        const uint64_t t0 = gtimer();
+        uint32_t spin = 0;
+        while (ok) {
+            if (ld_acquire_u32(&P.sync[0]) >= target) break;
+            if (*reinterpret_cast<volatile int*>(P.abort)) {
+                ok = false;
+                break;
+            }
+            if ((++spin & 63u) == 0u && gtimer() - t0 > kBarrierTimeoutNs) {
+                if (P.err) atomicExch(P.err, kErrGridTimeout);
+                atomicExch(P.abort, 1);
+                ok = false;
+            }
+        }
+        __threadfence();
+        flags[2] = ok ? 1 : 0;
+    }
+    __syncthreads();
+    return flags[2] != 0;
+}
+
+// Stream this warp's units of a projection; on failure drain the warp's copies
+// and mark the CTA failed.
+template <int KIND, int EPI>
+__device__ __forceinline__ void run_units(const Job& j, Stream& st, const JobSmem& JS, const StepParams& P,
+                                          int* flags, float& best_v, long long& best_i) {
+    if (!job_units_run<KIND, EPI>(j, st, JS, P.scratch, best_v, best_i)) {
+        if ((threadIdx.x & 31) == 0) {
+            atomicExch(&flags[0], 1);
+            if (P.err) atomicExch(P.err, kErrMbarTimeout);
+            stream_drain(st);
+        }
+        __syncwarp();
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepParams P) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t{127});
+    StepSmem S;
+    step_carve(smem, P.geom, &S);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nb = P.geom.nb;
+    acore::AttnSmem AS;
+    acore::attn_carve(S.uni, P.geom.head_dim, G, kAttnT, &AS);
+    AS.bar = S.abar;
+    if (tid == 0) {
+        mbar_init(S.pbar, 1);
+        acore::attn_bar_init(AS);
+        S.flags[0] = S.flags[1] = S.flags[2] = S.flags[3] = 0;
+    }
+    __syncthreads();
+    const JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.uni, S.xsx, S.wpart};
+    const int njobs = 4 * P.nlayers + 1;
+    Stream st;
+    stream_start(st, S.full + warp * nb, S.ring + static_cast<size_t>(warp) * nb * kSlotBytes, nb, kSlotBytes, P.jobs,
+                 njobs, lane);
+    if (tid == 0) prefetch_gammas(P.jobs[0], kProEmbedNorm, JS);
+    uint32_t pph = 0;  // gamma barrier phase
+    uint32_t nsync = 0;
+    uint32_t aph = 0;  // attention barrier phases completed
+    float best_v = -INFINITY;
+    long long best_i = -1;
+
+    // Phase timeline of CTA 0 (tracing; a few stores per phase).
+    const bool tr = P.trace && blockIdx.x == 0 && tid == 0;
+    auto stamp = [&](int slot) {
+        if (tr && slot < kStepTraceLen) P.trace[slot] = gtimer();
+    };
+    stamp(0);
+    bool ok = true;
+    for (int l = 0; l < P.nlayers && ok; ++l) {
+        const Job& jq = P.jobs[4 * l];
+        const Job& jo = P.jobs[4 * l + 1];
+        const Job& jg = P.jobs[4 * l + 2];
+        const Job& jd = P.jobs[4 * l + 3];
+        const AttnArgs& at = P.attn[l];
+        // ---- QKV (residual update + attention RMSNorm in the prologue) ----
+        if (l == 0) job_prologue<kQ4K, kProEmbedNorm>(jq, JS, pph);
+        else job_prologue<kQ4K, kProResidNorm>(jq, JS, pph);
+        pph ^= 1u;
+        if (tid == 0) prefetch_gammas(jg, kProResidNorm, JS);
+        run_units<kQ4K, kEpiPlain>(jq, st, JS, P, S.flags, best_v, best_i);
+        cta_combine<kEpiPlain>(jq, JS, best_v, best_i);
+        stamp(1 + 10 * l);
+        // ---- attention: its first cached K/V tile is copied during the barrier ----
+        const int items = at.nkv * at.nsplit;
+        const int h = blockIdx.x / at.nsplit, s = blockIdx.x % at.nsplit;
+        const bool has_item = static_cast<int>(blockIdx.x) < items;
+        acore::AttnRange R{};
+        __syncthreads();  // every warp is done with the projection's planes
+        if (has_item) {
+            R = acore::attn_range(at, h, s, kAttnT);
+            if (tid == 0) {
+                acore::attn_prefetch(at, R, AS, kAttnT);
+                S.flags[3] = R.active && R.ntiles > 0;
+            }
+        }
+        ok = grid_sync(P, nsync, S.flags);
+        stamp(2 + 10 * l);
+        if (ok && has_item) {
+            if (!acore::attn_run<G, kAttnT>(at, h, s, R, AS, aph & 1u)) {
+                if (tid == 0) atomicExch(&S.flags[0], 1);
+            }
+            if (tid == 0) S.flags[3] = 0;
+            if (R.active) aph += static_cast<uint32_t>(R.ntiles);
+        }
+        stamp(3 + 10 * l);
+        if (ok) ok = grid_sync(P, nsync, S.flags);
+        stamp(4 + 10 * l);
+        if (!ok) break;
+        // ---- O ----
+        job_prologue<kQ4K, kProPlain>(jo, JS, 0u);
+        run_units<kQ4K, kEpiPlain>(jo, st, JS, P, S.flags, best_v, best_i);
+        cta_combine<kEpiPlain>(jo, JS, best_v, best_i);
+        stamp(5 + 10 * l);
+        if (!(ok = grid_sync(P, nsync, S.flags))) break;
+        stamp(6 + 10 * l);
+        // ---- gate / up (residual update + FFN RMSNorm), GELU gate ----
+        job_prologue<kQ4K, kProResidNorm>(jg, JS, pph);
+        pph ^= 1u;
+        if (tid == 0) prefetch_gammas(P.jobs[l + 1 < P.nlayers ? 4 * (l + 1) : 4 * P.nlayers], kProResidNorm, JS);
+        run_units<kQ4K, kEpiGeluPair>(jg, st, JS, P, S.flags, best_v, best_i);
+        cta_combine<kEpiGeluPair>(jg, JS, best_v, best_i);
+        stamp(7 + 10 * l);
+        if (!(ok = grid_sync(P, nsync, S.flags))) break;
+        stamp(8 + 10 * l);
+        // ---- down ----
+        job_prologue<kQ4K, kProPlain>(jd, JS, 0u);
+        run_units<kQ4K, kEpiPlain>(jd, st, JS, P, S.flags, best_v, best_i);
+        cta_combine<kEpiPlain>(jd, JS, best_v, best_i);
+        stamp(9 + 10 * l);
+        ok = grid_sync(P, nsync, S.flags);
+        stamp(10 + 10 * l);
+    }
+    if (ok) {
+        // ---- LM head: residual update + final norm, BF16 GEMV, greedy argmax ----
+        const Job& jl = P.jobs[4 * P.nlayers];
+        job_prologue<kBF16, kProResidNorm>(jl, JS, pph);
+        run_units<kBF16, kEpiArgmax>(jl, st, JS, P, S.flags, best_v, best_i);
+        cta_combine<kEpiArgmax>(jl, JS, best_v, best_i);
+        stamp(kStepTraceLen - 2);
+        __syncthreads();
+        if (S.flags[0]) {
+            ok = false;
+            if (tid == 0) atomicExch(P.abort, 1);
+        } else {
+            argmax_finish(jl, JS, best_v, best_i);
+            stamp(kStepTraceLen - 1);
+        }
+    }
+    if (!ok) {
+        // Leaving early: no copy of this CTA may still be landing in shared memory.
+        if (lane == 0) stream_drain(st);
+        if (tid == 0 && S.flags[3]) (void)mbar_wait(AS.bar, aph & 1u);
+        __syncthreads();
+        return;
+    }
+    // The last CTA out returns the barrier counters to zero for the next launch.
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(&P.sync[1], 1u);
+        if (prev == gridDim.x - 1) {
+            P.sync[0] = 0u;
+            P.sync[1] = 0u;
+        }
+    }
+}
+
+template <typename F>
+bool dispatch_g(int G, F&& f) {
+    switch (G) {
+        case 1: f(step_kernel<1>); return true;
+        case 2: f(step_kernel<2>); return true;
+        case 4: f(step_kernel<4>); return true;
+        default: return false;
+    }
+}
+
+}  // namespace
+
+StepGeom step_geometry(int hidden, int kp_max, int head_dim, int group) {
+    StepGeom g;
+    g.warps = kStepWarps;
+    g.nb = kStepNb;
+    g.hidden = hidden;
+    g.kp_max = kp_max;
+    g.kp_lm = (hidden + kBF16SegCols - 1) / kBF16SegCols * kBF16SegCols;
+    g.head_dim = head_dim;
+    g.group = group;
+    // The norm prologues hold at most kMaxV8 chunks of 8 columns per thread;
+    // head_dim must fit one thread per column in the attention PV loop.
+    const bool fits_threads = hidden <= kMaxV8 * 8 * kStepWarps * 32 && head_dim <= kStepWarps * 32 && head_dim % 32 == 0;
+    const bool fits_group = group == 1 || group == 2 || group == 4;
+    g.smem = step_carve(nullptr, g, nullptr) + 128;
+    if (!fits_threads || !fits_group || g.smem > 226 * 1024) g.warps = 0;
+    return g;
+}
+
+cudaError_t step_prepare(const StepGeom& g) {
+    cudaError_t e = cudaErrorInvalidValue;
+    dispatch_g(g.group, [&](auto k) {
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(g.smem));
+    });
+    return e;
+}
+
+int step_max_grid(const StepGeom& g) {
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    dispatch_g(g.group, [&](auto k) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, g.warps * 32, g.smem) != cudaSuccess) per_sm = 0;
+    });
+    cudaGetLastError();
+    return sms * std::min(per_sm, 1);
+}
+
+cudaError_t step_launch(const StepParams& p, const StepGeom& g, int grid, cudaStream_t s) {
+    cudaError_t err = cudaErrorInvalidValue;
+    dispatch_g(g.group, [&](auto k) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(g.warps * 32);
+        cfg.dynamicSmemBytes = g.smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        err = cudaLaunchKernelEx(&cfg, k, p);
+    });
+    return err;
+}
+
+}  // namespace rt

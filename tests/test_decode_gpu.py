@@ -16,6 +16,18 @@ pytestmark = pytest.mark.gpu
 REL_L2 = 2e-3
 
 
+@pytest.fixture(params=["step", "graph"])
+def decode_path(request, monkeypatch):
+    """The engine's two decode paths: the persistent step kernel (default) and
+    one launch per projection replayed as a CUDA graph (RT_DECODER_GRAPH set
+    when the context is created)."""
+    if request.param == "graph":
+        monkeypatch.setenv("RT_DECODER_GRAPH", "1")
+    else:
+        monkeypatch.delenv("RT_DECODER_GRAPH", raising=False)
+    return request.param
+
+
 def rel_l2(a, b):
     return float(np.linalg.norm(a.astype(np.float64) - b) / (np.linalg.norm(b.astype(np.float64)) + 1e-30))
 
@@ -59,7 +71,7 @@ def _run_pair(orc, cfg, w, prompt, n_decode, cap):
     return om, dec, worst, toks_o, toks_g, pos
 
 
-def test_tiny_decode_matches_oracle(orc, tiny):
+def test_tiny_decode_matches_oracle(orc, tiny, decode_path):
     cfg, w = tiny
     # 12-token prompt > window 8 exercises the sliding window on local layers;
     # layer 5 is global.
@@ -139,7 +151,7 @@ def gemma4b_6layer():
     return cfg, synth_gemma3(cfg, seed=1234)
 
 
-def test_gemma4b_width_decode_matches_oracle(orc, gemma4b_6layer):
+def test_gemma4b_width_decode_matches_oracle(orc, gemma4b_6layer, decode_path):
     cfg, w = gemma4b_6layer
     prompt = synth_tokens(1234, 1, 6, cfg.vocab_size)
     om, dec, worst, to, tg, pos = _run_pair(orc, cfg, w, prompt, 10, 32)
