@@ -24,7 +24,7 @@ struct AttnArgs {
     int32_t nsplit;         // context splits per KV head (gridDim.x)
     float scale;            // 1 / sqrt(query_pre_attn_scalar)
     float eps;              // RMSNorm epsilon
-    float* part;            // [nkv][nsplit][G][D + 2] per-split (m, l, unnormalised out)
+    float* part;            // [nkv][nsplit][G][attn_part_stride(D)] per-split (unnormalised out, m, l)
     uint32_t* counter;      // [nkv], zero before the launch; the combining CTA resets it
     float* out;             // [nq*D]
     int* err;
@@ -32,6 +32,10 @@ struct AttnArgs {
 
 constexpr int kAttnTile = 32;     // cached positions per shared-memory tile
 constexpr int kAttnThreads = 256;
+
+// Floats per (split, query head) row of the attention partials: D outputs,
+// then m and l; padded to a multiple of 4 so every row starts 16-byte aligned.
+__host__ __device__ constexpr int attn_part_stride(int D) { return D + 4; }
 
 size_t attention_smem_bytes(int D, int G);
 // Set kernel attributes; call once per device before the first launch / capture.

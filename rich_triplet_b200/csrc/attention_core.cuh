@@ -195,6 +195,93 @@ __device__ __forceinline__ void attn_issue(const AttnArgs& a, const AttnRange& R
     bulk_g2s_nohint(S.vt, a.vcache + (R.head_base + r0) * a.D, bytes, S.bar);
 }
 
+// exp(mx - m) for the rescaling of a partial state whose running max is mx
+// (an empty state, mx = -inf, weighs 0).
+__device__ __forceinline__ float lse_scale(float mx, float m) { return mx == -INFINITY ? 0.f : expf(mx - m); }
+
+// Merge of the nsplit partial states of KV head h (the CTA that finished last;
+// all threads).  Per query head: M = max m_q, w_q = exp(m_q - M),
+// out = sum w_q acc_q / sum w_q l_q.  Thread (c, k), k = tid % kg, takes
+// float4 column c of the G*D outputs and splits k, k + kg, ... (kBatch loads
+// in flight, running max rescaled per batch); the kg states of a column sit
+// in adjacent lanes and are combined by a butterfly, so every load of the
+// merge is issued in one round for nsplit <= kg * kBatch.
+template <int G>
+__device__ __forceinline__ void attn_merge(const AttnArgs& a, int h, int nsplit) {
+    constexpr int kBatch = 12;
+    const int D = a.D, stride = attn_part_stride(D);
+    const int Q = G * D / 4;  // float4 columns
+    int kg = 1;
+    while (kg < 32 && 2 * kg * Q <= static_cast<int>(blockDim.x)) kg *= 2;
+    const int tid = threadIdx.x, per_pass = static_cast<int>(blockDim.x) / kg;
+    const int k = tid % kg;
+    for (int c0 = 0; c0 < Q; c0 += per_pass) {
+        const int c = c0 + tid / kg;
+        const bool col = c < Q;
+        const int g = col ? 4 * c / D : 0, d = col ? 4 * c - g * D : 0;
+        const float* base = a.part + (static_cast<size_t>(h) * a.nsplit * G + g) * stride;
+        float M = -INFINITY, den = 0.f;
+        float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q0 = k; col && q0 < nsplit; q0 += kg * kBatch) {
+            float2 ml[kBatch];
+            float4 v[kBatch];
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) {
+                const int q = q0 + i * kg;
+                if (q < nsplit) {
+                    const float* row = base + static_cast<size_t>(q) * G * stride;
+                    ml[i] = __ldcg(reinterpret_cast<const float2*>(row + D));
+                    v[i] = __ldcg(reinterpret_cast<const float4*>(row + d));
+                } else {
+                    ml[i] = make_float2(-INFINITY, 0.f);
+                    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            float bm = M;
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) bm = fmaxf(bm, ml[i].x);
+            const float cr = lse_scale(M, bm);
+            den *= cr;
+            num.x *= cr;
+            num.y *= cr;
+            num.z *= cr;
+            num.w *= cr;
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i) {
+                const float w = lse_scale(ml[i].x, bm);
+                den += w * ml[i].y;
+                num.x += w * v[i].x;
+                num.y += w * v[i].y;
+                num.z += w * v[i].z;
+                num.w += w * v[i].w;
+            }
+            M = bm;
+        }
+        // Butterfly over the kg lanes of column c (aligned groups of a warp).
+        for (int o = 1; o < kg; o <<= 1) {
+            const float oM = __shfl_xor_sync(0xffffffffu, M, o);
+            const float oden = __shfl_xor_sync(0xffffffffu, den, o);
+            float4 on;
+            on.x = __shfl_xor_sync(0xffffffffu, num.x, o);
+            on.y = __shfl_xor_sync(0xffffffffu, num.y, o);
+            on.z = __shfl_xor_sync(0xffffffffu, num.z, o);
+            on.w = __shfl_xor_sync(0xffffffffu, num.w, o);
+            const float nm = fmaxf(M, oM);
+            const float sa = lse_scale(M, nm), sb = lse_scale(oM, nm);
+            den = den * sa + oden * sb;
+            num.x = num.x * sa + on.x * sb;
+            num.y = num.y * sa + on.y * sb;
+            num.z = num.z * sa + on.z * sb;
+            num.w = num.w * sa + on.w * sb;
+            M = nm;
+        }
+        if (col && k == 0) {
+            float* out = a.out + static_cast<size_t>(h * G + g) * D + d;
+            *reinterpret_cast<float4*>(out) = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
+        }
+    }
+}
+
 // Thread 0: initialise the tile barrier.  An initialised mbarrier owns its 8
 // bytes until it is invalidated: ordinary stores to them are undefined (on
 // B200 they do not stick), so the barrier must not live in memory that other
@@ -278,7 +365,7 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
     if (R.has_new) attend_tile<G, T>(S, S.knew, S.vnew, 1, D, a.scale, acc);
 
     // Per-split partial state.
-    const int stride = D + 2;
+    const int stride = attn_part_stride(D);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         float* pp = a.part + (static_cast<size_t>(h * a.nsplit + s) * G + g) * stride;
@@ -297,43 +384,7 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
     __syncthreads();
     if (!S.flag[0]) return true;
     __threadfence();
-    // Merge the splits of head h (this CTA finished last).  Per query head:
-    // M = max m_q, w_q = exp(m_q - M), out = sum w_q acc_q / sum w_q l_q, the
-    // sums in split order.  The (m, l) pairs are staged in shared memory (the
-    // score buffer, G * T floats >= 2 * nsplit * G is not guaranteed, so the K
-    // tile buffer is used), and every thread keeps eight loads in flight.
-    float* ml = S.kt;  // [G][nsplit][2]
-    for (int i = tid; i < G * R.nsplit; i += blockDim.x) {
-        const int g = i / R.nsplit, q = i - g * R.nsplit;
-        const float* pp = a.part + (static_cast<size_t>(h * a.nsplit + q) * G + g) * stride;
-        ml[2 * i] = __ldcg(pp + D);
-        ml[2 * i + 1] = __ldcg(pp + D + 1);
-    }
-    __syncthreads();
-    for (int i = tid; i < G * D; i += blockDim.x) {
-        const int g = i / D, d = i - g * D;
-        const float* mlg = ml + 2 * g * R.nsplit;
-        float M = -INFINITY;
-        for (int q = 0; q < R.nsplit; ++q) M = fmaxf(M, mlg[2 * q]);
-        float num = 0.f, den = 0.f;
-        for (int q0 = 0; q0 < R.nsplit; q0 += 8) {
-            float v[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-                v[k] = q0 + k < R.nsplit
-                           ? __ldcg(a.part + (static_cast<size_t>(h * a.nsplit + q0 + k) * G + g) * stride + d)
-                           : 0.f;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                if (q0 + k < R.nsplit) {
-                    const float w = expf(mlg[2 * (q0 + k)] - M);
-                    den += w * mlg[2 * (q0 + k) + 1];
-                    num += w * v[k];
-                }
-            }
-        }
-        a.out[static_cast<size_t>(h * G + g) * D + d] = num / den;
-    }
+    attn_merge<G>(a, h, R.nsplit);
     if (tid == 0) a.counter[h] = 0u;
     return true;
 }

@@ -665,7 +665,7 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
     {
         const size_t G_ = static_cast<size_t>(G);
         const size_t n_act = 2 * static_cast<size_t>(H) + d->qkv_rows + static_cast<size_t>(d->NQ) * D + H + d->F + H +
-                             d->V + static_cast<size_t>(d->NKV) * d->nsplit * G_ * (D + 2) + d->p_lm.grid + 10 * 64;
+                             d->V + static_cast<size_t>(d->NKV) * d->nsplit * G_ * rt::attn_part_stride(D) + d->p_lm.grid + 10 * 64;
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->act), n_act * 4 + 1024, "activations")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->act, 0, n_act * 4 + 1024, s);
         // Every slice starts on a 256-byte boundary (the kernels move these
@@ -684,7 +684,7 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
         d->hbuf = slice(d->F);
         d->down = slice(H);
         d->logits = slice(d->V);
-        d->attn_part = slice(static_cast<size_t>(d->NKV) * d->nsplit * G_ * (D + 2));
+        d->attn_part = slice(static_cast<size_t>(d->NKV) * d->nsplit * G_ * rt::attn_part_stride(D));
         d->am_val = slice(d->p_lm.grid);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->am_idx), sizeof(int32_t) * d->p_lm.grid, "argmax idx")) != RT_OK) return bail(rc);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->counters), sizeof(uint32_t) * (d->NKV + 1), "counters")) != RT_OK) return bail(rc);

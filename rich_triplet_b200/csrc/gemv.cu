@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     }
     __syncthreads();
     const Job& job = *S.job;
-    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx, nullptr};
+    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx, nullptr, nullptr};
 
     // Each warp's weight stream starts before the wait on the previous kernel
     // (weights are constants), and so do the norm weights.

@@ -34,7 +34,8 @@
 // columns 2(j&3), 2(j&3)+1 (and plane 2 in column 2(j&3) of a second MMA), zero
 // elsewhere, so lane t of every lane quad ends up holding the three plane sums
 // of sub-blocks t and t+4 for two rows, and all 32 lanes share the scale
-// epilogue.
+// epilogue.  (Two planes would halve the MMAs but leave errors near 3e-5 of
+// rms(y): the dot product of K terms accumulates the 16-bit rounding of x.)
 //
 // BF16 (MatBf16::dot_row, src/autograd2.rs:861-888).  The weights, loaded by
 // ldmatrix, are the A operand of mma.m16n8k16.bf16; x is split exactly into
@@ -115,17 +116,17 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Round to the nearest integer (ties to even) without the XU pipe:
-// adding 1.5 * 2^23 leaves the integer in the low mantissa bits (|y| < 2^22).
-__device__ __forceinline__ int round_magic(float y, float* yr) {
-    const float m = __fadd_rn(y, 12582912.0f);
-    *yr = __fsub_rn(m, 12582912.0f);
-    return __float_as_int(m) - 0x4B400000;
+// round(y) clamped to [-127, 127], as a float; *bits gets the integer in its
+// low byte (two's complement), from the same magic-number sum.
+__device__ __forceinline__ float round_clamp127(float y, uint32_t* bits) {
+    const float f = fminf(fmaxf(__fsub_rn(__fadd_rn(y, 12582912.0f), 12582912.0f), -127.0f), 127.0f);
+    *bits = __float_as_uint(__fadd_rn(f, 12582912.0f));
+    return f;
 }
 
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-    return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
-           ((static_cast<uint32_t>(c) & 0xFFu) << 16) | (static_cast<uint32_t>(d) << 24);
+// Bytes 0 of a, b, c, d -> one word (a lowest).
+__device__ __forceinline__ uint32_t pack4_low(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 // f32 -> bf16 bits, round to nearest even (finite inputs).
@@ -157,22 +158,22 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     // x = s (p0 + p1/254 + p2/254^2): each residual spans the full int8 range,
-    // |error| <= s / (2 * 254^2).  The clamps only guard the rounding edge.
-    const float s = m / 127.0f;
-    const float inv = m > 0.f ? 127.0f / m : 0.f;
+    // |error| <= s / (2 * 254^2).  Each residual is taken against the stored
+    // scale s, so the reciprocal only has to be close (|x inv| stays below
+    // 127.5); the clamps only guard the rounding edge.  Sub-blocks whose
+    // largest magnitude is below 1e-30 quantise to zero.
+    const float s = m * (1.0f / 127.0f);
+    const float inv = m > 1e-30f ? __fdividef(127.0f, m) : 0.f;
     const float s254 = s * (1.0f / 254.0f);
     const float inv254 = inv * 254.0f, inv254sq = inv * 64516.0f;
-    int q0[8], q1[8], q2[8];
+    uint32_t b0[8], b1[8], b2[8];  // low byte: the plane value (two's complement)
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-        float f0, f1, f2;
-        q0[e] = min(127, max(-127, round_magic(xv[e] * inv, &f0)));
-        f0 = static_cast<float>(q0[e]);
+        const float f0 = round_clamp127(xv[e] * inv, &b0[e]);
         const float r1 = fmaf(-f0, s, xv[e]);
-        q1[e] = min(127, max(-127, round_magic(r1 * inv254, &f1)));
-        f1 = static_cast<float>(q1[e]);
+        const float f1 = round_clamp127(r1 * inv254, &b1[e]);
         const float r2 = fmaf(-f1, s254, r1);
-        q2[e] = min(127, max(-127, round_magic(r2 * inv254sq, &f2)));
+        (void)round_clamp127(r2 * inv254sq, &b2[e]);
     }
     const int j = lane >> 2;  // sub-block of this lane's elements
     const int r = j & 3, half = j >> 2;
@@ -183,13 +184,14 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
     uint8_t* P0 = planes;
     uint8_t* P1 = planes + pstride;
     uint8_t* P2 = planes + 2 * pstride;
-    *reinterpret_cast<uint32_t*>(P0 + o0) = pack4(q0[0], q0[1], q0[2], q0[3]);
-    *reinterpret_cast<uint32_t*>(P0 + o1) = pack4(q0[4], q0[5], q0[6], q0[7]);
-    *reinterpret_cast<uint32_t*>(P1 + o0) = pack4(q1[0], q1[1], q1[2], q1[3]);
-    *reinterpret_cast<uint32_t*>(P1 + o1) = pack4(q1[4], q1[5], q1[6], q1[7]);
-    *reinterpret_cast<uint32_t*>(P2 + o0) = pack4(q2[0], q2[1], q2[2], q2[3]);
-    *reinterpret_cast<uint32_t*>(P2 + o1) = pack4(q2[4], q2[5], q2[6], q2[7]);
+    *reinterpret_cast<uint32_t*>(P0 + o0) = pack4_low(b0[0], b0[1], b0[2], b0[3]);
+    *reinterpret_cast<uint32_t*>(P0 + o1) = pack4_low(b0[4], b0[5], b0[6], b0[7]);
+    *reinterpret_cast<uint32_t*>(P1 + o0) = pack4_low(b1[0], b1[1], b1[2], b1[3]);
+    *reinterpret_cast<uint32_t*>(P1 + o1) = pack4_low(b1[4], b1[5], b1[6], b1[7]);
+    *reinterpret_cast<uint32_t*>(P2 + o0) = pack4_low(b2[0], b2[1], b2[2], b2[3]);
+    *reinterpret_cast<uint32_t*>(P2 + o1) = pack4_low(b2[4], b2[5], b2[6], b2[7]);
     if ((lane & 3) == 0) {
+        // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
         // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
         const float unit = s * (1.0f / 64516.0f) * ((j & 1) ? 0.0625f : 1.0f);
         xsx[seg * 8 + j] = make_float2(unit, sum);
@@ -437,6 +439,7 @@ struct JobSmem {
     uint8_t* planes;
     float2* xsx;
     float* wpart;    // [warps][2][16] per-warp pieces of tiles shared within the CTA (cta_combine)
+    uint2* wse;      // [warps] each warp's units [s, e) of the current tile-split job
 };
 
 // Thread 0: fetch the norm weights of `j` (prologue `pro`) into gpost / gpre,
@@ -608,6 +611,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     const Share sh = warp_share(a, st.cta, st.ncta, st.warp, st.nw);
     const uint32_t u_begin = sh.s;
     const int n = static_cast<int>(sh.e - sh.s);
+    if (a.tile_split && lane == 0) S.wse[st.warp] = make_uint2(sh.s, sh.e);
 
     // Row epilogue: lane L < 16 holds the sum of row r0 + L.
     auto emit_rows = [&](int64_t r0, float v) {
@@ -806,7 +810,8 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
 // After every warp of the CTA ran job_units_run on a job with tile_split set:
 // add, in warp order, the pieces of the tiles this CTA's warps shared (one
 // warp per tile, from shared memory) and run the epilogue on them.  All
-// threads call it; it starts with __syncthreads.
+// threads call it; it starts with __syncthreads.  The warps' unit ranges come
+// from the table job_units_run filled (no division per piece).
 template <int EPI>
 __device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, float& best_v, long long& best_i) {
     __syncthreads();
@@ -817,26 +822,26 @@ __device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, floa
     Split ct;
     ct.init(ntiles, gridDim.x);
     const uint32_t tb = ct.start(blockIdx.x), te = ct.start(blockIdx.x + 1);
-    if (tb >= te) return;
-    Split wt;  // the warps' split of this CTA's units, numbered from the CTA's first unit
-    wt.init((te - tb) * nseg, nw);
     // lane -> row (or the first row of a GELU pair)
     constexpr int kPer = EPI == kEpiGeluPair ? kTile / 2 : kTile;
     const int row = EPI == kEpiGeluPair ? 2 * lane : lane;
     for (uint32_t T = tb + warp; T < te; T += nw) {
-        const uint32_t u0 = (T - tb) * nseg;
-        const uint32_t wa = wt.owner(u0), wb = wt.owner(u0 + nseg - 1);
-        if (wa == wb) continue;  // one warp had it all: already through the epilogue
-        if (lane >= kPer) continue;
+        const uint32_t u0 = T * nseg, u1 = u0 + nseg;
         float v0 = 0.f, v1 = 0.f;
-        for (uint32_t w = wa; w <= wb; ++w) {
-            const uint32_t s_w = wt.start(w);
-            if (wt.start(w + 1) <= s_w) continue;
+        int pieces = 0;
+        for (uint32_t w = 0; w < nw; ++w) {
+            const uint2 se = S.wse[w];
+            if (se.x >= se.y || se.x >= u1 || se.y <= u0) continue;
+            ++pieces;
             // a warp that began in an earlier tile keeps this one in slot 1
-            const float* pw = S.wpart + (w * 2 + (s_w < u0 ? 1 : 0)) * kTile;
-            v0 += pw[row];
-            if constexpr (EPI == kEpiGeluPair) v1 += pw[row + 1];
+            const float* pw = S.wpart + (w * 2 + (se.x < u0 ? 1 : 0)) * kTile;
+            if (lane < kPer) {
+                v0 += pw[row];
+                if constexpr (EPI == kEpiGeluPair) v1 += pw[row + 1];
+            }
         }
+        if (pieces < 2) continue;  // one warp had it all: already through the epilogue
+        if (lane >= kPer) continue;
         const int64_t r = static_cast<int64_t>(T) * kTile + row;
         if (r >= a.rows) continue;
         if constexpr (EPI == kEpiGeluPair) {

@@ -63,6 +63,7 @@ struct StepSmem {
     float* gpost;    // [hidden]
     float* gpre;     // [hidden]
     float* wpart;    // [warps][2][16]
+    uint2* wse;      // [warps]
     uint8_t* uni;    // planes + xsx of a projection, or an attention item
     float2* xsx;
     uint8_t* ring;   // [warps][nb][kSlotBytes]
@@ -86,6 +87,7 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
     uint8_t* gpost = take(sizeof(float) * g.hidden, 16);
     uint8_t* gpre = take(sizeof(float) * g.hidden, 16);
     uint8_t* wpart = take(sizeof(float) * g.warps * 2 * 16, 16);
+    uint8_t* wse = take(sizeof(uint2) * g.warps, 16);
     const size_t q4 = (planes_bytes(kQ4K, g.kp_max) + 127) / 128 * 128;
     const size_t q4all = q4 + xsx_bytes(kQ4K, g.kp_max), bf = planes_bytes(kBF16, g.kp_lm);
     const size_t proj = q4all > bf ? q4all : bf;
@@ -103,6 +105,7 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
         S->gpost = reinterpret_cast<float*>(gpost);
         S->gpre = reinterpret_cast<float*>(gpre);
         S->wpart = reinterpret_cast<float*>(wpart);
+        S->wse = reinterpret_cast<uint2*>(wse);
         S->uni = uni;
         S->xsx = reinterpret_cast<float2*>(uni + q4);
         S->ring = ring;
@@ -174,7 +177,7 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         S.flags[0] = S.flags[1] = S.flags[2] = S.flags[3] = 0;
     }
     __syncthreads();
-    const JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.uni, S.xsx, S.wpart};
+    const JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse};
     const int njobs = 4 * P.nlayers + 1;
     Stream st;
     stream_start(st, S.full + warp * nb, S.ring + static_cast<size_t>(warp) * nb * kSlotBytes, nb, kSlotBytes, P.jobs,
@@ -193,21 +196,40 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
     };
     stamp(0);
     bool ok = true;
-    for (int l = 0; l < P.nlayers && ok; ++l) {
-        const Job& jq = P.jobs[4 * l];
-        const Job& jo = P.jobs[4 * l + 1];
-        const Job& jg = P.jobs[4 * l + 2];
-        const Job& jd = P.jobs[4 * l + 3];
-        const AttnArgs& at = P.attn[l];
-        // ---- QKV (residual update + attention RMSNorm in the prologue) ----
-        if (l == 0) job_prologue<kQ4K, kProEmbedNorm>(jq, JS, pph);
-        else job_prologue<kQ4K, kProResidNorm>(jq, JS, pph);
-        pph ^= 1u;
-        if (tid == 0) prefetch_gammas(jg, kProResidNorm, JS);
-        run_units<kQ4K, kEpiPlain>(jq, st, JS, P, S.flags, best_v, best_i);
-        cta_combine<kEpiPlain>(jq, JS, best_v, best_i);
-        stamp(1 + 10 * l);
+    // One pass per projection: per layer QKV (then attention), O, gate/up,
+    // down.  A runtime loop over the phases, not an unrolled layer body, so
+    // each variant of a stage is compiled once: the per-layer code path then
+    // stays small enough to keep hot in the instruction cache.
+#pragma unroll 1
+    for (int p = 0; p < 4 * P.nlayers && ok; ++p) {
+        const int l = p >> 2, k = p & 3;  // k: 0 QKV, 1 O, 2 gate/up, 3 down
+        const Job& j = P.jobs[p];
+        if (k == 1 || k == 3) {
+            job_prologue<kQ4K, kProPlain>(j, JS, 0u);
+        } else {
+            // residual update + attention / FFN RMSNorm (the embedding row at p = 0)
+            if (p == 0) job_prologue<kQ4K, kProEmbedNorm>(j, JS, pph);
+            else job_prologue<kQ4K, kProResidNorm>(j, JS, pph);
+            pph ^= 1u;
+            // the next norm prologue's weights: gate/up's, the next layer's QKV or the LM head's
+            if (tid == 0) prefetch_gammas(P.jobs[p + 2], kProResidNorm, JS);
+        }
+        if (k == 2) {
+            run_units<kQ4K, kEpiGeluPair>(j, st, JS, P, S.flags, best_v, best_i);
+            cta_combine<kEpiGeluPair>(j, JS, best_v, best_i);
+        } else {
+            run_units<kQ4K, kEpiPlain>(j, st, JS, P, S.flags, best_v, best_i);
+            cta_combine<kEpiPlain>(j, JS, best_v, best_i);
+        }
+        const int slot = 1 + 10 * l + (k == 0 ? 0 : 2 + 2 * k);
+        stamp(slot);
+        if (k != 0) {
+            ok = grid_sync(P, nsync, S.flags);
+            stamp(slot + 1);
+            continue;
+        }
         // ---- attention: its first cached K/V tile is copied during the barrier ----
+        const AttnArgs& at = P.attn[l];
         const int items = at.nkv * at.nsplit;
         const int h = blockIdx.x / at.nsplit, s = blockIdx.x % at.nsplit;
         const bool has_item = static_cast<int>(blockIdx.x) < items;
@@ -221,7 +243,7 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
             }
         }
         ok = grid_sync(P, nsync, S.flags);
-        stamp(2 + 10 * l);
+        stamp(slot + 1);
         if (ok && has_item) {
             if (!acore::attn_run<G, kAttnT>(at, h, s, R, AS, aph & 1u)) {
                 if (tid == 0) atomicExch(&S.flags[0], 1);
@@ -229,33 +251,9 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
             if (tid == 0) S.flags[3] = 0;
             if (R.active) aph += static_cast<uint32_t>(R.ntiles);
         }
-        stamp(3 + 10 * l);
+        stamp(slot + 2);
         if (ok) ok = grid_sync(P, nsync, S.flags);
-        stamp(4 + 10 * l);
-        if (!ok) break;
-        // ---- O ----
-        job_prologue<kQ4K, kProPlain>(jo, JS, 0u);
-        run_units<kQ4K, kEpiPlain>(jo, st, JS, P, S.flags, best_v, best_i);
-        cta_combine<kEpiPlain>(jo, JS, best_v, best_i);
-        stamp(5 + 10 * l);
-        if (!(ok = grid_sync(P, nsync, S.flags))) break;
-        stamp(6 + 10 * l);
-        // ---- gate / up (residual update + FFN RMSNorm), GELU gate ----
-        job_prologue<kQ4K, kProResidNorm>(jg, JS, pph);
-        pph ^= 1u;
-        if (tid == 0) prefetch_gammas(P.jobs[l + 1 < P.nlayers ? 4 * (l + 1) : 4 * P.nlayers], kProResidNorm, JS);
-        run_units<kQ4K, kEpiGeluPair>(jg, st, JS, P, S.flags, best_v, best_i);
-        cta_combine<kEpiGeluPair>(jg, JS, best_v, best_i);
-        stamp(7 + 10 * l);
-        if (!(ok = grid_sync(P, nsync, S.flags))) break;
-        stamp(8 + 10 * l);
-        // ---- down ----
-        job_prologue<kQ4K, kProPlain>(jd, JS, 0u);
-        run_units<kQ4K, kEpiPlain>(jd, st, JS, P, S.flags, best_v, best_i);
-        cta_combine<kEpiPlain>(jd, JS, best_v, best_i);
-        stamp(9 + 10 * l);
-        ok = grid_sync(P, nsync, S.flags);
-        stamp(10 + 10 * l);
+        stamp(slot + 3);
     }
     if (ok) {
         // ---- LM head: residual update + final norm, BF16 GEMV, greedy argmax ----
