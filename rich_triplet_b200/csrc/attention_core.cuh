@@ -28,6 +28,8 @@
 namespace rt {
 namespace acore {
 
+constexpr int kMaxHeadDim = 256;  // the decoder accepts head_dim <= 256, a multiple of 32
+
 struct AttnSmem {
     uint64_t* bar;
     float* red;    // [32]
@@ -81,25 +83,36 @@ __host__ __device__ inline size_t attn_carve(uint8_t* base, int D, int G, int T,
     return off;
 }
 
-// In-place per-head RMSNorm (1 + gamma) of `v[D]` in shared memory.
-__device__ __forceinline__ void head_norm(float* v, const float* gamma, int D, float eps, float* red) {
+// One warp: dst[D] = rope(rmsnorm(raw) * (1 + gamma)) -- the per-head norm
+// (rms_norm_gemma3 per head, src/transformer4.rs:2485-2510) and the NeoX
+// rotation of pairs (j, j + D/2) (src/transformer4.rs:2742-2772).
+__device__ __forceinline__ void head_prep_warp(const float* raw, const float* gamma, const float* cs, const float* sn,
+                                               int D, float eps, float* dst) {
+    constexpr int kMaxPer = kMaxHeadDim / 32;
+    const int lane = threadIdx.x & 31, half = D / 2;
+    float x[kMaxPer];
     float ss = 0.f;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) ss += v[d] * v[d];
-    ss = block_sum(ss, red);
-    const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(D)) + eps);
-    for (int d = threadIdx.x; d < D; d += blockDim.x) v[d] = __fmul_rn(__fmul_rn(v[d], r), __fadd_rn(1.0f, gamma[d]));
-    __syncthreads();
-}
-
-// In-place NeoX rotation of `v[D]`: (x0, x1) = (v[j], v[j + D/2]).
-__device__ __forceinline__ void head_rope(float* v, const float* cs, const float* sn, int D) {
-    const int half = D / 2;
-    for (int j = threadIdx.x; j < half; j += blockDim.x) {
-        const float x0 = v[j], x1 = v[j + half], c = cs[j], s = sn[j];
-        v[j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        v[j + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {  // every load of the row in flight at once
+        const int j = lane + 32 * i;
+        x[i] = j < D ? raw[j] : 0.f;
     }
-    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+        const int j = lane + 32 * i;
+        if (j < D) dst[j] = x[i];
+        ss += x[i] * x[i];
+    }
+    ss = warp_sum(ss);
+    __syncwarp();  // the row is in dst for the pairs other lanes own
+    const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(D)) + eps);
+    for (int j = lane; j < half; j += 32) {
+        const float x0 = __fmul_rn(__fmul_rn(dst[j], r), __fadd_rn(1.0f, gamma[j]));
+        const float x1 = __fmul_rn(__fmul_rn(dst[j + half], r), __fadd_rn(1.0f, gamma[j + half]));
+        const float c = cs[j], s = sn[j];
+        dst[j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        dst[j + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    }
 }
 
 template <int G, int T>
@@ -308,31 +321,26 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
     if (!R.active) return true;
     const int D = a.D;
     const int tid = threadIdx.x;
-    // Query heads h*G .. h*G+G-1 (kvh = qh / group, src/transformer4.rs:2819).
-    const float* qraw = a.qkv + static_cast<size_t>(h) * G * D;
-    for (int i = tid; i < G * D; i += blockDim.x) S.qv[i] = qraw[i];
+    // Query heads h*G .. h*G+G-1 (kvh = qh / group, src/transformer4.rs:2819):
+    // warp g < G prepares query head g, warp G the new K row, warp G + 1
+    // copies the new V row.
+    const float* cs = a.rope_cos + static_cast<size_t>(R.pos) * (D / 2);
+    const float* sn = a.rope_sin + static_cast<size_t>(R.pos) * (D / 2);
+    const int warp = tid >> 5;
+    if (warp < G) {
+        head_prep_warp(a.qkv + static_cast<size_t>(h * G + warp) * D, a.q_norm, cs, sn, D, a.eps, S.qv + warp * D);
+    } else if (warp == G && R.has_new) {
+        head_prep_warp(a.qkv + static_cast<size_t>(a.nq + h) * D, a.k_norm, cs, sn, D, a.eps, S.knew);
+    } else if (warp == G + 1 && R.has_new) {
+        const float* vraw = a.qkv + static_cast<size_t>(a.nq + a.nkv + h) * D;
+        for (int d = tid & 31; d < D; d += 32) S.vnew[d] = vraw[d];
+    }
     if (tid < G) {
         S.m_run[tid] = -INFINITY;
         S.l_run[tid] = 0.f;
     }
     __syncthreads();
-    const float* cs = a.rope_cos + static_cast<size_t>(R.pos) * (D / 2);
-    const float* sn = a.rope_sin + static_cast<size_t>(R.pos) * (D / 2);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        head_norm(S.qv + g * D, a.q_norm, D, a.eps, S.red);
-        head_rope(S.qv + g * D, cs, sn, D);
-    }
     if (R.has_new) {
-        const float* kraw = a.qkv + static_cast<size_t>(a.nq) * D + static_cast<size_t>(h) * D;
-        const float* vraw = a.qkv + static_cast<size_t>(a.nq + a.nkv) * D + static_cast<size_t>(h) * D;
-        for (int d = tid; d < D; d += blockDim.x) {
-            S.knew[d] = kraw[d];
-            S.vnew[d] = vraw[d];
-        }
-        __syncthreads();
-        head_norm(S.knew, a.k_norm, D, a.eps, S.red);
-        head_rope(S.knew, cs, sn, D);
         float* kdst = a.kcache + (R.head_base + R.pos) * D;
         float* vdst = a.vcache + (R.head_base + R.pos) * D;
         for (int d = tid; d < D; d += blockDim.x) {
@@ -341,28 +349,33 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
         }
     }
 
+    // Cached tiles (copied into S.kt / S.vt), then the new row as a last tile.
     float acc[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g] = 0.f;
-    for (int t = 0; t < R.ntiles; ++t) {
-        const bool ok = mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) {
-                if (a.err) atomicExch(a.err, kErrMbarTimeout);
-                // the one outstanding copy must land (bounded) before shared memory is reused
-                (void)mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
+    const int nsteps = R.ntiles + (R.has_new ? 1 : 0);
+#pragma unroll 1
+    for (int t = 0; t < nsteps; ++t) {
+        const bool cached = t < R.ntiles;
+        if (cached) {
+            const bool ok = mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
+            if (__syncthreads_or(!ok)) {
+                if (tid == 0) {
+                    if (a.err) atomicExch(a.err, kErrMbarTimeout);
+                    // the one outstanding copy must land (bounded) before shared memory is reused
+                    (void)mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
+                }
+                __syncthreads();
+                return false;
             }
-            __syncthreads();
-            return false;
         }
-        const int nt = min(T, R.ncached - t * T);
-        attend_tile<G, T>(S, S.kt, S.vt, nt, D, a.scale, acc);
+        attend_tile<G, T>(S, cached ? S.kt : S.knew, cached ? S.vt : S.vnew, cached ? min(T, R.ncached - t * T) : 1, D,
+                          a.scale, acc);
         if (tid == 0 && t + 1 < R.ntiles) {
             fence_proxy_async_smem();
             attn_issue(a, R, S, t + 1, T);
         }
     }
-    if (R.has_new) attend_tile<G, T>(S, S.knew, S.vnew, 1, D, a.scale, acc);
 
     // Per-split partial state.
     const int stride = attn_part_stride(D);

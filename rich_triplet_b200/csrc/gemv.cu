@@ -29,6 +29,8 @@ struct Smem {
     Job* job;
     float* gpost;    // [K] post-norm weight (residual-norm prologue)
     float* gpre;     // [K] pre-norm weight (norm prologues)
+    float* xs;       // [K] residual stream (norm prologues)
+    float* sub;      // [K] sub-layer output (residual-update prologue)
     uint8_t* planes;
     float2* xsx;
     uint8_t* ring;   // [warps][nb][unit_bytes]
@@ -52,6 +54,8 @@ __host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg
     uint8_t* job = take(sizeof(Job), 16);
     uint8_t* gpost = take(pro == kProResidNorm ? sizeof(float) * K : 0, 16);
     uint8_t* gpre = take(pro != kProPlain ? sizeof(float) * K : 0, 16);
+    uint8_t* xs = take(pro == kProPlain ? 0 : sizeof(float) * K, 16);
+    uint8_t* sub = take(pro == kProResidNorm ? sizeof(float) * K : 0, 16);
     uint8_t* planes = take(planes_bytes(kind, Kp), 128);
     uint8_t* xsx = take(xsx_bytes(kind, Kp), 16);
     uint8_t* ring = take(static_cast<size_t>(warps) * nb * unit_bytes(kind), 128);
@@ -65,6 +69,8 @@ __host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg
         S->job = reinterpret_cast<Job*>(job);
         S->gpost = reinterpret_cast<float*>(gpost);
         S->gpre = reinterpret_cast<float*>(gpre);
+        S->xs = reinterpret_cast<float*>(xs);
+        S->sub = reinterpret_cast<float*>(sub);
         S->planes = planes;
         S->xsx = reinterpret_cast<float2*>(xsx);
         S->ring = ring;
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     }
     __syncthreads();
     const Job& job = *S.job;
-    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx, nullptr, nullptr};
+    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx, nullptr, nullptr, S.xs, S.sub};
 
     // Each warp's weight stream starts before the wait on the previous kernel
     // (weights are constants), and so do the norm weights.
@@ -129,7 +135,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     job_prologue<KIND, PRO>(job, JS, 0u);
     float best_v = -INFINITY;
     long long best_i = -1;
-    const bool ok = job_units_run<KIND, EPI>(job, st, JS, SplitScratch{a.part, a.tile_cnt}, best_v, best_i);
+    const bool ok = job_units_run<KIND, EPI, kSplitGrid>(job, st, JS, SplitScratch{a.part, a.tile_cnt}, best_v, best_i);
     if (!ok) {
         // A bounded wait gave up: record it, then wait (bounded) for the copies
         // this warp still has in flight before its shared memory goes away.
@@ -201,11 +207,6 @@ GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int ep
     p.unit_bytes = kind == kQ4K ? kQ4KUnit : kBF16Unit;
     p.box_x = kind == kQ4K ? kQ4KPitch / 8 : kBF16Pitch / 8;
     p.warps = cps == 2 ? kMaxWarps / 2 : kMaxWarps;
-    const int nthr = p.warps * 32;
-    if (prologue != kProPlain && nseg * seg_cols > kMaxV8 * 8 * nthr) {
-        p.warps = 0;  // the norm prologues hold at most kMaxV8 chunks of 8 per thread
-        return p;
-    }
     // Ring depth: about 32 TMA copies in flight per SM stream fastest (more
     // outstanding copies slow the stream down), within the CTA's share of
     // shared memory.

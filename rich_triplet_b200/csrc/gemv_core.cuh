@@ -56,7 +56,6 @@ namespace gcore {
 
 constexpr int kTile = 16;
 constexpr int kMaxWarps = 16;
-constexpr int kMaxV8 = 4;  // 8-element chunks of x per thread held by the norm prologues
 constexpr int kQ4KSegCols = 256;
 constexpr int kBF16SegCols = 128;
 constexpr int kQ4KPitch = 144;   // one Q4_K block per row of a unit
@@ -440,6 +439,9 @@ struct JobSmem {
     float2* xsx;
     float* wpart;    // [warps][2][16] per-warp pieces of tiles shared within the CTA (cta_combine)
     uint2* wse;      // [warps] each warp's units [s, e) of the current tile-split job
+    float* xs;       // [K] residual stream of a norm prologue (null if none)
+    float* sub;      // [K] sub-layer output of the residual-update prologue; may share memory with
+                     // `planes` (dead before the planes are written)
 };
 
 // Thread 0: fetch the norm weights of `j` (prologue `pro`) into gpost / gpre,
@@ -452,152 +454,154 @@ __device__ __forceinline__ void prefetch_gammas(const Job& j, int pro, const Job
     bulk_g2s_nohint(S.gpre, j.g_pre, kb, S.pbar);
 }
 
+// Eight consecutive floats of x at column c0 (zeros at and past K; K is a
+// multiple of 8).
+__device__ __forceinline__ void load8(const float* x, int c0, int K, float4& lo, float4& hi) {
+    if (c0 + 8 <= K) {
+        lo = *reinterpret_cast<const float4*>(x + c0);
+        hi = *reinterpret_cast<const float4*>(x + c0 + 4);
+    } else {
+        lo = hi = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// Planes of one 8-column chunk (BF16: chunk q) or of one warp's 256-column
+// segment (Q4_K: lane l holds its columns 8l..8l+7).
+template <int KIND>
+__device__ __forceinline__ void chunk_planes(const float4& lo, const float4& hi, int idx, int lane, int pstride,
+                                             const JobSmem& S) {
+    const float xv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    if constexpr (KIND == kQ4K) q4k_segment_planes(xv, idx, lane, pstride, S.planes, S.xsx);
+    else bf16_chunk_planes(xv, idx, pstride, S.planes);
+}
+
+// Planes of x read from global memory.  Q4_K: warp w takes segments w, w + nw,
+// ...; BF16: thread t takes chunks t, t + nthr, ...  The next item's loads are
+// issued before the current item is quantised, so the load latency is paid
+// once, and the quantiser is compiled once.
+template <int KIND>
+__device__ __forceinline__ void planes_from_global(const float* x, int K, int Kp, int pstride, const JobSmem& S) {
+    const int lane = threadIdx.x & 31;
+    const int first = KIND == kQ4K ? static_cast<int>(threadIdx.x >> 5) : static_cast<int>(threadIdx.x);
+    const int step = KIND == kQ4K ? static_cast<int>(blockDim.x >> 5) : static_cast<int>(blockDim.x);
+    const int n = KIND == kQ4K ? Kp / kQ4KSegCols : Kp / 8;
+    auto col = [&](int i) { return KIND == kQ4K ? i * kQ4KSegCols + lane * 8 : i * 8; };
+    float4 lo, hi;
+    if (first < n) load8(x, col(first), K, lo, hi);
+#pragma unroll 1
+    for (int i = first; i < n; i += step) {
+        float4 nlo = make_float4(0.f, 0.f, 0.f, 0.f), nhi = nlo;
+        if (i + step < n) load8(x, col(i + step), K, nlo, nhi);
+        chunk_planes<KIND>(lo, hi, i, lane, pstride, S);
+        lo = nlo;
+        hi = nhi;
+    }
+}
+
+// Planes of the pre-normed x: S.xs holds the residual stream (K floats), and
+// x = xs * r * (1 + g_pre) (rms_norm_gemma3, src/autograd2.rs:3477-3496) is
+// formed as it is read.
+template <int KIND>
+__device__ __forceinline__ void planes_from_smem(int K, int Kp, int pstride, float r, const JobSmem& S) {
+    const int lane = threadIdx.x & 31;
+    const int first = KIND == kQ4K ? static_cast<int>(threadIdx.x >> 5) : static_cast<int>(threadIdx.x);
+    const int step = KIND == kQ4K ? static_cast<int>(blockDim.x >> 5) : static_cast<int>(blockDim.x);
+    const int n = KIND == kQ4K ? Kp / kQ4KSegCols : Kp / 8;
+#pragma unroll 1
+    for (int i = first; i < n; i += step) {
+        const int c0 = KIND == kQ4K ? i * kQ4KSegCols + lane * 8 : i * 8;
+        float4 lo, hi, glo, ghi;
+        load8(S.xs, c0, K, lo, hi);
+        load8(S.gpre, c0, K, glo, ghi);
+        auto nrm = [&](float v, float gm) { return __fmul_rn(__fmul_rn(v, r), __fadd_rn(1.0f, gm)); };
+        lo = make_float4(nrm(lo.x, glo.x), nrm(lo.y, glo.y), nrm(lo.z, glo.z), nrm(lo.w, glo.w));
+        hi = make_float4(nrm(hi.x, ghi.x), nrm(hi.y, ghi.y), nrm(hi.z, ghi.z), nrm(hi.w, ghi.w));
+        chunk_planes<KIND>(lo, hi, i, lane, pstride, S);
+    }
+}
+
+__device__ __forceinline__ float sumsq4(const float4& v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+
 // Build the planes of x for job j in shared memory (all threads of the CTA).
-// Norm prologues wait for gamma phase `pbar_phase`.  Ends with __syncthreads.
+// Norm prologues wait for gamma phase `pbar_phase` and stage the residual
+// stream in S.xs (K floats; the residual-update prologue also stages the
+// sub-layer output in S.sub).  Ends with __syncthreads.
 template <int KIND, int PRO>
 __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uint32_t pbar_phase) {
     const int tid = threadIdx.x, nthr = blockDim.x;
-    const int lane = tid & 31, warp = tid >> 5;
+    const int lane = tid & 31;
     const int K = a.K, nseg = a.nseg;
     const int Kp = nseg * seg_cols(KIND);
     const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
     if constexpr (PRO == kProPlain) {
-        // 8-column chunks q = tid + i * nthr; for Q4_K a warp covers one segment
-        // per i.  All loads of a group of kMaxV8 chunks are in flight together.
-        const int nq = Kp / 8;
-        for (int base0 = 0; base0 < nq; base0 += kMaxV8 * nthr) {
-            float4 xl[kMaxV8][2];
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (base0 + i * nthr + tid) * 8;
-                if (c0 + 8 <= K) {
-                    xl[i][0] = *reinterpret_cast<const float4*>(a.x + c0);
-                    xl[i][1] = *reinterpret_cast<const float4*>(a.x + c0 + 4);
-                } else {
-                    xl[i][0] = xl[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int base = base0 + i * nthr;
-                if (base >= nq) break;
-                const int qi = base + tid;
-                const float xv[8] = {xl[i][0].x, xl[i][0].y, xl[i][0].z, xl[i][0].w,
-                                     xl[i][1].x, xl[i][1].y, xl[i][1].z, xl[i][1].w};
-                if constexpr (KIND == kQ4K) {
-                    if (base + warp * 32 < nq) q4k_segment_planes(xv, (base >> 5) + warp, lane, pstride, S.planes, S.xsx);
-                } else {
-                    if (qi < nq) bf16_chunk_planes(xv, qi, pstride, S.planes);
-                }
-            }
-        }
+        planes_from_global<KIND>(a.x, K, Kp, pstride, S);
     } else {
-        // Thread chunk i holds columns 8q..8q+7, q = tid + i * nthr.
         const float inv_d = 1.0f / static_cast<float>(K);
-        float xr[kMaxV8][8];
         float ss = 0.f;
         if constexpr (PRO == kProResidNorm) {
             // post-norm of the sub-layer output, then the residual add
             // (Gemma3Block::forward_cached, src/transformer4.rs:1954-1964)
-            float v[kMaxV8][8];
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (tid + i * nthr) * 8;
-                if (c0 < K) {
-                    const float4 s0 = *reinterpret_cast<const float4*>(a.src + c0);
-                    const float4 s1 = *reinterpret_cast<const float4*>(a.src + c0 + 4);
-                    v[i][0] = s0.x; v[i][1] = s0.y; v[i][2] = s0.z; v[i][3] = s0.w;
-                    v[i][4] = s1.x; v[i][5] = s1.y; v[i][6] = s1.z; v[i][7] = s1.w;
-                    const float4 r0 = *reinterpret_cast<const float4*>(a.resid_in + c0);
-                    const float4 r1 = *reinterpret_cast<const float4*>(a.resid_in + c0 + 4);
-                    xr[i][0] = r0.x; xr[i][1] = r0.y; xr[i][2] = r0.z; xr[i][3] = r0.w;
-                    xr[i][4] = r1.x; xr[i][5] = r1.y; xr[i][6] = r1.z; xr[i][7] = r1.w;
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) v[i][e] = xr[i][e] = 0.f;
-                }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+            float* sub = S.sub;
+#pragma unroll 2
+            for (int c = tid * 4; c < K; c += nthr * 4) {
+                const float4 s4 = *reinterpret_cast<const float4*>(a.src + c);
+                const float4 r4 = *reinterpret_cast<const float4*>(a.resid_in + c);
+                *reinterpret_cast<float4*>(sub + c) = s4;
+                *reinterpret_cast<float4*>(S.xs + c) = r4;
+                ss += sumsq4(s4);
             }
             ss = block_sum(ss, S.red);
             if (!mbar_wait(S.pbar, pbar_phase) && lane == 0) atomicExch(&S.flag[0], 1);
             const float r1 = 1.0f / sqrtf(ss * inv_d + a.eps);
             float ss2 = 0.f;
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (tid + i * nthr) * 8;
-                if (c0 < K) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float nv =
-                            __fadd_rn(xr[i][e], __fmul_rn(__fmul_rn(v[i][e], r1), __fadd_rn(1.0f, S.gpost[c0 + e])));
-                        xr[i][e] = nv;
-                        ss2 += nv * nv;
-                    }
-                    if (blockIdx.x == 0) {
-                        *reinterpret_cast<float4*>(a.resid_out + c0) = make_float4(xr[i][0], xr[i][1], xr[i][2], xr[i][3]);
-                        *reinterpret_cast<float4*>(a.resid_out + c0 + 4) = make_float4(xr[i][4], xr[i][5], xr[i][6], xr[i][7]);
-                    }
-                }
+#pragma unroll 1
+            for (int c = tid * 4; c < K; c += nthr * 4) {
+                const float4 s4 = *reinterpret_cast<const float4*>(sub + c);
+                const float4 r4 = *reinterpret_cast<const float4*>(S.xs + c);
+                const float4 g4 = *reinterpret_cast<const float4*>(S.gpost + c);
+                auto upd = [&](float rv, float sv, float gv) {
+                    return __fadd_rn(rv, __fmul_rn(__fmul_rn(sv, r1), __fadd_rn(1.0f, gv)));
+                };
+                const float4 nv = make_float4(upd(r4.x, s4.x, g4.x), upd(r4.y, s4.y, g4.y), upd(r4.z, s4.z, g4.z),
+                                              upd(r4.w, s4.w, g4.w));
+                *reinterpret_cast<float4*>(S.xs + c) = nv;
+                if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.resid_out + c) = nv;
+                ss2 += sumsq4(nv);
             }
             ss = block_sum(ss2, S.red);
         } else {
             // embedding row * sqrt(hidden) (src/transformer4.rs:2360-2364)
-            const int64_t tok = static_cast<int64_t>(*a.token);
-            const uint16_t* er = a.embed + tok * K;
-#pragma unroll
-            for (int i = 0; i < kMaxV8; ++i) {
-                const int c0 = (tid + i * nthr) * 8;
-                if (c0 < K) {
-                    const uint4 e = *reinterpret_cast<const uint4*>(er + c0);
-                    const uint32_t ew[4] = {e.x, e.y, e.z, e.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        xr[i][2 * k] = __fmul_rn(bf16_bits_to_f32(ew[k] & 0xFFFFu), a.embed_scale);
-                        xr[i][2 * k + 1] = __fmul_rn(bf16_bits_to_f32(ew[k] >> 16), a.embed_scale);
-                    }
-#pragma unroll
-                    for (int e2 = 0; e2 < 8; ++e2) ss += xr[i][e2] * xr[i][e2];
-                    if (blockIdx.x == 0) {
-                        *reinterpret_cast<float4*>(a.resid_out + c0) = make_float4(xr[i][0], xr[i][1], xr[i][2], xr[i][3]);
-                        *reinterpret_cast<float4*>(a.resid_out + c0 + 4) = make_float4(xr[i][4], xr[i][5], xr[i][6], xr[i][7]);
-                    }
-                } else {
-#pragma unroll
-                    for (int e2 = 0; e2 < 8; ++e2) xr[i][e2] = 0.f;
-                }
+            const uint16_t* er = a.embed + static_cast<int64_t>(*a.token) * K;
+#pragma unroll 2
+            for (int c = tid * 4; c < K; c += nthr * 4) {
+                const uint2 e = *reinterpret_cast<const uint2*>(er + c);
+                const float4 v = make_float4(__fmul_rn(bf16_bits_to_f32(e.x & 0xFFFFu), a.embed_scale),
+                                             __fmul_rn(bf16_bits_to_f32(e.x >> 16), a.embed_scale),
+                                             __fmul_rn(bf16_bits_to_f32(e.y & 0xFFFFu), a.embed_scale),
+                                             __fmul_rn(bf16_bits_to_f32(e.y >> 16), a.embed_scale));
+                *reinterpret_cast<float4*>(S.xs + c) = v;
+                if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.resid_out + c) = v;
+                ss += sumsq4(v);
             }
             ss = block_sum(ss, S.red);
             if (!mbar_wait(S.pbar, pbar_phase) && lane == 0) atomicExch(&S.flag[0], 1);
         }
-        // pre-norm producing the projection input (rms_norm_gemma3,
-        // src/autograd2.rs:3477-3496), then the planes
-        const float r2 = 1.0f / sqrtf(ss * inv_d + a.eps);
-        const int nq = Kp / 8;
-#pragma unroll
-        for (int i = 0; i < kMaxV8; ++i) {
-            const int base = i * nthr;
-            if (base >= nq) break;
-            const int qi = base + tid;
-            const int c0 = qi * 8;
-            float xv[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-                xv[e] = c0 < K ? __fmul_rn(__fmul_rn(xr[i][e], r2), __fadd_rn(1.0f, S.gpre[c0 + e])) : 0.f;
-            if constexpr (KIND == kQ4K) {
-                if (base + warp * 32 < nq) q4k_segment_planes(xv, (base >> 5) + warp, lane, pstride, S.planes, S.xsx);
-            } else {
-                if (qi < nq) bf16_chunk_planes(xv, qi, pstride, S.planes);
-            }
-        }
+        // pre-norm producing the projection input, applied as the planes are built
+        planes_from_smem<KIND>(K, Kp, pstride, 1.0f / sqrtf(ss * inv_d + a.eps), S);
     }
     __syncthreads();
 }
 
+// How the warps' shares of a job are laid out (Job::tile_split matches it).
+enum SplitMode : int {
+    kSplitGrid = 0,  // whole-grid warp split; shared tiles combined through global scratch
+    kSplitTile = 1,  // CTAs own whole tiles; shared tiles combined in shared memory (cta_combine)
+};
+
 // Stream this warp's units of job `a` (whose planes are ready) through the
 // epilogue.  Returns false if a wait gave up (the warp's stream is then
 // abandoned; the caller drains it).  best_v / best_i: running greedy argmax.
-template <int KIND, int EPI>
+template <int KIND, int EPI, int SPLIT>
 __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const JobSmem& S, const SplitScratch& sc,
                                               float& best_v, long long& best_i) {
     const int lane = threadIdx.x & 31;
@@ -605,13 +609,10 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     const int nseg = a.nseg;
     const int Kp = nseg * seg_cols(KIND);
     const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
-    const uint32_t gw = st.cta * st.nw + st.warp;
-    Split sp;  // the whole-grid split (owner lookups of the per-warp combine)
-    sp.init(job_units(a), st.ncta * st.nw);
     const Share sh = warp_share(a, st.cta, st.ncta, st.warp, st.nw);
     const uint32_t u_begin = sh.s;
     const int n = static_cast<int>(sh.e - sh.s);
-    if (a.tile_split && lane == 0) S.wse[st.warp] = make_uint2(sh.s, sh.e);
+    if (SPLIT == kSplitTile && lane == 0) S.wse[st.warp] = make_uint2(sh.s, sh.e);
 
     // Row epilogue: lane L < 16 holds the sum of row r0 + L.
     auto emit_rows = [&](int64_t r0, float v) {
@@ -750,11 +751,14 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
             const int64_t r0 = static_cast<int64_t>(tile) * kTile;
             if (pu == nseg) {
                 emit_rows(r0, rowv);
-            } else if (a.tile_split) {
+            } else if constexpr (SPLIT == kSplitTile) {
                 // Combined later by the CTA (cta_combine), in shared memory.
                 const int slot = tile == first_tile ? 0 : 1;
                 if (lane < kTile) S.wpart[((threadIdx.x >> 5) * 2 + slot) * kTile + lane] = rowv;
             } else {
+                Split sp;  // the whole-grid split (owner lookups)
+                sp.init(job_units(a), st.ncta * st.nw);
+                const uint32_t gw = st.cta * st.nw + st.warp;
                 // Lanes 16..31 (row = lane - 16) publish the piece.
                 const int slot = tile == first_tile ? 0 : 1;
                 const bool pub = lane >= kTile;
@@ -829,16 +833,19 @@ __device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, floa
         const uint32_t u0 = T * nseg, u1 = u0 + nseg;
         float v0 = 0.f, v1 = 0.f;
         int pieces = 0;
-        for (uint32_t w = 0; w < nw; ++w) {
-            const uint2 se = S.wse[w];
-            if (se.x >= se.y || se.x >= u1 || se.y <= u0) continue;
-            ++pieces;
+        // All warps' table entries and pieces are loaded at once (unrolled,
+        // predicated); the sum runs in warp order, adding zero for warps
+        // without a piece of this tile.
+#pragma unroll
+        for (int w = 0; w < kMaxWarps; ++w) {
+            const uint2 se = w < static_cast<int>(nw) ? S.wse[w] : make_uint2(0u, 0u);
+            const bool in = se.x < se.y && se.x < u1 && se.y > u0;
+            pieces += in ? 1 : 0;
             // a warp that began in an earlier tile keeps this one in slot 1
             const float* pw = S.wpart + (w * 2 + (se.x < u0 ? 1 : 0)) * kTile;
-            if (lane < kPer) {
-                v0 += pw[row];
-                if constexpr (EPI == kEpiGeluPair) v1 += pw[row + 1];
-            }
+            const bool rd = in && lane < kPer;
+            v0 += rd ? pw[row] : 0.f;
+            if constexpr (EPI == kEpiGeluPair) v1 += rd ? pw[row + 1] : 0.f;
         }
         if (pieces < 2) continue;  // one warp had it all: already through the epilogue
         if (lane >= kPer) continue;

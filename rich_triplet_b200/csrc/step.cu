@@ -62,9 +62,11 @@ struct StepSmem {
     long long* bi;
     float* gpost;    // [hidden]
     float* gpre;     // [hidden]
+    float* xs;       // [hidden] residual stream (norm prologues)
     float* wpart;    // [warps][2][16]
     uint2* wse;      // [warps]
-    uint8_t* uni;    // planes + xsx of a projection, or an attention item
+    uint8_t* uni;    // planes + xsx of a projection (first the sub-layer output of a norm
+                     // prologue), or an attention item
     float2* xsx;
     uint8_t* ring;   // [warps][nb][kSlotBytes]
 };
@@ -86,13 +88,16 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
     uint8_t* bi = take(8 * 32, 16);
     uint8_t* gpost = take(sizeof(float) * g.hidden, 16);
     uint8_t* gpre = take(sizeof(float) * g.hidden, 16);
+    uint8_t* xs = take(sizeof(float) * g.hidden, 16);
     uint8_t* wpart = take(sizeof(float) * g.warps * 2 * 16, 16);
     uint8_t* wse = take(sizeof(uint2) * g.warps, 16);
     const size_t q4 = (planes_bytes(kQ4K, g.kp_max) + 127) / 128 * 128;
     const size_t q4all = q4 + xsx_bytes(kQ4K, g.kp_max), bf = planes_bytes(kBF16, g.kp_lm);
     const size_t proj = q4all > bf ? q4all : bf;
     const size_t att = acore::attn_carve(nullptr, g.head_dim, g.group, kAttnT, nullptr);
-    uint8_t* uni = take(proj > att ? proj : att, 128);
+    size_t un = proj > att ? proj : att;
+    if (un < sizeof(float) * g.hidden) un = sizeof(float) * g.hidden;  // the sub-layer output of a norm prologue
+    uint8_t* uni = take(un, 128);
     uint8_t* ring = take(static_cast<size_t>(g.warps) * g.nb * kSlotBytes, 128);
     if (S) {
         S->full = reinterpret_cast<uint64_t*>(full);
@@ -104,6 +109,7 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
         S->bi = reinterpret_cast<long long*>(bi);
         S->gpost = reinterpret_cast<float*>(gpost);
         S->gpre = reinterpret_cast<float*>(gpre);
+        S->xs = reinterpret_cast<float*>(xs);
         S->wpart = reinterpret_cast<float*>(wpart);
         S->wse = reinterpret_cast<uint2*>(wse);
         S->uni = uni;
@@ -150,7 +156,7 @@ __device__ __forceinline__ bool grid_sync(const StepParams& P, uint32_t& nsync, 
 template <int KIND, int EPI>
 __device__ __forceinline__ void run_units(const Job& j, Stream& st, const JobSmem& JS, const StepParams& P,
                                           int* flags, float& best_v, long long& best_i) {
-    if (!job_units_run<KIND, EPI>(j, st, JS, P.scratch, best_v, best_i)) {
+    if (!job_units_run<KIND, EPI, kSplitTile>(j, st, JS, P.scratch, best_v, best_i)) {
         if ((threadIdx.x & 31) == 0) {
             atomicExch(&flags[0], 1);
             if (P.err) atomicExch(P.err, kErrMbarTimeout);
@@ -177,7 +183,7 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         S.flags[0] = S.flags[1] = S.flags[2] = S.flags[3] = 0;
     }
     __syncthreads();
-    const JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse};
+    const JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse, S.xs, reinterpret_cast<float*>(S.uni)};
     const int njobs = 4 * P.nlayers + 1;
     Stream st;
     stream_start(st, S.full + warp * nb, S.ring + static_cast<size_t>(warp) * nb * kSlotBytes, nb, kSlotBytes, P.jobs,
@@ -310,9 +316,8 @@ StepGeom step_geometry(int hidden, int kp_max, int head_dim, int group) {
     g.kp_lm = (hidden + kBF16SegCols - 1) / kBF16SegCols * kBF16SegCols;
     g.head_dim = head_dim;
     g.group = group;
-    // The norm prologues hold at most kMaxV8 chunks of 8 columns per thread;
     // head_dim must fit one thread per column in the attention PV loop.
-    const bool fits_threads = hidden <= kMaxV8 * 8 * kStepWarps * 32 && head_dim <= kStepWarps * 32 && head_dim % 32 == 0;
+    const bool fits_threads = head_dim <= kStepWarps * 32 && head_dim % 32 == 0;
     const bool fits_group = group == 1 || group == 2 || group == 4;
     g.smem = step_carve(nullptr, g, nullptr) + 128;
     if (!fits_threads || !fits_group || g.smem > 226 * 1024) g.warps = 0;
