@@ -127,6 +127,19 @@ int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags
 int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int cols, const float* x_dev, float* y_dev,
                                int32_t* token_dev, void* stream, char* errbuf, size_t errlen);
 
+/* GEMV throughput measurement (no counterpart in the reference, whose GEMV
+ * test times nothing).  Captures one CUDA graph of `launches` GEMVs of the
+ * same shape, launch i reading ws[i % nw] (a rotation over several weight
+ * copies keeps them out of L2), x_dev -> y_dev (device memory, 16-byte
+ * aligned), each launch chained to the previous one by programmatic
+ * dependent launch; replays it `reps` times and writes the mean device time
+ * per GEMV in microseconds.  ctas_per_sm 1: one CTA per SM (the plan
+ * rt_gemv_q4k uses); 2: half-size CTAs, so that the next GEMV of the chain
+ * streams its weights beside the previous one.  Synchronises the context.
+ * fmt: RT_FMT_Q4K or RT_FMT_BF16, matching every weight. */
+int rt_gemv_bench(rt_ctx* ctx, int fmt, const rt_w* const* ws, int nw, const float* x_dev, float* y_dev, int launches,
+                  int ctas_per_sm, int reps, float* us_per_gemv);
+
 /* ---- load-time conversions (bit-exact with the reference CPU code) ---- */
 
 /* GGUF Q4_0 bytes of a [rows, cols] tensor -> Q4_K weight in HBM, as

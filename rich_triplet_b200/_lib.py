@@ -91,6 +91,8 @@ SIGNATURES = {
         ctypes.c_int,
         [_vp, ctypes.c_int64, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_char_p, ctypes.c_size_t],
     ),
+    "rt_gemv_bench": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp), ctypes.c_int, _vp, _vp, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),
     "rt_convert_q4_0_to_q4k": (ctypes.c_int, [_vp, _vp, _i64, _i64, ctypes.c_int, _pp]),
     "rt_convert_q6k_to_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i64, ctypes.c_int, _pp]),
     "rt_decoder_create": (ctypes.c_int, [_vp, ctypes.POINTER(RtGemma3Cfg), ctypes.POINTER(RtGemma3Layer), _vp,

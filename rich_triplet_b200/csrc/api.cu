@@ -5,6 +5,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <vector>
 #include <atomic>
 #include <mutex>
 
@@ -279,6 +280,66 @@ int rt_gemv_q4k(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags)
 
 int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags) {
     return gemv_common(ctx, w, x, y, flags, rt::kBF16);
+}
+
+int rt_gemv_bench(rt_ctx* ctx, int fmt, const rt_w* const* ws, int nw, const float* x, float* y, int launches,
+                  int ctas_per_sm, int reps, float* us_per_gemv) {
+    if (!ctx || !ws || nw < 1 || !x || !y || !us_per_gemv) return fail(ctx, RT_E_INVAL, "rt_gemv_bench: null argument");
+    if (fmt != RT_FMT_Q4K && fmt != RT_FMT_BF16) return fail(ctx, RT_E_FORMAT, "rt_gemv_bench: fmt %d", fmt);
+    if (launches < 1 || launches > 4096 || reps < 1 || (ctas_per_sm != 1 && ctas_per_sm != 2))
+        return fail(ctx, RT_E_INVAL, "rt_gemv_bench: launches 1..4096, reps >= 1, ctas_per_sm 1 or 2");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+        return fail(ctx, RT_E_INVAL, "rt_gemv_bench: x and y must be 16-byte aligned device pointers");
+    for (int i = 0; i < nw; ++i)
+        if (!ws[i] || ws[i]->fmt != fmt || ws[i]->rows != ws[0]->rows || ws[i]->cols != ws[0]->cols)
+            return fail(ctx, RT_E_SHAPE, "rt_gemv_bench: weight %d differs in format or shape", i);
+    const int kind = fmt == RT_FMT_Q4K ? rt::kQ4K : rt::kBF16;
+    const int64_t rows = ws[0]->rows;
+    const int K = static_cast<int>(ws[0]->cols);
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const rt::GemvPlan p = rt::gemv_plan(kind, rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, ctas_per_sm);
+    if (p.warps == 0) return fail(ctx, RT_E_SHAPE, "rt_gemv_bench: no launch geometry for cols %d", K);
+    std::vector<CUtensorMap> tm(nw);
+    for (int i = 0; i < nw; ++i)
+        if (!rt::gemv_make_tmap(kind, ws[i]->d, rows, K, p, &tm[i]))
+            return fail(ctx, RT_E_CUDA, "rt_gemv_bench: TMA descriptor rejected");
+    if (int rc = ensure_gemv_scratch(ctx, p); rc != RT_OK) return rc;
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+    for (int i = 0; e == cudaSuccess && i < launches; ++i) {
+        rt::GemvArgs a = {};
+        a.w = static_cast<const uint8_t*>(ws[i % nw]->d);
+        a.rows = rows;
+        a.K = K;
+        a.x = x;
+        a.y = y;
+        a.part = ctx->gemv_part;
+        a.tile_cnt = ctx->gemv_cnt;
+        a.err = ctx->d_err;
+        e = rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, tm[i % nw], p, ctx->stream, i > 0);
+    }
+    const cudaError_t ec = cudaStreamEndCapture(ctx->stream, &graph);
+    if (e == cudaSuccess) e = ec;
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, ctx->stream);  // warm-up
+    if (e == cudaSuccess) e = cudaEventRecord(e0, ctx->stream);
+    for (int r = 0; e == cudaSuccess && r < reps; ++r) e = cudaGraphLaunch(exec, ctx->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(e1, ctx->stream);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    RT_CHECK_CUDA(ctx, e);
+    *us_per_gemv = ms * 1000.f / static_cast<float>(reps * launches);
+    return rt_sync(ctx);
 }
 
 int rt_convert_q4_0_to_q4k(rt_ctx* ctx, const void* q4_0, int64_t rows, int64_t cols, int flags, rt_w** out) {

@@ -155,6 +155,16 @@ def gemv_device(ctx, w: DeviceWeight, x_ptr, y_ptr):
     check(fn(ctx.h, w.h, x_ptr, y_ptr, RT_DEVICE), ctx.h)
 
 
+def gemv_bench(ctx, weights, x_ptr, y_ptr, launches=256, ctas_per_sm=2, reps=3):
+    """Mean device time (us) per GEMV over a CUDA graph of `launches` chained
+    GEMVs rotating over `weights` (same format and shape); see rt_gemv_bench."""
+    arr = (ctypes.c_void_p * len(weights))(*[w.h for w in weights])
+    us = ctypes.c_float()
+    check(lib().rt_gemv_bench(ctx.h, weights[0].fmt, arr, len(weights), x_ptr, y_ptr, launches, ctas_per_sm, reps,
+                              ctypes.byref(us)), ctx.h)
+    return us.value
+
+
 def convert_q4_0_to_q4k(ctx, q4_0_bytes, rows, cols):
     """GGUF Q4_0 -> Q4_K on the GPU, bit-exact with decode_q4_0_to_q4mat +
     Q4KMat::from_q4mat (src/gguf_loader.rs:282-350, src/autograd2.rs:1291-1320)."""

@@ -132,3 +132,31 @@ def test_q4k_gemv_zero_and_extreme_blocks(orc):
     ref = orc.q4k_gemv(blocks, rows, cols, x)
     assert np.all(y[:10] == 0.0)
     assert _rel(y, ref).max() < REL_TOL
+
+
+@pytest.mark.parametrize("ctas_per_sm", [1, 2])
+def test_gemv_bench_graph_matches_gemv(ctas_per_sm):
+    # rt_gemv_bench replays a graph of chained GEMVs over rotating weights; the
+    # last launch's y must equal a plain GEMV of the same weight.
+    import torch
+
+    from rich_triplet_b200.ops import Context, gemv_bench, gemv_device
+
+    rows, cols = 1000, 2304
+    ctx = Context(0)
+    try:
+        ws = [DeviceWeight.upload(ctx, RT_FMT_Q4K, synth_q4k(5, 40 + c, rows, cols), rows, cols) for c in range(3)]
+        x = torch.from_numpy(synth_normal(6, 1, cols)).cuda()
+        y = torch.empty(rows, dtype=torch.float32, device="cuda")
+        y_ref = torch.empty(rows, dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        launches = 5  # last launch reads ws[4 % 3] = ws[1]
+        us = gemv_bench(ctx, ws, x.data_ptr(), y.data_ptr(), launches=launches, ctas_per_sm=ctas_per_sm, reps=2)
+        assert us > 0.0
+        gemv_device(ctx, ws[1], x.data_ptr(), y_ref.data_ptr())
+        ctx.sync()
+        assert np.allclose(y.cpu().numpy(), y_ref.cpu().numpy(), rtol=1e-5, atol=1e-4)
+        for w in ws:
+            w.free()
+    finally:
+        ctx.close()
