@@ -222,12 +222,17 @@ cudaError_t q6k_to_bf16_launch(const uint8_t* q6, int64_t n_elem, uint16_t* out,
 namespace {
 
 // One warp per 16-row x 144-byte unit, 16-byte words.
-__global__ void q4k_tile_major_kernel(const uint4* in, int64_t rows, int nseg, uint4* out, int64_t nunits) {
+__global__ void q4k_tile_major_kernel(const uint4* in, int64_t rows, int nseg, int parts, uint4* out, int64_t nunits) {
     const int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (u >= nunits) return;
-    const int64_t t = u / nseg;
-    const int s = static_cast<int>(u - t * nseg);
+    // u = (p * ntiles + t) * nsp + j  ->  block (t, p * nsp + j) of the source
+    const int nsp = nseg / parts;
+    const int64_t ntiles = (rows + 15) / 16;
+    const int64_t v = u / nsp;
+    const int j = static_cast<int>(u - v * nsp);
+    const int64_t p = v / ntiles, t = v - p * ntiles;
+    const int s = static_cast<int>(p) * nsp + j;
     for (int k = lane; k < 16 * 9; k += 32) {
         const int i = k / 9, c = k - 9 * (k / 9);
         const int64_t r = t * 16 + i;
@@ -237,13 +242,14 @@ __global__ void q4k_tile_major_kernel(const uint4* in, int64_t rows, int nseg, u
 
 }  // namespace
 
-cudaError_t q4k_tile_major_launch(const uint8_t* in, int64_t rows, int nseg, uint8_t* out, cudaStream_t s) {
+cudaError_t q4k_tile_major_launch(const uint8_t* in, int64_t rows, int nseg, int parts, uint8_t* out, cudaStream_t s) {
+    if (parts < 1 || nseg % parts != 0) return cudaErrorInvalidValue;
     const int64_t nunits = (rows + 15) / 16 * nseg;
     if (nunits <= 0) return cudaSuccess;
     const int threads = 256;
     const int64_t blocks = (nunits * 32 + threads - 1) / threads;
     q4k_tile_major_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(reinterpret_cast<const uint4*>(in), rows, nseg,
-                                                                          reinterpret_cast<uint4*>(out), nunits);
+                                                                          parts, reinterpret_cast<uint4*>(out), nunits);
     return cudaGetLastError();
 }
 

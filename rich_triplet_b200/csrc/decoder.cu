@@ -43,6 +43,9 @@
 
 using rt::fail;
 
+// Column parts of the step kernel's down projection (a divisor of FFN / 256).
+constexpr int kMaxDownParts = 4;
+
 struct rt_dec {
     rt_ctx* ctx = nullptr;
     rt_gemma3_cfg cfg{};
@@ -72,6 +75,7 @@ struct rt_dec {
     std::vector<CUtensorMap> t_qkv, t_o, t_gu, t_down;  // TMA descriptors of the weights
     CUtensorMap t_lm;
     int nsplit = 0;
+    int down_parts = 1;  // column parts of the step kernel's down projection (partials in `down`)
     int final_resid = 0;
     int launches = 0;
     cudaGraph_t graph = nullptr;
@@ -340,12 +344,12 @@ int build_step(rt_dec* d) {
     if ((rc = dalloc(d, reinterpret_cast<void**>(&d_sync), 4 * sizeof(uint32_t), "step sync")) != RT_OK) return rc;
     // Tile-major copies of the Q4_K projections: each warp's share of a
     // projection is then one contiguous byte range (1-D bulk copies).
-    auto tile_major = [&](const uint8_t* w, int64_t rows, int K, const uint8_t** out) -> int {
+    auto tile_major = [&](const uint8_t* w, int64_t rows, int K, int parts, const uint8_t** out) -> int {
         uint8_t* t = nullptr;
         const size_t bytes = static_cast<size_t>((rows + 15) / 16) * (K / 256) * 2304;
         int r = dalloc(d, reinterpret_cast<void**>(&t), bytes, "tile-major weight");
         if (r != RT_OK) return r;
-        if (rt::q4k_tile_major_launch(w, rows, K / 256, t, ctx->stream) != cudaSuccess)
+        if (rt::q4k_tile_major_launch(w, rows, K / 256, parts, t, ctx->stream) != cudaSuccess)
             return fail(ctx, RT_E_CUDA, "tile-major weight copy");
         *out = t;
         return RT_OK;
@@ -378,6 +382,7 @@ int build_step(rt_dec* d) {
             p = 0;
         } else {
             jq.src = d->down;
+            jq.src_parts = d->down_parts;
             jq.resid_in = d->resid[p];
             jq.resid_out = d->resid[1 - p];
             jq.g_post = norm_ptr(d, l - 1, 3);
@@ -396,14 +401,19 @@ int build_step(rt_dec* d) {
         jg.y = d->hbuf;
         jg.tile_split = 1;
         p = 1 - p;
-        rt::gcore::Job& jd = q4k(4 * l + 3, H, d->F);
+        // down: column split into down_parts GEMVs (the 160 tiles of a 2560-row
+        // output would leave some CTAs twice the units of others)
+        rt::gcore::Job& jd = q4k(4 * l + 3, static_cast<int64_t>(d->down_parts) * H, d->F);
+        jd.nseg = d->F / 256 / d->down_parts;
+        jd.kparts = d->down_parts;
+        jd.ptiles = static_cast<int32_t>(H / 16);
         jd.x = d->hbuf;
         jd.y = d->down;
         jd.tile_split = 1;
-        if ((rc = tile_major(d->w_qkv[l], d->qkv_rows, H, &jq.wt)) != RT_OK ||
-            (rc = tile_major(d->w_o[l], H, d->NQ * D, &jo.wt)) != RT_OK ||
-            (rc = tile_major(d->w_gu[l], 2LL * d->F, H, &jg.wt)) != RT_OK ||
-            (rc = tile_major(d->w_down[l], H, d->F, &jd.wt)) != RT_OK)
+        if ((rc = tile_major(d->w_qkv[l], d->qkv_rows, H, 1, &jq.wt)) != RT_OK ||
+            (rc = tile_major(d->w_o[l], H, d->NQ * D, 1, &jo.wt)) != RT_OK ||
+            (rc = tile_major(d->w_gu[l], 2LL * d->F, H, 1, &jg.wt)) != RT_OK ||
+            (rc = tile_major(d->w_down[l], H, d->F, d->down_parts, &jd.wt)) != RT_OK)
             return rc;
         rt::AttnArgs& a = attn[l];
         a = rt::AttnArgs{};
@@ -439,6 +449,7 @@ int build_step(rt_dec* d) {
     jl.rows = d->V;
     jl.eps = eps;
     jl.src = d->down;
+    jl.src_parts = d->down_parts;
     jl.resid_in = d->resid[p];
     jl.resid_out = d->resid[1 - p];
     jl.g_post = norm_ptr(d, NL - 1, 3);
@@ -660,11 +671,17 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
     if (!rt::gemv_make_tmap(rt::kBF16, d->embed, d->V, H, d->p_lm, &d->t_lm))
         return bail(fail(ctx, RT_E_CUDA, "rt_decoder_create: TMA descriptor rejected (LM head)"));
     d->nsplit = std::max(1, std::min(64, (ctx->num_sms + d->NKV - 1) / d->NKV));
+    for (int parts = kMaxDownParts; parts >= 1; parts /= 2)
+        if ((d->F / 256) % parts == 0) {
+            d->down_parts = parts;
+            break;
+        }
     if (rt::attention_prepare() != cudaSuccess) return bail(fail(ctx, RT_E_CUDA, "attention kernel attributes"));
     // --- activations ---
     {
         const size_t G_ = static_cast<size_t>(G);
-        const size_t n_act = 2 * static_cast<size_t>(H) + d->qkv_rows + static_cast<size_t>(d->NQ) * D + H + d->F + H +
+        const size_t n_act = 2 * static_cast<size_t>(H) + d->qkv_rows + static_cast<size_t>(d->NQ) * D + H + d->F +
+                             static_cast<size_t>(kMaxDownParts) * H +
                              d->V + static_cast<size_t>(d->NKV) * d->nsplit * G_ * rt::attn_part_stride(D) + d->p_lm.grid + 10 * 64;
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->act), n_act * 4 + 1024, "activations")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->act, 0, n_act * 4 + 1024, s);
@@ -682,7 +699,7 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
         d->attn = slice(static_cast<size_t>(d->NQ) * D);
         d->o_out = slice(H);
         d->hbuf = slice(d->F);
-        d->down = slice(H);
+        d->down = slice(static_cast<size_t>(kMaxDownParts) * H);  // the step path keeps down_parts partials
         d->logits = slice(d->V);
         d->attn_part = slice(static_cast<size_t>(d->NKV) * d->nsplit * G_ * rt::attn_part_stride(D));
         d->am_val = slice(d->p_lm.grid);
@@ -821,6 +838,20 @@ int rt_decoder_read_activation(rt_dec* d, int32_t which, float* host, int64_t co
     } else if (which == 1) {
         src = d->logits;
         n = d->V;
+    } else if (which == 7 && d->use_step && d->down_parts > 1) {
+        // the step kernel leaves the down projection as column-part partials
+        if (count < 0 || count > d->H) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_read_activation: count %lld > %lld",
+                                                   static_cast<long long>(count), static_cast<long long>(d->H));
+        std::vector<float> parts(static_cast<size_t>(d->down_parts) * d->H);
+        RT_CHECK_CUDA(d->ctx, cudaMemcpyAsync(parts.data(), d->down, sizeof(float) * parts.size(), cudaMemcpyDeviceToHost,
+                                              d->ctx->stream));
+        RT_CHECK_CUDA(d->ctx, cudaStreamSynchronize(d->ctx->stream));
+        for (int64_t i = 0; i < count; ++i) {
+            float v = parts[i];
+            for (int q = 1; q < d->down_parts; ++q) v += parts[static_cast<size_t>(q) * d->H + i];
+            host[i] = v;
+        }
+        return RT_OK;
     } else if (which >= 3 && which <= 7) {
         // the last layer's intermediate vectors: qkv, attention output, O
         // projection, GELU-gated FFN hidden, down projection

@@ -263,6 +263,15 @@ struct Job {
     int32_t pad;
     int64_t rows;
     int32_t tile_split;  // 1: each CTA takes whole tiles, its warps split them (combined by cta_combine)
+    // Column split (0 or 1: none; needs `wt`).  With kparts = P the job is P
+    // stacked GEMVs over consecutive column ranges of nseg segments each:
+    // virtual tile p * ptiles + t covers rows 16t..16t+15 of the matrix over
+    // x segments [p * nseg, (p + 1) * nseg), `rows` counts P * 16 * ptiles
+    // virtual rows, and y holds P partial vectors [P][16 * ptiles] that the
+    // consumer adds (src_parts).
+    int32_t kparts;
+    int32_t ptiles;
+    int32_t src_parts;  // residual-update prologue: src is the sum of this many vectors of K (0 or 1: one)
     // prologue
     const float* x;
     const float* src;
@@ -530,8 +539,8 @@ template <int KIND, int PRO>
 __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uint32_t pbar_phase) {
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int lane = tid & 31;
-    const int K = a.K, nseg = a.nseg;
-    const int Kp = nseg * seg_cols(KIND);
+    const int K = a.K;
+    const int Kp = (K + seg_cols(KIND) - 1) / seg_cols(KIND) * seg_cols(KIND);
     const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
     if constexpr (PRO == kProPlain) {
         planes_from_global<KIND>(a.x, K, Kp, pstride, S);
@@ -544,7 +553,11 @@ __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uin
             float* sub = S.sub;
 #pragma unroll 2
             for (int c = tid * 4; c < K; c += nthr * 4) {
-                const float4 s4 = *reinterpret_cast<const float4*>(a.src + c);
+                float4 s4 = *reinterpret_cast<const float4*>(a.src + c);
+                for (int q = 1; q < a.src_parts; ++q) {  // the column parts of a split GEMV, in part order
+                    const float4 t4 = *reinterpret_cast<const float4*>(a.src + static_cast<size_t>(q) * K + c);
+                    s4 = make_float4(s4.x + t4.x, s4.y + t4.y, s4.z + t4.z, s4.w + t4.w);
+                }
                 const float4 r4 = *reinterpret_cast<const float4*>(a.resid_in + c);
                 *reinterpret_cast<float4*>(sub + c) = s4;
                 *reinterpret_cast<float4*>(S.xs + c) = r4;
@@ -607,7 +620,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int nseg = a.nseg;
-    const int Kp = nseg * seg_cols(KIND);
+    const int Kp = (a.K + seg_cols(KIND) - 1) / seg_cols(KIND) * seg_cols(KIND);
     const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
     const Share sh = warp_share(a, st.cta, st.ncta, st.warp, st.nw);
     const uint32_t u_begin = sh.s;
@@ -645,6 +658,9 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     uint32_t tile = u_begin / nseg;
     int seg = static_cast<int>(u_begin - tile * nseg);
     const uint32_t first_tile = tile;
+    // first segment of x for the current tile (column-split jobs)
+    auto part_base = [&](uint32_t tl) { return a.kparts > 1 ? static_cast<int>(tl / a.ptiles) * nseg : 0; };
+    int xseg = part_base(tile) + seg;
     int pu = 0;  // units of the current tile piece
     const int upc = a.wt ? kTileMajorUnitsPerCopy : 1;
     int in_copy = 0, uic = 0;  // units left in / consumed from the current copy
@@ -659,11 +675,11 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
         if constexpr (KIND == kQ4K) {
             // B fragments: planes 0/1 of sub-blocks q and q+4 (this lane's column
             // pair) and, for even g, plane 2.
-            const uint8_t* pb = S.planes + seg * 256 + q * 64 + t * 16;
+            const uint8_t* pb = S.planes + xseg * 256 + q * 64 + t * 16;
             const uint4 B01 = lds128(pb + (g & 1) * pstride);
             const uint4 B2 = (g & 1) ? make_uint4(0u, 0u, 0u, 0u) : lds128(pb + 2 * pstride);
             const uint4 h0 = lds128(ub + g * kQ4KPitch), h1 = lds128(ub + (g + 8) * kQ4KPitch);
-            const float2 xa = S.xsx[seg * 8 + t], xb = S.xsx[seg * 8 + t + 4];
+            const float2 xa = S.xsx[xseg * 8 + t], xb = S.xsx[xseg * 8 + t + 4];
             int c01[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, c2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -707,7 +723,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
             }
         } else {
             // BF16: lanes g < 3 feed B column g (plane g); the rest feed zeros.
-            const uint8_t* pb = S.planes + (g < 3 ? g : 0) * pstride + seg * (kBF16SegCols * 2) + t * 8;
+            const uint8_t* pb = S.planes + (g < 3 ? g : 0) * pstride + xseg * (kBF16SegCols * 2) + t * 8;
             float c[4][4];
 #pragma unroll
             for (int k = 0; k < 4; ++k)
@@ -738,6 +754,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
                 st.ph ^= 1u;
             }
         }
+        ++xseg;
         const bool tile_end = ++seg == nseg;
         if (tile_end || i == n - 1) {
             // Row sums of this piece: quad reduction, then lane L < 16 takes row L.
@@ -805,6 +822,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
             if (tile_end) {
                 seg = 0;
                 ++tile;
+                xseg = part_base(tile);
             }
         }
     }
