@@ -44,7 +44,7 @@
 using rt::fail;
 
 // Column parts of the step kernel's down projection (a divisor of FFN / 256).
-constexpr int kMaxDownParts = 4;
+constexpr int kMaxDownParts = rt::gcore::kMaxSrcParts;
 
 struct rt_dec {
     rt_ctx* ctx = nullptr;

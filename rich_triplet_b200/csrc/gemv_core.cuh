@@ -250,6 +250,9 @@ struct Split {
 // Q4_K units per copy when W is stored tile-major (see Job::wt).
 constexpr int kTileMajorUnitsPerCopy = 2;
 
+// Partial vectors a residual-update prologue can add (Job::src_parts).
+constexpr int kMaxSrcParts = 4;
+
 // One GEMV as the kernels see it.
 struct Job {
     const void* tmap;   // CUtensorMap of W (parameter or global memory), row-major W
@@ -271,7 +274,8 @@ struct Job {
     // consumer adds (src_parts).
     int32_t kparts;
     int32_t ptiles;
-    int32_t src_parts;  // residual-update prologue: src is the sum of this many vectors of K (0 or 1: one)
+    int32_t src_parts;  // residual-update prologue: src is the sum of this many vectors of K (0 or 1: one;
+                        // at most kMaxSrcParts)
     // prologue
     const float* x;
     const float* src;
@@ -553,11 +557,16 @@ __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uin
             float* sub = S.sub;
 #pragma unroll 2
             for (int c = tid * 4; c < K; c += nthr * 4) {
-                float4 s4 = *reinterpret_cast<const float4*>(a.src + c);
-                for (int q = 1; q < a.src_parts; ++q) {  // the column parts of a split GEMV, in part order
-                    const float4 t4 = *reinterpret_cast<const float4*>(a.src + static_cast<size_t>(q) * K + c);
-                    s4 = make_float4(s4.x + t4.x, s4.y + t4.y, s4.z + t4.z, s4.w + t4.w);
-                }
+                // the column parts of a split GEMV, added in part order (loads all in flight)
+                float4 t4[kMaxSrcParts];
+#pragma unroll
+                for (int q = 0; q < kMaxSrcParts; ++q)
+                    t4[q] = q == 0 || q < a.src_parts ? *reinterpret_cast<const float4*>(a.src + static_cast<size_t>(q) * K + c)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                float4 s4 = t4[0];
+#pragma unroll
+                for (int q = 1; q < kMaxSrcParts; ++q)
+                    if (q < a.src_parts) s4 = make_float4(s4.x + t4[q].x, s4.y + t4[q].y, s4.z + t4[q].z, s4.w + t4[q].w);
                 const float4 r4 = *reinterpret_cast<const float4*>(a.resid_in + c);
                 *reinterpret_cast<float4*>(sub + c) = s4;
                 *reinterpret_cast<float4*>(S.xs + c) = r4;
