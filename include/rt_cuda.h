@@ -127,6 +127,15 @@ int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags
 int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int cols, const float* x_dev, float* y_dev,
                                int32_t* token_dev, void* stream, char* errbuf, size_t errlen);
 
+/* C[m, N] = A[m, K] . dequant(W)^T for a Q4_K weight W [N, K] (K a multiple
+ * of 256): the prompt-length GEMM of prefill.  Replaces Q4KMat::matmul_q4k_t
+ * (src/autograd2.rs:1437-1457) and matmul_q4k_t_exact (:1507-1625).  A is bf16
+ * row-major [m, K] (uint16 bits), C is f32 row-major [m, N].  flags RT_HOST:
+ * host A and C, the call copies and waits; RT_DEVICE: device pointers (16-byte
+ * aligned), enqueued on the context stream.  The weights are rounded to bf16
+ * for the tensor cores (relative error <= 2^-9 per weight). */
+int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags);
+
 /* GEMV throughput measurement (no counterpart in the reference, whose GEMV
  * test times nothing).  Captures one CUDA graph of `launches` GEMVs of the
  * same shape, launch i reading ws[i % nw] (a rotation over several weight

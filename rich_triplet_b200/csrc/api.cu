@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "convert.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 
 #include "rt_internal.h"
@@ -91,6 +92,7 @@ int rt_init(int device, rt_ctx** out) {
     }
     cudaMemset(ctx->d_err, 0, sizeof(int) * 4);
     rt::gemv_prepare();
+    if (rt::gemm_q4k_prepare() != cudaSuccess) cudaGetLastError();  // a launch then reports the failure
     *out = ctx;
     return RT_OK;
 }
@@ -280,6 +282,42 @@ int rt_gemv_q4k(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags)
 
 int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags) {
     return gemv_common(ctx, w, x, y, flags, rt::kBF16);
+}
+
+int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags) {
+    if (!ctx || !w || !a || !c) return fail(ctx, RT_E_INVAL, "rt_gemm_q4k: null argument");
+    if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "rt_gemm_q4k: flags must be RT_HOST or RT_DEVICE");
+    if (w->fmt != RT_FMT_Q4K) return fail(ctx, RT_E_FORMAT, "rt_gemm_q4k: weight format %d is not Q4_K", w->fmt);
+    const int64_t n = w->rows;
+    const int k = static_cast<int>(w->cols);
+    const rt::GemmPlan p = rt::gemm_q4k_plan(m, n, k);
+    if (p.bm == 0) return fail(ctx, RT_E_SHAPE, "rt_gemm_q4k: no launch geometry for M %lld, N %lld, K %d",
+                               static_cast<long long>(m), static_cast<long long>(n), k);
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const void* da = a;
+    float* dc = c;
+    const size_t a_bytes = static_cast<size_t>(m) * k * 2;
+    if (flags == RT_DEVICE) {
+        if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(c) & 15))
+            return fail(ctx, RT_E_INVAL, "rt_gemm_q4k: device A and C must be 16-byte aligned");
+    } else {
+        const size_t a_floats = (a_bytes + 255) / 256 * 64;  // C starts 256-byte aligned
+        int rc = ensure_scratch(ctx, a_floats + static_cast<size_t>(m) * n);
+        if (rc != RT_OK) return rc;
+        da = ctx->scratch;
+        dc = ctx->scratch + a_floats;
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(const_cast<void*>(da), a, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
+    }
+    CUtensorMap tm_a, tm_w;
+    if (!rt::gemm_q4k_tmaps(da, m, w->d, n, k, &tm_a, &tm_w))
+        return fail(ctx, RT_E_CUDA, "rt_gemm_q4k: TMA descriptor rejected");
+    RT_CHECK_CUDA(ctx, rt::gemm_q4k_launch(tm_a, tm_w, dc, m, n, k, p, ctx->d_err, ctx->stream));
+    if (flags == RT_HOST) {
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(c, dc, sizeof(float) * static_cast<size_t>(m) * n, cudaMemcpyDeviceToHost,
+                                           ctx->stream));
+        return rt_sync(ctx);
+    }
+    return RT_OK;
 }
 
 int rt_gemv_bench(rt_ctx* ctx, int fmt, const rt_w* const* ws, int nw, const float* x, float* y, int launches,

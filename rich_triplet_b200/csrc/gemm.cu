@@ -1,0 +1,431 @@
+// gemm.cu -- Q4_K prefill GEMM on the tcgen05 tensor cores.
+//
+// C[M, N] = A[M, K] . dequant(W[N, K])^T, A bf16, W Q4_K, f32 accumulate
+// (Q4KMat::matmul_q4k_t, src/autograd2.rs:1437-1457).
+//
+// One CTA computes a 128 x 128 tile of C; K advances in blocks of 64 columns
+// (one 128-byte swizzle row of bf16).  Warp roles:
+//   warp 0, lane 0   TMA producer: the A tile of each K-block (2-D tensor
+//                    copy, 128-byte swizzle) and, once per Q4_K super-block
+//                    (four K-blocks), the 128 raw 144-byte blocks of W
+//   warp 1, lane 0   MMA issuer: four tcgen05.mma (M128 N128 K16, bf16 in,
+//                    f32 accumulator in tensor memory) per K-block, then a
+//                    tcgen05.commit that frees the stage
+//   warps 2..9       dequantisers: w = d*sc*q - dmin*m (the Q4_K block
+//                    format, src/autograd2.rs:1003-1085) rounded to bf16 and
+//                    stored in the swizzled K-major layout the MMA reads;
+//                    then warps 2..5 move the accumulator tensor memory ->
+//                    registers -> C
+// Every mbarrier wait gives up after a second; a CTA that gives up records kErrMbarTimeout,
+// waits (bounded) for its own copies and MMAs in flight, frees its tensor
+// memory and returns.
+//
+// Precision: the MMA takes both operands in one type, and A is bf16, so each
+// dequantised weight (computed in f32 in the reference's order) is rounded to
+// bf16 (relative error <= 2^-9; about 1.6e-3 relative L2 on the product).  The
+// result is the product with those bf16 weights up to f32 summation order.
+#include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace rt {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kStages = 4;              // A / B tile ring
+constexpr int kRawStages = 3;           // raw W super-block ring
+constexpr int kBlockBytes = 144;        // one Q4_K super-block (256 columns) of one row
+constexpr int kKBPerBlock = 256 / kBK;  // K-blocks per super-block
+constexpr int kATile = kBM * kBK * 2;   // 16 KB
+constexpr int kBTile = kBN * kBK * 2;   // 16 KB
+constexpr int kRawTile = kBN * kBlockBytes;
+constexpr int kDeqWarps = 8;            // two threads per W row of the tile
+constexpr int kThreads = (2 + kDeqWarps) * 32;
+constexpr int kTmemCols = kBN;          // f32 accumulator: 128 lanes x 128 columns
+
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kATile;
+constexpr int kOffRaw = kOffB + kStages * kBTile;
+constexpr int kOffBar = kOffRaw + kRawStages * kRawTile;
+constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + slack for the 1024-byte alignment of the tiles
+static_assert(kOffB % 1024 == 0 && kOffRaw % 1024 == 0 && kRawTile % 128 == 0, "tile alignment");
+
+// Instruction descriptor (kind::f16): f32 accumulator, bf16 A and B, both
+// K-major, N = 128, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+                            (static_cast<uint32_t>(kBM >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major tile of 64-element (128-byte)
+// bf16 rows in the 128-byte swizzle: 8-row groups 1024 bytes apart (stride
+// byte offset), descriptor version 1, layout type 2.  `addr` is the start of
+// the K16 slice (tile base + 32 bytes per slice; the tile base is 1024-aligned).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return static_cast<uint64_t>((addr & 0x3FFFFu) >> 4) | (uint64_t{1} << 16) | (uint64_t{1024 >> 4} << 32) |
+           (uint64_t{1} << 46) | (uint64_t{2} << 61);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 2-D tensor copy without a cache hint, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 32 consecutive f32 columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_128(const void* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_u32(p)));
+    return v;
+}
+
+__device__ __forceinline__ void st_shared_128(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Byte i of `x` (a value below 16) as a float: 2^23 + q has q in its low bits.
+__device__ __forceinline__ float nib_to_float(uint32_t x, uint32_t i) {
+    return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u | i)) - 8388608.0f;
+}
+
+// Eight weights w = d1 * q - m1 (two roundings, the order of
+// Q4KMat::dequantize_row_into, src/autograd2.rs:1326-1366) from the bytes of w0
+// and w1 (one q in each byte), as four bf16 pairs.
+__device__ __forceinline__ float deq(float d1, float q, float m1) { return __fsub_rn(__fmul_rn(d1, q), m1); }
+__device__ __forceinline__ void dequant8(uint32_t w0, uint32_t w1, float d1, float m1, uint32_t (&out)[4]) {
+    out[0] = pack_bf16(deq(d1, nib_to_float(w0, 0), m1), deq(d1, nib_to_float(w0, 1), m1));
+    out[1] = pack_bf16(deq(d1, nib_to_float(w0, 2), m1), deq(d1, nib_to_float(w0, 3), m1));
+    out[2] = pack_bf16(deq(d1, nib_to_float(w1, 0), m1), deq(d1, nib_to_float(w1, 1), m1));
+    out[3] = pack_bf16(deq(d1, nib_to_float(w1, 2), m1), deq(d1, nib_to_float(w1, 3), m1));
+}
+
+// Wait for phase `parity` of `bar`, giving up after one second (globaltimer):
+// a CTA that stalls ends within seconds, with its error recorded.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity) {
+    const uint32_t addr = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((it & 63u) == 0u) {
+            uint64_t t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (it == 0) t0 = t;
+            else if (t - t0 > 1000000000ull) return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void fail(int* abort_flag, int* err) {
+    atomicExch(abort_flag, 1);
+    if (err) atomicExch(err, kErrMbarTimeout);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                    float* __restrict__ c, int64_t M, int64_t N, int K, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+    uint8_t* sA = sm + kOffA;
+    uint8_t* sB = sm + kOffB;
+    uint8_t* sRaw = sm + kOffRaw;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint64_t* a_full = bars;
+    uint64_t* b_full = a_full + kStages;
+    uint64_t* empty = b_full + kStages;
+    uint64_t* raw_full = empty + kStages;
+    uint64_t* raw_empty = raw_full + kRawStages;
+    uint64_t* tmem_full = raw_empty + kRawStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffMisc);
+    int* abort_flag = reinterpret_cast<int*>(sm + kOffMisc + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkb = K / kBK;
+    const int m0 = static_cast<int>(blockIdx.y) * kBM, n0 = static_cast<int>(blockIdx.x) * kBN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&a_full[s], 1);
+            mbar_init(&b_full[s], kDeqWarps);
+            mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < kRawStages; ++r) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_empty[r], kDeqWarps);
+        }
+        mbar_init(tmem_full, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer ----
+            int a_issued[kStages] = {0, 0, 0, 0}, raw_issued[kRawStages] = {0, 0, 0};
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+                const int s = kb % kStages, sb = kb / kKBPerBlock;
+                if (kb % kKBPerBlock == 0) {
+                    const int r = sb % kRawStages;
+                    if (sb >= kRawStages && !wait_phase(&raw_empty[r], static_cast<uint32_t>(sb / kRawStages - 1) & 1u)) {
+                        fail(abort_flag, err);
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&raw_full[r], kRawTile);
+                    tma_load_2d(sRaw + r * kRawTile, &tm_w, sb * (kBlockBytes / 8), n0, &raw_full[r]);
+                    ++raw_issued[r];
+                }
+                if (kb >= kStages && !wait_phase(&empty[s], static_cast<uint32_t>(kb / kStages - 1) & 1u)) {
+                    fail(abort_flag, err);
+                    break;
+                }
+                mbar_arrive_expect_tx(&a_full[s], kATile);
+                tma_load_2d(sA + s * kATile, &tm_a, kb * kBK, m0, &a_full[s]);
+                ++a_issued[s];
+            }
+            // No copy of this CTA may still be landing when it exits.
+            for (int s = 0; s < kStages; ++s)
+                if (a_issued[s]) (void)wait_phase(&a_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
+            for (int r = 0; r < kRawStages; ++r)
+                if (raw_issued[r]) (void)wait_phase(&raw_full[r], static_cast<uint32_t>(raw_issued[r] - 1) & 1u);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer ----
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % kStages;
+                const uint32_t par = static_cast<uint32_t>(kb / kStages) & 1u;
+                if (!wait_phase(&a_full[s], par) || !wait_phase(&b_full[s], par)) {
+                    fail(abort_flag, err);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + s * kATile), b_addr = smem_u32(sB + s * kBTile);
+#pragma unroll
+                for (int k16 = 0; k16 < kBK / 16; ++k16)
+                    umma_bf16(tmem, sw128_desc(a_addr + 32 * k16), sw128_desc(b_addr + 32 * k16), (kb | k16) != 0);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(tmem_full);  // also on failure: arrives once every MMA above has completed
+        }
+    } else {
+        // ---- dequantisers: thread (row n of the tile, half h of each 64-column K-block) ----
+        const int d = threadIdx.x - 64;
+        const int n = d >> 1, h = d & 1;
+        for (int kb = 0; kb < nkb; ++kb) {
+            if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+            const int s = kb % kStages, sb = kb / kKBPerBlock, ch = kb % kKBPerBlock, r = sb % kRawStages;
+            if (ch == 0 && !wait_phase(&raw_full[r], static_cast<uint32_t>(sb / kRawStages) & 1u)) {
+                fail(abort_flag, err);
+                break;
+            }
+            if (kb >= kStages && !wait_phase(&empty[s], static_cast<uint32_t>(kb / kStages - 1) & 1u)) {
+                fail(abort_flag, err);
+                break;
+            }
+            const uint8_t* row = sRaw + r * kRawTile + n * kBlockBytes;
+            const uint4 hdr = ld_shared_128(row);  // d, dmin, 12 bytes of scales/mins
+            const uint4 qs = ld_shared_128(row + 16 + 32 * ch + 16 * h);
+            const float dd = f16_bits_to_f32(hdr.x & 0xFFFFu), dmin = f16_bits_to_f32(hdr.x >> 16);
+            // scale_min of sub-blocks 2ch (low nibbles) and 2ch + 1 (high nibbles)
+            // (Q4KMat::scale_min, src/autograd2.rs:1075-1085)
+            auto scb = [&](int b) -> uint32_t {
+                const uint32_t wd = b < 4 ? hdr.y : (b < 8 ? hdr.z : hdr.w);
+                return (wd >> (8 * (b & 3))) & 0xFFu;
+            };
+            auto scale_min = [&](int j, float& d1, float& m1) {
+                uint32_t sc, mn;
+                if (j < 4) {
+                    sc = scb(j) & 63u;
+                    mn = scb(j + 4) & 63u;
+                } else {
+                    sc = (scb(j + 4) & 0xFu) | ((scb(j - 4) >> 6) << 4);
+                    mn = (scb(j + 4) >> 4) | ((scb(j) >> 6) << 4);
+                }
+                d1 = __fmul_rn(dd, static_cast<float>(sc));
+                m1 = __fmul_rn(dmin, static_cast<float>(mn));
+            };
+            float d_lo, m_lo, d_hi, m_hi;
+            scale_min(2 * ch, d_lo, m_lo);
+            scale_min(2 * ch + 1, d_hi, m_hi);
+            const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
+            uint8_t* tile = sB + s * kBTile + (n >> 3) * 1024 + (n & 7) * 128;
+            const int sw = n & 7;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {  // 0: low nibbles (columns 16h..), 1: high (32 + 16h..)
+                const uint32_t mask_shift = half ? 4u : 0u;
+                const float d1 = half ? d_hi : d_lo, m1 = half ? m_hi : m_lo;
+#pragma unroll
+                for (int part = 0; part < 2; ++part) {  // 8 columns per 16-byte chunk
+                    uint32_t o[4];
+                    dequant8((q[2 * part] >> mask_shift) & 0x0F0F0F0Fu, (q[2 * part + 1] >> mask_shift) & 0x0F0F0F0Fu, d1,
+                             m1, o);
+                    const int chunk = half * 4 + 2 * h + part;  // 16-byte chunk of the 128-byte row
+                    st_shared_128(tile + ((chunk ^ sw) << 4), o[0], o[1], o[2], o[3]);
+                }
+            }
+            fence_proxy_async_smem();  // the MMA (async proxy) reads these stores; the raw reads precede the TMA refill
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&b_full[s]);
+                if (ch == kKBPerBlock - 1) mbar_arrive(&raw_empty[r]);
+            }
+        }
+        // ---- epilogue: warps 2..5 own tensor-memory lanes 32 (warp % 4) .. +31 ----
+        if (warp < 6) {
+            const int quad = warp & 3;
+            const bool ok = wait_phase(tmem_full, 0u);
+            if (!ok) fail(abort_flag, err);
+            if (ok && !*reinterpret_cast<volatile int*>(abort_flag)) {
+                tc_fence_after();
+                const int64_t rowi = static_cast<int64_t>(m0) + 32 * quad + lane;
+                float* crow = c + rowi * N;
+                for (int cc = 0; cc < kBN / 32; ++cc) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(32 * cc), v);
+                    const int64_t col0 = n0 + 32 * cc;
+                    if (rowi < M) {
+                        if (col0 + 32 <= N && (N & 3) == 0) {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                *reinterpret_cast<float4*>(crow + col0 + 4 * i) =
+                                    make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                                __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                        } else {
+                            for (int i = 0; i < 32; ++i)
+                                if (col0 + i < N) crow[col0 + i] = __uint_as_float(v[i]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // ---- teardown: every tensor-memory access done, then warp 0 frees it ----
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+}  // namespace
+
+GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k) {
+    GemmPlan p;
+    if (m <= 0 || n <= 0 || k <= 0 || k % 256 != 0) return p;
+    const int64_t gx = (n + kBN - 1) / kBN, gy = (m + kBM - 1) / kBM;
+    if (gx > 0x7FFFFFFF || gy > 65535 || m > 0x7FFFFFFF || n > 0x7FFFFFFF) return p;
+    p.bm = kBM;
+    p.bn = kBN;
+    p.grid = dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+    p.smem = kSmemBytes;
+    return p;
+}
+
+cudaError_t gemm_q4k_prepare() {
+    return cudaFuncSetAttribute(gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+}
+
+bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, CUtensorMap* tm_a, CUtensorMap* tm_w) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn) {
+            cudaGetLastError();
+            return false;
+        }
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint32_t estr[2] = {1, 1};
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+        const cuuint32_t box[2] = {kBK, kBM};
+        if (encode(tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    {
+        const uint64_t row_bytes = static_cast<uint64_t>(k / 256) * kBlockBytes;
+        const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(n)};
+        const cuuint64_t strides[1] = {row_bytes};
+        const cuuint32_t box[2] = {kBlockBytes / 8, kBN};
+        if (encode(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
+}
+
+cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, float* c, int64_t m, int64_t n, int k,
+                            const GemmPlan& p, int* err, cudaStream_t s) {
+    if (p.bm == 0) return cudaErrorInvalidValue;
+    gemm_q4k_kernel<<<p.grid, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, err);
+    return cudaGetLastError();
+}
+
+}  // namespace rt

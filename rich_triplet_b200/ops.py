@@ -149,6 +149,32 @@ def cuda_gemv_bf16_t(a, bf16: MatBf16):
     return y.reshape(1, -1)
 
 
+def bf16_bits(a):
+    """f32 -> bf16 bits (uint16), round to nearest even."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
+
+
+def cuda_matmul_q4k_t(a, q4k: Q4KMat):
+    """C[M, N] = A[M, K] @ dequant(Q4K[N, K])^T on the tensor cores, f32
+    accumulation (Q4KMat::matmul_q4k_t, src/autograd2.rs:1437-1457).  `a` is
+    bf16 bits (uint16) or f32, which is rounded to bf16 first."""
+    ctx = default_context()
+    a = np.ascontiguousarray(a)
+    if a.ndim != 2 or a.shape[1] != q4k.cols:
+        raise ValueError(f"cuda_matmul_q4k_t: a shape {a.shape} does not match weight cols {q4k.cols}")
+    bits = a if a.dtype == np.uint16 else bf16_bits(a)
+    w = _cached_weight(ctx, RT_FMT_Q4K, q4k.blocks, q4k.rows, q4k.cols)
+    c = np.empty((a.shape[0], q4k.rows), dtype=np.float32)
+    check(lib().rt_gemm_q4k(ctx.h, w.h, bits.ctypes.data, a.shape[0], c.ctypes.data, RT_HOST), ctx.h)
+    return c
+
+
+def gemm_device(ctx, w: DeviceWeight, a_ptr, m, c_ptr):
+    """Enqueue C[m, N] = A[m, K] @ dequant(W)^T on device pointers (A bf16)."""
+    check(lib().rt_gemm_q4k(ctx.h, w.h, a_ptr, m, c_ptr, RT_DEVICE), ctx.h)
+
+
 def gemv_device(ctx, w: DeviceWeight, x_ptr, y_ptr):
     """Enqueue one GEMV on device pointers (no synchronisation)."""
     fn = lib().rt_gemv_q4k if w.fmt == RT_FMT_Q4K else lib().rt_gemv_bf16
