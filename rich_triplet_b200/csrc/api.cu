@@ -290,7 +290,7 @@ int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
     if (w->fmt != RT_FMT_Q4K) return fail(ctx, RT_E_FORMAT, "rt_gemm_q4k: weight format %d is not Q4_K", w->fmt);
     const int64_t n = w->rows;
     const int k = static_cast<int>(w->cols);
-    const rt::GemmPlan p = rt::gemm_q4k_plan(m, n, k);
+    const rt::GemmPlan p = rt::gemm_q4k_plan(m, n, k, ctx->num_sms);
     if (p.bm == 0) return fail(ctx, RT_E_SHAPE, "rt_gemm_q4k: no launch geometry for M %lld, N %lld, K %d",
                                static_cast<long long>(m), static_cast<long long>(n), k);
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
@@ -309,7 +309,7 @@ int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
         RT_CHECK_CUDA(ctx, cudaMemcpyAsync(const_cast<void*>(da), a, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
     }
     CUtensorMap tm_a, tm_w;
-    if (!rt::gemm_q4k_tmaps(da, m, w->d, n, k, &tm_a, &tm_w))
+    if (!rt::gemm_q4k_tmaps(da, m, w->d, n, k, p, &tm_a, &tm_w))
         return fail(ctx, RT_E_CUDA, "rt_gemm_q4k: TMA descriptor rejected");
     RT_CHECK_CUDA(ctx, rt::gemm_q4k_launch(tm_a, tm_w, dc, m, n, k, p, ctx->d_err, ctx->stream));
     if (flags == RT_HOST) {

@@ -3,18 +3,19 @@
 // C[M, N] = A[M, K] . dequant(W[N, K])^T, A bf16, W Q4_K, f32 accumulate
 // (Q4KMat::matmul_q4k_t, src/autograd2.rs:1437-1457).
 //
-// One CTA computes a 128 x 128 tile of C; K advances in blocks of 64 columns
-// (one 128-byte swizzle row of bf16).  Warp roles:
+// One CTA computes a 128 x 128 or 256 x 256 tile of C (one or two M128
+// accumulators in tensor memory); K advances in blocks of 64 columns (one
+// 128-byte swizzle row of bf16).  Warp roles:
 //   warp 0, lane 0   TMA producer: the A tile of each K-block (2-D tensor
 //                    copy, 128-byte swizzle) and, once per Q4_K super-block
 //                    (four K-blocks), the 128 raw 144-byte blocks of W
-//   warp 1, lane 0   MMA issuer: four tcgen05.mma (M128 N128 K16, bf16 in,
-//                    f32 accumulator in tensor memory) per K-block, then a
-//                    tcgen05.commit that frees the stage
+//   warp 1, lane 0   MMA issuer: four tcgen05.mma (M128 N128/256 K16, bf16
+//                    in, f32 accumulator in tensor memory) per K-block and
+//                    accumulator, then a tcgen05.commit that frees the stage
 //   warps 2..9       dequantisers: w = d*sc*q - dmin*m (the Q4_K block
 //                    format, src/autograd2.rs:1003-1085) rounded to bf16 and
 //                    stored in the swizzled K-major layout the MMA reads;
-//                    then warps 2..5 move the accumulator tensor memory ->
+//                    then they move the accumulators tensor memory ->
 //                    registers -> C
 // Every mbarrier wait gives up after a second; a CTA that gives up records kErrMbarTimeout,
 // waits (bounded) for its own copies and MMAs in flight, frees its tensor
@@ -25,6 +26,7 @@
 // bf16 (relative error <= 2^-9; about 1.6e-3 relative L2 on the product).  The
 // result is the product with those bf16 weights up to f32 summation order.
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -33,31 +35,40 @@ namespace rt {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;
-constexpr int kStages = 4;              // A / B tile ring
-constexpr int kRawStages = 3;           // raw W super-block ring
+constexpr int kBK = 64;                 // K-block: one 128-byte swizzle row of bf16
 constexpr int kBlockBytes = 144;        // one Q4_K super-block (256 columns) of one row
 constexpr int kKBPerBlock = 256 / kBK;  // K-blocks per super-block
-constexpr int kATile = kBM * kBK * 2;   // 16 KB
-constexpr int kBTile = kBN * kBK * 2;   // 16 KB
-constexpr int kRawTile = kBN * kBlockBytes;
-constexpr int kDeqWarps = 8;            // two threads per W row of the tile
+constexpr int kATile = 128 * kBK * 2;   // the A rows of one accumulator, 16 KB
+constexpr int kDeqWarps = 8;
 constexpr int kThreads = (2 + kDeqWarps) * 32;
-constexpr int kTmemCols = kBN;          // f32 accumulator: 128 lanes x 128 columns
 
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStages * kATile;
-constexpr int kOffRaw = kOffB + kStages * kBTile;
-constexpr int kOffBar = kOffRaw + kRawStages * kRawTile;
-constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
-constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + slack for the 1024-byte alignment of the tiles
-static_assert(kOffB % 1024 == 0 && kOffRaw % 1024 == 0 && kRawTile % 128 == 0, "tile alignment");
-
-// Instruction descriptor (kind::f16): f32 accumulator, bf16 A and B, both
-// K-major, N = 128, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
-                            (static_cast<uint32_t>(kBM >> 4) << 24);
+// Tile configuration: NACC accumulators of M128 x N=BN stacked along M (CTA
+// tile 128 NACC x BN; NACC * BN tensor-memory columns).  Larger tiles read A
+// fewer times (N / BN) and dequantise W fewer times (M / (128 NACC)).
+template <int NACC, int BN>
+struct Cfg {
+    static constexpr int kBM = 128 * NACC;
+    static constexpr int kBTile = BN * kBK * 2;
+    static constexpr int kRawTile = BN * kBlockBytes;
+    static constexpr int kStages = NACC * BN >= 512 ? 2 : 4;  // A / B ring
+    static constexpr int kRawStages = BN >= 256 ? 2 : 3;      // raw W super-block ring
+    static constexpr int kTmemCols = NACC * BN;
+    static constexpr int kTpr = 256 / BN;  // dequantiser threads per W row
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * NACC * kATile;
+    static constexpr int kOffRaw = kOffB + kStages * kBTile;
+    static constexpr int kOffBar = kOffRaw + kRawStages * kRawTile;
+    static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
+    static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+    static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + slack for the 1024-byte alignment of the tiles
+    // Instruction descriptor (kind::f16): f32 accumulator, bf16 A and B, both
+    // K-major, N = BN, M = 128.
+    static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                       (static_cast<uint32_t>(128 >> 4) << 24);
+    static_assert(kOffB % 1024 == 0 && kOffRaw % 1024 == 0 && kRawTile % 128 == 0, "tile alignment");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kTmemCols <= 512 && (BN == 128 || BN == 256), "tensor memory");
+};
 
 // Shared-memory matrix descriptor of a K-major tile of 64-element (128-byte)
 // bf16 rows in the 128-byte swizzle: 8-row groups 1024 bytes apart (stride
@@ -68,13 +79,13 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
            (uint64_t{1} << 46) | (uint64_t{2} << 61);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     const uint32_t z = 0;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-        ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
 }
 
 // Arrive on `bar` once every tcgen05 operation this thread issued has completed.
@@ -170,26 +181,29 @@ __device__ __forceinline__ void fail(int* abort_flag, int* err) {
     if (err) atomicExch(err, kErrMbarTimeout);
 }
 
+template <int NACC, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                     float* __restrict__ c, int64_t M, int64_t N, int K, int* err) {
+    using C = Cfg<NACC, BN>;
+    constexpr int kStages = C::kStages, kRawStages = C::kRawStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
-    uint8_t* sA = sm + kOffA;
-    uint8_t* sB = sm + kOffB;
-    uint8_t* sRaw = sm + kOffRaw;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint8_t* sA = sm + C::kOffA;
+    uint8_t* sB = sm + C::kOffB;
+    uint8_t* sRaw = sm + C::kOffRaw;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::kOffBar);
     uint64_t* a_full = bars;
     uint64_t* b_full = a_full + kStages;
     uint64_t* empty = b_full + kStages;
     uint64_t* raw_full = empty + kStages;
     uint64_t* raw_empty = raw_full + kRawStages;
     uint64_t* tmem_full = raw_empty + kRawStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kOffMisc);
-    int* abort_flag = reinterpret_cast<int*>(sm + kOffMisc + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffMisc);
+    int* abort_flag = reinterpret_cast<int*>(sm + C::kOffMisc + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkb = K / kBK;
-    const int m0 = static_cast<int>(blockIdx.y) * kBM, n0 = static_cast<int>(blockIdx.x) * kBN;
+    const int m0 = static_cast<int>(blockIdx.y) * C::kBM, n0 = static_cast<int>(blockIdx.x) * BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -208,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTmemCols)
+                     "r"(C::kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -220,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer ----
-            int a_issued[kStages] = {0, 0, 0, 0}, raw_issued[kRawStages] = {0, 0, 0};
+            int a_issued[kStages] = {}, raw_issued[kRawStages] = {};
             for (int kb = 0; kb < nkb; ++kb) {
                 if (*reinterpret_cast<volatile int*>(abort_flag)) break;
                 const int s = kb % kStages, sb = kb / kKBPerBlock;
@@ -230,16 +244,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         fail(abort_flag, err);
                         break;
                     }
-                    mbar_arrive_expect_tx(&raw_full[r], kRawTile);
-                    tma_load_2d(sRaw + r * kRawTile, &tm_w, sb * (kBlockBytes / 8), n0, &raw_full[r]);
+                    mbar_arrive_expect_tx(&raw_full[r], C::kRawTile);
+                    tma_load_2d(sRaw + r * C::kRawTile, &tm_w, sb * (kBlockBytes / 8), n0, &raw_full[r]);
                     ++raw_issued[r];
                 }
                 if (kb >= kStages && !wait_phase(&empty[s], static_cast<uint32_t>(kb / kStages - 1) & 1u)) {
                     fail(abort_flag, err);
                     break;
                 }
-                mbar_arrive_expect_tx(&a_full[s], kATile);
-                tma_load_2d(sA + s * kATile, &tm_a, kb * kBK, m0, &a_full[s]);
+                mbar_arrive_expect_tx(&a_full[s], NACC * kATile);
+#pragma unroll
+                for (int ac = 0; ac < NACC; ++ac)
+                    tma_load_2d(sA + (s * NACC + ac) * kATile, &tm_a, kb * kBK, m0 + 128 * ac, &a_full[s]);
                 ++a_issued[s];
             }
             // No copy of this CTA may still be landing when it exits.
@@ -250,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---- MMA issuer ----
+            // ---- MMA issuer: accumulator ac in tensor-memory columns [ac * BN, (ac + 1) * BN) ----
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kStages;
                 const uint32_t par = static_cast<uint32_t>(kb / kStages) & 1u;
@@ -259,18 +275,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(sA + s * kATile), b_addr = smem_u32(sB + s * kBTile);
+                const uint32_t b_addr = smem_u32(sB + s * C::kBTile);
 #pragma unroll
-                for (int k16 = 0; k16 < kBK / 16; ++k16)
-                    umma_bf16(tmem, sw128_desc(a_addr + 32 * k16), sw128_desc(b_addr + 32 * k16), (kb | k16) != 0);
+                for (int ac = 0; ac < NACC; ++ac) {
+                    const uint32_t a_addr = smem_u32(sA + (s * NACC + ac) * kATile);
+#pragma unroll
+                    for (int k16 = 0; k16 < kBK / 16; ++k16)
+                        umma_bf16(tmem + static_cast<uint32_t>(ac * BN), sw128_desc(a_addr + 32 * k16),
+                                  sw128_desc(b_addr + 32 * k16), C::kIdesc, (kb | k16) != 0);
+                }
                 umma_commit(&empty[s]);
             }
             umma_commit(tmem_full);  // also on failure: arrives once every MMA above has completed
         }
     } else {
-        // ---- dequantisers: thread (row n of the tile, half h of each 64-column K-block) ----
+        // ---- dequantisers: W row n of the tile; halves h0.. of each 64-column K-block ----
         const int d = threadIdx.x - 64;
-        const int n = d >> 1, h = d & 1;
+        const int n = d / C::kTpr;
+        const int h_first = C::kTpr == 2 ? (d & 1) : 0, h_count = C::kTpr == 2 ? 1 : 2;
         for (int kb = 0; kb < nkb; ++kb) {
             if (*reinterpret_cast<volatile int*>(abort_flag)) break;
             const int s = kb % kStages, sb = kb / kKBPerBlock, ch = kb % kKBPerBlock, r = sb % kRawStages;
@@ -282,9 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fail(abort_flag, err);
                 break;
             }
-            const uint8_t* row = sRaw + r * kRawTile + n * kBlockBytes;
+            const uint8_t* row = sRaw + r * C::kRawTile + n * kBlockBytes;
             const uint4 hdr = ld_shared_128(row);  // d, dmin, 12 bytes of scales/mins
-            const uint4 qs = ld_shared_128(row + 16 + 32 * ch + 16 * h);
             const float dd = f16_bits_to_f32(hdr.x & 0xFFFFu), dmin = f16_bits_to_f32(hdr.x >> 16);
             // scale_min of sub-blocks 2ch (low nibbles) and 2ch + 1 (high nibbles)
             // (Q4KMat::scale_min, src/autograd2.rs:1075-1085)
@@ -307,20 +328,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             float d_lo, m_lo, d_hi, m_hi;
             scale_min(2 * ch, d_lo, m_lo);
             scale_min(2 * ch + 1, d_hi, m_hi);
-            const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
-            uint8_t* tile = sB + s * kBTile + (n >> 3) * 1024 + (n & 7) * 128;
+            uint8_t* tile = sB + s * C::kBTile + (n >> 3) * 1024 + (n & 7) * 128;
             const int sw = n & 7;
+            for (int hh = 0; hh < h_count; ++hh) {
+                const int h = h_first + hh;
+                const uint4 qs = ld_shared_128(row + 16 + 32 * ch + 16 * h);
+                const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {  // 0: low nibbles (columns 16h..), 1: high (32 + 16h..)
-                const uint32_t mask_shift = half ? 4u : 0u;
-                const float d1 = half ? d_hi : d_lo, m1 = half ? m_hi : m_lo;
+                for (int half = 0; half < 2; ++half) {  // 0: low nibbles (columns 16h..), 1: high (32 + 16h..)
+                    const uint32_t mask_shift = half ? 4u : 0u;
+                    const float d1 = half ? d_hi : d_lo, m1 = half ? m_hi : m_lo;
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {  // 8 columns per 16-byte chunk
-                    uint32_t o[4];
-                    dequant8((q[2 * part] >> mask_shift) & 0x0F0F0F0Fu, (q[2 * part + 1] >> mask_shift) & 0x0F0F0F0Fu, d1,
-                             m1, o);
-                    const int chunk = half * 4 + 2 * h + part;  // 16-byte chunk of the 128-byte row
-                    st_shared_128(tile + ((chunk ^ sw) << 4), o[0], o[1], o[2], o[3]);
+                    for (int part = 0; part < 2; ++part) {  // 8 columns per 16-byte chunk
+                        uint32_t o[4];
+                        dequant8((q[2 * part] >> mask_shift) & 0x0F0F0F0Fu, (q[2 * part + 1] >> mask_shift) & 0x0F0F0F0Fu,
+                                 d1, m1, o);
+                        const int chunk = half * 4 + 2 * h + part;  // 16-byte chunk of the 128-byte row
+                        st_shared_128(tile + ((chunk ^ sw) << 4), o[0], o[1], o[2], o[3]);
+                    }
                 }
             }
             fence_proxy_async_smem();  // the MMA (async proxy) reads these stores; the raw reads precede the TMA refill
@@ -330,30 +355,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ch == kKBPerBlock - 1) mbar_arrive(&raw_empty[r]);
             }
         }
-        // ---- epilogue: warps 2..5 own tensor-memory lanes 32 (warp % 4) .. +31 ----
-        if (warp < 6) {
-            const int quad = warp & 3;
-            const bool ok = wait_phase(tmem_full, 0u);
-            if (!ok) fail(abort_flag, err);
-            if (ok && !*reinterpret_cast<volatile int*>(abort_flag)) {
-                tc_fence_after();
-                const int64_t rowi = static_cast<int64_t>(m0) + 32 * quad + lane;
-                float* crow = c + rowi * N;
-                for (int cc = 0; cc < kBN / 32; ++cc) {
-                    uint32_t v[32];
-                    tmem_ld32(tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(32 * cc), v);
-                    const int64_t col0 = n0 + 32 * cc;
-                    if (rowi < M) {
-                        if (col0 + 32 <= N && (N & 3) == 0) {
+        // ---- epilogue: warp w owns tensor-memory lanes 32 (w % 4) .. +31; the
+        // two warps of a lane quarter split the (accumulator, 32-column) chunks ----
+        const int quad = warp & 3, grp = (warp - 2) >> 2;
+        const bool ok = wait_phase(tmem_full, 0u);
+        if (!ok) fail(abort_flag, err);
+        if (ok && !*reinterpret_cast<volatile int*>(abort_flag)) {
+            tc_fence_after();
+            for (int item = grp; item < NACC * (BN / 32); item += 2) {
+                const int ac = item / (BN / 32), cc = item % (BN / 32);
+                uint32_t v[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(ac * BN + 32 * cc), v);
+                const int64_t rowi = static_cast<int64_t>(m0) + 128 * ac + 32 * quad + lane;
+                const int64_t col0 = n0 + 32 * cc;
+                if (rowi < M) {
+                    float* crow = c + rowi * N;
+                    if (col0 + 32 <= N && (N & 3) == 0) {
 #pragma unroll
-                            for (int i = 0; i < 8; ++i)
-                                *reinterpret_cast<float4*>(crow + col0 + 4 * i) =
-                                    make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                                __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-                        } else {
-                            for (int i = 0; i < 32; ++i)
-                                if (col0 + i < N) crow[col0 + i] = __uint_as_float(v[i]);
-                        }
+                        for (int i = 0; i < 8; ++i)
+                            *reinterpret_cast<float4*>(crow + col0 + 4 * i) =
+                                make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                            __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                    } else {
+                        for (int i = 0; i < 32; ++i)
+                            if (col0 + i < N) crow[col0 + i] = __uint_as_float(v[i]);
                     }
                 }
             }
@@ -364,29 +389,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
     }
 }
 
 }  // namespace
 
-GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k) {
+GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms) {
     GemmPlan p;
-    if (m <= 0 || n <= 0 || k <= 0 || k % 256 != 0) return p;
-    const int64_t gx = (n + kBN - 1) / kBN, gy = (m + kBM - 1) / kBM;
-    if (gx > 0x7FFFFFFF || gy > 65535 || m > 0x7FFFFFFF || n > 0x7FFFFFFF) return p;
-    p.bm = kBM;
-    p.bn = kBN;
+    if (m <= 0 || n <= 0 || k <= 0 || k % 256 != 0 || m > 0x7FFFFFFF || n > 0x7FFFFFFF) return p;
+    // The 256 x 256 tile streams A half as often and dequantises W half as
+    // often as the 128 x 128 tile, at about half the cost per FLOP (measured);
+    // estimated time: waves of CTAs x per-tile cost (2 units big, 1 small).
+    const int64_t small = ((m + 127) / 128) * ((n + 127) / 128), big = ((m + 255) / 256) * ((n + 255) / 256);
+    const int64_t sms = num_sms > 0 ? num_sms : 148;
+    bool use_big = ((big + sms - 1) / sms) * 2 <= (small + sms - 1) / sms;
+    // RT_GEMM_TILE=128 or 256 forces the tile (tests and tuning).
+    if (const char* t = getenv("RT_GEMM_TILE")) {
+        if (atoi(t) == 128) use_big = false;
+        else if (atoi(t) == 256) use_big = true;
+    }
+    p.bm = use_big ? 256 : 128;
+    p.bn = use_big ? 256 : 128;
+    const int64_t gx = (n + p.bn - 1) / p.bn, gy = (m + p.bm - 1) / p.bm;
+    if (gx > 0x7FFFFFFF || gy > 65535) return GemmPlan{};
     p.grid = dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
-    p.smem = kSmemBytes;
+    p.smem = use_big ? Cfg<2, 256>::kSmemBytes : Cfg<1, 128>::kSmemBytes;
     return p;
 }
 
 cudaError_t gemm_q4k_prepare() {
-    return cudaFuncSetAttribute(gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(gemm_q4k_kernel<1, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<1, 128>::kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_q4k_kernel<2, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg<2, 256>::kSmemBytes);
+    return e;
 }
 
-bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, CUtensorMap* tm_a, CUtensorMap* tm_w) {
+bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, const GemmPlan& p, CUtensorMap* tm_a,
+                    CUtensorMap* tm_w) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
         cudaDriverEntryPointQueryResult q;
@@ -402,7 +444,7 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, C
     {
         const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-        const cuuint32_t box[2] = {kBK, kBM};
+        const cuuint32_t box[2] = {kBK, 128};
         if (encode(tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -412,7 +454,7 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, C
         const uint64_t row_bytes = static_cast<uint64_t>(k / 256) * kBlockBytes;
         const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(n)};
         const cuuint64_t strides[1] = {row_bytes};
-        const cuuint32_t box[2] = {kBlockBytes / 8, kBN};
+        const cuuint32_t box[2] = {kBlockBytes / 8, static_cast<cuuint32_t>(p.bn)};
         if (encode(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -423,8 +465,9 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, C
 
 cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, float* c, int64_t m, int64_t n, int k,
                             const GemmPlan& p, int* err, cudaStream_t s) {
-    if (p.bm == 0) return cudaErrorInvalidValue;
-    gemm_q4k_kernel<<<p.grid, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, err);
+    if (p.bm == 256) gemm_q4k_kernel<2, 256><<<p.grid, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, err);
+    else if (p.bm == 128) gemm_q4k_kernel<1, 128><<<p.grid, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, err);
+    else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 

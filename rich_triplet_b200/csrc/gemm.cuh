@@ -19,12 +19,14 @@ struct GemmPlan {
     size_t smem = 0;
 };
 
-GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k);
+GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms);
 // Raise the kernel's shared-memory limit on the current device (outside capture).
 cudaError_t gemm_q4k_prepare();
-// Tensor maps of A (bf16 [m, k], 128-byte swizzled tiles) and of the raw Q4_K
-// rows of W ([n, k/256 blocks] of 144 bytes).  False if the driver refuses.
-bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, CUtensorMap* tm_a, CUtensorMap* tm_w);
+// Tensor maps of A (bf16 [m, k], 128-row 128-byte swizzled tiles) and of the
+// raw Q4_K rows of W ([n, k/256 blocks] of 144 bytes, p.bn rows per copy).
+// False if the driver refuses.
+bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, const GemmPlan& p, CUtensorMap* tm_a,
+                    CUtensorMap* tm_w);
 cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, float* c, int64_t m, int64_t n, int k,
                             const GemmPlan& p, int* err, cudaStream_t s);
 

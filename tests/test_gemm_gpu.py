@@ -49,11 +49,19 @@ def _check(orc, blocks, n, k, a_bits, c, row_tol=ROW_TOL):
     assert l2 <= L2_TOL, l2
 
 
+@pytest.fixture(params=["128", "256"])
+def tile(request, monkeypatch):
+    """Both CTA tiles (128 x 128 with one accumulator, 256 x 256 with two),
+    forced through RT_GEMM_TILE; the plan otherwise picks by grid size."""
+    monkeypatch.setenv("RT_GEMM_TILE", request.param)
+    return int(request.param)
+
+
 @pytest.mark.parametrize("m,n,k", [
     (1, 128, 256), (5, 256, 512), (128, 128, 256), (200, 300, 512),  # ragged M and N tiles
-    (130, 384, 2560), (64, 256, 10240),                               # hidden and FFN widths
+    (130, 384, 2560), (64, 256, 10240), (300, 600, 2048),             # hidden and FFN widths
 ])
-def test_gemm_q4k_vs_oracle(orc, m, n, k):
+def test_gemm_q4k_vs_oracle(orc, tile, m, n, k):
     blocks = synth_q4k(21, m * 3 + n + k, n, k)
     a = synth_normal_bf16(22, m + n, m * k).reshape(m, k)
     c = cuda_matmul_q4k_t(a, Q4KMat(n, k, blocks))
@@ -64,7 +72,7 @@ def test_gemm_q4k_vs_oracle(orc, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(512, 2560, 2560), (512, 2560, 2048), (256, 4096, 2560)])
-def test_gemm_q4k_config2_shapes(orc, m, n, k):
+def test_gemm_q4k_config2_shapes(orc, tile, m, n, k):
     # BASELINE config 2 shapes at the smaller M
     blocks = synth_q4k(31, n + k, n, k)
     a = synth_normal_bf16(32, m, m * k).reshape(m, k)
