@@ -317,25 +317,25 @@ def run_ours(args):
         from rich_triplet_b200.ops import DeviceWeight, gemm_device
         shapes = (("qkv", 2560, 4096), ("o", 2048, 2560), ("gate_up", 2560, 20480), ("down", 10240, 2560))
         for name, k, n in shapes:
-            w = DeviceWeight.upload(ctx, RT_FMT_Q4K, synth_q4k(args.seed, 9200 + n + k, n, k), n, k)
+            gw = DeviceWeight.upload(ctx, RT_FMT_Q4K, synth_q4k(args.seed, 9200 + n + k, n, k), n, k)
             for m in (512, 2048):
-                a = torch.from_numpy(synth_normal_bf16(args.seed, 9300 + m, m * k).view(np.int16)).cuda()
+                ga = torch.from_numpy(synth_normal_bf16(args.seed, 9300 + m, m * k).view(np.int16)).cuda()
                 cm = torch.empty((m, n), dtype=torch.float32, device="cuda")
                 torch.cuda.synchronize()
                 for _ in range(3):
-                    gemm_device(ctx, w, a.data_ptr(), m, cm.data_ptr())
+                    gemm_device(ctx, gw, ga.data_ptr(), m, cm.data_ptr())
                 ctx.sync()
                 reps = 5
                 e0.record(ext)
                 for _ in range(reps):
-                    gemm_device(ctx, w, a.data_ptr(), m, cm.data_ptr())
+                    gemm_device(ctx, gw, ga.data_ptr(), m, cm.data_ptr())
                 e1.record(ext)
                 e1.synchronize()
                 us = e0.elapsed_time(e1) * 1e3 / reps
                 tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
                 gemm2[f"{name}_M{m}_K{k}_N{n}"] = {"us": us, "tflops": tf, "frac": tf / tc_peak}
-                del a, cm
-            w.free()
+                del ga, cm
+            gw.free()
         gemm2["peak_tflops"] = tc_peak
         gemm2["method"] = "device time per GEMM (CUDA events, mean of 5 after 3 warm-up), A bf16 ~ N(0,1) resident"
 
