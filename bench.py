@@ -195,11 +195,12 @@ def run_ours(args):
 
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
     else:
         torch.cuda.set_device(0)
     device = torch.cuda.current_device()
 
+    from rich_triplet_b200 import dp
     from rich_triplet_b200.decode import CudaDecodeContext
     from rich_triplet_b200.model import Config4, synth_gemma3, synth_tokens
     from rich_triplet_b200.ops import Context
@@ -216,7 +217,9 @@ def run_ours(args):
     cap = PROMPT + SPAN
     dec = CudaDecodeContext(w, cap, ctx)
     ext = torch.cuda.ExternalStream(ctx.stream_ptr)
-    prompt = synth_tokens(args.seed, 100 + rank, PROMPT, cfg.vocab_size)
+    # one sequence per rank: the rank's share of `world` independent sequences
+    seq0, _ = dp.shard(world, world, rank)
+    prompt = synth_tokens(args.seed, dp.prompt_stream(seq0), PROMPT, cfg.vocab_size)
     last = dec.prefill(prompt)
     first = argmax_last(last)
 
@@ -247,11 +250,8 @@ def run_ours(args):
     ms = e0.elapsed_time(e1)
     barrier()
     clock_info = clocks.stop()
-    t = torch.tensor([ms], device="cuda")
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1e3)
+    ms_max = dp.max_over_ranks(ms, dist, device)
+    value = dp.job_rate(world * args.steps, ms_max)
 
     # ---- whole-step bytes (weights + KV read), for the step roofline ----
     H, D, NKV = cfg.hidden_size, cfg.head_dim, cfg.num_key_value_heads
