@@ -135,6 +135,10 @@ int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int cols, const 
  * aligned), enqueued on the context stream.  The weights are rounded to bf16
  * for the tensor cores (relative error <= 2^-9 per weight). */
 int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags);
+/* The same product for a BF16 weight W [N, K] (K a multiple of 256), such as
+ * the tied LM head over several sequences' final hidden states: replaces
+ * MatBf16::matmul_by_t with M > 1 (src/autograd2.rs:757-776, 954-1000). */
+int rt_gemm_bf16(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags);
 
 /* GEMV throughput measurement (no counterpart in the reference, whose GEMV
  * test times nothing).  Captures one CUDA graph of `launches` GEMVs of the

@@ -92,6 +92,7 @@ SIGNATURES = {
         [_vp, ctypes.c_int64, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_char_p, ctypes.c_size_t],
     ),
     "rt_gemm_q4k": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp, ctypes.c_int]),
+    "rt_gemm_bf16": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp, ctypes.c_int]),
     "rt_gemv_bench": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp), ctypes.c_int, _vp, _vp, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),
     "rt_convert_q4_0_to_q4k": (ctypes.c_int, [_vp, _vp, _i64, _i64, ctypes.c_int, _pp]),

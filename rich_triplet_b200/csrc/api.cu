@@ -272,6 +272,47 @@ int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags
     return RT_OK;
 }
 
+int gemm_common(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags, int fmt) {
+    if (!ctx || !w || !a || !c) return fail(ctx, RT_E_INVAL, "rt_gemm: null argument");
+    if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "rt_gemm: flags must be RT_HOST or RT_DEVICE");
+    if (w->fmt != fmt) return fail(ctx, RT_E_FORMAT, "rt_gemm: weight format %d, this entry point takes %d", w->fmt, fmt);
+    const int64_t n = w->rows;
+    const int k = static_cast<int>(w->cols);
+    const rt::GemmPlan p = rt::gemm_q4k_plan(m, n, k, ctx->num_sms, fmt == RT_FMT_BF16, true);
+    if (p.bm == 0) return fail(ctx, RT_E_SHAPE, "rt_gemm: no launch geometry for M %lld, N %lld, K %d",
+                               static_cast<long long>(m), static_cast<long long>(n), k);
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const size_t a_bytes = static_cast<size_t>(m) * k * 2;
+    if (flags == RT_DEVICE && ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(c) & 15)))
+        return fail(ctx, RT_E_INVAL, "rt_gemm: device A and C must be 16-byte aligned");
+    // scratch: [A (host calls)] [C (host calls)] [split partials], each 256-byte aligned
+    auto al = [](size_t floats) { return (floats + 63) / 64 * 64; };
+    const size_t a_floats = flags == RT_HOST ? al((a_bytes + 3) / 4) : 0;
+    const size_t c_floats = flags == RT_HOST ? al(static_cast<size_t>(m) * n) : 0;
+    const size_t part_floats = p.splits > 1 ? static_cast<size_t>(p.splits) * m * n : 0;
+    if (a_floats + c_floats + part_floats > 0) {
+        int rc = ensure_scratch(ctx, a_floats + c_floats + part_floats);
+        if (rc != RT_OK) return rc;
+    }
+    const void* da = flags == RT_HOST ? static_cast<const void*>(ctx->scratch) : a;
+    float* dc = flags == RT_HOST ? ctx->scratch + a_floats : c;
+    float* parts = ctx->scratch + a_floats + c_floats;
+    if (flags == RT_HOST)
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(const_cast<void*>(da), a, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
+    CUtensorMap tm_a, tm_w;
+    if (!rt::gemm_q4k_tmaps(da, m, w->d, n, k, p, &tm_a, &tm_w))
+        return fail(ctx, RT_E_CUDA, "rt_gemm: TMA descriptor rejected");
+    RT_CHECK_CUDA(ctx, rt::gemm_q4k_launch(tm_a, tm_w, p.splits > 1 ? parts : dc, m, n, k, p, ctx->d_err, ctx->stream));
+    if (p.splits > 1)
+        RT_CHECK_CUDA(ctx, rt::sum_parts_launch(parts, p.splits, static_cast<int64_t>(m) * n, dc, ctx->num_sms, ctx->stream));
+    if (flags == RT_HOST) {
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(c, dc, sizeof(float) * static_cast<size_t>(m) * n, cudaMemcpyDeviceToHost,
+                                           ctx->stream));
+        return rt_sync(ctx);
+    }
+    return RT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -285,39 +326,11 @@ int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags
 }
 
 int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags) {
-    if (!ctx || !w || !a || !c) return fail(ctx, RT_E_INVAL, "rt_gemm_q4k: null argument");
-    if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "rt_gemm_q4k: flags must be RT_HOST or RT_DEVICE");
-    if (w->fmt != RT_FMT_Q4K) return fail(ctx, RT_E_FORMAT, "rt_gemm_q4k: weight format %d is not Q4_K", w->fmt);
-    const int64_t n = w->rows;
-    const int k = static_cast<int>(w->cols);
-    const rt::GemmPlan p = rt::gemm_q4k_plan(m, n, k, ctx->num_sms);
-    if (p.bm == 0) return fail(ctx, RT_E_SHAPE, "rt_gemm_q4k: no launch geometry for M %lld, N %lld, K %d",
-                               static_cast<long long>(m), static_cast<long long>(n), k);
-    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
-    const void* da = a;
-    float* dc = c;
-    const size_t a_bytes = static_cast<size_t>(m) * k * 2;
-    if (flags == RT_DEVICE) {
-        if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(c) & 15))
-            return fail(ctx, RT_E_INVAL, "rt_gemm_q4k: device A and C must be 16-byte aligned");
-    } else {
-        const size_t a_floats = (a_bytes + 255) / 256 * 64;  // C starts 256-byte aligned
-        int rc = ensure_scratch(ctx, a_floats + static_cast<size_t>(m) * n);
-        if (rc != RT_OK) return rc;
-        da = ctx->scratch;
-        dc = ctx->scratch + a_floats;
-        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(const_cast<void*>(da), a, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
-    }
-    CUtensorMap tm_a, tm_w;
-    if (!rt::gemm_q4k_tmaps(da, m, w->d, n, k, p, &tm_a, &tm_w))
-        return fail(ctx, RT_E_CUDA, "rt_gemm_q4k: TMA descriptor rejected");
-    RT_CHECK_CUDA(ctx, rt::gemm_q4k_launch(tm_a, tm_w, dc, m, n, k, p, ctx->d_err, ctx->stream));
-    if (flags == RT_HOST) {
-        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(c, dc, sizeof(float) * static_cast<size_t>(m) * n, cudaMemcpyDeviceToHost,
-                                           ctx->stream));
-        return rt_sync(ctx);
-    }
-    return RT_OK;
+    return gemm_common(ctx, w, a, m, c, flags, RT_FMT_Q4K);
+}
+
+int rt_gemm_bf16(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags) {
+    return gemm_common(ctx, w, a, m, c, flags, RT_FMT_BF16);
 }
 
 int rt_gemv_bench(rt_ctx* ctx, int fmt, const rt_w* const* ws, int nw, const float* x, float* y, int launches,

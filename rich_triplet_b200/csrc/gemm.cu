@@ -28,6 +28,8 @@
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
 #include <stdlib.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm.cuh"
 
@@ -181,10 +183,13 @@ __device__ __forceinline__ void fail(int* abort_flag, int* err) {
     if (err) atomicExch(err, kErrMbarTimeout);
 }
 
-template <int NACC, int BN>
+// WB: W is bf16 [N, K] (copied by TMA into the B tiles; no dequantisation).
+// Split-K: CTA z of the grid's third dimension takes columns [z kps, (z+1) kps)
+// of K and writes its partial product to c + z M N.
+template <int NACC, int BN, bool WB>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                    float* __restrict__ c, int64_t M, int64_t N, int K, int* err) {
+                    float* __restrict__ c, int64_t M, int64_t N, int K, int kps, int* err) {
     using C = Cfg<NACC, BN>;
     constexpr int kStages = C::kStages, kRawStages = C::kRawStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -202,13 +207,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffMisc);
     int* abort_flag = reinterpret_cast<int*>(sm + C::kOffMisc + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nkb = K / kBK;
+    const int k0 = static_cast<int>(blockIdx.z) * kps;
+    const int nkb = (min(K, k0 + kps) - k0) / kBK;
+    c += static_cast<int64_t>(blockIdx.z) * M * N;
     const int m0 = static_cast<int>(blockIdx.y) * C::kBM, n0 = static_cast<int>(blockIdx.x) * BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&a_full[s], 1);
-            mbar_init(&b_full[s], kDeqWarps);
+            mbar_init(&b_full[s], WB ? 1 : kDeqWarps);
             mbar_init(&empty[s], 1);
         }
         for (int r = 0; r < kRawStages; ++r) {
@@ -238,14 +245,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kb = 0; kb < nkb; ++kb) {
                 if (*reinterpret_cast<volatile int*>(abort_flag)) break;
                 const int s = kb % kStages, sb = kb / kKBPerBlock;
-                if (kb % kKBPerBlock == 0) {
+                if (!WB && kb % kKBPerBlock == 0) {
                     const int r = sb % kRawStages;
                     if (sb >= kRawStages && !wait_phase(&raw_empty[r], static_cast<uint32_t>(sb / kRawStages - 1) & 1u)) {
                         fail(abort_flag, err);
                         break;
                     }
                     mbar_arrive_expect_tx(&raw_full[r], C::kRawTile);
-                    tma_load_2d(sRaw + r * C::kRawTile, &tm_w, sb * (kBlockBytes / 8), n0, &raw_full[r]);
+                    tma_load_2d(sRaw + r * C::kRawTile, &tm_w, (k0 / 256 + sb) * (kBlockBytes / 8), n0, &raw_full[r]);
                     ++raw_issued[r];
                 }
                 if (kb >= kStages && !wait_phase(&empty[s], static_cast<uint32_t>(kb / kStages - 1) & 1u)) {
@@ -255,12 +262,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(&a_full[s], NACC * kATile);
 #pragma unroll
                 for (int ac = 0; ac < NACC; ++ac)
-                    tma_load_2d(sA + (s * NACC + ac) * kATile, &tm_a, kb * kBK, m0 + 128 * ac, &a_full[s]);
+                    tma_load_2d(sA + (s * NACC + ac) * kATile, &tm_a, k0 + kb * kBK, m0 + 128 * ac, &a_full[s]);
+                if constexpr (WB) {
+                    mbar_arrive_expect_tx(&b_full[s], C::kBTile);
+                    tma_load_2d(sB + s * C::kBTile, &tm_w, k0 + kb * kBK, n0, &b_full[s]);
+                }
                 ++a_issued[s];
             }
             // No copy of this CTA may still be landing when it exits.
             for (int s = 0; s < kStages; ++s)
-                if (a_issued[s]) (void)wait_phase(&a_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
+                if (a_issued[s]) {
+                    (void)wait_phase(&a_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
+                    if (WB) (void)wait_phase(&b_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
+                }
             for (int r = 0; r < kRawStages; ++r)
                 if (raw_issued[r]) (void)wait_phase(&raw_full[r], static_cast<uint32_t>(raw_issued[r] - 1) & 1u);
         }
@@ -293,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d = threadIdx.x - 64;
         const int n = d / C::kTpr;
         const int h_first = C::kTpr == 2 ? (d & 1) : 0, h_count = C::kTpr == 2 ? 1 : 2;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = 0; kb < (WB ? 0 : nkb); ++kb) {
             if (*reinterpret_cast<volatile int*>(abort_flag)) break;
             const int s = kb % kStages, sb = kb / kKBPerBlock, ch = kb % kKBPerBlock, r = sb % kRawStages;
             if (ch == 0 && !wait_phase(&raw_full[r], static_cast<uint32_t>(sb / kRawStages) & 1u)) {
@@ -395,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms) {
+GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms, bool wbf16, bool allow_split) {
     GemmPlan p;
     if (m <= 0 || n <= 0 || k <= 0 || k % 256 != 0 || m > 0x7FFFFFFF || n > 0x7FFFFFFF) return p;
     // The 256 x 256 tile streams A half as often and dequantises W half as
@@ -411,19 +425,34 @@ GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms) {
     }
     p.bm = use_big ? 256 : 128;
     p.bn = use_big ? 256 : 128;
+    p.wbf16 = wbf16;
     const int64_t gx = (n + p.bn - 1) / p.bn, gy = (m + p.bm - 1) / p.bm;
     if (gx > 0x7FFFFFFF || gy > 65535) return GemmPlan{};
-    p.grid = dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+    // Split K (in whole 256-column super-blocks) while the tiles leave SMs idle.
+    const int nsb = k / 256;
+    // Split K only while the product is a weight stream (M <= 128): then
+    // filling the SMs pays (measured at M = 64: 101 -> 30 us for a 10240-column
+    // down projection); at larger M the partial products' traffic costs more.
+    int splits = 1;
+    if (allow_split && m <= 128) splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(std::min(nsb, 8), sms / (gx * gy))));
+    if (const char* t = getenv("RT_GEMM_SPLITS")) splits = std::max(1, std::min(nsb, atoi(t)));  // tests
+    const int per = (nsb + splits - 1) / splits;
+    p.kps = per * 256;
+    p.splits = (nsb + per - 1) / per;
+    p.grid = dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(p.splits));
     p.smem = use_big ? Cfg<2, 256>::kSmemBytes : Cfg<1, 128>::kSmemBytes;
     return p;
 }
 
 cudaError_t gemm_q4k_prepare() {
-    cudaError_t e = cudaFuncSetAttribute(gemm_q4k_kernel<1, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<1, 128>::kSmemBytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_q4k_kernel<2, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Cfg<2, 256>::kSmemBytes);
+    cudaError_t e = cudaSuccess;
+    auto set = [&](auto kernel, int bytes) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    };
+    set(gemm_q4k_kernel<1, 128, false>, Cfg<1, 128>::kSmemBytes);
+    set(gemm_q4k_kernel<2, 256, false>, Cfg<2, 256>::kSmemBytes);
+    set(gemm_q4k_kernel<1, 128, true>, Cfg<1, 128>::kSmemBytes);
+    set(gemm_q4k_kernel<2, 256, true>, Cfg<2, 256>::kSmemBytes);
     return e;
 }
 
@@ -441,33 +470,52 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, c
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
     const cuuint32_t estr[2] = {1, 1};
-    {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
+    auto bf16_map = [&](CUtensorMap* out, const void* base, int64_t rows, int box_rows) {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-        const cuuint32_t box[2] = {kBK, 128};
-        if (encode(tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    {
-        const uint64_t row_bytes = static_cast<uint64_t>(k / 256) * kBlockBytes;
-        const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(n)};
-        const cuuint64_t strides[1] = {row_bytes};
-        const cuuint32_t box[2] = {kBlockBytes / 8, static_cast<cuuint32_t>(p.bn)};
-        if (encode(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    return true;
+        const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(box_rows)};
+        return encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    if (!bf16_map(tm_a, a, m, 128)) return false;
+    if (p.wbf16) return bf16_map(tm_w, w, n, p.bn);
+    const uint64_t row_bytes = static_cast<uint64_t>(k / 256) * kBlockBytes;
+    const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {kBlockBytes / 8, static_cast<cuuint32_t>(p.bn)};
+    return encode(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, float* c, int64_t m, int64_t n, int k,
                             const GemmPlan& p, int* err, cudaStream_t s) {
-    if (p.bm == 256) gemm_q4k_kernel<2, 256><<<p.grid, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, err);
-    else if (p.bm == 128) gemm_q4k_kernel<1, 128><<<p.grid, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, err);
+    const dim3 g = p.grid;
+    if (p.bm == 256 && !p.wbf16) gemm_q4k_kernel<2, 256, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
+    else if (p.bm == 128 && !p.wbf16) gemm_q4k_kernel<1, 128, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
+    else if (p.bm == 256) gemm_q4k_kernel<2, 256, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
+    else if (p.bm == 128) gemm_q4k_kernel<1, 128, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
     else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+namespace {
+// out[i] = sum over z < parts of in[z * count + i], in part order.
+__global__ void sum_parts_kernel(const float* __restrict__ in, int parts, int64_t count, float* __restrict__ out) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+        float v = in[i];
+        for (int z = 1; z < parts; ++z) v += in[z * count + i];
+        out[i] = v;
+    }
+}
+}  // namespace
+
+cudaError_t sum_parts_launch(const float* in, int parts, int64_t count, float* out, int num_sms, cudaStream_t s) {
+    if (count <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((count + 255) / 256, static_cast<int64_t>(num_sms > 0 ? num_sms : 148) * 8);
+    sum_parts_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(in, parts, count, out);
     return cudaGetLastError();
 }
 

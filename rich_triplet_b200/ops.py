@@ -170,9 +170,23 @@ def cuda_matmul_q4k_t(a, q4k: Q4KMat):
     return c
 
 
+def cuda_matmul_bf16_t(a, bf16: MatBf16):
+    """C[M, N] = A[M, K] @ BF16[N, K]^T on the tensor cores (MatBf16::matmul_by_t, M > 1)."""
+    ctx = default_context()
+    a = np.ascontiguousarray(a)
+    if a.ndim != 2 or a.shape[1] != bf16.cols:
+        raise ValueError(f"cuda_matmul_bf16_t: a shape {a.shape} does not match weight cols {bf16.cols}")
+    bits = a if a.dtype == np.uint16 else bf16_bits(a)
+    w = _cached_weight(ctx, RT_FMT_BF16, bf16.data, bf16.rows, bf16.cols)
+    c = np.empty((a.shape[0], bf16.rows), dtype=np.float32)
+    check(lib().rt_gemm_bf16(ctx.h, w.h, bits.ctypes.data, a.shape[0], c.ctypes.data, RT_HOST), ctx.h)
+    return c
+
+
 def gemm_device(ctx, w: DeviceWeight, a_ptr, m, c_ptr):
-    """Enqueue C[m, N] = A[m, K] @ dequant(W)^T on device pointers (A bf16)."""
-    check(lib().rt_gemm_q4k(ctx.h, w.h, a_ptr, m, c_ptr, RT_DEVICE), ctx.h)
+    """Enqueue C[m, N] = A[m, K] @ W^T on device pointers (A bf16; W Q4_K or BF16)."""
+    fn = lib().rt_gemm_q4k if w.fmt == RT_FMT_Q4K else lib().rt_gemm_bf16
+    check(fn(ctx.h, w.h, a_ptr, m, c_ptr, RT_DEVICE), ctx.h)
 
 
 def gemv_device(ctx, w: DeviceWeight, x_ptr, y_ptr):

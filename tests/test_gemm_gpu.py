@@ -118,3 +118,32 @@ def test_gemm_q4k_rejects_bad_shapes():
         cuda_matmul_q4k_t(np.zeros((4, 128), np.float32), Q4KMat(16, 256, blocks))
     with pytest.raises(RtError):
         cuda_matmul_q4k_t(np.zeros((0, 256), np.float32), Q4KMat(16, 256, blocks))
+
+
+@pytest.mark.parametrize("splits", [2, 3])
+@pytest.mark.parametrize("m,n,k", [(64, 256, 2560), (200, 300, 2048)])
+def test_gemm_q4k_split_k(orc, tile, monkeypatch, splits, m, n, k):
+    # K split across CTAs (RT_GEMM_SPLITS forces the count); the partial
+    # products are added in split order.
+    monkeypatch.setenv("RT_GEMM_SPLITS", str(splits))
+    blocks = synth_q4k(61, m + n + k, n, k)
+    a = synth_normal_bf16(62, m, m * k).reshape(m, k)
+    c = cuda_matmul_q4k_t(a, Q4KMat(n, k, blocks))
+    _check(orc, blocks, n, k, a, c)
+
+
+@pytest.mark.parametrize("splits", [1, 2])
+@pytest.mark.parametrize("m,n,k", [(8, 512, 2560), (130, 1000, 512)])
+def test_gemm_bf16_weights(tile, monkeypatch, splits, m, n, k):
+    # BF16 weights (the LM head of a many-sequence step): both operands are
+    # exact bf16, so the product matches float64 to f32 accumulation.
+    from rich_triplet_b200.model import MatBf16
+    from rich_triplet_b200.ops import cuda_matmul_bf16_t
+
+    monkeypatch.setenv("RT_GEMM_SPLITS", str(splits))
+    wb = synth_normal_bf16(71, n, n * k, 0.0, 0.05)
+    a = synth_normal_bf16(72, m, m * k).reshape(m, k)
+    c = cuda_matmul_bf16_t(a, MatBf16(n, k, wb))
+    ref = _bf16_to_f32(a).astype(np.float64) @ _bf16_to_f32(wb).reshape(n, k).astype(np.float64).T
+    assert np.all(np.isfinite(c))
+    assert _row_err(c, ref) <= EXACT_TOL, _row_err(c, ref)
