@@ -254,6 +254,33 @@ int rt_decoder_launches_per_step(const rt_dec* dec, int32_t* n);
  * f32 values to copy. */
 int rt_decoder_read_activation(rt_dec* dec, int32_t which, float* host, int64_t count);
 
+/* ---- many-sequence decode ----
+ * The reference decodes one sequence per step; its decode_step_batch
+ * (src/metal_decode.rs:2079-2579) batches positions of ONE sequence.  An
+ * rt_batch advances `nseq` independent sequences per step on the weights of
+ * an existing decoder (shared, not copied), each with its own f32 KV cache of
+ * `cap` positions: every projection is one tensor-core GEMM over the
+ * sequences (bf16 activations, f32 accumulation), attention runs per
+ * sequence, and the greedy token of each sequence feeds its next step.
+ * Tokens and positions stay on the device between steps. */
+typedef struct rt_batch rt_batch;
+int rt_batch_create(rt_dec* dec, int32_t nseq, int32_t cap, rt_batch** out);
+void rt_batch_destroy(rt_batch* batch);
+/* Host arrays [nseq]: each sequence's next input token and its position. */
+int rt_batch_set(rt_batch* batch, const int32_t* tokens, const int32_t* positions);
+/* One step; logits (host [nseq][vocab]) and next_tokens (host [nseq]) may be
+ * NULL.  Afterwards each sequence's token is its greedy argmax and its
+ * position has advanced by one.  Waits for the step. */
+int rt_batch_step(rt_batch* batch, float* logits, int32_t* next_tokens);
+/* `steps` greedy steps from the current tokens and positions.  RT_DEVICE:
+ * enqueue only; RT_HOST: wait and report errors. */
+int rt_batch_generate(rt_batch* batch, int32_t steps, int flags);
+/* Fill every sequence's cache with synthetic values (a seeded hash, unit
+ * variance) and set every position to seq_len: the state a benchmark decodes
+ * from without prefilling. */
+int rt_batch_synth_kv(rt_batch* batch, uint64_t seed, int32_t seq_len);
+int rt_batch_info(const rt_batch* batch, uint64_t* bytes, int32_t* launches_per_step);
+
 /* ---- synthetic inputs ---------------------------------------------------
  * Deterministic, counter-based (SplitMix64) generators for benchmarks and
  * tests; the same (seed, stream) always gives the same bytes, independent of

@@ -92,6 +92,13 @@ SIGNATURES = {
         [_vp, ctypes.c_int64, ctypes.c_int, _vp, _vp, _vp, _vp, ctypes.c_char_p, ctypes.c_size_t],
     ),
     "rt_gemm_q4k": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp, ctypes.c_int]),
+    "rt_batch_create": (ctypes.c_int, [_vp, _i32, _i32, _pp]),
+    "rt_batch_destroy": (None, [_vp]),
+    "rt_batch_set": (ctypes.c_int, [_vp, _vp, _vp]),
+    "rt_batch_step": (ctypes.c_int, [_vp, _vp, _vp]),
+    "rt_batch_generate": (ctypes.c_int, [_vp, _i32, ctypes.c_int]),
+    "rt_batch_synth_kv": (ctypes.c_int, [_vp, _u64, _i32]),
+    "rt_batch_info": (ctypes.c_int, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_i32)]),
     "rt_gemm_bf16": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp, ctypes.c_int]),
     "rt_gemv_bench": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp), ctypes.c_int, _vp, _vp, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),

@@ -29,9 +29,22 @@ namespace {
 
 using namespace acore;
 
-// Grid (nsplit, nkv): CTA (s, h) runs item (h, s).
+// Grid (nsplit, nkv, sequences): CTA (s, h, b) runs item (h, s) of sequence b.
 template <int G>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs a0) {
+    // Each of sequence b's pointers is formed from the parameter itself.  (A
+    // conditional in-place update of the copy, `if (b) a.qkv += ...`, built
+    // with nvcc 12.9 -O3, left a.qkv at sequence 0's rows while the other
+    // members moved: every plane then attended with sequence 0's q/k/v.)
+    AttnArgs a = a0;
+    const int64_t b = blockIdx.z;
+    a.qkv = a0.qkv + b * a0.seq_qkv;
+    a.kcache = a0.kcache + b * a0.seq_kv;
+    a.vcache = a0.vcache + b * a0.seq_kv;
+    a.part = a0.part + b * a0.seq_part;
+    a.out = a0.out + b * a0.seq_out;
+    a.pos = a0.pos + b;
+    a.counter = a0.counter + b * a0.nkv;
     extern __shared__ __align__(128) uint8_t smem[];
     AttnSmem S;
     attn_carve(smem, a.D, G, kAttnTile, &S);
@@ -48,8 +61,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
 }
 
 template <int G>
-cudaError_t launch_g(const AttnArgs& a, cudaStream_t s, bool pdl) {
-    return rt_launch(attention_kernel<G>, dim3(a.nsplit, a.nkv), dim3(kAttnThreads), attention_smem_bytes(a.D, G), s,
+cudaError_t launch_g(const AttnArgs& a, cudaStream_t s, bool pdl, int nseq = 1) {
+    return rt_launch(attention_kernel<G>, dim3(a.nsplit, a.nkv, nseq), dim3(kAttnThreads), attention_smem_bytes(a.D, G), s,
                      pdl, a);
 }
 
@@ -73,6 +86,17 @@ cudaError_t attention_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {
         case 2: return launch_g<2>(a, s, pdl);
         case 4: return launch_g<4>(a, s, pdl);
         case 8: return launch_g<8>(a, s, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t attention_launch_batch(const AttnArgs& a, int nseq, cudaStream_t s) {
+    if (a.D > kAttnThreads || a.D % 32 != 0 || a.nq % a.nkv != 0 || nseq < 1 || nseq > 65535) return cudaErrorInvalidValue;
+    switch (a.nq / a.nkv) {
+        case 1: return launch_g<1>(a, s, false, nseq);
+        case 2: return launch_g<2>(a, s, false, nseq);
+        case 4: return launch_g<4>(a, s, false, nseq);
+        case 8: return launch_g<8>(a, s, false, nseq);
         default: return cudaErrorInvalidValue;
     }
 }

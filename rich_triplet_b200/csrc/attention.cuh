@@ -28,6 +28,10 @@ struct AttnArgs {
     uint32_t* counter;      // [nkv], zero before the launch; the combining CTA resets it
     float* out;             // [nq*D]
     int* err;
+    // Several sequences in one launch (grid z = sequence b): b's qkv, caches,
+    // partials and output sit these many floats after sequence 0's, its
+    // position at pos[b] and its counters at counter[b * nkv].  Unused with one.
+    int64_t seq_qkv = 0, seq_kv = 0, seq_part = 0, seq_out = 0;
 };
 
 constexpr int kAttnTile = 32;     // cached positions per shared-memory tile
@@ -41,6 +45,8 @@ size_t attention_smem_bytes(int D, int G);
 // Set kernel attributes; call once per device before the first launch / capture.
 cudaError_t attention_prepare();
 cudaError_t attention_launch(const AttnArgs& a, cudaStream_t s, bool pdl);
+// The same for `nseq` sequences (AttnArgs::seq_* strides), one grid plane each.
+cudaError_t attention_launch_batch(const AttnArgs& a, int nseq, cudaStream_t s);
 // Algorithmic bytes at context length L (positions attended) for one layer.
 uint64_t attention_algorithmic_bytes(int nq, int nkv, int D, int64_t L);
 

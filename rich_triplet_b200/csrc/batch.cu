@@ -1,0 +1,524 @@
+// batch.cu -- many-sequence Gemma 3 decode: one step
+// advances B independent sequences, each with its own KV cache and position.
+//
+// The reference decodes one sequence at a time (MetalDecodeContext::
+// decode_step, src/metal_decode.rs:2028-2074; its decode_step_batch,
+// :2079-2579, batches the positions of ONE sequence).  Per step here, the
+// weights are read once for all B sequences: every projection is the tcgen05
+// GEMM with M = B (gemm.cu), bf16 activations and f32 accumulation, split
+// across K when B alone leaves SMs idle.  Per layer l:
+//   rows    residual += post-FFN-norm(down_{l-1}) (embedding * sqrt(H) at l = 0);
+//           x = RMSNorm(residual) -> bf16                      (Gemma3Block, src/transformer4.rs:1954-1964)
+//   GEMM    qkv = x . Wqkv^T
+//   attn    per sequence and KV head: q/k norm + RoPE, KV append, split-context
+//           flash decode (attention.cu, one grid plane per sequence)
+//   GEMM    o = bf16(attn) . Wo^T
+//   rows    residual += post-attn-norm(o); x = pre-FFN RMSNorm -> bf16
+//   GEMM    gu = x . Wgu^T  (gate/up rows interleaved)
+//   rows    h = gelu_tanh(gate) * up -> bf16
+//   GEMM    down = h . Wdown^T
+// then the final norm, the LM head as a bf16-weight GEMM over the tied
+// embedding, and a per-sequence greedy argmax (ties to the higher index, as
+// sample_token, src/transformer4.rs:3084-3091) that also advances each
+// sequence's position.  One step is captured once as a CUDA graph; tokens and
+// positions live in device memory, so generation is graph launches alone.
+//
+// Weights, norms and the RoPE conventions are the single-sequence engine's
+// (decoder_internal.h); this engine adds the B KV caches and its activations.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "decoder_internal.h"
+#include "gemm.cuh"
+#include "gemv_core.cuh"
+#include "rt_internal.h"
+
+using rt::fail;
+
+namespace {
+
+struct BatchGemm {
+    rt::GemmPlan p;
+    CUtensorMap ta, tw;
+    int64_t n = 0;
+    int k = 0;
+};
+
+}  // namespace
+
+struct rt_batch {
+    rt_dec* dec = nullptr;
+    rt_ctx* ctx = nullptr;
+    int B = 0, cap = 0, H = 0, D = 0, NQ = 0, NKV = 0, F = 0, V = 0, NL = 0, qkv_rows = 0, nsplit = 0;
+    int64_t seq_kv = 0;          // floats of one sequence's caches
+    float* kv = nullptr;         // [B][NL][2 (K, V)][NKV][cap][D]
+    float* rope = nullptr;       // [2 (local, global)][2 (cos, sin)][cap][D/2]
+    uint16_t* xa = nullptr;      // bf16 [B][K] input of the next GEMM
+    float* parts = nullptr;      // GEMM outputs [splits][B][N]
+    float* qkv = nullptr;        // [B][qkv_rows]
+    float* attn = nullptr;       // [B][NQ * D]
+    float* resid[2] = {nullptr, nullptr};  // [B][H], ping-pong
+    float* logits = nullptr;     // [B][V]
+    float* attn_part = nullptr;  // [B][NKV][nsplit][G][D + 4]
+    uint32_t* counters = nullptr;  // [B][NKV], zero between launches
+    int32_t* tokens = nullptr;   // [B] input token of the next step
+    int32_t* pos = nullptr;      // [B] position of the next step
+    int* h_err = nullptr;        // pinned copy of the context's error word
+    std::vector<BatchGemm> g_qkv, g_o, g_gu, g_down;
+    BatchGemm g_lm;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+    uint64_t dev_bytes = 0;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+// ---- row kernels (one CTA per sequence row unless stated) ----
+
+// Residual update and RMSNorm of one row (the fused prologues of the
+// single-sequence engine, in the same operation order):
+//   embed != null: r = bf16(embed[tokens[b]]) * embed_scale   (src/transformer4.rs:2360-2364)
+//   else:          s = src parts added in order; r = resid_in + s * rms(s) * (1 + gpost)
+//   resid_out = r;  out = bf16(r * rms(r) * (1 + gpre))          (rms_norm_gemma3, src/autograd2.rs:3477-3496)
+__global__ void resid_norm_rows_kernel(const uint16_t* embed, const int32_t* tokens, float embed_scale,
+                                       const float* src, int src_parts, int64_t part_stride, const float* resid_in,
+                                       float* resid_out, const float* gpost, const float* gpre, float eps, int H,
+                                       uint16_t* out) {
+    extern __shared__ float row[];  // [H]
+    __shared__ float red[32];
+    const int b = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x;
+    const int64_t base = static_cast<int64_t>(b) * H;
+    const float inv_d = 1.0f / static_cast<float>(H);
+    float ss = 0.f;
+    if (embed) {
+        const uint16_t* er = embed + static_cast<int64_t>(tokens[b]) * H;
+        for (int c = tid; c < H; c += nthr) {
+            const float v = __fmul_rn(rt::bf16_bits_to_f32(er[c]), embed_scale);
+            row[c] = v;
+            resid_out[base + c] = v;
+            ss += v * v;
+        }
+    } else {
+        for (int c = tid; c < H; c += nthr) {
+            float s = src[base + c];
+            for (int q = 1; q < src_parts; ++q) s += src[q * part_stride + base + c];
+            row[c] = s;
+            ss += s * s;
+        }
+        ss = rt::block_sum(ss, red);
+        const float r1 = 1.0f / sqrtf(ss * inv_d + eps);
+        ss = 0.f;
+        for (int c = tid; c < H; c += nthr) {
+            const float nv = __fadd_rn(resid_in[base + c], __fmul_rn(__fmul_rn(row[c], r1), __fadd_rn(1.0f, gpost[c])));
+            row[c] = nv;
+            resid_out[base + c] = nv;
+            ss += nv * nv;
+        }
+    }
+    ss = rt::block_sum(ss, red);
+    const float r2 = 1.0f / sqrtf(ss * inv_d + eps);
+    for (int c = tid; c < H; c += nthr)
+        out[base + c] = static_cast<uint16_t>(
+            rt::gcore::bf16_rne(__fmul_rn(__fmul_rn(row[c], r2), __fadd_rn(1.0f, gpre[c]))));
+}
+
+// h[b][j] = bf16(gelu_tanh(gate) * up) from the interleaved gate/up GEMM
+// output (column 2j gate, 2j + 1 up), its split parts added in order.
+// Grid (ceil(F / 256), B).
+__global__ void gelu_rows_kernel(const float* c, int parts, int64_t part_stride, int F, uint16_t* out) {
+    const int b = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= F) return;
+    const float* r = c + static_cast<int64_t>(b) * 2 * F;
+    float g = r[2 * j], u = r[2 * j + 1];
+    for (int q = 1; q < parts; ++q) {
+        g += r[q * part_stride + 2 * j];
+        u += r[q * part_stride + 2 * j + 1];
+    }
+    out[static_cast<int64_t>(b) * F + j] = static_cast<uint16_t>(rt::gcore::bf16_rne(__fmul_rn(rt::gcore::gelu_tanh_dev(g), u)));
+}
+
+__global__ void to_bf16_kernel(const float* in, int64_t n, uint16_t* out) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = static_cast<uint16_t>(rt::gcore::bf16_rne(in[i]));
+}
+
+// Greedy token of each row (largest logit, ties to the higher index), then
+// tokens[b] = it and pos[b] += 1.  1024 threads per row.
+__global__ void argmax_rows_kernel(const float* logits, int V, int32_t* tokens, int32_t* pos) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* r = logits + static_cast<int64_t>(b) * V;
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int i = tid; i < V; i += blockDim.x) {
+        const float v = r[i];
+        if (v > bv || (v == bv && i > bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi > bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] > bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        tokens[b] = bi;
+        pos[b] += 1;
+    }
+}
+
+// Synthetic cache contents for benchmarks: a hash of (seed, index) mapped to
+// a uniform value of unit variance.
+__global__ void synth_kv_kernel(float* kv, int64_t n, uint64_t seed) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        uint64_t z = seed + static_cast<uint64_t>(i) * 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        z ^= z >> 31;
+        kv[i] = (static_cast<float>(z >> 40) * (1.0f / 16777216.0f) - 0.5f) * 3.4641016f;
+    }
+}
+
+__global__ void fill_i32_kernel(int32_t* p, int n, int32_t v) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+int balloc(rt_batch* t, void** p, size_t bytes, const char* what) {
+    int rc = rt::dev_alloc(t->ctx, p, bytes, what);
+    if (rc == RT_OK) {
+        t->allocs.push_back(*p);
+        t->dev_bytes += bytes;
+    }
+    return rc;
+}
+
+void release(rt_batch* t) {
+    if (!t) return;
+    if (t->exec) cudaGraphExecDestroy(t->exec);
+    if (t->graph) cudaGraphDestroy(t->graph);
+    for (void* p : t->allocs) cudaFree(p);
+    if (t->h_err) cudaFreeHost(t->h_err);
+    delete t;
+}
+
+float* k_layer(rt_batch* t, int l) { return t->kv + static_cast<int64_t>(l) * 2 * t->NKV * t->cap * t->D; }
+float* v_layer(rt_batch* t, int l) { return k_layer(t, l) + static_cast<int64_t>(t->NKV) * t->cap * t->D; }
+
+bool make_gemm(rt_batch* t, const void* w, int64_t n, int k, bool wbf16, bool allow_split, BatchGemm* g) {
+    g->n = n;
+    g->k = k;
+    g->p = rt::gemm_q4k_plan(t->B, n, k, t->ctx->num_sms, wbf16, allow_split);
+    if (g->p.bm == 0) return false;
+    return rt::gemm_q4k_tmaps(t->xa, t->B, w, n, k, g->p, &g->ta, &g->tw);
+}
+
+// Enqueue one step (all launches of it) on `s`.
+cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
+    rt_dec* d = t->dec;
+    const int B = t->B, H = t->H, D = t->D, G = t->NQ / t->NKV;
+    const size_t norm_smem = sizeof(float) * H;
+    const float eps = d->cfg.rms_norm_eps;
+    int p = 0;
+    int n = 0;
+    cudaError_t e = cudaSuccess;
+    auto ok = [&](cudaError_t r) {
+        if (e == cudaSuccess) e = r;
+        ++n;
+        return e == cudaSuccess;
+    };
+    auto gemm = [&](const BatchGemm& g, float* c) {
+        return ok(rt::gemm_q4k_launch(g.ta, g.tw, c, B, g.n, g.k, g.p, t->ctx->d_err, s));
+    };
+    for (int l = 0; l < t->NL && e == cudaSuccess; ++l) {
+        // residual update (or embedding) + attention RMSNorm -> x
+        if (l == 0) {
+            resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(d->embed, t->tokens, sqrtf(static_cast<float>(H)), nullptr,
+                                                             0, 0, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0),
+                                                             eps, H, t->xa);
+        } else {
+            const BatchGemm& gd = t->g_down[l - 1];
+            resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
+                                                             static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
+                                                             rt::norm_ptr(d, l - 1, 3), rt::norm_ptr(d, l, 0), eps, H,
+                                                             t->xa);
+            p = 1 - p;
+        }
+        if (!ok(cudaGetLastError())) break;
+        // qkv
+        const BatchGemm& gq = t->g_qkv[l];
+        if (gq.p.splits > 1) {
+            if (!gemm(gq, t->parts)) break;
+            if (!ok(rt::sum_parts_launch(t->parts, gq.p.splits, static_cast<int64_t>(B) * t->qkv_rows, t->qkv,
+                                         t->ctx->num_sms, s)))
+                break;
+        } else if (!gemm(gq, t->qkv)) {
+            break;
+        }
+        // attention, one grid plane per sequence
+        rt::AttnArgs a{};
+        a.qkv = t->qkv;
+        a.q_norm = d->qk_norms + static_cast<size_t>(l) * 2 * D;
+        a.k_norm = a.q_norm + D;
+        a.kcache = k_layer(t, l);
+        a.vcache = v_layer(t, l);
+        const size_t tab = static_cast<size_t>(t->cap) * (D / 2);
+        const int gsel = rt::is_global(l) ? 1 : 0;
+        a.rope_cos = t->rope + (static_cast<size_t>(gsel) * 2 + 0) * tab;
+        a.rope_sin = t->rope + (static_cast<size_t>(gsel) * 2 + 1) * tab;
+        a.pos = t->pos;
+        a.cap = t->cap;
+        a.nq = t->NQ;
+        a.nkv = t->NKV;
+        a.D = D;
+        a.window = rt::is_global(l) ? 0 : d->cfg.sliding_window;
+        a.nsplit = t->nsplit;
+        a.scale = 1.0f / sqrtf(d->cfg.query_pre_attn_scalar);
+        a.eps = eps;
+        a.part = t->attn_part;
+        a.counter = t->counters;
+        a.out = t->attn;
+        a.err = t->ctx->d_err;
+        a.seq_qkv = t->qkv_rows;
+        a.seq_kv = t->seq_kv;
+        a.seq_part = static_cast<int64_t>(t->NKV) * t->nsplit * G * rt::attn_part_stride(D);
+        a.seq_out = static_cast<int64_t>(t->NQ) * D;
+        if (!ok(rt::attention_launch_batch(a, B, s))) break;
+        const int64_t na = static_cast<int64_t>(B) * t->NQ * D;
+        to_bf16_kernel<<<static_cast<unsigned>(std::min<int64_t>((na + 255) / 256, 4096)), 256, 0, s>>>(t->attn, na, t->xa);
+        if (!ok(cudaGetLastError())) break;
+        // o, then residual update + pre-FFN RMSNorm
+        const BatchGemm& go = t->g_o[l];
+        if (!gemm(go, t->parts)) break;
+        resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, go.p.splits,
+                                                         static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
+                                                         rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa);
+        p = 1 - p;
+        if (!ok(cudaGetLastError())) break;
+        // gate/up, GELU gate
+        const BatchGemm& gg = t->g_gu[l];
+        if (!gemm(gg, t->parts)) break;
+        gelu_rows_kernel<<<dim3((t->F + 255) / 256, B), 256, 0, s>>>(t->parts, gg.p.splits, static_cast<int64_t>(B) * 2 * t->F,
+                                                                     t->F, t->xa);
+        if (!ok(cudaGetLastError())) break;
+        // down
+        if (!gemm(t->g_down[l], t->parts)) break;
+    }
+    if (e == cudaSuccess) {
+        // final residual update + norm, LM head, greedy tokens
+        const BatchGemm& gd = t->g_down[t->NL - 1];
+        resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
+                                                         static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
+                                                         rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa);
+        if (ok(cudaGetLastError()) && gemm(t->g_lm, t->logits)) {
+            argmax_rows_kernel<<<B, 1024, 0, s>>>(t->logits, t->V, t->tokens, t->pos);
+            ok(cudaGetLastError());
+        }
+    }
+    t->launches = n;
+    return e;
+}
+
+int check_error_word(rt_batch* t) {
+    if (*t->h_err) {
+        const int w = *t->h_err;
+        *t->h_err = 0;
+        cudaMemsetAsync(t->ctx->d_err, 0, sizeof(int), t->ctx->stream);
+        cudaStreamSynchronize(t->ctx->stream);
+        return fail(t->ctx, RT_E_TIMEOUT, "batch step: a kernel reported error word %d", w);
+    }
+    return RT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
+    if (!d || !out) return RT_E_INVAL;
+    *out = nullptr;
+    rt_ctx* ctx = d->ctx;
+    if (nseq < 1 || nseq > 1024 || cap < 1) return fail(ctx, RT_E_SHAPE, "rt_batch_create: nseq %d / cap %d", nseq, cap);
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    rt_batch* t = new rt_batch;
+    t->dec = d;
+    t->ctx = ctx;
+    t->B = nseq;
+    t->cap = cap;
+    t->H = d->H;
+    t->D = d->D;
+    t->NQ = d->NQ;
+    t->NKV = d->NKV;
+    t->F = d->F;
+    t->V = d->V;
+    t->NL = d->NL;
+    t->qkv_rows = d->qkv_rows;
+    const int G = t->NQ / t->NKV;
+    // Enough attention items to fill the SMs about four times over.
+    t->nsplit = std::max(1, std::min(64, (4 * ctx->num_sms + nseq * t->NKV - 1) / (nseq * t->NKV)));
+    auto bail = [&](int rc) {
+        release(t);
+        return rc;
+    };
+    int rc;
+    t->seq_kv = static_cast<int64_t>(t->NL) * 2 * t->NKV * cap * t->D;
+    if ((rc = balloc(t, reinterpret_cast<void**>(&t->kv), sizeof(float) * t->seq_kv * nseq, "batch KV caches")) != RT_OK)
+        return bail(rc);
+    RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->kv, 0, sizeof(float) * t->seq_kv * nseq, ctx->stream));
+    {
+        const size_t tab = static_cast<size_t>(cap) * (t->D / 2);
+        std::vector<float> r(4 * tab);
+        const rt_gemma3_cfg& c = d->cfg;
+        rt::rope_table(c.rope_theta_local, c.rope_freq_scale_local, t->D, cap, &r[0], &r[tab]);
+        rt::rope_table(c.rope_theta_global, c.rope_freq_scale_global, t->D, cap, &r[2 * tab], &r[3 * tab]);
+        if ((rc = balloc(t, reinterpret_cast<void**>(&t->rope), r.size() * 4, "batch rope tables")) != RT_OK) return bail(rc);
+        if (cudaMemcpy(t->rope, r.data(), r.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: upload rope tables"));
+    }
+    const int64_t B = nseq;
+    const int64_t kmax = std::max<int64_t>({t->H, static_cast<int64_t>(t->NQ) * t->D, t->F});
+    if ((rc = balloc(t, reinterpret_cast<void**>(&t->xa), sizeof(uint16_t) * B * kmax + 256, "batch GEMM input")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->qkv), sizeof(float) * B * t->qkv_rows, "batch qkv")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->attn), sizeof(float) * B * t->NQ * t->D, "batch attention")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->resid[0]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->resid[1]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->logits), sizeof(float) * B * t->V, "batch logits")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->attn_part),
+                     sizeof(float) * B * t->NKV * t->nsplit * G * rt::attn_part_stride(t->D), "batch attention partials")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->counters), sizeof(uint32_t) * B * t->NKV, "batch counters")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->tokens), sizeof(int32_t) * B, "batch tokens")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->pos), sizeof(int32_t) * B, "batch positions")) != RT_OK)
+        return bail(rc);
+    RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->counters, 0, sizeof(uint32_t) * B * t->NKV, ctx->stream));
+    RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->tokens, 0, sizeof(int32_t) * B, ctx->stream));
+    RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->pos, 0, sizeof(int32_t) * B, ctx->stream));
+    if (cudaMallocHost(reinterpret_cast<void**>(&t->h_err), sizeof(int)) != cudaSuccess) return bail(fail(ctx, RT_E_NOMEM, "pinned error word"));
+    *t->h_err = 0;
+    // GEMM plans and tensor maps (A is always xa, read as [B][K])
+    const int64_t H = t->H;
+    t->g_qkv.resize(t->NL);
+    t->g_o.resize(t->NL);
+    t->g_gu.resize(t->NL);
+    t->g_down.resize(t->NL);
+    int64_t part_floats = 0;
+    for (int l = 0; l < t->NL; ++l) {
+        if (!make_gemm(t, d->w_qkv[l], t->qkv_rows, static_cast<int>(H), false, true, &t->g_qkv[l]) ||
+            !make_gemm(t, d->w_o[l], H, t->NQ * t->D, false, true, &t->g_o[l]) ||
+            !make_gemm(t, d->w_gu[l], 2LL * t->F, static_cast<int>(H), false, true, &t->g_gu[l]) ||
+            !make_gemm(t, d->w_down[l], H, t->F, false, true, &t->g_down[l]))
+            return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: no GEMM geometry for layer %d", l));
+        for (const BatchGemm* g : {&t->g_qkv[l], &t->g_o[l], &t->g_gu[l], &t->g_down[l]})
+            part_floats = std::max<int64_t>(part_floats, static_cast<int64_t>(g->p.splits) * B * g->n);
+    }
+    if (!make_gemm(t, d->embed, t->V, static_cast<int>(H), true, false, &t->g_lm))
+        return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: no GEMM geometry for the LM head"));
+    if ((rc = balloc(t, reinterpret_cast<void**>(&t->parts), sizeof(float) * part_floats, "batch GEMM outputs")) != RT_OK)
+        return bail(rc);
+    if (rt::gemm_q4k_prepare() != cudaSuccess || rt::attention_prepare() != cudaSuccess)
+        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: kernel attributes"));
+    const size_t norm_smem = sizeof(float) * H;
+    if (norm_smem > 48 * 1024 &&
+        cudaFuncSetAttribute(resid_norm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(norm_smem)) != cudaSuccess)
+        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: norm kernel attributes"));
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    // capture one step
+    cudaStream_t s = ctx->stream;
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: begin capture"));
+    const cudaError_t ce = enqueue(t, s);
+    const cudaError_t ee = cudaStreamEndCapture(s, &t->graph);
+    if (ce != cudaSuccess || ee != cudaSuccess || cudaGraphInstantiate(&t->exec, t->graph, 0) != cudaSuccess) {
+        cudaGetLastError();
+        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: step capture failed (%s)", cudaGetErrorString(ce != cudaSuccess ? ce : ee)));
+    }
+    *out = t;
+    return RT_OK;
+}
+
+void rt_batch_destroy(rt_batch* t) {
+    if (!t) return;
+    cudaSetDevice(t->ctx->device);
+    cudaStreamSynchronize(t->ctx->stream);
+    release(t);
+}
+
+int rt_batch_set(rt_batch* t, const int32_t* tokens, const int32_t* positions) {
+    if (!t || !tokens || !positions) return t ? fail(t->ctx, RT_E_INVAL, "rt_batch_set: null argument") : RT_E_INVAL;
+    for (int b = 0; b < t->B; ++b) {
+        if (tokens[b] < 0 || tokens[b] >= t->V) return fail(t->ctx, RT_E_INVAL, "rt_batch_set: token %d out of range", tokens[b]);
+        if (positions[b] < 0 || positions[b] >= t->cap)
+            return fail(t->ctx, RT_E_STATE, "rt_batch_set: position %d outside the cache", positions[b]);
+    }
+    RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(t->tokens, tokens, sizeof(int32_t) * t->B, cudaMemcpyHostToDevice, t->ctx->stream));
+    RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(t->pos, positions, sizeof(int32_t) * t->B, cudaMemcpyHostToDevice, t->ctx->stream));
+    RT_CHECK_CUDA(t->ctx, cudaStreamSynchronize(t->ctx->stream));
+    return RT_OK;
+}
+
+int rt_batch_step(rt_batch* t, float* logits, int32_t* next_tokens) {
+    if (!t) return RT_E_INVAL;
+    cudaStream_t s = t->ctx->stream;
+    RT_CHECK_CUDA(t->ctx, cudaGraphLaunch(t->exec, s));
+    if (logits)
+        RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(logits, t->logits, sizeof(float) * t->B * t->V, cudaMemcpyDeviceToHost, s));
+    if (next_tokens)
+        RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(next_tokens, t->tokens, sizeof(int32_t) * t->B, cudaMemcpyDeviceToHost, s));
+    RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(t->h_err, t->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    RT_CHECK_CUDA(t->ctx, cudaStreamSynchronize(s));
+    return check_error_word(t);
+}
+
+int rt_batch_generate(rt_batch* t, int32_t steps, int flags) {
+    if (!t) return RT_E_INVAL;
+    if (flags != RT_HOST && flags != RT_DEVICE) return fail(t->ctx, RT_E_INVAL, "rt_batch_generate: bad flags");
+    for (int i = 0; i < steps; ++i) RT_CHECK_CUDA(t->ctx, cudaGraphLaunch(t->exec, t->ctx->stream));
+    if (flags == RT_DEVICE) return RT_OK;
+    RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(t->h_err, t->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, t->ctx->stream));
+    RT_CHECK_CUDA(t->ctx, cudaStreamSynchronize(t->ctx->stream));
+    return check_error_word(t);
+}
+
+int rt_batch_synth_kv(rt_batch* t, uint64_t seed, int32_t seq_len) {
+    if (!t) return RT_E_INVAL;
+    if (seq_len < 0 || seq_len >= t->cap) return fail(t->ctx, RT_E_STATE, "rt_batch_synth_kv: length %d outside the cache", seq_len);
+    const int64_t n = t->seq_kv * t->B;
+    synth_kv_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 65536)), 256, 0, t->ctx->stream>>>(t->kv, n, seed);
+    fill_i32_kernel<<<(t->B + 255) / 256, 256, 0, t->ctx->stream>>>(t->pos, t->B, seq_len);
+    RT_CHECK_CUDA(t->ctx, cudaGetLastError());
+    RT_CHECK_CUDA(t->ctx, cudaStreamSynchronize(t->ctx->stream));
+    return RT_OK;
+}
+
+int rt_batch_info(const rt_batch* t, uint64_t* bytes, int32_t* launches_per_step) {
+    if (!t) return RT_E_INVAL;
+    if (bytes) *bytes = t->dev_bytes;
+    if (launches_per_step) *launches_per_step = t->launches;
+    return RT_OK;
+}
+
+}  // extern "C"

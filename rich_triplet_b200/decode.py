@@ -144,3 +144,64 @@ class CudaDecodeContext:
             self.close()
         except Exception:
             pass
+
+
+class CudaBatchDecoder:
+    """Many-sequence decode on the weights of a
+    CudaDecodeContext: `nseq` independent sequences, each with its own f32 KV
+    cache of `cap` positions, advance together; every projection is one
+    tensor-core GEMM over the sequences (bf16 activations, f32 accumulation).
+    The reference decodes one sequence at a time; this has no counterpart
+    there (its decode_step_batch, src/metal_decode.rs:2079, batches positions
+    of one sequence)."""
+
+    def __init__(self, dec: CudaDecodeContext, nseq, cap):
+        self.dec = dec
+        self.ctx = dec.ctx
+        self.nseq = nseq
+        self.cap = cap
+        self.vocab = dec.lm_head_vocab
+        h = ctypes.c_void_p()
+        check(lib().rt_batch_create(dec.h, nseq, cap, ctypes.byref(h)), self.ctx.h)
+        self.h = h
+
+    def set(self, tokens, positions):
+        """Each sequence's next input token and its position (arrays of nseq)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        if t.shape != (self.nseq,) or p.shape != (self.nseq,):
+            raise ValueError(f"CudaBatchDecoder.set: need {self.nseq} tokens and positions")
+        check(lib().rt_batch_set(self.h, t.ctypes.data, p.ctypes.data), self.ctx.h)
+
+    def step(self, want_logits=True):
+        """One step for every sequence; returns (logits [nseq, vocab] or None,
+        greedy next tokens [nseq]).  Positions advance by one."""
+        logits = np.empty((self.nseq, self.vocab), dtype=np.float32) if want_logits else None
+        nxt = np.empty(self.nseq, dtype=np.int32)
+        check(lib().rt_batch_step(self.h, logits.ctypes.data if want_logits else None, nxt.ctypes.data), self.ctx.h)
+        return logits, nxt
+
+    def generate(self, steps, wait=True):
+        """`steps` greedy steps from the current tokens and positions."""
+        check(lib().rt_batch_generate(self.h, steps, RT_HOST if wait else RT_DEVICE), self.ctx.h)
+
+    def synth_kv(self, seed, seq_len):
+        """Synthetic cache contents for benchmarks; every position = seq_len."""
+        check(lib().rt_batch_synth_kv(self.h, seed, seq_len), self.ctx.h)
+
+    def info(self):
+        b = ctypes.c_uint64()
+        n = ctypes.c_int32()
+        check(lib().rt_batch_info(self.h, ctypes.byref(b), ctypes.byref(n)), self.ctx.h)
+        return b.value, n.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().rt_batch_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
