@@ -132,8 +132,10 @@ int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int cols, const 
  * (src/autograd2.rs:1437-1457) and matmul_q4k_t_exact (:1507-1625).  A is bf16
  * row-major [m, K] (uint16 bits), C is f32 row-major [m, N].  flags RT_HOST:
  * host A and C, the call copies and waits; RT_DEVICE: device pointers (16-byte
- * aligned), enqueued on the context stream.  The weights are rounded to bf16
- * for the tensor cores (relative error <= 2^-9 per weight). */
+ * aligned), enqueued on the context stream.  The tensor cores take fp16: each
+ * row of A is scaled by a power of two into fp16's range (exact for bf16
+ * input), each dequantised weight is rounded to fp16 (relative error <= 2^-11),
+ * and the scale is undone on the f32 result. */
 int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags);
 /* The same product for a BF16 weight W [N, K] (K a multiple of 256), such as
  * the tied LM head over several sequences' final hidden states: replaces

@@ -285,24 +285,28 @@ int gemm_common(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
     const size_t a_bytes = static_cast<size_t>(m) * k * 2;
     if (flags == RT_DEVICE && ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(c) & 15)))
         return fail(ctx, RT_E_INVAL, "rt_gemm: device A and C must be 16-byte aligned");
-    // scratch: [A (host calls)] [C (host calls)] [split partials], each 256-byte aligned
+    // scratch: [A (host calls)] [A as fp16 rows] [row scales] [C (host calls)]
+    // [split partials], each 256-byte aligned
     auto al = [](size_t floats) { return (floats + 63) / 64 * 64; };
     const size_t a_floats = flags == RT_HOST ? al((a_bytes + 3) / 4) : 0;
+    const size_t a16_floats = al((a_bytes + 3) / 4), s_floats = al(static_cast<size_t>(m));
     const size_t c_floats = flags == RT_HOST ? al(static_cast<size_t>(m) * n) : 0;
     const size_t part_floats = p.splits > 1 ? static_cast<size_t>(p.splits) * m * n : 0;
-    if (a_floats + c_floats + part_floats > 0) {
-        int rc = ensure_scratch(ctx, a_floats + c_floats + part_floats);
-        if (rc != RT_OK) return rc;
-    }
+    int rc = ensure_scratch(ctx, a_floats + a16_floats + s_floats + c_floats + part_floats);
+    if (rc != RT_OK) return rc;
     const void* da = flags == RT_HOST ? static_cast<const void*>(ctx->scratch) : a;
-    float* dc = flags == RT_HOST ? ctx->scratch + a_floats : c;
-    float* parts = ctx->scratch + a_floats + c_floats;
+    uint16_t* a16 = reinterpret_cast<uint16_t*>(ctx->scratch + a_floats);
+    float* ascale = ctx->scratch + a_floats + a16_floats;
+    float* dc = flags == RT_HOST ? ascale + s_floats : c;
+    float* parts = ascale + s_floats + c_floats;
     if (flags == RT_HOST)
         RT_CHECK_CUDA(ctx, cudaMemcpyAsync(const_cast<void*>(da), a, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
+    RT_CHECK_CUDA(ctx, rt::a_to_f16_launch(static_cast<const uint16_t*>(da), m, k, a16, ascale, ctx->stream));
     CUtensorMap tm_a, tm_w;
-    if (!rt::gemm_q4k_tmaps(da, m, w->d, n, k, p, &tm_a, &tm_w))
+    if (!rt::gemm_q4k_tmaps(a16, m, w->d, n, k, p, &tm_a, &tm_w))
         return fail(ctx, RT_E_CUDA, "rt_gemm: TMA descriptor rejected");
-    RT_CHECK_CUDA(ctx, rt::gemm_q4k_launch(tm_a, tm_w, p.splits > 1 ? parts : dc, m, n, k, p, ctx->d_err, ctx->stream));
+    RT_CHECK_CUDA(ctx, rt::gemm_q4k_launch(tm_a, tm_w, ascale, p.splits > 1 ? parts : dc, m, n, k, p, ctx->d_err,
+                                           ctx->stream));
     if (p.splits > 1)
         RT_CHECK_CUDA(ctx, rt::sum_parts_launch(parts, p.splits, static_cast<int64_t>(m) * n, dc, ctx->num_sms, ctx->stream));
     if (flags == RT_HOST) {

@@ -5,19 +5,20 @@
 // decode_step, src/metal_decode.rs:2028-2074; its decode_step_batch,
 // :2079-2579, batches the positions of ONE sequence).  Per step here, the
 // weights are read once for all B sequences: every projection is the tcgen05
-// GEMM with M = B (gemm.cu), bf16 activations and f32 accumulation, split
-// across K when B alone leaves SMs idle.  Per layer l:
+// GEMM with M = B (gemm.cu), fp16 activations (each row scaled by a power of
+// two into fp16's range, undone on the f32 product) and f32 accumulation,
+// split across K when B alone leaves SMs idle.  Per layer l:
 //   rows    residual += post-FFN-norm(down_{l-1}) (embedding * sqrt(H) at l = 0);
-//           x = RMSNorm(residual) -> bf16                      (Gemma3Block, src/transformer4.rs:1954-1964)
+//           x = RMSNorm(residual) -> fp16                      (Gemma3Block, src/transformer4.rs:1954-1964)
 //   GEMM    qkv = x . Wqkv^T
 //   attn    per sequence and KV head: q/k norm + RoPE, KV append, split-context
 //           flash decode (attention.cu, one grid plane per sequence)
-//   GEMM    o = bf16(attn) . Wo^T
-//   rows    residual += post-attn-norm(o); x = pre-FFN RMSNorm -> bf16
+//   GEMM    o = fp16(attn) . Wo^T
+//   rows    residual += post-attn-norm(o); x = pre-FFN RMSNorm -> fp16
 //   GEMM    gu = x . Wgu^T  (gate/up rows interleaved)
-//   rows    h = gelu_tanh(gate) * up -> bf16
+//   rows    h = gelu_tanh(gate) * up -> fp16
 //   GEMM    down = h . Wdown^T
-// then the final norm, the LM head as a bf16-weight GEMM over the tied
+// then the final norm, the LM head as a GEMM over the tied bf16
 // embedding, and a per-sequence greedy argmax (ties to the higher index, as
 // sample_token, src/transformer4.rs:3084-3091) that also advances each
 // sequence's position.  One step is captured once as a CUDA graph; tokens and
@@ -58,7 +59,8 @@ struct rt_batch {
     int64_t seq_kv = 0;          // floats of one sequence's caches
     float* kv = nullptr;         // [B][NL][2 (K, V)][NKV][cap][D]
     float* rope = nullptr;       // [2 (local, global)][2 (cos, sin)][cap][D/2]
-    uint16_t* xa = nullptr;      // bf16 [B][K] input of the next GEMM
+    uint16_t* xa = nullptr;      // fp16 [B][K] input of the next GEMM, row b scaled by 1 / xscale[b]
+    float* xscale = nullptr;     // [B] power-of-two row scales of xa
     float* parts = nullptr;      // GEMM outputs [splits][B][N]
     float* qkv = nullptr;        // [B][qkv_rows]
     float* attn = nullptr;       // [B][NQ * D]
@@ -80,17 +82,44 @@ struct rt_batch {
 
 namespace {
 
-// ---- row kernels (one CTA per sequence row unless stated) ----
+// ---- row kernels (one CTA per sequence row) ----
+
+constexpr int kMaxParts = 8;  // split-K partial products a row kernel adds (gemm_q4k_plan caps splits at 8)
+constexpr int kRowThreads = 512;
+
+// src[i] + src[stride + i] + ... (`parts` <= kMaxParts terms, in part order),
+// every load issued before the first add.
+__device__ __forceinline__ float sum_parts_at(const float* src, int parts, int64_t stride, int64_t i) {
+    float v[kMaxParts];
+#pragma unroll
+    for (int q = 0; q < kMaxParts; ++q) v[q] = q < parts ? src[q * stride + i] : 0.f;
+    float s = v[0];
+#pragma unroll
+    for (int q = 1; q < kMaxParts; ++q)
+        if (q < parts) s += v[q];
+    return s;
+}
+
+// The row's GEMM input: out = fp16(v * 2^-e) for v = row[0..n), oscale[b] = 2^e.
+__device__ __forceinline__ void store_f16_row(const float* row, int n, float mx, float* red, uint16_t* out,
+                                              float* oscale) {
+    mx = rt::block_max(mx, red);
+    float inv, sc;
+    rt::row_scale_f16(mx, &inv, &sc);
+    for (int c = threadIdx.x; c < n; c += blockDim.x) out[c] = __half_as_ushort(__float2half_rn(row[c] * inv));
+    if (threadIdx.x == 0) *oscale = sc;
+}
 
 // Residual update and RMSNorm of one row (the fused prologues of the
 // single-sequence engine, in the same operation order):
 //   embed != null: r = bf16(embed[tokens[b]]) * embed_scale   (src/transformer4.rs:2360-2364)
 //   else:          s = src parts added in order; r = resid_in + s * rms(s) * (1 + gpost)
-//   resid_out = r;  out = bf16(r * rms(r) * (1 + gpre))          (rms_norm_gemma3, src/autograd2.rs:3477-3496)
-__global__ void resid_norm_rows_kernel(const uint16_t* embed, const int32_t* tokens, float embed_scale,
-                                       const float* src, int src_parts, int64_t part_stride, const float* resid_in,
-                                       float* resid_out, const float* gpost, const float* gpre, float eps, int H,
-                                       uint16_t* out) {
+//   resid_out = r;  x = r * rms(r) * (1 + gpre)                 (rms_norm_gemma3, src/autograd2.rs:3477-3496)
+// and x goes out as an fp16 GEMM row with its scale.
+__global__ void __launch_bounds__(kRowThreads) resid_norm_rows_kernel(
+    const uint16_t* embed, const int32_t* tokens, float embed_scale, const float* src, int src_parts,
+    int64_t part_stride, const float* resid_in, float* resid_out, const float* gpost, const float* gpre, float eps, int H,
+    uint16_t* out, float* oscale) {
     extern __shared__ float row[];  // [H]
     __shared__ float red[32];
     const int b = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x;
@@ -107,8 +136,7 @@ __global__ void resid_norm_rows_kernel(const uint16_t* embed, const int32_t* tok
         }
     } else {
         for (int c = tid; c < H; c += nthr) {
-            float s = src[base + c];
-            for (int q = 1; q < src_parts; ++q) s += src[q * part_stride + base + c];
+            const float s = sum_parts_at(src, src_parts, part_stride, base + c);
             row[c] = s;
             ss += s * s;
         }
@@ -124,31 +152,47 @@ __global__ void resid_norm_rows_kernel(const uint16_t* embed, const int32_t* tok
     }
     ss = rt::block_sum(ss, red);
     const float r2 = 1.0f / sqrtf(ss * inv_d + eps);
-    for (int c = tid; c < H; c += nthr)
-        out[base + c] = static_cast<uint16_t>(
-            rt::gcore::bf16_rne(__fmul_rn(__fmul_rn(row[c], r2), __fadd_rn(1.0f, gpre[c]))));
-}
-
-// h[b][j] = bf16(gelu_tanh(gate) * up) from the interleaved gate/up GEMM
-// output (column 2j gate, 2j + 1 up), its split parts added in order.
-// Grid (ceil(F / 256), B).
-__global__ void gelu_rows_kernel(const float* c, int parts, int64_t part_stride, int F, uint16_t* out) {
-    const int b = blockIdx.y;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= F) return;
-    const float* r = c + static_cast<int64_t>(b) * 2 * F;
-    float g = r[2 * j], u = r[2 * j + 1];
-    for (int q = 1; q < parts; ++q) {
-        g += r[q * part_stride + 2 * j];
-        u += r[q * part_stride + 2 * j + 1];
+    float mx = 0.f;
+    for (int c = tid; c < H; c += nthr) {
+        const float x = __fmul_rn(__fmul_rn(row[c], r2), __fadd_rn(1.0f, gpre[c]));
+        row[c] = x;
+        mx = fmaxf(mx, fabsf(x));
     }
-    out[static_cast<int64_t>(b) * F + j] = static_cast<uint16_t>(rt::gcore::bf16_rne(__fmul_rn(rt::gcore::gelu_tanh_dev(g), u)));
+    store_f16_row(row, H, mx, red, out + base, oscale + b);
 }
 
-__global__ void to_bf16_kernel(const float* in, int64_t n, uint16_t* out) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
-        out[i] = static_cast<uint16_t>(rt::gcore::bf16_rne(in[i]));
+// h[b][j] = gelu_tanh(gate) * up from the interleaved gate/up GEMM output
+// (column 2j gate, 2j + 1 up), its split parts added in order; h goes out as an
+// fp16 GEMM row with its scale.  Dynamic shared memory: F floats.
+__global__ void __launch_bounds__(kRowThreads) gelu_rows_kernel(const float* c, int parts, int64_t part_stride, int F,
+                                                                uint16_t* out, float* oscale) {
+    extern __shared__ float h[];  // [F]
+    __shared__ float red[32];
+    const int b = blockIdx.x;
+    const float* r = c + static_cast<int64_t>(b) * 2 * F;
+    float mx = 0.f;
+    for (int j = threadIdx.x; j < F; j += blockDim.x) {
+        const float g = sum_parts_at(r, parts, part_stride, 2 * j), u = sum_parts_at(r, parts, part_stride, 2 * j + 1);
+        const float v = __fmul_rn(rt::gcore::gelu_tanh_dev(g), u);
+        h[j] = v;
+        mx = fmaxf(mx, fabsf(v));
+    }
+    store_f16_row(h, F, mx, red, out + static_cast<int64_t>(b) * F, oscale + b);
+}
+
+// Row b of `in` ([B][n] f32) as an fp16 GEMM row with its scale.  Dynamic
+// shared memory: n floats.
+__global__ void __launch_bounds__(kRowThreads) f16_rows_kernel(const float* in, int n, uint16_t* out, float* oscale) {
+    extern __shared__ float v[];  // [n]
+    __shared__ float red[32];
+    const int b = blockIdx.x;
+    const float* r = in + static_cast<int64_t>(b) * n;
+    float mx = 0.f;
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+        v[c] = r[c];
+        mx = fmaxf(mx, fabsf(v[c]));
+    }
+    store_f16_row(v, n, mx, red, out + static_cast<int64_t>(b) * n, oscale + b);
 }
 
 // Greedy token of each row (largest logit, ties to the higher index), then
@@ -253,20 +297,20 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
         return e == cudaSuccess;
     };
     auto gemm = [&](const BatchGemm& g, float* c) {
-        return ok(rt::gemm_q4k_launch(g.ta, g.tw, c, B, g.n, g.k, g.p, t->ctx->d_err, s));
+        return ok(rt::gemm_q4k_launch(g.ta, g.tw, t->xscale, c, B, g.n, g.k, g.p, t->ctx->d_err, s));
     };
     for (int l = 0; l < t->NL && e == cudaSuccess; ++l) {
         // residual update (or embedding) + attention RMSNorm -> x
         if (l == 0) {
-            resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(d->embed, t->tokens, sqrtf(static_cast<float>(H)), nullptr,
+            resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(d->embed, t->tokens, sqrtf(static_cast<float>(H)), nullptr,
                                                              0, 0, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0),
-                                                             eps, H, t->xa);
+                                                             eps, H, t->xa, t->xscale);
         } else {
             const BatchGemm& gd = t->g_down[l - 1];
-            resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
+            resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
                                                              static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
                                                              rt::norm_ptr(d, l - 1, 3), rt::norm_ptr(d, l, 0), eps, H,
-                                                             t->xa);
+                                                             t->xa, t->xscale);
             p = 1 - p;
         }
         if (!ok(cudaGetLastError())) break;
@@ -309,22 +353,23 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
         a.seq_part = static_cast<int64_t>(t->NKV) * t->nsplit * G * rt::attn_part_stride(D);
         a.seq_out = static_cast<int64_t>(t->NQ) * D;
         if (!ok(rt::attention_launch_batch(a, B, s))) break;
-        const int64_t na = static_cast<int64_t>(B) * t->NQ * D;
-        to_bf16_kernel<<<static_cast<unsigned>(std::min<int64_t>((na + 255) / 256, 4096)), 256, 0, s>>>(t->attn, na, t->xa);
+        f16_rows_kernel<<<B, kRowThreads, sizeof(float) * t->NQ * D, s>>>(t->attn, t->NQ * D, t->xa, t->xscale);
         if (!ok(cudaGetLastError())) break;
         // o, then residual update + pre-FFN RMSNorm
         const BatchGemm& go = t->g_o[l];
         if (!gemm(go, t->parts)) break;
-        resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, go.p.splits,
+        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, go.p.splits,
                                                          static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
-                                                         rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa);
+                                                         rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa,
+                                                         t->xscale);
         p = 1 - p;
         if (!ok(cudaGetLastError())) break;
         // gate/up, GELU gate
         const BatchGemm& gg = t->g_gu[l];
         if (!gemm(gg, t->parts)) break;
-        gelu_rows_kernel<<<dim3((t->F + 255) / 256, B), 256, 0, s>>>(t->parts, gg.p.splits, static_cast<int64_t>(B) * 2 * t->F,
-                                                                     t->F, t->xa);
+        gelu_rows_kernel<<<B, kRowThreads, sizeof(float) * t->F, s>>>(t->parts, gg.p.splits,
+                                                                    static_cast<int64_t>(B) * 2 * t->F, t->F, t->xa,
+                                                                    t->xscale);
         if (!ok(cudaGetLastError())) break;
         // down
         if (!gemm(t->g_down[l], t->parts)) break;
@@ -332,9 +377,10 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
     if (e == cudaSuccess) {
         // final residual update + norm, LM head, greedy tokens
         const BatchGemm& gd = t->g_down[t->NL - 1];
-        resid_norm_rows_kernel<<<B, 256, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
+        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
                                                          static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
-                                                         rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa);
+                                                         rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
+                                                         t->xscale);
         if (ok(cudaGetLastError()) && gemm(t->g_lm, t->logits)) {
             argmax_rows_kernel<<<B, 1024, 0, s>>>(t->logits, t->V, t->tokens, t->pos);
             ok(cudaGetLastError());
@@ -403,6 +449,7 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
     const int64_t B = nseq;
     const int64_t kmax = std::max<int64_t>({t->H, static_cast<int64_t>(t->NQ) * t->D, t->F});
     if ((rc = balloc(t, reinterpret_cast<void**>(&t->xa), sizeof(uint16_t) * B * kmax + 256, "batch GEMM input")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->xscale), sizeof(float) * B, "batch GEMM row scales")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->qkv), sizeof(float) * B * t->qkv_rows, "batch qkv")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->attn), sizeof(float) * B * t->NQ * t->D, "batch attention")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[0]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
@@ -442,8 +489,17 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
     if (rt::gemm_q4k_prepare() != cudaSuccess || rt::attention_prepare() != cudaSuccess)
         return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: kernel attributes"));
     const size_t norm_smem = sizeof(float) * H;
-    if (norm_smem > 48 * 1024 &&
-        cudaFuncSetAttribute(resid_norm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(norm_smem)) != cudaSuccess)
+    auto smem_limit = [](auto kernel, size_t bytes) {
+        return bytes <= 48 * 1024 ||
+               cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) == cudaSuccess;
+    };
+    if (!smem_limit(gelu_rows_kernel, sizeof(float) * t->F) ||
+        !smem_limit(f16_rows_kernel, sizeof(float) * t->NQ * t->D))
+        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: row kernel attributes"));
+    for (const auto* gv : {&t->g_qkv, &t->g_o, &t->g_gu, &t->g_down})
+        for (const BatchGemm& g : *gv)
+            if (g.p.splits > kMaxParts) return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: %d split-K parts", g.p.splits));
+    if (!smem_limit(resid_norm_rows_kernel, norm_smem))
         return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: norm kernel attributes"));
     RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     // capture one step

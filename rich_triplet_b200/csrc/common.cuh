@@ -147,6 +147,18 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Maximum over the whole block; every thread gets it (`red` as for block_sum).
+__device__ __forceinline__ float block_max(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = red[0];
+    for (int i = 1; i < nw; ++i) t = fmaxf(t, red[i]);
+    return t;
+}
+
 // Sum over the whole block; every thread gets the result.  `red` must hold
 // 32 floats of shared memory; blockDim.x is a multiple of 32.
 __device__ __forceinline__ float block_sum(float v, float* red) {

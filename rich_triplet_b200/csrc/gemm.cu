@@ -1,6 +1,7 @@
 // gemm.cu -- Q4_K prefill GEMM on the tcgen05 tensor cores.
 //
-// C[M, N] = A[M, K] . dequant(W[N, K])^T, A bf16, W Q4_K, f32 accumulate
+// C[M, N] = diag(ascale) . A[M, K] . dequant(W[N, K])^T, A fp16 with a
+// power-of-two scale per row, W Q4_K (or bf16), f32 accumulate
 // (Q4KMat::matmul_q4k_t, src/autograd2.rs:1437-1457).
 //
 // One CTA computes a 128 x 128 or 256 x 256 tile of C (one or two M128
@@ -9,22 +10,27 @@
 //   warp 0, lane 0   TMA producer: the A tile of each K-block (2-D tensor
 //                    copy, 128-byte swizzle) and, once per Q4_K super-block
 //                    (four K-blocks), the 128 raw 144-byte blocks of W
-//   warp 1, lane 0   MMA issuer: four tcgen05.mma (M128 N128/256 K16, bf16
+//   warp 1, lane 0   MMA issuer: four tcgen05.mma (M128 N128/256 K16, fp16
 //                    in, f32 accumulator in tensor memory) per K-block and
 //                    accumulator, then a tcgen05.commit that frees the stage
-//   warps 2..9       dequantisers: w = d*sc*q - dmin*m (the Q4_K block
-//                    format, src/autograd2.rs:1003-1085) rounded to bf16 and
-//                    stored in the swizzled K-major layout the MMA reads;
-//                    then they move the accumulators tensor memory ->
-//                    registers -> C
+//   warps 2..9       dequantisers: w = q * (d*sc) - dmin*m (the Q4_K block
+//                    format, src/autograd2.rs:1003-1085) in fp16, stored in
+//                    the swizzled K-major layout the MMA reads (bf16 W tiles
+//                    are converted to fp16 in place instead); then they move
+//                    the accumulators tensor memory -> registers -> C, times
+//                    the row's scale
 // Every mbarrier wait gives up after a second; a CTA that gives up records kErrMbarTimeout,
 // waits (bounded) for its own copies and MMAs in flight, frees its tensor
 // memory and returns.
 //
-// Precision: the MMA takes both operands in one type, and A is bf16, so each
-// dequantised weight (computed in f32 in the reference's order) is rounded to
-// bf16 (relative error <= 2^-9; about 1.6e-3 relative L2 on the product).  The
-// result is the product with those bf16 weights up to f32 summation order.
+// Precision: the MMA takes both operands in one 16-bit type.  fp16 keeps 11
+// significant bits (bf16: 8), so each operand is within 2^-11 relative of its
+// f32 value: about 3e-4 relative L2 on a product, against 2.5e-3 with bf16
+// operands.  fp16's range is kept by scaling each row of A by a power of two
+// (its largest magnitude lands in [2^14, 2^15)), undone exactly in the
+// epilogue.  A dequantised weight is fma(q, fp16(d*sc), fp16(-dmin*m)) with
+// one fp16 rounding; q is exact (0..15).  The result is the product of those
+// fp16 operands up to f32 summation order.
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
 #include <stdlib.h>
 
@@ -37,7 +43,7 @@ namespace rt {
 
 namespace {
 
-constexpr int kBK = 64;                 // K-block: one 128-byte swizzle row of bf16
+constexpr int kBK = 64;                 // K-block: one 128-byte swizzle row of 16-bit elements
 constexpr int kBlockBytes = 144;        // one Q4_K super-block (256 columns) of one row
 constexpr int kKBPerBlock = 256 / kBK;  // K-blocks per super-block
 constexpr int kATile = 128 * kBK * 2;   // the A rows of one accumulator, 16 KB
@@ -60,20 +66,20 @@ struct Cfg {
     static constexpr int kOffB = kOffA + kStages * NACC * kATile;
     static constexpr int kOffRaw = kOffB + kStages * kBTile;
     static constexpr int kOffBar = kOffRaw + kRawStages * kRawTile;
-    static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
+    static constexpr int kNumBars = 4 * kStages + 2 * kRawStages + 1;
     static constexpr int kOffMisc = kOffBar + kNumBars * 8;
     static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + slack for the 1024-byte alignment of the tiles
-    // Instruction descriptor (kind::f16): f32 accumulator, bf16 A and B, both
-    // K-major, N = BN, M = 128.
-    static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
-                                       (static_cast<uint32_t>(128 >> 4) << 24);
+    // Instruction descriptor (kind::f16): f32 accumulator (bits 4-5 = 1), fp16
+    // A and B (bits 7-9 and 10-12 = 0), both K-major, N = BN, M = 128.
+    static constexpr uint32_t kIdesc =
+        (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
     static_assert(kOffB % 1024 == 0 && kOffRaw % 1024 == 0 && kRawTile % 128 == 0, "tile alignment");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory");
     static_assert(kTmemCols <= 512 && (BN == 128 || BN == 256), "tensor memory");
 };
 
 // Shared-memory matrix descriptor of a K-major tile of 64-element (128-byte)
-// bf16 rows in the 128-byte swizzle: 8-row groups 1024 bytes apart (stride
+// 16-bit rows in the 128-byte swizzle: 8-row groups 1024 bytes apart (stride
 // byte offset), descriptor version 1, layout type 2.  `addr` is the start of
 // the K16 slice (tile base + 32 bytes per slice; the tile base is 1024-aligned).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
@@ -81,7 +87,7 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
            (uint64_t{1} << 46) | (uint64_t{2} << 61);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     const uint32_t z = 0;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -132,26 +138,49 @@ __device__ __forceinline__ void st_shared_128(void* p, uint32_t a, uint32_t b, u
                  : "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
     uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
 }
 
-// Byte i of `x` (a value below 16) as a float: 2^23 + q has q in its low bits.
-__device__ __forceinline__ float nib_to_float(uint32_t x, uint32_t i) {
-    return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u | i)) - 8388608.0f;
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
 }
 
-// Eight weights w = d1 * q - m1 (two roundings, the order of
-// Q4KMat::dequantize_row_into, src/autograd2.rs:1326-1366) from the bytes of w0
-// and w1 (one q in each byte), as four bf16 pairs.
-__device__ __forceinline__ float deq(float d1, float q, float m1) { return __fsub_rn(__fmul_rn(d1, q), m1); }
-__device__ __forceinline__ void dequant8(uint32_t w0, uint32_t w1, float d1, float m1, uint32_t (&out)[4]) {
-    out[0] = pack_bf16(deq(d1, nib_to_float(w0, 0), m1), deq(d1, nib_to_float(w0, 1), m1));
-    out[1] = pack_bf16(deq(d1, nib_to_float(w0, 2), m1), deq(d1, nib_to_float(w0, 3), m1));
-    out[2] = pack_bf16(deq(d1, nib_to_float(w1, 0), m1), deq(d1, nib_to_float(w1, 1), m1));
-    out[3] = pack_bf16(deq(d1, nib_to_float(w1, 2), m1), deq(d1, nib_to_float(w1, 3), m1));
+// fp16 bits of x (round to nearest even), twice.
+__device__ __forceinline__ uint32_t f16_pair(float x) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+// Two bf16 values -> the same two values in fp16 (exact in fp16's normal range).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(__uint_as_float(x & 0xFFFF0000u)), "f"(__uint_as_float(x << 16)));
+    return r;
+}
+
+// Sixteen weights from the 8 bytes w0, w1 (16 nibbles): lo[] gets the low
+// nibbles of bytes 0..7 in order as fp16 pairs, w = q * d_lo - m_lo; hi[] the
+// high nibbles, w = q * d_hi - m_hi (dd / nm: the fp16 scale and negated min,
+// twice).  A byte spread into a 16-bit lane and OR-ed into the fp16 pattern of
+// 1024 (ulp 1) holds 1024 + q for its low nibble; its high nibble (q << 4)
+// OR-ed into 64 (ulp 1/16) holds 64 + q.  Subtracting 1024 / 64 is exact, so
+// the one rounding is the fma's.
+__device__ __forceinline__ void dequant16_f16(uint32_t w0, uint32_t w1, uint32_t d_lo, uint32_t nm_lo, uint32_t d_hi,
+                                              uint32_t nm_hi, uint32_t (&lo)[4], uint32_t (&hi)[4]) {
+    constexpr uint32_t k1024 = 0x64006400u, k64 = 0x54005400u;
+    const uint32_t sp[4] = {__byte_perm(w0, 0u, 0x4140u), __byte_perm(w0, 0u, 0x4342u), __byte_perm(w1, 0u, 0x4140u),
+                            __byte_perm(w1, 0u, 0x4342u)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo[i] = h2_fma(h2_sub((sp[i] & 0x000F000Fu) | k1024, k1024), d_lo, nm_lo);
+        hi[i] = h2_fma(h2_sub((sp[i] & 0x00F000F0u) | k64, k64), d_hi, nm_hi);
+    }
 }
 
 // Wait for phase `parity` of `bar`, giving up after one second (globaltimer):
@@ -183,13 +212,15 @@ __device__ __forceinline__ void fail(int* abort_flag, int* err) {
     if (err) atomicExch(err, kErrMbarTimeout);
 }
 
-// WB: W is bf16 [N, K] (copied by TMA into the B tiles; no dequantisation).
-// Split-K: CTA z of the grid's third dimension takes columns [z kps, (z+1) kps)
-// of K and writes its partial product to c + z M N.
+// WB: W is bf16 [N, K] (copied by TMA into the B tiles, then converted to
+// fp16 in place).  ascale: row m of the product is multiplied by ascale[m]
+// (null: 1).  Split-K: CTA z of the grid's third dimension takes columns
+// [z kps, (z+1) kps) of K and writes its partial product to c + z M N.
 template <int NACC, int BN, bool WB>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                    float* __restrict__ c, int64_t M, int64_t N, int K, int kps, int* err) {
+                    const float* __restrict__ ascale, float* __restrict__ c, int64_t M, int64_t N, int K, int kps,
+                    int* err) {
     using C = Cfg<NACC, BN>;
     constexpr int kStages = C::kStages, kRawStages = C::kRawStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -201,7 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* a_full = bars;
     uint64_t* b_full = a_full + kStages;
     uint64_t* empty = b_full + kStages;
-    uint64_t* raw_full = empty + kStages;
+    uint64_t* w_full = empty + kStages;  // WB: the bf16 W tile of the stage has landed
+    uint64_t* raw_full = w_full + kStages;
     uint64_t* raw_empty = raw_full + kRawStages;
     uint64_t* tmem_full = raw_empty + kRawStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::kOffMisc);
@@ -215,8 +247,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&a_full[s], 1);
-            mbar_init(&b_full[s], WB ? 1 : kDeqWarps);
+            mbar_init(&b_full[s], kDeqWarps);
             mbar_init(&empty[s], 1);
+            mbar_init(&w_full[s], 1);
         }
         for (int r = 0; r < kRawStages; ++r) {
             mbar_init(&raw_full[r], 1);
@@ -264,8 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int ac = 0; ac < NACC; ++ac)
                     tma_load_2d(sA + (s * NACC + ac) * kATile, &tm_a, k0 + kb * kBK, m0 + 128 * ac, &a_full[s]);
                 if constexpr (WB) {
-                    mbar_arrive_expect_tx(&b_full[s], C::kBTile);
-                    tma_load_2d(sB + s * C::kBTile, &tm_w, k0 + kb * kBK, n0, &b_full[s]);
+                    mbar_arrive_expect_tx(&w_full[s], C::kBTile);
+                    tma_load_2d(sB + s * C::kBTile, &tm_w, k0 + kb * kBK, n0, &w_full[s]);
                 }
                 ++a_issued[s];
             }
@@ -273,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int s = 0; s < kStages; ++s)
                 if (a_issued[s]) {
                     (void)wait_phase(&a_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
-                    if (WB) (void)wait_phase(&b_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
+                    if (WB) (void)wait_phase(&w_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
                 }
             for (int r = 0; r < kRawStages; ++r)
                 if (raw_issued[r]) (void)wait_phase(&raw_full[r], static_cast<uint32_t>(raw_issued[r] - 1) & 1u);
@@ -295,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_addr = smem_u32(sA + (s * NACC + ac) * kATile);
 #pragma unroll
                     for (int k16 = 0; k16 < kBK / 16; ++k16)
-                        umma_bf16(tmem + static_cast<uint32_t>(ac * BN), sw128_desc(a_addr + 32 * k16),
+                        umma_f16(tmem + static_cast<uint32_t>(ac * BN), sw128_desc(a_addr + 32 * k16),
                                   sw128_desc(b_addr + 32 * k16), C::kIdesc, (kb | k16) != 0);
                 }
                 umma_commit(&empty[s]);
@@ -307,6 +340,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d = threadIdx.x - 64;
         const int n = d / C::kTpr;
         const int h_first = C::kTpr == 2 ? (d & 1) : 0, h_count = C::kTpr == 2 ? 1 : 2;
+        if constexpr (WB) {
+            // bf16 W tile -> fp16 in place (the swizzled layout is the same for
+            // both types); the stage's previous MMA finished before its refill.
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+                const int s = kb % kStages;
+                if (!wait_phase(&w_full[s], static_cast<uint32_t>(kb / kStages) & 1u)) {
+                    fail(abort_flag, err);
+                    break;
+                }
+                uint8_t* tile = sB + s * C::kBTile;
+                for (int ci = d; ci < C::kBTile / 16; ci += kDeqWarps * 32) {
+                    const uint4 v = ld_shared_128(tile + 16 * ci);
+                    st_shared_128(tile + 16 * ci, bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z),
+                                  bf16x2_to_f16x2(v.w));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_full[s]);
+            }
+        }
         for (int kb = 0; kb < (WB ? 0 : nkb); ++kb) {
             if (*reinterpret_cast<volatile int*>(abort_flag)) break;
             const int s = kb % kStages, sb = kb / kKBPerBlock, ch = kb % kKBPerBlock, r = sb % kRawStages;
@@ -342,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float d_lo, m_lo, d_hi, m_hi;
             scale_min(2 * ch, d_lo, m_lo);
             scale_min(2 * ch + 1, d_hi, m_hi);
+            const uint32_t hd_lo = f16_pair(d_lo), hm_lo = f16_pair(-m_lo), hd_hi = f16_pair(d_hi), hm_hi = f16_pair(-m_hi);
             uint8_t* tile = sB + s * C::kBTile + (n >> 3) * 1024 + (n & 7) * 128;
             const int sw = n & 7;
             for (int hh = 0; hh < h_count; ++hh) {
@@ -349,17 +404,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint4 qs = ld_shared_128(row + 16 + 32 * ch + 16 * h);
                 const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {  // 0: low nibbles (columns 16h..), 1: high (32 + 16h..)
-                    const uint32_t mask_shift = half ? 4u : 0u;
-                    const float d1 = half ? d_hi : d_lo, m1 = half ? m_hi : m_lo;
-#pragma unroll
-                    for (int part = 0; part < 2; ++part) {  // 8 columns per 16-byte chunk
-                        uint32_t o[4];
-                        dequant8((q[2 * part] >> mask_shift) & 0x0F0F0F0Fu, (q[2 * part + 1] >> mask_shift) & 0x0F0F0F0Fu,
-                                 d1, m1, o);
-                        const int chunk = half * 4 + 2 * h + part;  // 16-byte chunk of the 128-byte row
-                        st_shared_128(tile + ((chunk ^ sw) << 4), o[0], o[1], o[2], o[3]);
-                    }
+                for (int part = 0; part < 2; ++part) {  // 8 bytes: columns 16h + 8part.. (low), 32 + .. (high)
+                    uint32_t lo[4], hi[4];
+                    dequant16_f16(q[2 * part], q[2 * part + 1], hd_lo, hm_lo, hd_hi, hm_hi, lo, hi);
+                    const int c_lo = 2 * h + part, c_hi = 4 + 2 * h + part;  // 16-byte chunks of the 128-byte row
+                    st_shared_128(tile + ((c_lo ^ sw) << 4), lo[0], lo[1], lo[2], lo[3]);
+                    st_shared_128(tile + ((c_hi ^ sw) << 4), hi[0], hi[1], hi[2], hi[3]);
                 }
             }
             fence_proxy_async_smem();  // the MMA (async proxy) reads these stores; the raw reads precede the TMA refill
@@ -384,6 +434,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int64_t col0 = n0 + 32 * cc;
                 if (rowi < M) {
                     float* crow = c + rowi * N;
+                    const float rs = ascale ? ascale[rowi] : 1.0f;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * rs);
                     if (col0 + 32 <= N && (N & 3) == 0) {
 #pragma unroll
                         for (int i = 0; i < 8; ++i)
@@ -470,16 +523,16 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, c
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
     const cuuint32_t estr[2] = {1, 1};
-    auto bf16_map = [&](CUtensorMap* out, const void* base, int64_t rows, int box_rows) {
+    auto map16 = [&](CUtensorMap* out, CUtensorMapDataType dt, const void* base, int64_t rows, int box_rows) {
         const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
         const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(box_rows)};
-        return encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        return encode(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     };
-    if (!bf16_map(tm_a, a, m, 128)) return false;
-    if (p.wbf16) return bf16_map(tm_w, w, n, p.bn);
+    if (!map16(tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, m, 128)) return false;
+    if (p.wbf16) return map16(tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, n, p.bn);
     const uint64_t row_bytes = static_cast<uint64_t>(k / 256) * kBlockBytes;
     const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(n)};
     const cuuint64_t strides[1] = {row_bytes};
@@ -489,18 +542,37 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, c
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, float* c, int64_t m, int64_t n, int k,
-                            const GemmPlan& p, int* err, cudaStream_t s) {
+cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, const float* ascale, float* c, int64_t m,
+                            int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s) {
     const dim3 g = p.grid;
-    if (p.bm == 256 && !p.wbf16) gemm_q4k_kernel<2, 256, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
-    else if (p.bm == 128 && !p.wbf16) gemm_q4k_kernel<1, 128, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
-    else if (p.bm == 256) gemm_q4k_kernel<2, 256, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
-    else if (p.bm == 128) gemm_q4k_kernel<1, 128, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, c, m, n, k, p.kps, err);
+    if (p.bm == 256 && !p.wbf16)
+        gemm_q4k_kernel<2, 256, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
+    else if (p.bm == 128 && !p.wbf16)
+        gemm_q4k_kernel<1, 128, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
+    else if (p.bm == 256)
+        gemm_q4k_kernel<2, 256, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
+    else if (p.bm == 128)
+        gemm_q4k_kernel<1, 128, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 
 namespace {
+// One CTA per row: out = fp16(a * 2^-e), scale[row] = 2^e (row_scale_f16).
+__global__ void a_to_f16_rows_kernel(const uint16_t* __restrict__ a, int k, uint16_t* __restrict__ out,
+                                     float* __restrict__ scale) {
+    __shared__ float red[32];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * k;
+    float mx = 0.f;
+    for (int c = threadIdx.x; c < k; c += blockDim.x) mx = fmaxf(mx, fabsf(bf16_bits_to_f32(a[base + c])));
+    mx = block_max(mx, red);
+    float inv, sc;
+    row_scale_f16(mx, &inv, &sc);
+    for (int c = threadIdx.x; c < k; c += blockDim.x)
+        out[base + c] = __half_as_ushort(__float2half_rn(bf16_bits_to_f32(a[base + c]) * inv));
+    if (threadIdx.x == 0) scale[blockIdx.x] = sc;
+}
+
 // out[i] = sum over z < parts of in[z * count + i], in part order.
 __global__ void sum_parts_kernel(const float* __restrict__ in, int parts, int64_t count, float* __restrict__ out) {
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -511,6 +583,13 @@ __global__ void sum_parts_kernel(const float* __restrict__ in, int parts, int64_
     }
 }
 }  // namespace
+
+cudaError_t a_to_f16_launch(const uint16_t* a_bf16, int64_t m, int k, uint16_t* out, float* scale, cudaStream_t s) {
+    if (m <= 0) return cudaSuccess;
+    if (m > 0x7FFFFFFF) return cudaErrorInvalidValue;
+    a_to_f16_rows_kernel<<<static_cast<unsigned>(m), 256, 0, s>>>(a_bf16, k, out, scale);
+    return cudaGetLastError();
+}
 
 cudaError_t sum_parts_launch(const float* in, int parts, int64_t count, float* out, int num_sms, cudaStream_t s) {
     if (count <= 0) return cudaSuccess;

@@ -2,17 +2,19 @@
 single-sequence engine and the CPU oracle.
 
 Every sequence of a batch must decode exactly as it would alone: per-step
-logits within REL_L2_BATCH of the single-sequence CUDA engine (itself within
-2e-3 of the oracle), identical greedy tokens, and rows that depend only on
+logits within the tolerances below of the single-sequence CUDA engine (itself
+within 2e-6 of the oracle), identical greedy tokens, and rows that depend only on
 their own sequence (bit-identical rows for identical inputs, outputs that
 follow a permutation of the sequences).
 
-REL_L2_BATCH: the batch engine's projections are tensor-core GEMMs over
-16-bit operands (activations and dequantised Q4_K weights rounded to bf16
-before the product, f32 accumulation).  Each rounding is relative 2^-9; with
-the synthetic weights' mean (about 1.2, so each row's products cancel) one
-projection's output moves by about 2.5e-3 relative, and a 2-layer model's
-logits by up to 4e-2 (measured 3.8e-2 worst over 20 steps).
+Tolerances.  The batch engine's projections are tensor-core GEMMs over fp16
+operands (activation rows scaled by a power of two, dequantised Q4_K weights
+rounded once to fp16; f32 accumulation): each operand is within 2^-11 relative,
+about 3e-4 relative L2 on one projection.  REL_L2 (2e-3) is the north star's
+bar for full-model logits; the full 34-layer 4B model measures 2.9e-4 against
+the single-sequence engine and tiny 3.1e-4 against the oracle.
+REL_L2_REDUCED (5e-3) bounds the 2-layer 4B-width slice, whose logits move
+more under the same operand error (up to 3.5e-3 measured over 20 greedy steps).
 """
 
 import numpy as np
@@ -25,7 +27,8 @@ from rich_triplet_b200.ops import Context
 
 pytestmark = pytest.mark.gpu
 
-REL_L2_BATCH = 6e-2
+REL_L2 = 2e-3
+REL_L2_REDUCED = 5e-3
 TOP2_MARGIN = 0.05  # greedy tokens compared where the single engine's top-2 gap exceeds this
 
 
@@ -89,14 +92,23 @@ def test_batch_matches_single_engine_tiny(ctx, tiny):
     cfg, w = tiny
     # 12 prompt tokens exceed the sliding window (8) on the local layers.
     worst, compared = _vs_singles(ctx, cfg, w, 3, 12, 8)
-    assert worst < REL_L2_BATCH, worst
+    assert worst < REL_L2, worst
     assert compared > 0
 
 
 def test_batch_matches_single_engine_4b_width(ctx, w4b_2l):
     cfg, w = w4b_2l
     worst, compared = _vs_singles(ctx, cfg, w, 3, 6, 4)
-    assert worst < REL_L2_BATCH, worst
+    assert worst < REL_L2_REDUCED, worst
+    assert compared > 0
+
+
+def test_batch_matches_single_engine_full_4b(ctx):
+    # The full 34-layer Gemma 3 4B (synthetic weights): the north star's bar.
+    cfg = Config4.gemma3_4b(vocab_size=262144)
+    w = synth_gemma3(cfg, seed=1234)
+    worst, compared = _vs_singles(ctx, cfg, w, 3, 4, 4)
+    assert worst < REL_L2, worst
     assert compared > 0
 
 
@@ -148,7 +160,9 @@ def test_batch_vs_oracle_tiny(ctx, orc, tiny):
     finally:
         bat.close()
         dec.close()
-    assert worst < REL_L2_BATCH, worst
+        for om in oms:
+            om.close()
+    assert worst < REL_L2, worst
 
 
 def test_batch_synthetic_context_generate(ctx, w4b_2l):
