@@ -11,8 +11,8 @@
 //   rows    residual += post-FFN-norm(down_{l-1}) (embedding * sqrt(H) at l = 0);
 //           x = RMSNorm(residual) -> fp16                      (Gemma3Block, src/transformer4.rs:1954-1964)
 //   GEMM    qkv = x . Wqkv^T
-//   attn    per sequence and KV head: q/k norm + RoPE, KV append, split-context
-//           flash decode (attention.cu, one grid plane per sequence)
+//   attn    per sequence: q/k norm + RoPE and KV append; then per (sequence,
+//           KV head, 256-position chunk) flash decode (attn_batch.cu)
 //   GEMM    o = fp16(attn) . Wo^T
 //   rows    residual += post-attn-norm(o); x = pre-FFN RMSNorm -> fp16
 //   GEMM    gu = x . Wgu^T  (gate/up rows interleaved)
@@ -33,6 +33,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "attn_batch.cuh"
 #include "common.cuh"
 #include "decoder_internal.h"
 #include "gemm.cuh"
@@ -66,7 +67,9 @@ struct rt_batch {
     float* attn = nullptr;       // [B][NQ * D]
     float* resid[2] = {nullptr, nullptr};  // [B][H], ping-pong
     float* logits = nullptr;     // [B][V]
-    float* attn_part = nullptr;  // [B][NKV][nsplit][G][D + 4]
+    float* attn_part = nullptr;  // per-chunk (or per-split) attention states
+    float* q_rot = nullptr;      // [B][NQ][D] rotated queries (chunk path)
+    bool chunk_path = false;     // attn_batch.cu kernels (false: attention.cu, one grid plane per sequence)
     uint32_t* counters = nullptr;  // [B][NKV], zero between launches
     int32_t* tokens = nullptr;   // [B] input token of the next step
     int32_t* pos = nullptr;      // [B] position of the next step
@@ -324,35 +327,77 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
         } else if (!gemm(gq, t->qkv)) {
             break;
         }
-        // attention, one grid plane per sequence
-        rt::AttnArgs a{};
-        a.qkv = t->qkv;
-        a.q_norm = d->qk_norms + static_cast<size_t>(l) * 2 * D;
-        a.k_norm = a.q_norm + D;
-        a.kcache = k_layer(t, l);
-        a.vcache = v_layer(t, l);
+        // attention
         const size_t tab = static_cast<size_t>(t->cap) * (D / 2);
         const int gsel = rt::is_global(l) ? 1 : 0;
-        a.rope_cos = t->rope + (static_cast<size_t>(gsel) * 2 + 0) * tab;
-        a.rope_sin = t->rope + (static_cast<size_t>(gsel) * 2 + 1) * tab;
-        a.pos = t->pos;
-        a.cap = t->cap;
-        a.nq = t->NQ;
-        a.nkv = t->NKV;
-        a.D = D;
-        a.window = rt::is_global(l) ? 0 : d->cfg.sliding_window;
-        a.nsplit = t->nsplit;
-        a.scale = 1.0f / sqrtf(d->cfg.query_pre_attn_scalar);
-        a.eps = eps;
-        a.part = t->attn_part;
-        a.counter = t->counters;
-        a.out = t->attn;
-        a.err = t->ctx->d_err;
-        a.seq_qkv = t->qkv_rows;
-        a.seq_kv = t->seq_kv;
-        a.seq_part = static_cast<int64_t>(t->NKV) * t->nsplit * G * rt::attn_part_stride(D);
-        a.seq_out = static_cast<int64_t>(t->NQ) * D;
-        if (!ok(rt::attention_launch_batch(a, B, s))) break;
+        const float* rope_cos = t->rope + (static_cast<size_t>(gsel) * 2 + 0) * tab;
+        const float* rope_sin = t->rope + (static_cast<size_t>(gsel) * 2 + 1) * tab;
+        const int window = rt::is_global(l) ? 0 : d->cfg.sliding_window;
+        if (t->chunk_path) {
+            rt::AttnRowsArgs pr{};
+            pr.qkv = t->qkv;
+            pr.qkv_stride = t->qkv_rows;
+            pr.q_norm = d->qk_norms + static_cast<size_t>(l) * 2 * D;
+            pr.k_norm = pr.q_norm + D;
+            pr.rope_cos = rope_cos;
+            pr.rope_sin = rope_sin;
+            pr.pos = t->pos;
+            pr.kcache = k_layer(t, l);
+            pr.vcache = v_layer(t, l);
+            pr.seq_kv = t->seq_kv;
+            pr.cap = t->cap;
+            pr.nq = t->NQ;
+            pr.nkv = t->NKV;
+            pr.D = D;
+            pr.eps = eps;
+            pr.q_out = t->q_rot;
+            if (!ok(rt::attn_rows_prep_launch(pr, B, s))) break;
+            rt::AttnChunkArgs ca{};
+            ca.q = t->q_rot;
+            ca.kcache = k_layer(t, l);
+            ca.vcache = v_layer(t, l);
+            ca.seq_kv = t->seq_kv;
+            ca.pos = t->pos;
+            ca.B = B;
+            ca.nq = t->NQ;
+            ca.nkv = t->NKV;
+            ca.D = D;
+            ca.cap = t->cap;
+            ca.window = window;
+            ca.nchunk = rt::attn_chunk_count(t->cap, window);
+            ca.scale = 1.0f / sqrtf(d->cfg.query_pre_attn_scalar);
+            ca.part = t->attn_part;
+            ca.out = t->attn;
+            ca.err = t->ctx->d_err;
+            if (!ok(rt::attn_chunk_launch(ca, t->ctx->num_sms, s))) break;
+        } else {
+            rt::AttnArgs a{};
+            a.qkv = t->qkv;
+            a.q_norm = d->qk_norms + static_cast<size_t>(l) * 2 * D;
+            a.k_norm = a.q_norm + D;
+            a.kcache = k_layer(t, l);
+            a.vcache = v_layer(t, l);
+            a.rope_cos = rope_cos;
+            a.rope_sin = rope_sin;
+            a.pos = t->pos;
+            a.cap = t->cap;
+            a.nq = t->NQ;
+            a.nkv = t->NKV;
+            a.D = D;
+            a.window = window;
+            a.nsplit = t->nsplit;
+            a.scale = 1.0f / sqrtf(d->cfg.query_pre_attn_scalar);
+            a.eps = eps;
+            a.part = t->attn_part;
+            a.counter = t->counters;
+            a.out = t->attn;
+            a.err = t->ctx->d_err;
+            a.seq_qkv = t->qkv_rows;
+            a.seq_kv = t->seq_kv;
+            a.seq_part = static_cast<int64_t>(t->NKV) * t->nsplit * G * rt::attn_part_stride(D);
+            a.seq_out = static_cast<int64_t>(t->NQ) * D;
+            if (!ok(rt::attention_launch_batch(a, B, s))) break;
+        }
         f16_rows_kernel<<<B, kRowThreads, sizeof(float) * t->NQ * D, s>>>(t->attn, t->NQ * D, t->xa, t->xscale);
         if (!ok(cudaGetLastError())) break;
         // o, then residual update + pre-FFN RMSNorm
@@ -447,6 +492,10 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
             return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: upload rope tables"));
     }
     const int64_t B = nseq;
+    t->chunk_path = rt::attn_chunk_supported(t->D, G);
+    const size_t part_floats_attn =
+        t->chunk_path ? rt::attn_chunk_part_floats(nseq, t->NKV, rt::attn_chunk_count(cap, 0), G, t->D)
+                      : static_cast<size_t>(B) * t->NKV * t->nsplit * G * rt::attn_part_stride(t->D);
     const int64_t kmax = std::max<int64_t>({t->H, static_cast<int64_t>(t->NQ) * t->D, t->F});
     if ((rc = balloc(t, reinterpret_cast<void**>(&t->xa), sizeof(uint16_t) * B * kmax + 256, "batch GEMM input")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->xscale), sizeof(float) * B, "batch GEMM row scales")) != RT_OK ||
@@ -455,8 +504,9 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[0]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[1]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->logits), sizeof(float) * B * t->V, "batch logits")) != RT_OK ||
-        (rc = balloc(t, reinterpret_cast<void**>(&t->attn_part),
-                     sizeof(float) * B * t->NKV * t->nsplit * G * rt::attn_part_stride(t->D), "batch attention partials")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->attn_part), sizeof(float) * part_floats_attn, "batch attention partials")) != RT_OK ||
+        (t->chunk_path &&
+         (rc = balloc(t, reinterpret_cast<void**>(&t->q_rot), sizeof(float) * B * t->NQ * t->D, "batch rotated queries")) != RT_OK) ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->counters), sizeof(uint32_t) * B * t->NKV, "batch counters")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->tokens), sizeof(int32_t) * B, "batch tokens")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->pos), sizeof(int32_t) * B, "batch positions")) != RT_OK)
@@ -486,7 +536,8 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
         return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: no GEMM geometry for the LM head"));
     if ((rc = balloc(t, reinterpret_cast<void**>(&t->parts), sizeof(float) * part_floats, "batch GEMM outputs")) != RT_OK)
         return bail(rc);
-    if (rt::gemm_q4k_prepare() != cudaSuccess || rt::attention_prepare() != cudaSuccess)
+    if (rt::gemm_q4k_prepare() != cudaSuccess || rt::attention_prepare() != cudaSuccess ||
+        rt::attn_chunk_prepare() != cudaSuccess)
         return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: kernel attributes"));
     const size_t norm_smem = sizeof(float) * H;
     auto smem_limit = [](auto kernel, size_t bytes) {
