@@ -279,7 +279,9 @@ def run_ours(args):
     # one sequence per rank: the rank's share of `world` independent sequences
     seq0, _ = dp.shard(world, world, rank)
     prompt = synth_tokens(args.seed, dp.prompt_stream(seq0), PROMPT, cfg.vocab_size)
+    t_pf = time.perf_counter()
     last = dec.prefill(prompt)
+    prefill_token_ms = (time.perf_counter() - t_pf) * 1e3
     first = argmax_last(last)
 
     def enqueue(n):
@@ -424,6 +426,23 @@ def run_ours(args):
                          "KV cache copied from the GPU prefill; oracle/ restatement of the reference's x86 path"}
         om.close()
 
+    # ---- prefill of config 1's prompt with every position at once (tensor-core
+    # GEMMs over the 512 tokens), against the token-by-token prefill above ----
+    prefill = None
+    if rank == 0:
+        for _ in range(2):
+            dec.prefill_gemm(prompt, want_logits=False)
+        reps = 5
+        t_pf = time.perf_counter()
+        for _ in range(reps):
+            lg = dec.prefill_gemm(prompt)
+        gemm_ms = (time.perf_counter() - t_pf) * 1e3 / reps
+        prefill = {"tokens": PROMPT, "gemm_ms": gemm_ms, "gemm_tok_s": PROMPT / (gemm_ms / 1e3),
+                   "token_by_token_ms": prefill_token_ms, "token_by_token_tok_s": PROMPT / (prefill_token_ms / 1e3),
+                   "same_greedy_token": argmax_last(lg) == first,
+                   "method": "host wall time of rt_decoder_prefill_gemm (mean of 5 after 2 warm-up, host tokens in, "
+                             "last logits out) vs one rt_decoder_prefill of the same prompt"}
+
     launches = dec.launches_per_step
     # The dominant kernel: the persistent step kernel (one launch per token),
     # or the per-projection GEMVs when the CUDA-graph path is selected.
@@ -450,6 +469,7 @@ def run_ours(args):
             "q4k_gemv_config0": gemv0,
             "q4k_gemm_config2": gemm2,
             "batch_decode_config3": batch3,
+            "prefill_config1": prefill,
         }
         print(json.dumps(line), flush=True)
     dec.close()

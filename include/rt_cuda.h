@@ -226,6 +226,21 @@ int rt_decoder_step(rt_dec* dec, int32_t token, int32_t position, float* logits)
  * (src/transformer4.rs:2103-2164, 2190-2212). */
 int rt_decoder_prefill(rt_dec* dec, const int32_t* tokens, int32_t n, int32_t start_pos, float* last_logits);
 
+/* The same prefill with every position of a piece at once (up to 512 per
+ * piece, longer prompts in order): each projection is one tensor-core GEMM
+ * over the piece's tokens (fp16 operands, f32 accumulation), each token
+ * attends causally to the cache and the piece's earlier tokens, and every
+ * token's K/V lands in the cache as with rt_decoder_prefill.  Writes the last
+ * token's logits (may be NULL).  The GPU counterpart of the reference's CPU
+ * prefill (src/transformer4.rs:2103-2164). */
+int rt_decoder_prefill_gemm(rt_dec* dec, const int32_t* tokens, int32_t n, int32_t start_pos, float* last_logits);
+
+/* m (1..64) consecutive positions start_pos.. of this sequence in one pass,
+ * their K/V appended, logits of all m rows to host `logits` ([m][vocab], may
+ * be NULL): MetalDecodeContext::decode_step_batch (src/metal_decode.rs:
+ * 2079-2579, M <= 8 there), the verify step of speculative decoding. */
+int rt_decoder_step_batch(rt_dec* dec, const int32_t* tokens, int32_t m, int32_t start_pos, float* logits);
+
 /* Greedy decode entirely on the device: step i feeds the argmax of step i-1
  * (largest logit, ties to the higher index) back as its token.  Starts from
  * `first_token` at `start_pos`.  tokens_out (host, may be NULL) receives the n

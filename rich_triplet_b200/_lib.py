@@ -111,6 +111,8 @@ SIGNATURES = {
     "rt_decoder_read_kv": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32]),
     "rt_decoder_step": (ctypes.c_int, [_vp, _i32, _i32, _vp]),
     "rt_decoder_prefill": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
+    "rt_decoder_prefill_gemm": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
+    "rt_decoder_step_batch": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
     "rt_decoder_generate": (ctypes.c_int, [_vp, _i32, _i32, _i32, _vp, ctypes.c_int]),
     "rt_decoder_enqueue_q4k_gemvs": (ctypes.c_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_u64)]),
     "rt_decoder_memory": (ctypes.c_int, [_vp, ctypes.POINTER(_u64)]),

@@ -47,8 +47,18 @@ namespace {
 struct BatchGemm {
     rt::GemmPlan p;
     CUtensorMap ta, tw;
-    int64_t n = 0;
+    const float* ascale = nullptr;  // row scales of A
+    int64_t m = 0, n = 0;
     int k = 0;
+};
+
+// GEMM launches of one step over m rows; the LM head covers rows
+// [lm_row0, lm_row0 + lm_rows) (none if lm_rows == 0).
+struct RowsPlan {
+    int m = 0, lm_row0 = 0, lm_rows = 0;
+    std::vector<BatchGemm> qkv, o, gu, down;
+    BatchGemm lm;
+    int64_t part_floats = 0;  // split-K outputs the plan needs
 };
 
 }  // namespace
@@ -57,16 +67,26 @@ struct rt_batch {
     rt_dec* dec = nullptr;
     rt_ctx* ctx = nullptr;
     int B = 0, cap = 0, H = 0, D = 0, NQ = 0, NKV = 0, F = 0, V = 0, NL = 0, qkv_rows = 0, nsplit = 0;
-    int64_t seq_kv = 0;          // floats of one sequence's caches
-    float* kv = nullptr;         // [B][NL][2 (K, V)][NKV][cap][D]
-    float* rope = nullptr;       // [2 (local, global)][2 (cos, sin)][cap][D/2]
+    // KV caches: layer l's K of row b at kv_k0 + l * kv_lstride + b * seq_kv
+    // ([NKV][cap][D]), V likewise from kv_v0.  Many-sequence mode owns
+    // kv = [B][NL][2 (K, V)][NKV][cap][D]; rows mode (positions of one
+    // sequence) uses the decoder's caches with seq_kv = 0.
+    bool rows_mode = false;
+    int64_t seq_kv = 0;
+    int64_t kv_lstride = 0;
+    float* kv = nullptr;
+    float* kv_k0 = nullptr;
+    float* kv_v0 = nullptr;
+    float* rope = nullptr;       // [2 (local, global)][2 (cos, sin)][cap][D/2] (the decoder's in rows mode)
     uint16_t* xa = nullptr;      // fp16 [B][K] input of the next GEMM, row b scaled by 1 / xscale[b]
     float* xscale = nullptr;     // [B] power-of-two row scales of xa
-    float* parts = nullptr;      // GEMM outputs [splits][B][N]
+    float* parts = nullptr;      // GEMM outputs [splits][rows][N]
+    int64_t part_cap = 0;        // floats allocated at `parts`
     float* qkv = nullptr;        // [B][qkv_rows]
     float* attn = nullptr;       // [B][NQ * D]
     float* resid[2] = {nullptr, nullptr};  // [B][H], ping-pong
-    float* logits = nullptr;     // [B][V]
+    float* logits = nullptr;     // [logit_rows][V]
+    int logit_rows = 0;
     float* attn_part = nullptr;  // per-chunk (or per-split) attention states
     float* q_rot = nullptr;      // [B][NQ][D] rotated queries (chunk path)
     bool chunk_path = false;     // attn_batch.cu kernels (false: attention.cu, one grid plane per sequence)
@@ -74,8 +94,7 @@ struct rt_batch {
     int32_t* tokens = nullptr;   // [B] input token of the next step
     int32_t* pos = nullptr;      // [B] position of the next step
     int* h_err = nullptr;        // pinned copy of the context's error word
-    std::vector<BatchGemm> g_qkv, g_o, g_gu, g_down;
-    BatchGemm g_lm;
+    RowsPlan plan;               // the captured step's (many-sequence mode) or the last call's (rows mode)
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
@@ -89,6 +108,8 @@ namespace {
 
 constexpr int kMaxParts = 8;  // split-K partial products a row kernel adds (gemm_q4k_plan caps splits at 8)
 constexpr int kRowThreads = 512;
+constexpr int kRowsMax = 512;            // rows mode: positions per call (longer prompts run in pieces)
+constexpr int kRowsMaxLogitRows = 64;    // rows mode: rows whose logits one call can return
 
 // src[i] + src[stride + i] + ... (`parts` <= kMaxParts terms, in part order),
 // every load issued before the first add.
@@ -274,21 +295,48 @@ void release(rt_batch* t) {
     delete t;
 }
 
-float* k_layer(rt_batch* t, int l) { return t->kv + static_cast<int64_t>(l) * 2 * t->NKV * t->cap * t->D; }
-float* v_layer(rt_batch* t, int l) { return k_layer(t, l) + static_cast<int64_t>(t->NKV) * t->cap * t->D; }
+float* k_layer(rt_batch* t, int l) { return t->kv_k0 + static_cast<int64_t>(l) * t->kv_lstride; }
+float* v_layer(rt_batch* t, int l) { return t->kv_v0 + static_cast<int64_t>(l) * t->kv_lstride; }
 
-bool make_gemm(rt_batch* t, const void* w, int64_t n, int k, bool wbf16, bool allow_split, BatchGemm* g) {
+// C[m, n] = rows [row0, row0 + m) of xa (K = k) . W^T.
+bool make_gemm(rt_batch* t, int m, int row0, const void* w, int64_t n, int k, bool wbf16, bool allow_split, BatchGemm* g) {
+    g->m = m;
     g->n = n;
     g->k = k;
-    g->p = rt::gemm_q4k_plan(t->B, n, k, t->ctx->num_sms, wbf16, allow_split);
-    if (g->p.bm == 0) return false;
-    return rt::gemm_q4k_tmaps(t->xa, t->B, w, n, k, g->p, &g->ta, &g->tw);
+    g->ascale = t->xscale + row0;
+    g->p = rt::gemm_q4k_plan(m, n, k, t->ctx->num_sms, wbf16, allow_split);
+    if (g->p.bm == 0 || g->p.splits > kMaxParts) return false;
+    return rt::gemm_q4k_tmaps(t->xa + static_cast<int64_t>(row0) * k, m, w, n, k, g->p, &g->ta, &g->tw);
 }
 
-// Enqueue one step (all launches of it) on `s`.
-cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
+bool build_plan(rt_batch* t, int m, int lm_row0, int lm_rows, RowsPlan* pl) {
     rt_dec* d = t->dec;
-    const int B = t->B, H = t->H, D = t->D, G = t->NQ / t->NKV;
+    const int H = t->H;
+    pl->m = m;
+    pl->lm_row0 = lm_row0;
+    pl->lm_rows = lm_rows;
+    pl->qkv.assign(t->NL, BatchGemm{});
+    pl->o.assign(t->NL, BatchGemm{});
+    pl->gu.assign(t->NL, BatchGemm{});
+    pl->down.assign(t->NL, BatchGemm{});
+    pl->part_floats = 0;
+    for (int l = 0; l < t->NL; ++l) {
+        if (!make_gemm(t, m, 0, d->w_qkv[l], t->qkv_rows, H, false, true, &pl->qkv[l]) ||
+            !make_gemm(t, m, 0, d->w_o[l], H, t->NQ * t->D, false, true, &pl->o[l]) ||
+            !make_gemm(t, m, 0, d->w_gu[l], 2LL * t->F, H, false, true, &pl->gu[l]) ||
+            !make_gemm(t, m, 0, d->w_down[l], H, t->F, false, true, &pl->down[l]))
+            return false;
+        for (const BatchGemm* g : {&pl->qkv[l], &pl->o[l], &pl->gu[l], &pl->down[l]})
+            pl->part_floats = std::max<int64_t>(pl->part_floats, static_cast<int64_t>(g->p.splits) * m * g->n);
+    }
+    return lm_rows == 0 || make_gemm(t, lm_rows, lm_row0, d->embed, t->V, H, true, false, &pl->lm);
+}
+
+// Enqueue one step over pl.m rows (all launches of it) on `s`; `argmax`: the
+// greedy token of every row, which also advances its position.
+cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax) {
+    rt_dec* d = t->dec;
+    const int B = pl.m, H = t->H, D = t->D, G = t->NQ / t->NKV;
     const size_t norm_smem = sizeof(float) * H;
     const float eps = d->cfg.rms_norm_eps;
     int p = 0;
@@ -300,7 +348,7 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
         return e == cudaSuccess;
     };
     auto gemm = [&](const BatchGemm& g, float* c) {
-        return ok(rt::gemm_q4k_launch(g.ta, g.tw, t->xscale, c, B, g.n, g.k, g.p, t->ctx->d_err, s));
+        return ok(rt::gemm_q4k_launch(g.ta, g.tw, g.ascale, c, g.m, g.n, g.k, g.p, t->ctx->d_err, s));
     };
     for (int l = 0; l < t->NL && e == cudaSuccess; ++l) {
         // residual update (or embedding) + attention RMSNorm -> x
@@ -309,7 +357,7 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
                                                              0, 0, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0),
                                                              eps, H, t->xa, t->xscale);
         } else {
-            const BatchGemm& gd = t->g_down[l - 1];
+            const BatchGemm& gd = pl.down[l - 1];
             resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
                                                              static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
                                                              rt::norm_ptr(d, l - 1, 3), rt::norm_ptr(d, l, 0), eps, H,
@@ -318,7 +366,7 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
         }
         if (!ok(cudaGetLastError())) break;
         // qkv
-        const BatchGemm& gq = t->g_qkv[l];
+        const BatchGemm& gq = pl.qkv[l];
         if (gq.p.splits > 1) {
             if (!gemm(gq, t->parts)) break;
             if (!ok(rt::sum_parts_launch(t->parts, gq.p.splits, static_cast<int64_t>(B) * t->qkv_rows, t->qkv,
@@ -401,7 +449,7 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
         f16_rows_kernel<<<B, kRowThreads, sizeof(float) * t->NQ * D, s>>>(t->attn, t->NQ * D, t->xa, t->xscale);
         if (!ok(cudaGetLastError())) break;
         // o, then residual update + pre-FFN RMSNorm
-        const BatchGemm& go = t->g_o[l];
+        const BatchGemm& go = pl.o[l];
         if (!gemm(go, t->parts)) break;
         resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, go.p.splits,
                                                          static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
@@ -410,24 +458,24 @@ cudaError_t enqueue(rt_batch* t, cudaStream_t s) {
         p = 1 - p;
         if (!ok(cudaGetLastError())) break;
         // gate/up, GELU gate
-        const BatchGemm& gg = t->g_gu[l];
+        const BatchGemm& gg = pl.gu[l];
         if (!gemm(gg, t->parts)) break;
         gelu_rows_kernel<<<B, kRowThreads, sizeof(float) * t->F, s>>>(t->parts, gg.p.splits,
                                                                     static_cast<int64_t>(B) * 2 * t->F, t->F, t->xa,
                                                                     t->xscale);
         if (!ok(cudaGetLastError())) break;
         // down
-        if (!gemm(t->g_down[l], t->parts)) break;
+        if (!gemm(pl.down[l], t->parts)) break;
     }
-    if (e == cudaSuccess) {
+    if (e == cudaSuccess && pl.lm_rows > 0) {
         // final residual update + norm, LM head, greedy tokens
-        const BatchGemm& gd = t->g_down[t->NL - 1];
+        const BatchGemm& gd = pl.down[t->NL - 1];
         resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
                                                          static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
                                                          rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
                                                          t->xscale);
-        if (ok(cudaGetLastError()) && gemm(t->g_lm, t->logits)) {
-            argmax_rows_kernel<<<B, 1024, 0, s>>>(t->logits, t->V, t->tokens, t->pos);
+        if (ok(cudaGetLastError()) && gemm(pl.lm, t->logits) && argmax) {
+            argmax_rows_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->V, t->tokens, t->pos);
             ok(cudaGetLastError());
         }
     }
@@ -446,21 +494,34 @@ int check_error_word(rt_batch* t) {
     return RT_OK;
 }
 
-}  // namespace
+int grow_parts(rt_batch* t, int64_t floats) {
+    if (floats <= t->part_cap) return RT_OK;
+    if (t->parts) {
+        cudaStreamSynchronize(t->ctx->stream);
+        cudaFree(t->parts);
+        t->allocs.erase(std::find(t->allocs.begin(), t->allocs.end(), static_cast<void*>(t->parts)));
+        t->dev_bytes -= sizeof(float) * t->part_cap;
+        t->parts = nullptr;
+        t->part_cap = 0;
+    }
+    const int rc = balloc(t, reinterpret_cast<void**>(&t->parts), sizeof(float) * floats, "batch GEMM outputs");
+    if (rc == RT_OK) t->part_cap = floats;
+    return rc;
+}
 
-extern "C" {
-
-int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
-    if (!d || !out) return RT_E_INVAL;
-    *out = nullptr;
+// Many-sequence mode: `rows` sequences with their own caches of `cap`
+// positions and one captured step.  Rows mode: up to `rows` positions of the
+// decoder's sequence per call, on the decoder's caches (cap = the decoder's),
+// launched eagerly.
+int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, rt_batch** out) {
     rt_ctx* ctx = d->ctx;
-    if (nseq < 1 || nseq > 1024 || cap < 1) return fail(ctx, RT_E_SHAPE, "rt_batch_create: nseq %d / cap %d", nseq, cap);
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
     rt_batch* t = new rt_batch;
     t->dec = d;
     t->ctx = ctx;
-    t->B = nseq;
-    t->cap = cap;
+    t->rows_mode = rows_mode;
+    t->B = rows;
+    t->cap = rows_mode ? d->cap : cap;
     t->H = d->H;
     t->D = d->D;
     t->NQ = d->NQ;
@@ -470,18 +531,31 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
     t->NL = d->NL;
     t->qkv_rows = d->qkv_rows;
     const int G = t->NQ / t->NKV;
-    // Enough attention items to fill the SMs about four times over.
-    t->nsplit = std::max(1, std::min(64, (4 * ctx->num_sms + nseq * t->NKV - 1) / (nseq * t->NKV)));
+    cap = t->cap;
+    // Enough attention items to fill the SMs about four times over (attention.cu path).
+    t->nsplit = std::max(1, std::min(64, (4 * ctx->num_sms + rows * t->NKV - 1) / (rows * t->NKV)));
+    t->chunk_path = rt::attn_chunk_supported(t->D, G);
     auto bail = [&](int rc) {
         release(t);
         return rc;
     };
+    if (rows_mode && !t->chunk_path)
+        return bail(fail(ctx, RT_E_SHAPE, "rows engine: head_dim %d with %d query heads per KV head is not supported", t->D, G));
     int rc;
-    t->seq_kv = static_cast<int64_t>(t->NL) * 2 * t->NKV * cap * t->D;
-    if ((rc = balloc(t, reinterpret_cast<void**>(&t->kv), sizeof(float) * t->seq_kv * nseq, "batch KV caches")) != RT_OK)
-        return bail(rc);
-    RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->kv, 0, sizeof(float) * t->seq_kv * nseq, ctx->stream));
-    {
+    if (rows_mode) {
+        t->seq_kv = 0;
+        t->kv_lstride = static_cast<int64_t>(t->NKV) * cap * t->D;
+        t->kv_k0 = d->kcache;
+        t->kv_v0 = d->vcache;
+        t->rope = d->rope;
+    } else {
+        t->kv_lstride = 2LL * t->NKV * cap * t->D;
+        t->seq_kv = static_cast<int64_t>(t->NL) * t->kv_lstride;
+        if ((rc = balloc(t, reinterpret_cast<void**>(&t->kv), sizeof(float) * t->seq_kv * rows, "batch KV caches")) != RT_OK)
+            return bail(rc);
+        RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->kv, 0, sizeof(float) * t->seq_kv * rows, ctx->stream));
+        t->kv_k0 = t->kv;
+        t->kv_v0 = t->kv + static_cast<int64_t>(t->NKV) * cap * t->D;
         const size_t tab = static_cast<size_t>(cap) * (t->D / 2);
         std::vector<float> r(4 * tab);
         const rt_gemma3_cfg& c = d->cfg;
@@ -489,12 +563,12 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
         rt::rope_table(c.rope_theta_global, c.rope_freq_scale_global, t->D, cap, &r[2 * tab], &r[3 * tab]);
         if ((rc = balloc(t, reinterpret_cast<void**>(&t->rope), r.size() * 4, "batch rope tables")) != RT_OK) return bail(rc);
         if (cudaMemcpy(t->rope, r.data(), r.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
-            return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: upload rope tables"));
+            return bail(fail(ctx, RT_E_CUDA, "batch engine: upload rope tables"));
     }
-    const int64_t B = nseq;
-    t->chunk_path = rt::attn_chunk_supported(t->D, G);
+    const int64_t B = rows;
+    t->logit_rows = rows_mode ? std::min(rows, kRowsMaxLogitRows) : rows;
     const size_t part_floats_attn =
-        t->chunk_path ? rt::attn_chunk_part_floats(nseq, t->NKV, rt::attn_chunk_count(cap, 0), G, t->D)
+        t->chunk_path ? rt::attn_chunk_part_floats(rows, t->NKV, rt::attn_chunk_count(cap, 0), G, t->D)
                       : static_cast<size_t>(B) * t->NKV * t->nsplit * G * rt::attn_part_stride(t->D);
     const int64_t kmax = std::max<int64_t>({t->H, static_cast<int64_t>(t->NQ) * t->D, t->F});
     if ((rc = balloc(t, reinterpret_cast<void**>(&t->xa), sizeof(uint16_t) * B * kmax + 256, "batch GEMM input")) != RT_OK ||
@@ -503,7 +577,7 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
         (rc = balloc(t, reinterpret_cast<void**>(&t->attn), sizeof(float) * B * t->NQ * t->D, "batch attention")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[0]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[1]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
-        (rc = balloc(t, reinterpret_cast<void**>(&t->logits), sizeof(float) * B * t->V, "batch logits")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->logits), sizeof(float) * t->logit_rows * t->V, "batch logits")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->attn_part), sizeof(float) * part_floats_attn, "batch attention partials")) != RT_OK ||
         (t->chunk_path &&
          (rc = balloc(t, reinterpret_cast<void**>(&t->q_rot), sizeof(float) * B * t->NQ * t->D, "batch rotated queries")) != RT_OK) ||
@@ -516,55 +590,98 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
     RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->pos, 0, sizeof(int32_t) * B, ctx->stream));
     if (cudaMallocHost(reinterpret_cast<void**>(&t->h_err), sizeof(int)) != cudaSuccess) return bail(fail(ctx, RT_E_NOMEM, "pinned error word"));
     *t->h_err = 0;
-    // GEMM plans and tensor maps (A is always xa, read as [B][K])
-    const int64_t H = t->H;
-    t->g_qkv.resize(t->NL);
-    t->g_o.resize(t->NL);
-    t->g_gu.resize(t->NL);
-    t->g_down.resize(t->NL);
-    int64_t part_floats = 0;
-    for (int l = 0; l < t->NL; ++l) {
-        if (!make_gemm(t, d->w_qkv[l], t->qkv_rows, static_cast<int>(H), false, true, &t->g_qkv[l]) ||
-            !make_gemm(t, d->w_o[l], H, t->NQ * t->D, false, true, &t->g_o[l]) ||
-            !make_gemm(t, d->w_gu[l], 2LL * t->F, static_cast<int>(H), false, true, &t->g_gu[l]) ||
-            !make_gemm(t, d->w_down[l], H, t->F, false, true, &t->g_down[l]))
-            return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: no GEMM geometry for layer %d", l));
-        for (const BatchGemm* g : {&t->g_qkv[l], &t->g_o[l], &t->g_gu[l], &t->g_down[l]})
-            part_floats = std::max<int64_t>(part_floats, static_cast<int64_t>(g->p.splits) * B * g->n);
-    }
-    if (!make_gemm(t, d->embed, t->V, static_cast<int>(H), true, false, &t->g_lm))
-        return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: no GEMM geometry for the LM head"));
-    if ((rc = balloc(t, reinterpret_cast<void**>(&t->parts), sizeof(float) * part_floats, "batch GEMM outputs")) != RT_OK)
-        return bail(rc);
     if (rt::gemm_q4k_prepare() != cudaSuccess || rt::attention_prepare() != cudaSuccess ||
         rt::attn_chunk_prepare() != cudaSuccess)
-        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: kernel attributes"));
-    const size_t norm_smem = sizeof(float) * H;
+        return bail(fail(ctx, RT_E_CUDA, "batch engine: kernel attributes"));
     auto smem_limit = [](auto kernel, size_t bytes) {
         return bytes <= 48 * 1024 ||
                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) == cudaSuccess;
     };
-    if (!smem_limit(gelu_rows_kernel, sizeof(float) * t->F) ||
-        !smem_limit(f16_rows_kernel, sizeof(float) * t->NQ * t->D))
-        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: row kernel attributes"));
-    for (const auto* gv : {&t->g_qkv, &t->g_o, &t->g_gu, &t->g_down})
-        for (const BatchGemm& g : *gv)
-            if (g.p.splits > kMaxParts) return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: %d split-K parts", g.p.splits));
-    if (!smem_limit(resid_norm_rows_kernel, norm_smem))
-        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: norm kernel attributes"));
-    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-    // capture one step
-    cudaStream_t s = ctx->stream;
-    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
-        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: begin capture"));
-    const cudaError_t ce = enqueue(t, s);
-    const cudaError_t ee = cudaStreamEndCapture(s, &t->graph);
-    if (ce != cudaSuccess || ee != cudaSuccess || cudaGraphInstantiate(&t->exec, t->graph, 0) != cudaSuccess) {
-        cudaGetLastError();
-        return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: step capture failed (%s)", cudaGetErrorString(ce != cudaSuccess ? ce : ee)));
+    if (!smem_limit(gelu_rows_kernel, sizeof(float) * t->F) || !smem_limit(f16_rows_kernel, sizeof(float) * t->NQ * t->D) ||
+        !smem_limit(resid_norm_rows_kernel, sizeof(float) * t->H))
+        return bail(fail(ctx, RT_E_CUDA, "batch engine: row kernel attributes"));
+    if (!rows_mode) {
+        // the step's GEMM plans and tensor maps (A is xa, read as [B][K]), then its capture
+        if (!build_plan(t, rows, 0, rows, &t->plan)) return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: no GEMM geometry"));
+        if ((rc = grow_parts(t, t->plan.part_floats)) != RT_OK) return bail(rc);
+        RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+        cudaStream_t s = ctx->stream;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+            return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: begin capture"));
+        const cudaError_t ce = enqueue(t, t->plan, s, true);
+        const cudaError_t ee = cudaStreamEndCapture(s, &t->graph);
+        if (ce != cudaSuccess || ee != cudaSuccess || cudaGraphInstantiate(&t->exec, t->graph, 0) != cudaSuccess) {
+            cudaGetLastError();
+            return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: step capture failed (%s)",
+                             cudaGetErrorString(ce != cudaSuccess ? ce : ee)));
+        }
     }
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     *out = t;
     return RT_OK;
+}
+
+// Rows mode: tokens[0..m) at positions start, start + 1, ... through every
+// layer (their K/V appended to the decoder's caches); logits of the last
+// `lm_rows` rows (0: none) to host `logits` ([lm_rows][V]).
+int rows_run(rt_batch* t, const int32_t* tokens, int m, int start, int lm_rows, float* logits) {
+    rt_ctx* ctx = t->ctx;
+    cudaStream_t s = ctx->stream;
+    std::vector<int32_t> pos(m);
+    for (int i = 0; i < m; ++i) pos[i] = start + i;
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(t->tokens, tokens, sizeof(int32_t) * m, cudaMemcpyHostToDevice, s));
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(t->pos, pos.data(), sizeof(int32_t) * m, cudaMemcpyHostToDevice, s));
+    if (t->plan.m != m || t->plan.lm_rows != lm_rows) {
+        if (!build_plan(t, m, m - lm_rows, lm_rows, &t->plan)) {
+            t->plan = RowsPlan{};
+            return fail(ctx, RT_E_SHAPE, "rows engine: no GEMM geometry for %d rows", m);
+        }
+        const int rc = grow_parts(t, t->plan.part_floats);
+        if (rc != RT_OK) {
+            t->plan = RowsPlan{};
+            return rc;
+        }
+    }
+    RT_CHECK_CUDA(ctx, enqueue(t, t->plan, s, false));
+    if (logits && lm_rows > 0)
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(logits, t->logits, sizeof(float) * lm_rows * t->V, cudaMemcpyDeviceToHost, s));
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(t->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(s));
+    return check_error_word(t);
+}
+
+int rows_engine(rt_dec* d, rt_batch** out) {
+    if (!d->rows) {
+        const int rc = create_engine(d, kRowsMax, 0, true, &d->rows);
+        if (rc != RT_OK) return rc;
+    }
+    *out = d->rows;
+    return RT_OK;
+}
+
+int check_rows_args(rt_dec* d, const int32_t* tokens, int32_t n, int32_t start_pos, const char* who) {
+    if (!tokens && n > 0) return fail(d->ctx, RT_E_INVAL, "%s: null tokens", who);
+    if (start_pos < 0 || static_cast<int64_t>(start_pos) + n > d->cap)
+        return fail(d->ctx, RT_E_STATE, "%s: positions %d..%d outside the %d-position cache", who, start_pos,
+                    start_pos + n - 1, d->cap);
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= d->V) return fail(d->ctx, RT_E_INVAL, "%s: token %d out of range", who, tokens[i]);
+    return RT_OK;
+}
+
+}  // namespace
+
+namespace rt {
+void rows_engine_free(rt_batch* t) { release(t); }
+}  // namespace rt
+
+extern "C" {
+
+int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
+    if (!d || !out) return RT_E_INVAL;
+    *out = nullptr;
+    if (nseq < 1 || nseq > 1024 || cap < 1) return fail(d->ctx, RT_E_SHAPE, "rt_batch_create: nseq %d / cap %d", nseq, cap);
+    return create_engine(d, nseq, cap, false, out);
 }
 
 void rt_batch_destroy(rt_batch* t) {
@@ -626,6 +743,32 @@ int rt_batch_info(const rt_batch* t, uint64_t* bytes, int32_t* launches_per_step
     if (bytes) *bytes = t->dev_bytes;
     if (launches_per_step) *launches_per_step = t->launches;
     return RT_OK;
+}
+
+int rt_decoder_prefill_gemm(rt_dec* d, const int32_t* tokens, int32_t n, int32_t start_pos, float* last_logits) {
+    if (!d) return RT_E_INVAL;
+    int rc = check_rows_args(d, tokens, n, start_pos, "rt_decoder_prefill_gemm");
+    if (rc != RT_OK || n <= 0) return n < 0 ? fail(d->ctx, RT_E_SHAPE, "rt_decoder_prefill_gemm: n = %d", n) : rc;
+    rt_batch* t = nullptr;
+    if ((rc = rows_engine(d, &t)) != RT_OK) return rc;
+    for (int off = 0; off < n; off += kRowsMax) {
+        const int m = std::min(kRowsMax, n - off);
+        const bool last = off + m == n;
+        rc = rows_run(t, tokens + off, m, start_pos + off, last && last_logits ? 1 : 0, last ? last_logits : nullptr);
+        if (rc != RT_OK) return rc;
+    }
+    return RT_OK;
+}
+
+int rt_decoder_step_batch(rt_dec* d, const int32_t* tokens, int32_t m, int32_t start_pos, float* logits) {
+    if (!d) return RT_E_INVAL;
+    if (m < 1 || m > kRowsMaxLogitRows)
+        return fail(d->ctx, RT_E_SHAPE, "rt_decoder_step_batch: %d positions (1..%d)", m, kRowsMaxLogitRows);
+    int rc = check_rows_args(d, tokens, m, start_pos, "rt_decoder_step_batch");
+    if (rc != RT_OK) return rc;
+    rt_batch* t = nullptr;
+    if ((rc = rows_engine(d, &t)) != RT_OK) return rc;
+    return rows_run(t, tokens, m, start_pos, logits ? m : 0, logits);
 }
 
 }  // extern "C"

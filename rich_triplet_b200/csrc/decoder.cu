@@ -490,6 +490,7 @@ void rt_decoder_destroy(rt_dec* d) {
     if (!d) return;
     cudaSetDevice(d->ctx->device);
     cudaStreamSynchronize(d->ctx->stream);
+    if (d->rows) rt::rows_engine_free(d->rows);
     if (d->exec) cudaGraphExecDestroy(d->exec);
     if (d->graph) cudaGraphDestroy(d->graph);
     for (void* p : d->allocs) cudaFree(p);

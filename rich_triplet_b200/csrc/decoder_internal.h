@@ -58,6 +58,9 @@ struct rt_dec {
     rt::StepGeom step_geom;
     rt::StepParams step_params{};
     uint64_t dev_bytes = 0;
+    // Positions of this sequence several at a time (prefill, batched verify):
+    // the many-sequence engine in rows mode on these caches, made at first use.
+    rt_batch* rows = nullptr;
     std::vector<void*> allocs;
 };
 
@@ -71,4 +74,9 @@ inline float* norm_ptr(rt_dec* d, int layer, int which) {
     return d->norms + (static_cast<size_t>(layer) * 4 + which) * d->H;
 }
 
+}  // namespace rt
+
+namespace rt {
+// Frees the rows engine of a decoder (batch.cu).
+void rows_engine_free(rt_batch* t);
 }  // namespace rt

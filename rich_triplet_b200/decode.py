@@ -99,6 +99,25 @@ class CudaDecodeContext:
                                        logits.ctypes.data if want_logits else None), self.ctx.h)
         return logits
 
+    def prefill_gemm(self, tokens, start_pos=0, want_logits=True):
+        """Prompt tokens through the engine all positions at once (tensor-core
+        GEMMs over the tokens, causal attention); returns the last token's
+        logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        logits = np.empty(self.lm_head_vocab, dtype=np.float32) if want_logits else None
+        check(lib().rt_decoder_prefill_gemm(self.h, t.ctypes.data, t.size, start_pos,
+                                            logits.ctypes.data if want_logits else None), self.ctx.h)
+        return logits
+
+    def decode_step_batch(self, token_ids, start_position):
+        """Logits [m, vocab] of m consecutive positions in one pass
+        (MetalDecodeContext::decode_step_batch, src/metal_decode.rs:2079)."""
+        t = np.ascontiguousarray(token_ids, dtype=np.int32)
+        logits = np.empty((t.size, self.lm_head_vocab), dtype=np.float32)
+        check(lib().rt_decoder_step_batch(self.h, t.ctypes.data, t.size, start_position, logits.ctypes.data),
+              self.ctx.h)
+        return logits
+
     def generate(self, first_token, start_pos, n):
         """Greedy decode on the device; returns the n argmax tokens."""
         toks = np.empty(n, dtype=np.int32)
