@@ -292,6 +292,23 @@ int rt_batch_step(rt_batch* batch, float* logits, int32_t* next_tokens);
 /* `steps` greedy steps from the current tokens and positions.  RT_DEVICE:
  * enqueue only; RT_HOST: wait and report errors. */
 int rt_batch_generate(rt_batch* batch, int32_t steps, int flags);
+/* Tensor-parallel many-sequence decode (the reference has
+ * no multi-GPU path).  `shard` is this rank's decoder: the model with its
+ * 1/nranks of the query and KV heads and of the FFN columns (a multiple of
+ * 256 each), the full embedding, norms replicated.  Per layer the o and down
+ * outputs are summed over the ranks by an NCCL all-reduce; the LM head covers
+ * this rank's vocab slice (rt_batch_vocab_slice) and the greedy token comes
+ * from an all-gather of every rank's best logit.  Every rank calls this
+ * together with the same nccl_id (rt_nccl_unique_id on one rank, 128 bytes,
+ * shared by the caller; unused when nranks == 1) and then drives the returned
+ * engine with rt_batch_set / rt_batch_step / rt_batch_generate in step. */
+int rt_nccl_unique_id(void* id_out);
+int rt_tp_create(rt_dec* shard, const void* nccl_id, int32_t nranks, int32_t rank, int32_t nseq, int32_t cap,
+                 rt_batch** out);
+/* The vocab rows [v0, v0 + vr) whose logits this engine's steps return (the
+ * whole vocabulary without tensor parallelism). */
+int rt_batch_vocab_slice(const rt_batch* b, int32_t* v0, int32_t* vr);
+
 /* Fill every sequence's cache with synthetic values (a seeded hash, unit
  * variance) and set every position to seq_len: the state a benchmark decodes
  * from without prefilling. */
@@ -307,6 +324,11 @@ int rt_batch_info(const rt_batch* batch, uint64_t* bytes, int32_t* launches_per_
  * Q4KMat::f32_to_f16), 8 scales + 8 mins U{0..63} packed by pack_scales, 128
  * quant bytes U{0..255}.  out: rows*cols/256*144 bytes. */
 void rt_synth_q4k(uint64_t seed, uint64_t stream, int64_t rows, int64_t cols, uint8_t* out);
+/* Rows [row0, row0 + nrows) x columns [col0, col0 + ncols) (multiples of 256)
+ * of rt_synth_q4k(seed, stream, rows, cols) as a Q4_K matrix of its own: the
+ * bytes of slicing the whole matrix, made without it (tensor-parallel shards). */
+void rt_synth_q4k_slice(uint64_t seed, uint64_t stream, int64_t rows, int64_t cols, int64_t row0, int64_t nrows,
+                        int64_t col0, int64_t ncols, uint8_t* out);
 void rt_synth_normal_f32(uint64_t seed, uint64_t stream, int64_t n, float mean, float stddev, float* out);
 /* Normal values rounded to BF16 (round to nearest even). */
 void rt_synth_normal_bf16(uint64_t seed, uint64_t stream, int64_t n, float mean, float stddev, uint16_t* out);

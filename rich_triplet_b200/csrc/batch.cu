@@ -38,6 +38,7 @@
 #include "decoder_internal.h"
 #include "gemm.cuh"
 #include "gemv_core.cuh"
+#include "nccl_dl.h"
 #include "rt_internal.h"
 
 using rt::fail;
@@ -95,6 +96,17 @@ struct rt_batch {
     int32_t* pos = nullptr;      // [B] position of the next step
     int* h_err = nullptr;        // pinned copy of the context's error word
     RowsPlan plan;               // the captured step's (many-sequence mode) or the last call's (rows mode)
+    // Tensor parallelism (nranks > 1): the decoder holds this rank's shard
+    // (its query / KV heads and FFN columns); the o and down outputs are
+    // summed over the ranks (NCCL all-reduce) and the LM head covers vocab
+    // rows [v0, v0 + vr), the greedy token coming from an all-gather of every
+    // rank's best (value, index).
+    int nranks = 1, rank = 0, v0 = 0, vr = 0;
+    const rt::NcclApi* nccl = nullptr;
+    ncclComm_t comm = nullptr;
+    float* ar_buf = nullptr;      // [B][H] summed projection
+    uint32_t* am_send = nullptr;  // [B][2] this rank's best logit: (value bits, vocab index)
+    uint32_t* am_recv = nullptr;  // [nranks][B][2]
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
@@ -259,6 +271,66 @@ __global__ void argmax_rows_kernel(const float* logits, int V, int32_t* tokens, 
     }
 }
 
+// Row b's largest logit of this rank's vocab slice [v0, v0 + V) as (value
+// bits, vocab index), ties to the higher index.  1024 threads per row.
+__global__ void argmax_local_kernel(const float* logits, int V, int v0, uint32_t* out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* r = logits + static_cast<int64_t>(b) * V;
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int i = tid; i < V; i += blockDim.x) {
+        const float v = r[i];
+        if (v > bv || (v == bv && i > bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi > bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] > bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        out[2 * b] = __float_as_uint(bv);
+        out[2 * b + 1] = static_cast<uint32_t>(v0 + bi);
+    }
+}
+
+// The greedy token of each row from every rank's (value, index) pair (ranks'
+// slices in vocab order; ties to the higher index), then tokens[b] = it and
+// pos[b] += 1.
+__global__ void argmax_merge_kernel(const uint32_t* pairs, int nranks, int B, int32_t* tokens, int32_t* pos) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int r = 0; r < nranks; ++r) {
+        const float v = __uint_as_float(pairs[(static_cast<int64_t>(r) * B + b) * 2]);
+        const int i = static_cast<int>(pairs[(static_cast<int64_t>(r) * B + b) * 2 + 1]);
+        if (v > bv || (v == bv && i > bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    tokens[b] = bi;
+    pos[b] += 1;
+}
+
 // Synthetic cache contents for benchmarks: a hash of (seed, index) mapped to
 // a uniform value of unit variance.
 __global__ void synth_kv_kernel(float* kv, int64_t n, uint64_t seed) {
@@ -290,6 +362,7 @@ void release(rt_batch* t) {
     if (!t) return;
     if (t->exec) cudaGraphExecDestroy(t->exec);
     if (t->graph) cudaGraphDestroy(t->graph);
+    if (t->comm && t->nccl) t->nccl->comm_destroy(t->comm);  // after the graphs that hold its calls
     for (void* p : t->allocs) cudaFree(p);
     if (t->h_err) cudaFreeHost(t->h_err);
     delete t;
@@ -329,7 +402,8 @@ bool build_plan(rt_batch* t, int m, int lm_row0, int lm_rows, RowsPlan* pl) {
         for (const BatchGemm* g : {&pl->qkv[l], &pl->o[l], &pl->gu[l], &pl->down[l]})
             pl->part_floats = std::max<int64_t>(pl->part_floats, static_cast<int64_t>(g->p.splits) * m * g->n);
     }
-    return lm_rows == 0 || make_gemm(t, lm_rows, lm_row0, d->embed, t->V, H, true, false, &pl->lm);
+    return lm_rows == 0 ||
+           make_gemm(t, lm_rows, lm_row0, d->embed + static_cast<int64_t>(t->v0) * H, t->vr, H, true, false, &pl->lm);
 }
 
 // Enqueue one step over pl.m rows (all launches of it) on `s`; `argmax`: the
@@ -350,6 +424,26 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
     auto gemm = [&](const BatchGemm& g, float* c) {
         return ok(rt::gemm_q4k_launch(g.ta, g.tw, g.ascale, c, g.m, g.n, g.k, g.p, t->ctx->d_err, s));
     };
+    auto nccl_ok = [&](ncclResult_t r) { return ok(r == ncclSuccess ? cudaSuccess : cudaErrorUnknown); };
+    // A row-split projection's output as a row kernel reads it: (source,
+    // split parts, part stride).  With several ranks the parts are added and
+    // the sum is all-reduced over the ranks into ar_buf.
+    struct Proj {
+        const float* src = nullptr;
+        int parts = 1;
+        int64_t stride = 0;
+    };
+    auto project = [&](const BatchGemm& g) -> Proj {
+        const int64_t count = static_cast<int64_t>(B) * g.n;
+        if (t->nranks == 1) return gemm(g, t->parts) ? Proj{t->parts, g.p.splits, count} : Proj{};
+        if (!gemm(g, g.p.splits > 1 ? t->parts : t->ar_buf)) return Proj{};
+        if (g.p.splits > 1 && !ok(rt::sum_parts_launch(t->parts, g.p.splits, count, t->ar_buf, t->ctx->num_sms, s)))
+            return Proj{};
+        if (!nccl_ok(t->nccl->all_reduce(t->ar_buf, t->ar_buf, static_cast<size_t>(count), ncclFloat32, ncclSum, t->comm, s)))
+            return Proj{};
+        return Proj{t->ar_buf, 1, count};
+    };
+    Proj pdown;  // the previous layer's down projection
     for (int l = 0; l < t->NL && e == cudaSuccess; ++l) {
         // residual update (or embedding) + attention RMSNorm -> x
         if (l == 0) {
@@ -357,9 +451,8 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
                                                              0, 0, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0),
                                                              eps, H, t->xa, t->xscale);
         } else {
-            const BatchGemm& gd = pl.down[l - 1];
-            resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
-                                                             static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
+            resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, pdown.src, pdown.parts,
+                                                             pdown.stride, t->resid[p], t->resid[1 - p],
                                                              rt::norm_ptr(d, l - 1, 3), rt::norm_ptr(d, l, 0), eps, H,
                                                              t->xa, t->xscale);
             p = 1 - p;
@@ -449,10 +542,10 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         f16_rows_kernel<<<B, kRowThreads, sizeof(float) * t->NQ * D, s>>>(t->attn, t->NQ * D, t->xa, t->xscale);
         if (!ok(cudaGetLastError())) break;
         // o, then residual update + pre-FFN RMSNorm
-        const BatchGemm& go = pl.o[l];
-        if (!gemm(go, t->parts)) break;
-        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, go.p.splits,
-                                                         static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
+        const Proj po = project(pl.o[l]);
+        if (!po.src) break;
+        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, po.src, po.parts, po.stride,
+                                                         t->resid[p], t->resid[1 - p],
                                                          rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa,
                                                          t->xscale);
         p = 1 - p;
@@ -465,18 +558,29 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
                                                                     t->xscale);
         if (!ok(cudaGetLastError())) break;
         // down
-        if (!gemm(pl.down[l], t->parts)) break;
+        pdown = project(pl.down[l]);
+        if (!pdown.src) break;
     }
     if (e == cudaSuccess && pl.lm_rows > 0) {
         // final residual update + norm, LM head, greedy tokens
-        const BatchGemm& gd = pl.down[t->NL - 1];
-        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, t->parts, gd.p.splits,
-                                                         static_cast<int64_t>(B) * H, t->resid[p], t->resid[1 - p],
+        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, pdown.src, pdown.parts,
+                                                         pdown.stride, t->resid[p], t->resid[1 - p],
                                                          rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
                                                          t->xscale);
         if (ok(cudaGetLastError()) && gemm(pl.lm, t->logits) && argmax) {
-            argmax_rows_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->V, t->tokens, t->pos);
-            ok(cudaGetLastError());
+            if (t->nranks == 1) {
+                argmax_rows_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->vr, t->tokens, t->pos);
+                ok(cudaGetLastError());
+            } else {
+                argmax_local_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->vr, t->v0, t->am_send);
+                if (ok(cudaGetLastError()) &&
+                    nccl_ok(t->nccl->all_gather(t->am_send, t->am_recv, 2 * static_cast<size_t>(pl.lm_rows), ncclUint32,
+                                                t->comm, s))) {
+                    argmax_merge_kernel<<<(pl.lm_rows + 127) / 128, 128, 0, s>>>(t->am_recv, t->nranks, pl.lm_rows,
+                                                                                 t->tokens, t->pos);
+                    ok(cudaGetLastError());
+                }
+            }
         }
     }
     t->launches = n;
@@ -509,11 +613,17 @@ int grow_parts(rt_batch* t, int64_t floats) {
     return rc;
 }
 
+// Tensor-parallel set-up of a many-sequence engine (nranks 1: none).
+struct TpInit {
+    int nranks = 1, rank = 0;
+    ncclUniqueId id{};
+};
+
 // Many-sequence mode: `rows` sequences with their own caches of `cap`
-// positions and one captured step.  Rows mode: up to `rows` positions of the
-// decoder's sequence per call, on the decoder's caches (cap = the decoder's),
-// launched eagerly.
-int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, rt_batch** out) {
+// positions and one captured step (on `tp->nranks` GPUs, this rank's shard).
+// Rows mode: up to `rows` positions of the decoder's sequence per call, on
+// the decoder's caches (cap = the decoder's), launched eagerly.
+int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, const TpInit* tp, rt_batch** out) {
     rt_ctx* ctx = d->ctx;
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
     rt_batch* t = new rt_batch;
@@ -532,6 +642,10 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, rt_batch** out) 
     t->qkv_rows = d->qkv_rows;
     const int G = t->NQ / t->NKV;
     cap = t->cap;
+    t->nranks = tp ? tp->nranks : 1;
+    t->rank = tp ? tp->rank : 0;
+    t->v0 = static_cast<int>(static_cast<int64_t>(t->V) * t->rank / t->nranks);
+    t->vr = static_cast<int>(static_cast<int64_t>(t->V) * (t->rank + 1) / t->nranks) - t->v0;
     // Enough attention items to fill the SMs about four times over (attention.cu path).
     t->nsplit = std::max(1, std::min(64, (4 * ctx->num_sms + rows * t->NKV - 1) / (rows * t->NKV)));
     t->chunk_path = rt::attn_chunk_supported(t->D, G);
@@ -577,7 +691,7 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, rt_batch** out) 
         (rc = balloc(t, reinterpret_cast<void**>(&t->attn), sizeof(float) * B * t->NQ * t->D, "batch attention")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[0]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[1]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||
-        (rc = balloc(t, reinterpret_cast<void**>(&t->logits), sizeof(float) * t->logit_rows * t->V, "batch logits")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->logits), sizeof(float) * t->logit_rows * t->vr, "batch logits")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->attn_part), sizeof(float) * part_floats_attn, "batch attention partials")) != RT_OK ||
         (t->chunk_path &&
          (rc = balloc(t, reinterpret_cast<void**>(&t->q_rot), sizeof(float) * B * t->NQ * t->D, "batch rotated queries")) != RT_OK) ||
@@ -590,6 +704,20 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, rt_batch** out) 
     RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->pos, 0, sizeof(int32_t) * B, ctx->stream));
     if (cudaMallocHost(reinterpret_cast<void**>(&t->h_err), sizeof(int)) != cudaSuccess) return bail(fail(ctx, RT_E_NOMEM, "pinned error word"));
     *t->h_err = 0;
+    if (t->nranks > 1) {
+        const char* why = nullptr;
+        if (!(t->nccl = rt::nccl_api(&why))) return bail(fail(ctx, RT_E_CUDA, "tensor parallel: NCCL unavailable (%s)", why));
+        if ((rc = balloc(t, reinterpret_cast<void**>(&t->ar_buf), sizeof(float) * B * t->H, "tp all-reduce buffer")) != RT_OK ||
+            (rc = balloc(t, reinterpret_cast<void**>(&t->am_send), sizeof(uint32_t) * 2 * B, "tp argmax pairs")) != RT_OK ||
+            (rc = balloc(t, reinterpret_cast<void**>(&t->am_recv), sizeof(uint32_t) * 2 * B * t->nranks, "tp argmax pairs")) != RT_OK)
+            return bail(rc);
+        RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+        const ncclResult_t nr = t->nccl->comm_init_rank(&t->comm, t->nranks, tp->id, t->rank);
+        if (nr != ncclSuccess) {
+            t->comm = nullptr;
+            return bail(fail(ctx, RT_E_CUDA, "tensor parallel: ncclCommInitRank: %s", t->nccl->error_string(nr)));
+        }
+    }
     if (rt::gemm_q4k_prepare() != cudaSuccess || rt::attention_prepare() != cudaSuccess ||
         rt::attn_chunk_prepare() != cudaSuccess)
         return bail(fail(ctx, RT_E_CUDA, "batch engine: kernel attributes"));
@@ -644,7 +772,7 @@ int rows_run(rt_batch* t, const int32_t* tokens, int m, int start, int lm_rows, 
     }
     RT_CHECK_CUDA(ctx, enqueue(t, t->plan, s, false));
     if (logits && lm_rows > 0)
-        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(logits, t->logits, sizeof(float) * lm_rows * t->V, cudaMemcpyDeviceToHost, s));
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(logits, t->logits, sizeof(float) * lm_rows * t->vr, cudaMemcpyDeviceToHost, s));
     RT_CHECK_CUDA(ctx, cudaMemcpyAsync(t->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     RT_CHECK_CUDA(ctx, cudaStreamSynchronize(s));
     return check_error_word(t);
@@ -652,7 +780,7 @@ int rows_run(rt_batch* t, const int32_t* tokens, int m, int start, int lm_rows, 
 
 int rows_engine(rt_dec* d, rt_batch** out) {
     if (!d->rows) {
-        const int rc = create_engine(d, kRowsMax, 0, true, &d->rows);
+        const int rc = create_engine(d, kRowsMax, 0, true, nullptr, &d->rows);
         if (rc != RT_OK) return rc;
     }
     *out = d->rows;
@@ -681,7 +809,7 @@ int rt_batch_create(rt_dec* d, int32_t nseq, int32_t cap, rt_batch** out) {
     if (!d || !out) return RT_E_INVAL;
     *out = nullptr;
     if (nseq < 1 || nseq > 1024 || cap < 1) return fail(d->ctx, RT_E_SHAPE, "rt_batch_create: nseq %d / cap %d", nseq, cap);
-    return create_engine(d, nseq, cap, false, out);
+    return create_engine(d, nseq, cap, false, nullptr, out);
 }
 
 void rt_batch_destroy(rt_batch* t) {
@@ -709,7 +837,7 @@ int rt_batch_step(rt_batch* t, float* logits, int32_t* next_tokens) {
     cudaStream_t s = t->ctx->stream;
     RT_CHECK_CUDA(t->ctx, cudaGraphLaunch(t->exec, s));
     if (logits)
-        RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(logits, t->logits, sizeof(float) * t->B * t->V, cudaMemcpyDeviceToHost, s));
+        RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(logits, t->logits, sizeof(float) * t->B * t->vr, cudaMemcpyDeviceToHost, s));
     if (next_tokens)
         RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(next_tokens, t->tokens, sizeof(int32_t) * t->B, cudaMemcpyDeviceToHost, s));
     RT_CHECK_CUDA(t->ctx, cudaMemcpyAsync(t->h_err, t->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -742,6 +870,37 @@ int rt_batch_info(const rt_batch* t, uint64_t* bytes, int32_t* launches_per_step
     if (!t) return RT_E_INVAL;
     if (bytes) *bytes = t->dev_bytes;
     if (launches_per_step) *launches_per_step = t->launches;
+    return RT_OK;
+}
+
+int rt_nccl_unique_id(void* id_out) {
+    if (!id_out) return RT_E_INVAL;
+    const char* why = nullptr;
+    const rt::NcclApi* api = rt::nccl_api(&why);
+    if (!api) return RT_E_CUDA;
+    ncclUniqueId id;
+    if (api->get_unique_id(&id) != ncclSuccess) return RT_E_CUDA;
+    memcpy(id_out, &id, sizeof(id));
+    return RT_OK;
+}
+
+int rt_tp_create(rt_dec* shard, const void* nccl_id, int32_t nranks, int32_t rank, int32_t nseq, int32_t cap,
+                 rt_batch** out) {
+    if (!shard || !out || (nranks > 1 && !nccl_id)) return shard ? fail(shard->ctx, RT_E_INVAL, "rt_tp_create: null argument") : RT_E_INVAL;
+    *out = nullptr;
+    if (nranks < 1 || rank < 0 || rank >= nranks || nseq < 1 || nseq > 1024 || cap < 1)
+        return fail(shard->ctx, RT_E_SHAPE, "rt_tp_create: nranks %d rank %d nseq %d cap %d", nranks, rank, nseq, cap);
+    TpInit tp;
+    tp.nranks = nranks;
+    tp.rank = rank;
+    if (nranks > 1) memcpy(&tp.id, nccl_id, sizeof(tp.id));
+    return create_engine(shard, nseq, cap, false, &tp, out);
+}
+
+int rt_batch_vocab_slice(const rt_batch* t, int32_t* v0, int32_t* vr) {
+    if (!t) return RT_E_INVAL;
+    if (v0) *v0 = t->v0;
+    if (vr) *vr = t->vr;
     return RT_OK;
 }
 

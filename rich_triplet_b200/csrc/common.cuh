@@ -107,7 +107,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 
 // 2-D tiled TMA load (tensor map in the kernel's parameter space) completing on `bar`.
-// No multicast.  x is the innermost coordinate in elements of the map.
+// Into this CTA's shared memory only.  x is the innermost coordinate in elements of the map.
 __device__ __forceinline__ void tma_2d_g2s(void* dst, const void* tmap, int x, int y, uint64_t* bar, uint64_t policy) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(

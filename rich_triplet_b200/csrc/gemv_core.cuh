@@ -8,7 +8,7 @@
 // one contiguous, equal share of that sequence, so all warps stream the same
 // number of bytes whatever the shape.  A warp copies its units HBM -> shared
 // memory itself: lane 0 issues one 2-D TMA tensor copy per unit (8-byte
-// elements, box = unit width x 16 rows, no multicast) into a private ring of
+// elements, box = unit width x 16 rows, one destination CTA) into a private ring of
 // `nb` buffers, each completed on its own mbarrier (bounded waits).  A warp's
 // stream runs through a list of GEMVs ("jobs") back to back: the copies of the
 // next job's first units are issued as soon as ring slots free up, before that

@@ -85,6 +85,36 @@ inline float normal_at(uint64_t key, uint64_t i) {
     return static_cast<float>(sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2));
 }
 
+// Block `blk` (row-major block index of the whole matrix) of the seeded Q4_K
+// matrix: BASELINE config 0's distributions.
+void synth_q4k_block(uint64_t key, int64_t blk, uint8_t* o) {
+    const uint64_t base = static_cast<uint64_t>(blk) * 20;
+    const uint64_t r0 = draw(key, base);
+    const float d = 1e-3f + 9e-3f * unit(r0);
+    const float dmin = 5e-3f * unit(draw(key, base + 1));
+    const uint16_t d16 = f32_to_f16_trunc(d), m16 = f32_to_f16_trunc(dmin);
+    o[0] = static_cast<uint8_t>(d16 & 0xFF);
+    o[1] = static_cast<uint8_t>(d16 >> 8);
+    o[2] = static_cast<uint8_t>(m16 & 0xFF);
+    o[3] = static_cast<uint8_t>(m16 >> 8);
+    // 8 scales + 8 mins, 6 bits each, then pack_scales (src/autograd2.rs:1119-1132).
+    const uint64_t r2 = draw(key, base + 2), r3 = draw(key, base + 3);
+    uint8_t sv[8], mv[8];
+    for (int j = 0; j < 8; ++j) {
+        sv[j] = static_cast<uint8_t>((r2 >> (6 * j)) & 63u);
+        mv[j] = static_cast<uint8_t>((r3 >> (6 * j)) & 63u);
+    }
+    for (int j = 0; j < 4; ++j) {
+        o[4 + j] = static_cast<uint8_t>((sv[j] & 0x3F) | ((sv[j + 4] & 0x30) << 2));
+        o[8 + j] = static_cast<uint8_t>((mv[j] & 0x3F) | ((mv[j + 4] & 0x30) << 2));
+        o[12 + j] = static_cast<uint8_t>((sv[j + 4] & 0x0F) | ((mv[j + 4] & 0x0F) << 4));
+    }
+    for (int w = 0; w < 16; ++w) {
+        const uint64_t r = draw(key, base + 4 + w);
+        memcpy(o + 16 + 8 * w, &r, 8);
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -93,33 +123,22 @@ void rt_synth_q4k(uint64_t seed, uint64_t stream, int64_t rows, int64_t cols, ui
     const int64_t nblk = rows * (cols / 256);
     const uint64_t key = key_of(seed, stream);
     parallel_for(nblk, [&](int64_t a, int64_t b) {
-        for (int64_t blk = a; blk < b; ++blk) {
-            uint8_t* o = out + blk * 144;
-            const uint64_t base = static_cast<uint64_t>(blk) * 20;
-            const uint64_t r0 = draw(key, base);
-            const float d = 1e-3f + 9e-3f * unit(r0);
-            const float dmin = 5e-3f * unit(draw(key, base + 1));
-            const uint16_t d16 = f32_to_f16_trunc(d), m16 = f32_to_f16_trunc(dmin);
-            o[0] = static_cast<uint8_t>(d16 & 0xFF);
-            o[1] = static_cast<uint8_t>(d16 >> 8);
-            o[2] = static_cast<uint8_t>(m16 & 0xFF);
-            o[3] = static_cast<uint8_t>(m16 >> 8);
-            // 8 scales + 8 mins, 6 bits each, then pack_scales (src/autograd2.rs:1119-1132).
-            const uint64_t r2 = draw(key, base + 2), r3 = draw(key, base + 3);
-            uint8_t sv[8], mv[8];
-            for (int j = 0; j < 8; ++j) {
-                sv[j] = static_cast<uint8_t>((r2 >> (6 * j)) & 63u);
-                mv[j] = static_cast<uint8_t>((r3 >> (6 * j)) & 63u);
-            }
-            for (int j = 0; j < 4; ++j) {
-                o[4 + j] = static_cast<uint8_t>((sv[j] & 0x3F) | ((sv[j + 4] & 0x30) << 2));
-                o[8 + j] = static_cast<uint8_t>((mv[j] & 0x3F) | ((mv[j + 4] & 0x30) << 2));
-                o[12 + j] = static_cast<uint8_t>((sv[j + 4] & 0x0F) | ((mv[j + 4] & 0x0F) << 4));
-            }
-            for (int w = 0; w < 16; ++w) {
-                const uint64_t r = draw(key, base + 4 + w);
-                memcpy(o + 16 + 8 * w, &r, 8);
-            }
+        for (int64_t blk = a; blk < b; ++blk) synth_q4k_block(key, blk, out + blk * 144);
+    });
+}
+
+// Rows [row0, row0 + nrows) x columns [col0, col0 + ncols) (multiples of 256)
+// of the matrix rt_synth_q4k(seed, stream, rows, cols) makes, as a Q4_K
+// matrix of its own: the same bytes as slicing the whole one.
+void rt_synth_q4k_slice(uint64_t seed, uint64_t stream, int64_t rows, int64_t cols, int64_t row0, int64_t nrows,
+                        int64_t col0, int64_t ncols, uint8_t* out) {
+    (void)rows;
+    const int64_t nb = cols / 256, b0 = col0 / 256, nbs = ncols / 256;
+    const uint64_t key = key_of(seed, stream);
+    parallel_for(nrows * nbs, [&](int64_t a, int64_t b) {
+        for (int64_t i = a; i < b; ++i) {
+            const int64_t r = row0 + i / nbs, c = b0 + i % nbs;
+            synth_q4k_block(key, r * nb + c, out + i * 144);
         }
     });
 }

@@ -169,7 +169,7 @@ class CudaBatchDecoder:
     """Many-sequence decode on the weights of a
     CudaDecodeContext: `nseq` independent sequences, each with its own f32 KV
     cache of `cap` positions, advance together; every projection is one
-    tensor-core GEMM over the sequences (bf16 activations, f32 accumulation).
+    tensor-core GEMM over the sequences (fp16 operands, f32 accumulation).
     The reference decodes one sequence at a time; this has no counterpart
     there (its decode_step_batch, src/metal_decode.rs:2079, batches positions
     of one sequence)."""
