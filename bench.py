@@ -43,6 +43,7 @@ def parse():
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--layers", type=int, default=34, help="model depth (34 = Gemma 3 4B)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-config4", action="store_true", help="skip the 27B tensor-parallel section")
     p.add_argument("--cpu-steps", type=int, default=3)
     p.add_argument("--prompt", type=int, default=PROMPT,
                    help="prompt tokens prefilled before the timed steps (512 = BASELINE config 1; "
@@ -241,6 +242,114 @@ def batch_decode_config3(args, cfg, dec, ctx, ext, world, rank, dist, device, hb
     }
 
 
+CONFIG4_CONTEXT, CONFIG4_STEPS, CONFIG4_BATCHES = 8192, 16, (1, 8)
+
+
+def tp_step_bytes(cfg, nranks, rank, context, nseq):
+    """Bytes one tensor-parallel step must move on `rank`: its Q4_K shard, its
+    slice of the BF16 LM head, and its KV heads' rows at `context`."""
+    from rich_triplet_b200.tp import shard_config
+
+    sc = shard_config(cfg, nranks, rank)
+    H, D = cfg.hidden_size, cfg.head_dim
+    q, kv, f = sc.num_attention_heads * D, sc.num_key_value_heads * D, sc.intermediate_size
+    per_layer = (q * H + 2 * kv * H + H * q + 3 * f * H) // 256 * 144
+    vr = cfg.vocab_size * (rank + 1) // nranks - cfg.vocab_size * rank // nranks
+    kv_bytes = 0
+    for layer in range(cfg.num_hidden_layers):
+        n = context + 1
+        if not cfg.is_global_layer(layer) and cfg.sliding_window:
+            n = min(n, cfg.sliding_window)
+        kv_bytes += 2 * kv * 4 * n
+    return cfg.num_hidden_layers * per_layer + vr * H * 2 + nseq * kv_bytes
+
+
+def all_ok(flag, dist, device):
+    """True on every rank iff `flag` is true on every rank."""
+    if dist is None:
+        return bool(flag)
+    import torch
+
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def tp_decode_config4(args, world, rank, dist, device, hbm_peak):
+    """Gemma 3 27B (synthetic weights), tensor parallel over
+    the job's ranks, batch 1 and 8, each sequence at an 8192-token synthetic
+    f32 KV cache; greedy steps timed with CUDA events, max over ranks."""
+    import torch
+
+    from rich_triplet_b200 import dp
+    from rich_triplet_b200.decode import CudaDecodeContext
+    from rich_triplet_b200.model import Config4
+    from rich_triplet_b200.ops import Context
+    from rich_triplet_b200.tp import TpBatchDecoder, share_nccl_id, synth_shard_weights
+
+    cfg = Config4.gemma3_27b()
+    out = {"model": "gemma3-27b (62 layers, hidden 5376, FFN 21504, 32/16 heads of 128), synthetic Q4_K weights",
+           "parallelism": f"tp{world}: heads and FFN columns split, NCCL all-reduce after o and down, vocab-split LM head",
+           "context": CONFIG4_CONTEXT, "steps": CONFIG4_STEPS, "kv": "f32, synthetic contents (no prefill)",
+           "gemm_operands": "fp16, f32 accumulation"}
+    ctx = dec = None
+    err = None
+    try:
+        ctx = Context(device)
+        t0 = time.perf_counter()
+        dec = CudaDecodeContext(synth_shard_weights(cfg, args.seed, world, rank), 16, ctx)
+        out["setup_s"] = time.perf_counter() - t0
+    except Exception as e:  # reported in the line; every rank learns of it below
+        err = f"{type(e).__name__}: {e}"
+    if not all_ok(err is None, dist, device):
+        out["error"] = err or "another rank failed to build its shard"
+        if dec is not None:
+            dec.close()
+        if ctx is not None:
+            ctx.close()
+        return out
+    ext = torch.cuda.ExternalStream(ctx.stream_ptr)
+    warm = 3
+    for nseq in CONFIG4_BATCHES:
+        nccl_id = share_nccl_id(dist, rank) if world > 1 else None
+        bat = None
+        try:
+            bat = TpBatchDecoder(dec, nseq, CONFIG4_CONTEXT + warm + CONFIG4_STEPS + 1, world, rank, nccl_id)
+            bat.synth_kv(args.seed + rank, CONFIG4_CONTEXT)
+        except Exception as e:
+            err = f"{type(e).__name__}: {e}"
+        if not all_ok(err is None, dist, device):
+            out[f"batch{nseq}"] = {"error": err or "another rank failed"}
+            if bat is not None:
+                bat.close()
+            break
+        bat.generate(warm)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        bat.generate(CONFIG4_STEPS, wait=False)
+        e1.record(ext)
+        e1.synchronize()
+        ctx.sync()
+        ms = e0.elapsed_time(e1)
+        mem, launches = bat.info()
+        bat.close()
+        ms_max = dp.max_over_ranks(ms, dist, device)
+        per_step = sum(tp_step_bytes(cfg, world, rank, CONFIG4_CONTEXT + warm + i, nseq)
+                       for i in range(CONFIG4_STEPS)) / CONFIG4_STEPS
+        gbs = per_step * CONFIG4_STEPS / (ms / 1e3) / 1e9
+        out[f"batch{nseq}"] = {"value": dp.job_rate(nseq * CONFIG4_STEPS, ms_max), "unit": "tok/s",
+                               "ms_per_step": ms_max / CONFIG4_STEPS, "hbm_gbs_rank0": gbs, "frac": gbs / hbm_peak,
+                               "bytes_per_step_rank0": per_step, "device_bytes_engine_rank0": mem,
+                               "launches_per_step": launches, "all_reduces_per_step": 2 * cfg.num_hidden_layers
+                               if world > 1 else 0}
+    dec.close()
+    ctx.close()
+    return out
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -348,6 +457,9 @@ def run_ours(args):
     # sequence over the ranks, 128 greedy steps each (synthetic f32 caches) ----
     batch3 = batch_decode_config3(args, cfg, dec, ctx, ext, world, rank, dist, device, hbm_peak,
                                   w.q4k_bytes() + cfg.vocab_size * cfg.hidden_size * 2)
+
+    # ---- Gemma 3 27B tensor parallel over the ranks ----
+    tp4 = tp_decode_config4(args, world, rank, dist, device, hbm_peak) if not args.no_config4 else None
 
     # ---- standalone Q4_K GEMV, CUDA graph of 256 chained
     # launches rotating over 16 weight copies (236 MB > L2) ----
@@ -470,6 +582,7 @@ def run_ours(args):
             "q4k_gemm_config2": gemm2,
             "batch_decode_config3": batch3,
             "prefill_config1": prefill,
+            "tp_decode_config4": tp4,
         }
         print(json.dumps(line), flush=True)
     dec.close()

@@ -608,8 +608,18 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
     d->p_gu = rt::gemv_plan(rt::kQ4K, 2LL * d->F, H, 2, rt::kProResidNorm, rt::kEpiGeluPair, ctx->num_sms, 1);
     d->p_down = rt::gemv_plan(rt::kQ4K, H, d->F, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 1);
     d->p_lm = rt::gemv_plan(rt::kBF16, d->V, H, 1, rt::kProResidNorm, rt::kEpiArgmax, ctx->num_sms, 1);
-    if (!d->p_qkv.warps || !d->p_o.warps || !d->p_gu.warps || !d->p_down.warps || !d->p_lm.warps)
-        return bail(fail(ctx, RT_E_SHAPE, "rt_decoder_create: no GEMV geometry for these shapes"));
+    // Without GEMV geometry for these shapes the decoder holds the weights,
+    // caches and tables for the GEMM-based engines (rows mode, many-sequence,
+    // tensor-parallel shards) and refuses the single-sequence calls.
+    d->single = d->p_qkv.warps && d->p_o.warps && d->p_gu.warps && d->p_down.warps && d->p_lm.warps;
+    if (!d->single) {
+        if (cudaMallocHost(reinterpret_cast<void**>(&d->h_err), sizeof(int) * 4) != cudaSuccess)
+            return bail(fail(ctx, RT_E_NOMEM, "pinned staging"));
+        *d->h_err = 0;
+        if (cudaStreamSynchronize(s) != cudaSuccess) return bail(fail(ctx, RT_E_CUDA, "rt_decoder_create: set-up failed"));
+        *out = d;
+        return RT_OK;
+    }
     d->t_qkv.resize(NL);
     d->t_o.resize(NL);
     d->t_gu.resize(NL);
@@ -714,6 +724,7 @@ int rt_decoder_read_kv(rt_dec* d, int32_t layer, float* k, float* v, int32_t seq
 
 int rt_decoder_step(rt_dec* d, int32_t token, int32_t position, float* logits) {
     if (!d) return RT_E_INVAL;
+    if (!d->single) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_step: no single-sequence path for these shapes");
     if (token < 0 || token >= d->V) return fail(d->ctx, RT_E_INVAL, "rt_decoder_step: token %d out of range", token);
     if (position < 0 || position >= d->cap)
         return fail(d->ctx, RT_E_STATE, "rt_decoder_step: position %d outside the %d-position cache", position, d->cap);
@@ -728,6 +739,7 @@ int rt_decoder_step(rt_dec* d, int32_t token, int32_t position, float* logits) {
 
 int rt_decoder_prefill(rt_dec* d, const int32_t* tokens, int32_t n, int32_t start_pos, float* last_logits) {
     if (!d || (!tokens && n > 0)) return fail(d ? d->ctx : nullptr, RT_E_INVAL, "rt_decoder_prefill: null argument");
+    if (!d->single) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_prefill: no single-sequence path for these shapes");
     if (n <= 0) return RT_OK;
     if (start_pos < 0 || static_cast<int64_t>(start_pos) + n > d->cap)
         return fail(d->ctx, RT_E_STATE, "rt_decoder_prefill: positions %d..%d outside the cache", start_pos, start_pos + n - 1);
@@ -746,6 +758,7 @@ int rt_decoder_prefill(rt_dec* d, const int32_t* tokens, int32_t n, int32_t star
 
 int rt_decoder_generate(rt_dec* d, int32_t first_token, int32_t start_pos, int32_t n, int32_t* tokens_out, int flags) {
     if (!d) return RT_E_INVAL;
+    if (!d->single) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_generate: no single-sequence path for these shapes");
     if (flags != RT_HOST && flags != RT_DEVICE) return fail(d->ctx, RT_E_INVAL, "rt_decoder_generate: bad flags");
     if (flags == RT_DEVICE && tokens_out) return fail(d->ctx, RT_E_INVAL, "rt_decoder_generate: RT_DEVICE takes no tokens_out");
     if (first_token < 0 || first_token >= d->V) return fail(d->ctx, RT_E_INVAL, "rt_decoder_generate: token out of range");
@@ -765,6 +778,7 @@ int rt_decoder_generate(rt_dec* d, int32_t first_token, int32_t start_pos, int32
 
 int rt_decoder_enqueue_q4k_gemvs(rt_dec* d, int32_t* n_launches, uint64_t* bytes) {
     if (!d) return RT_E_INVAL;
+    if (!d->single) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_enqueue_q4k_gemvs: no single-sequence path for these shapes");
     RT_CHECK_CUDA(d->ctx, enqueue_step(d, d->ctx->stream, false, true, n_launches, bytes));
     return RT_OK;
 }
@@ -783,6 +797,7 @@ int rt_decoder_launches_per_step(const rt_dec* d, int32_t* n) {
 
 int rt_decoder_read_activation(rt_dec* d, int32_t which, float* host, int64_t count) {
     if (!d || !host) return RT_E_INVAL;
+    if (!d->single) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_read_activation: no single-sequence path for these shapes");
     const float* src = nullptr;
     int64_t n = 0;
     if (which == 0) {

@@ -54,6 +54,7 @@ struct rt_dec {
     // The persistent step kernel (one cooperative launch per step), when the
     // shapes fit it; otherwise the captured graph of per-projection kernels.
     bool use_step = false;
+    bool single = false;  // the single-sequence path (GEMV plans, step kernel or graph) exists
     int step_grid = 0;
     rt::StepGeom step_geom;
     rt::StepParams step_params{};
