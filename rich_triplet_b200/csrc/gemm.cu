@@ -13,7 +13,8 @@
 //   warp 1, lane 0   MMA issuer: four tcgen05.mma (M128 N128/256 K16, fp16
 //                    in, f32 accumulator in tensor memory) per K-block and
 //                    accumulator, then a tcgen05.commit that frees the stage
-//   warps 2..9       dequantisers: w = q * (d*sc) - dmin*m (the Q4_K block
+//   warps 2..17      dequantisers, two groups of 8 taking alternate K-blocks
+//                    (two K-blocks in flight): w = q * (d*sc) - dmin*m (the Q4_K block
 //                    format, src/autograd2.rs:1003-1085) in fp16, stored in
 //                    the swizzled K-major layout the MMA reads (bf16 W tiles
 //                    are converted to fp16 in place instead); then they move
@@ -46,24 +47,37 @@ namespace {
 constexpr int kBK = 64;                 // K-block: one 128-byte swizzle row of 16-bit elements
 constexpr int kBlockBytes = 144;        // one Q4_K super-block (256 columns) of one row
 constexpr int kKBPerBlock = 256 / kBK;  // K-blocks per super-block
-constexpr int kATile = 128 * kBK * 2;   // the A rows of one accumulator, 16 KB
-constexpr int kDeqWarps = 8;
+constexpr int kDeqGroups = 2;                    // dequantiser groups: group g takes K-blocks g, g + 2, ...
+constexpr int kGroupWarps = 8;                   // warps per group (one stage is filled by one group)
+constexpr int kDeqWarps = kDeqGroups * kGroupWarps;
 constexpr int kThreads = (2 + kDeqWarps) * 32;
 
 // Tile configuration: NACC accumulators of M128 x N=BN stacked along M (CTA
 // tile 128 NACC x BN; NACC * BN tensor-memory columns).  Larger tiles read A
 // fewer times (N / BN) and dequantise W fewer times (M / (128 NACC)).
-template <int NACC, int BN>
+// AROWS < 128 (one accumulator, M <= AROWS): the operands swap roles.  The
+// dequantised W tile is the MMA's A operand (M = 128 weight rows) and the
+// AROWS rows of activations its B operand (N = AROWS), so the accumulator is
+// C^T (tensor-memory lane = weight row, column = activation row).  Each MMA
+// then reads 4 KB of weights and AROWS x 32 bytes of activations from shared
+// memory instead of 128 rows of each; at small M the product is bound by
+// that shared-memory traffic.  The smaller A stages also buy a deeper ring.
+template <int NACC, int BN, int AROWS = 128>
 struct Cfg {
     static constexpr int kBM = 128 * NACC;
+    static constexpr int kATileC = AROWS * kBK * 2;  // one accumulator's A stage
     static constexpr int kBTile = BN * kBK * 2;
     static constexpr int kRawTile = BN * kBlockBytes;
-    static constexpr int kStages = NACC * BN >= 512 ? 2 : 4;  // A / B ring
-    static constexpr int kRawStages = BN >= 256 ? 2 : 3;      // raw W super-block ring
-    static constexpr int kTmemCols = NACC * BN;
+    // Swapped (small M): two CTAs per SM, so each gets about half of the
+    // shared memory.
+    static constexpr int kStages = AROWS == 16 ? 4 : AROWS == 64 ? 3 : (NACC * BN >= 512 ? 2 : 4);  // A / B ring
+    static constexpr int kRawStages = (BN >= 256 || AROWS < 128) ? 2 : 4;  // raw W super-block ring
+    static constexpr int kCtasPerSm = AROWS < 128 ? 2 : 1;
+    static constexpr bool kSwap = AROWS < 128;
+    static constexpr int kTmemCols = kSwap ? (AROWS < 32 ? 32 : AROWS) : NACC * BN;
     static constexpr int kTpr = 256 / BN;  // dequantiser threads per W row
     static constexpr int kOffA = 0;
-    static constexpr int kOffB = kOffA + kStages * NACC * kATile;
+    static constexpr int kOffB = kOffA + kStages * NACC * kATileC;
     static constexpr int kOffRaw = kOffB + kStages * kBTile;
     static constexpr int kOffBar = kOffRaw + kRawStages * kRawTile;
     static constexpr int kNumBars = 4 * kStages + 2 * kRawStages + 1;
@@ -71,10 +85,14 @@ struct Cfg {
     static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + slack for the 1024-byte alignment of the tiles
     // Instruction descriptor (kind::f16): f32 accumulator (bits 4-5 = 1), fp16
     // A and B (bits 7-9 and 10-12 = 0), both K-major, N = BN, M = 128.
+    // (Swapped: M = BN weight rows, N = AROWS activation rows.)
     static constexpr uint32_t kIdesc =
-        (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
-    static_assert(kOffB % 1024 == 0 && kOffRaw % 1024 == 0 && kRawTile % 128 == 0, "tile alignment");
-    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+        (1u << 4) | (static_cast<uint32_t>((kSwap ? AROWS : BN) >> 3) << 17) |
+        (static_cast<uint32_t>((kSwap ? BN : 128) >> 4) << 24);
+    static_assert(kOffB % 1024 == 0 && kOffRaw % 1024 == 0 && kRawTile % 128 == 0 && kATileC % 1024 == 0, "tile alignment");
+    static_assert(AROWS == 128 || (NACC == 1 && BN == 128 && AROWS % 16 == 0), "swapped operands: one M128 accumulator");
+    static_assert(kTmemCols >= 32 && (kTmemCols & (kTmemCols - 1)) == 0 && kTmemCols <= 512, "tensor memory allocation");
+    static_assert(kSmemBytes * kCtasPerSm <= 227 * 1024, "shared memory");
     static_assert(kTmemCols <= 512 && (BN == 128 || BN == 256), "tensor memory");
 };
 
@@ -183,12 +201,13 @@ __device__ __forceinline__ void dequant16_f16(uint32_t w0, uint32_t w1, uint32_t
     }
 }
 
-// Wait for phase `parity` of `bar`, giving up after one second (globaltimer):
-// a CTA that stalls ends within seconds, with its error recorded.
+// Wait for phase `parity` of `bar`, giving up after about one second
+// (globaltimer, first read after 1024 polls so that short waits never pay
+// for it): a CTA that stalls ends within seconds, with its error recorded.
 __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity) {
     const uint32_t addr = smem_u32(bar);
     uint64_t t0 = 0;
-    for (uint32_t it = 0;; ++it) {
+    for (uint32_t it = 1;; ++it) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -198,13 +217,26 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity) {
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if ((it & 63u) == 0u) {
+        if ((it & 1023u) == 0u) {
             uint64_t t;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-            if (it == 0) t0 = t;
+            if (it == 1024u) t0 = t;
             else if (t - t0 > 1000000000ull) return false;
         }
     }
+}
+
+// True if phase `parity` of `bar` has completed (no waiting).
+__device__ __forceinline__ bool test_phase(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
 }
 
 __device__ __forceinline__ void fail(int* abort_flag, int* err) {
@@ -216,12 +248,12 @@ __device__ __forceinline__ void fail(int* abort_flag, int* err) {
 // fp16 in place).  ascale: row m of the product is multiplied by ascale[m]
 // (null: 1).  Split-K: CTA z of the grid's third dimension takes columns
 // [z kps, (z+1) kps) of K and writes its partial product to c + z M N.
-template <int NACC, int BN, bool WB>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NACC, int BN, bool WB, int AROWS>
+__global__ void __launch_bounds__(kThreads, Cfg<NACC, BN, AROWS>::kCtasPerSm)
     gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                     const float* __restrict__ ascale, float* __restrict__ c, int64_t M, int64_t N, int K, int kps,
                     int* err) {
-    using C = Cfg<NACC, BN>;
+    using C = Cfg<NACC, BN, AROWS>;
     constexpr int kStages = C::kStages, kRawStages = C::kRawStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
@@ -247,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&a_full[s], 1);
-            mbar_init(&b_full[s], kDeqWarps);
+            mbar_init(&b_full[s], kGroupWarps);
             mbar_init(&empty[s], 1);
             mbar_init(&w_full[s], 1);
         }
@@ -274,42 +306,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer ----
-            int a_issued[kStages] = {}, raw_issued[kRawStages] = {};
+            // Raw W super-blocks run ahead of the A/B stages as far as their
+            // ring allows: the one a K-block needs is waited for, the next
+            // ones are issued whenever a ring slot has been released.
+            int kb_issued = 0;  // K-blocks whose A (and bf16 W) copies were issued
+            const int nsb = WB ? 0 : nkb / kKBPerBlock;
+            int sb_next = 0;  // next raw super-block to issue
+            auto issue_raw = [&](bool block) -> int {  // 1 issued, 0 slot busy, -1 gave up
+                const int r = sb_next % kRawStages;
+                if (sb_next >= kRawStages) {
+                    const uint32_t par = static_cast<uint32_t>(sb_next / kRawStages - 1) & 1u;
+                    if (!block && !test_phase(&raw_empty[r], par)) return 0;
+                    if (block && !wait_phase(&raw_empty[r], par)) return -1;
+                }
+                mbar_arrive_expect_tx(&raw_full[r], C::kRawTile);
+                tma_load_2d(sRaw + r * C::kRawTile, &tm_w, (k0 / 256 + sb_next) * (kBlockBytes / 8), n0, &raw_full[r]);
+                ++sb_next;
+                return 1;
+            };
             for (int kb = 0; kb < nkb; ++kb) {
                 if (*reinterpret_cast<volatile int*>(abort_flag)) break;
-                const int s = kb % kStages, sb = kb / kKBPerBlock;
-                if (!WB && kb % kKBPerBlock == 0) {
-                    const int r = sb % kRawStages;
-                    if (sb >= kRawStages && !wait_phase(&raw_empty[r], static_cast<uint32_t>(sb / kRawStages - 1) & 1u)) {
+                const int s = kb % kStages;
+                if (!WB) {
+                    bool gave_up = false;
+                    while (sb_next <= kb / kKBPerBlock)
+                        if (issue_raw(true) < 0) {
+                            gave_up = true;
+                            break;
+                        }
+                    if (gave_up) {
                         fail(abort_flag, err);
                         break;
                     }
-                    mbar_arrive_expect_tx(&raw_full[r], C::kRawTile);
-                    tma_load_2d(sRaw + r * C::kRawTile, &tm_w, (k0 / 256 + sb) * (kBlockBytes / 8), n0, &raw_full[r]);
-                    ++raw_issued[r];
+                    while (sb_next < nsb && issue_raw(false) > 0) {
+                    }
                 }
                 if (kb >= kStages && !wait_phase(&empty[s], static_cast<uint32_t>(kb / kStages - 1) & 1u)) {
                     fail(abort_flag, err);
                     break;
                 }
-                mbar_arrive_expect_tx(&a_full[s], NACC * kATile);
+                mbar_arrive_expect_tx(&a_full[s], NACC * C::kATileC);
 #pragma unroll
                 for (int ac = 0; ac < NACC; ++ac)
-                    tma_load_2d(sA + (s * NACC + ac) * kATile, &tm_a, k0 + kb * kBK, m0 + 128 * ac, &a_full[s]);
+                    tma_load_2d(sA + (s * NACC + ac) * C::kATileC, &tm_a, k0 + kb * kBK, m0 + 128 * ac, &a_full[s]);
                 if constexpr (WB) {
                     mbar_arrive_expect_tx(&w_full[s], C::kBTile);
                     tma_load_2d(sB + s * C::kBTile, &tm_w, k0 + kb * kBK, n0, &w_full[s]);
                 }
-                ++a_issued[s];
+                ++kb_issued;
             }
-            // No copy of this CTA may still be landing when it exits.
-            for (int s = 0; s < kStages; ++s)
-                if (a_issued[s]) {
-                    (void)wait_phase(&a_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
-                    if (WB) (void)wait_phase(&w_full[s], static_cast<uint32_t>(a_issued[s] - 1) & 1u);
-                }
-            for (int r = 0; r < kRawStages; ++r)
-                if (raw_issued[r]) (void)wait_phase(&raw_full[r], static_cast<uint32_t>(raw_issued[r] - 1) & 1u);
+            // No copy of this CTA may still be landing when it exits: the last
+            // copy into each stage (K-block / super-block i of a ring of n
+            // slots completes phase i / n of slot i % n).
+            for (int i = kb_issued > kStages ? kb_issued - kStages : 0; i < kb_issued; ++i) {
+                (void)wait_phase(&a_full[i % kStages], static_cast<uint32_t>(i / kStages) & 1u);
+                if (WB) (void)wait_phase(&w_full[i % kStages], static_cast<uint32_t>(i / kStages) & 1u);
+            }
+            for (int i = sb_next > kRawStages ? sb_next - kRawStages : 0; i < sb_next; ++i)
+                (void)wait_phase(&raw_full[i % kRawStages], static_cast<uint32_t>(i / kRawStages) & 1u);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -323,9 +377,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t b_addr = smem_u32(sB + s * C::kBTile);
+                if constexpr (C::kSwap) {
+                    const uint32_t x_addr = smem_u32(sA + s * C::kATileC);
 #pragma unroll
-                for (int ac = 0; ac < NACC; ++ac) {
-                    const uint32_t a_addr = smem_u32(sA + (s * NACC + ac) * kATile);
+                    for (int k16 = 0; k16 < kBK / 16; ++k16)
+                        umma_f16(tmem, sw128_desc(b_addr + 32 * k16), sw128_desc(x_addr + 32 * k16), C::kIdesc,
+                                 (kb | k16) != 0);
+                }
+#pragma unroll
+                for (int ac = 0; ac < (C::kSwap ? 0 : NACC); ++ac) {
+                    const uint32_t a_addr = smem_u32(sA + (s * NACC + ac) * C::kATileC);
 #pragma unroll
                     for (int k16 = 0; k16 < kBK / 16; ++k16)
                         umma_f16(tmem + static_cast<uint32_t>(ac * BN), sw128_desc(a_addr + 32 * k16),
@@ -337,13 +398,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---- dequantisers: W row n of the tile; halves h0.. of each 64-column K-block ----
-        const int d = threadIdx.x - 64;
+        const int dgrp = (warp - 2) / kGroupWarps;
+        const int d = threadIdx.x - 64 - dgrp * kGroupWarps * 32;  // thread of the group
         const int n = d / C::kTpr;
         const int h_first = C::kTpr == 2 ? (d & 1) : 0, h_count = C::kTpr == 2 ? 1 : 2;
         if constexpr (WB) {
             // bf16 W tile -> fp16 in place (the swizzled layout is the same for
             // both types); the stage's previous MMA finished before its refill.
-            for (int kb = 0; kb < nkb; ++kb) {
+            for (int kb = dgrp; kb < nkb; kb += kDeqGroups) {
                 if (*reinterpret_cast<volatile int*>(abort_flag)) break;
                 const int s = kb % kStages;
                 if (!wait_phase(&w_full[s], static_cast<uint32_t>(kb / kStages) & 1u)) {
@@ -351,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 uint8_t* tile = sB + s * C::kBTile;
-                for (int ci = d; ci < C::kBTile / 16; ci += kDeqWarps * 32) {
+                for (int ci = d; ci < C::kBTile / 16; ci += kGroupWarps * 32) {
                     const uint4 v = ld_shared_128(tile + 16 * ci);
                     st_shared_128(tile + 16 * ci, bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z),
                                   bf16x2_to_f16x2(v.w));
@@ -361,10 +423,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&b_full[s]);
             }
         }
-        for (int kb = 0; kb < (WB ? 0 : nkb); ++kb) {
+        for (int kb = dgrp; kb < (WB ? 0 : nkb); kb += kDeqGroups) {
             if (*reinterpret_cast<volatile int*>(abort_flag)) break;
             const int s = kb % kStages, sb = kb / kKBPerBlock, ch = kb % kKBPerBlock, r = sb % kRawStages;
-            if (ch == 0 && !wait_phase(&raw_full[r], static_cast<uint32_t>(sb / kRawStages) & 1u)) {
+            // the group's first K-block of a super-block waits for its raw tile
+            if (ch == dgrp && !wait_phase(&raw_full[r], static_cast<uint32_t>(sb / kRawStages) & 1u)) {
                 fail(abort_flag, err);
                 break;
             }
@@ -416,17 +479,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&b_full[s]);
-                if (ch == kKBPerBlock - 1) mbar_arrive(&raw_empty[r]);
+                if (ch >= kKBPerBlock - kDeqGroups) mbar_arrive(&raw_empty[r]);  // the group's last K-block of it
             }
         }
         // ---- epilogue: warp w owns tensor-memory lanes 32 (w % 4) .. +31; the
-        // two warps of a lane quarter split the (accumulator, 32-column) chunks ----
+        // warps of a lane quarter split the (accumulator, 32-column) chunks ----
         const int quad = warp & 3, grp = (warp - 2) >> 2;
+        constexpr int kEpiGroups = kDeqWarps / 4;
         const bool ok = wait_phase(tmem_full, 0u);
         if (!ok) fail(abort_flag, err);
-        if (ok && !*reinterpret_cast<volatile int*>(abort_flag)) {
+        if (ok && !*reinterpret_cast<volatile int*>(abort_flag) && C::kSwap) {
+            // lane = weight row n0 + 32 quad + lane; columns = activation rows
             tc_fence_after();
-            for (int item = grp; item < NACC * (BN / 32); item += 2) {
+            const int64_t col = static_cast<int64_t>(n0) + 32 * quad + lane;
+            for (int cc = grp; cc < (AROWS + 31) / 32; cc += kEpiGroups) {
+                uint32_t v[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(32 * cc), v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int64_t row = 32 * cc + i;  // m0 = 0: one row tile
+                    if (row < M && row < AROWS && col < N)
+                        c[row * N + col] = __uint_as_float(v[i]) * (ascale ? ascale[row] : 1.0f);
+                }
+            }
+        } else if (ok && !*reinterpret_cast<volatile int*>(abort_flag)) {
+            tc_fence_after();
+            for (int item = grp; item < NACC * (BN / 32); item += kEpiGroups) {
                 const int ac = item / (BN / 32), cc = item % (BN / 32);
                 uint32_t v[32];
                 tmem_ld32(tmem + (static_cast<uint32_t>(32 * quad) << 16) + static_cast<uint32_t>(ac * BN + 32 * cc), v);
@@ -487,13 +565,20 @@ GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms, bool wbf16, boo
     // filling the SMs pays (measured at M = 64: 101 -> 30 us for a 10240-column
     // down projection); at larger M the partial products' traffic costs more.
     int splits = 1;
-    if (allow_split && m <= 128) splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(std::min(nsb, 8), sms / (gx * gy))));
+    // Resident CTAs: two per SM for the swapped small-M tiles; only at M <= 16
+    // do the extra splits pay (measured: M = 8 down projection 87 -> 67 us, M =
+    // 64 projections 10-30% slower from the partial sums).
+    const int64_t slots = sms * ((!use_big && m <= 16) ? 2 : 1);
+    if (allow_split && m <= 128) splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(std::min(nsb, 8), slots / (gx * gy))));
     if (const char* t = getenv("RT_GEMM_SPLITS")) splits = std::max(1, std::min(nsb, atoi(t)));  // tests
     const int per = (nsb + splits - 1) / splits;
     p.kps = per * 256;
     p.splits = (nsb + per - 1) / per;
     p.grid = dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(p.splits));
-    p.smem = use_big ? Cfg<2, 256>::kSmemBytes : Cfg<1, 128>::kSmemBytes;
+    p.arows = use_big ? 128 : (m <= 16 ? 16 : m <= 64 ? 64 : 128);
+    p.smem = use_big ? Cfg<2, 256>::kSmemBytes
+                     : (p.arows == 16 ? Cfg<1, 128, 16>::kSmemBytes
+                                      : p.arows == 64 ? Cfg<1, 128, 64>::kSmemBytes : Cfg<1, 128>::kSmemBytes);
     return p;
 }
 
@@ -502,10 +587,14 @@ cudaError_t gemm_q4k_prepare() {
     auto set = [&](auto kernel, int bytes) {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     };
-    set(gemm_q4k_kernel<1, 128, false>, Cfg<1, 128>::kSmemBytes);
-    set(gemm_q4k_kernel<2, 256, false>, Cfg<2, 256>::kSmemBytes);
-    set(gemm_q4k_kernel<1, 128, true>, Cfg<1, 128>::kSmemBytes);
-    set(gemm_q4k_kernel<2, 256, true>, Cfg<2, 256>::kSmemBytes);
+    set(gemm_q4k_kernel<1, 128, false, 128>, Cfg<1, 128>::kSmemBytes);
+    set(gemm_q4k_kernel<1, 128, false, 64>, Cfg<1, 128, 64>::kSmemBytes);
+    set(gemm_q4k_kernel<1, 128, false, 16>, Cfg<1, 128, 16>::kSmemBytes);
+    set(gemm_q4k_kernel<2, 256, false, 128>, Cfg<2, 256>::kSmemBytes);
+    set(gemm_q4k_kernel<1, 128, true, 128>, Cfg<1, 128>::kSmemBytes);
+    set(gemm_q4k_kernel<1, 128, true, 64>, Cfg<1, 128, 64>::kSmemBytes);
+    set(gemm_q4k_kernel<1, 128, true, 16>, Cfg<1, 128, 16>::kSmemBytes);
+    set(gemm_q4k_kernel<2, 256, true, 128>, Cfg<2, 256>::kSmemBytes);
     return e;
 }
 
@@ -531,7 +620,7 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, c
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     };
-    if (!map16(tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, m, 128)) return false;
+    if (!map16(tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, m, p.arows)) return false;
     if (p.wbf16) return map16(tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, n, p.bn);
     const uint64_t row_bytes = static_cast<uint64_t>(k / 256) * kBlockBytes;
     const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(n)};
@@ -545,14 +634,17 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, c
 cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, const float* ascale, float* c, int64_t m,
                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s) {
     const dim3 g = p.grid;
-    if (p.bm == 256 && !p.wbf16)
-        gemm_q4k_kernel<2, 256, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
-    else if (p.bm == 128 && !p.wbf16)
-        gemm_q4k_kernel<1, 128, false><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
-    else if (p.bm == 256)
-        gemm_q4k_kernel<2, 256, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
-    else if (p.bm == 128)
-        gemm_q4k_kernel<1, 128, true><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err);
+#define RT_GEMM_LAUNCH(NA, BNN, WBB, AR) \
+    gemm_q4k_kernel<NA, BNN, WBB, AR><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err)
+    if (p.bm == 256 && !p.wbf16) RT_GEMM_LAUNCH(2, 256, false, 128);
+    else if (p.bm == 256) RT_GEMM_LAUNCH(2, 256, true, 128);
+    else if (p.bm == 128 && !p.wbf16 && p.arows == 16) RT_GEMM_LAUNCH(1, 128, false, 16);
+    else if (p.bm == 128 && !p.wbf16 && p.arows == 64) RT_GEMM_LAUNCH(1, 128, false, 64);
+    else if (p.bm == 128 && !p.wbf16) RT_GEMM_LAUNCH(1, 128, false, 128);
+    else if (p.bm == 128 && p.arows == 16) RT_GEMM_LAUNCH(1, 128, true, 16);
+    else if (p.bm == 128 && p.arows == 64) RT_GEMM_LAUNCH(1, 128, true, 64);
+    else if (p.bm == 128) RT_GEMM_LAUNCH(1, 128, true, 128);
+#undef RT_GEMM_LAUNCH
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }

@@ -20,6 +20,7 @@ struct GemmPlan {
     bool wbf16 = false;  // W is bf16 [n, k] instead of Q4_K
     int splits = 1;      // K split across the grid's third dimension
     int kps = 0;         // K columns per split (a multiple of 256)
+    int arows = 128;     // rows of an A stage (16 / 64 for M up to that: a deeper A/B ring)
     dim3 grid;
     size_t smem = 0;
 };
