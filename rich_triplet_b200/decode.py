@@ -48,14 +48,17 @@ class CudaDecodeContext:
             for i, L in enumerate(weights.layers):
                 for n in _PROJ:
                     r, c = shapes[n]
-                    w = DeviceWeight.upload(self.ctx, RT_FMT_Q4K, getattr(L, n), r, c)
+                    src = getattr(L, n)
+                    # host Q4_K bytes, or a device weight (a GGUF load) that the engine copies and frees
+                    w = src if isinstance(src, DeviceWeight) else DeviceWeight.upload(self.ctx, RT_FMT_Q4K, src, r, c)
                     staged.append(w)
                     setattr(layers[i], n, w.h.value)
                 for n in _NORMS:
                     a = np.ascontiguousarray(getattr(L, n), dtype=np.float32)
                     keep.append(a)
                     setattr(layers[i], n, a.ctypes.data)
-            emb = DeviceWeight.upload(self.ctx, RT_FMT_BF16, weights.embed, cfg.vocab_size, H)
+            emb = weights.embed if isinstance(weights.embed, DeviceWeight) else \
+                DeviceWeight.upload(self.ctx, RT_FMT_BF16, weights.embed, cfg.vocab_size, H)
             staged.append(emb)
             fnorm = np.ascontiguousarray(weights.final_norm, dtype=np.float32)
             c = cfg_to_c(cfg)
