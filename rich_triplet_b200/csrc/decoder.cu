@@ -634,6 +634,8 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
     if (!rt::gemv_make_tmap(rt::kBF16, d->embed, d->V, H, d->p_lm, &d->t_lm))
         return bail(fail(ctx, RT_E_CUDA, "rt_decoder_create: TMA descriptor rejected (LM head)"));
     d->nsplit = std::max(1, std::min(64, (ctx->num_sms + d->NKV - 1) / d->NKV));
+    // RT_STEP_ATTN_SPLITS overrides the context splits per KV head (tuning).
+    if (const char* e = getenv("RT_STEP_ATTN_SPLITS")) d->nsplit = std::max(1, std::min(d->nsplit, atoi(e)));
     for (int parts = kMaxDownParts; parts >= 1; parts /= 2)
         if ((d->F / 256) % parts == 0) {
             d->down_parts = parts;
