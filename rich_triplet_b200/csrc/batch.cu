@@ -95,7 +95,14 @@ struct rt_batch {
     int32_t* tokens = nullptr;   // [B] input token of the next step
     int32_t* pos = nullptr;      // [B] position of the next step
     int* h_err = nullptr;        // pinned copy of the context's error word
-    RowsPlan plan;               // the captured step's (many-sequence mode) or the last call's (rows mode)
+    RowsPlan plan;               // the captured step's (many-sequence mode)
+    // Rows mode: a plan and a captured graph per (rows, logit rows) met so far.
+    struct RowsGraph {
+        RowsPlan plan;
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+    };
+    std::vector<RowsGraph*> rows_graphs;
     // Tensor parallelism (nranks > 1): the decoder holds this rank's shard
     // (its query / KV heads and FFN columns); the o and down outputs are
     // summed over the ranks (NCCL all-reduce) and the LM head covers vocab
@@ -358,8 +365,18 @@ int balloc(rt_batch* t, void** p, size_t bytes, const char* what) {
     return rc;
 }
 
+void drop_rows_graphs(rt_batch* t) {
+    for (rt_batch::RowsGraph* r : t->rows_graphs) {
+        if (r->exec) cudaGraphExecDestroy(r->exec);
+        if (r->graph) cudaGraphDestroy(r->graph);
+        delete r;
+    }
+    t->rows_graphs.clear();
+}
+
 void release(rt_batch* t) {
     if (!t) return;
+    drop_rows_graphs(t);
     if (t->exec) cudaGraphExecDestroy(t->exec);
     if (t->graph) cudaGraphDestroy(t->graph);
     if (t->comm && t->nccl) t->nccl->comm_destroy(t->comm);  // after the graphs that hold its calls
@@ -759,18 +776,40 @@ int rows_run(rt_batch* t, const int32_t* tokens, int m, int start, int lm_rows, 
     for (int i = 0; i < m; ++i) pos[i] = start + i;
     RT_CHECK_CUDA(ctx, cudaMemcpyAsync(t->tokens, tokens, sizeof(int32_t) * m, cudaMemcpyHostToDevice, s));
     RT_CHECK_CUDA(ctx, cudaMemcpyAsync(t->pos, pos.data(), sizeof(int32_t) * m, cudaMemcpyHostToDevice, s));
-    if (t->plan.m != m || t->plan.lm_rows != lm_rows) {
-        if (!build_plan(t, m, m - lm_rows, lm_rows, &t->plan)) {
-            t->plan = RowsPlan{};
+    rt_batch::RowsGraph* rg = nullptr;
+    for (rt_batch::RowsGraph* r : t->rows_graphs)
+        if (r->plan.m == m && r->plan.lm_rows == lm_rows) rg = r;
+    if (!rg) {
+        // a new shape: its plan, then one captured step replayed from now on
+        auto* r = new rt_batch::RowsGraph;
+        if (!build_plan(t, m, m - lm_rows, lm_rows, &r->plan)) {
+            delete r;
             return fail(ctx, RT_E_SHAPE, "rows engine: no GEMM geometry for %d rows", m);
         }
-        const int rc = grow_parts(t, t->plan.part_floats);
+        if (r->plan.part_floats > t->part_cap || t->rows_graphs.size() >= 32)
+            drop_rows_graphs(t);  // the graphs hold the old split-K buffer
+        const int rc = grow_parts(t, r->plan.part_floats);
         if (rc != RT_OK) {
-            t->plan = RowsPlan{};
+            delete r;
             return rc;
         }
+        cudaError_t ce = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+        if (ce == cudaSuccess) {
+            const cudaError_t ee = enqueue(t, r->plan, s, false);
+            ce = cudaStreamEndCapture(s, &r->graph);
+            if (ee != cudaSuccess) ce = ee;
+        }
+        if (ce == cudaSuccess) ce = cudaGraphInstantiate(&r->exec, r->graph, 0);
+        if (ce != cudaSuccess) {
+            cudaGetLastError();
+            if (r->graph) cudaGraphDestroy(r->graph);
+            delete r;
+            return fail(ctx, RT_E_CUDA, "rows engine: step capture failed (%s)", cudaGetErrorString(ce));
+        }
+        t->rows_graphs.push_back(r);
+        rg = r;
     }
-    RT_CHECK_CUDA(ctx, enqueue(t, t->plan, s, false));
+    RT_CHECK_CUDA(ctx, cudaGraphLaunch(rg->exec, s));
     if (logits && lm_rows > 0)
         RT_CHECK_CUDA(ctx, cudaMemcpyAsync(logits, t->logits, sizeof(float) * lm_rows * t->vr, cudaMemcpyDeviceToHost, s));
     RT_CHECK_CUDA(ctx, cudaMemcpyAsync(t->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
