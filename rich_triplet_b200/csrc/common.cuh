@@ -65,12 +65,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 
 // L2 policy for streamed-once data (weights): evict first, so the weight
 // stream does not push activations and the KV cache out of L2.
-// Wait for phase `parity` of `bar`, giving up after one second of
-// globaltimer: false if it gave up.
+// Wait for phase `parity` of `bar`, giving up after about one second of
+// globaltimer (first read after 1024 polls, so that short waits never pay
+// for it): false if it gave up.
 __device__ __forceinline__ bool mbar_wait_timed(uint64_t* bar, uint32_t parity) {
     const uint32_t addr = smem_u32(bar);
     uint64_t t0 = 0;
-    for (uint32_t it = 0;; ++it) {
+    for (uint32_t it = 1;; ++it) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -80,10 +81,10 @@ __device__ __forceinline__ bool mbar_wait_timed(uint64_t* bar, uint32_t parity) 
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if ((it & 63u) == 0u) {
+        if ((it & 1023u) == 0u) {
             uint64_t t;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-            if (it == 0) t0 = t;
+            if (it == 1024u) t0 = t;
             else if (t - t0 > 1000000000ull) return false;
         }
     }

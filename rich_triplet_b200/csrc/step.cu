@@ -130,7 +130,9 @@ __device__ __forceinline__ bool grid_sync(const StepParams& P, uint32_t& nsync, 
         __threadfence();
         atomicAdd(&P.sync[0], 1u);
         const uint32_t target = nsync * gridDim.x;
-        const uint64_t t0 = gtimer();
+        // The time bound starts after 1024 polls, so that a barrier the grid
+        // reaches promptly never reads the globaltimer.
+        uint64_t t0 = 0;
         uint32_t spin = 0;
         while (ok) {
             if (ld_acquire_u32(&P.sync[0]) >= target) break;
@@ -138,10 +140,13 @@ __device__ __forceinline__ bool grid_sync(const StepParams& P, uint32_t& nsync, 
                 ok = false;
                 break;
             }
-            if ((++spin & 63u) == 0u && gtimer() - t0 > kBarrierTimeoutNs) {
-                if (P.err) atomicExch(P.err, kErrGridTimeout);
-                atomicExch(P.abort, 1);
-                ok = false;
+            if ((++spin & 1023u) == 0u) {
+                if (spin == 1024u) t0 = gtimer();
+                else if (gtimer() - t0 > kBarrierTimeoutNs) {
+                    if (P.err) atomicExch(P.err, kErrGridTimeout);
+                    atomicExch(P.abort, 1);
+                    ok = false;
+                }
             }
         }
         __threadfence();
