@@ -44,6 +44,8 @@ def parse():
     p.add_argument("--layers", type=int, default=34, help="model depth (34 = Gemma 3 4B)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-config4", action="store_true", help="skip the 27B tensor-parallel section")
+    p.add_argument("--tp-allreduce", default="nccl", choices=["peer", "nccl"],
+                   help="config 4's per-layer sums: peer all-reduce kernel over NVLink, or NCCL")
     p.add_argument("--cpu-steps", type=int, default=3)
     p.add_argument("--prompt", type=int, default=PROMPT,
                    help="prompt tokens prefilled before the timed steps (512 = BASELINE config 1; "
@@ -289,7 +291,9 @@ def tp_decode_config4(args, world, rank, dist, device, hbm_peak):
 
     cfg = Config4.gemma3_27b()
     out = {"model": "gemma3-27b (62 layers, hidden 5376, FFN 21504, 32/16 heads of 128), synthetic Q4_K weights",
-           "parallelism": f"tp{world}: heads and FFN columns split, NCCL all-reduce after o and down, vocab-split LM head",
+           "parallelism": f"tp{world}: heads and FFN columns split, all-reduce after o and down, vocab-split LM head",
+           "allreduce": ("none" if world == 1 else
+                         "peer kernel (NVLink stores, one launch per sum)" if args.tp_allreduce == "peer" else "NCCL"),
            "context": CONFIG4_CONTEXT, "steps": CONFIG4_STEPS, "kv": "f32, synthetic contents (no prefill)",
            "gemm_operands": "fp16, f32 accumulation"}
     ctx = dec = None
@@ -316,6 +320,8 @@ def tp_decode_config4(args, world, rank, dist, device, hbm_peak):
         try:
             bat = TpBatchDecoder(dec, nseq, CONFIG4_CONTEXT + warm + CONFIG4_STEPS + 1, world, rank, nccl_id)
             bat.synth_kv(args.seed + rank, CONFIG4_CONTEXT)
+            if world > 1 and args.tp_allreduce == "peer":
+                bat.enable_peer_allreduce(dist)
         except Exception as e:
             err = f"{type(e).__name__}: {e}"
         if not all_ok(err is None, dist, device):

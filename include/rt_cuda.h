@@ -308,6 +308,17 @@ int rt_tp_create(rt_dec* shard, const void* nccl_id, int32_t nranks, int32_t ran
 /* The vocab rows [v0, v0 + vr) whose logits this engine's steps return (the
  * whole vocabulary without tensor parallelism). */
 int rt_batch_vocab_slice(const rt_batch* b, int32_t* v0, int32_t* vr);
+/* Peer all-reduce for a tensor-parallel engine (no reference counterpart):
+ * the per-layer sums of the o and down outputs then cross NVLink as stores
+ * into every rank's buffer, one kernel per sum, instead of NCCL all-reduces.
+ * Every rank calls rt_tp_peer_handle (64 bytes: the CUDA IPC handle of this
+ * rank's buffer), the caller gathers the handles in rank order, and every rank
+ * calls rt_tp_peer_open with the nranks * 64 bytes; the step is then captured
+ * again with the peer kernel.  Each wait on a peer is bounded (2 s), after
+ * which the engine reports RT_E_TIMEOUT from the step and stops waiting.
+ * Needs 2 to 8 ranks in one process each, on GPUs that reach each other. */
+int rt_tp_peer_handle(rt_batch* b, void* handle_out);
+int rt_tp_peer_open(rt_batch* b, const void* handles);
 
 /* Fill every sequence's cache with synthetic values (a seeded hash, unit
  * variance) and set every position to seq_len: the state a benchmark decodes

@@ -45,6 +45,16 @@ using rt::fail;
 
 namespace {
 
+// Peer all-reduce of the tensor-parallel step (rt_tp_peer_open).
+constexpr int kMaxRanks = 8;
+constexpr int kArCtas = 16;          // CTAs of one all-reduce; CTA c owns slice c of the vector
+constexpr int64_t kArFlagBytes = 4096;  // [2 parities][kMaxRanks][kArCtas] u32 flags, then the receive areas
+
+// Every rank's symmetric buffer, as this rank addresses it (its own: local).
+struct PeerBufs {
+    uint8_t* base[kMaxRanks];
+};
+
 struct BatchGemm {
     rt::GemmPlan p;
     CUtensorMap ta, tw;
@@ -112,6 +122,15 @@ struct rt_batch {
     const rt::NcclApi* nccl = nullptr;
     ncclComm_t comm = nullptr;
     float* ar_buf = nullptr;      // [B][H] summed projection
+    // Peer all-reduce (after rt_tp_peer_open; NCCL's before): this rank's
+    // symmetric buffer [flags][2][nranks][B*H] (exported through CUDA IPC),
+    // every rank's buffer as mapped here, and the step counter that tags the
+    // flags.
+    bool p2p = false;
+    uint8_t* ar_sym = nullptr;
+    PeerBufs peers{};
+    void* opened[kMaxRanks] = {};
+    int32_t* step_ctr = nullptr;
     uint32_t* am_send = nullptr;  // [B][2] this rank's best logit: (value bits, vocab index)
     uint32_t* am_recv = nullptr;  // [nranks][B][2]
     cudaGraph_t graph = nullptr;
@@ -338,6 +357,75 @@ __global__ void argmax_merge_kernel(const uint32_t* pairs, int nranks, int B, in
     pos[b] += 1;
 }
 
+// Sum over the ranks of this rank's partial into buf[0..count), through the
+// ranks' symmetric buffers.  The partial is src's `parts` split-K parts
+// (stride count) added in part order, as sum_parts_launch adds them; src may
+// be buf itself (one part).  CTA c stores its slice of the partial into
+// every rank's receive area of this rank (NVLink stores), fences at system
+// scope and raises its flag there with `tag`; then it waits (bounded) for the
+// flag of every rank's CTA c in its own buffer and adds the ranks' slices in
+// rank order, so every rank gets the same bits.  Two receive areas alternate
+// between consecutive calls (`parity`): a rank cannot reach call s + 2 before
+// every rank has finished call s, so no area or flag is rewritten while it is
+// read.  After a wait gives up (err set) later calls no longer wait.
+__global__ void __launch_bounds__(256) peer_allreduce_kernel(const float* src, int parts, float* buf, int64_t count,
+                                                             int64_t cap_count, PeerBufs pb,
+                                                             int nranks, int rank, int parity, uint32_t call,
+                                                             const int32_t* step_ctr, int* err) {
+    const int c = blockIdx.x, tid = threadIdx.x;
+    const int64_t per = (count + 4 * kArCtas - 1) / (4 * kArCtas) * 4;
+    const int64_t i0 = c * per, i1 = min(count, i0 + per);
+    const uint32_t tag = static_cast<uint32_t>(*step_ctr) * 256u + call + 1u;
+    const bool broken = *reinterpret_cast<volatile int*>(err) != 0;
+    auto recv = [&](int owner, int src) {
+        return reinterpret_cast<float*>(pb.base[owner] + kArFlagBytes) + static_cast<int64_t>(parity * nranks + src) * cap_count;
+    };
+    auto flag = [&](int owner, int src) {
+        return reinterpret_cast<uint32_t*>(pb.base[owner]) + (parity * kMaxRanks + src) * kArCtas + c;
+    };
+    for (int64_t i = i0 + 4 * tid; i < i1; i += 4 * blockDim.x) {
+        float4 v = *reinterpret_cast<const float4*>(src + i);
+        for (int z = 1; z < parts; ++z) {
+            const float4 w = *reinterpret_cast<const float4*>(src + z * count + i);
+            v = make_float4(v.x + w.x, v.y + w.y, v.z + w.z, v.w + w.w);
+        }
+        for (int r = 0; r < nranks; ++r) *reinterpret_cast<float4*>(recv(r, rank) + i) = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid < nranks)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag(tid, rank)), "r"(tag) : "memory");
+    if (tid < nranks && !broken) {
+        const uint32_t* f = flag(rank, tid);
+        uint64_t t0 = 0;
+        for (uint32_t it = 1;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (v == tag) break;
+            if ((it & 1023u) == 0u) {
+                uint64_t t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                if (it == 1024u) t0 = t;
+                else if (t - t0 > 2000000000ull) {
+                    atomicExch(err, rt::kErrGridTimeout);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    for (int64_t i = i0 + 4 * tid; i < i1; i += 4 * blockDim.x) {
+        float4 a = __ldcg(reinterpret_cast<const float4*>(recv(rank, 0) + i));
+        for (int r = 1; r < nranks; ++r) {
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(recv(rank, r) + i));
+            a = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+        }
+        *reinterpret_cast<float4*>(buf + i) = a;
+    }
+}
+
+__global__ void tick_kernel(int32_t* ctr) { *ctr += 1; }
+
 // Synthetic cache contents for benchmarks: a hash of (seed, index) mapped to
 // a uniform value of unit variance.
 __global__ void synth_kv_kernel(float* kv, int64_t n, uint64_t seed) {
@@ -380,6 +468,8 @@ void release(rt_batch* t) {
     if (t->exec) cudaGraphExecDestroy(t->exec);
     if (t->graph) cudaGraphDestroy(t->graph);
     if (t->comm && t->nccl) t->nccl->comm_destroy(t->comm);  // after the graphs that hold its calls
+    for (void* p : t->opened)
+        if (p) cudaIpcCloseMemHandle(p);
     for (void* p : t->allocs) cudaFree(p);
     if (t->h_err) cudaFreeHost(t->h_err);
     delete t;
@@ -442,6 +532,7 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         return ok(rt::gemm_q4k_launch(g.ta, g.tw, g.ascale, c, g.m, g.n, g.k, g.p, t->ctx->d_err, s));
     };
     auto nccl_ok = [&](ncclResult_t r) { return ok(r == ncclSuccess ? cudaSuccess : cudaErrorUnknown); };
+    uint32_t ar_call = 0;  // peer all-reduces of this step so far
     // A row-split projection's output as a row kernel reads it: (source,
     // split parts, part stride).  With several ranks the parts are added and
     // the sum is all-reduced over the ranks into ar_buf.
@@ -454,10 +545,22 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         const int64_t count = static_cast<int64_t>(B) * g.n;
         if (t->nranks == 1) return gemm(g, t->parts) ? Proj{t->parts, g.p.splits, count} : Proj{};
         if (!gemm(g, g.p.splits > 1 ? t->parts : t->ar_buf)) return Proj{};
+        if (t->p2p) {  // split-K sum and all-reduce in one kernel
+            const bool split = g.p.splits > 1;
+            peer_allreduce_kernel<<<kArCtas, 256, 0, s>>>(split ? t->parts : t->ar_buf, split ? g.p.splits : 1, t->ar_buf,
+                                                        count, static_cast<int64_t>(t->B) * t->H, t->peers, t->nranks,
+                                                        t->rank, static_cast<int>(ar_call & 1), ar_call, t->step_ctr,
+                                                        t->ctx->d_err);
+            ++ar_call;
+            if (!ok(cudaGetLastError())) return Proj{};
+            return Proj{t->ar_buf, 1, count};
+        }
         if (g.p.splits > 1 && !ok(rt::sum_parts_launch(t->parts, g.p.splits, count, t->ar_buf, t->ctx->num_sms, s)))
             return Proj{};
-        if (!nccl_ok(t->nccl->all_reduce(t->ar_buf, t->ar_buf, static_cast<size_t>(count), ncclFloat32, ncclSum, t->comm, s)))
+        if (!nccl_ok(t->nccl->all_reduce(t->ar_buf, t->ar_buf, static_cast<size_t>(count), ncclFloat32, ncclSum,
+                                                t->comm, s))) {
             return Proj{};
+        }
         return Proj{t->ar_buf, 1, count};
     };
     Proj pdown;  // the previous layer's down projection
@@ -600,6 +703,10 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
             }
         }
     }
+    if (e == cudaSuccess && t->p2p) {  // the next step's peer all-reduces carry the next tag
+        tick_kernel<<<1, 1, 0, s>>>(t->step_ctr);
+        ok(cudaGetLastError());
+    }
     t->launches = n;
     return e;
 }
@@ -628,6 +735,26 @@ int grow_parts(rt_batch* t, int64_t floats) {
     const int rc = balloc(t, reinterpret_cast<void**>(&t->parts), sizeof(float) * floats, "batch GEMM outputs");
     if (rc == RT_OK) t->part_cap = floats;
     return rc;
+}
+
+// (Re)capture the many-sequence step as t->graph / t->exec.
+int capture_step(rt_batch* t) {
+    rt_ctx* ctx = t->ctx;
+    if (t->exec) cudaGraphExecDestroy(t->exec);
+    if (t->graph) cudaGraphDestroy(t->graph);
+    t->exec = nullptr;
+    t->graph = nullptr;
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaStream_t s = ctx->stream;
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return fail(ctx, RT_E_CUDA, "batch engine: begin capture");
+    const cudaError_t ce = enqueue(t, t->plan, s, true);
+    const cudaError_t ee = cudaStreamEndCapture(s, &t->graph);
+    if (ce != cudaSuccess || ee != cudaSuccess || cudaGraphInstantiate(&t->exec, t->graph, 0) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, RT_E_CUDA, "batch engine: step capture failed (%s)", cudaGetErrorString(ce != cudaSuccess ? ce : ee));
+    }
+    return RT_OK;
 }
 
 // Tensor-parallel set-up of a many-sequence engine (nranks 1: none).
@@ -749,17 +876,7 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, const TpInit* tp
         // the step's GEMM plans and tensor maps (A is xa, read as [B][K]), then its capture
         if (!build_plan(t, rows, 0, rows, &t->plan)) return bail(fail(ctx, RT_E_SHAPE, "rt_batch_create: no GEMM geometry"));
         if ((rc = grow_parts(t, t->plan.part_floats)) != RT_OK) return bail(rc);
-        RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-        cudaStream_t s = ctx->stream;
-        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
-            return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: begin capture"));
-        const cudaError_t ce = enqueue(t, t->plan, s, true);
-        const cudaError_t ee = cudaStreamEndCapture(s, &t->graph);
-        if (ce != cudaSuccess || ee != cudaSuccess || cudaGraphInstantiate(&t->exec, t->graph, 0) != cudaSuccess) {
-            cudaGetLastError();
-            return bail(fail(ctx, RT_E_CUDA, "rt_batch_create: step capture failed (%s)",
-                             cudaGetErrorString(ce != cudaSuccess ? ce : ee)));
-        }
+        if ((rc = capture_step(t)) != RT_OK) return bail(rc);
     }
     RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     *out = t;
@@ -934,6 +1051,55 @@ int rt_tp_create(rt_dec* shard, const void* nccl_id, int32_t nranks, int32_t ran
     tp.rank = rank;
     if (nranks > 1) memcpy(&tp.id, nccl_id, sizeof(tp.id));
     return create_engine(shard, nseq, cap, false, &tp, out);
+}
+
+int rt_tp_peer_handle(rt_batch* t, void* handle_out) {
+    if (!t || !handle_out) return t ? fail(t->ctx, RT_E_INVAL, "rt_tp_peer_handle: null argument") : RT_E_INVAL;
+    if (t->nranks < 2 || t->nranks > kMaxRanks || 2 * t->NL + 1 > 255)
+        return fail(t->ctx, RT_E_SHAPE, "rt_tp_peer_handle: %d ranks, %d layers", t->nranks, t->NL);
+    RT_CHECK_CUDA(t->ctx, cudaSetDevice(t->ctx->device));
+    if (!t->ar_sym) {
+        const size_t bytes = kArFlagBytes + sizeof(float) * 2 * t->nranks * static_cast<size_t>(t->B) * t->H;
+        int rc = balloc(t, reinterpret_cast<void**>(&t->ar_sym), bytes, "tp peer all-reduce buffer");
+        if (rc == RT_OK) rc = balloc(t, reinterpret_cast<void**>(&t->step_ctr), sizeof(int32_t), "tp step counter");
+        if (rc != RT_OK) return rc;
+        // zeroed flags before any peer can see the handle
+        RT_CHECK_CUDA(t->ctx, cudaMemsetAsync(t->ar_sym, 0, bytes, t->ctx->stream));
+        RT_CHECK_CUDA(t->ctx, cudaMemsetAsync(t->step_ctr, 0, sizeof(int32_t), t->ctx->stream));
+        RT_CHECK_CUDA(t->ctx, cudaStreamSynchronize(t->ctx->stream));
+    }
+    cudaIpcMemHandle_t h;
+    RT_CHECK_CUDA(t->ctx, cudaIpcGetMemHandle(&h, t->ar_sym));
+    memcpy(handle_out, &h, sizeof(h));
+    return RT_OK;
+}
+
+int rt_tp_peer_open(rt_batch* t, const void* handles) {
+    if (!t || !handles) return t ? fail(t->ctx, RT_E_INVAL, "rt_tp_peer_open: null argument") : RT_E_INVAL;
+    if (!t->ar_sym) return fail(t->ctx, RT_E_STATE, "rt_tp_peer_open: call rt_tp_peer_handle first");
+    if (t->p2p) return RT_OK;
+    RT_CHECK_CUDA(t->ctx, cudaSetDevice(t->ctx->device));
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (int r = 0; r < t->nranks; ++r) {
+        if (r == t->rank) {
+            t->peers.base[r] = t->ar_sym;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + r * sizeof(h), sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(t->ctx, RT_E_CUDA, "rt_tp_peer_open: rank %d's buffer: %s", r, cudaGetErrorString(e));
+        }
+        t->opened[r] = p;
+        t->peers.base[r] = static_cast<uint8_t*>(p);
+    }
+    t->p2p = true;
+    const int rc = capture_step(t);
+    if (rc != RT_OK) t->p2p = false;
+    return rc;
 }
 
 int rt_batch_vocab_slice(const rt_batch* t, int32_t* v0, int32_t* vr) {

@@ -147,6 +147,25 @@ class TpBatchDecoder(CudaBatchDecoder):
         check(lib().rt_batch_vocab_slice(self.h, ctypes.byref(v0), ctypes.byref(vr)), self.ctx.h)
         self.vocab_lo, self.vocab = v0.value, vr.value
 
+    def peer_handle(self):
+        """64 bytes: the CUDA IPC handle of this rank's peer all-reduce buffer."""
+        buf = ctypes.create_string_buffer(64)
+        check(lib().rt_tp_peer_handle(self.h, buf), self.ctx.h)
+        return buf.raw
+
+    def peer_open(self, handles):
+        """Map every rank's buffer (`handles` in rank order) and switch the
+        per-layer sums from NCCL to the peer all-reduce kernel."""
+        blob = b"".join(bytes(h) for h in handles)
+        check(lib().rt_tp_peer_open(self.h, ctypes.create_string_buffer(blob, len(blob))), self.ctx.h)
+
+    def enable_peer_allreduce(self, dist):
+        """peer_handle on every rank, an all-gather of the handles over the
+        torch.distributed group `dist` (any backend), then peer_open."""
+        handles = [None] * dist.get_world_size()
+        dist.all_gather_object(handles, self.peer_handle())
+        self.peer_open(handles)
+
 
 def share_nccl_id(dist, rank, make=nccl_unique_id):
     """The NCCL id made on rank 0, on every rank of the torch.distributed

@@ -4,7 +4,10 @@ single-GPU engine on the same weights.
 With one rank the engine is the many-sequence engine itself (bit-identical
 logits).  With two ranks (two GPUs; skipped on a one-GPU machine) each rank
 holds half of the heads and FFN columns; the o / down outputs are summed by
-NCCL all-reduces and the greedy token comes from an all-gather.  Tolerance
+NCCL all-reduces and the greedy token comes from an all-gather.  The same
+engine with the peer all-reduce (rt_tp_peer_open: NVLink stores into every
+rank's buffer) must give the NCCL run's logits bit for bit: with two ranks
+every element is one addition of the same two values.  Tolerance
 REL_L2 (2e-3, the north star's bar for logits): the shards' GEMM operands are
 rounded to fp16 with row scales taken over each rank's columns, so the sums
 differ from the single-GPU ones at that rounding (about 3e-4).
@@ -87,8 +90,16 @@ def _tp_worker(rank, world, port, out):
         dec = CudaDecodeContext(synth_shard_weights(CFG, 77, world, rank), 16, ctx)
         bat = TpBatchDecoder(dec, NSEQ, CAP, world, rank, nccl_id)
         logits, toks = _run(bat, _inputs())
-        np.savez(os.path.join(out, f"rank{rank}.npz"), v0=bat.vocab_lo, logits=np.stack(logits), toks=np.stack(toks))
+        v0 = bat.vocab_lo
         bat.close()
+        peer = TpBatchDecoder(dec, NSEQ, CAP, world, rank, share_nccl_id(dist, rank))
+        peer.enable_peer_allreduce(dist)
+        dist.barrier()
+        plog, ptok = _run(peer, _inputs())
+        dist.barrier()  # no rank frees its buffer while a peer may still store into it
+        peer.close()
+        np.savez(os.path.join(out, f"rank{rank}.npz"), v0=v0, logits=np.stack(logits), toks=np.stack(toks),
+                 peer_logits=np.stack(plog), peer_toks=np.stack(ptok))
         dec.close()
         ctx.close()
     finally:
@@ -106,6 +117,9 @@ def test_tp2_matches_single_gpu(tmp_path):
     mp.spawn(_tp_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     parts = [np.load(tmp_path / f"rank{r}.npz") for r in range(2)]
     assert np.array_equal(parts[0]["toks"], parts[1]["toks"])
+    for p in parts:
+        assert np.array_equal(p["peer_logits"], p["logits"])
+        assert np.array_equal(p["peer_toks"], p["toks"])
     tp_logits = np.concatenate([p["logits"] for p in parts], axis=2)
     assert int(parts[1]["v0"]) == parts[0]["logits"].shape[2]
 
