@@ -29,6 +29,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <vector>
 
@@ -42,6 +44,7 @@
 #include "rt_internal.h"
 
 using rt::fail;
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -145,116 +148,221 @@ namespace {
 // ---- row kernels (one CTA per sequence row) ----
 
 constexpr int kMaxParts = 8;  // split-K partial products a row kernel adds (gemm_q4k_plan caps splits at 8)
-constexpr int kRowThreads = 512;
 constexpr int kRowsMax = 512;            // rows mode: positions per call (longer prompts run in pieces)
 constexpr int kRowsMaxLogitRows = 64;    // rows mode: rows whose logits one call can return
 
-// src[i] + src[stride + i] + ... (`parts` <= kMaxParts terms, in part order),
-// every load issued before the first add.
-__device__ __forceinline__ float sum_parts_at(const float* src, int parts, int64_t stride, int64_t i) {
-    float v[kMaxParts];
-#pragma unroll
-    for (int q = 0; q < kMaxParts; ++q) v[q] = q < parts ? src[q * stride + i] : 0.f;
-    float s = v[0];
-#pragma unroll
-    for (int q = 1; q < kMaxParts; ++q)
-        if (q < parts) s += v[q];
-    return s;
+// Row kernels.  One sequence row is split over a thread-block cluster of
+// `cl` CTAs (cluster rank q: columns [q * chunk, (q + 1) * chunk), chunk a
+// multiple of 4, float4 accesses); the row's sums and maxima are block
+// reductions combined over the cluster through distributed shared memory, the
+// CTAs' partials added in cluster-rank order, so every CTA gets the same bits.
+// Dynamic shared memory: chunk floats (the CTA's slice of the row).
+constexpr int kRowCta = 256;
+
+struct RowSlice {
+    int64_t base;  // row start (elements)
+    int c0, c1;    // this CTA's columns
+};
+
+__device__ __forceinline__ RowSlice row_slice(int n) {
+    cg::cluster_group cl = cg::this_cluster();
+    const int q = static_cast<int>(cl.block_rank()), csize = static_cast<int>(cl.num_blocks());
+    const int chunk = (n + 4 * csize - 1) / (4 * csize) * 4;
+    const int b = blockIdx.x / csize;
+    return RowSlice{static_cast<int64_t>(b) * n, min(n, q * chunk), min(n, (q + 1) * chunk)};
 }
 
-// The row's GEMM input: out = fp16(v * 2^-e) for v = row[0..n), oscale[b] = 2^e.
-__device__ __forceinline__ void store_f16_row(const float* row, int n, float mx, float* red, uint16_t* out,
-                                              float* oscale) {
-    mx = rt::block_max(mx, red);
+// Sum (kMax false) or maximum (kMax true) of v over the cluster's threads.
+// `slot` is a shared float used by this reduction alone: its CTA's partial,
+// read by the other CTAs after the cluster barrier.
+template <bool kMax>
+__device__ __forceinline__ float cluster_reduce(float v, float* red, float* slot) {
+    cg::cluster_group cl = cg::this_cluster();
+    v = kMax ? rt::block_max(v, red) : rt::block_sum(v, red);
+    if (threadIdx.x == 0) *slot = v;
+    cl.sync();
+    const int csize = static_cast<int>(cl.num_blocks());
+    float t = *cl.map_shared_rank(slot, 0);
+    for (int r = 1; r < csize; ++r) {
+        const float x = *cl.map_shared_rank(slot, r);
+        t = kMax ? fmaxf(t, x) : t + x;
+    }
+    return t;
+}
+
+// src[i..i+4) + src[stride + i..] + ... (`parts` <= kMaxParts terms, in part
+// order), every load issued before the first add.
+__device__ __forceinline__ float4 ld_parts4(const float* src, int parts, int64_t stride, int64_t i) {
+    float4 w[kMaxParts];
+#pragma unroll
+    for (int q = 0; q < kMaxParts; ++q)
+        w[q] = q < parts ? *reinterpret_cast<const float4*>(src + q * stride + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 v = w[0];
+#pragma unroll
+    for (int q = 1; q < kMaxParts; ++q)
+        if (q < parts) v = make_float4(v.x + w[q].x, v.y + w[q].y, v.z + w[q].z, v.w + w[q].w);
+    return v;
+}
+
+__device__ __forceinline__ float abs_max4(float m, float4 v) {
+    return fmaxf(fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+// The slice row[0..c1-c0) as fp16 GEMM input: out = fp16(v * 2^-e), oscale =
+// 2^e, e from the row's maximum |v| (`mx`, this thread's part of it), then a
+// last cluster barrier: no CTA leaves while another still reads its slots.
+__device__ __forceinline__ void store_f16_slice(const float* row, RowSlice rs, float mx, float* red, float* slot,
+                                                uint16_t* out, float* oscale) {
+    mx = cluster_reduce<true>(mx, red, slot);
     float inv, sc;
     rt::row_scale_f16(mx, &inv, &sc);
-    for (int c = threadIdx.x; c < n; c += blockDim.x) out[c] = __half_as_ushort(__float2half_rn(row[c] * inv));
-    if (threadIdx.x == 0) *oscale = sc;
+    for (int c = rs.c0 + 4 * threadIdx.x; c < rs.c1; c += 4 * blockDim.x) {
+        const float4 v = *reinterpret_cast<const float4*>(row + (c - rs.c0));
+        const __half2 lo = __floats2half2_rn(v.x * inv, v.y * inv), hi = __floats2half2_rn(v.z * inv, v.w * inv);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(out + rs.base + c) = pk;
+    }
+    if (threadIdx.x == 0 && cg::this_cluster().block_rank() == 0) *oscale = sc;
+    cg::this_cluster().sync();
 }
 
 // Residual update and RMSNorm of one row (the fused prologues of the
-// single-sequence engine, in the same operation order):
+// single-sequence engine, in the same operation order per element):
 //   embed != null: r = bf16(embed[tokens[b]]) * embed_scale   (src/transformer4.rs:2360-2364)
 //   else:          s = src parts added in order; r = resid_in + s * rms(s) * (1 + gpost)
 //   resid_out = r;  x = r * rms(r) * (1 + gpre)                 (rms_norm_gemma3, src/autograd2.rs:3477-3496)
-// and x goes out as an fp16 GEMM row with its scale.
-__global__ void __launch_bounds__(kRowThreads) resid_norm_rows_kernel(
+// and x goes out as an fp16 GEMM row with its scale.  Rows of H (a multiple of 4).
+__global__ void __launch_bounds__(kRowCta) resid_norm_rows_kernel(
     const uint16_t* embed, const int32_t* tokens, float embed_scale, const float* src, int src_parts,
     int64_t part_stride, const float* resid_in, float* resid_out, const float* gpost, const float* gpre, float eps, int H,
     uint16_t* out, float* oscale) {
-    extern __shared__ float row[];  // [H]
+    extern __shared__ float4 row4[];  // this CTA's slice of the row
+    float* row = reinterpret_cast<float*>(row4);
     __shared__ float red[32];
-    const int b = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x;
-    const int64_t base = static_cast<int64_t>(b) * H;
+    __shared__ float slot[4];
+    const RowSlice rs = row_slice(H);
+    const int b = static_cast<int>(rs.base / H), tid = threadIdx.x, step = 4 * blockDim.x;
     const float inv_d = 1.0f / static_cast<float>(H);
     float ss = 0.f;
     if (embed) {
         const uint16_t* er = embed + static_cast<int64_t>(tokens[b]) * H;
-        for (int c = tid; c < H; c += nthr) {
-            const float v = __fmul_rn(rt::bf16_bits_to_f32(er[c]), embed_scale);
-            row[c] = v;
-            resid_out[base + c] = v;
-            ss += v * v;
+        for (int c = rs.c0 + 4 * tid; c < rs.c1; c += step) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(er + c);
+            const float4 v = make_float4(__fmul_rn(rt::bf16_bits_to_f32(raw.x & 0xFFFFu), embed_scale),
+                                         __fmul_rn(rt::bf16_bits_to_f32(raw.x >> 16), embed_scale),
+                                         __fmul_rn(rt::bf16_bits_to_f32(raw.y & 0xFFFFu), embed_scale),
+                                         __fmul_rn(rt::bf16_bits_to_f32(raw.y >> 16), embed_scale));
+            *reinterpret_cast<float4*>(row + (c - rs.c0)) = v;
+            *reinterpret_cast<float4*>(resid_out + rs.base + c) = v;
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
     } else {
-        for (int c = tid; c < H; c += nthr) {
-            const float s = sum_parts_at(src, src_parts, part_stride, base + c);
-            row[c] = s;
-            ss += s * s;
+        for (int c = rs.c0 + 4 * tid; c < rs.c1; c += step) {
+            const float4 v = ld_parts4(src, src_parts, part_stride, rs.base + c);
+            *reinterpret_cast<float4*>(row + (c - rs.c0)) = v;
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
-        ss = rt::block_sum(ss, red);
+        ss = cluster_reduce<false>(ss, red, &slot[0]);
         const float r1 = 1.0f / sqrtf(ss * inv_d + eps);
         ss = 0.f;
-        for (int c = tid; c < H; c += nthr) {
-            const float nv = __fadd_rn(resid_in[base + c], __fmul_rn(__fmul_rn(row[c], r1), __fadd_rn(1.0f, gpost[c])));
-            row[c] = nv;
-            resid_out[base + c] = nv;
-            ss += nv * nv;
+        for (int c = rs.c0 + 4 * tid; c < rs.c1; c += step) {
+            const float4 v = *reinterpret_cast<const float4*>(row + (c - rs.c0));
+            const float4 ri = *reinterpret_cast<const float4*>(resid_in + rs.base + c);
+            const float4 g = *reinterpret_cast<const float4*>(gpost + c);
+            const float4 nv = make_float4(__fadd_rn(ri.x, __fmul_rn(__fmul_rn(v.x, r1), __fadd_rn(1.0f, g.x))),
+                                          __fadd_rn(ri.y, __fmul_rn(__fmul_rn(v.y, r1), __fadd_rn(1.0f, g.y))),
+                                          __fadd_rn(ri.z, __fmul_rn(__fmul_rn(v.z, r1), __fadd_rn(1.0f, g.z))),
+                                          __fadd_rn(ri.w, __fmul_rn(__fmul_rn(v.w, r1), __fadd_rn(1.0f, g.w))));
+            *reinterpret_cast<float4*>(row + (c - rs.c0)) = nv;
+            *reinterpret_cast<float4*>(resid_out + rs.base + c) = nv;
+            ss += nv.x * nv.x + nv.y * nv.y + nv.z * nv.z + nv.w * nv.w;
         }
     }
-    ss = rt::block_sum(ss, red);
+    ss = cluster_reduce<false>(ss, red, &slot[1]);
     const float r2 = 1.0f / sqrtf(ss * inv_d + eps);
     float mx = 0.f;
-    for (int c = tid; c < H; c += nthr) {
-        const float x = __fmul_rn(__fmul_rn(row[c], r2), __fadd_rn(1.0f, gpre[c]));
-        row[c] = x;
-        mx = fmaxf(mx, fabsf(x));
+    for (int c = rs.c0 + 4 * tid; c < rs.c1; c += step) {
+        const float4 v = *reinterpret_cast<const float4*>(row + (c - rs.c0));
+        const float4 g = *reinterpret_cast<const float4*>(gpre + c);
+        const float4 x = make_float4(__fmul_rn(__fmul_rn(v.x, r2), __fadd_rn(1.0f, g.x)),
+                                     __fmul_rn(__fmul_rn(v.y, r2), __fadd_rn(1.0f, g.y)),
+                                     __fmul_rn(__fmul_rn(v.z, r2), __fadd_rn(1.0f, g.z)),
+                                     __fmul_rn(__fmul_rn(v.w, r2), __fadd_rn(1.0f, g.w)));
+        *reinterpret_cast<float4*>(row + (c - rs.c0)) = x;
+        mx = abs_max4(mx, x);
     }
-    store_f16_row(row, H, mx, red, out + base, oscale + b);
+    store_f16_slice(row, rs, mx, red, &slot[2], out, oscale + b);
 }
 
 // h[b][j] = gelu_tanh(gate) * up from the interleaved gate/up GEMM output
 // (column 2j gate, 2j + 1 up), its split parts added in order; h goes out as an
-// fp16 GEMM row with its scale.  Dynamic shared memory: F floats.
-__global__ void __launch_bounds__(kRowThreads) gelu_rows_kernel(const float* c, int parts, int64_t part_stride, int F,
-                                                                uint16_t* out, float* oscale) {
-    extern __shared__ float h[];  // [F]
+// fp16 GEMM row with its scale.  Rows of F outputs (a multiple of 4).
+__global__ void __launch_bounds__(kRowCta) gelu_rows_kernel(const float* c, int parts, int64_t part_stride, int F,
+                                                           uint16_t* out, float* oscale) {
+    extern __shared__ float4 h4[];
+    float* h = reinterpret_cast<float*>(h4);
     __shared__ float red[32];
-    const int b = blockIdx.x;
-    const float* r = c + static_cast<int64_t>(b) * 2 * F;
+    __shared__ float slot[1];
+    const RowSlice rs = row_slice(F);
+    const int b = static_cast<int>(rs.base / F);
+    const int64_t in = 2 * rs.base;  // row b of the [B][2F] input
     float mx = 0.f;
-    for (int j = threadIdx.x; j < F; j += blockDim.x) {
-        const float g = sum_parts_at(r, parts, part_stride, 2 * j), u = sum_parts_at(r, parts, part_stride, 2 * j + 1);
-        const float v = __fmul_rn(rt::gcore::gelu_tanh_dev(g), u);
-        h[j] = v;
-        mx = fmaxf(mx, fabsf(v));
+    for (int j = rs.c0 + 4 * threadIdx.x; j < rs.c1; j += 4 * blockDim.x) {
+        const float4 a = ld_parts4(c, parts, part_stride, in + 2 * j);      // g0 u0 g1 u1
+        const float4 e = ld_parts4(c, parts, part_stride, in + 2 * j + 4);  // g2 u2 g3 u3
+        const float4 v = make_float4(__fmul_rn(rt::gcore::gelu_tanh_dev(a.x), a.y),
+                                     __fmul_rn(rt::gcore::gelu_tanh_dev(a.z), a.w),
+                                     __fmul_rn(rt::gcore::gelu_tanh_dev(e.x), e.y),
+                                     __fmul_rn(rt::gcore::gelu_tanh_dev(e.z), e.w));
+        *reinterpret_cast<float4*>(h + (j - rs.c0)) = v;
+        mx = abs_max4(mx, v);
     }
-    store_f16_row(h, F, mx, red, out + static_cast<int64_t>(b) * F, oscale + b);
+    store_f16_slice(h, rs, mx, red, &slot[0], out, oscale + b);
 }
 
-// Row b of `in` ([B][n] f32) as an fp16 GEMM row with its scale.  Dynamic
-// shared memory: n floats.
-__global__ void __launch_bounds__(kRowThreads) f16_rows_kernel(const float* in, int n, uint16_t* out, float* oscale) {
-    extern __shared__ float v[];  // [n]
+// Row b of `in` ([B][n] f32, n a multiple of 4) as an fp16 GEMM row with its
+// scale.
+__global__ void __launch_bounds__(kRowCta) f16_rows_kernel(const float* in, int n, uint16_t* out, float* oscale) {
+    extern __shared__ float4 v4[];
+    float* v = reinterpret_cast<float*>(v4);
     __shared__ float red[32];
-    const int b = blockIdx.x;
-    const float* r = in + static_cast<int64_t>(b) * n;
+    __shared__ float slot[1];
+    const RowSlice rs = row_slice(n);
     float mx = 0.f;
-    for (int c = threadIdx.x; c < n; c += blockDim.x) {
-        v[c] = r[c];
-        mx = fmaxf(mx, fabsf(v[c]));
+    for (int c = rs.c0 + 4 * threadIdx.x; c < rs.c1; c += 4 * blockDim.x) {
+        const float4 x = *reinterpret_cast<const float4*>(in + rs.base + c);
+        *reinterpret_cast<float4*>(v + (c - rs.c0)) = x;
+        mx = abs_max4(mx, x);
     }
-    store_f16_row(v, n, mx, red, out + static_cast<int64_t>(b) * n, oscale + b);
+    store_f16_slice(v, rs, mx, red, &slot[0], out, oscale + rs.base / n);
+}
+
+// CTAs per row: enough CTAs in flight for small batches, at most 8 (the
+// portable cluster size), and a slice that fits 48 KB of shared memory.
+int row_cluster(int rows, int n) {
+    int cl = rows >= 128 ? 2 : rows >= 32 ? 4 : 8;
+    while (cl < 8 && (n + 4 * cl - 1) / (4 * cl) * 4 * sizeof(float) > 48 * 1024) cl *= 2;
+    return cl;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_rows(void (*k)(KArgs...), int rows, int n, cudaStream_t s, Args... args) {
+    const int cl = row_cluster(rows, n);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(rows * cl));
+    cfg.blockDim = dim3(kRowCta);
+    cfg.dynamicSmemBytes = sizeof(float) * ((n + 4 * cl - 1) / (4 * cl) * 4);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = static_cast<unsigned>(cl);
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
 // Greedy token of each row (largest logit, ties to the higher index), then
@@ -518,7 +626,6 @@ bool build_plan(rt_batch* t, int m, int lm_row0, int lm_rows, RowsPlan* pl) {
 cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax) {
     rt_dec* d = t->dec;
     const int B = pl.m, H = t->H, D = t->D, G = t->NQ / t->NKV;
-    const size_t norm_smem = sizeof(float) * H;
     const float eps = d->cfg.rms_norm_eps;
     int p = 0;
     int n = 0;
@@ -567,17 +674,17 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
     for (int l = 0; l < t->NL && e == cudaSuccess; ++l) {
         // residual update (or embedding) + attention RMSNorm -> x
         if (l == 0) {
-            resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(d->embed, t->tokens, sqrtf(static_cast<float>(H)), nullptr,
-                                                             0, 0, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0),
-                                                             eps, H, t->xa, t->xscale);
+            if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, d->embed, t->tokens, sqrtf(static_cast<float>(H)),
+                                nullptr, 0, int64_t{0}, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0), eps, H,
+                                t->xa, t->xscale)))
+                break;
         } else {
-            resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, pdown.src, pdown.parts,
-                                                             pdown.stride, t->resid[p], t->resid[1 - p],
-                                                             rt::norm_ptr(d, l - 1, 3), rt::norm_ptr(d, l, 0), eps, H,
-                                                             t->xa, t->xscale);
+            if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts,
+                                pdown.stride, t->resid[p], t->resid[1 - p], rt::norm_ptr(d, l - 1, 3),
+                                rt::norm_ptr(d, l, 0), eps, H, t->xa, t->xscale)))
+                break;
             p = 1 - p;
         }
-        if (!ok(cudaGetLastError())) break;
         // qkv
         const BatchGemm& gq = pl.qkv[l];
         if (gq.p.splits > 1) {
@@ -659,35 +766,31 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
             a.seq_out = static_cast<int64_t>(t->NQ) * D;
             if (!ok(rt::attention_launch_batch(a, B, s))) break;
         }
-        f16_rows_kernel<<<B, kRowThreads, sizeof(float) * t->NQ * D, s>>>(t->attn, t->NQ * D, t->xa, t->xscale);
-        if (!ok(cudaGetLastError())) break;
+        if (!ok(launch_rows(f16_rows_kernel, B, t->NQ * D, s, t->attn, t->NQ * D, t->xa, t->xscale))) break;
         // o, then residual update + pre-FFN RMSNorm
         const Proj po = project(pl.o[l]);
         if (!po.src) break;
-        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, po.src, po.parts, po.stride,
-                                                         t->resid[p], t->resid[1 - p],
-                                                         rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa,
-                                                         t->xscale);
+        if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, po.src, po.parts, po.stride,
+                            t->resid[p], t->resid[1 - p], rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa,
+                            t->xscale)))
+            break;
         p = 1 - p;
-        if (!ok(cudaGetLastError())) break;
         // gate/up, GELU gate
         const BatchGemm& gg = pl.gu[l];
         if (!gemm(gg, t->parts)) break;
-        gelu_rows_kernel<<<B, kRowThreads, sizeof(float) * t->F, s>>>(t->parts, gg.p.splits,
-                                                                    static_cast<int64_t>(B) * 2 * t->F, t->F, t->xa,
-                                                                    t->xscale);
-        if (!ok(cudaGetLastError())) break;
+        if (!ok(launch_rows(gelu_rows_kernel, B, t->F, s, t->parts, gg.p.splits, static_cast<int64_t>(B) * 2 * t->F,
+                            t->F, t->xa, t->xscale)))
+            break;
         // down
         pdown = project(pl.down[l]);
         if (!pdown.src) break;
     }
     if (e == cudaSuccess && pl.lm_rows > 0) {
         // final residual update + norm, LM head, greedy tokens
-        resid_norm_rows_kernel<<<B, kRowThreads, norm_smem, s>>>(nullptr, nullptr, 0.f, pdown.src, pdown.parts,
-                                                         pdown.stride, t->resid[p], t->resid[1 - p],
-                                                         rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
-                                                         t->xscale);
-        if (ok(cudaGetLastError()) && gemm(pl.lm, t->logits) && argmax) {
+        if (ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts, pdown.stride,
+                           t->resid[p], t->resid[1 - p], rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
+                           t->xscale)) &&
+            gemm(pl.lm, t->logits) && argmax) {
             if (t->nranks == 1) {
                 argmax_rows_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->vr, t->tokens, t->pos);
                 ok(cudaGetLastError());
@@ -797,6 +900,9 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, const TpInit* tp
         release(t);
         return rc;
     };
+    if (t->H % 4 || t->F % 4 || (t->NQ * t->D) % 4)  // the row kernels' float4 slices
+        return bail(fail(ctx, RT_E_SHAPE, "batch engine: hidden %d / FFN %d / heads x head_dim %d not multiples of 4",
+                         t->H, t->F, t->NQ * t->D));
     if (rows_mode && !t->chunk_path)
         return bail(fail(ctx, RT_E_SHAPE, "rows engine: head_dim %d with %d query heads per KV head is not supported", t->D, G));
     int rc;
