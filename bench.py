@@ -239,7 +239,7 @@ def batch_decode_config3(args, cfg, dec, ctx, ext, world, rank, dist, device, hb
         "hbm_gbs_per_gpu": gbs, "frac": gbs / hbm_peak, "bytes_per_step_per_gpu": per_step,
         "device_bytes_per_gpu": mem, "gpu_launches_per_step": launches,
         "kv": "f32, synthetic contents at the 4096-token context (no prefill)",
-        "gemm_operands": "bf16 activations and dequantised weights, f32 accumulation",
+        "gemm_operands": "fp16 activation rows (power-of-two row scales) and dequantised weights, f32 accumulation",
         "method": "one CUDA graph replay per step, CUDA events around 128 steps after 3 warm-up, max over ranks",
     }
 
