@@ -570,6 +570,13 @@ GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms, bool wbf16, boo
     // 64 projections 10-30% slower from the partial sums).
     const int64_t slots = sms * ((!use_big && m <= 16) ? 2 : 1);
     if (allow_split && m <= 128) splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(std::min(nsb, 8), slots / (gx * gy))));
+    // Q4_K tiles that alone fill half a wave to two waves of the small-M slots
+    // leave the last wave's SMs idle; 3 splits above one wave, 4 below, give
+    // them work when K is long (measured, M = 1 and 8: 27B gate/up N = 43008
+    // 117 -> 103 us, its 2-rank shard N = 21504 91 -> 84 us; with K = 2560,
+    // 10 super-blocks, splitting is slower, so K needs 16 or more).
+    if (allow_split && !wbf16 && m <= 16 && splits == 1 && nsb >= 16 && 2 * gx * gy >= slots && gx * gy < 2 * slots)
+        splits = gx * gy > slots ? 3 : 4;
     if (const char* t = getenv("RT_GEMM_SPLITS")) splits = std::max(1, std::min(nsb, atoi(t)));  // tests
     const int per = (nsb + splits - 1) / splits;
     p.kps = per * 256;
