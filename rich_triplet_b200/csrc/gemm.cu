@@ -404,10 +404,18 @@ __global__ void __launch_bounds__(kThreads, Cfg<NACC, BN, AROWS>::kCtasPerSm)
         const int h_first = C::kTpr == 2 ? (d & 1) : 0, h_count = C::kTpr == 2 ? 1 : 2;
         if constexpr (WB) {
             // bf16 W tile -> fp16 in place (the swizzled layout is the same for
-            // both types); the stage's previous MMA finished before its refill.
+            // both types).  The stage's previous MMA is waited for first: with
+            // an odd ring (3 stages) a stage alternates between the two groups,
+            // and without that wait a group could test w_full[s] while the
+            // previous K-block's copy into the stage had not landed, so that
+            // its parity matched the phase two back.
             for (int kb = dgrp; kb < nkb; kb += kDeqGroups) {
                 if (*reinterpret_cast<volatile int*>(abort_flag)) break;
                 const int s = kb % kStages;
+                if (kb >= kStages && !wait_phase(&empty[s], static_cast<uint32_t>(kb / kStages - 1) & 1u)) {
+                    fail(abort_flag, err);
+                    break;
+                }
                 if (!wait_phase(&w_full[s], static_cast<uint32_t>(kb / kStages) & 1u)) {
                     fail(abort_flag, err);
                     break;
@@ -549,6 +557,10 @@ GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms, bool wbf16, boo
     const int64_t small = ((m + 127) / 128) * ((n + 127) / 128), big = ((m + 255) / 256) * ((n + 255) / 256);
     const int64_t sms = num_sms > 0 ? num_sms : 148;
     bool use_big = ((big + sms - 1) / sms) * 2 <= (small + sms - 1) / sms;
+    // BF16 weights at M <= 64 (LM heads) stream at twice the rate through the
+    // swapped 128 tile, two CTAs per SM (measured: 262144 x 5376 at M = 1 / 8
+    // 886 / 926 -> 439 / 447 us; 262144 x 2560 at M = 64 426 -> 257 us).
+    if (wbf16 && m <= 64) use_big = false;
     // RT_GEMM_TILE=128 or 256 forces the tile (tests and tuning).
     if (const char* t = getenv("RT_GEMM_TILE")) {
         if (atoi(t) == 128) use_big = false;

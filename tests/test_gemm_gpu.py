@@ -181,7 +181,7 @@ def test_gemm_q4k_split_k(orc, tile, monkeypatch, splits, m, n, k):
 
 
 @pytest.mark.parametrize("splits", [1, 2])
-@pytest.mark.parametrize("m,n,k", [(8, 512, 2560), (130, 1000, 512)])
+@pytest.mark.parametrize("m,n,k", [(8, 512, 2560), (48, 1000, 2560), (64, 4096, 2560), (130, 1000, 512)])
 def test_gemm_bf16_weights(tile, monkeypatch, splits, m, n, k):
     # BF16 weights (the LM head of a many-sequence step): both operands are
     # bf16 values, exact in fp16 (A after its row scale), so the product
