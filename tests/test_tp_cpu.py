@@ -1,7 +1,8 @@
 """Tensor-parallel sharding (rich_triplet_b200.tp) on the host: shards made
 directly equal slices of the whole model, the row-split projections add up
 to the whole product (dequantised with the oracle), and the NCCL id reaches
-every rank (gloo, two processes)."""
+every rank and the peer all-reduce handles are gathered in rank order
+(gloo, two processes)."""
 
 import os
 
@@ -78,3 +79,44 @@ def test_nccl_id_reaches_every_rank(tmp_path):
     mp.spawn(_id_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         assert (tmp_path / f"id{r}").read_bytes() == bytes(range(128))
+
+
+class _PeerStub:
+    """TpBatchDecoder's handle exchange with the C-ABI calls replaced: each
+    rank's handle is 64 bytes of its rank number; peer_open records what it
+    was given."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.opened = None
+
+    def peer_handle(self):
+        return bytes([self.rank]) * 64
+
+    def peer_open(self, handles):
+        self.opened = b"".join(bytes(h) for h in handles)
+
+
+def _peer_worker(rank, world, port, out):
+    import torch.distributed as dist
+
+    from rich_triplet_b200.tp import TpBatchDecoder
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        stub = _PeerStub(rank)
+        TpBatchDecoder.enable_peer_allreduce(stub, dist)
+        with open(os.path.join(out, f"peer{rank}"), "wb") as f:
+            f.write(stub.opened)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_handles_reach_every_rank_in_rank_order(tmp_path):
+    # rt_tp_peer_open takes every rank's 64-byte handle, rank 0 first.
+    import torch.multiprocessing as mp
+    port = 29700 + os.getpid() % 1000
+    mp.spawn(_peer_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        assert (tmp_path / f"peer{r}").read_bytes() == bytes([0]) * 64 + bytes([1]) * 64
