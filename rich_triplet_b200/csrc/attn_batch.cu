@@ -353,8 +353,22 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const AttnChunkArgs a) 
 // acore::head_prep_warp in the same order, with the NeoX pairs (j, j + D/2)
 // taken from registers: for D a multiple of 64 both halves of a pair belong
 // to the same lane (element j is lane j % 32's value D/32-slot j / 32).
-__device__ __forceinline__ void head_prep_reg(const float* raw, const float* gamma, const float* cs, const float* sn,
-                                              int D, float eps, float* dst) {
+// raw[0] + raw[stride] + ... (`parts` <= 8 terms, added in part order as the
+// split-K sum kernel adds them), every load issued before the first add.
+__device__ __forceinline__ float ld_parts(const float* raw, int parts, int64_t stride) {
+    constexpr int kMax = 8;  // the GEMM plan's split cap
+    float w[kMax];
+#pragma unroll
+    for (int q = 0; q < kMax; ++q) w[q] = q < parts ? raw[q * stride] : 0.f;
+    float v = w[0];
+#pragma unroll
+    for (int q = 1; q < kMax; ++q)
+        if (q < parts) v += w[q];
+    return v;
+}
+
+__device__ __forceinline__ void head_prep_reg(const float* raw, int parts, int64_t stride, const float* gamma,
+                                              const float* cs, const float* sn, int D, float eps, float* dst) {
     constexpr int kMaxPer = acore::kMaxHeadDim / 32;
     const int lane = threadIdx.x & 31, per = D / 32, hp = per / 2;
     float x[kMaxPer];
@@ -362,7 +376,7 @@ __device__ __forceinline__ void head_prep_reg(const float* raw, const float* gam
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
         const int j = lane + 32 * i;
-        x[i] = i < per ? raw[j] : 0.f;
+        x[i] = i < per ? ld_parts(raw + j, parts, stride) : 0.f;
     }
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) ss += x[i] * x[i];
@@ -385,18 +399,20 @@ __global__ void attn_rows_prep_kernel(const AttnRowsArgs a) {
     const int b = blockIdx.x, head = blockIdx.y, lane = threadIdx.x;
     const int D = a.D;
     const int p = a.pos[b];
+    const int parts = a.parts > 1 ? a.parts : 1;
     const float* row = a.qkv + static_cast<int64_t>(b) * a.qkv_stride;
     const float* cs = a.rope_cos + static_cast<int64_t>(p) * (D / 2);
     const float* sn = a.rope_sin + static_cast<int64_t>(p) * (D / 2);
     if (head < a.nq) {
-        head_prep_reg(row + static_cast<int64_t>(head) * D, a.q_norm, cs, sn, D, a.eps,
+        head_prep_reg(row + static_cast<int64_t>(head) * D, parts, a.part_stride, a.q_norm, cs, sn, D, a.eps,
                       a.q_out + (static_cast<int64_t>(b) * a.nq + head) * D);
     } else {
         const int h = head - a.nq;
         const int64_t off = b * a.seq_kv + (static_cast<int64_t>(h) * a.cap + p) * D;
-        head_prep_reg(row + static_cast<int64_t>(a.nq + h) * D, a.k_norm, cs, sn, D, a.eps, a.kcache + off);
+        head_prep_reg(row + static_cast<int64_t>(a.nq + h) * D, parts, a.part_stride, a.k_norm, cs, sn, D, a.eps,
+                      a.kcache + off);
         const float* vr = row + static_cast<int64_t>(a.nq + a.nkv + h) * D;
-        for (int d = lane; d < D; d += 32) a.vcache[off + d] = vr[d];
+        for (int d = lane; d < D; d += 32) a.vcache[off + d] = ld_parts(vr + d, parts, a.part_stride);
     }
 }
 

@@ -28,6 +28,8 @@ constexpr int kAttnChunk = 256;  // cached positions per work item
 struct AttnRowsArgs {
     const float* qkv;                 // [B][qkv_stride]: row b's [nq*D | nkv*D | nkv*D] raw projections
     int64_t qkv_stride;
+    int parts;                        // split-K parts at qkv + q * part_stride, added in part order (<= 1: one)
+    int64_t part_stride;
     const float* q_norm;              // [D] gamma of the per-head q norm
     const float* k_norm;              // [D]
     const float* rope_cos;            // [cap][D/2] for this layer's theta / scale

@@ -687,7 +687,10 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         }
         // qkv
         const BatchGemm& gq = pl.qkv[l];
-        if (gq.p.splits > 1) {
+        const bool qkv_parts = t->chunk_path && gq.p.splits > 1;  // the prep kernel adds the parts
+        if (qkv_parts) {
+            if (!gemm(gq, t->parts)) break;
+        } else if (gq.p.splits > 1) {
             if (!gemm(gq, t->parts)) break;
             if (!ok(rt::sum_parts_launch(t->parts, gq.p.splits, static_cast<int64_t>(B) * t->qkv_rows, t->qkv,
                                          t->ctx->num_sms, s)))
@@ -703,8 +706,10 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         const int window = rt::is_global(l) ? 0 : d->cfg.sliding_window;
         if (t->chunk_path) {
             rt::AttnRowsArgs pr{};
-            pr.qkv = t->qkv;
+            pr.qkv = qkv_parts ? t->parts : t->qkv;
             pr.qkv_stride = t->qkv_rows;
+            pr.parts = qkv_parts ? gq.p.splits : 1;
+            pr.part_stride = static_cast<int64_t>(B) * t->qkv_rows;
             pr.q_norm = d->qk_norms + static_cast<size_t>(l) * 2 * D;
             pr.k_norm = pr.q_norm + D;
             pr.rope_cos = rope_cos;

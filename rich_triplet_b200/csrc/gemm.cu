@@ -557,10 +557,12 @@ GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms, bool wbf16, boo
     const int64_t small = ((m + 127) / 128) * ((n + 127) / 128), big = ((m + 255) / 256) * ((n + 255) / 256);
     const int64_t sms = num_sms > 0 ? num_sms : 148;
     bool use_big = ((big + sms - 1) / sms) * 2 <= (small + sms - 1) / sms;
-    // BF16 weights at M <= 64 (LM heads) stream at twice the rate through the
-    // swapped 128 tile, two CTAs per SM (measured: 262144 x 5376 at M = 1 / 8
-    // 886 / 926 -> 439 / 447 us; 262144 x 2560 at M = 64 426 -> 257 us).
-    if (wbf16 && m <= 64) use_big = false;
+    // At M <= 64 the product is a weight stream, and the swapped 128 tile (two
+    // CTAs per SM) streams faster than the 256 tile that the estimate picks
+    // for wide N (measured: BF16 262144 x 5376 at M = 1 / 8 886 / 926 -> 446 /
+    // 454 us, 262144 x 2560 at M = 64 426 -> 262 us; Q4_K 20480 x 2560 at
+    // M = 1 / 8 / 64 51.3 / 43.0 / 47.5 -> 39.1 / 40.3 / 43.4 us).
+    if (m <= 64) use_big = false;
     // RT_GEMM_TILE=128 or 256 forces the tile (tests and tuning).
     if (const char* t = getenv("RT_GEMM_TILE")) {
         if (atoi(t) == 128) use_big = false;
