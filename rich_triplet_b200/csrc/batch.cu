@@ -743,6 +743,7 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
             ca.out = t->attn;
             ca.err = t->ctx->d_err;
             if (!ok(rt::attn_chunk_launch(ca, t->ctx->num_sms, s))) break;
+            if (ca.nchunk > 1) ++n;  // the merge kernel launched with it
         } else {
             rt::AttnArgs a{};
             a.qkv = t->qkv;
