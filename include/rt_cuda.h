@@ -141,6 +141,14 @@ int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
  * the tied LM head over several sequences' final hidden states: replaces
  * MatBf16::matmul_by_t with M > 1 (src/autograd2.rs:757-776, 954-1000). */
 int rt_gemm_bf16(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags);
+/* The launch plan rt_gemm_q4k / rt_gemm_bf16 (and the many-sequence engines)
+ * choose for an [m, k] x [n, k]^T product on a GPU with num_sms SMs, without
+ * a GPU (no counterpart in the reference): out[0] the CTA tile (128: weight
+ * rows as the 128-row operand, activations as the narrow one when m <= 64;
+ * 256: 256 x 256), out[1] the split-K count, out[2] the activation rows per
+ * tile, out[3] the K columns per split.  RT_E_SHAPE when no plan exists.
+ * The RT_GEMM_TILE / RT_GEMM_SPLITS tuning overrides apply. */
+int rt_gemm_plan(int64_t m, int64_t n, int32_t k, int32_t num_sms, int32_t bf16_weights, int32_t* out);
 
 /* GEMV throughput measurement (no counterpart in the reference, whose GEMV
  * test times nothing).  Captures one CUDA graph of `launches` GEMVs of the

@@ -337,6 +337,17 @@ int rt_gemm_bf16(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c,
     return gemm_common(ctx, w, a, m, c, flags, RT_FMT_BF16);
 }
 
+int rt_gemm_plan(int64_t m, int64_t n, int32_t k, int32_t num_sms, int32_t bf16_weights, int32_t* out) {
+    if (!out) return RT_E_INVAL;
+    const rt::GemmPlan p = rt::gemm_q4k_plan(m, n, k, num_sms, bf16_weights != 0, true);
+    if (p.bm == 0) return RT_E_SHAPE;
+    out[0] = p.bm;
+    out[1] = p.splits;
+    out[2] = p.arows;
+    out[3] = p.kps;
+    return RT_OK;
+}
+
 int rt_gemv_bench(rt_ctx* ctx, int fmt, const rt_w* const* ws, int nw, const float* x, float* y, int launches,
                   int ctas_per_sm, int reps, float* us_per_gemv) {
     if (!ctx || !ws || nw < 1 || !x || !y || !us_per_gemv) return fail(ctx, RT_E_INVAL, "rt_gemv_bench: null argument");
