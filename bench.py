@@ -46,7 +46,7 @@ def parse():
     p.add_argument("--no-config4", action="store_true", help="skip the 27B tensor-parallel section")
     p.add_argument("--tp-allreduce", default="nccl", choices=["peer", "nccl"],
                    help="config 4's per-layer sums: peer all-reduce kernel over NVLink, or NCCL")
-    p.add_argument("--cpu-steps", type=int, default=3)
+    p.add_argument("--cpu-steps", type=int, default=10)
     p.add_argument("--prompt", type=int, default=PROMPT,
                    help="prompt tokens prefilled before the timed steps (512 = BASELINE config 1; "
                         "shorter only for profiling)")
@@ -132,10 +132,24 @@ def argmax_last(v):
     return int(np.flatnonzero(v == v.max())[-1])
 
 
+def config1_dict(cfg, world):
+    """The `config` object of both arms' lines."""
+    return {"workload": f"gemma3-4b Q4_K decode bs=1 (BASELINE config 1), layers={cfg.num_hidden_layers}",
+            "prompt": PROMPT, "decode_positions": [PROMPT, PROMPT + SPAN - 1], "kv": "f32",
+            "vocab": cfg.vocab_size, "l2": "inputs larger than L2: 3.3 GB of weights + KV per step",
+            "parallelism": f"dp{world} (one sequence and weight replica per GPU)"}
+
+
+REF_MAX_STEPS = 64
+
+
 def run_reference(args):
     """Reference arm: the CPU decode step (oracle restatement of the reference's
-    x86 path) on all host threads, on config 1's shapes."""
+    x86 path) on all host threads, on config 1's shapes.  Only liboracle.so is
+    loaded: the synthetic model comes from its own copy of the seeded
+    generator."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import numpy as np
@@ -143,22 +157,23 @@ def run_reference(args):
     from oracle import oracle as orc
     from rich_triplet_b200.model import Config4, synth_gemma3, synth_normal, synth_tokens
 
+    gen = orc.lib
     cfg = Config4.gemma3_4b(vocab_size=262144).with_layers(args.layers)
-    w = synth_gemma3(cfg, seed=args.seed)
+    w = synth_gemma3(cfg, seed=args.seed, gen=gen)
     cap = PROMPT + SPAN
     om = orc.OracleModel(cfg, w, cap, nthreads=0)
     kvd = cfg.num_key_value_heads * cfg.head_dim
     # Positions 0..511 of every layer's f32 cache hold N(0,1) values: prefilling
-    # 512 tokens through the CPU path would take tens of minutes, and a decode
-    # step reads the same bytes whatever the cached values are.
+    # 512 tokens through the CPU path would take minutes, and a decode step
+    # reads the same bytes whatever the cached values are.
     for layer in range(cfg.num_hidden_layers):
         kc = np.ctypeslib.as_array(orc.lib.or_model_kcache(om._h, layer), shape=(cap * kvd,))
         vc = np.ctypeslib.as_array(orc.lib.or_model_vcache(om._h, layer), shape=(cap * kvd,))
-        kc[: PROMPT * kvd] = synth_normal(args.seed, 5000 + 2 * layer, PROMPT * kvd)
-        vc[: PROMPT * kvd] = synth_normal(args.seed, 5001 + 2 * layer, PROMPT * kvd)
-    tok = int(synth_tokens(args.seed, 100, 1, cfg.vocab_size)[0])
-    n_warm = min(args.warmup, 1)
-    n_steps = max(1, min(args.steps, args.cpu_steps))
+        kc[: PROMPT * kvd] = synth_normal(args.seed, 5000 + 2 * layer, PROMPT * kvd, gen=gen)
+        vc[: PROMPT * kvd] = synth_normal(args.seed, 5001 + 2 * layer, PROMPT * kvd, gen=gen)
+    tok = int(synth_tokens(args.seed, 100, 1, cfg.vocab_size, gen=gen)[0])
+    n_warm = max(1, min(args.warmup, 8))
+    n_steps = max(1, min(args.steps, REF_MAX_STEPS))
     om.set_seq_len(PROMPT)
     for _ in range(n_warm):
         tok = orc.sample_greedy(om.step(tok))
@@ -173,16 +188,53 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": n_steps, "warmup": n_warm, "ms_per_step": dt * 1e3 / n_steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"gemma3-4b decode bs=1 (layers={cfg.num_hidden_layers}), positions 512..",
-                   "prompt": PROMPT, "kv": "f32", "parallelism": "cpu threads"},
+        "config": config1_dict(cfg, world),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": f"{n_steps} CPU decode steps at positions 512.. (requested {args.steps}); "
+                         "sample": f"{n_steps} CPU decode steps at positions 512.. (steps capped at {REF_MAX_STEPS}); "
                                    "reference is Rust (no toolchain here): oracle/ C restatement of its x86 path, "
                                    "row-parallel over all host threads; KV rows 0..511 synthetic"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     om.close()
+
+
+def cpu_baselines_config0_config2(args, orc):
+    """The reference CPU path of BASELINE configs 0 and 2 timed on the host:
+    config 0's Q4_K GEMV (Q4KMat::gemv_mt: rows split over all host threads)
+    and config 2's Q4_K GEMM at M = 512 (Q4KMat::matmul_q4k_t, single-threaded
+    in the reference), the latter on a bounded sample of output rows."""
+    import numpy as np
+
+    from rich_triplet_b200.model import synth_normal, synth_q4k
+
+    gen = orc.lib
+    out = {}
+    for rows, cols in ((10240, 2560), (2560, 10240)):
+        blocks = synth_q4k(args.seed, 9000, rows, cols, gen=gen)
+        x = synth_normal(args.seed, 9100, cols, gen=gen)
+        orc.q4k_gemv(blocks, rows, cols, x)
+        reps = 20
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            orc.q4k_gemv(blocks, rows, cols, x)
+        us = (time.perf_counter() - t0) * 1e6 / reps
+        b = rows * cols // 256 * 144 + cols * 4 + rows * 4
+        out[f"config0_gemv_{rows}x{cols}"] = {"us": us, "gbs": b / (us * 1e-6) / 1e9, "cores": os.cpu_count(),
+                                              "kind": "port", "sample": f"{reps} GEMVs, all host threads"}
+    m = 512
+    for name, k, n in (("qkv", 2560, 4096), ("o", 2048, 2560), ("gate_up", 2560, 20480), ("down", 10240, 2560)):
+        ns = 16  # output rows sampled: the loop is the same for every row
+        blocks = synth_q4k(args.seed, 9200 + n + k, ns, k, gen=gen)
+        a = synth_normal(args.seed, 9300 + m, m * k, gen=gen).reshape(m, k)
+        t0 = time.perf_counter()
+        orc.q4k_gemm(blocks, ns, k, a)
+        dt = time.perf_counter() - t0
+        tf = 2.0 * m * ns * k / dt / 1e12
+        out[f"config2_gemm_{name}_M{m}_K{k}_N{n}"] = {
+            "tflops": tf, "est_ms_full": dt * n / ns * 1e3, "cores": 1, "kind": "port",
+            "sample": f"{ns} of {n} output rows, f32 A (the reference's loop is single-threaded)"}
+    return out
 
 
 CONFIG3_SEQS, CONFIG3_CONTEXT, CONFIG3_STEPS = 64, 4096, 128
@@ -543,6 +595,7 @@ def run_ours(args):
                "sample": f"{args.cpu_steps} decode steps at positions 512..{511 + args.cpu_steps} of the same model, "
                          "KV cache copied from the GPU prefill; oracle/ restatement of the reference's x86 path"}
         om.close()
+        cpu["per_config"] = cpu_baselines_config0_config2(args, orc)
 
     # ---- prefill of config 1's prompt with every position at once (tensor-core
     # GEMMs over the 512 tokens), against the token-by-token prefill above ----
@@ -571,10 +624,7 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"gemma3-4b Q4_K decode bs=1 (BASELINE config 1), layers={cfg.num_hidden_layers}",
-                       "prompt": PROMPT, "decode_positions": [PROMPT, PROMPT + SPAN - 1], "kv": "f32",
-                       "vocab": cfg.vocab_size, "l2": "inputs larger than L2: 3.3 GB of weights + KV per step",
-                       "parallelism": f"dp{world} (one sequence and weight replica per GPU)"},
+            "config": config1_dict(cfg, world),
             "roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": step_gbs / hbm_peak, "traffic": traffic, "kernel": kernel_name,
                          "launch_us": ms / args.steps * 1e3, "bytes_per_launch": step_bytes, "peak_kind": peak_kind,

@@ -26,8 +26,13 @@ def build():
     subprocess.run(["make", "-s", "-C", _HERE, "liboracle.so"], check=True)
 
 
+_SOURCES = (os.path.join(_HERE, "oracle.c"), os.path.join(_HERE, "..", "rich_triplet_b200", "csrc", "synth.cpp"))
+
+
 def _load():
-    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "oracle.c")):
+    stale = not os.path.exists(_LIB_PATH) or any(
+        os.path.exists(src) and os.path.getmtime(_LIB_PATH) < os.path.getmtime(src) for src in _SOURCES)
+    if stale:
         build()
     lib = ctypes.CDLL(_LIB_PATH)
     sig = {
@@ -62,6 +67,15 @@ def _load():
         "or_model_set_seq_len": (None, [ctypes.c_void_p, _i64]),
         "or_model_kcache": (_c_f32p, [ctypes.c_void_p, ctypes.c_int]),
         "or_model_vcache": (_c_f32p, [ctypes.c_void_p, ctypes.c_int]),
+        # the seeded generator (synth.cpp, linked in): the same bytes as the
+        # product library's rt_synth_* for the same arguments
+        "rt_synth_q4k": (None, [ctypes.c_uint64, ctypes.c_uint64, _i64, _i64, ctypes.c_void_p]),
+        "rt_synth_normal_f32": (None, [ctypes.c_uint64, ctypes.c_uint64, _i64, ctypes.c_float, ctypes.c_float,
+                                       ctypes.c_void_p]),
+        "rt_synth_normal_bf16": (None, [ctypes.c_uint64, ctypes.c_uint64, _i64, ctypes.c_float, ctypes.c_float,
+                                        ctypes.c_void_p]),
+        "rt_synth_tokens": (None, [ctypes.c_uint64, ctypes.c_uint64, _i64, ctypes.c_int32, ctypes.c_void_p]),
+        "rt_synth_bytes": (None, [ctypes.c_uint64, ctypes.c_uint64, _i64, ctypes.c_void_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -137,55 +137,65 @@ def _ptr(a):
     return ctypes.c_void_p(a.ctypes.data)
 
 
-def synth_q4k(seed, stream, rows, cols):
+# The generator functions below run in whichever loaded library `gen` names
+# (default: librtcuda.so).  Any library that links synth.cpp exports the same
+# rt_synth_* symbols and produces the same bytes; a CPU-only caller passes its
+# own handle so that it never maps the CUDA library.
+def _gen(gen):
+    return gen if gen is not None else lib()
+
+
+def synth_q4k(seed, stream, rows, cols, gen=None):
     """Seeded Q4_K blocks distributed as BASELINE config 0 describes."""
     out = np.empty(rows * (cols // 256) * 144, dtype=np.uint8)
-    lib().rt_synth_q4k(seed, stream, rows, cols, _ptr(out))
+    _gen(gen).rt_synth_q4k(seed, stream, rows, cols, _ptr(out))
     return out
 
 
-def synth_normal(seed, stream, n, mean=0.0, std=1.0):
+def synth_normal(seed, stream, n, mean=0.0, std=1.0, gen=None):
     out = np.empty(n, dtype=np.float32)
-    lib().rt_synth_normal_f32(seed, stream, n, mean, std, _ptr(out))
+    _gen(gen).rt_synth_normal_f32(seed, stream, n, mean, std, _ptr(out))
     return out
 
 
-def synth_normal_bf16(seed, stream, n, mean=0.0, std=1.0):
+def synth_normal_bf16(seed, stream, n, mean=0.0, std=1.0, gen=None):
     out = np.empty(n, dtype=np.uint16)
-    lib().rt_synth_normal_bf16(seed, stream, n, mean, std, _ptr(out))
+    _gen(gen).rt_synth_normal_bf16(seed, stream, n, mean, std, _ptr(out))
     return out
 
 
-def synth_tokens(seed, stream, n, vocab):
+def synth_tokens(seed, stream, n, vocab, gen=None):
     out = np.empty(n, dtype=np.int32)
-    lib().rt_synth_tokens(seed, stream, n, vocab, _ptr(out))
+    _gen(gen).rt_synth_tokens(seed, stream, n, vocab, _ptr(out))
     return out
 
 
-def synth_bytes(seed, stream, n):
+def synth_bytes(seed, stream, n, gen=None):
     out = np.empty(n, dtype=np.uint8)
-    lib().rt_synth_bytes(seed, stream, n, _ptr(out))
+    _gen(gen).rt_synth_bytes(seed, stream, n, _ptr(out))
     return out
 
 
-def synth_gemma3(cfg: Config4, seed=1234, norm_std=0.1, embed_std=0.02):
+def synth_gemma3(cfg: Config4, seed=1234, norm_std=0.1, embed_std=0.02, gen=None):
     """Random-init Gemma 3 weights: Q4_K projections as BASELINE config 0,
-    norm gamma ~ N(0, norm_std), embedding bf16 ~ N(0, embed_std)."""
+    norm gamma ~ N(0, norm_std), embedding bf16 ~ N(0, embed_std).  `gen`: the
+    library whose rt_synth_* generators to run (default librtcuda.so)."""
     H, D, F = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
     q, kv = cfg.num_attention_heads * D, cfg.num_key_value_heads * D
     w = Gemma3Weights(cfg)
     for i in range(cfg.num_hidden_layers):
         s = 1000 + 32 * i
         w.layers.append(Gemma3LayerWeights(
-            q=synth_q4k(seed, s + 0, q, H), k=synth_q4k(seed, s + 1, kv, H), v=synth_q4k(seed, s + 2, kv, H),
-            o=synth_q4k(seed, s + 3, H, q), gate=synth_q4k(seed, s + 4, F, H), up=synth_q4k(seed, s + 5, F, H),
-            down=synth_q4k(seed, s + 6, H, F),
-            attn_norm=synth_normal(seed, s + 7, H, 0.0, norm_std),
-            post_attn_norm=synth_normal(seed, s + 8, H, 0.0, norm_std),
-            pre_ffn_norm=synth_normal(seed, s + 9, H, 0.0, norm_std),
-            post_ffn_norm=synth_normal(seed, s + 10, H, 0.0, norm_std),
-            q_norm=synth_normal(seed, s + 11, D, 0.0, norm_std),
-            k_norm=synth_normal(seed, s + 12, D, 0.0, norm_std)))
-    w.embed = synth_normal_bf16(seed, 7, cfg.vocab_size * H, 0.0, embed_std)
-    w.final_norm = synth_normal(seed, 8, H, 0.0, norm_std)
+            q=synth_q4k(seed, s + 0, q, H, gen), k=synth_q4k(seed, s + 1, kv, H, gen),
+            v=synth_q4k(seed, s + 2, kv, H, gen), o=synth_q4k(seed, s + 3, H, q, gen),
+            gate=synth_q4k(seed, s + 4, F, H, gen), up=synth_q4k(seed, s + 5, F, H, gen),
+            down=synth_q4k(seed, s + 6, H, F, gen),
+            attn_norm=synth_normal(seed, s + 7, H, 0.0, norm_std, gen),
+            post_attn_norm=synth_normal(seed, s + 8, H, 0.0, norm_std, gen),
+            pre_ffn_norm=synth_normal(seed, s + 9, H, 0.0, norm_std, gen),
+            post_ffn_norm=synth_normal(seed, s + 10, H, 0.0, norm_std, gen),
+            q_norm=synth_normal(seed, s + 11, D, 0.0, norm_std, gen),
+            k_norm=synth_normal(seed, s + 12, D, 0.0, norm_std, gen)))
+    w.embed = synth_normal_bf16(seed, 7, cfg.vocab_size * H, 0.0, embed_std, gen)
+    w.final_norm = synth_normal(seed, 8, H, 0.0, norm_std, gen)
     return w
