@@ -98,27 +98,36 @@ int rt_gemv_bf16(rt_ctx* ctx, const rt_w* w, const float* x, float* y, int flags
 
 /* Greedy LM-head step that allocates nothing.  No counterpart in the
  * reference: its LM head and argmax run inside the decode context, whose
- * buffers are created up front (src/metal_decode.rs:1002-1121).
+ * buffers are created up front (src/metal_decode.rs:1002-1121).  It is for
+ * callers that cannot call cudaMalloc at that point: a serving process that
+ * has handed nearly all HBM to its own KV-cache pool, or a token loop that
+ * cannot take cudaMalloc's implicit device synchronisation.
  *
  * Enqueues, on `stream` (a cudaStream_t; NULL = the legacy default stream) of
  * the CURRENT device: y_dev[r] = bf16(W[r, :]) . x_dev for the [rows, cols]
- * row-major BF16 matrix at w_dev, then *token_dev = the row of the largest
- * y_dev (ties to the higher row, as sample_greedy).  All four pointers are
- * device memory the caller owns; w_dev and x_dev 16-byte aligned; cols a
- * multiple of 8.  Returns once the work is enqueued.
+ * row-major BF16 matrix at w_dev, then *token_dev = the greedy token of y_dev
+ * by sample_token's rule at temperature 0 (src/transformer4.rs:3036-3091: the
+ * LAST row of the largest softmax probability; see GreedySlot in the
+ * sources).  All four pointers are device memory the caller owns; w_dev and
+ * x_dev 16-byte aligned; cols a multiple of 8.  Returns once the work is
+ * enqueued.
  *
  * Scratch: no context, no cudaMalloc, no allocating library call.  The only
  * scratch is a file-scope device array (~1.3 MiB per device): for up to
- * RT_ARGMAX_STATIC_SLOTS CTAs a (value, row) argmax slot each and an arrival
- * counter, 32 partial row sums per warp, and a unit counter per 16-row tile
- * for up to RT_ARGMAX_STATIC_MAX_ROWS rows.  The counters must be zero when a
- * launch starts: they are zero at module load and every launch that completes
- * sets them back to zero.  rows beyond RT_ARGMAX_STATIC_MAX_ROWS, cols beyond
- * 2^20 and launches needing more than RT_ARGMAX_STATIC_SLOTS CTAs are
- * rejected with RT_E_SHAPE.
+ * RT_ARGMAX_STATIC_SLOTS CTAs a greedy slot each and an arrival counter, 32
+ * partial row sums per warp, and a unit counter per 16-row tile for up to
+ * RT_ARGMAX_STATIC_MAX_ROWS rows.  The counters must be zero when a launch
+ * starts: they are zero at module load and every launch sets them back to
+ * zero, also a launch in which a bounded device-side wait gave up.  Such a
+ * launch writes *token_dev = -1 (the caller reads the token anyway, so this
+ * is how a failure is reported); the next call starts clean.  rows beyond
+ * RT_ARGMAX_STATIC_MAX_ROWS, cols beyond 2^20 and launches needing more than
+ * RT_ARGMAX_STATIC_SLOTS CTAs are rejected with RT_E_SHAPE.
  * Setup: the first call on each device (with that device current) looks up
  * the scratch address (cudaGetSymbolAddress) and sets the kernel's
- * shared-memory limit; make that first call before any stream capture.
+ * shared-memory limit.  Under CUDA's lazy module loading that first call is
+ * also when the module loads and the array's device memory is reserved: make
+ * it before any stream capture, and while memory for the array is still free.
  * Overlapping calls on one device (two streams, or two threads) share the
  * scratch and race: serialize them.
  * errbuf (may be NULL) receives a one-line reason on failure. */
@@ -327,6 +336,14 @@ int rt_batch_vocab_slice(const rt_batch* b, int32_t* v0, int32_t* vr);
  * Needs 2 to 8 ranks in one process each, on GPUs that reach each other. */
 int rt_tp_peer_handle(rt_batch* b, void* handle_out);
 int rt_tp_peer_open(rt_batch* b, const void* handles);
+
+/* Test hook, no reference counterpart: the peer all-reduce kernel run by
+ * this process as rank 0 of two, with the second rank's buffer a local zeroed
+ * allocation whose flag never rises.  *err_word receives the error word after
+ * two calls (3 = kErrGridTimeout when the first call's bounded flag wait gave
+ * up), *first_ms / *second_ms their device times: the first call waits about
+ * 2 s, the second, seeing the error word, does not wait at all. */
+int rt_test_peer_allreduce_lonely(rt_ctx* ctx, int* err_word, float* first_ms, float* second_ms);
 
 /* Fill every sequence's cache with synthetic values (a seeded hash, unit
  * variance) and set every position to seq_len: the state a benchmark decodes

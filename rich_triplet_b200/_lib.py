@@ -125,6 +125,8 @@ SIGNATURES = {
     "rt_batch_vocab_slice": (ctypes.c_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "rt_tp_peer_handle": (ctypes.c_int, [_vp, _vp]),
     "rt_tp_peer_open": (ctypes.c_int, [_vp, _vp]),
+    "rt_test_peer_allreduce_lonely": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int),
+                                                     ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float)]),
     "rt_synth_q4k_slice": (None, [_u64, _u64, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "rt_synth_normal_f32": (None, [_u64, _u64, _i64, ctypes.c_float, ctypes.c_float, _vp]),
     "rt_synth_normal_bf16": (None, [_u64, _u64, _i64, ctypes.c_float, ctypes.c_float, _vp]),

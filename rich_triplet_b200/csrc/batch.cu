@@ -134,8 +134,8 @@ struct rt_batch {
     PeerBufs peers{};
     void* opened[kMaxRanks] = {};
     int32_t* step_ctr = nullptr;
-    uint32_t* am_send = nullptr;  // [B][2] this rank's best logit: (value bits, vocab index)
-    uint32_t* am_recv = nullptr;  // [nranks][B][2]
+    uint32_t* am_send = nullptr;  // [B][kTpWords] this rank's greedy record of each row
+    uint32_t* am_recv = nullptr;  // [nranks][B][kTpWords]
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
@@ -365,103 +365,167 @@ cudaError_t launch_rows(void (*k)(KArgs...), int rows, int n, cudaStream_t s, Ar
     return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
-// Greedy token of each row (largest logit, ties to the higher index), then
-// tokens[b] = it and pos[b] += 1.  1024 threads per row.
-__global__ void argmax_rows_kernel(const float* logits, int V, int32_t* tokens, int32_t* pos) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const float* r = logits + static_cast<int64_t>(b) * V;
-    float bv = -INFINITY;
-    int bi = -1;
-    for (int i = tid; i < V; i += blockDim.x) {
-        const float v = r[i];
-        if (v > bv || (v == bv && i > bi)) {
-            bv = v;
-            bi = i;
-        }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi > bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
+// Greedy sampling per row, with sample_token's rule at temperature 0 (the last
+// index of the largest softmax probability; see kGreedyTau in gemv_core.cuh).
+// One CTA of 1024 threads per row: each thread keeps the online state (max,
+// sum of exp(y - max), row of the max) of its strided elements; the CTA
+// combines them in a fixed order into M and S; then only threads whose own
+// maximum is within kGreedyTau of M re-read their elements for candidates.
+struct RowGreedy {
+    float M, S;
+    int best;  // highest candidate index whose probability equals the maximum's
+};
+
+__device__ __forceinline__ RowGreedy row_greedy(const float* r, int V, float* sm, float* ss, long long* si,
+                                                int* sbest) {
+    using rt::gcore::Greedy;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    Greedy g;
+    g.init();
+    for (int i = tid; i < V; i += blockDim.x) g.add(r[i], i);
+    const float my_m = g.m;
+    g.warp_merge();
     if (lane == 0) {
-        sv[warp] = bv;
-        si[warp] = bi;
+        sm[warp] = g.m;
+        ss[warp] = g.s;
+        si[warp] = g.i;
+    }
+    if (tid == 0) *sbest = -1;
+    __syncthreads();
+    Greedy c;
+    c.init();
+    for (int w = 0; w < nw; ++w) c.merge(sm[w], ss[w], si[w], 0, 0);  // every thread, same order
+    RowGreedy out;
+    out.M = c.m;
+    out.S = c.s;
+    const float q = __fdiv_rn(1.0f, c.s), lim = c.m - rt::gcore::kGreedyTau;
+    if (my_m >= lim) {
+        int best = -1;
+        for (int i = tid; i < V; i += blockDim.x) {
+            const float v = r[i];
+            if (v >= lim && rt::gcore::greedy_ties_max(v, c.m, c.s, q)) best = i;
+        }
+        if (best >= 0) atomicMax(sbest, best);
     }
     __syncthreads();
-    if (tid == 0) {
-        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
-            if (sv[w] > bv || (sv[w] == bv && si[w] > bi)) {
-                bv = sv[w];
-                bi = si[w];
-            }
-        tokens[b] = bi;
+    out.best = *sbest;
+    return out;
+}
+
+// Greedy token of each row, then tokens[b] = it and pos[b] += 1.
+__global__ void argmax_rows_kernel(const float* logits, int V, int32_t* tokens, int32_t* pos) {
+    __shared__ float sm[32], ss[32];
+    __shared__ long long si[32];
+    __shared__ int sbest;
+    const int b = blockIdx.x;
+    const RowGreedy g = row_greedy(logits + static_cast<int64_t>(b) * V, V, sm, ss, si, &sbest);
+    if (threadIdx.x == 0) {
+        tokens[b] = g.best;
         pos[b] += 1;
     }
 }
 
-// Row b's largest logit of this rank's vocab slice [v0, v0 + V) as (value
-// bits, vocab index), ties to the higher index.  1024 threads per row.
+// Tensor-parallel greedy: what each rank sends for a row of its vocab slice
+// [v0, v0 + V).  Words: [0] m (its largest logit, bits), [1] s (sum of
+// exp(y - m) over the slice, bits), [2] the number of its logits within
+// kGreedyTau of m, [3] unused, then up to kTpCand (value bits, vocab index)
+// pairs of those logits, highest indices first.  The merge then has every
+// candidate of the global maximum unless a rank holds more than kTpCand logits
+// within kGreedyTau of its own maximum (counted in word 2): it then decides
+// among the kTpCand highest of them.
+constexpr int kTpCand = 4;
+constexpr int kTpWords = 4 + 2 * kTpCand;
+
 __global__ void argmax_local_kernel(const float* logits, int V, int v0, uint32_t* out) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float sm[32], ss[32];
+    __shared__ long long si[32];
+    __shared__ int sbest, ncand;
+    __shared__ int cand[kTpCand];
+    using rt::gcore::Greedy;
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const float* r = logits + static_cast<int64_t>(b) * V;
-    float bv = -INFINITY;
-    int bi = -1;
-    for (int i = tid; i < V; i += blockDim.x) {
-        const float v = r[i];
-        if (v > bv || (v == bv && i > bi)) {
-            bv = v;
-            bi = i;
-        }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi > bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
+    Greedy g;
+    g.init();
+    for (int i = tid; i < V; i += blockDim.x) g.add(r[i], i);
+    const float my_m = g.m;
+    g.warp_merge();
     if (lane == 0) {
-        sv[warp] = bv;
-        si[warp] = bi;
+        sm[warp] = g.m;
+        ss[warp] = g.s;
+        si[warp] = g.i;
+    }
+    if (tid == 0) {
+        sbest = -1;
+        ncand = 0;
     }
     __syncthreads();
+    Greedy c;
+    c.init();
+    for (int w = 0; w < nw; ++w) c.merge(sm[w], ss[w], si[w], 0, 0);
+    const float lim = c.m - rt::gcore::kGreedyTau;
+    // Candidates of this slice: the kTpCand highest indices within kGreedyTau
+    // of its maximum, found one at a time from the top (a few passes at most,
+    // by the few threads that hold any).
+    int below = V;  // next candidate must have a lower index
+    for (int k = 0; k < kTpCand; ++k) {
+        int best = -1, cnt = 0;
+        if (my_m >= lim)
+            for (int i = tid; i < V; i += blockDim.x)
+                if (r[i] >= lim) {
+                    if (i < below) best = i;
+                    ++cnt;
+                }
+        if (best >= 0) atomicMax(&sbest, best);
+        if (k == 0 && cnt) atomicAdd(&ncand, cnt);
+        __syncthreads();
+        const int found = sbest;
+        __syncthreads();
+        if (found < 0) break;
+        if (tid == 0) {
+            cand[k] = found;
+            sbest = -1;
+        }
+        below = found;
+        __syncthreads();
+    }
     if (tid == 0) {
-        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
-            if (sv[w] > bv || (sv[w] == bv && si[w] > bi)) {
-                bv = sv[w];
-                bi = si[w];
-            }
-        out[2 * b] = __float_as_uint(bv);
-        out[2 * b + 1] = static_cast<uint32_t>(v0 + bi);
+        uint32_t* o = out + static_cast<int64_t>(b) * kTpWords;
+        o[0] = __float_as_uint(c.m);
+        o[1] = __float_as_uint(c.s);
+        o[2] = static_cast<uint32_t>(ncand);
+        o[3] = 0u;
+        const int n = min(ncand, kTpCand);
+        for (int k = 0; k < kTpCand; ++k) {
+            o[4 + 2 * k] = __float_as_uint(k < n ? r[cand[k]] : -INFINITY);
+            o[5 + 2 * k] = k < n ? static_cast<uint32_t>(v0 + cand[k]) : 0xFFFFFFFFu;
+        }
     }
 }
 
-// The greedy token of each row from every rank's (value, index) pair (ranks'
-// slices in vocab order; ties to the higher index), then tokens[b] = it and
-// pos[b] += 1.
-__global__ void argmax_merge_kernel(const uint32_t* pairs, int nranks, int B, int32_t* tokens, int32_t* pos) {
+// The greedy token of each row from every rank's record (ranks' slices in
+// vocab order): M = max m_r, S = sum_r s_r exp(m_r - M) in rank order, then
+// the highest candidate index whose probability equals the maximum's; then
+// tokens[b] = it and pos[b] += 1.
+__global__ void argmax_merge_kernel(const uint32_t* recs, int nranks, int B, int32_t* tokens, int32_t* pos) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
-    float bv = -INFINITY;
-    int bi = -1;
+    auto rec = [&](int r) { return recs + (static_cast<int64_t>(r) * B + b) * kTpWords; };
+    float M = -INFINITY;
+    for (int r = 0; r < nranks; ++r) M = fmaxf(M, __uint_as_float(rec(r)[0]));
+    float S = 0.f;
+    for (int r = 0; r < nranks; ++r) S += __uint_as_float(rec(r)[1]) * expf(__uint_as_float(rec(r)[0]) - M);
+    const float q = __fdiv_rn(1.0f, S), lim = M - rt::gcore::kGreedyTau;
+    int best = -1;
     for (int r = 0; r < nranks; ++r) {
-        const float v = __uint_as_float(pairs[(static_cast<int64_t>(r) * B + b) * 2]);
-        const int i = static_cast<int>(pairs[(static_cast<int64_t>(r) * B + b) * 2 + 1]);
-        if (v > bv || (v == bv && i > bi)) {
-            bv = v;
-            bi = i;
+        const uint32_t* o = rec(r);
+        if (__uint_as_float(o[0]) < lim) continue;
+        for (int k = 0; k < kTpCand; ++k) {
+            const float v = __uint_as_float(o[4 + 2 * k]);
+            const int i = static_cast<int>(o[5 + 2 * k]);
+            if (i >= 0 && v >= lim && i > best && rt::gcore::greedy_ties_max(v, M, S, q)) best = i;
         }
     }
-    tokens[b] = bi;
+    tokens[b] = best;
     pos[b] += 1;
 }
 
@@ -803,7 +867,7 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
             } else {
                 argmax_local_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->vr, t->v0, t->am_send);
                 if (ok(cudaGetLastError()) &&
-                    nccl_ok(t->nccl->all_gather(t->am_send, t->am_recv, 2 * static_cast<size_t>(pl.lm_rows), ncclUint32,
+                    nccl_ok(t->nccl->all_gather(t->am_send, t->am_recv, kTpWords * static_cast<size_t>(pl.lm_rows), ncclUint32,
                                                 t->comm, s))) {
                     argmax_merge_kernel<<<(pl.lm_rows + 127) / 128, 128, 0, s>>>(t->am_recv, t->nranks, pl.lm_rows,
                                                                                  t->tokens, t->pos);
@@ -964,8 +1028,8 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, const TpInit* tp
         const char* why = nullptr;
         if (!(t->nccl = rt::nccl_api(&why))) return bail(fail(ctx, RT_E_CUDA, "tensor parallel: NCCL unavailable (%s)", why));
         if ((rc = balloc(t, reinterpret_cast<void**>(&t->ar_buf), sizeof(float) * B * t->H, "tp all-reduce buffer")) != RT_OK ||
-            (rc = balloc(t, reinterpret_cast<void**>(&t->am_send), sizeof(uint32_t) * 2 * B, "tp argmax pairs")) != RT_OK ||
-            (rc = balloc(t, reinterpret_cast<void**>(&t->am_recv), sizeof(uint32_t) * 2 * B * t->nranks, "tp argmax pairs")) != RT_OK)
+            (rc = balloc(t, reinterpret_cast<void**>(&t->am_send), sizeof(uint32_t) * kTpWords * B, "tp greedy records")) != RT_OK ||
+            (rc = balloc(t, reinterpret_cast<void**>(&t->am_recv), sizeof(uint32_t) * kTpWords * B * t->nranks, "tp greedy records")) != RT_OK)
             return bail(rc);
         RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
         const ncclResult_t nr = t->nccl->comm_init_rank(&t->comm, t->nranks, tp->id, t->rank);
@@ -1245,6 +1309,67 @@ int rt_decoder_step_batch(rt_dec* d, const int32_t* tokens, int32_t m, int32_t s
     rt_batch* t = nullptr;
     if ((rc = rows_engine(d, &t)) != RT_OK) return rc;
     return rows_run(t, tokens, m, start_pos, logits ? m : 0, logits);
+}
+
+// Test hook: the peer all-reduce kernel run by one process as rank 0 of two,
+// the second rank's buffer a local zeroed allocation whose flag never rises.
+// The first call's bounded wait must give up (error word kErrGridTimeout)
+// and every later call must return without waiting.  Nothing faults and no
+// wait is unbounded: the flag wait ends after 2 s of globaltimer.
+int rt_test_peer_allreduce_lonely(rt_ctx* ctx, int* err_word, float* first_ms, float* second_ms) {
+    if (!ctx || !err_word || !first_ms || !second_ms) return fail(ctx, RT_E_INVAL, "rt_test_peer_allreduce_lonely: null");
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const int64_t count = 4096;
+    const size_t bytes = kArFlagBytes + sizeof(float) * 2 * kMaxRanks * count;
+    void *b0 = nullptr, *b1 = nullptr, *src = nullptr, *out = nullptr, *ctr = nullptr, *err = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr, e2 = nullptr;
+    cudaError_t e = cudaSuccess;
+    auto chk = [&](cudaError_t r) {
+        if (e == cudaSuccess) e = r;
+        return e == cudaSuccess;
+    };
+    chk(cudaMalloc(&b0, bytes));
+    chk(cudaMalloc(&b1, bytes));
+    chk(cudaMalloc(&src, sizeof(float) * count));
+    chk(cudaMalloc(&out, sizeof(float) * count));
+    chk(cudaMalloc(&ctr, sizeof(int32_t)));
+    chk(cudaMalloc(&err, sizeof(int)));
+    if (e == cudaSuccess) {
+        chk(cudaMemsetAsync(b0, 0, bytes, ctx->stream));
+        chk(cudaMemsetAsync(b1, 0, bytes, ctx->stream));
+        chk(cudaMemsetAsync(src, 0, sizeof(float) * count, ctx->stream));
+        chk(cudaMemsetAsync(ctr, 0, sizeof(int32_t), ctx->stream));
+        chk(cudaMemsetAsync(err, 0, sizeof(int), ctx->stream));
+        chk(cudaEventCreate(&e0));
+        chk(cudaEventCreate(&e1));
+        chk(cudaEventCreate(&e2));
+    }
+    if (e == cudaSuccess) {
+        PeerBufs pb = {};
+        pb.base[0] = static_cast<uint8_t*>(b0);
+        pb.base[1] = static_cast<uint8_t*>(b1);
+        chk(cudaEventRecord(e0, ctx->stream));
+        peer_allreduce_kernel<<<kArCtas, 256, 0, ctx->stream>>>(static_cast<const float*>(src), 1,
+                                                                static_cast<float*>(out), count, count, pb, 2, 0, 0, 0u,
+                                                                static_cast<const int32_t*>(ctr), static_cast<int*>(err));
+        chk(cudaGetLastError());
+        chk(cudaEventRecord(e1, ctx->stream));
+        peer_allreduce_kernel<<<kArCtas, 256, 0, ctx->stream>>>(static_cast<const float*>(src), 1,
+                                                                static_cast<float*>(out), count, count, pb, 2, 0, 1, 1u,
+                                                                static_cast<const int32_t*>(ctr), static_cast<int*>(err));
+        chk(cudaGetLastError());
+        chk(cudaEventRecord(e2, ctx->stream));
+        chk(cudaMemcpyAsync(err_word, err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+        chk(cudaStreamSynchronize(ctx->stream));
+        chk(cudaEventElapsedTime(first_ms, e0, e1));
+        chk(cudaEventElapsedTime(second_ms, e1, e2));
+    }
+    for (void* q : {b0, b1, src, out, ctr, err})
+        if (q) cudaFree(q);
+    for (cudaEvent_t ev : {e0, e1, e2})
+        if (ev) cudaEventDestroy(ev);
+    RT_CHECK_CUDA(ctx, e);
+    return RT_OK;
 }
 
 }  // extern "C"

@@ -46,6 +46,28 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// Bounded wait for phase `parity` of `bar`.  iters == 0: the default bound
+// (mbar_wait).  iters > 0: at most `iters` non-blocking polls (test_wait, which
+// never suspends the thread), so a small limit really does give up when the
+// phase is not complete yet.  Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity);
+__device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t parity, uint32_t iters) {
+    if (iters == 0) return mbar_wait(bar, parity);
+    const uint32_t addr = smem_u32(bar);
+    for (uint32_t it = 0; it < iters; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 // Bounded wait for phase `parity` of `bar`.  Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     uint32_t addr = smem_u32(bar);

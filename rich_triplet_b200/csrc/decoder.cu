@@ -210,8 +210,7 @@ cudaError_t enqueue_step(rt_dec* d, cudaStream_t s, bool pdl, bool q4k_only, int
         a.g_post = norm_ptr(d, d->NL - 1, 3);
         a.g_pre = d->final_norm;
         a.y = d->logits;
-        a.am_val = d->am_val;
-        a.am_idx = d->am_idx;
+        a.am_slot = d->am_slot;
         a.am_counter = d->counters + d->NKV;
         a.token_out = d->ctl;
         a.pos_inout = d->ctl + 1;
@@ -283,13 +282,11 @@ int build_step(rt_dec* d) {
     // Scratch indexed by CTA or by warp must cover the step kernel's own grid
     // (the per-projection plans may use fewer CTAs).
     float* s_part = nullptr;
-    float* s_am_val = nullptr;
-    int32_t* s_am_idx = nullptr;
+    rt::GreedySlot* s_am_slot = nullptr;
     const int64_t part_floats = static_cast<int64_t>(grid) * d->step_geom.warps * 2 * 16;
     int rc;
     if ((rc = dalloc(d, reinterpret_cast<void**>(&s_part), sizeof(float) * part_floats, "step partials")) != RT_OK) return rc;
-    if ((rc = dalloc(d, reinterpret_cast<void**>(&s_am_val), sizeof(float) * grid, "step argmax values")) != RT_OK) return rc;
-    if ((rc = dalloc(d, reinterpret_cast<void**>(&s_am_idx), sizeof(int32_t) * grid, "step argmax rows")) != RT_OK) return rc;
+    if ((rc = dalloc(d, reinterpret_cast<void**>(&s_am_slot), sizeof(rt::GreedySlot) * grid, "step greedy slots")) != RT_OK) return rc;
     if ((rc = dalloc(d, reinterpret_cast<void**>(&d_tm), sizeof(CUtensorMap) * njobs, "step tensor maps")) != RT_OK) return rc;
     if ((rc = dalloc(d, reinterpret_cast<void**>(&d_jobs), sizeof(rt::gcore::Job) * njobs, "step jobs")) != RT_OK) return rc;
     if ((rc = dalloc(d, reinterpret_cast<void**>(&d_attn), sizeof(rt::AttnArgs) * NL, "step attention")) != RT_OK) return rc;
@@ -408,8 +405,7 @@ int build_step(rt_dec* d) {
     jl.g_pre = d->final_norm;
     jl.tile_split = 1;
     jl.y = d->logits;
-    jl.am_val = s_am_val;
-    jl.am_idx = s_am_idx;
+    jl.am_slot = s_am_slot;
     jl.am_counter = d->counters + d->NKV;
     jl.token_out = d->ctl;
     jl.pos_inout = d->ctl + 1;
@@ -429,6 +425,7 @@ int build_step(rt_dec* d) {
     P.abort = reinterpret_cast<int*>(d_sync + 2);
     P.scratch = rt::gcore::SplitScratch{s_part, d->g_cnt};
     P.err = ctx->d_err;
+
     if ((rc = dalloc(d, reinterpret_cast<void**>(&P.trace), sizeof(uint64_t) * rt::kStepTraceLen, "step trace")) != RT_OK)
         return rc;
     RT_CHECK_CUDA(ctx, cudaMemset(P.trace, 0, sizeof(uint64_t) * rt::kStepTraceLen));
@@ -471,6 +468,10 @@ int post_launch_check(rt_dec* d) {
         const int w = *d->h_err;
         *d->h_err = 0;
         cudaMemsetAsync(d->ctx->d_err, 0, sizeof(int), d->ctx->stream);
+        // Counters a failed launch can leave behind: attention merges and the
+        // greedy arrivals, and the GEMVs' split-tile unit counts.
+        cudaMemsetAsync(d->counters, 0, sizeof(uint32_t) * (d->NKV + 1), d->ctx->stream);
+        if (d->g_cnt && d->g_cnt_words) cudaMemsetAsync(d->g_cnt, 0, sizeof(uint32_t) * d->g_cnt_words, d->ctx->stream);
         if (d->use_step) {
             // an aborted step kernel leaves its barrier counters behind
             cudaMemsetAsync(d->step_params.sync, 0, 2 * sizeof(uint32_t), d->ctx->stream);
@@ -667,8 +668,7 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
         d->down = slice(static_cast<size_t>(kMaxDownParts) * H);  // the step path keeps down_parts partials
         d->logits = slice(d->V);
         d->attn_part = slice(static_cast<size_t>(d->NKV) * d->nsplit * G_ * rt::attn_part_stride(D));
-        d->am_val = slice(d->p_lm.grid);
-        if ((rc = dalloc(d, reinterpret_cast<void**>(&d->am_idx), sizeof(int32_t) * d->p_lm.grid, "argmax idx")) != RT_OK) return bail(rc);
+        if ((rc = dalloc(d, reinterpret_cast<void**>(&d->am_slot), sizeof(rt::GreedySlot) * d->p_lm.grid, "greedy slots")) != RT_OK) return bail(rc);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->counters), sizeof(uint32_t) * (d->NKV + 1), "counters")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->counters, 0, sizeof(uint32_t) * (d->NKV + 1), s);
         int64_t part_floats = 0, cnt_words = 0;
@@ -678,6 +678,7 @@ int rt_decoder_create(rt_ctx* ctx, const rt_gemma3_cfg* cfg, const rt_gemma3_lay
         }
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->g_part), sizeof(float) * part_floats, "gemv partials")) != RT_OK) return bail(rc);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->g_cnt), sizeof(uint32_t) * cnt_words, "gemv counters")) != RT_OK) return bail(rc);
+        d->g_cnt_words = cnt_words;
         cudaMemsetAsync(d->g_cnt, 0, sizeof(uint32_t) * cnt_words, s);
         if ((rc = dalloc(d, reinterpret_cast<void**>(&d->ctl), sizeof(int32_t) * (2 + d->cap), "control")) != RT_OK) return bail(rc);
         cudaMemsetAsync(d->ctl, 0, sizeof(int32_t) * (2 + d->cap), s);

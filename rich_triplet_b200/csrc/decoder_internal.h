@@ -34,11 +34,12 @@ struct rt_dec {
     // activations
     float* act = nullptr;  // one allocation, sliced below
     float *resid[2] = {nullptr, nullptr}, *qkv = nullptr, *attn = nullptr, *o_out = nullptr, *hbuf = nullptr,
-          *down = nullptr, *logits = nullptr, *attn_part = nullptr, *am_val = nullptr;
-    int32_t* am_idx = nullptr;
+          *down = nullptr, *logits = nullptr, *attn_part = nullptr;
+    rt::GreedySlot* am_slot = nullptr;
     uint32_t* counters = nullptr;  // [NKV] attention + [1] argmax
     float* g_part = nullptr;       // GEMV split-tile partials (shared by the step's GEMVs, which run in order)
     uint32_t* g_cnt = nullptr;     // GEMV split-tile counters, zero between launches
+    int64_t g_cnt_words = 0;
     int32_t* ctl = nullptr;        // [0] token, [1] position, [2..] token history [cap]
     int* h_err = nullptr;          // pinned copy of the context's error word
     // launch geometry

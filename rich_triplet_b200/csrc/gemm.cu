@@ -39,6 +39,7 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "gemv.cuh"
 
 namespace rt {
 
@@ -621,17 +622,8 @@ cudaError_t gemm_q4k_prepare() {
 
 bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, const GemmPlan& p, CUtensorMap* tm_a,
                     CUtensorMap* tm_w) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
-        cudaDriverEntryPointQueryResult q;
-        void* fn = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess || !fn) {
-            cudaGetLastError();
-            return false;
-        }
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+    const TmapEncodeFn encode = tmap_encoder();
+    if (!encode) return false;
     const cuuint32_t estr[2] = {1, 1};
     auto map16 = [&](CUtensorMap* out, CUtensorMapDataType dt, const void* base, int64_t rows, int box_rows) {
         const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};

@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -24,8 +25,7 @@ struct Smem {
     uint64_t* pbar;  // norm weights landed
     float* red;      // [32]
     int* flags;      // [4]: 0 = a wait gave up, 1 = last CTA (argmax)
-    float* bv;       // [32] per-warp argmax value
-    long long* bi;   // [32] per-warp argmax row
+    GreedySmem* gs;  // greedy epilogue reductions
     Job* job;
     float* gpost;    // [K] post-norm weight (residual-norm prologue)
     float* gpre;     // [K] pre-norm weight (norm prologues)
@@ -49,8 +49,7 @@ __host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg
     uint8_t* pbar = take(sizeof(uint64_t), 16);
     uint8_t* red = take(32 * 4, 16);
     uint8_t* flags = take(4 * 4, 16);
-    uint8_t* bv = take(4 * 32, 16);
-    uint8_t* bi = take(8 * 32, 16);
+    uint8_t* gs = take(sizeof(GreedySmem), 16);
     uint8_t* job = take(sizeof(Job), 16);
     uint8_t* gpost = take(pro == kProResidNorm ? sizeof(float) * K : 0, 16);
     uint8_t* gpre = take(pro != kProPlain ? sizeof(float) * K : 0, 16);
@@ -64,8 +63,7 @@ __host__ __device__ inline size_t carve(uint8_t* base, int kind, int K, int nseg
         S->pbar = reinterpret_cast<uint64_t*>(pbar);
         S->red = reinterpret_cast<float*>(red);
         S->flags = reinterpret_cast<int*>(flags);
-        S->bv = reinterpret_cast<float*>(bv);
-        S->bi = reinterpret_cast<long long*>(bi);
+        S->gs = reinterpret_cast<GreedySmem*>(gs);
         S->job = reinterpret_cast<Job*>(job);
         S->gpost = reinterpret_cast<float*>(gpost);
         S->gpre = reinterpret_cast<float*>(gpre);
@@ -107,12 +105,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         j.embed_scale = a.embed_scale;
         j.eps = a.eps;
         j.y = a.y;
-        j.am_val = a.am_val;
-        j.am_idx = a.am_idx;
+        j.am_slot = a.am_slot;
         j.am_counter = a.am_counter;
         j.token_out = a.token_out;
         j.pos_inout = a.pos_inout;
         j.token_hist = a.token_hist;
+        j.fail_token = a.fail_token;
+        j.wait_iters = a.wait_iters;
         mbar_init(S.pbar, 1);
         fence_mbar_init();
         S.flags[0] = 0;
@@ -120,7 +119,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     }
     __syncthreads();
     const Job& job = *S.job;
-    JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.planes, S.xsx, nullptr, nullptr, S.xs, S.sub};
+    JobSmem JS{S.pbar, S.red, S.flags, S.gs, S.gpost, S.gpre, S.planes, S.xsx, nullptr, nullptr, S.xs, S.sub};
 
     // Each warp's weight stream starts before the wait on the previous kernel
     // (weights are constants), and so do the norm weights.
@@ -133,9 +132,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     pdl_wait();
 
     job_prologue<KIND, PRO>(job, JS, 0u);
-    float best_v = -INFINITY;
-    long long best_i = -1;
-    const bool ok = job_units_run<KIND, EPI, kSplitGrid>(job, st, JS, SplitScratch{a.part, a.tile_cnt}, best_v, best_i);
+    Greedy gr;
+    gr.init();
+    const bool ok = job_units_run<KIND, EPI, kSplitGrid>(job, st, JS, SplitScratch{a.part, a.tile_cnt}, gr);
     if (!ok) {
         // A bounded wait gave up: record it, then wait (bounded) for the copies
         // this warp still has in flight before its shared memory goes away.
@@ -146,11 +145,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         __syncwarp();
     }
     __syncthreads();
-    if (S.flags[0]) {
-        if (tid == 0 && a.err) atomicExch(a.err, kErrMbarTimeout);
-        return;
-    }
-    if constexpr (EPI == kEpiArgmax) argmax_finish(job, JS, best_v, best_i);
+    const bool failed = S.flags[0] != 0;
+    if (failed && tid == 0 && a.err) atomicExch(a.err, kErrMbarTimeout);
+    // The greedy epilogue runs also after a failure: every CTA must still
+    // arrive so that the last one can reset the launch's counters.
+    if constexpr (EPI == kEpiArgmax) argmax_finish(job, JS, gr, failed, a.tile_cnt);
 }
 
 // Calls f(kernel) for the instantiation matching (kind, prologue, epilogue).
@@ -242,18 +241,26 @@ GemvPlan gemv_plan(int kind, int64_t rows, int K, int pair, int prologue, int ep
     return p;
 }
 
-bool gemv_make_tmap(int kind, const void* w, int64_t rows, int K, const GemvPlan& p, CUtensorMap* out) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
+TmapEncodeFn tmap_encoder() {
+    static std::once_flag once;
+    static TmapEncodeFn encode = nullptr;
+    std::call_once(once, [] {
         cudaDriverEntryPointQueryResult q;
         void* fn = nullptr;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
             q != cudaDriverEntryPointSuccess || !fn) {
             cudaGetLastError();
-            return false;
+            return;
         }
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+        PFN_cuTensorMapEncodeTiled_v12000 f = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        encode = f;
+    });
+    return encode;
+}
+
+bool gemv_make_tmap(int kind, const void* w, int64_t rows, int K, const GemvPlan& p, CUtensorMap* out) {
+    const TmapEncodeFn encode = tmap_encoder();
+    if (!encode) return false;
     const uint64_t row_bytes = kind == kQ4K ? static_cast<uint64_t>(K / 256) * 144 : static_cast<uint64_t>(K) * 2;
     const cuuint64_t dims[2] = {row_bytes / 8, static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {row_bytes};

@@ -28,7 +28,27 @@ enum Prologue : int {
 enum Epilogue : int {
     kEpiPlain = 0,     // y[r] = sum
     kEpiGeluPair = 1,  // rows interleaved (gate, up): y[r/2] = gelu_tanh(gate) * up
-    kEpiArgmax = 2,    // y[r] = sum, plus the greedy token (max, ties to higher index)
+    kEpiArgmax = 2,    // y[r] = sum, plus the greedy token (GreedySlot)
+};
+
+// Per-CTA state of the greedy epilogue, combined by the last CTA to finish.
+// sample_token at temperature 0 (src/transformer4.rs:3036-3091) takes the
+// LAST index of the largest softmax probability p_i = exp(y_i - M) / S:
+//   m   the CTA's largest y (M is the maximum over the CTAs' m);
+//   s   sum over the CTA's rows of exp(y - m) (so S = sum_c s_c exp(m_c - M));
+//   idx the CTA's row of m (ties to the higher row);
+//   lo, hi  the lowest and highest row the CTA emitted: the rows the last CTA
+//       re-reads for near-ties when m is within kGreedyTau of M;
+//   failed  a bounded wait of the CTA gave up: the launch has no token, and
+//       the last CTA returns the launch's counters to zero.
+struct GreedySlot {
+    float m;
+    float s;
+    int32_t idx;
+    int32_t lo;
+    int32_t hi;
+    int32_t failed;
+    int32_t pad[2];
 };
 
 struct GemvArgs {
@@ -55,13 +75,14 @@ struct GemvArgs {
     float eps;
     // outputs
     float* y;
-    float* am_val;         // [gridDim.x] per-CTA best logit
-    int32_t* am_idx;       // [gridDim.x] per-CTA best index
+    GreedySlot* am_slot;   // [gridDim.x] per-CTA greedy state
     uint32_t* am_counter;  // zero before the launch; the last CTA resets it
     int32_t* token_out;    // greedy token written by the last CTA
     int32_t* pos_inout;    // incremented by the last CTA (device-side decode loop)
     int32_t* token_hist;   // token_hist[pos] = greedy token of the step at pos (may be null)
     int* err;              // error word (kErr*), may be null
+    int32_t fail_token;    // 1: a launch whose bounded wait gave up writes token_out = -1
+    uint32_t wait_iters;   // poll limit of the weight-stream waits (0: the default bound)
 };
 
 struct GemvPlan {
@@ -74,6 +95,13 @@ struct GemvPlan {
     int64_t part_floats = 0;  // split-tile scratch this plan needs (GemvArgs::part)
     int64_t cnt_words = 0;    // and GemvArgs::tile_cnt, zeroed once by the owner
 };
+
+// cuTensorMapEncodeTiled, fetched from the driver once per process (thread-safe);
+// null if the driver does not provide it.
+using TmapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+TmapEncodeFn tmap_encoder();
 
 // Raise the dynamic shared-memory limit of every kernel instantiation on the
 // current device.  Call once per device before planning or capturing.

@@ -51,6 +51,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 
+
 namespace rt {
 namespace gcore {
 
@@ -253,6 +254,98 @@ constexpr int kTileMajorUnitsPerCopy = 2;
 // Partial vectors a residual-update prologue can add (Job::src_parts).
 constexpr int kMaxSrcParts = 4;
 
+// Greedy sampling (sample_token at temperature 0, src/transformer4.rs:3036-3091):
+// the token is the LAST index of the largest softmax probability
+// p_i = expf(y_i - M) / S, M = max y, S = sum_i expf(y_i - M).  exp(y_i - M) is
+// at most 1, reached by the maximum itself, so only rows whose exp rounds to
+// within one quotient ulp of 1 can share its probability: exp(y_i - M) >=
+// 1 - 2^-23, i.e. y_i >= M - 2^-23 (a little more for the rounding of exp).
+// Rows within kGreedyTau = 2^-21 of M are therefore the only candidates; for
+// them p_i is formed as the reference does (f32 difference, exp rounded to
+// f32, one f32 division by S) and the highest candidate row whose p_i equals
+// 1/S wins.  Distinct logits tie exactly when exp(y_i - M) rounds to 1 (|y_i -
+// M| < 2^-25: logits of magnitude below ~0.25 one ulp apart).  The one value
+// in between, exp = 1 - 2^-24, ties or not depending on the last bits of S,
+// whose summation order differs from the reference's sequential sum.
+constexpr float kGreedyTau = 4.76837158203125e-07f;  // 2^-21
+
+// Running greedy state of one lane, warp or CTA: the largest value m, the sum
+// s of exp(y - m) over the rows seen (online rescaling), the row of m (ties to
+// the higher row) and the range of rows seen.
+struct Greedy {
+    float m;
+    float s;
+    long long i;
+    int lo, hi;
+    __device__ __forceinline__ void init() {
+        m = -INFINITY;
+        s = 0.f;
+        i = -1;
+        lo = 0x7fffffff;
+        hi = -1;
+    }
+    __device__ __forceinline__ void add(float v, long long r) {
+        if (v > m) {
+            s = s * expf(m - v) + 1.0f;  // exp(-inf) = 0 for the first row
+            m = v;
+            i = r;
+        } else {
+            s += expf(v - m);
+            if (v == m && r > i) i = r;
+        }
+        lo = min(lo, static_cast<int>(r));
+        hi = max(hi, static_cast<int>(r));
+    }
+    __device__ __forceinline__ void merge(float om, float os, long long oi, int olo, int ohi) {
+        if (oi < 0) return;
+        if (i < 0) {
+            m = om;
+            s = os;
+            i = oi;
+            lo = olo;
+            hi = ohi;
+            return;
+        }
+        const float M = fmaxf(m, om);
+        s = s * expf(m - M) + os * expf(om - M);
+        if (om > m || (om == m && oi > i)) i = oi;
+        m = M;
+        lo = min(lo, olo);
+        hi = max(hi, ohi);
+    }
+    // Butterfly over the warp: every lane ends with the warp's state.
+    __device__ __forceinline__ void warp_merge() {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, m, o);
+            const float os = __shfl_xor_sync(0xffffffffu, s, o);
+            const long long oi = __shfl_xor_sync(0xffffffffu, i, o);
+            const int olo = __shfl_xor_sync(0xffffffffu, lo, o);
+            const int ohi = __shfl_xor_sync(0xffffffffu, hi, o);
+            merge(om, os, oi, olo, ohi);
+        }
+    }
+};
+
+// Shared memory of the greedy epilogue's reductions.
+struct GreedySmem {
+    float m[32];
+    float s[32];
+    long long i[32];
+    int lo[32];
+    int hi[32];
+    int cand[16];  // CTAs whose maximum is within kGreedyTau of the grid's
+    int ncand;
+    int best;
+};
+
+// p_i == p_max for a candidate row of value v (M the maximum, q = 1/S).
+__device__ __forceinline__ bool greedy_ties_max(float v, float M, float S, float q) {
+    const float x = __fsub_rn(v, M);
+    const float e = static_cast<float>(exp(static_cast<double>(x)));  // exp correctly rounded to f32
+    return __fdiv_rn(e, S) == q;
+}
+
 // One GEMV as the kernels see it.
 struct Job {
     const void* tmap;   // CUtensorMap of W (parameter or global memory), row-major W
@@ -289,12 +382,13 @@ struct Job {
     float eps;
     // epilogue
     float* y;
-    float* am_val;
-    int32_t* am_idx;
+    GreedySlot* am_slot;
     uint32_t* am_counter;
     int32_t* token_out;
     int32_t* pos_inout;
     int32_t* token_hist;
+    int32_t fail_token;   // 1: a failed launch writes token_out = -1 (GemvArgs::fail_token)
+    uint32_t wait_iters;  // poll limit of the weight-stream waits (0: default)
 };
 
 __device__ __forceinline__ uint32_t job_units(const Job& j) {
@@ -357,7 +451,6 @@ struct Stream {
     int islot;           // slot the next copy goes to
     int issued;          // copies issued, all jobs
     int consumed;        // copies consumed, all jobs
-
     // Move the cursor to the next job in which this warp has units.
     __device__ __forceinline__ void seek(int j) {
         for (ij = j; ij < njobs; ++ij) {
@@ -444,8 +537,7 @@ struct JobSmem {
     uint64_t* pbar;  // norm weights landed
     float* red;      // [32]
     int* flag;       // [4] block-wide flags: 0 = failure, 1 = last-CTA
-    float* bv;       // [32] per-warp argmax value
-    long long* bi;   // [32] per-warp argmax row
+    GreedySmem* gs;  // greedy epilogue reductions
     float* gpost;    // [K]
     float* gpre;     // [K]
     uint8_t* planes;
@@ -622,10 +714,10 @@ enum SplitMode : int {
 
 // Stream this warp's units of job `a` (whose planes are ready) through the
 // epilogue.  Returns false if a wait gave up (the warp's stream is then
-// abandoned; the caller drains it).  best_v / best_i: running greedy argmax.
+// abandoned; the caller drains it).  gr: this lane's running greedy state.
 template <int KIND, int EPI, int SPLIT>
 __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const JobSmem& S, const SplitScratch& sc,
-                                              float& best_v, long long& best_i) {
+                                              Greedy& gr) {
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int nseg = a.nseg;
@@ -645,12 +737,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
         } else {
             if (lane < kTile && r < a.rows) {
                 a.y[r] = v;
-                if constexpr (EPI == kEpiArgmax) {
-                    if (v > best_v || (v == best_v && r > best_i)) {
-                        best_v = v;
-                        best_i = r;
-                    }
-                }
+                if constexpr (EPI == kEpiArgmax) gr.add(v, r);
             }
         }
     };
@@ -675,7 +762,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     int in_copy = 0, uic = 0;  // units left in / consumed from the current copy
     for (int i = 0; i < n; ++i) {
         if (in_copy == 0) {
-            const bool ok = mbar_wait(&st.full[st.jb], st.ph);
+            const bool ok = mbar_wait_n(&st.full[st.jb], st.ph, a.wait_iters);
             if (__any_sync(0xffffffffu, !ok)) return false;
             in_copy = min(upc, n - i);
             uic = 0;
@@ -844,7 +931,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
 // threads call it; it starts with __syncthreads.  The warps' unit ranges come
 // from the table job_units_run filled (no division per piece).
 template <int EPI>
-__device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, float& best_v, long long& best_i) {
+__device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, Greedy& gr) {
     __syncthreads();
     const uint32_t nw = blockDim.x >> 5, warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -882,64 +969,113 @@ __device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, floa
             a.y[r >> 1] = __fmul_rn(gelu_tanh_dev(v0), v1);
         } else {
             a.y[r] = v0;
-            if constexpr (EPI == kEpiArgmax) {
-                if (v0 > best_v || (v0 == best_v && r > best_i)) {
-                    best_v = v0;
-                    best_i = r;
-                }
-            }
+            if constexpr (EPI == kEpiArgmax) gr.add(v0, r);
         }
     }
 }
 
-// Greedy argmax over the grid (largest value; ties to the higher row index),
-// after every warp of every CTA ran job_units_run: per CTA a slot, the last
-// CTA to arrive combines them, writes the token (and advances the device-side
-// decode position) and resets the counter.  All threads of the CTA call it.
-__device__ __forceinline__ void argmax_finish(const Job& a, const JobSmem& S, float best_v, long long best_i) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-        const long long oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-        if (ov > best_v || (ov == best_v && oi > best_i)) {
-            best_v = ov;
-            best_i = oi;
-        }
-    }
+// Greedy token over the grid (sample_token's rule, see kGreedyTau), after
+// every warp of every CTA ran job_units_run: per CTA a GreedySlot; the last CTA
+// to arrive combines them (M, S in a fixed order), re-reads the rows of the
+// CTAs whose maximum is within kGreedyTau of M, writes the token (and advances
+// the device-side decode position) and resets the counter.  All threads of
+// the CTA call it, also when one of its bounded waits gave up (`failed`): the
+// last CTA then writes no token (-1 with Job::fail_token), leaves the decode
+// position alone and returns the split-tile counters to zero, so the next
+// launch starts clean.
+__device__ __forceinline__ void argmax_finish(const Job& a, const JobSmem& S, Greedy gr, bool failed,
+                                              uint32_t* tile_cnt) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5, nthr = blockDim.x;
+    GreedySmem& G = *S.gs;
+    gr.warp_merge();
     if (lane == 0) {
-        S.bv[warp] = best_v;
-        S.bi[warp] = best_i;
+        G.m[warp] = gr.m;
+        G.s[warp] = gr.s;
+        G.i[warp] = gr.i;
+        G.lo[warp] = gr.lo;
+        G.hi[warp] = gr.hi;
     }
     __syncthreads();
     if (tid == 0) {
-        float bv = S.bv[0];
-        long long bi = S.bi[0];
-        for (int w = 1; w < nw; ++w)
-            if (S.bv[w] > bv || (S.bv[w] == bv && S.bi[w] > bi)) {
-                bv = S.bv[w];
-                bi = S.bi[w];
-            }
-        a.am_val[blockIdx.x] = bv;
-        a.am_idx[blockIdx.x] = static_cast<int32_t>(bi);
+        Greedy c;
+        c.init();
+        for (int w = 0; w < nw; ++w) c.merge(G.m[w], G.s[w], G.i[w], G.lo[w], G.hi[w]);
+        GreedySlot sl;
+        sl.m = c.m;
+        sl.s = c.s;
+        sl.idx = static_cast<int32_t>(c.i);
+        sl.lo = c.lo;
+        sl.hi = c.hi;
+        sl.failed = failed ? 1 : 0;
+        sl.pad[0] = sl.pad[1] = 0;
+        a.am_slot[blockIdx.x] = sl;
         __threadfence();
         const uint32_t prev = atomicAdd(a.am_counter, 1u);
         S.flag[1] = prev == gridDim.x - 1;
+        G.ncand = 0;
+        G.best = -1;
     }
     __syncthreads();
-    if (S.flag[1] && tid == 0) {
-        __threadfence();
-        const volatile float* vv = a.am_val;
-        const volatile int32_t* vi = a.am_idx;
-        float bv = vv[0];
-        int32_t bi = vi[0];
-        for (unsigned k = 1; k < gridDim.x; ++k) {
-            const float v = vv[k];
-            const int32_t i = vi[k];
-            if (v > bv || (v == bv && i > bi)) {
-                bv = v;
-                bi = i;
+    if (!S.flag[1]) return;
+    __threadfence();
+    // M, then S = sum_c s_c exp(m_c - M) in a fixed order; the CTAs that may
+    // hold candidates.
+    const int ncta = static_cast<int>(gridDim.x);
+    const volatile GreedySlot* slots = a.am_slot;
+    int any_failed = 0;
+    for (int k = tid; k < ncta; k += nthr) any_failed |= slots[k].failed;
+    if (__syncthreads_or(any_failed)) {
+        // Units that never arrived left split tiles half-counted.
+        if (tile_cnt) {
+            const int64_t ntiles = (a.rows + kTile - 1) / kTile;
+            for (int64_t t = tid; t < ntiles; t += nthr) tile_cnt[t] = 0u;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            if (a.token_out && a.fail_token) *a.token_out = -1;
+            __threadfence();
+            *a.am_counter = 0u;
+        }
+        return;
+    }
+    float lm = -INFINITY;
+    for (int k = tid; k < ncta; k += nthr)
+        if (slots[k].idx >= 0) lm = fmaxf(lm, slots[k].m);
+    const float M = block_max(lm, S.red);
+    float ls = 0.f;
+    for (int k = tid; k < ncta; k += nthr) {
+        if (slots[k].idx < 0) continue;
+        const float mk = slots[k].m;
+        ls += slots[k].s * expf(mk - M);
+        if (mk >= M - kGreedyTau) {
+            const int n = atomicAdd(&G.ncand, 1);
+            if (n < 16) G.cand[n] = k;
+        }
+    }
+    const float Ssum = block_sum(ls, S.red);  // ends with every thread past a __syncthreads
+    const float q = __fdiv_rn(1.0f, Ssum);
+    const float lim = M - kGreedyTau;
+    int best = -1;
+    const volatile float* y = a.y;
+    if (G.ncand <= 16) {
+        for (int c = 0; c < G.ncand; ++c) {
+            const int k = G.cand[c];
+            const int lo = slots[k].lo, hi = slots[k].hi;
+            for (int r = lo + tid; r <= hi; r += nthr) {
+                const float v = y[r];
+                if (v >= lim && r > best && greedy_ties_max(v, M, Ssum, q)) best = r;
             }
         }
+    } else {  // many CTAs near the maximum: every row
+        for (int r = tid; r < a.rows; r += nthr) {
+            const float v = y[r];
+            if (v >= lim && r > best && greedy_ties_max(v, M, Ssum, q)) best = r;
+        }
+    }
+    if (best >= 0) atomicMax(&G.best, best);
+    __syncthreads();
+    if (tid == 0) {
+        const int32_t bi = G.best;
         if (a.token_out) *a.token_out = bi;
         if (a.pos_inout) {
             const int32_t p = *a.pos_inout;

@@ -2,12 +2,16 @@
 // (y = W x over a BF16 matrix, then the argmax of y) whose only scratch is a
 // file-scope device array, so the call path allocates no device memory.
 //
-// The kernel is the library's GEMV with the greedy-argmax epilogue: every CTA
-// leaves its best (value, row) in a slot, bumps an arrival counter, and the
-// last CTA to arrive combines the slots, writes the token and puts the counter
-// back to zero.  Here the slots and the counter live in g_argmax_scratch
-// instead of a context- or engine-owned allocation.
+// The kernel is the library's GEMV with the greedy epilogue: every CTA leaves
+// its greedy state (largest value, its row, the sum of exp(y - max)) in a
+// slot, bumps an arrival counter, and the last CTA to arrive combines the
+// slots, writes the token and puts the counter back to zero.  Here the slots
+// and the counter live in g_argmax_scratch instead of a context- or
+// engine-owned allocation.  A launch in which a bounded wait gave up still
+// runs the arrival protocol: its last CTA writes token -1 and returns every
+// counter it used to zero, so the next call starts clean.
 #include <cstddef>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -22,8 +26,7 @@ constexpr int64_t kMaxTiles = RT_ARGMAX_STATIC_MAX_ROWS / 16;  // 16-row tiles
 constexpr int kMaxDevices = 64;
 
 struct ArgmaxScratch {
-    float val[kSlots];                       // per-CTA best logit
-    int32_t idx[kSlots];                     // per-CTA best row
+    rt::GreedySlot slot[kSlots];             // per-CTA greedy state
     uint32_t counter;                        // CTAs arrived; zero when a launch starts
     uint32_t tile_cnt[kMaxTiles];            // split-tile unit counters; zero when a launch starts
     float part[kSlots * kWarpsPerCta * 32];  // split-tile partial row sums
@@ -121,12 +124,15 @@ extern "C" int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int c
     a.x = x_dev;
     a.y = y_dev;
     uint8_t* base = reinterpret_cast<uint8_t*>(s.scratch);  // device address: offsets only, never dereferenced here
-    a.am_val = reinterpret_cast<float*>(base + offsetof(ArgmaxScratch, val));
-    a.am_idx = reinterpret_cast<int32_t*>(base + offsetof(ArgmaxScratch, idx));
+    a.am_slot = reinterpret_cast<rt::GreedySlot*>(base + offsetof(ArgmaxScratch, slot));
     a.am_counter = reinterpret_cast<uint32_t*>(base + offsetof(ArgmaxScratch, counter));
     a.tile_cnt = reinterpret_cast<uint32_t*>(base + offsetof(ArgmaxScratch, tile_cnt));
     a.part = reinterpret_cast<float*>(base + offsetof(ArgmaxScratch, part));
     a.token_out = token_dev;
+    a.fail_token = 1;  // a launch whose bounded wait gave up reports itself as token -1
+    // Test override: RT_TEST_MBAR_WAIT_ITERS=n bounds each weight-stream wait
+    // to n polls, so that a test can make the bounded wait give up.
+    if (const char* w = getenv("RT_TEST_MBAR_WAIT_ITERS")) a.wait_iters = static_cast<uint32_t>(strtoul(w, nullptr, 10));
     e = rt::gemv_launch(rt::kBF16, rt::kProPlain, rt::kEpiArgmax, a, tmap, p, static_cast<cudaStream_t>(stream), false);
     if (e != cudaSuccess)
         return report(errbuf, errlen, RT_E_CUDA, "rt_gemv_bf16_argmax_static: launch: %s", cudaGetErrorString(e));

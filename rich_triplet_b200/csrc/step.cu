@@ -58,8 +58,7 @@ struct StepSmem {
     uint64_t* abar;  // attention tile barrier (kept out of `uni`: see attn_bar_init)
     float* red;
     int* flags;      // 0: this CTA failed, 1: last CTA (argmax), 2: barrier result, 3: attention copy pending
-    float* bv;
-    long long* bi;
+    GreedySmem* gs;
     float* gpost;    // [hidden]
     float* gpre;     // [hidden]
     float* xs;       // [hidden] residual stream (norm prologues)
@@ -84,8 +83,7 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
     uint8_t* abar = take(sizeof(uint64_t), 16);
     uint8_t* red = take(32 * 4, 16);
     uint8_t* flags = take(4 * 4, 16);
-    uint8_t* bv = take(4 * 32, 16);
-    uint8_t* bi = take(8 * 32, 16);
+    uint8_t* gs = take(sizeof(GreedySmem), 16);
     uint8_t* gpost = take(sizeof(float) * g.hidden, 16);
     uint8_t* gpre = take(sizeof(float) * g.hidden, 16);
     uint8_t* xs = take(sizeof(float) * g.hidden, 16);
@@ -105,8 +103,7 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
         S->abar = reinterpret_cast<uint64_t*>(abar);
         S->red = reinterpret_cast<float*>(red);
         S->flags = reinterpret_cast<int*>(flags);
-        S->bv = reinterpret_cast<float*>(bv);
-        S->bi = reinterpret_cast<long long*>(bi);
+        S->gs = reinterpret_cast<GreedySmem*>(gs);
         S->gpost = reinterpret_cast<float*>(gpost);
         S->gpre = reinterpret_cast<float*>(gpre);
         S->xs = reinterpret_cast<float*>(xs);
@@ -160,8 +157,8 @@ __device__ __forceinline__ bool grid_sync(const StepParams& P, uint32_t& nsync, 
 // and mark the CTA failed.
 template <int KIND, int EPI>
 __device__ __forceinline__ void run_units(const Job& j, Stream& st, const JobSmem& JS, const StepParams& P,
-                                          int* flags, float& best_v, long long& best_i) {
-    if (!job_units_run<KIND, EPI, kSplitTile>(j, st, JS, P.scratch, best_v, best_i)) {
+                                          int* flags, Greedy& gr) {
+    if (!job_units_run<KIND, EPI, kSplitTile>(j, st, JS, P.scratch, gr)) {
         if ((threadIdx.x & 31) == 0) {
             atomicExch(&flags[0], 1);
             if (P.err) atomicExch(P.err, kErrMbarTimeout);
@@ -188,7 +185,7 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         S.flags[0] = S.flags[1] = S.flags[2] = S.flags[3] = 0;
     }
     __syncthreads();
-    const JobSmem JS{S.pbar, S.red, S.flags, S.bv, S.bi, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse, S.xs, reinterpret_cast<float*>(S.uni)};
+    const JobSmem JS{S.pbar, S.red, S.flags, S.gs, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse, S.xs, reinterpret_cast<float*>(S.uni)};
     const int njobs = 4 * P.nlayers + 1;
     Stream st;
     stream_start(st, S.full + warp * nb, S.ring + static_cast<size_t>(warp) * nb * kSlotBytes, nb, kSlotBytes, P.jobs,
@@ -197,8 +194,8 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
     uint32_t pph = 0;  // gamma barrier phase
     uint32_t nsync = 0;
     uint32_t aph = 0;  // attention barrier phases completed
-    float best_v = -INFINITY;
-    long long best_i = -1;
+    Greedy gr;
+    gr.init();
 
     // Phase timeline of CTA 0 (tracing; a few stores per phase).
     const bool tr = P.trace && blockIdx.x == 0 && tid == 0;
@@ -226,11 +223,11 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
             if (tid == 0) prefetch_gammas(P.jobs[p + 2], kProResidNorm, JS);
         }
         if (k == 2) {
-            run_units<kQ4K, kEpiGeluPair>(j, st, JS, P, S.flags, best_v, best_i);
-            cta_combine<kEpiGeluPair>(j, JS, best_v, best_i);
+            run_units<kQ4K, kEpiGeluPair>(j, st, JS, P, S.flags, gr);
+            cta_combine<kEpiGeluPair>(j, JS, gr);
         } else {
-            run_units<kQ4K, kEpiPlain>(j, st, JS, P, S.flags, best_v, best_i);
-            cta_combine<kEpiPlain>(j, JS, best_v, best_i);
+            run_units<kQ4K, kEpiPlain>(j, st, JS, P, S.flags, gr);
+            cta_combine<kEpiPlain>(j, JS, gr);
         }
         const int slot = 1 + 10 * l + (k == 0 ? 0 : 2 + 2 * k);
         stamp(slot);
@@ -270,15 +267,15 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         // ---- LM head: residual update + final norm, BF16 GEMV, greedy argmax ----
         const Job& jl = P.jobs[4 * P.nlayers];
         job_prologue<kBF16, kProResidNorm>(jl, JS, pph);
-        run_units<kBF16, kEpiArgmax>(jl, st, JS, P, S.flags, best_v, best_i);
-        cta_combine<kEpiArgmax>(jl, JS, best_v, best_i);
+        run_units<kBF16, kEpiArgmax>(jl, st, JS, P, S.flags, gr);
+        cta_combine<kEpiArgmax>(jl, JS, gr);
         stamp(kStepTraceLen - 2);
         __syncthreads();
         if (S.flags[0]) {
             ok = false;
             if (tid == 0) atomicExch(P.abort, 1);
         } else {
-            argmax_finish(jl, JS, best_v, best_i);
+            argmax_finish(jl, JS, gr, false, nullptr);
             stamp(kStepTraceLen - 1);
         }
     }
@@ -367,3 +364,4 @@ cudaError_t step_launch(const StepParams& p, const StepGeom& g, int grid, cudaSt
 }
 
 }  // namespace rt
+

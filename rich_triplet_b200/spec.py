@@ -46,10 +46,26 @@ class NgramDraftEngine:
         return []
 
 
+GREEDY_TAU = np.float32(2.0 ** -21)
+
+
 def greedy_token(logits):
-    """Largest logit, ties to the higher index (the engine's argmax)."""
-    row = np.asarray(logits)
-    return int(np.flatnonzero(row == row.max())[-1])
+    """sample_token at temperature 0 (src/transformer4.rs:3036-3091): the LAST
+    index of the largest softmax probability p_i = exp(y_i - M) / S, computed
+    the way the device kernels compute it.  Only rows within 2^-21 of the
+    maximum M can share its probability; for them p_i is formed as the
+    reference does (f32 difference, exp rounded to f32, one f32 division by
+    S), and the highest such row whose p_i equals 1/S wins.  Logits of
+    magnitude below ~0.25 one f32 ulp apart therefore tie (exp rounds to 1)
+    and the later index wins, where a plain argmax would take the larger."""
+    row = np.asarray(logits, dtype=np.float32)
+    m = row.max()
+    s = np.float32(np.exp((row - m).astype(np.float64)).astype(np.float32).sum(dtype=np.float32))
+    q = np.float32(1.0) / s
+    cand = np.flatnonzero(row >= m - GREEDY_TAU)
+    e = np.exp((row[cand] - m).astype(np.float64)).astype(np.float32)
+    ties = cand[(e / s).astype(np.float32) == q]
+    return int(ties[-1])
 
 
 def speculative_generate(dec, prompt, first_token, start_pos, max_new, draft_len=4, max_n=4):

@@ -66,3 +66,24 @@ def test_speculative_loop_emits_the_greedy_sequence():
 
 def test_greedy_token_ties_to_higher_index():
     assert greedy_token(np.array([1.0, 3.0, 3.0, 0.0])) == 2
+
+
+def test_greedy_token_follows_sample_token_on_near_ties(orc):
+    """Two logits one f32 ulp apart: below ~0.25 in magnitude exp() of their
+    difference rounds to 1, so sample_token (softmax, last index of the
+    largest probability) takes the LATER index; at magnitude 4 the
+    probabilities differ and the larger logit wins.  greedy_token must agree
+    with the oracle's restatement in both cases, and on random rows."""
+    y = np.full(1000, -10.0, np.float32)
+    y[10] = np.float32(0.125) + np.float32(2.0 ** -26)  # one ulp above 0.125
+    y[20] = np.float32(0.125)
+    assert orc.sample_greedy(y) == 20 and greedy_token(y) == 20 and int(np.argmax(y)) == 10
+    y = np.full(1000, -10.0, np.float32)
+    y[10] = np.float32(4.0) + np.float32(2.0 ** -21)  # one ulp above 4
+    y[20] = np.float32(4.0)
+    assert orc.sample_greedy(y) == 10 and greedy_token(y) == 10
+    rng = np.random.default_rng(3)
+    for scale in (0.01, 1.0, 30.0):
+        for _ in range(20):
+            v = (rng.standard_normal(4096) * scale).astype(np.float32)
+            assert greedy_token(v) == orc.sample_greedy(v)
