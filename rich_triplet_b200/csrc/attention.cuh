@@ -28,6 +28,11 @@ struct AttnArgs {
     uint32_t* counter;      // [nkv], zero before the launch; the combining CTA resets it
     float* out;             // [nq*D]
     int* err;
+    // Tagged-word form (decode-step kernel): q/k/v read from qkv_ll, the merged
+    // output written to out_ll, when the caller passes nonzero tags.
+    const uint64_t* qkv_ll = nullptr;
+    uint64_t* out_ll = nullptr;
+    uint64_t* part_ll = nullptr;  // the per-split partials as tagged words (layout of `part`)
     // Several sequences in one launch (grid z = sequence b): b's qkv, caches,
     // partials and output sit these many floats after sequence 0's, its
     // position at pos[b] and its counters at counter[b * nkv].  Unused with one.

@@ -86,17 +86,44 @@ __host__ __device__ inline size_t attn_carve(uint8_t* base, int D, int G, int T,
 // One warp: dst[D] = rope(rmsnorm(raw) * (1 + gamma)) -- the per-head norm
 // (rms_norm_gemma3 per head, src/transformer4.rs:2485-2510) and the NeoX
 // rotation of pairs (j, j + D/2) (src/transformer4.rs:2742-2772).
-__device__ __forceinline__ void head_prep_warp(const float* raw, const float* gamma, const float* cs, const float* sn,
-                                               int D, float eps, float* dst) {
+// With `tag` != 0 the row is read from tagged words at raw_ll (polled until
+// every word carries the tag); false if that wait gave up.
+__device__ __forceinline__ bool head_load_warp(const float* raw, const uint64_t* raw_ll, uint32_t tag, int D,
+                                               const int* abort, float (&x)[kMaxHeadDim / 32]) {
+    constexpr int kMaxPer = kMaxHeadDim / 32;
+    const int lane = threadIdx.x & 31;
+    if (!tag) {
+#pragma unroll
+        for (int i = 0; i < kMaxPer; ++i) {  // every load of the row in flight at once
+            const int j = lane + 32 * i;
+            x[i] = j < D ? raw[j] : 0.f;
+        }
+        return true;
+    }
+    LLPoll pl;
+    pl.init(abort);
+    for (;;) {
+        bool ready = true;
+#pragma unroll
+        for (int i = 0; i < kMaxPer; ++i) {
+            const int j = lane + 32 * i;
+            const uint64_t w = j < D ? ll_load(raw_ll + j) : ll_word(0.f, tag);
+            x[i] = ll_val(w);
+            ready &= ll_has(w, tag);
+        }
+        if (__all_sync(0xffffffffu, ready)) return true;
+        if (!pl.again()) return false;
+    }
+}
+
+__device__ __forceinline__ bool head_prep_warp(const float* raw, const uint64_t* raw_ll, uint32_t tag,
+                                               const float* gamma, const float* cs, const float* sn, int D, float eps,
+                                               float* dst, const int* abort) {
     constexpr int kMaxPer = kMaxHeadDim / 32;
     const int lane = threadIdx.x & 31, half = D / 2;
     float x[kMaxPer];
     float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i) {  // every load of the row in flight at once
-        const int j = lane + 32 * i;
-        x[i] = j < D ? raw[j] : 0.f;
-    }
+    if (!head_load_warp(raw, raw_ll, tag, D, abort, x)) return false;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
         const int j = lane + 32 * i;
@@ -113,6 +140,7 @@ __device__ __forceinline__ void head_prep_warp(const float* raw, const float* ga
         dst[j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
         dst[j + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
     }
+    return true;
 }
 
 template <int G, int T>
@@ -180,9 +208,9 @@ struct AttnRange {
     size_t head_base;
 };
 
-__device__ __forceinline__ AttnRange attn_range(const AttnArgs& a, int h, int s, int T) {
+__device__ __forceinline__ AttnRange attn_range(const AttnArgs& a, int h, int s, int T, int pos = -1) {
     AttnRange R;
-    R.pos = *a.pos;
+    R.pos = pos >= 0 ? pos : *a.pos;
     const int L = R.pos + 1;
     const int kstart = a.window > 0 ? max(0, L - a.window) : 0;
     const int n = L - kstart;
@@ -220,7 +248,7 @@ __device__ __forceinline__ float lse_scale(float mx, float m) { return mx == -IN
 // in adjacent lanes and are combined by a butterfly, so every load of the
 // merge is issued in one round for nsplit <= kg * kBatch.
 template <int G>
-__device__ __forceinline__ void attn_merge(const AttnArgs& a, int h, int nsplit) {
+__device__ __forceinline__ void attn_merge(const AttnArgs& a, int h, int nsplit, uint32_t out_tag) {
     constexpr int kBatch = 12;
     const int D = a.D, stride = attn_part_stride(D);
     const int Q = G * D / 4;  // float4 columns
@@ -289,10 +317,104 @@ __device__ __forceinline__ void attn_merge(const AttnArgs& a, int h, int nsplit)
             M = nm;
         }
         if (col && k == 0) {
-            float* out = a.out + static_cast<size_t>(h * G + g) * D + d;
-            *reinterpret_cast<float4*>(out) = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
+            const size_t o = static_cast<size_t>(h * G + g) * D + d;
+            if (out_tag) {
+                ll_store2(a.out_ll + o, num.x / den, num.y / den, out_tag);
+                ll_store2(a.out_ll + o + 2, num.z / den, num.w / den, out_tag);
+            } else {
+                *reinterpret_cast<float4*>(a.out + o) = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
+            }
         }
     }
+}
+
+// Merge of KV head h's partials, spread over the head's active items: item s
+// of ns takes the float4 quads [s Q / ns, (s+1) Q / ns) of the G*D outputs
+// (Q = G*D/4), one warp per quad.  Lane j polls splits j and j + 32 (ns <= 64):
+// their outputs at the quad and their (m, l), published by the items as
+// tagged words (part_tag); it merges its splits online, and a butterfly over
+// the warp combines the lanes in a fixed order.  The quad's four outputs go
+// to a.out_ll as tagged words (out_tag).  Each item reads about ns * 48 bytes
+// per quad, instead of one CTA reading every split's partial.  False (on
+// every thread) if a poll gave up.
+template <int G>
+__device__ __forceinline__ bool attn_merge_slice_ll(const AttnArgs& a, int h, int s, int ns, uint32_t part_tag,
+                                                    uint32_t out_tag, const int* abort) {
+    const int D = a.D, stride = attn_part_stride(D);
+    const int Q = G * D / 4;
+    const int q0 = s * Q / ns, q1 = (s + 1) * Q / ns;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    bool ok = true;
+    for (int qd = q0 + warp; qd < q1 && ok; qd += nw) {
+        const int g = 4 * qd / D, d = 4 * qd - g * D;
+        const uint64_t* base = a.part_ll + (static_cast<size_t>(h) * a.nsplit * G + g) * stride;
+        ulonglong2 w[2][3];
+        LLPoll pl;
+        pl.init(abort);
+        for (;;) {
+            bool ready = true;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int q = lane + 32 * i;
+                if (q < ns) {
+                    const uint64_t* row = base + static_cast<size_t>(q) * G * stride;
+                    w[i][0] = ll_load2(row + d);
+                    w[i][1] = ll_load2(row + d + 2);
+                    w[i][2] = ll_load2(row + D);
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) ready &= ll_has(w[i][k].x, part_tag) && ll_has(w[i][k].y, part_tag);
+                }
+            }
+            if (__all_sync(0xffffffffu, ready)) break;
+            if (!pl.again()) {
+                ok = false;
+                break;
+            }
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+        }
+        float M = -INFINITY, den = 0.f;
+        float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            if (lane + 32 * i >= ns) continue;
+            const float m = ll_val(w[i][2].x), l = ll_val(w[i][2].y);
+            const float nm = fmaxf(M, m);
+            const float sa = lse_scale(M, nm), sb = lse_scale(m, nm);
+            den = den * sa + l * sb;
+            num.x = num.x * sa + ll_val(w[i][0].x) * sb;
+            num.y = num.y * sa + ll_val(w[i][0].y) * sb;
+            num.z = num.z * sa + ll_val(w[i][1].x) * sb;
+            num.w = num.w * sa + ll_val(w[i][1].y) * sb;
+            M = nm;
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float oM = __shfl_xor_sync(0xffffffffu, M, o);
+            const float oden = __shfl_xor_sync(0xffffffffu, den, o);
+            float4 on;
+            on.x = __shfl_xor_sync(0xffffffffu, num.x, o);
+            on.y = __shfl_xor_sync(0xffffffffu, num.y, o);
+            on.z = __shfl_xor_sync(0xffffffffu, num.z, o);
+            on.w = __shfl_xor_sync(0xffffffffu, num.w, o);
+            const float nm = fmaxf(M, oM);
+            const float sa = lse_scale(M, nm), sb = lse_scale(oM, nm);
+            den = den * sa + oden * sb;
+            num.x = num.x * sa + on.x * sb;
+            num.y = num.y * sa + on.y * sb;
+            num.z = num.z * sa + on.z * sb;
+            num.w = num.w * sa + on.w * sb;
+            M = nm;
+        }
+        if (lane == 0) {
+            uint64_t* out = a.out_ll + static_cast<size_t>(h * G + g) * D + d;
+            ll_store2(out, num.x / den, num.y / den, out_tag);
+            ll_store2(out + 2, num.z / den, num.w / den, out_tag);
+        }
+    }
+    return !__syncthreads_or(!ok);
 }
 
 // Thread 0: initialise the tile barrier.  An initialised mbarrier owns its 8
@@ -311,13 +433,19 @@ __device__ __forceinline__ void attn_prefetch(const AttnArgs& a, const AttnRange
     if (R.active && R.ntiles > 0) attn_issue(a, R, S, 0, T);
 }
 
-// The item itself, once q/k/v of this step are in a.qkv (all threads).  `ph0`:
-// parity of the barrier's next phase (phases it completed before, mod 2); the
+// The item itself (all threads).  q/k/v of this step come from a.qkv, or with
+// in_tag != 0 from the tagged words a.qkv_ll (polled); the merged output goes
+// to a.out, or with out_tag != 0 to a.out_ll as tagged words.  With part_tag
+// != 0 the item publishes its partial as tagged words (a.part_ll) and then
+// merges its slice of the head's outputs (attn_merge_slice_ll); otherwise the
+// last item of the head to finish (atomic counter) merges them all.  `ph0`: parity
+// of the tile barrier's next phase (phases it completed before, mod 2); the
 // item completes R.ntiles phases.  Returns false if a bounded wait gave up
 // (after waiting, bounded, for the copy in flight); `a.err` is then set.
 template <int G, int T>
 __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const AttnRange& R, const AttnSmem& S,
-                                         uint32_t ph0) {
+                                         uint32_t ph0, uint32_t in_tag = 0, uint32_t out_tag = 0,
+                                         const int* abort = nullptr, uint32_t part_tag = 0) {
     if (!R.active) return true;
     const int D = a.D;
     const int tid = threadIdx.x;
@@ -327,19 +455,37 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
     const float* cs = a.rope_cos + static_cast<size_t>(R.pos) * (D / 2);
     const float* sn = a.rope_sin + static_cast<size_t>(R.pos) * (D / 2);
     const int warp = tid >> 5;
+    bool got = true;
     if (warp < G) {
-        head_prep_warp(a.qkv + static_cast<size_t>(h * G + warp) * D, a.q_norm, cs, sn, D, a.eps, S.qv + warp * D);
+        const size_t o = static_cast<size_t>(h * G + warp) * D;
+        got = head_prep_warp(a.qkv + o, a.qkv_ll + o, in_tag, a.q_norm, cs, sn, D, a.eps, S.qv + warp * D, abort);
     } else if (warp == G && R.has_new) {
-        head_prep_warp(a.qkv + static_cast<size_t>(a.nq + h) * D, a.k_norm, cs, sn, D, a.eps, S.knew);
+        const size_t o = static_cast<size_t>(a.nq + h) * D;
+        got = head_prep_warp(a.qkv + o, a.qkv_ll + o, in_tag, a.k_norm, cs, sn, D, a.eps, S.knew, abort);
     } else if (warp == G + 1 && R.has_new) {
-        const float* vraw = a.qkv + static_cast<size_t>(a.nq + a.nkv + h) * D;
-        for (int d = tid & 31; d < D; d += 32) S.vnew[d] = vraw[d];
+        const size_t o = static_cast<size_t>(a.nq + a.nkv + h) * D;
+        float v[kMaxHeadDim / 32];
+        got = head_load_warp(a.qkv + o, a.qkv_ll + o, in_tag, D, abort, v);
+#pragma unroll
+        for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+            const int d = (tid & 31) + 32 * i;
+            if (d < D) S.vnew[d] = v[i];
+        }
     }
     if (tid < G) {
         S.m_run[tid] = -INFINITY;
         S.l_run[tid] = 0.f;
     }
-    __syncthreads();
+    if (__syncthreads_or(!got)) {
+        // the inputs never came: the prefetched tile must still land (bounded)
+        // before this shared memory is reused
+        if (tid == 0) {
+            if (a.err) atomicExch(a.err, kErrGridTimeout);
+            if (R.ntiles > 0) (void)mbar_wait(S.bar, ph0 & 1u);
+        }
+        __syncthreads();
+        return false;
+    }
     if (R.has_new) {
         float* kdst = a.kcache + (R.head_base + R.pos) * D;
         float* vdst = a.vcache + (R.head_base + R.pos) * D;
@@ -349,11 +495,14 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
         }
     }
 
-    // Cached tiles (copied into S.kt / S.vt), then the new row as a last tile.
+    // Cached tiles (copied into S.kt / S.vt); the new row joins the last of
+    // them when it has room, else it is a tile of its own.
     float acc[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g] = 0.f;
-    const int nsteps = R.ntiles + (R.has_new ? 1 : 0);
+    const int last_nt = R.ntiles > 0 ? R.ncached - (R.ntiles - 1) * T : 0;
+    const bool fold_new = R.has_new && R.ntiles > 0 && last_nt < T;
+    const int nsteps = R.ntiles + (R.has_new && !fold_new ? 1 : 0);
 #pragma unroll 1
     for (int t = 0; t < nsteps; ++t) {
         const bool cached = t < R.ntiles;
@@ -369,8 +518,16 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
                 return false;
             }
         }
-        attend_tile<G, T>(S, cached ? S.kt : S.knew, cached ? S.vt : S.vnew, cached ? min(T, R.ncached - t * T) : 1, D,
-                          a.scale, acc);
+        int nt = cached ? min(T, R.ncached - t * T) : 1;
+        if (fold_new && t == R.ntiles - 1) {
+            for (int d = tid; d < D; d += blockDim.x) {
+                S.kt[static_cast<size_t>(nt) * D + d] = S.knew[d];
+                S.vt[static_cast<size_t>(nt) * D + d] = S.vnew[d];
+            }
+            ++nt;
+            __syncthreads();
+        }
+        attend_tile<G, T>(S, cached ? S.kt : S.knew, cached ? S.vt : S.vnew, nt, D, a.scale, acc);
         if (tid == 0 && t + 1 < R.ntiles) {
             fence_proxy_async_smem();
             attn_issue(a, R, S, t + 1, T);
@@ -379,6 +536,15 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
 
     // Per-split partial state.
     const int stride = attn_part_stride(D);
+    if (part_tag) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            uint64_t* pp = a.part_ll + (static_cast<size_t>(h * a.nsplit + s) * G + g) * stride;
+            if (tid < D) ll_store(pp + tid, acc[g], part_tag);
+            if (tid == 0) ll_store2(pp + D, S.m_run[g], S.l_run[g], part_tag);
+        }
+        return attn_merge_slice_ll<G>(a, h, s, R.nsplit, part_tag, out_tag, abort);
+    }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         float* pp = a.part + (static_cast<size_t>(h * a.nsplit + s) * G + g) * stride;
@@ -397,8 +563,15 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
     __syncthreads();
     if (!S.flag[0]) return true;
     __threadfence();
-    attn_merge<G>(a, h, R.nsplit);
-    if (tid == 0) a.counter[h] = 0u;
+    // The counter is reset before the merged output is published: a later
+    // layer's items of this head (which can only start after consumers saw the
+    // output) must find it at zero.
+    if (tid == 0) {
+        a.counter[h] = 0u;
+        __threadfence();
+    }
+    __syncthreads();
+    attn_merge<G>(a, h, R.nsplit, out_tag);
     return true;
 }
 

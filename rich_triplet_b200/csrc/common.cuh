@@ -219,6 +219,60 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return t;
 }
 
+// ---- Tagged words ("LL" words, after NCCL's low-latency protocol) ----------
+// A 32-bit value and the 32-bit tag of the phase that wrote it, stored as one
+// naturally aligned 64-bit word, so a reader sees either the old pair or the
+// new one, never a mix.  A consumer polls the words it needs until each
+// carries the tag it expects: the data itself says it is ready, with no
+// barrier or flag between producer and consumer.
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t tag) {
+    return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void ll_store(uint64_t* p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, tag)) : "memory");
+}
+// Two consecutive words at p (16-byte aligned).
+__device__ __forceinline__ void ll_store2(uint64_t* p, float a, float b, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(ll_word(a, tag)), "l"(ll_word(b, tag))
+                 : "memory");
+}
+__device__ __forceinline__ ulonglong2 ll_load2(const uint64_t* p) {
+    ulonglong2 r;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "l"(p) : "memory");
+    return r;
+}
+__device__ __forceinline__ uint64_t ll_load(const uint64_t* p) {
+    uint64_t r;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
+    return r;
+}
+__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+__device__ __forceinline__ bool ll_has(uint64_t w, uint32_t tag) { return static_cast<uint32_t>(w >> 32) == tag; }
+
+// Bound of a poll on tagged words: about two seconds of globaltimer (first
+// read after 32 polls), and an early stop when another CTA raised `abort`.
+struct LLPoll {
+    const int* abort;
+    uint64_t t0;
+    uint32_t it;
+    __device__ __forceinline__ void init(const int* ab) {
+        abort = ab;
+        t0 = 0;
+        it = 0;
+    }
+    // After a poll that found some word not ready: false when the wait must stop.
+    __device__ __forceinline__ bool again() {
+        if ((++it & 31u) == 0u) {
+            if (abort && *reinterpret_cast<const volatile int*>(abort)) return false;
+            uint64_t t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (it == 32u) t0 = t;
+            else if (t - t0 > 2000000000ull) return false;
+        }
+        return true;
+    }
+};
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
 
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {

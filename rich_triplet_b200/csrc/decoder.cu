@@ -291,6 +291,24 @@ int build_step(rt_dec* d) {
     if ((rc = dalloc(d, reinterpret_cast<void**>(&d_jobs), sizeof(rt::gcore::Job) * njobs, "step jobs")) != RT_OK) return rc;
     if ((rc = dalloc(d, reinterpret_cast<void**>(&d_attn), sizeof(rt::AttnArgs) * NL, "step attention")) != RT_OK) return rc;
     if ((rc = dalloc(d, reinterpret_cast<void**>(&d_sync), 4 * sizeof(uint32_t), "step sync")) != RT_OK) return rc;
+    {
+        // Tagged-word vectors of the step kernel; each slice 32-byte aligned.
+        const size_t nv[6] = {static_cast<size_t>(d->qkv_rows), static_cast<size_t>(d->NQ) * D, static_cast<size_t>(H),
+                              static_cast<size_t>(d->F), static_cast<size_t>(d->down_parts) * H,
+                              static_cast<size_t>(d->NKV) * nsplit * (d->NQ / d->NKV) * rt::attn_part_stride(D)};
+        size_t words = 0;
+        for (size_t n : nv) words += (n + 3) & ~size_t(3);
+        if ((rc = dalloc(d, reinterpret_cast<void**>(&d->ll), sizeof(uint64_t) * words, "step tagged vectors")) != RT_OK)
+            return rc;
+        RT_CHECK_CUDA(ctx, cudaMemsetAsync(d->ll, 0, sizeof(uint64_t) * words, ctx->stream));  // tag 0: never current
+        d->ll_words = words;
+        uint64_t* q = d->ll;
+        uint64_t** dst[6] = {&d->qkv_ll, &d->attn_ll, &d->o_ll, &d->h_ll, &d->down_ll, &d->part_ll};
+        for (int i = 0; i < 6; ++i) {
+            *dst[i] = q;
+            q += (nv[i] + 3) & ~size_t(3);
+        }
+    }
     // Tile-major copies of the Q4_K projections: each warp's share of a
     // projection is then one contiguous byte range (1-D bulk copies).
     auto tile_major = [&](const uint8_t* w, int64_t rows, int K, int parts, const uint8_t** out) -> int {
@@ -323,6 +341,7 @@ int build_step(rt_dec* d) {
         jq.tile_split = 1;
         jq.g_pre = norm_ptr(d, l, 0);
         jq.y = d->qkv;
+        jq.out_ll = d->qkv_ll;
         if (l == 0) {
             jq.embed = d->embed;
             jq.token = d->ctl;
@@ -331,6 +350,7 @@ int build_step(rt_dec* d) {
             p = 0;
         } else {
             jq.src = d->down;
+            jq.in_ll = d->down_ll;
             jq.src_parts = d->down_parts;
             jq.resid_in = d->resid[p];
             jq.resid_out = d->resid[1 - p];
@@ -340,9 +360,13 @@ int build_step(rt_dec* d) {
         rt::gcore::Job& jo = q4k(4 * l + 1, H, d->NQ * D);
         jo.x = d->attn;
         jo.y = d->o_out;
+        jo.in_ll = d->attn_ll;
+        jo.out_ll = d->o_ll;
         jo.tile_split = 1;
         rt::gcore::Job& jg = q4k(4 * l + 2, 2LL * d->F, H);
         jg.src = d->o_out;
+        jg.in_ll = d->o_ll;
+        jg.out_ll = d->h_ll;
         jg.resid_in = d->resid[p];
         jg.resid_out = d->resid[1 - p];
         jg.g_post = norm_ptr(d, l, 1);
@@ -358,6 +382,8 @@ int build_step(rt_dec* d) {
         jd.ptiles = static_cast<int32_t>(H / 16);
         jd.x = d->hbuf;
         jd.y = d->down;
+        jd.in_ll = d->h_ll;
+        jd.out_ll = d->down_ll;
         jd.tile_split = 1;
         if ((rc = tile_major(d->w_qkv[l], d->qkv_rows, H, 1, &jq.wt)) != RT_OK ||
             (rc = tile_major(d->w_o[l], H, d->NQ * D, 1, &jo.wt)) != RT_OK ||
@@ -387,6 +413,9 @@ int build_step(rt_dec* d) {
         a.part = d->attn_part;
         a.counter = d->counters;
         a.out = d->attn;
+        a.qkv_ll = d->qkv_ll;
+        a.out_ll = d->attn_ll;
+        a.part_ll = d->part_ll;
         a.err = ctx->d_err;
     }
     rt::gcore::Job& jl = jobs[4 * NL];
@@ -398,6 +427,7 @@ int build_step(rt_dec* d) {
     jl.rows = d->V;
     jl.eps = eps;
     jl.src = d->down;
+    jl.in_ll = d->down_ll;
     jl.src_parts = d->down_parts;
     jl.resid_in = d->resid[p];
     jl.resid_out = d->resid[1 - p];
@@ -473,9 +503,12 @@ int post_launch_check(rt_dec* d) {
         cudaMemsetAsync(d->counters, 0, sizeof(uint32_t) * (d->NKV + 1), d->ctx->stream);
         if (d->g_cnt && d->g_cnt_words) cudaMemsetAsync(d->g_cnt, 0, sizeof(uint32_t) * d->g_cnt_words, d->ctx->stream);
         if (d->use_step) {
-            // an aborted step kernel leaves its barrier counters behind
+            // an aborted step kernel leaves its counters behind; with the launch
+            // count back at zero, the tagged vectors are cleared too (tag 0 is
+            // never current), so no word of the aborted launch can pass for new
             cudaMemsetAsync(d->step_params.sync, 0, 2 * sizeof(uint32_t), d->ctx->stream);
             cudaMemsetAsync(d->step_params.abort, 0, sizeof(int), d->ctx->stream);
+            if (d->ll) cudaMemsetAsync(d->ll, 0, sizeof(uint64_t) * d->ll_words, d->ctx->stream);
         }
         cudaStreamSynchronize(d->ctx->stream);
         return fail(d->ctx, RT_E_TIMEOUT, "decode step: a kernel reported error word %d", w);
@@ -809,6 +842,31 @@ int rt_decoder_read_activation(rt_dec* d, int32_t which, float* host, int64_t co
     } else if (which == 1) {
         src = d->logits;
         n = d->V;
+    } else if (which >= 3 && which <= 7 && d->use_step) {
+        // the step kernel keeps these vectors as tagged words (value in the low 32 bits);
+        // the down projection as its column parts, added here in part order
+        uint64_t* v[5] = {d->qkv_ll, d->attn_ll, d->o_ll, d->h_ll, d->down_ll};
+        const int64_t nv[5] = {d->qkv_rows, static_cast<int64_t>(d->NQ) * d->D, d->H, d->F, d->H};
+        const int64_t nn = nv[which - 3];
+        const int parts = which == 7 ? d->down_parts : 1;
+        if (count < 0 || count > nn) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_read_activation: count %lld > %lld",
+                                                 static_cast<long long>(count), static_cast<long long>(nn));
+        std::vector<uint64_t> w(static_cast<size_t>(parts) * nn);
+        RT_CHECK_CUDA(d->ctx, cudaMemcpyAsync(w.data(), v[which - 3], sizeof(uint64_t) * w.size(), cudaMemcpyDeviceToHost,
+                                              d->ctx->stream));
+        RT_CHECK_CUDA(d->ctx, cudaStreamSynchronize(d->ctx->stream));
+        auto val = [](uint64_t x) {
+            const uint32_t b = static_cast<uint32_t>(x);
+            float f;
+            memcpy(&f, &b, 4);
+            return f;
+        };
+        for (int64_t i = 0; i < count; ++i) {
+            float a = val(w[static_cast<size_t>(i)]);
+            for (int q = 1; q < parts; ++q) a += val(w[static_cast<size_t>(q) * nn + i]);
+            host[i] = a;
+        }
+        return RT_OK;
     } else if (which == 7 && d->use_step && d->down_parts > 1) {
         // the step kernel leaves the down projection as column-part partials
         if (count < 0 || count > d->H) return fail(d->ctx, RT_E_SHAPE, "rt_decoder_read_activation: count %lld > %lld",

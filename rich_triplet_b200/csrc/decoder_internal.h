@@ -36,6 +36,12 @@ struct rt_dec {
     float *resid[2] = {nullptr, nullptr}, *qkv = nullptr, *attn = nullptr, *o_out = nullptr, *hbuf = nullptr,
           *down = nullptr, *logits = nullptr, *attn_part = nullptr;
     rt::GreedySlot* am_slot = nullptr;
+    // The step kernel's vectors as tagged words (value + phase tag, 8 bytes each):
+    // q/k/v, attention output, O, gated FFN hidden, down projection parts.
+    uint64_t* ll = nullptr;
+    uint64_t *qkv_ll = nullptr, *attn_ll = nullptr, *o_ll = nullptr, *h_ll = nullptr, *down_ll = nullptr,
+             *part_ll = nullptr;
+    size_t ll_words = 0;
     uint32_t* counters = nullptr;  // [NKV] attention + [1] argmax
     float* g_part = nullptr;       // GEMV split-tile partials (shared by the step's GEMVs, which run in order)
     uint32_t* g_cnt = nullptr;     // GEMV split-tile counters, zero between launches

@@ -30,12 +30,13 @@
 // (sub-block 2c+1, as 16 q) as the u8 A operand of mma.m16n8k32.u8.s8.  x is
 // split once per job, per sub-block, into three int8 planes
 // x = s * (p0 + p1/254 + p2/254^2) (|error| <= s/129032, s = max|x|/127 over
-// the sub-block), the s8 B operand.  The MMA of sub-block j puts planes 0/1 in B
-// columns 2(j&3), 2(j&3)+1 (and plane 2 in column 2(j&3) of a second MMA), zero
-// elsewhere, so lane t of every lane quad ends up holding the three plane sums
-// of sub-blocks t and t+4 for two rows, and all 32 lanes share the scale
-// epilogue.  (Two planes would halve the MMAs but leave errors near 3e-5 of
-// rms(y): the dot product of K terms accumulates the 16-bit rounding of x.)
+// the sub-block), the s8 B operand.  One MMA per sub-block: its planes sit in
+// B columns 4 (j&1) + 0..2, zero elsewhere, and the two MMAs of a chunk share
+// an accumulator, so eight MMAs cover a 16-row unit.  Two shuffles per chunk
+// pair up each row's three plane sums, and every lane runs the scale
+// epilogue for one row and four sub-blocks.  (Two planes would halve the
+// B columns but leave errors near 3e-5 of rms(y): the dot product of K terms
+// accumulates the 16-bit rounding of x.)
 //
 // BF16 (MatBf16::dot_row, src/autograd2.rs:861-888).  The weights, loaded by
 // ldmatrix, are the A operand of mma.m16n8k16.bf16; x is split exactly into
@@ -71,11 +72,16 @@ __host__ __device__ constexpr int box_x(int kind) { return kind == kQ4K ? kQ4KPi
 __host__ __device__ constexpr int box_step(int kind) { return kind == kQ4K ? kQ4KPitch / 8 : kBF16SegCols * 2 / 8; }
 
 // Shared-memory plane layout.
-//  Q4_K: plane p (0..2) at p * pstride bytes; per 256-column segment 256 bytes,
-//  ordered so that lane t of the quad feeding B column pair r gets, in one
-//  16-byte load, its MMA fragments of sub-blocks r and r+4:
-//      byte r*64 + t*16 + (j>>2)*8 + (e>=16)*4 + (e&3) holds element e of
-//      sub-block j (r = j&3, t = (e&15)>>2).
+//  Q4_K: plane p (0..2) at p * pstride bytes; per 256-column segment 256 bytes.
+//  For the four sub-blocks j = 2 jj + par of one parity, lane t of the lane
+//  group feeding B column 4 par + p needs, per sub-block, the B fragment (b0,
+//  b1) = (elements 4t..4t+3, elements 16+4t..19+4t) of plane p: byte
+//      seg*256 + (jj >> 1)*128 + (par*4 + t)*16 + (jj & 1)*8 + (e >= 16)*4 + (e & 3)
+//  holds element e of sub-block j, t = (e & 15) >> 2, so that lane fetches
+//  its fragments for all four sub-blocks in two 16-byte loads, and the 24
+//  lanes that feed B read whole 128-byte lines per plane.  Per
+//  segment and parity the four {unit, sum} of xsx sit together (xsx index
+//  (seg*2 + par)*4 + jj), so a lane fetches its four in two 16-byte loads.
 //  BF16: plane p (hi, mid, lo) at p * pstride bytes, u16 elements; per 16
 //  columns, lane t's B fragment (columns 2t, 2t+1, 8+2t, 9+2t) is 8 bytes at 8t.
 __host__ __device__ inline int q4k_pstride(int Kp) { return Kp + 64; }       // = 64 mod 128: no bank conflicts
@@ -175,11 +181,10 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
         const float r2 = fmaf(-f1, s254, r1);
         (void)round_clamp127(r2 * inv254sq, &b2[e]);
     }
-    const int j = lane >> 2;  // sub-block of this lane's elements
-    const int r = j & 3, half = j >> 2;
-    const int t0 = (lane & 1) ? 2 : 0;    // elements 8(l&3)..: t of the first four
-    const int posb = (lane & 2) ? 4 : 0;  // second 16 elements of the sub-block
-    const int o0 = seg * 256 + r * 64 + t0 * 16 + half * 8 + posb;
+    const int j = lane >> 2;  // sub-block of this lane's elements (8(lane&3)..8(lane&3)+7 of it)
+    const int par = j & 1, jj = j >> 1, q = lane & 3;
+    const int t0 = 2 * (q & 1), hi = q >> 1;  // elements 8q..8q+3: t = t0; 8q+4..8q+7: t = t0 + 1
+    const int o0 = seg * 256 + (jj >> 1) * 128 + (par * 4 + t0) * 16 + (jj & 1) * 8 + hi * 4;
     const int o1 = o0 + 16;
     uint8_t* P0 = planes;
     uint8_t* P1 = planes + pstride;
@@ -190,11 +195,10 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
     *reinterpret_cast<uint32_t*>(P1 + o1) = pack4_low(b1[4], b1[5], b1[6], b1[7]);
     *reinterpret_cast<uint32_t*>(P2 + o0) = pack4_low(b2[0], b2[1], b2[2], b2[3]);
     *reinterpret_cast<uint32_t*>(P2 + o1) = pack4_low(b2[4], b2[5], b2[6], b2[7]);
-    if ((lane & 3) == 0) {
+    if (q == 0) {
         // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
-        // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
-        const float unit = s * (1.0f / 64516.0f) * ((j & 1) ? 0.0625f : 1.0f);
-        xsx[seg * 8 + j] = make_float2(unit, sum);
+        const float unit = s * (1.0f / 64516.0f) * (par ? 0.0625f : 1.0f);
+        xsx[(seg * 2 + par) * 4 + jj] = make_float2(unit, sum);
     }
 }
 
@@ -387,6 +391,10 @@ struct Job {
     int32_t* token_out;
     int32_t* pos_inout;
     int32_t* token_hist;
+    // Tagged-word input and output (decode-step kernel): in_ll holds x, or the
+    // src_parts vectors of a residual-update prologue; out_ll receives y.
+    const uint64_t* in_ll;
+    uint64_t* out_ll;
     int32_t fail_token;   // 1: a failed launch writes token_out = -1 (GemvArgs::fail_token)
     uint32_t wait_iters;  // poll limit of the weight-stream waits (0: default)
 };
@@ -706,6 +714,212 @@ __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uin
     __syncthreads();
 }
 
+// ---- Prologues over tagged-word inputs (decode-step kernel) ----------------
+// The input vector is read straight from the producers' tagged words: a
+// thread loads every word it needs at once and re-polls until each carries
+// `tag`.  They return false (the same on every thread) if a wait gave up
+// (LLPoll: about two seconds, or another CTA raised `abort`), and end with
+// __syncthreads.
+
+// Planes of x = a.in_ll[0 .. K) (K a multiple of 8).  Q4_K: warp w takes
+// segments w, w + nw, ...; each lane loads its 8 values of every segment of
+// the warp (up to kLLSegs at once).
+constexpr int kLLSegs = 3;
+
+template <int KIND>
+__device__ __forceinline__ bool ll_prologue_plain(const Job& a, const JobSmem& S, uint32_t tag, const int* abort) {
+    static_assert(KIND == kQ4K, "the step kernel's plain prologues are Q4_K projections");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int K = a.K;
+    const int Kp = (K + kQ4KSegCols - 1) / kQ4KSegCols * kQ4KSegCols;
+    const int pstride = q4k_pstride(Kp);
+    const int nseg = Kp / kQ4KSegCols;
+    bool ok = true;
+    for (int s0 = warp; s0 < nseg && ok; s0 += kLLSegs * nw) {
+        ulonglong2 w[kLLSegs][4];
+        LLPoll pl;
+        pl.init(abort);
+        for (;;) {
+            bool ready = true;
+#pragma unroll
+            for (int b = 0; b < kLLSegs; ++b) {
+                const int seg = s0 + b * nw, c0 = seg * kQ4KSegCols + lane * 8;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    w[b][h] = seg < nseg && c0 + 2 * h < K ? ll_load2(a.in_ll + c0 + 2 * h)
+                                                           : make_ulonglong2(ll_word(0.f, tag), ll_word(0.f, tag));
+                    ready &= ll_has(w[b][h].x, tag) && ll_has(w[b][h].y, tag);
+                }
+            }
+            if (__all_sync(0xffffffffu, ready)) break;
+            if (!pl.again()) {
+                ok = false;
+                break;
+            }
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int b = 0; b < kLLSegs; ++b) {
+            const int seg = s0 + b * nw;
+            if (seg >= nseg) break;
+            const float4 lo = make_float4(ll_val(w[b][0].x), ll_val(w[b][0].y), ll_val(w[b][1].x), ll_val(w[b][1].y));
+            const float4 hi = make_float4(ll_val(w[b][2].x), ll_val(w[b][2].y), ll_val(w[b][3].x), ll_val(w[b][3].y));
+            chunk_planes<KIND>(lo, hi, seg, lane, pstride, S);
+        }
+    }
+    return !__syncthreads_or(!ok);
+}
+
+// The residual-update + RMSNorm prologue with the residual stream kept in
+// S.xs between prologues (every CTA computes it identically, so no CTA reads
+// it back from global memory): sub = sum of the a.src_parts vectors of K at
+// a.in_ll (in part order), xs += rmsnorm(sub) * (1 + g_post), x = rmsnorm(xs) *
+// (1 + g_pre) (Gemma3Block::forward_cached, src/transformer4.rs:1954-1964;
+// rms_norm_gemma3, src/autograd2.rs:3477-3496).  CTA 0 also stores the new
+// residual at a.resid_out when that is set.
+constexpr int kLLPairs = 3;  // pairs of elements of the vector per thread and poll (K <= 6 * threads)
+
+template <int KIND>
+__device__ __forceinline__ bool ll_prologue_resid_norm(const Job& a, const JobSmem& S, uint32_t pbar_phase,
+                                                       uint32_t tag, const int* abort) {
+    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31;
+    const int K = a.K;
+    const int Kp = (K + seg_cols(KIND) - 1) / seg_cols(KIND) * seg_cols(KIND);
+    const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
+    const int parts = a.src_parts > 1 ? a.src_parts : 1;
+    const float inv_d = 1.0f / static_cast<float>(K);
+    float* sub = S.sub;
+    bool ok = true;
+    float ss = 0.f;
+    const int npairs = K / 2;
+    for (int pb = tid; pb < npairs && ok; pb += kLLPairs * nthr) {
+        ulonglong2 w[kLLPairs][kMaxSrcParts];
+        LLPoll pl;
+        pl.init(abort);
+        for (;;) {
+            bool ready = true;
+#pragma unroll
+            for (int i = 0; i < kLLPairs; ++i) {
+                const int c = 2 * (pb + i * nthr);
+#pragma unroll
+                for (int q = 0; q < kMaxSrcParts; ++q) {
+                    const bool use = c < K && q < parts;
+                    w[i][q] = use ? ll_load2(a.in_ll + static_cast<size_t>(q) * K + c)
+                                  : make_ulonglong2(ll_word(0.f, tag), ll_word(0.f, tag));
+                    ready &= ll_has(w[i][q].x, tag) && ll_has(w[i][q].y, tag);
+                }
+            }
+            if (ready) break;
+            if (!pl.again()) {
+                ok = false;
+                break;
+            }
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int i = 0; i < kLLPairs; ++i) {
+            const int c = 2 * (pb + i * nthr);
+            if (c >= K) break;
+            float2 s2 = make_float2(ll_val(w[i][0].x), ll_val(w[i][0].y));
+#pragma unroll
+            for (int q = 1; q < kMaxSrcParts; ++q)
+                if (q < parts) s2 = make_float2(s2.x + ll_val(w[i][q].x), s2.y + ll_val(w[i][q].y));
+            *reinterpret_cast<float2*>(sub + c) = s2;
+            ss += s2.x * s2.x + s2.y * s2.y;
+        }
+    }
+    if (__syncthreads_or(!ok)) return false;
+    ss = block_sum(ss, S.red);
+    if (!mbar_wait(S.pbar, pbar_phase) && lane == 0) atomicExch(&S.flag[0], 1);
+    const float r1 = 1.0f / sqrtf(ss * inv_d + a.eps);
+    float ss2 = 0.f;
+#pragma unroll 1
+    for (int c = tid * 4; c < K; c += nthr * 4) {
+        const float4 s4 = *reinterpret_cast<const float4*>(sub + c);
+        const float4 r4 = *reinterpret_cast<const float4*>(S.xs + c);
+        const float4 g4 = *reinterpret_cast<const float4*>(S.gpost + c);
+        auto upd = [&](float rv, float sv, float gv) {
+            return __fadd_rn(rv, __fmul_rn(__fmul_rn(sv, r1), __fadd_rn(1.0f, gv)));
+        };
+        const float4 nv = make_float4(upd(r4.x, s4.x, g4.x), upd(r4.y, s4.y, g4.y), upd(r4.z, s4.z, g4.z),
+                                      upd(r4.w, s4.w, g4.w));
+        *reinterpret_cast<float4*>(S.xs + c) = nv;
+        if (blockIdx.x == 0 && a.resid_out) *reinterpret_cast<float4*>(a.resid_out + c) = nv;
+        ss2 += sumsq4(nv);
+    }
+    ss2 = block_sum(ss2, S.red);
+    planes_from_smem<KIND>(K, Kp, pstride, 1.0f / sqrtf(ss2 * inv_d + a.eps), S);
+    __syncthreads();
+    return true;
+}
+
+// This lane's share of one Q4_K unit (16 rows x one 256-column segment at
+// shared-memory address ub, x segment xseg): the sum over the four sub-blocks
+// of parity (t >> 1) of row g + 8 (t & 1), scales applied.
+__device__ __forceinline__ float q4k_unit_value(const uint8_t* ub, int xseg, int g, int t, int pstride, int ldsm_off,
+                                                const JobSmem& S) {
+    // One MMA per sub-block j (k = its 32 elements).  B column 4 par + p
+    // holds plane p of x's sub-block j when j has parity par (lane
+    // group g = 4 par + p feeds it); columns 3 and 7 stay zero.  The
+    // MMAs of chunk c (sub-blocks 2c, 2c+1: low and high nibbles of the
+    // same 32 bytes) share accumulator c: columns 0..2 the plane sums
+    // of 2c, columns 4..6 those of 2c+1.
+    const int bpar = g >> 2, bpl = g & 3;
+    const uint32_t own0 = bpar == 0 && bpl < 3 ? 0xFFFFFFFFu : 0u;
+    const uint32_t own1 = bpar == 1 && bpl < 3 ? 0xFFFFFFFFu : 0u;
+    uint4 Bw0 = make_uint4(0u, 0u, 0u, 0u), Bw1 = Bw0;
+    if (bpl < 3) {
+        const uint8_t* pb = S.planes + bpl * pstride + xseg * 256 + (bpar * 4 + t) * 16;
+        Bw0 = lds128(pb);
+        Bw1 = lds128(pb + 128);
+    }
+    // The scale epilogue of lane (g, t) covers row g + 8 (t & 1) and the
+    // four sub-blocks of parity t >> 1.
+    const int lpar = t >> 1, odd = t & 1;
+    const uint4 hd = lds128(ub + (g + 8 * odd) * kQ4KPitch);
+    const float4 xs01 = *reinterpret_cast<const float4*>(S.xsx + (xseg * 2 + lpar) * 4);
+    const float4 xs23 = *reinterpret_cast<const float4*>(S.xsx + (xseg * 2 + lpar) * 4 + 2);
+    int acc[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0;
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(ub + ldsm_off + 32 * c, a0, a1, a2, a3);
+        const uint32_t w0 = c == 0 ? Bw0.x : c == 1 ? Bw0.z : c == 2 ? Bw1.x : Bw1.z;
+        const uint32_t w1 = c == 0 ? Bw0.y : c == 1 ? Bw0.w : c == 2 ? Bw1.y : Bw1.w;
+        mma_u8s8(acc[c], a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu, w0 & own0,
+                 w1 & own0);
+        mma_u8s8(acc[c], a0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, a2 & 0xF0F0F0F0u, a3 & 0xF0F0F0F0u, w0 & own1,
+                 w1 & own1);
+    }
+    // Lane t even holds (p0, p1) of rows g and g+8, its odd neighbour
+    // (p2, 0): they swap so that the even lane has row g's three sums
+    // and the odd lane row g+8's.
+    const float d = f16_bits_to_f32(hd.x & 0xFFFFu), dmin = f16_bits_to_f32(hd.x >> 16);
+    // scale_min (src/autograd2.rs:1075-1085), four 6-bit fields per word
+    const uint32_t s_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
+    const uint32_t s_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+    const uint32_t sel_a = 0x7540u | static_cast<uint32_t>(lpar), sel_b = 0x7540u | static_cast<uint32_t>(2 + lpar);
+    float vs = 0.f, vm = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const int x = __shfl_xor_sync(0xffffffffu, odd ? acc[c][0] : acc[c][2], 1);
+        const int y = __shfl_xor_sync(0xffffffffu, acc[c][3], 1);
+        const int P0 = odd ? x : acc[c][0], P1 = odd ? y : acc[c][1], P2 = odd ? acc[c][2] : x;
+        const float T = fmaf(static_cast<float>(P0), 64516.0f,
+                             fmaf(static_cast<float>(P1), 254.0f, static_cast<float>(P2)));
+        // sub-block 2c + lpar: bytes lpar / 2 + lpar of the low (c < 2) or high words
+        const uint32_t sw = c < 2 ? s_lo : s_hi, mw = c < 2 ? m_lo : m_hi;
+        const uint32_t sel = (c & 1) ? sel_b : sel_a;
+        const float2 us = c == 0 ? make_float2(xs01.x, xs01.y) : c == 1 ? make_float2(xs01.z, xs01.w)
+                        : c == 2 ? make_float2(xs23.x, xs23.y) : make_float2(xs23.z, xs23.w);
+        vs = fmaf(byte_to_float(sw, sel), T * us.x, vs);
+        vm = fmaf(byte_to_float(mw, sel), us.y, vm);
+    }
+    return d * vs - dmin * vm;
+}
+
 // How the warps' shares of a job are laid out (Job::tile_split matches it).
 enum SplitMode : int {
     kSplitGrid = 0,  // whole-grid warp split; shared tiles combined through global scratch
@@ -715,9 +929,10 @@ enum SplitMode : int {
 // Stream this warp's units of job `a` (whose planes are ready) through the
 // epilogue.  Returns false if a wait gave up (the warp's stream is then
 // abandoned; the caller drains it).  gr: this lane's running greedy state.
+// out_tag != 0: rows go to a.out_ll as tagged words with that tag.
 template <int KIND, int EPI, int SPLIT>
 __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const JobSmem& S, const SplitScratch& sc,
-                                              Greedy& gr) {
+                                              Greedy& gr, uint32_t out_tag = 0) {
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int nseg = a.nseg;
@@ -733,17 +948,20 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
         const int64_t r = r0 + lane;
         if constexpr (EPI == kEpiGeluPair) {
             const float up = __shfl_down_sync(0xffffffffu, v, 1);
-            if (lane < kTile && !(lane & 1) && r < a.rows) a.y[r >> 1] = __fmul_rn(gelu_tanh_dev(v), up);
+            if (lane < kTile && !(lane & 1) && r < a.rows) {
+                const float h = __fmul_rn(gelu_tanh_dev(v), up);
+                if (out_tag) ll_store(a.out_ll + (r >> 1), h, out_tag);
+                else a.y[r >> 1] = h;
+            }
         } else {
             if (lane < kTile && r < a.rows) {
-                a.y[r] = v;
+                if (out_tag) ll_store(a.out_ll + r, v, out_tag);
+                else a.y[r] = v;
                 if constexpr (EPI == kEpiArgmax) gr.add(v, r);
             }
         }
     };
 
-    const int q = g >> 1;  // Q4_K: the B column pair this lane feeds
-    const uint32_t jsel = 0x7540u | static_cast<uint32_t>(t);
     // ldmatrix row address of this lane within a unit (matrix l/8: rows 0-7 or
     // 8-15, first or second 16 bytes of the 32-byte k slice)
     const int ldsm_off = KIND == kQ4K
@@ -760,6 +978,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     int pu = 0;  // units of the current tile piece
     const int upc = a.wt ? kTileMajorUnitsPerCopy : 1;
     int in_copy = 0, uic = 0;  // units left in / consumed from the current copy
+    float cv0 = 0.f, cv1 = 0.f;  // Q4_K: this lane's values of the current copy's units
     for (int i = 0; i < n; ++i) {
         if (in_copy == 0) {
             const bool ok = mbar_wait_n(&st.full[st.jb], st.ph, a.wait_iters);
@@ -769,54 +988,18 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
         }
         const uint8_t* ub = st.ring + static_cast<size_t>(st.jb) * st.slot_bytes + uic * unit_bytes(KIND);
         if constexpr (KIND == kQ4K) {
-            // B fragments: planes 0/1 of sub-blocks q and q+4 (this lane's column
-            // pair) and, for even g, plane 2.
-            const uint8_t* pb = S.planes + xseg * 256 + q * 64 + t * 16;
-            const uint4 B01 = lds128(pb + (g & 1) * pstride);
-            const uint4 B2 = (g & 1) ? make_uint4(0u, 0u, 0u, 0u) : lds128(pb + 2 * pstride);
-            const uint4 h0 = lds128(ub + g * kQ4KPitch), h1 = lds128(ub + (g + 8) * kQ4KPitch);
-            const float2 xa = S.xsx[xseg * 8 + t], xb = S.xsx[xseg * 8 + t + 4];
-            int c01[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, c2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(ub + ldsm_off + 32 * c, a0, a1, a2, a3);
-#pragma unroll
-                for (int hi = 0; hi < 2; ++hi) {
-                    const int j = 2 * c + hi;  // sub-block
-                    const int r = j & 3, set = j >> 2;
-                    const uint32_t m = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-                    const bool own = q == r;
-                    const uint32_t b0 = own ? (set ? B01.z : B01.x) : 0u;
-                    const uint32_t b1 = own ? (set ? B01.w : B01.y) : 0u;
-                    const uint32_t e0 = own ? (set ? B2.z : B2.x) : 0u;
-                    const uint32_t e1 = own ? (set ? B2.w : B2.y) : 0u;
-                    mma_u8s8(c01[set], a0 & m, a1 & m, a2 & m, a3 & m, b0, b1);
-                    mma_u8s8(c2[set], a0 & m, a1 & m, a2 & m, a3 & m, e0, e1);
+            // The units of a copy are computed together (independent chains, so
+            // the scheduler can interleave them), then consumed one by one.
+            if (uic == 0) {
+                cv0 = q4k_unit_value(ub, xseg, g, t, pstride, ldsm_off, S);
+                if (in_copy > 1) {
+                    const int xs1 = seg + 1 < nseg ? xseg + 1 : part_base(tile + 1);
+                    cv1 = q4k_unit_value(ub + kQ4KUnit, xs1, g, t, pstride, ldsm_off, S);
                 }
             }
-            // Lane t: sub-blocks t (set 0) and t+4 (set 1); c01[.][0]/[1] = planes
-            // 0/1 of row g, [2]/[3] of row g+8; plane 2 sits in the even columns
-            // (c2[.][0] row g, c2[.][2] row g+8).
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const uint4 h = half ? h1 : h0;
-                const float d = f16_bits_to_f32(h.x & 0xFFFFu), dmin = f16_bits_to_f32(h.x >> 16);
-                // scale_min (src/autograd2.rs:1075-1085), four 6-bit fields per word
-                const uint32_t s_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
-                const uint32_t s_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-                const uint32_t m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-                const float sc0 = byte_to_float(s_lo, jsel), mn0 = byte_to_float(m_lo, jsel);
-                const float sc1 = byte_to_float(s_hi, jsel), mn1 = byte_to_float(m_hi, jsel);
-                const int i0 = 2 * half;
-                const float T0 = fmaf(static_cast<float>(c01[0][i0]), 64516.0f,
-                                      fmaf(static_cast<float>(c01[0][i0 + 1]), 254.0f, static_cast<float>(c2[0][i0])));
-                const float T1 = fmaf(static_cast<float>(c01[1][i0]), 64516.0f,
-                                      fmaf(static_cast<float>(c01[1][i0 + 1]), 254.0f, static_cast<float>(c2[1][i0])));
-                const float v = d * (sc0 * (T0 * xa.x) + sc1 * (T1 * xb.x)) - dmin * (mn0 * xa.y + mn1 * xb.y);
-                if (half) acc1 += v;
-                else acc0 += v;
-            }
+            const float v = uic == 0 ? cv0 : cv1;
+            if (t & 1) acc1 += v;
+            else acc0 += v;
         } else {
             // BF16: lanes g < 3 feed B column g (plane g); the rest feed zeros.
             const uint8_t* pb = S.planes + (g < 3 ? g : 0) * pstride + xseg * (kBF16SegCols * 2) + t * 8;
@@ -931,7 +1114,7 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
 // threads call it; it starts with __syncthreads.  The warps' unit ranges come
 // from the table job_units_run filled (no division per piece).
 template <int EPI>
-__device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, Greedy& gr) {
+__device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, Greedy& gr, uint32_t out_tag = 0) {
     __syncthreads();
     const uint32_t nw = blockDim.x >> 5, warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -966,9 +1149,12 @@ __device__ __forceinline__ void cta_combine(const Job& a, const JobSmem& S, Gree
         const int64_t r = static_cast<int64_t>(T) * kTile + row;
         if (r >= a.rows) continue;
         if constexpr (EPI == kEpiGeluPair) {
-            a.y[r >> 1] = __fmul_rn(gelu_tanh_dev(v0), v1);
+            const float h = __fmul_rn(gelu_tanh_dev(v0), v1);
+            if (out_tag) ll_store(a.out_ll + (r >> 1), h, out_tag);
+            else a.y[r >> 1] = h;
         } else {
-            a.y[r] = v0;
+            if (out_tag) ll_store(a.out_ll + r, v0, out_tag);
+            else a.y[r] = v0;
             if constexpr (EPI == kEpiArgmax) gr.add(v0, r);
         }
     }

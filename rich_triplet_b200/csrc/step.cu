@@ -5,21 +5,28 @@
 // projection, gate/up with the GELU gate and the down projection, then the LM
 // head with the greedy argmax (Gemma3Block::forward_cached,
 // src/transformer4.rs:1954-1964, and MetalDecodeContext::decode_step,
-// src/metal_decode.rs:1930-2074).  One CTA per SM, all resident at once; a
-// grid-wide barrier separates phases whose inputs are the previous phase's
-// outputs.
+// src/metal_decode.rs:1930-2074).  One CTA per SM, all resident at once.
+//
+// No grid-wide barrier: every vector a phase produces (q/k/v, the attention
+// output, O, the gated FFN hidden, the down projection's column parts) is
+// published as tagged words (common.cuh), and the next phase's prologue polls
+// exactly the words it needs until they carry this launch's tag for that
+// vector.  A CTA that finishes a phase early starts the next one as soon as
+// its inputs exist, and the data itself says when that is, so there is no
+// separate arrival round trip.  Every CTA keeps the residual stream in its
+// own shared memory (each computes it identically), so it is never read back.
 //
 // What this buys over one launch per projection: every warp's weight stream
 // (gemv_core.cuh) runs through all the step's projections back to back, so
 // the copies of the next projection's weights are already in flight, or in
-// shared memory, while the grid waits at a barrier; and there is no kernel
+// shared memory, while the CTA waits for its input; and there is no kernel
 // launch, no first-copy latency and no drain between projections.  The GEMV
 // and attention arithmetic is the same code the standalone kernels run.
 //
-// Every wait is bounded: mbarrier waits by iteration count, grid barriers by
-// time (globaltimer).  A CTA that gives up raises `abort`; the others see it
-// at their next barrier, wait (bounded) for their own copies in flight, and
-// leave.
+// Every wait is bounded: mbarrier waits by iteration count, tagged-word polls
+// by time (globaltimer, about 2 s).  A CTA that gives up raises `abort`; the
+// others see it in their polls, wait (bounded) for their own copies in
+// flight, and leave.
 #include <algorithm>
 
 #include "attention_core.cuh"
@@ -38,7 +45,6 @@ constexpr int kStepNb = 2;           // 32 copies in flight per SM
 constexpr int kSlotBytes =  // a ring slot holds a BF16 unit or a copy of tile-major Q4_K units
     kBF16Unit > kTileMajorUnitsPerCopy * kQ4KUnit ? kBF16Unit : kTileMajorUnitsPerCopy * kQ4KUnit;
 constexpr int kAttnT = 16;           // cached positions per attention tile
-constexpr uint64_t kBarrierTimeoutNs = 2000000000ull;
 
 __device__ __forceinline__ uint64_t gtimer() {
     uint64_t t;
@@ -46,18 +52,12 @@ __device__ __forceinline__ uint64_t gtimer() {
     return t;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 struct StepSmem {
     uint64_t* full;  // [warps][nb]
     uint64_t* pbar;
     uint64_t* abar;  // attention tile barrier (kept out of `uni`: see attn_bar_init)
     float* red;
-    int* flags;      // 0: this CTA failed, 1: last CTA (argmax), 2: barrier result, 3: attention copy pending
+    int* flags;      // 0: this CTA failed, 1: last CTA (argmax), 2: unused, 3: attention copy pending
     GreedySmem* gs;
     float* gpost;    // [hidden]
     float* gpre;     // [hidden]
@@ -116,49 +116,12 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
     return off;
 }
 
-// Grid-wide barrier (all threads call it).  Returns false when the grid must
-// stop: this CTA failed, another CTA raised `abort`, or the wait timed out.
-__device__ __forceinline__ bool grid_sync(const StepParams& P, uint32_t& nsync, int* flags) {
-    __syncthreads();
-    ++nsync;
-    if (threadIdx.x == 0) {
-        bool ok = flags[0] == 0;
-        if (!ok) atomicExch(P.abort, 1);
-        __threadfence();
-        atomicAdd(&P.sync[0], 1u);
-        const uint32_t target = nsync * gridDim.x;
-        // The time bound starts after 1024 polls, so that a barrier the grid
-        // reaches promptly never reads the globaltimer.
-        uint64_t t0 = 0;
-        uint32_t spin = 0;
-        while (ok) {
-            if (ld_acquire_u32(&P.sync[0]) >= target) break;
-            if (*reinterpret_cast<volatile int*>(P.abort)) {
-                ok = false;
-                break;
-            }
-            if ((++spin & 1023u) == 0u) {
-                if (spin == 1024u) t0 = gtimer();
-                else if (gtimer() - t0 > kBarrierTimeoutNs) {
-                    if (P.err) atomicExch(P.err, kErrGridTimeout);
-                    atomicExch(P.abort, 1);
-                    ok = false;
-                }
-            }
-        }
-        __threadfence();
-        flags[2] = ok ? 1 : 0;
-    }
-    __syncthreads();
-    return flags[2] != 0;
-}
-
 // Stream this warp's units of a projection; on failure drain the warp's copies
 // and mark the CTA failed.
 template <int KIND, int EPI>
 __device__ __forceinline__ void run_units(const Job& j, Stream& st, const JobSmem& JS, const StepParams& P,
-                                          int* flags, Greedy& gr) {
-    if (!job_units_run<KIND, EPI, kSplitTile>(j, st, JS, P.scratch, gr)) {
+                                          int* flags, Greedy& gr, uint32_t out_tag) {
+    if (!job_units_run<KIND, EPI, kSplitTile>(j, st, JS, P.scratch, gr, out_tag)) {
         if ((threadIdx.x & 31) == 0) {
             atomicExch(&flags[0], 1);
             if (P.err) atomicExch(P.err, kErrMbarTimeout);
@@ -167,6 +130,15 @@ __device__ __forceinline__ void run_units(const Job& j, Stream& st, const JobSme
         __syncwarp();
     }
 }
+
+// Raise the grid's abort flag after a wait of this CTA gave up (thread 0).
+__device__ __forceinline__ void step_fail(const StepParams& P, int code) {
+    if (P.err) atomicCAS(P.err, 0, code);
+    atomicExch(P.abort, 1);
+}
+
+// Tag of the vector phase k of layer l writes in this launch (never 0).
+enum StepVec : int { kVecQkv = 0, kVecAttn = 1, kVecO = 2, kVecH = 3, kVecDown = 4, kVecAttnPart = 5 };
 
 template <int G>
 __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepParams P) {
@@ -185,14 +157,20 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         S.flags[0] = S.flags[1] = S.flags[2] = S.flags[3] = 0;
     }
     __syncthreads();
-    const JobSmem JS{S.pbar, S.red, S.flags, S.gs, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse, S.xs, reinterpret_cast<float*>(S.uni)};
+    const JobSmem JS{S.pbar, S.red, S.flags, S.gs, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse, S.xs,
+                     reinterpret_cast<float*>(S.uni)};
+    // Every vector a phase produces is published as tagged words; the tag is
+    // unique to (launch, layer, vector), so a consumer can tell this launch's
+    // words from any earlier ones.  P.sync[0] counts completed launches.
+    const uint32_t base = *reinterpret_cast<const volatile uint32_t*>(&P.sync[0]) << 10;
+    auto tag_of = [&](int l, int v) { return base + static_cast<uint32_t>(l * 8 + v + 1); };
+    const int pos = *P.attn[0].pos;  // this step's position (the same for every layer)
     const int njobs = 4 * P.nlayers + 1;
     Stream st;
     stream_start(st, S.full + warp * nb, S.ring + static_cast<size_t>(warp) * nb * kSlotBytes, nb, kSlotBytes, P.jobs,
                  njobs, lane);
     if (tid == 0) prefetch_gammas(P.jobs[0], kProEmbedNorm, JS);
     uint32_t pph = 0;  // gamma barrier phase
-    uint32_t nsync = 0;
     uint32_t aph = 0;  // attention barrier phases completed
     Greedy gr;
     gr.init();
@@ -205,78 +183,90 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
     stamp(0);
     bool ok = true;
     // One pass per projection: per layer QKV (then attention), O, gate/up,
-    // down.  A runtime loop over the phases, not an unrolled layer body, so
-    // each variant of a stage is compiled once: the per-layer code path then
-    // stays small enough to keep hot in the instruction cache.
+    // down.  No grid-wide barrier: each prologue polls the tagged words of
+    // its input, which the previous phase's CTAs publish as they finish.  A
+    // runtime loop over the phases keeps each stage variant compiled once (the
+    // per-layer code path stays small enough for the instruction cache).
 #pragma unroll 1
     for (int p = 0; p < 4 * P.nlayers && ok; ++p) {
         const int l = p >> 2, k = p & 3;  // k: 0 QKV, 1 O, 2 gate/up, 3 down
         const Job& j = P.jobs[p];
-        if (k == 1 || k == 3) {
-            job_prologue<kQ4K, kProPlain>(j, JS, 0u);
+        const int slot = 1 + 10 * l + 2 * k + (k ? 1 : 0);
+        if (k == 0 && l == 0) {
+            job_prologue<kQ4K, kProEmbedNorm>(j, JS, pph);  // the embedding row: no producer to wait for
+        } else if (k == 0 || k == 2) {
+            // residual update + attention / FFN RMSNorm over the previous down / O output
+            ok = ll_prologue_resid_norm<kQ4K>(j, JS, pph, k == 0 ? tag_of(l - 1, kVecDown) : tag_of(l, kVecO), P.abort);
         } else {
-            // residual update + attention / FFN RMSNorm (the embedding row at p = 0)
-            if (p == 0) job_prologue<kQ4K, kProEmbedNorm>(j, JS, pph);
-            else job_prologue<kQ4K, kProResidNorm>(j, JS, pph);
+            ok = ll_prologue_plain<kQ4K>(j, JS, k == 1 ? tag_of(l, kVecAttn) : tag_of(l, kVecH), P.abort);
+        }
+        if (k == 0 || k == 2) {
             pph ^= 1u;
             // the next norm prologue's weights: gate/up's, the next layer's QKV or the LM head's
             if (tid == 0) prefetch_gammas(P.jobs[p + 2], kProResidNorm, JS);
         }
-        if (k == 2) {
-            run_units<kQ4K, kEpiGeluPair>(j, st, JS, P, S.flags, gr);
-            cta_combine<kEpiGeluPair>(j, JS, gr);
-        } else {
-            run_units<kQ4K, kEpiPlain>(j, st, JS, P, S.flags, gr);
-            cta_combine<kEpiPlain>(j, JS, gr);
+        if (!ok) {
+            if (tid == 0) step_fail(P, kErrGridTimeout);
+            break;
         }
-        const int slot = 1 + 10 * l + (k == 0 ? 0 : 2 + 2 * k);
         stamp(slot);
-        if (k != 0) {
-            ok = grid_sync(P, nsync, S.flags);
-            stamp(slot + 1);
-            continue;
+        const uint32_t out_tag = tag_of(l, k == 0 ? kVecQkv : k == 1 ? kVecO : k == 2 ? kVecH : kVecDown);
+        if (k == 2) {
+            run_units<kQ4K, kEpiGeluPair>(j, st, JS, P, S.flags, gr, out_tag);
+            cta_combine<kEpiGeluPair>(j, JS, gr, out_tag);
+        } else {
+            run_units<kQ4K, kEpiPlain>(j, st, JS, P, S.flags, gr, out_tag);
+            cta_combine<kEpiPlain>(j, JS, gr, out_tag);
         }
-        // ---- attention: its first cached K/V tile is copied during the barrier ----
+        stamp(slot + 1);
+        __syncthreads();  // every warp is done with the projection's planes (and S.flags[0] is final)
+        if (S.flags[0]) {
+            ok = false;
+            if (tid == 0) atomicExch(P.abort, 1);
+            break;
+        }
+        if (k != 0) continue;
+        // ---- attention (item h, s of this CTA) over the QKV words as they arrive ----
         const AttnArgs& at = P.attn[l];
         const int items = at.nkv * at.nsplit;
         const int h = blockIdx.x / at.nsplit, s = blockIdx.x % at.nsplit;
-        const bool has_item = static_cast<int>(blockIdx.x) < items;
-        acore::AttnRange R{};
-        __syncthreads();  // every warp is done with the projection's planes
-        if (has_item) {
-            R = acore::attn_range(at, h, s, kAttnT);
+        if (static_cast<int>(blockIdx.x) < items) {
+            const acore::AttnRange R = acore::attn_range(at, h, s, kAttnT, pos);
             if (tid == 0) {
                 acore::attn_prefetch(at, R, AS, kAttnT);
                 S.flags[3] = R.active && R.ntiles > 0;
             }
-        }
-        ok = grid_sync(P, nsync, S.flags);
-        stamp(slot + 1);
-        if (ok && has_item) {
-            if (!acore::attn_run<G, kAttnT>(at, h, s, R, AS, aph & 1u)) {
-                if (tid == 0) atomicExch(&S.flags[0], 1);
-            }
+            __syncthreads();
+            const bool done = acore::attn_run<G, kAttnT>(at, h, s, R, AS, aph & 1u, tag_of(l, kVecQkv),
+                                                         tag_of(l, kVecAttn), P.abort, tag_of(l, kVecAttnPart));
             if (tid == 0) S.flags[3] = 0;
             if (R.active) aph += static_cast<uint32_t>(R.ntiles);
+            if (!done) {
+                ok = false;
+                if (tid == 0) step_fail(P, kErrGridTimeout);
+            }
         }
+        __syncthreads();  // the attention item's shared memory is dead before the O planes
         stamp(slot + 2);
-        if (ok) ok = grid_sync(P, nsync, S.flags);
-        stamp(slot + 3);
     }
     if (ok) {
-        // ---- LM head: residual update + final norm, BF16 GEMV, greedy argmax ----
+        // ---- LM head: residual update + final norm, BF16 GEMV, greedy token ----
         const Job& jl = P.jobs[4 * P.nlayers];
-        job_prologue<kBF16, kProResidNorm>(jl, JS, pph);
-        run_units<kBF16, kEpiArgmax>(jl, st, JS, P, S.flags, gr);
-        cta_combine<kEpiArgmax>(jl, JS, gr);
-        stamp(kStepTraceLen - 2);
-        __syncthreads();
-        if (S.flags[0]) {
-            ok = false;
-            if (tid == 0) atomicExch(P.abort, 1);
+        ok = ll_prologue_resid_norm<kBF16>(jl, JS, pph, tag_of(P.nlayers - 1, kVecDown), P.abort);
+        if (!ok) {
+            if (tid == 0) step_fail(P, kErrGridTimeout);
         } else {
-            argmax_finish(jl, JS, gr, false, nullptr);
-            stamp(kStepTraceLen - 1);
+            run_units<kBF16, kEpiArgmax>(jl, st, JS, P, S.flags, gr, 0u);
+            cta_combine<kEpiArgmax>(jl, JS, gr);
+            stamp(kStepTraceLen - 2);
+            __syncthreads();
+            if (S.flags[0]) {
+                ok = false;
+                if (tid == 0) atomicExch(P.abort, 1);
+            } else {
+                argmax_finish(jl, JS, gr, false, nullptr);
+                stamp(kStepTraceLen - 1);
+            }
         }
     }
     if (!ok) {
@@ -286,13 +276,14 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         __syncthreads();
         return;
     }
-    // The last CTA out returns the barrier counters to zero for the next launch.
+    // The last CTA out counts the launch (the next launch's tags) and returns
+    // the exit counter to zero.
     __syncthreads();
     if (tid == 0) {
         const uint32_t prev = atomicAdd(&P.sync[1], 1u);
         if (prev == gridDim.x - 1) {
-            P.sync[0] = 0u;
             P.sync[1] = 0u;
+            P.sync[0] = P.sync[0] + 1u;
         }
     }
 }

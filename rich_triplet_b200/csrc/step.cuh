@@ -29,17 +29,17 @@ struct StepParams {
     const gcore::Job* jobs;  // [4 * nlayers + 1]: per layer QKV, O, gate/up, down; then the LM head
     const AttnArgs* attn;    // [nlayers]
     int32_t nlayers;
-    uint32_t* sync;          // [2]: grid-barrier arrivals, CTA exits; zero between launches
+    uint32_t* sync;          // [0] launches completed (the tags' high bits), [1] CTA exits (zero between launches)
     int* abort;              // set when a CTA gives up; zero between launches
     gcore::SplitScratch scratch;
     int* err;                // error word (kErr*)
     uint64_t* trace;         // [kStepTraceLen] phase timeline of CTA 0 (globaltimer ns), may be null
 };
 
-// Timeline slots: layer l, event e (0 projection QKV done, 1 attention barrier,
-// 2 attention done, 3 barrier, 4 O done, 5 barrier, 6 gate/up done, 7 barrier,
-// 8 down done, 9 barrier) at 1 + 10 l + e; slot 0 = kernel start; the last
-// two slots: LM head projection done, argmax done.
+// Timeline slots: layer l, event e (0 QKV prologue done, 1 QKV done, 2
+// attention done, 3 O prologue done, 4 O done, 5 gate/up prologue done, 6
+// gate/up done, 7 down prologue done, 8 down done) at 1 + 10 l + e; slot 0 =
+// kernel start; the last two slots: LM head projection done, token done.
 constexpr int kStepTraceLen = 1024;
 
 StepGeom step_geometry(int hidden, int kp_max, int head_dim, int group);
