@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
-    (void)attn_run<G, kAttnTile>(a, h, s, R, S, 0u);
+    (void)attn_run<G, kAttnTile, false>(a, h, s, R, S, 0u);
 }
 
 template <int G>

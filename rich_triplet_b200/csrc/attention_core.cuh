@@ -64,8 +64,10 @@ __host__ __device__ inline size_t attn_carve(uint8_t* base, int D, int G, int T,
     uint8_t* sc = take(static_cast<size_t>(G) * T * 4, 16);
     uint8_t* kn = take(static_cast<size_t>(D) * 4, 16);
     uint8_t* vn = take(static_cast<size_t>(D) * 4, 16);
-    uint8_t* kt = take(static_cast<size_t>(T) * D * 4, 128);
-    uint8_t* vt = take(static_cast<size_t>(T) * D * 4, 128);
+    // K and V tiles, one region (after the tile loop it holds the warps'
+    // partial outputs while they are combined)
+    uint8_t* kt = take(2 * static_cast<size_t>(T) * D * 4, 128);
+    uint8_t* vt = kt + static_cast<size_t>(T) * D * 4;
     if (S) {
         S->bar = reinterpret_cast<uint64_t*>(bar);
         S->red = reinterpret_cast<float*>(red);
@@ -86,13 +88,14 @@ __host__ __device__ inline size_t attn_carve(uint8_t* base, int D, int G, int T,
 // One warp: dst[D] = rope(rmsnorm(raw) * (1 + gamma)) -- the per-head norm
 // (rms_norm_gemma3 per head, src/transformer4.rs:2485-2510) and the NeoX
 // rotation of pairs (j, j + D/2) (src/transformer4.rs:2742-2772).
-// With `tag` != 0 the row is read from tagged words at raw_ll (polled until
-// every word carries the tag); false if that wait gave up.
+// LL: the row is read from tagged words at raw_ll (polled until every word
+// carries `tag`); false if that wait gave up.  Otherwise from raw.
+template <bool LL>
 __device__ __forceinline__ bool head_load_warp(const float* raw, const uint64_t* raw_ll, uint32_t tag, int D,
                                                const int* abort, float (&x)[kMaxHeadDim / 32]) {
     constexpr int kMaxPer = kMaxHeadDim / 32;
     const int lane = threadIdx.x & 31;
-    if (!tag) {
+    if constexpr (!LL) {
 #pragma unroll
         for (int i = 0; i < kMaxPer; ++i) {  // every load of the row in flight at once
             const int j = lane + 32 * i;
@@ -116,6 +119,7 @@ __device__ __forceinline__ bool head_load_warp(const float* raw, const uint64_t*
     }
 }
 
+template <bool LL>
 __device__ __forceinline__ bool head_prep_warp(const float* raw, const uint64_t* raw_ll, uint32_t tag,
                                                const float* gamma, const float* cs, const float* sn, int D, float eps,
                                                float* dst, const int* abort) {
@@ -123,7 +127,7 @@ __device__ __forceinline__ bool head_prep_warp(const float* raw, const uint64_t*
     const int lane = threadIdx.x & 31, half = D / 2;
     float x[kMaxPer];
     float ss = 0.f;
-    if (!head_load_warp(raw, raw_ll, tag, D, abort, x)) return false;
+    if (!head_load_warp<LL>(raw, raw_ll, tag, D, abort, x)) return false;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
         const int j = lane + 32 * i;
@@ -133,6 +137,7 @@ __device__ __forceinline__ bool head_prep_warp(const float* raw, const uint64_t*
     ss = warp_sum(ss);
     __syncwarp();  // the row is in dst for the pairs other lanes own
     const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(D)) + eps);
+    #pragma unroll 1
     for (int j = lane; j < half; j += 32) {
         const float x0 = __fmul_rn(__fmul_rn(dst[j], r), __fadd_rn(1.0f, gamma[j]));
         const float x1 = __fmul_rn(__fmul_rn(dst[j + half], r), __fadd_rn(1.0f, gamma[j + half]));
@@ -147,12 +152,14 @@ template <int G, int T>
 __device__ __forceinline__ void attend_tile(const AttnSmem& S, const float* K, const float* V, int nt, int D,
                                             float scale, float (&acc)[G]) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    #pragma unroll 1
     for (int j = warp; j < nt; j += nw) {
         const float* kr = K + static_cast<size_t>(j) * D;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             const float* q = S.qv + g * D;
             float dot = 0.f;
+            #pragma unroll 1
             for (int d = lane; d < D; d += 32) dot += q[d] * kr[d];
             dot = warp_sum(dot);
             if (lane == 0) S.sc[g * T + j] = dot * scale;
@@ -185,6 +192,7 @@ __device__ __forceinline__ void attend_tile(const AttnSmem& S, const float* K, c
         for (int g = 0; g < G; ++g) {
             float v = acc[g] * S.corr[g];
             const float* p = S.sc + g * T;
+            #pragma unroll 2
             for (int j = 0; j < nt; ++j) v += p[j] * V[static_cast<size_t>(j) * D + tid];
             acc[g] = v;
         }
@@ -299,6 +307,7 @@ __device__ __forceinline__ void attn_merge(const AttnArgs& a, int h, int nsplit,
             M = bm;
         }
         // Butterfly over the kg lanes of column c (aligned groups of a warp).
+        #pragma unroll 1
         for (int o = 1; o < kg; o <<= 1) {
             const float oM = __shfl_xor_sync(0xffffffffu, M, o);
             const float oden = __shfl_xor_sync(0xffffffffu, den, o);
@@ -345,6 +354,7 @@ __device__ __forceinline__ bool attn_merge_slice_ll(const AttnArgs& a, int h, in
     const int q0 = s * Q / ns, q1 = (s + 1) * Q / ns;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     bool ok = true;
+    #pragma unroll 1
     for (int qd = q0 + warp; qd < q1 && ok; qd += nw) {
         const int g = 4 * qd / D, d = 4 * qd - g * D;
         const uint64_t* base = a.part_ll + (static_cast<size_t>(h) * a.nsplit * G + g) * stride;
@@ -390,7 +400,7 @@ __device__ __forceinline__ bool attn_merge_slice_ll(const AttnArgs& a, int h, in
             num.w = num.w * sa + ll_val(w[i][1].y) * sb;
             M = nm;
         }
-#pragma unroll
+        #pragma unroll 1
         for (int o = 1; o < 32; o <<= 1) {
             const float oM = __shfl_xor_sync(0xffffffffu, M, o);
             const float oden = __shfl_xor_sync(0xffffffffu, den, o);
@@ -433,16 +443,16 @@ __device__ __forceinline__ void attn_prefetch(const AttnArgs& a, const AttnRange
     if (R.active && R.ntiles > 0) attn_issue(a, R, S, 0, T);
 }
 
-// The item itself (all threads).  q/k/v of this step come from a.qkv, or with
-// in_tag != 0 from the tagged words a.qkv_ll (polled); the merged output goes
-// to a.out, or with out_tag != 0 to a.out_ll as tagged words.  With part_tag
-// != 0 the item publishes its partial as tagged words (a.part_ll) and then
-// merges its slice of the head's outputs (attn_merge_slice_ll); otherwise the
-// last item of the head to finish (atomic counter) merges them all.  `ph0`: parity
-// of the tile barrier's next phase (phases it completed before, mod 2); the
-// item completes R.ntiles phases.  Returns false if a bounded wait gave up
-// (after waiting, bounded, for the copy in flight); `a.err` is then set.
-template <int G, int T>
+// The item itself (all threads).  LL (decode-step kernel): q/k/v of this step
+// come from the tagged words a.qkv_ll (polled until they carry in_tag), the
+// item publishes its partial as tagged words (a.part_ll, part_tag) and then
+// merges its slice of the head's outputs (attn_merge_slice_ll) into a.out_ll
+// (out_tag).  Otherwise q/k/v come from a.qkv and the last item of the head to
+// finish (atomic counter) merges every split into a.out.  `ph0`: parity of the
+// tile barrier's next phase (phases it completed before, mod 2); the item
+// completes R.ntiles phases.  Returns false if a bounded wait gave up (after
+// waiting, bounded, for the copy in flight); `a.err` is then set.
+template <int G, int T, bool LL>
 __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const AttnRange& R, const AttnSmem& S,
                                          uint32_t ph0, uint32_t in_tag = 0, uint32_t out_tag = 0,
                                          const int* abort = nullptr, uint32_t part_tag = 0) {
@@ -456,16 +466,16 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
     const float* sn = a.rope_sin + static_cast<size_t>(R.pos) * (D / 2);
     const int warp = tid >> 5;
     bool got = true;
-    if (warp < G) {
-        const size_t o = static_cast<size_t>(h * G + warp) * D;
-        got = head_prep_warp(a.qkv + o, a.qkv_ll + o, in_tag, a.q_norm, cs, sn, D, a.eps, S.qv + warp * D, abort);
-    } else if (warp == G && R.has_new) {
-        const size_t o = static_cast<size_t>(a.nq + h) * D;
-        got = head_prep_warp(a.qkv + o, a.qkv_ll + o, in_tag, a.k_norm, cs, sn, D, a.eps, S.knew, abort);
+    if (warp < G || (warp == G && R.has_new)) {
+        // one call site for the query heads and the new K row (smaller code)
+        const bool qh = warp < G;
+        const size_t o = static_cast<size_t>(qh ? h * G + warp : a.nq + h) * D;
+        got = head_prep_warp<LL>(a.qkv + o, a.qkv_ll + o, in_tag, qh ? a.q_norm : a.k_norm, cs, sn, D, a.eps,
+                                 qh ? S.qv + warp * D : S.knew, abort);
     } else if (warp == G + 1 && R.has_new) {
         const size_t o = static_cast<size_t>(a.nq + a.nkv + h) * D;
         float v[kMaxHeadDim / 32];
-        got = head_load_warp(a.qkv + o, a.qkv_ll + o, in_tag, D, abort, v);
+        got = head_load_warp<LL>(a.qkv + o, a.qkv_ll + o, in_tag, D, abort, v);
 #pragma unroll
         for (int i = 0; i < kMaxHeadDim / 32; ++i) {
             const int d = (tid & 31) + 32 * i;
@@ -489,90 +499,194 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
     if (R.has_new) {
         float* kdst = a.kcache + (R.head_base + R.pos) * D;
         float* vdst = a.vcache + (R.head_base + R.pos) * D;
+        #pragma unroll 1
         for (int d = tid; d < D; d += blockDim.x) {
             kdst[d] = S.knew[d];
             vdst[d] = S.vnew[d];
         }
     }
 
-    // Cached tiles (copied into S.kt / S.vt); the new row joins the last of
-    // them when it has room, else it is a tile of its own.
-    float acc[G];
+    // Per-warp online softmax.  Lane l owns the float4 columns c = l + 32 f
+    // (dims 4c..4c+3) of every row, so each warp-wide float4 load of a row
+    // reads 512 contiguous bytes; warp w takes positions w, w + nw, ... of each
+    // tile, and one warp the new row.  Every warp keeps its own running max,
+    // sum and output per query head, with no block-wide step per position; the
+    // warps' states are combined once at the end.
+    constexpr int kNF = kMaxHeadDim / 128;
+    const int lane = tid & 31, nw = static_cast<int>(blockDim.x >> 5);
+    const int nc4 = D / 4;
+    float4 q4[G][kNF];
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0.f;
-    const int last_nt = R.ntiles > 0 ? R.ncached - (R.ntiles - 1) * T : 0;
-    const bool fold_new = R.has_new && R.ntiles > 0 && last_nt < T;
-    const int nsteps = R.ntiles + (R.has_new && !fold_new ? 1 : 0);
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int f = 0; f < kNF; ++f) {
+            const int c = lane + 32 * f;
+            q4[g][f] = c < nc4 ? reinterpret_cast<const float4*>(S.qv + g * D)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    float m[G], l[G];
+    float4 acc[G][kNF];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int f = 0; f < kNF; ++f) acc[g][f] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // One position: scores q . k * scale, then the online update with v.
+    auto visit = [&](const float* kr, const float* vr) {
+        float4 k4[kNF], v4[kNF];
+#pragma unroll
+        for (int f = 0; f < kNF; ++f) {
+            const int c = lane + 32 * f;
+            k4[f] = c < nc4 ? reinterpret_cast<const float4*>(kr)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            v4[f] = c < nc4 ? reinterpret_cast<const float4*>(vr)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float sc[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float d = 0.f;
+#pragma unroll
+            for (int f = 0; f < kNF; ++f)
+                d += q4[g][f].x * k4[f].x + q4[g][f].y * k4[f].y + q4[g][f].z * k4[f].z + q4[g][f].w * k4[f].w;
+            sc[g] = d;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float x = sc[g] * a.scale;
+            const float mn = fmaxf(m[g], x);
+            const float cr = expf(m[g] - mn);  // 0 for the first position (m = -inf)
+            const float p = expf(x - mn);
+            l[g] = l[g] * cr + p;
+#pragma unroll
+            for (int f = 0; f < kNF; ++f) {
+                acc[g][f].x = acc[g][f].x * cr + p * v4[f].x;
+                acc[g][f].y = acc[g][f].y * cr + p * v4[f].y;
+                acc[g][f].z = acc[g][f].z * cr + p * v4[f].z;
+                acc[g][f].w = acc[g][f].w * cr + p * v4[f].w;
+            }
+            m[g] = mn;
+        }
+    };
 #pragma unroll 1
-    for (int t = 0; t < nsteps; ++t) {
-        const bool cached = t < R.ntiles;
-        if (cached) {
-            const bool ok = mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
-            if (__syncthreads_or(!ok)) {
-                if (tid == 0) {
-                    if (a.err) atomicExch(a.err, kErrMbarTimeout);
-                    // the one outstanding copy must land (bounded) before shared memory is reused
-                    (void)mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
-                }
-                __syncthreads();
-                return false;
+    for (int t = 0; t < R.ntiles; ++t) {
+        const bool ok = mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                if (a.err) atomicExch(a.err, kErrMbarTimeout);
+                // the one outstanding copy must land (bounded) before shared memory is reused
+                (void)mbar_wait(S.bar, (ph0 + static_cast<uint32_t>(t)) & 1u);
             }
-        }
-        int nt = cached ? min(T, R.ncached - t * T) : 1;
-        if (fold_new && t == R.ntiles - 1) {
-            for (int d = tid; d < D; d += blockDim.x) {
-                S.kt[static_cast<size_t>(nt) * D + d] = S.knew[d];
-                S.vt[static_cast<size_t>(nt) * D + d] = S.vnew[d];
-            }
-            ++nt;
             __syncthreads();
+            return false;
         }
-        attend_tile<G, T>(S, cached ? S.kt : S.knew, cached ? S.vt : S.vnew, nt, D, a.scale, acc);
+        const int nt = min(T, R.ncached - t * T);
+#pragma unroll 1
+        for (int j = warp; j < nt; j += nw) visit(S.kt + static_cast<size_t>(j) * D, S.vt + static_cast<size_t>(j) * D);
+        __syncthreads();  // every warp is done with the tile before the next copy overwrites it
         if (tid == 0 && t + 1 < R.ntiles) {
             fence_proxy_async_smem();
             attn_issue(a, R, S, t + 1, T);
         }
     }
+    if (R.has_new && warp == R.ncached % nw) visit(S.knew, S.vnew);
 
-    // Per-split partial state.
-    const int stride = attn_part_stride(D);
-    if (part_tag) {
+    // Combine the warps' states.  Per query head g: M = max_w m_w, weight
+    // e_w = exp(m_w - M), l = sum_w e_w l_w, output = sum_w e_w acc_w (the
+    // item's partial: unnormalised output, M, l).  S.qv (q is in registers now)
+    // holds the warps' m and l, S.sc the weights; the K/V tile region holds
+    // the warps' outputs, gpp query heads per pass.
+    float* wm = S.qv;
+    float* wl = S.qv + nw * G;
+    if (lane == 0) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            uint64_t* pp = a.part_ll + (static_cast<size_t>(h * a.nsplit + s) * G + g) * stride;
-            if (tid < D) ll_store(pp + tid, acc[g], part_tag);
-            if (tid == 0) ll_store2(pp + D, S.m_run[g], S.l_run[g], part_tag);
+            wm[warp * G + g] = m[g];
+            wl[warp * G + g] = l[g];
         }
-        return attn_merge_slice_ll<G>(a, h, s, R.nsplit, part_tag, out_tag, abort);
     }
+    __syncthreads();
+    if (warp < G) {
+        const float mv = lane < nw ? wm[lane * G + warp] : -INFINITY;
+        const float M = warp_max(mv);
+        const float e = lane < nw && mv != -INFINITY ? expf(mv - M) : 0.f;
+        const float den = warp_sum(lane < nw ? e * wl[lane * G + warp] : 0.f);
+        if (lane < nw) S.sc[lane * G + warp] = e;
+        if (lane == 0) {
+            S.m_run[warp] = M;
+            S.l_run[warp] = den;
+        }
+    }
+    const int stride = attn_part_stride(D);
+    const int gpp = max(1, 2 * T / nw);  // query heads per pass: nw * gpp * D floats fit the tile region
+    float4* wacc = reinterpret_cast<float4*>(S.kt);
+#pragma unroll 1
+    for (int g0 = 0; g0 < G; g0 += gpp) {
+        __syncthreads();  // the region's previous users (tile loop, previous pass) are done
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        float* pp = a.part + (static_cast<size_t>(h * a.nsplit + s) * G + g) * stride;
-        if (tid < D) pp[tid] = acc[g];
-        if (tid == 0) {
-            pp[D] = S.m_run[g];
-            pp[D + 1] = S.l_run[g];
+        for (int g = 0; g < G; ++g) {
+            if (g < g0 || g >= g0 + gpp) continue;
+#pragma unroll
+            for (int f = 0; f < kNF; ++f) {
+                const int c = lane + 32 * f;
+                if (c < nc4) wacc[(warp * gpp + (g - g0)) * nc4 + c] = acc[g][f];
+            }
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int k = tid; k < gpp * nc4; k += blockDim.x) {
+            const int gg = k / nc4, c = k - gg * nc4, g = g0 + gg;
+            if (g >= G) continue;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+            for (int w = 0; w < nw; ++w) {
+                const float e = S.sc[w * G + g];
+                const float4 v = wacc[(w * gpp + gg) * nc4 + c];
+                o.x += e * v.x;
+                o.y += e * v.y;
+                o.z += e * v.z;
+                o.w += e * v.w;
+            }
+            const size_t row = (static_cast<size_t>(h * a.nsplit + s) * G + g) * stride;
+            if constexpr (LL) {
+                ll_store2(a.part_ll + row + 4 * c, o.x, o.y, part_tag);
+                ll_store2(a.part_ll + row + 4 * c + 2, o.z, o.w, part_tag);
+                if (c == 0) ll_store2(a.part_ll + row + D, S.m_run[g], S.l_run[g], part_tag);
+            } else {
+                *reinterpret_cast<float4*>(a.part + row + 4 * c) = o;
+                if (c == 0) {
+                    a.part[row + D] = S.m_run[g];
+                    a.part[row + D + 1] = S.l_run[g];
+                }
+            }
         }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(&a.counter[h], 1u);
-        S.flag[0] = prev == static_cast<uint32_t>(R.nsplit - 1);
-    }
-    __syncthreads();
-    if (!S.flag[0]) return true;
-    __threadfence();
-    // The counter is reset before the merged output is published: a later
-    // layer's items of this head (which can only start after consumers saw the
-    // output) must find it at zero.
-    if (tid == 0) {
-        a.counter[h] = 0u;
+    if constexpr (LL) {
+        return attn_merge_slice_ll<G>(a, h, s, R.nsplit, part_tag, out_tag, abort);
+    } else {
         __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t prev = atomicAdd(&a.counter[h], 1u);
+            S.flag[0] = prev == static_cast<uint32_t>(R.nsplit - 1);
+        }
+        __syncthreads();
+        if (!S.flag[0]) return true;
+        __threadfence();
+        // The counter is reset before the merged output is published: a later
+        // layer's items of this head (which can only start after consumers saw the
+        // output) must find it at zero.
+        if (tid == 0) {
+            a.counter[h] = 0u;
+            __threadfence();
+        }
+        __syncthreads();
+        attn_merge<G>(a, h, R.nsplit, out_tag);
+        return true;
     }
-    __syncthreads();
-    attn_merge<G>(a, h, R.nsplit, out_tag);
-    return true;
 }
 
 }  // namespace acore

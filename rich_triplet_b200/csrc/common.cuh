@@ -201,22 +201,23 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     __syncthreads();
     if (lane == 0) red[warp] = v;
     __syncthreads();
-    float t = red[0];
-    for (int i = 1; i < nw; ++i) t = fmaxf(t, red[i]);
-    return t;
+    return warp_max(lane < nw ? red[lane] : -INFINITY);
 }
 
 // Sum over the whole block; every thread gets the result.  `red` must hold
-// 32 floats of shared memory; blockDim.x is a multiple of 32.
+// 32 floats of shared memory; blockDim.x is a multiple of 32.  The per-warp
+// sums are added by an xor butterfly in every warp: a fixed order (so the
+// result is deterministic) in which each addition pairs the same two values
+// on every lane, so every thread of the block, and every CTA that reduces the
+// same values, gets the same bits.  Five shuffles instead of a chain of 16
+// dependent shared-memory loads.
 __device__ __forceinline__ float block_sum(float v, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     v = warp_sum(v);
     __syncthreads();
     if (lane == 0) red[warp] = v;
     __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t += red[i];  // fixed order: deterministic
-    return t;
+    return warp_sum(lane < nw ? red[lane] : 0.f);
 }
 
 // ---- Tagged words ("LL" words, after NCCL's low-latency protocol) ----------

@@ -257,7 +257,7 @@ int build_step(rt_dec* d) {
     const int H = d->H, D = d->D, NL = d->NL;
     const int G = d->NQ / d->NKV;
     const int kp_max = std::max({H, d->NQ * D, d->F});
-    d->step_geom = rt::step_geometry(H, kp_max, D, G);
+    d->step_geom = rt::step_geometry(H, kp_max, D, G, 4 * NL + 1);
     if (!d->step_geom.warps) return RT_OK;  // shapes outside the step kernel: keep the graph
     if (rt::step_prepare(d->step_geom) != cudaSuccess) {
         cudaGetLastError();

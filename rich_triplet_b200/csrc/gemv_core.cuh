@@ -122,12 +122,15 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// round(y) clamped to [-127, 127], as a float; *bits gets the integer in its
-// low byte (two's complement), from the same magic-number sum.
+// round(y) for |y| <= 127.5, as a float; *bits gets the integer in its low
+// byte (two's complement), from the same magic-number sum.  The quantiser
+// below only passes values within that range (|x / s| <= 127 up to a few
+// ulps, and each residual is at most half a step of the plane above), so no
+// clamp is needed.
 __device__ __forceinline__ float round_clamp127(float y, uint32_t* bits) {
-    const float f = fminf(fmaxf(__fsub_rn(__fadd_rn(y, 12582912.0f), 12582912.0f), -127.0f), 127.0f);
-    *bits = __float_as_uint(__fadd_rn(f, 12582912.0f));
-    return f;
+    const float t = __fadd_rn(y, 12582912.0f);
+    *bits = __float_as_uint(t);
+    return __fsub_rn(t, 12582912.0f);
 }
 
 // Bytes 0 of a, b, c, d -> one word (a lowest).
@@ -166,8 +169,8 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
     // x = s (p0 + p1/254 + p2/254^2): each residual spans the full int8 range,
     // |error| <= s / (2 * 254^2).  Each residual is taken against the stored
     // scale s, so the reciprocal only has to be close (|x inv| stays below
-    // 127.5); the clamps only guard the rounding edge.  Sub-blocks whose
-    // largest magnitude is below 1e-30 quantise to zero.
+    // 127.5).  Sub-blocks whose largest magnitude is below 1e-30 quantise to
+    // zero.
     const float s = m * (1.0f / 127.0f);
     const float inv = m > 1e-30f ? __fdividef(127.0f, m) : 0.f;
     const float s254 = s * (1.0f / 254.0f);
@@ -438,6 +441,32 @@ struct SplitScratch {
     uint32_t* tile_cnt;  // [tiles of the largest job], zero between jobs
 };
 
+// What a stream needs of one job, kept in shared memory by the decode-step
+// kernel: the weight pointers, the kind and column segments, and this CTA's
+// units [u0, u1) of a tile-split job (the warps share them equally, as
+// warp_share does).
+struct JobLite {
+    const uint8_t* wt;
+    const void* tmap;
+    uint32_t u0, u1;
+    int32_t nseg;
+    int32_t kind;
+};
+
+// This CTA's JobLite of job j (tile-split jobs; called by one thread per job).
+__device__ __forceinline__ JobLite job_lite(const Job& j, uint32_t cta, uint32_t ncta) {
+    JobLite L;
+    L.wt = j.wt;
+    L.tmap = j.tmap;
+    L.nseg = j.nseg;
+    L.kind = j.kind;
+    Split ct;
+    ct.init(static_cast<uint32_t>((j.rows + kTile - 1) / kTile), ncta);
+    L.u0 = ct.start(cta) * static_cast<uint32_t>(j.nseg);
+    L.u1 = ct.start(cta + 1) * static_cast<uint32_t>(j.nseg);
+    return L;
+}
+
 // Per-warp weight stream over a list of jobs.  All lanes hold the same
 // consumer state; the issue cursor is advanced by lane 0 only.
 struct Stream {
@@ -449,6 +478,7 @@ struct Stream {
     uint32_t ph;         // its phase parity
     uint64_t pol;
     const Job* jobs;
+    const JobLite* jt;   // shared-memory table of the jobs (tile-split jobs only), or null
     int njobs;
     uint32_t cta, ncta, warp, nw;  // this warp's place in the grid
     // issue cursor
@@ -459,14 +489,48 @@ struct Stream {
     int islot;           // slot the next copy goes to
     int issued;          // copies issued, all jobs
     int consumed;        // copies consumed, all jobs
+    // Job ij's fields the copies need, loaded once by seek() (the Job table is
+    // in global memory; reading it per copy would put its latency on the path
+    // of every copy).
+    const uint8_t* iwt;
+    const void* itmap;
+    int ikind;
+    int inseg;
     // Move the cursor to the next job in which this warp has units.
     __device__ __forceinline__ void seek(int j) {
+        if (jt) {
+            // From the shared-memory table: no global read, no division.
+#pragma unroll 1
+            for (ij = j; ij < njobs; ++ij) {
+                const JobLite L = jt[ij];
+                const uint32_t n = L.u1 - L.u0;
+                iu = L.u0 + n * warp / nw;
+                iend = L.u0 + n * (warp + 1) / nw;
+                if (iu < iend) {
+                    inseg = L.nseg;
+                    ikind = L.kind;
+                    iwt = L.wt;
+                    itmap = L.tmap;
+                    const uint32_t ns = static_cast<uint32_t>(inseg);
+                    itile = iu / ns;
+                    iseg = static_cast<int>(iu - itile * ns);
+                    return;
+                }
+            }
+            return;
+        }
+#pragma unroll 1
         for (ij = j; ij < njobs; ++ij) {
-            const Share sh = warp_share(jobs[ij], cta, ncta, warp, nw);
+            const Job& jo = jobs[ij];
+            const Share sh = warp_share(jo, cta, ncta, warp, nw);
             iu = sh.s;
             iend = sh.e;
             if (iu < iend) {
-                const uint32_t ns = static_cast<uint32_t>(jobs[ij].nseg);
+                inseg = jo.nseg;
+                ikind = jo.kind;
+                iwt = jo.wt;
+                itmap = jo.tmap;
+                const uint32_t ns = static_cast<uint32_t>(inseg);
                 itile = iu / ns;
                 iseg = static_cast<int>(iu - itile * ns);
                 return;
@@ -477,27 +541,25 @@ struct Stream {
     // consecutive units of a tile-major W) into slot `islot`, if any is left.
     __device__ __forceinline__ bool issue() {
         if (ij >= njobs) return false;
-        const Job& jo = jobs[ij];
-        const int kind = jo.kind;
         uint64_t* bar = &full[islot];
         uint8_t* dst = ring + static_cast<size_t>(islot) * slot_bytes;
         int k = 1;
-        if (jo.wt) {
+        if (iwt) {
             k = min(static_cast<uint32_t>(kTileMajorUnitsPerCopy), iend - iu);
             const uint32_t bytes = static_cast<uint32_t>(k) * kQ4KUnit;
             mbar_arrive_expect_tx(bar, bytes);
-            bulk_g2s(dst, jo.wt + static_cast<size_t>(iu) * kQ4KUnit, bytes, bar, pol);
+            bulk_g2s(dst, iwt + static_cast<size_t>(iu) * kQ4KUnit, bytes, bar, pol);
         } else {
-            mbar_arrive_expect_tx(bar, static_cast<uint32_t>(unit_bytes(kind)));
-            tma_2d_g2s(dst, jo.tmap, iseg * box_step(kind), static_cast<int>(itile * kTile), bar, pol);
+            mbar_arrive_expect_tx(bar, static_cast<uint32_t>(unit_bytes(ikind)));
+            tma_2d_g2s(dst, itmap, iseg * box_step(ikind), static_cast<int>(itile * kTile), bar, pol);
         }
         if (++islot == nb) islot = 0;
         ++issued;
-        for (int u = 0; u < k; ++u)
-            if (++iseg == jo.nseg) {
-                iseg = 0;
-                ++itile;
-            }
+        iseg += k;
+        while (iseg >= inseg) {
+            iseg -= inseg;
+            ++itile;
+        }
         iu += static_cast<uint32_t>(k);
         if (iu == iend) seek(ij + 1);
         return true;
@@ -508,7 +570,8 @@ struct Stream {
 // issues the first copies.  The caller makes the barrier init visible
 // (__syncthreads or __syncwarp) before any other lane waits on them.
 __device__ __forceinline__ void stream_start(Stream& s, uint64_t* full, uint8_t* ring, int nb, int slot_bytes,
-                                             const Job* jobs, int njobs, int lane) {
+                                             const Job* jobs, int njobs, int lane, const JobLite* jt = nullptr) {
+    s.jt = jt;
     s.full = full;
     s.ring = ring;
     s.nb = nb;
@@ -735,23 +798,38 @@ __device__ __forceinline__ bool ll_prologue_plain(const Job& a, const JobSmem& S
     const int pstride = q4k_pstride(Kp);
     const int nseg = Kp / kQ4KSegCols;
     bool ok = true;
+    const uint64_t* in_ll = a.in_ll;
+#pragma unroll 1
     for (int s0 = warp; s0 < nseg && ok; s0 += kLLSegs * nw) {
         ulonglong2 w[kLLSegs][4];
+        // Words still to (re)load: a poll round reloads only the words that
+        // did not carry the tag yet.
+        uint32_t need = 0;
+#pragma unroll
+        for (int b = 0; b < kLLSegs; ++b) {
+            const int seg = s0 + b * nw, c0 = seg * kQ4KSegCols + lane * 8;
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                w[b][h] = make_ulonglong2(ll_word(0.f, tag), ll_word(0.f, tag));
+                if (seg < nseg && c0 + 2 * h < K) need |= 1u << (b * 4 + h);
+            }
+        }
         LLPoll pl;
         pl.init(abort);
         for (;;) {
-            bool ready = true;
 #pragma unroll
             for (int b = 0; b < kLLSegs; ++b) {
-                const int seg = s0 + b * nw, c0 = seg * kQ4KSegCols + lane * 8;
+                const int c0 = (s0 + b * nw) * kQ4KSegCols + lane * 8;
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    w[b][h] = seg < nseg && c0 + 2 * h < K ? ll_load2(a.in_ll + c0 + 2 * h)
-                                                           : make_ulonglong2(ll_word(0.f, tag), ll_word(0.f, tag));
-                    ready &= ll_has(w[b][h].x, tag) && ll_has(w[b][h].y, tag);
-                }
+                for (int h = 0; h < 4; ++h)
+                    if (need & (1u << (b * 4 + h))) w[b][h] = ll_load2(in_ll + c0 + 2 * h);
             }
-            if (__all_sync(0xffffffffu, ready)) break;
+#pragma unroll
+            for (int b = 0; b < kLLSegs; ++b)
+#pragma unroll
+                for (int h = 0; h < 4; ++h)
+                    if (ll_has(w[b][h].x, tag) && ll_has(w[b][h].y, tag)) need &= ~(1u << (b * 4 + h));
+            if (__all_sync(0xffffffffu, need == 0)) break;
             if (!pl.again()) {
                 ok = false;
                 break;
@@ -792,24 +870,39 @@ __device__ __forceinline__ bool ll_prologue_resid_norm(const Job& a, const JobSm
     bool ok = true;
     float ss = 0.f;
     const int npairs = K / 2;
+    const uint64_t* in_ll = a.in_ll;
+#pragma unroll 1
     for (int pb = tid; pb < npairs && ok; pb += kLLPairs * nthr) {
         ulonglong2 w[kLLPairs][kMaxSrcParts];
+        // Words still to (re)load: a poll round reloads only the words that
+        // did not carry the tag yet.
+        uint32_t need = 0;
+#pragma unroll
+        for (int i = 0; i < kLLPairs; ++i) {
+            const int c = 2 * (pb + i * nthr);
+#pragma unroll
+            for (int q = 0; q < kMaxSrcParts; ++q) {
+                w[i][q] = make_ulonglong2(ll_word(0.f, tag), ll_word(0.f, tag));
+                if (c < K && q < parts) need |= 1u << (i * kMaxSrcParts + q);
+            }
+        }
         LLPoll pl;
         pl.init(abort);
         for (;;) {
-            bool ready = true;
 #pragma unroll
             for (int i = 0; i < kLLPairs; ++i) {
                 const int c = 2 * (pb + i * nthr);
 #pragma unroll
-                for (int q = 0; q < kMaxSrcParts; ++q) {
-                    const bool use = c < K && q < parts;
-                    w[i][q] = use ? ll_load2(a.in_ll + static_cast<size_t>(q) * K + c)
-                                  : make_ulonglong2(ll_word(0.f, tag), ll_word(0.f, tag));
-                    ready &= ll_has(w[i][q].x, tag) && ll_has(w[i][q].y, tag);
-                }
+                for (int q = 0; q < kMaxSrcParts; ++q)
+                    if (need & (1u << (i * kMaxSrcParts + q)))
+                        w[i][q] = ll_load2(in_ll + static_cast<size_t>(q) * K + c);
             }
-            if (ready) break;
+#pragma unroll
+            for (int i = 0; i < kLLPairs; ++i)
+#pragma unroll
+                for (int q = 0; q < kMaxSrcParts; ++q)
+                    if (ll_has(w[i][q].x, tag) && ll_has(w[i][q].y, tag)) need &= ~(1u << (i * kMaxSrcParts + q));
+            if (need == 0) break;
             if (!pl.again()) {
                 ok = false;
                 break;
@@ -935,7 +1028,16 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
                                               Greedy& gr, uint32_t out_tag = 0) {
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
+    // The job's fields, read once: the Job table is in global memory, and every
+    // asm statement with a memory clobber below would otherwise make the
+    // compiler read them again.
     const int nseg = a.nseg;
+    const int64_t rows = a.rows;
+    const int kparts = a.kparts, ptiles = a.ptiles;
+    const uint32_t wait_iters = a.wait_iters;
+    uint64_t* const out_ll = a.out_ll;
+    float* const yv = a.y;
+    const bool tile_major = a.wt != nullptr;
     const int Kp = (a.K + seg_cols(KIND) - 1) / seg_cols(KIND) * seg_cols(KIND);
     const int pstride = KIND == kQ4K ? q4k_pstride(Kp) : bf16_pstride(Kp);
     const Share sh = warp_share(a, st.cta, st.ncta, st.warp, st.nw);
@@ -948,15 +1050,15 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
         const int64_t r = r0 + lane;
         if constexpr (EPI == kEpiGeluPair) {
             const float up = __shfl_down_sync(0xffffffffu, v, 1);
-            if (lane < kTile && !(lane & 1) && r < a.rows) {
+            if (lane < kTile && !(lane & 1) && r < rows) {
                 const float h = __fmul_rn(gelu_tanh_dev(v), up);
-                if (out_tag) ll_store(a.out_ll + (r >> 1), h, out_tag);
-                else a.y[r >> 1] = h;
+                if (out_tag) ll_store(out_ll + (r >> 1), h, out_tag);
+                else yv[r >> 1] = h;
             }
         } else {
-            if (lane < kTile && r < a.rows) {
-                if (out_tag) ll_store(a.out_ll + r, v, out_tag);
-                else a.y[r] = v;
+            if (lane < kTile && r < rows) {
+                if (out_tag) ll_store(out_ll + r, v, out_tag);
+                else yv[r] = v;
                 if constexpr (EPI == kEpiArgmax) gr.add(v, r);
             }
         }
@@ -973,15 +1075,15 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
     int seg = static_cast<int>(u_begin - tile * nseg);
     const uint32_t first_tile = tile;
     // first segment of x for the current tile (column-split jobs)
-    auto part_base = [&](uint32_t tl) { return a.kparts > 1 ? static_cast<int>(tl / a.ptiles) * nseg : 0; };
+    auto part_base = [&](uint32_t tl) { return kparts > 1 ? static_cast<int>(tl / ptiles) * nseg : 0; };
     int xseg = part_base(tile) + seg;
     int pu = 0;  // units of the current tile piece
-    const int upc = a.wt ? kTileMajorUnitsPerCopy : 1;
+    const int upc = tile_major ? kTileMajorUnitsPerCopy : 1;
     int in_copy = 0, uic = 0;  // units left in / consumed from the current copy
     float cv0 = 0.f, cv1 = 0.f;  // Q4_K: this lane's values of the current copy's units
     for (int i = 0; i < n; ++i) {
         if (in_copy == 0) {
-            const bool ok = mbar_wait_n(&st.full[st.jb], st.ph, a.wait_iters);
+            const bool ok = mbar_wait_n(&st.full[st.jb], st.ph, wait_iters);
             if (__any_sync(0xffffffffu, !ok)) return false;
             in_copy = min(upc, n - i);
             uic = 0;

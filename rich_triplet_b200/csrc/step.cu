@@ -67,6 +67,7 @@ struct StepSmem {
     uint8_t* uni;    // planes + xsx of a projection (first the sub-layer output of a norm
                      // prologue), or an attention item
     float2* xsx;
+    JobLite* jt;     // [njobs] this CTA's view of every projection (its weight streams' cursor)
     uint8_t* ring;   // [warps][nb][kSlotBytes]
 };
 
@@ -96,6 +97,7 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
     size_t un = proj > att ? proj : att;
     if (un < sizeof(float) * g.hidden) un = sizeof(float) * g.hidden;  // the sub-layer output of a norm prologue
     uint8_t* uni = take(un, 128);
+    uint8_t* jt = take(sizeof(JobLite) * g.njobs, 16);
     uint8_t* ring = take(static_cast<size_t>(g.warps) * g.nb * kSlotBytes, 128);
     if (S) {
         S->full = reinterpret_cast<uint64_t*>(full);
@@ -111,6 +113,7 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
         S->wse = reinterpret_cast<uint2*>(wse);
         S->uni = uni;
         S->xsx = reinterpret_cast<float2*>(uni + q4);
+        S->jt = reinterpret_cast<JobLite*>(jt);
         S->ring = ring;
     }
     return off;
@@ -156,6 +159,10 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         acore::attn_bar_init(AS);
         S.flags[0] = S.flags[1] = S.flags[2] = S.flags[3] = 0;
     }
+    const int njobs = 4 * P.nlayers + 1;
+    // This CTA's table of the jobs, read by the weight streams' cursors (one
+    // global read per job and launch instead of one per copy).
+    for (int j = tid; j < njobs; j += blockDim.x) S.jt[j] = job_lite(P.jobs[j], blockIdx.x, gridDim.x);
     __syncthreads();
     const JobSmem JS{S.pbar, S.red, S.flags, S.gs, S.gpost, S.gpre, S.uni, S.xsx, S.wpart, S.wse, S.xs,
                      reinterpret_cast<float*>(S.uni)};
@@ -165,10 +172,9 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
     const uint32_t base = *reinterpret_cast<const volatile uint32_t*>(&P.sync[0]) << 10;
     auto tag_of = [&](int l, int v) { return base + static_cast<uint32_t>(l * 8 + v + 1); };
     const int pos = *P.attn[0].pos;  // this step's position (the same for every layer)
-    const int njobs = 4 * P.nlayers + 1;
     Stream st;
     stream_start(st, S.full + warp * nb, S.ring + static_cast<size_t>(warp) * nb * kSlotBytes, nb, kSlotBytes, P.jobs,
-                 njobs, lane);
+                 njobs, lane, S.jt);
     if (tid == 0) prefetch_gammas(P.jobs[0], kProEmbedNorm, JS);
     uint32_t pph = 0;  // gamma barrier phase
     uint32_t aph = 0;  // attention barrier phases completed
@@ -237,7 +243,7 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
                 S.flags[3] = R.active && R.ntiles > 0;
             }
             __syncthreads();
-            const bool done = acore::attn_run<G, kAttnT>(at, h, s, R, AS, aph & 1u, tag_of(l, kVecQkv),
+            const bool done = acore::attn_run<G, kAttnT, true>(at, h, s, R, AS, aph & 1u, tag_of(l, kVecQkv),
                                                          tag_of(l, kVecAttn), P.abort, tag_of(l, kVecAttnPart));
             if (tid == 0) S.flags[3] = 0;
             if (R.active) aph += static_cast<uint32_t>(R.ntiles);
@@ -300,9 +306,10 @@ bool dispatch_g(int G, F&& f) {
 
 }  // namespace
 
-StepGeom step_geometry(int hidden, int kp_max, int head_dim, int group) {
+StepGeom step_geometry(int hidden, int kp_max, int head_dim, int group, int njobs) {
     StepGeom g;
     g.warps = kStepWarps;
+    g.njobs = njobs;
     g.nb = kStepNb;
     g.hidden = hidden;
     g.kp_max = kp_max;

@@ -21,6 +21,7 @@ struct StepGeom {
     int kp_lm = 0;     // LM head input (columns, multiple of 128)
     int head_dim = 0;
     int group = 0;     // query heads per KV head
+    int njobs = 0;     // projections of a step (4 per layer + the LM head)
     size_t smem = 0;
 };
 
@@ -42,7 +43,7 @@ struct StepParams {
 // kernel start; the last two slots: LM head projection done, token done.
 constexpr int kStepTraceLen = 1024;
 
-StepGeom step_geometry(int hidden, int kp_max, int head_dim, int group);
+StepGeom step_geometry(int hidden, int kp_max, int head_dim, int group, int njobs);
 // Raise the kernel's shared-memory limit on the current device (outside capture).
 cudaError_t step_prepare(const StepGeom& g);
 // Cooperative launch of one decode step on `grid` CTAs (one per SM).
