@@ -9,7 +9,9 @@
 
 namespace rt {
 
-struct AttnArgs {
+// 16-byte aligned (and so a multiple of 16 bytes): the decode-step kernel
+// brings a layer's entry into shared memory with one bulk copy.
+struct alignas(16) AttnArgs {
     const float* qkv;       // raw projections of this token: [nq*D | nkv*D | nkv*D]
     const float* q_norm;    // [D]  gamma of the per-head q norm
     const float* k_norm;    // [D]

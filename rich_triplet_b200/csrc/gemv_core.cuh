@@ -353,8 +353,10 @@ __device__ __forceinline__ bool greedy_ties_max(float v, float M, float S, float
     return __fdiv_rn(e, S) == q;
 }
 
-// One GEMV as the kernels see it.
-struct Job {
+// One GEMV as the kernels see it.  16-byte aligned (and so a multiple of 16
+// bytes), so that the decode-step kernel can bring a table entry into shared
+// memory with one bulk copy.
+struct alignas(16) Job {
     const void* tmap;   // CUtensorMap of W (parameter or global memory), row-major W
     const uint8_t* wt;  // Q4_K only, or null: W stored tile-major, unit (t, s) at
                         // ((t * nseg) + s) * 2304 bytes (16 rows x 144 bytes, rows
@@ -451,6 +453,10 @@ struct JobLite {
     uint32_t u0, u1;
     int32_t nseg;
     int32_t kind;
+    const float* g_post;  // norm weights of a norm prologue (prefetch_gammas)
+    const float* g_pre;
+    int32_t K;
+    int32_t pad;
 };
 
 // This CTA's JobLite of job j (tile-split jobs; called by one thread per job).
@@ -460,6 +466,10 @@ __device__ __forceinline__ JobLite job_lite(const Job& j, uint32_t cta, uint32_t
     L.tmap = j.tmap;
     L.nseg = j.nseg;
     L.kind = j.kind;
+    L.g_post = j.g_post;
+    L.g_pre = j.g_pre;
+    L.K = j.K;
+    L.pad = 0;
     Split ct;
     ct.init(static_cast<uint32_t>((j.rows + kTile - 1) / kTile), ncta);
     L.u0 = ct.start(cta) * static_cast<uint32_t>(j.nseg);
@@ -620,14 +630,18 @@ struct JobSmem {
                      // `planes` (dead before the planes are written)
 };
 
-// Thread 0: fetch the norm weights of `j` (prologue `pro`) into gpost / gpre,
-// completing one phase of pbar.
-__device__ __forceinline__ void prefetch_gammas(const Job& j, int pro, const JobSmem& S) {
+// Thread 0: fetch the norm weights (K floats each) of a norm prologue `pro`
+// into gpost / gpre, completing one phase of pbar.
+__device__ __forceinline__ void prefetch_gammas(int K, const float* g_post, const float* g_pre, int pro,
+                                                const JobSmem& S) {
     if (pro == kProPlain) return;
-    const uint32_t kb = static_cast<uint32_t>(j.K) * 4u;
+    const uint32_t kb = static_cast<uint32_t>(K) * 4u;
     mbar_arrive_expect_tx(S.pbar, pro == kProResidNorm ? 2u * kb : kb);
-    if (pro == kProResidNorm) bulk_g2s_nohint(S.gpost, j.g_post, kb, S.pbar);
-    bulk_g2s_nohint(S.gpre, j.g_pre, kb, S.pbar);
+    if (pro == kProResidNorm) bulk_g2s_nohint(S.gpost, g_post, kb, S.pbar);
+    bulk_g2s_nohint(S.gpre, g_pre, kb, S.pbar);
+}
+__device__ __forceinline__ void prefetch_gammas(const Job& j, int pro, const JobSmem& S) {
+    prefetch_gammas(j.K, j.g_post, j.g_pre, pro, S);
 }
 
 // Eight consecutive floats of x at column c0 (zeros at and past K; K is a
@@ -784,23 +798,37 @@ __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uin
 // (LLPoll: about two seconds, or another CTA raised `abort`), and end with
 // __syncthreads.
 
-// Planes of x = a.in_ll[0 .. K) (K a multiple of 8).  Q4_K: warp w takes
-// segments w, w + nw, ...; each lane loads its 8 values of every segment of
-// the warp (up to kLLSegs at once).
+// Planes of x = a.in_ll[0 .. K) (K a multiple of 8), restricted to the
+// column segments [seg_lo, seg_hi) this CTA's units read (a column-split job
+// reads only its parts' segments).  Q4_K: warp w takes segments seg_lo + w,
+// seg_lo + w + nw, ...; each lane loads its 8 values of every segment of the
+// warp (up to kLLSegs at once).
 constexpr int kLLSegs = 3;
 
+// The column segments [lo, hi) of x that this CTA's units of job `a` read
+// (tile split): all of them, or for a column-split job (kparts > 1) those of
+// the parts its virtual tiles belong to.
+__device__ __forceinline__ int2 cta_x_segments(const Job& a, const JobLite& L) {
+    const int kseg = (a.K + kQ4KSegCols - 1) / kQ4KSegCols;
+    if (a.kparts <= 1 || L.u1 <= L.u0) return make_int2(0, kseg);
+    const uint32_t nseg = static_cast<uint32_t>(a.nseg), pt = static_cast<uint32_t>(a.ptiles);
+    const int p0 = static_cast<int>(L.u0 / nseg / pt), p1 = static_cast<int>((L.u1 - 1) / nseg / pt);
+    return make_int2(p0 * a.nseg, (p1 + 1) * a.nseg);
+}
+
 template <int KIND>
-__device__ __forceinline__ bool ll_prologue_plain(const Job& a, const JobSmem& S, uint32_t tag, const int* abort) {
+__device__ __forceinline__ bool ll_prologue_plain(const Job& a, const JobSmem& S, uint32_t tag, const int* abort,
+                                                  int2 segs) {
     static_assert(KIND == kQ4K, "the step kernel's plain prologues are Q4_K projections");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int K = a.K;
     const int Kp = (K + kQ4KSegCols - 1) / kQ4KSegCols * kQ4KSegCols;
     const int pstride = q4k_pstride(Kp);
-    const int nseg = Kp / kQ4KSegCols;
+    const int nseg = segs.y;
     bool ok = true;
     const uint64_t* in_ll = a.in_ll;
 #pragma unroll 1
-    for (int s0 = warp; s0 < nseg && ok; s0 += kLLSegs * nw) {
+    for (int s0 = segs.x + warp; s0 < nseg && ok; s0 += kLLSegs * nw) {
         ulonglong2 w[kLLSegs][4];
         // Words still to (re)load: a poll round reloads only the words that
         // did not carry the tag yet.

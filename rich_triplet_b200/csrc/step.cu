@@ -54,6 +54,10 @@ __device__ __forceinline__ uint64_t gtimer() {
 
 struct StepSmem {
     uint64_t* full;  // [warps][nb]
+    uint64_t* jbar;  // [2] job copies landed (jbuf)
+    uint64_t* cbar;  // attention arguments landed (abuf)
+    Job* jbuf;       // [2] the current and the next projection's Job (bulk copies of the table entries)
+    AttnArgs* abuf;  // the current layer's attention arguments
     uint64_t* pbar;
     uint64_t* abar;  // attention tile barrier (kept out of `uni`: see attn_bar_init)
     float* red;
@@ -80,6 +84,10 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
         return p;
     };
     uint8_t* full = take(sizeof(uint64_t) * g.warps * g.nb, 16);
+    uint8_t* jbar = take(2 * sizeof(uint64_t), 16);
+    uint8_t* cbar = take(sizeof(uint64_t), 16);
+    uint8_t* jbuf = take(2 * sizeof(Job), 16);
+    uint8_t* abuf = take(sizeof(AttnArgs), 16);
     uint8_t* pbar = take(sizeof(uint64_t), 16);
     uint8_t* abar = take(sizeof(uint64_t), 16);
     uint8_t* red = take(32 * 4, 16);
@@ -101,6 +109,10 @@ __host__ __device__ inline size_t step_carve(uint8_t* base, const StepGeom& g, S
     uint8_t* ring = take(static_cast<size_t>(g.warps) * g.nb * kSlotBytes, 128);
     if (S) {
         S->full = reinterpret_cast<uint64_t*>(full);
+        S->jbar = reinterpret_cast<uint64_t*>(jbar);
+        S->cbar = reinterpret_cast<uint64_t*>(cbar);
+        S->jbuf = reinterpret_cast<Job*>(jbuf);
+        S->abuf = reinterpret_cast<AttnArgs*>(abuf);
         S->pbar = reinterpret_cast<uint64_t*>(pbar);
         S->abar = reinterpret_cast<uint64_t*>(abar);
         S->red = reinterpret_cast<float*>(red);
@@ -156,8 +168,14 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
     AS.bar = S.abar;
     if (tid == 0) {
         mbar_init(S.pbar, 1);
+        mbar_init(&S.jbar[0], 1);
+        mbar_init(&S.jbar[1], 1);
+        mbar_init(S.cbar, 1);
         acore::attn_bar_init(AS);
         S.flags[0] = S.flags[1] = S.flags[2] = S.flags[3] = 0;
+        // The first projection's Job; each phase brings in the next one.
+        mbar_arrive_expect_tx(&S.jbar[0], sizeof(Job));
+        bulk_g2s_nohint(&S.jbuf[0], &P.jobs[0], sizeof(Job), &S.jbar[0]);
     }
     const int njobs = 4 * P.nlayers + 1;
     // This CTA's table of the jobs, read by the weight streams' cursors (one
@@ -175,8 +193,10 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
     Stream st;
     stream_start(st, S.full + warp * nb, S.ring + static_cast<size_t>(warp) * nb * kSlotBytes, nb, kSlotBytes, P.jobs,
                  njobs, lane, S.jt);
-    if (tid == 0) prefetch_gammas(P.jobs[0], kProEmbedNorm, JS);
+    if (tid == 0) prefetch_gammas(S.jt[0].K, S.jt[0].g_post, S.jt[0].g_pre, kProEmbedNorm, JS);
     uint32_t pph = 0;  // gamma barrier phase
+    int jlast = 0;     // the last Job copy issued (jbuf), and the last attention-argument copy (abuf)
+    int alast = -1;
     uint32_t aph = 0;  // attention barrier phases completed
     Greedy gr;
     gr.init();
@@ -196,7 +216,27 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
 #pragma unroll 1
     for (int p = 0; p < 4 * P.nlayers && ok; ++p) {
         const int l = p >> 2, k = p & 3;  // k: 0 QKV, 1 O, 2 gate/up, 3 down
-        const Job& j = P.jobs[p];
+        // This projection's Job, copied into shared memory during the previous
+        // phase (its table entry is read once, off the critical path); then
+        // start the copy of the next one (its buffer's last reader was the
+        // previous phase, which every thread has left).
+        if (!mbar_wait(&S.jbar[p & 1], static_cast<uint32_t>(p >> 1) & 1u)) {
+            if (tid == 0) step_fail(P, kErrMbarTimeout);
+            ok = false;
+            break;
+        }
+        const Job& j = S.jbuf[p & 1];
+        if (tid == 0) {
+            mbar_arrive_expect_tx(&S.jbar[(p + 1) & 1], sizeof(Job));
+            bulk_g2s_nohint(&S.jbuf[(p + 1) & 1], &P.jobs[p + 1], sizeof(Job), &S.jbar[(p + 1) & 1]);
+            if (k == 0) {
+                // this layer's attention arguments (read after the QKV projection)
+                mbar_arrive_expect_tx(S.cbar, sizeof(AttnArgs));
+                bulk_g2s_nohint(S.abuf, &P.attn[l], sizeof(AttnArgs), S.cbar);
+            }
+        }
+        jlast = p + 1;
+        if (k == 0) alast = l;
         const int slot = 1 + 10 * l + 2 * k + (k ? 1 : 0);
         if (k == 0 && l == 0) {
             job_prologue<kQ4K, kProEmbedNorm>(j, JS, pph);  // the embedding row: no producer to wait for
@@ -204,12 +244,16 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
             // residual update + attention / FFN RMSNorm over the previous down / O output
             ok = ll_prologue_resid_norm<kQ4K>(j, JS, pph, k == 0 ? tag_of(l - 1, kVecDown) : tag_of(l, kVecO), P.abort);
         } else {
-            ok = ll_prologue_plain<kQ4K>(j, JS, k == 1 ? tag_of(l, kVecAttn) : tag_of(l, kVecH), P.abort);
+            ok = ll_prologue_plain<kQ4K>(j, JS, k == 1 ? tag_of(l, kVecAttn) : tag_of(l, kVecH), P.abort,
+                                         cta_x_segments(j, S.jt[p]));
         }
         if (k == 0 || k == 2) {
             pph ^= 1u;
             // the next norm prologue's weights: gate/up's, the next layer's QKV or the LM head's
-            if (tid == 0) prefetch_gammas(P.jobs[p + 2], kProResidNorm, JS);
+            if (tid == 0) {
+                const JobLite& jn = S.jt[p + 2];
+                prefetch_gammas(jn.K, jn.g_post, jn.g_pre, kProResidNorm, JS);
+            }
         }
         if (!ok) {
             if (tid == 0) step_fail(P, kErrGridTimeout);
@@ -233,7 +277,12 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         }
         if (k != 0) continue;
         // ---- attention (item h, s of this CTA) over the QKV words as they arrive ----
-        const AttnArgs& at = P.attn[l];
+        if (!mbar_wait(S.cbar, static_cast<uint32_t>(l) & 1u)) {
+            if (tid == 0) step_fail(P, kErrMbarTimeout);
+            ok = false;
+            break;
+        }
+        const AttnArgs& at = *S.abuf;
         const int items = at.nkv * at.nsplit;
         const int h = blockIdx.x / at.nsplit, s = blockIdx.x % at.nsplit;
         if (static_cast<int>(blockIdx.x) < items) {
@@ -257,10 +306,12 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
     }
     if (ok) {
         // ---- LM head: residual update + final norm, BF16 GEMV, greedy token ----
-        const Job& jl = P.jobs[4 * P.nlayers];
-        ok = ll_prologue_resid_norm<kBF16>(jl, JS, pph, tag_of(P.nlayers - 1, kVecDown), P.abort);
+        const int pl = 4 * P.nlayers;
+        const bool jok = mbar_wait(&S.jbar[pl & 1], static_cast<uint32_t>(pl >> 1) & 1u);
+        const Job& jl = S.jbuf[pl & 1];
+        ok = jok && ll_prologue_resid_norm<kBF16>(jl, JS, pph, tag_of(P.nlayers - 1, kVecDown), P.abort);
         if (!ok) {
-            if (tid == 0) step_fail(P, kErrGridTimeout);
+            if (tid == 0) step_fail(P, jok ? kErrGridTimeout : kErrMbarTimeout);
         } else {
             run_units<kBF16, kEpiArgmax>(jl, st, JS, P, S.flags, gr, 0u);
             cta_combine<kEpiArgmax>(jl, JS, gr);
@@ -279,6 +330,12 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         // Leaving early: no copy of this CTA may still be landing in shared memory.
         if (lane == 0) stream_drain(st);
         if (tid == 0 && S.flags[3]) (void)mbar_wait(AS.bar, aph & 1u);
+        if (tid == 0) {
+            // the last Job and attention-argument copies issued (bounded waits;
+            // a copy already consumed completes them at once)
+            (void)mbar_wait(&S.jbar[jlast & 1], static_cast<uint32_t>(jlast >> 1) & 1u);
+            if (alast >= 0) (void)mbar_wait(S.cbar, static_cast<uint32_t>(alast) & 1u);
+        }
         __syncthreads();
         return;
     }
