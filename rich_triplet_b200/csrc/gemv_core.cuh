@@ -28,14 +28,16 @@
 // ldmatrix hands each lane the A fragment of one 32-byte quant chunk c for 16
 // rows; a byte mask keeps the low nibbles (sub-block 2c) or the high nibbles
 // (sub-block 2c+1, as 16 q) as the u8 A operand of mma.m16n8k32.u8.s8.  x is
-// split once per job, per sub-block, into three int8 planes
+// split once per job, per 256-column segment, into three int8 planes
 // x = s * (p0 + p1/254 + p2/254^2) (|error| <= s/129032, s = max|x|/127 over
-// the sub-block), the s8 B operand.  One MMA per sub-block: its planes sit in
-// B columns 4 (j&1) + 0..2, zero elsewhere, and the two MMAs of a chunk share
-// an accumulator, so eight MMAs cover a 16-row unit.  Two shuffles per chunk
-// pair up each row's three plane sums, and every lane runs the scale
-// epilogue for one row and four sub-blocks.  (Two planes would halve the
-// B columns but leave errors near 3e-5 of rms(y): the dot product of K terms
+// the segment), the s8 B operand.  One MMA per sub-block: its planes sit in
+// B columns 4 (j&1) + 0..2, zero elsewhere (lanes feeding the other parity
+// read a zero line instead of masking), and the two MMAs of a chunk share an
+// accumulator, so eight MMAs cover a 16-row unit.  Two shuffles per chunk
+// pair up each row's three plane sums; with one x scale per segment, every
+// lane weights them by its row's 6-bit sub-block scales in integer
+// arithmetic and converts once per unit.  (Two planes would halve the B
+// columns but leave errors near 3e-5 of rms(y): the dot product of K terms
 // accumulates the 16-bit rounding of x.)
 //
 // BF16 (MatBf16::dot_row, src/autograd2.rs:861-888).  The weights, loaded by
@@ -89,7 +91,16 @@ __host__ __device__ inline int bf16_pstride(int Kp) { return Kp * 2 + 32; }  // 
 __host__ __device__ inline size_t planes_bytes(int kind, int Kp) {
     return kind == kQ4K ? 3 * static_cast<size_t>(q4k_pstride(Kp)) : 3 * static_cast<size_t>(bf16_pstride(Kp));
 }
-__host__ __device__ inline size_t xsx_bytes(int kind, int Kp) { return kind == kQ4K ? 8 * static_cast<size_t>(Kp / 32) : 0; }
+// Q4_K: per 256-column segment 12 floats (48 bytes): the sums of x over the
+// segment's eight sub-blocks, those of parity 0 first ([parity][jj], sub-block
+// 2 jj + parity), then the segment's plane unit s / 64516 and three unused;
+// after the last segment a zero line (kQ4KZeroBytes) that lanes read in place
+// of B fragments they must not feed.
+constexpr int kQ4KXsxFloats = 12;
+constexpr int kQ4KZeroBytes = 144;
+__host__ __device__ inline size_t xsx_bytes(int kind, int Kp) {
+    return kind == kQ4K ? static_cast<size_t>(Kp / 256) * kQ4KXsxFloats * 4 + kQ4KZeroBytes + 16 : 0;
+}
 
 __device__ __forceinline__ float gelu_tanh_dev(float x) {
     // TensorNode::gelu_tanh (src/autograd2.rs:3082-3091): x*0.5*(1+tanh(s*(x+c*x^3))),
@@ -151,26 +162,28 @@ __device__ __forceinline__ float ldcg_f32(const float* p) {
 }
 
 // Q4_K planes of one 256-column segment: lane l of the calling warp holds
-// elements 8l..8l+7 of it (zeros past K).  Writes the three planes and the
-// per-sub-block {unit, sum}.
+// elements 8l..8l+7 of it (zeros past K).  Writes the three planes, the
+// sub-block sums and the segment's plane unit (xsx layout above).
 __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg, int lane, int pstride,
-                                                   uint8_t* planes, float2* xsx) {
+                                                   uint8_t* planes, float2* xsx2) {
     float m = 0.f, sum = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
         m = fmaxf(m, fabsf(xv[e]));
         sum += xv[e];
     }
-    // a sub-block is 4 lanes
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    // a sub-block is 4 lanes; the scale covers the whole segment
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    // x = s (p0 + p1/254 + p2/254^2): each residual spans the full int8 range,
-    // |error| <= s / (2 * 254^2).  Each residual is taken against the stored
-    // scale s, so the reciprocal only has to be close (|x inv| stays below
-    // 127.5).  Sub-blocks whose largest magnitude is below 1e-30 quantise to
-    // zero.
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // x = s (p0 + p1/254 + p2/254^2) with one s = max|x| / 127 per segment:
+    // each residual spans the full int8 range, |error| <= s / (2 * 254^2).
+    // Each residual is taken against the stored scale s, so the reciprocal
+    // only has to be close (|x inv| stays below 127.5).  A segment whose
+    // largest magnitude is below 1e-30 quantises to zero.  One scale per
+    // segment (not per sub-block) lets the dot products apply the weights'
+    // 6-bit sub-block scales in integer arithmetic (q4k_unit_value).
     const float s = m * (1.0f / 127.0f);
     const float inv = m > 1e-30f ? __fdividef(127.0f, m) : 0.f;
     const float s254 = s * (1.0f / 254.0f);
@@ -198,10 +211,16 @@ __device__ __forceinline__ void q4k_segment_planes(const float (&xv)[8], int seg
     *reinterpret_cast<uint32_t*>(P1 + o1) = pack4_low(b1[4], b1[5], b1[6], b1[7]);
     *reinterpret_cast<uint32_t*>(P2 + o0) = pack4_low(b2[0], b2[1], b2[2], b2[3]);
     *reinterpret_cast<uint32_t*>(P2 + o1) = pack4_low(b2[4], b2[5], b2[6], b2[7]);
-    if (q == 0) {
-        // odd sub-blocks are the high nibbles, which the MMA sees as 16 q
-        const float unit = s * (1.0f / 64516.0f) * (par ? 0.0625f : 1.0f);
-        xsx[(seg * 2 + par) * 4 + jj] = make_float2(unit, sum);
+    float* xf = reinterpret_cast<float*>(xsx2) + seg * kQ4KXsxFloats;
+    if (q == 0) xf[par * 4 + jj] = sum;
+    if (lane == 0) xf[8] = s * (1.0f / 64516.0f);
+}
+
+// Threads 0..8 of the block: clear the zero line after the xsx of Kp columns.
+__device__ __forceinline__ void q4k_zero_line(float2* xsx2, int Kp) {
+    if (threadIdx.x < kQ4KZeroBytes / 16) {
+        uint8_t* z = reinterpret_cast<uint8_t*>(xsx2) + static_cast<size_t>(Kp / 256) * kQ4KXsxFloats * 4;
+        reinterpret_cast<uint4*>(z)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
     }
 }
 
@@ -788,6 +807,7 @@ __device__ __forceinline__ void job_prologue(const Job& a, const JobSmem& S, uin
         // pre-norm producing the projection input, applied as the planes are built
         planes_from_smem<KIND>(K, Kp, pstride, 1.0f / sqrtf(ss * inv_d + a.eps), S);
     }
+    if constexpr (KIND == kQ4K) q4k_zero_line(S.xsx, Kp);
     __syncthreads();
 }
 
@@ -873,6 +893,7 @@ __device__ __forceinline__ bool ll_prologue_plain(const Job& a, const JobSmem& S
             chunk_planes<KIND>(lo, hi, seg, lane, pstride, S);
         }
     }
+    q4k_zero_line(S.xsx, Kp);
     return !__syncthreads_or(!ok);
 }
 
@@ -970,75 +991,91 @@ __device__ __forceinline__ bool ll_prologue_resid_norm(const Job& a, const JobSm
     }
     ss2 = block_sum(ss2, S.red);
     planes_from_smem<KIND>(K, Kp, pstride, 1.0f / sqrtf(ss2 * inv_d + a.eps), S);
+    if constexpr (KIND == kQ4K) q4k_zero_line(S.xsx, Kp);
     __syncthreads();
     return true;
 }
 
+// a - b computed as a multiply-add (on the FMA pipe; the integer ALU pipe is
+// the one the unit arithmetic saturates).
+__device__ __forceinline__ uint32_t sub_on_fma(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(0xFFFFFFFFu), "r"(a));
+    return r;
+}
+
 // This lane's share of one Q4_K unit (16 rows x one 256-column segment at
-// shared-memory address ub, x segment xseg): the sum over the four sub-blocks
-// of parity (t >> 1) of row g + 8 (t & 1), scales applied.
-__device__ __forceinline__ float q4k_unit_value(const uint8_t* ub, int xseg, int g, int t, int pstride, int ldsm_off,
-                                                const JobSmem& S) {
+// shared-memory address ub): the value of row g + 8 (t & 1) over the four
+// sub-blocks of parity t >> 1, scales applied.  blo / bhi: where this lane
+// reads its B fragments for the low-nibble and high-nibble MMAs (its plane
+// bytes, or the zero line when its columns belong to the other parity);
+// useg: the segment's plane unit; xs4: the segment's sums of x over this
+// lane's four sub-blocks.
+__device__ __forceinline__ float q4k_unit_value(const uint8_t* ub, const uint8_t* blo, const uint8_t* bhi, int g,
+                                                int t, float useg, const float4 xs4, int ldsm_off) {
     // One MMA per sub-block j (k = its 32 elements).  B column 4 par + p
-    // holds plane p of x's sub-block j when j has parity par (lane
-    // group g = 4 par + p feeds it); columns 3 and 7 stay zero.  The
-    // MMAs of chunk c (sub-blocks 2c, 2c+1: low and high nibbles of the
-    // same 32 bytes) share accumulator c: columns 0..2 the plane sums
-    // of 2c, columns 4..6 those of 2c+1.
-    const int bpar = g >> 2, bpl = g & 3;
-    const uint32_t own0 = bpar == 0 && bpl < 3 ? 0xFFFFFFFFu : 0u;
-    const uint32_t own1 = bpar == 1 && bpl < 3 ? 0xFFFFFFFFu : 0u;
-    uint4 Bw0 = make_uint4(0u, 0u, 0u, 0u), Bw1 = Bw0;
-    if (bpl < 3) {
-        const uint8_t* pb = S.planes + bpl * pstride + xseg * 256 + (bpar * 4 + t) * 16;
-        Bw0 = lds128(pb);
-        Bw1 = lds128(pb + 128);
-    }
-    // The scale epilogue of lane (g, t) covers row g + 8 (t & 1) and the
-    // four sub-blocks of parity t >> 1.
+    // holds plane p of x's sub-block j when j has parity par (lane group
+    // g = 4 par + p feeds it); columns 3 and 7 stay zero.  The MMAs of chunk
+    // c (sub-blocks 2c, 2c+1: low and high nibbles of the same 32 bytes) share
+    // accumulator c: columns 0..2 the plane sums of 2c, columns 4..6 those of
+    // 2c+1 (whose A operand is the high nibble in place, i.e. 16 q).
+    const uint4 L0 = lds128(blo), L1 = lds128(blo + 128);
+    const uint4 H0 = lds128(bhi), H1 = lds128(bhi + 128);
     const int lpar = t >> 1, odd = t & 1;
     const uint4 hd = lds128(ub + (g + 8 * odd) * kQ4KPitch);
-    const float4 xs01 = *reinterpret_cast<const float4*>(S.xsx + (xseg * 2 + lpar) * 4);
-    const float4 xs23 = *reinterpret_cast<const float4*>(S.xsx + (xseg * 2 + lpar) * 4 + 2);
     int acc[4][4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0;
         uint32_t a0, a1, a2, a3;
         ldsm_x4(ub + ldsm_off + 32 * c, a0, a1, a2, a3);
-        const uint32_t w0 = c == 0 ? Bw0.x : c == 1 ? Bw0.z : c == 2 ? Bw1.x : Bw1.z;
-        const uint32_t w1 = c == 0 ? Bw0.y : c == 1 ? Bw0.w : c == 2 ? Bw1.y : Bw1.w;
-        mma_u8s8(acc[c], a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu, w0 & own0,
-                 w1 & own0);
-        mma_u8s8(acc[c], a0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, a2 & 0xF0F0F0F0u, a3 & 0xF0F0F0F0u, w0 & own1,
-                 w1 & own1);
+        const uint32_t l0 = a0 & 0x0F0F0F0Fu, l1 = a1 & 0x0F0F0F0Fu, l2 = a2 & 0x0F0F0F0Fu, l3 = a3 & 0x0F0F0F0Fu;
+        const uint32_t lw0 = c == 0 ? L0.x : c == 1 ? L0.z : c == 2 ? L1.x : L1.z;
+        const uint32_t lw1 = c == 0 ? L0.y : c == 1 ? L0.w : c == 2 ? L1.y : L1.w;
+        const uint32_t hw0 = c == 0 ? H0.x : c == 1 ? H0.z : c == 2 ? H1.x : H1.z;
+        const uint32_t hw1 = c == 0 ? H0.y : c == 1 ? H0.w : c == 2 ? H1.y : H1.w;
+        mma_u8s8(acc[c], l0, l1, l2, l3, lw0, lw1);
+        mma_u8s8(acc[c], sub_on_fma(a0, l0), sub_on_fma(a1, l1), sub_on_fma(a2, l2), sub_on_fma(a3, l3), hw0, hw1);
     }
-    // Lane t even holds (p0, p1) of rows g and g+8, its odd neighbour
-    // (p2, 0): they swap so that the even lane has row g's three sums
-    // and the odd lane row g+8's.
+    // Lane t even holds (p0, p1) of rows g and g+8, its odd neighbour (p2, 0).
+    // Two shuffles give the even lane row g's p2 and the odd lane row g+8's
+    // p0 and p1; every lane then weights its own and the received sums by
+    // the 6-bit sub-block scales of its row in integer arithmetic (exact:
+    // at most 4 * 63 * 32 * 240 * 127 < 2^31), and forms
+    // T = 64516 P0 + 254 P1 + P2 once per unit.
     const float d = f16_bits_to_f32(hd.x & 0xFFFFu), dmin = f16_bits_to_f32(hd.x >> 16);
     // scale_min (src/autograd2.rs:1075-1085), four 6-bit fields per word
     const uint32_t s_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
     const uint32_t s_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
     const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-    const uint32_t sel_a = 0x7540u | static_cast<uint32_t>(lpar), sel_b = 0x7540u | static_cast<uint32_t>(2 + lpar);
-    float vs = 0.f, vm = 0.f;
+    // sub-block 2c + lpar: byte lpar (c even) or 2 + lpar (c odd) of the low
+    // (c < 2) or high words; as an integer, or as an exact float
+    const uint32_t isel_a = 0x4440u | static_cast<uint32_t>(lpar), isel_b = 0x4440u | static_cast<uint32_t>(2 + lpar);
+    const uint32_t fsel_a = 0x7540u | static_cast<uint32_t>(lpar), fsel_b = 0x7540u | static_cast<uint32_t>(2 + lpar);
+    int A0 = 0, A1 = 0, A2 = 0, AX = 0, AY = 0;
+    float vm = 0.f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         const int x = __shfl_xor_sync(0xffffffffu, odd ? acc[c][0] : acc[c][2], 1);
         const int y = __shfl_xor_sync(0xffffffffu, acc[c][3], 1);
-        const int P0 = odd ? x : acc[c][0], P1 = odd ? y : acc[c][1], P2 = odd ? acc[c][2] : x;
-        const float T = fmaf(static_cast<float>(P0), 64516.0f,
-                             fmaf(static_cast<float>(P1), 254.0f, static_cast<float>(P2)));
-        // sub-block 2c + lpar: bytes lpar / 2 + lpar of the low (c < 2) or high words
         const uint32_t sw = c < 2 ? s_lo : s_hi, mw = c < 2 ? m_lo : m_hi;
-        const uint32_t sel = (c & 1) ? sel_b : sel_a;
-        const float2 us = c == 0 ? make_float2(xs01.x, xs01.y) : c == 1 ? make_float2(xs01.z, xs01.w)
-                        : c == 2 ? make_float2(xs23.x, xs23.y) : make_float2(xs23.z, xs23.w);
-        vs = fmaf(byte_to_float(sw, sel), T * us.x, vs);
-        vm = fmaf(byte_to_float(mw, sel), us.y, vm);
+        const int sc = static_cast<int>(__byte_perm(sw, 0u, (c & 1) ? isel_b : isel_a));
+        A0 += sc * acc[c][0];
+        A1 += sc * acc[c][1];
+        A2 += sc * acc[c][2];
+        AX += sc * x;
+        AY += sc * y;
+        const float xs = c == 0 ? xs4.x : c == 1 ? xs4.y : c == 2 ? xs4.z : xs4.w;
+        vm = fmaf(byte_to_float(mw, (c & 1) ? fsel_b : fsel_a), xs, vm);
     }
-    return d * vs - dmin * vm;
+    // even lane (row g): T = 64516 A0 + 254 A1 + AX; odd lane (row g+8): T = 64516 AX + 254 AY + A2
+    const float wa = odd ? 0.f : 64516.0f, wb = odd ? 0.f : 254.0f, wc = odd ? 1.0f : 0.f;
+    const float wx = odd ? 64516.0f : 1.0f, wy = odd ? 254.0f : 0.f;
+    const float T = fmaf(static_cast<float>(A0), wa,
+                         fmaf(static_cast<float>(A1), wb,
+                              fmaf(static_cast<float>(A2), wc, fmaf(static_cast<float>(AX), wx, static_cast<float>(AY) * wy))));
+    const float u = lpar ? useg * 0.0625f : useg;  // the high nibbles were seen as 16 q
+    return d * (T * u) - dmin * vm;
 }
 
 // How the warps' shares of a job are laid out (Job::tile_split matches it).
@@ -1098,6 +1135,20 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
                              ? ((lane & 7) + ((lane >> 3) & 1) * 8) * kQ4KPitch + 16 + ((lane >> 4) & 1) * 16
                              : ((lane & 7) + ((lane >> 3) & 1) * 8) * kBF16Pitch + ((lane >> 4) & 1) * 16;
 
+    // Q4_K: this lane's B fragments (planes at lane_b + 256 xseg, or the zero
+    // line) and its sub-block parity's sums of x.
+    const int bpar = g >> 2, bpl = g & 3;
+    const int lane_b = bpl * pstride + (bpar * 4 + t) * 16;
+    const uint8_t* zline = reinterpret_cast<const uint8_t*>(S.xsx) + static_cast<size_t>(Kp / 256) * kQ4KXsxFloats * 4;
+    const bool feeds_lo = bpl < 3 && bpar == 0, feeds_hi = bpl < 3 && bpar == 1;
+    const float* xsf = reinterpret_cast<const float*>(S.xsx);
+    auto unit_at = [&](const uint8_t* ub, int xs) {
+        const uint8_t* real = S.planes + lane_b + xs * 256;
+        const float* xf = xsf + xs * kQ4KXsxFloats;
+        return q4k_unit_value(ub, feeds_lo ? real : zline, feeds_hi ? real : zline, g, t, xf[8],
+                              *reinterpret_cast<const float4*>(xf + (t >> 1) * 4), ldsm_off);
+    };
+
     float acc0 = 0.f, acc1 = 0.f;  // this lane's share of rows g and g+8 of the current tile
     uint32_t tile = u_begin / nseg;
     int seg = static_cast<int>(u_begin - tile * nseg);
@@ -1121,10 +1172,10 @@ __device__ __forceinline__ bool job_units_run(const Job& a, Stream& st, const Jo
             // The units of a copy are computed together (independent chains, so
             // the scheduler can interleave them), then consumed one by one.
             if (uic == 0) {
-                cv0 = q4k_unit_value(ub, xseg, g, t, pstride, ldsm_off, S);
+                cv0 = unit_at(ub, xseg);
                 if (in_copy > 1) {
                     const int xs1 = seg + 1 < nseg ? xseg + 1 : part_base(tile + 1);
-                    cv1 = q4k_unit_value(ub + kQ4KUnit, xs1, g, t, pstride, ldsm_off, S);
+                    cv1 = unit_at(ub + kQ4KUnit, xs1);
                 }
             }
             const float v = uic == 0 ? cv0 : cv1;
