@@ -92,6 +92,8 @@ int rt_init(int device, rt_ctx** out) {
     }
     cudaMemset(ctx->d_err, 0, sizeof(int) * 4);
     rt::gemv_prepare();
+    (void)rt::gemv_cluster_prepare();
+    cudaGetLastError();
     if (rt::gemm_q4k_prepare() != cudaSuccess) cudaGetLastError();  // a launch then reports the failure
     *out = ctx;
     return RT_OK;
@@ -236,7 +238,9 @@ int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
     const int K = static_cast<int>(w->cols);
     if (!w->gemv_ready) {
-        w->plan = rt::gemv_plan(kind, w->rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 1);
+        // Q4_K: the cluster kernel (gemv_cluster.cu); BF16: the generic one
+        w->plan = kind == rt::kQ4K ? rt::gemv_cluster_plan(w->rows, K, ctx->num_sms)
+                                   : rt::gemv_plan(kind, w->rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, 1);
         if (w->plan.warps == 0) return fail(ctx, RT_E_SHAPE, "gemv: no launch geometry for cols %d", K);
         if (!rt::gemv_make_tmap(kind, w->d, w->rows, K, w->plan, &w->tmap))
             return fail(ctx, RT_E_CUDA, "gemv: TMA descriptor rejected for [%lld, %d]", static_cast<long long>(w->rows), K);
@@ -264,7 +268,10 @@ int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags
     a.part = ctx->gemv_part;
     a.tile_cnt = ctx->gemv_cnt;
     a.err = ctx->d_err;
-    RT_CHECK_CUDA(ctx, rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, w->tmap, p, ctx->stream, false));
+    if (kind == rt::kQ4K)
+        RT_CHECK_CUDA(ctx, rt::gemv_cluster_launch(a, w->tmap, p, ctx->stream, false));
+    else
+        RT_CHECK_CUDA(ctx, rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, w->tmap, p, ctx->stream, false));
     if (flags == RT_HOST) {
         RT_CHECK_CUDA(ctx, cudaMemcpyAsync(y, dy, sizeof(float) * w->rows, cudaMemcpyDeviceToHost, ctx->stream));
         return rt_sync(ctx);
@@ -363,7 +370,11 @@ int rt_gemv_bench(rt_ctx* ctx, int fmt, const rt_w* const* ws, int nw, const flo
     const int64_t rows = ws[0]->rows;
     const int K = static_cast<int>(ws[0]->cols);
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
-    const rt::GemvPlan p = rt::gemv_plan(kind, rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, ctas_per_sm);
+    // Q4_K with ctas_per_sm 1: the cluster kernel of rt_gemv_q4k; otherwise the
+    // generic kernel at the requested CTAs per SM (kept for comparison)
+    const bool cluster = kind == rt::kQ4K && ctas_per_sm == 1;
+    const rt::GemvPlan p = cluster ? rt::gemv_cluster_plan(rows, K, ctx->num_sms)
+                                   : rt::gemv_plan(kind, rows, K, 1, rt::kProPlain, rt::kEpiPlain, ctx->num_sms, ctas_per_sm);
     if (p.warps == 0) return fail(ctx, RT_E_SHAPE, "rt_gemv_bench: no launch geometry for cols %d", K);
     std::vector<CUtensorMap> tm(nw);
     for (int i = 0; i < nw; ++i)
@@ -385,7 +396,8 @@ int rt_gemv_bench(rt_ctx* ctx, int fmt, const rt_w* const* ws, int nw, const flo
         a.part = ctx->gemv_part;
         a.tile_cnt = ctx->gemv_cnt;
         a.err = ctx->d_err;
-        e = rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, tm[i % nw], p, ctx->stream, i > 0);
+        e = cluster ? rt::gemv_cluster_launch(a, tm[i % nw], p, ctx->stream, i > 0)
+                    : rt::gemv_launch(kind, rt::kProPlain, rt::kEpiPlain, a, tm[i % nw], p, ctx->stream, i > 0);
     }
     const cudaError_t ec = cudaStreamEndCapture(ctx->stream, &graph);
     if (e == cudaSuccess) e = ec;

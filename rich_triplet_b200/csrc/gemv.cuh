@@ -123,6 +123,13 @@ bool gemv_make_tmap(int kind, const void* w, int64_t rows, int K, const GemvPlan
 cudaError_t gemv_launch(int kind, int prologue, int epilogue, GemvArgs a, const CUtensorMap& tmap, const GemvPlan& p,
                         cudaStream_t stream, bool pdl);
 
+// The Q4_K GEMV of the standalone entry points (gemv_cluster.cu): plain x,
+// plain y, row-major weights; four-CTA clusters, two CTAs per SM where the
+// shared memory allows.  The plan's tensor map is gemv_make_tmap's (box_x, 16).
+GemvPlan gemv_cluster_plan(int64_t rows, int K, int num_sms);
+cudaError_t gemv_cluster_prepare();
+cudaError_t gemv_cluster_launch(GemvArgs a, const CUtensorMap& tmap, const GemvPlan& p, cudaStream_t stream, bool pdl);
+
 // Algorithmic bytes of one launch: weights + x + y (+ prologue vectors).
 uint64_t gemv_algorithmic_bytes(int kind, int64_t rows, int K, int prologue, int epilogue);
 
