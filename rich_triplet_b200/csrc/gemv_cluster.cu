@@ -26,7 +26,8 @@
 // Every wait is bounded: mbarrier waits by iteration count (GemvArgs::
 // wait_iters, or the default); a warp whose wait gave up records kErrMbarTimeout,
 // waits (bounded) for its copies in flight and still takes part in the cluster
-// barriers, which every thread of every CTA reaches exactly three times.
+// barriers: every thread of every CTA arrives at each of the three, and every
+// thread of CTA 0 (the other CTA: the first two) waits on it.
 #include <algorithm>
 
 #include "common.cuh"
@@ -90,6 +91,18 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 // stores (local and remote) before later accesses.
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The same without ordering: only that every CTA of the cluster is running.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+// Arrival alone (release: this thread's earlier remote stores become visible
+// to the threads that wait on the barrier).
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // Address of `local` (this CTA's shared memory) in CTA `rank` of the cluster.
@@ -191,7 +204,7 @@ __global__ void __cluster_dims__(kCC, 1, 1) __launch_bounds__(kCW * 32, 2)
         for (int k = 0; k < nb && iu < ue; ++k) issue(k);
     }
     if (tid == 0) S.flags[0] = 0;
-    cluster_sync();  // #1: every CTA of the cluster is running (its shared memory may be written)
+    cluster_sync_relaxed();  // #1: every CTA of the cluster is running (its shared memory may be written)
     pdl_launch_dependents();
     pdl_wait();
 
@@ -281,9 +294,13 @@ __global__ void __cluster_dims__(kCC, 1, 1) __launch_bounds__(kCW * 32, 2)
         }
     }
     __syncwarp();
-    cluster_sync();  // #3: every piece is in CTA 0
+    // #3: every piece is in CTA 0.  Only CTA 0 waits: the other CTA's shared
+    // memory is not read by anyone after #2, so it may leave once it arrived.
     if (tid == 0 && S.flags[0] && a.err) atomicExch(a.err, kErrMbarTimeout);
-    if (rank != 0 || n == 0) return;
+    cluster_arrive();
+    if (rank != 0) return;
+    cluster_wait();
+    if (n == 0) return;
     // ---- CTA 0: the shared tiles, pieces added in warp order ----
     auto wstart = [&](uint32_t w) { return n * w / kCWarps; };
     auto owner = [&](uint32_t uu) {  // warp whose share holds cluster unit uu
