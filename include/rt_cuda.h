@@ -150,6 +150,16 @@ int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
  * the tied LM head over several sequences' final hidden states: replaces
  * MatBf16::matmul_by_t with M > 1 (src/autograd2.rs:757-776, 954-1000). */
 int rt_gemm_bf16(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags);
+/* QLinear::forward (src/qlinear.rs:83-111) for a Q4_K or BF16 weight W
+ * [out, in]: y[t, out] = x[t, in] . dequant(W)^T + bias (add_bias_rows,
+ * src/qlinear.rs:49-61), x and y f32 row-major, bias f32 [out] or NULL.
+ * t == 1 runs the GEMV (x split into three int8 planes: f32-level accuracy);
+ * t > 1 the tensor-core GEMM of rt_gemm_q4k / rt_gemm_bf16 with fp16 operands
+ * (rows of x scaled by powers of two into fp16's range; relative error about
+ * 1e-4).  flags RT_HOST: host x, bias and y, the call copies and waits;
+ * RT_DEVICE: device pointers (x and y 16-byte aligned), enqueued on the
+ * context stream.  RT_E_FORMAT for other weight formats. */
+int rt_qlinear_forward(rt_ctx* ctx, const rt_w* w, const float* x, int64_t t, const float* bias, float* y, int flags);
 /* The launch plan rt_gemm_q4k / rt_gemm_bf16 (and the many-sequence engines)
  * choose for an [m, k] x [n, k]^T product on a GPU with num_sms SMs, without
  * a GPU (no counterpart in the reference): out[0] the CTA tile (128: weight

@@ -101,6 +101,7 @@ SIGNATURES = {
     "rt_batch_info": (ctypes.c_int, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_i32)]),
     "rt_gemm_bf16": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp, ctypes.c_int]),
     "rt_gemm_plan": (ctypes.c_int, [_i64, _i64, _i32, _i32, _i32, ctypes.POINTER(_i32)]),
+    "rt_qlinear_forward": (ctypes.c_int, [_vp, _vp, _vp, _i64, _vp, _vp, ctypes.c_int]),
     "rt_gemv_bench": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(_vp), ctypes.c_int, _vp, _vp, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),
     "rt_convert_q4_0_to_q4k": (ctypes.c_int, [_vp, _vp, _i64, _i64, ctypes.c_int, _pp]),

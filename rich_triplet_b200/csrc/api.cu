@@ -104,6 +104,7 @@ void rt_destroy(rt_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->scratch);
+    cudaFree(ctx->io);
     cudaFree(ctx->gemv_part);
     cudaFree(ctx->gemv_cnt);
     cudaFree(ctx->d_err);
@@ -208,6 +209,18 @@ int ensure_scratch(rt_ctx* ctx, size_t floats) {
     return RT_OK;
 }
 
+int ensure_io(rt_ctx* ctx, size_t floats) {
+    if (ctx->io_floats >= floats) return RT_OK;
+    RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(ctx->io);
+    ctx->io = nullptr;
+    ctx->io_floats = 0;
+    int rc = rt::dev_alloc(ctx, reinterpret_cast<void**>(&ctx->io), floats * sizeof(float), "qlinear io");
+    if (rc != RT_OK) return rc;
+    ctx->io_floats = floats;
+    return RT_OK;
+}
+
 int ensure_gemv_scratch(rt_ctx* ctx, const rt::GemvPlan& p) {
     if (ctx->gemv_part_floats >= p.part_floats && ctx->gemv_cnt_words >= p.cnt_words) return RT_OK;
     RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
@@ -279,7 +292,8 @@ int gemv_common(rt_ctx* ctx, const rt_w* wc, const float* x, float* y, int flags
     return RT_OK;
 }
 
-int gemm_common(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags, int fmt) {
+int gemm_common(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags, int fmt,
+                bool a_f32 = false) {
     if (!ctx || !w || !a || !c) return fail(ctx, RT_E_INVAL, "rt_gemm: null argument");
     if (flags != RT_HOST && flags != RT_DEVICE) return fail(ctx, RT_E_INVAL, "rt_gemm: flags must be RT_HOST or RT_DEVICE");
     if (w->fmt != fmt) return fail(ctx, RT_E_FORMAT, "rt_gemm: weight format %d, this entry point takes %d", w->fmt, fmt);
@@ -289,14 +303,15 @@ int gemm_common(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
     if (p.bm == 0) return fail(ctx, RT_E_SHAPE, "rt_gemm: no launch geometry for M %lld, N %lld, K %d",
                                static_cast<long long>(m), static_cast<long long>(n), k);
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
-    const size_t a_bytes = static_cast<size_t>(m) * k * 2;
+    const size_t a_bytes = static_cast<size_t>(m) * k * (a_f32 ? 4 : 2);
+    const size_t a16_bytes = static_cast<size_t>(m) * k * 2;
     if (flags == RT_DEVICE && ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(c) & 15)))
         return fail(ctx, RT_E_INVAL, "rt_gemm: device A and C must be 16-byte aligned");
     // scratch: [A (host calls)] [A as fp16 rows] [row scales] [C (host calls)]
     // [split partials], each 256-byte aligned
     auto al = [](size_t floats) { return (floats + 63) / 64 * 64; };
     const size_t a_floats = flags == RT_HOST ? al((a_bytes + 3) / 4) : 0;
-    const size_t a16_floats = al((a_bytes + 3) / 4), s_floats = al(static_cast<size_t>(m));
+    const size_t a16_floats = al((a16_bytes + 3) / 4), s_floats = al(static_cast<size_t>(m));
     const size_t c_floats = flags == RT_HOST ? al(static_cast<size_t>(m) * n) : 0;
     const size_t part_floats = p.splits > 1 ? static_cast<size_t>(p.splits) * m * n : 0;
     int rc = ensure_scratch(ctx, a_floats + a16_floats + s_floats + c_floats + part_floats);
@@ -308,7 +323,10 @@ int gemm_common(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
     float* parts = ascale + s_floats + c_floats;
     if (flags == RT_HOST)
         RT_CHECK_CUDA(ctx, cudaMemcpyAsync(const_cast<void*>(da), a, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
-    RT_CHECK_CUDA(ctx, rt::a_to_f16_launch(static_cast<const uint16_t*>(da), m, k, a16, ascale, ctx->stream));
+    if (a_f32)
+        RT_CHECK_CUDA(ctx, rt::a_f32_to_f16_launch(static_cast<const float*>(da), m, k, a16, ascale, ctx->stream));
+    else
+        RT_CHECK_CUDA(ctx, rt::a_to_f16_launch(static_cast<const uint16_t*>(da), m, k, a16, ascale, ctx->stream));
     CUtensorMap tm_a, tm_w;
     if (!rt::gemm_q4k_tmaps(a16, m, w->d, n, k, p, &tm_a, &tm_w))
         return fail(ctx, RT_E_CUDA, "rt_gemm: TMA descriptor rejected");
@@ -342,6 +360,46 @@ int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
 
 int rt_gemm_bf16(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags) {
     return gemm_common(ctx, w, a, m, c, flags, RT_FMT_BF16);
+}
+
+int rt_qlinear_forward(rt_ctx* ctx, const rt_w* w, const float* x, int64_t t, const float* bias, float* y, int flags) {
+    if (!ctx || !w || !x || !y) return fail(ctx, RT_E_INVAL, "rt_qlinear_forward: null argument");
+    if (flags != RT_HOST && flags != RT_DEVICE)
+        return fail(ctx, RT_E_INVAL, "rt_qlinear_forward: flags must be RT_HOST or RT_DEVICE");
+    if (w->fmt != RT_FMT_Q4K && w->fmt != RT_FMT_BF16)
+        return fail(ctx, RT_E_FORMAT, "rt_qlinear_forward: weight format %d (Q4_K or BF16 only)", w->fmt);
+    if (t < 1 || t > (int64_t{1} << 24)) return fail(ctx, RT_E_SHAPE, "rt_qlinear_forward: t = %lld rows", static_cast<long long>(t));
+    RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+    const int64_t in = w->cols, out = w->rows;
+    const float* dx = x;
+    const float* db = bias;
+    float* dy = y;
+    if (flags == RT_HOST) {
+        // device copies: [x][bias][y], each 256-byte aligned
+        auto al = [](int64_t f) { return static_cast<size_t>((f + 63) / 64 * 64); };
+        const size_t xf = al(t * in), bf = bias ? al(out) : 0, yf = al(t * out);
+        if (int rc = ensure_io(ctx, xf + bf + yf); rc != RT_OK) return rc;
+        float* dxw = ctx->io;
+        float* dbw = ctx->io + xf;
+        dy = ctx->io + xf + bf;
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(dxw, x, sizeof(float) * t * in, cudaMemcpyHostToDevice, ctx->stream));
+        if (bias) RT_CHECK_CUDA(ctx, cudaMemcpyAsync(dbw, bias, sizeof(float) * out, cudaMemcpyHostToDevice, ctx->stream));
+        dx = dxw;
+        db = bias ? dbw : nullptr;
+    } else if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15)) {
+        return fail(ctx, RT_E_INVAL, "rt_qlinear_forward: device x and y must be 16-byte aligned");
+    }
+    // One row: the GEMV (x split into three int8 planes, f32-level accuracy);
+    // more: the tensor-core GEMM over fp16 operands.
+    int rc = t == 1 ? gemv_common(ctx, w, dx, dy, RT_DEVICE, w->fmt == RT_FMT_Q4K ? rt::kQ4K : rt::kBF16)
+                    : gemm_common(ctx, w, dx, t, dy, RT_DEVICE, w->fmt, true);
+    if (rc != RT_OK) return rc;
+    if (db) RT_CHECK_CUDA(ctx, rt::bias_rows_launch(dy, t, out, db, ctx->num_sms, ctx->stream));
+    if (flags == RT_HOST) {
+        RT_CHECK_CUDA(ctx, cudaMemcpyAsync(y, dy, sizeof(float) * t * out, cudaMemcpyDeviceToHost, ctx->stream));
+        return rt_sync(ctx);
+    }
+    return RT_OK;
 }
 
 int rt_gemm_plan(int64_t m, int64_t n, int32_t k, int32_t num_sms, int32_t bf16_weights, int32_t* out) {

@@ -678,6 +678,27 @@ __global__ void a_to_f16_rows_kernel(const uint16_t* __restrict__ a, int k, uint
     if (threadIdx.x == 0) scale[blockIdx.x] = sc;
 }
 
+// The same from f32 rows.
+__global__ void a_f32_to_f16_rows_kernel(const float* __restrict__ a, int k, uint16_t* __restrict__ out,
+                                         float* __restrict__ scale) {
+    __shared__ float red[32];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * k;
+    float mx = 0.f;
+    for (int c = threadIdx.x; c < k; c += blockDim.x) mx = fmaxf(mx, fabsf(a[base + c]));
+    mx = block_max(mx, red);
+    float inv, sc;
+    row_scale_f16(mx, &inv, &sc);
+    for (int c = threadIdx.x; c < k; c += blockDim.x) out[base + c] = __half_as_ushort(__float2half_rn(a[base + c] * inv));
+    if (threadIdx.x == 0) scale[blockIdx.x] = sc;
+}
+
+// y[r][c] += bias[c] over m rows of n (add_bias_rows, src/qlinear.rs:49-61).
+__global__ void bias_rows_kernel(float* __restrict__ y, int64_t m, int64_t n, const float* __restrict__ bias) {
+    const int64_t total = m * n, stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride)
+        y[i] += bias[i % n];
+}
+
 // out[i] = sum over z < parts of in[z * count + i], in part order.
 __global__ void sum_parts_kernel(const float* __restrict__ in, int parts, int64_t count, float* __restrict__ out) {
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -693,6 +714,20 @@ cudaError_t a_to_f16_launch(const uint16_t* a_bf16, int64_t m, int k, uint16_t* 
     if (m <= 0) return cudaSuccess;
     if (m > 0x7FFFFFFF) return cudaErrorInvalidValue;
     a_to_f16_rows_kernel<<<static_cast<unsigned>(m), 256, 0, s>>>(a_bf16, k, out, scale);
+    return cudaGetLastError();
+}
+
+cudaError_t a_f32_to_f16_launch(const float* a, int64_t m, int k, uint16_t* out, float* scale, cudaStream_t s) {
+    if (m <= 0) return cudaSuccess;
+    if (m > 0x7FFFFFFF) return cudaErrorInvalidValue;
+    a_f32_to_f16_rows_kernel<<<static_cast<unsigned>(m), 256, 0, s>>>(a, k, out, scale);
+    return cudaGetLastError();
+}
+
+cudaError_t bias_rows_launch(float* y, int64_t m, int64_t n, const float* bias, int num_sms, cudaStream_t s) {
+    if (m <= 0 || n <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((m * n + 255) / 256, static_cast<int64_t>(num_sms > 0 ? num_sms : 148) * 8);
+    bias_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(y, m, n, bias);
     return cudaGetLastError();
 }
 

@@ -42,6 +42,10 @@ cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, co
                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s);
 // A rows for the GEMM from bf16 rows: out[r] = fp16(a[r] * 2^-e_r), scale[r] = 2^e_r.
 cudaError_t a_to_f16_launch(const uint16_t* a_bf16, int64_t m, int k, uint16_t* out, float* scale, cudaStream_t s);
+// The same from f32 rows.
+cudaError_t a_f32_to_f16_launch(const float* a, int64_t m, int k, uint16_t* out, float* scale, cudaStream_t s);
+// y[r][c] += bias[c] for m rows of n.
+cudaError_t bias_rows_launch(float* y, int64_t m, int64_t n, const float* bias, int num_sms, cudaStream_t s);
 // out[i] = in[i] + in[count + i] + ... (parts vectors of `count`, in order).
 cudaError_t sum_parts_launch(const float* in, int parts, int64_t count, float* out, int num_sms, cudaStream_t s);
 

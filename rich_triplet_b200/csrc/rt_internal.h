@@ -27,6 +27,11 @@ struct rt_ctx {
     float* gemv_part = nullptr;
     uint32_t* gemv_cnt = nullptr;
     int64_t gemv_part_floats = 0, gemv_cnt_words = 0;
+    // Device copies of host-pointer inputs and outputs of rt_qlinear_forward
+    // (kept apart from `scratch`, which the GEMV and GEMM use for their own
+    // intermediates).
+    float* io = nullptr;
+    size_t io_floats = 0;
 };
 
 struct rt_w {
