@@ -593,6 +593,9 @@ __device__ __forceinline__ bool attn_run(const AttnArgs& a, int h, int s, const 
         }
     }
     if (R.has_new && warp == R.ncached % nw) visit(S.knew, S.vnew);
+    // Every warp has read q from S.qv (which the states below overwrite) and
+    // finished its positions; with no cached tile there was no barrier yet.
+    __syncthreads();
 
     // Combine the warps' states.  Per query head g: M = max_w m_w, weight
     // e_w = exp(m_w - M), l = sum_w e_w l_w, output = sum_w e_w acc_w (the

@@ -227,6 +227,9 @@ __global__ void __launch_bounds__(kStepWarps * 32, 1) step_kernel(const StepPara
         }
         const Job& j = S.jbuf[p & 1];
         if (tid == 0) {
+            // the buffers' previous readers (generic proxy) finished before the
+            // barrier that ended their phase; order them before the copies
+            fence_proxy_async_smem();
             mbar_arrive_expect_tx(&S.jbar[(p + 1) & 1], sizeof(Job));
             bulk_g2s_nohint(&S.jbuf[(p + 1) & 1], &P.jobs[p + 1], sizeof(Job), &S.jbar[(p + 1) & 1]);
             if (k == 0) {
