@@ -331,7 +331,7 @@ int gemm_common(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, 
     if (!rt::gemm_q4k_tmaps(a16, m, w->d, n, k, p, &tm_a, &tm_w))
         return fail(ctx, RT_E_CUDA, "rt_gemm: TMA descriptor rejected");
     RT_CHECK_CUDA(ctx, rt::gemm_q4k_launch(tm_a, tm_w, ascale, p.splits > 1 ? parts : dc, m, n, k, p, ctx->d_err,
-                                           ctx->stream));
+                                           ctx->stream, a16));
     if (p.splits > 1)
         RT_CHECK_CUDA(ctx, rt::sum_parts_launch(parts, p.splits, static_cast<int64_t>(m) * n, dc, ctx->num_sms, ctx->stream));
     if (flags == RT_HOST) {

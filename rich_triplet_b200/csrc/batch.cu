@@ -62,6 +62,7 @@ struct BatchGemm {
     rt::GemmPlan p;
     CUtensorMap ta, tw;
     const float* ascale = nullptr;  // row scales of A
+    const uint16_t* a = nullptr;    // fp16 rows of A (the multi-row GEMV reads them directly)
     int64_t m = 0, n = 0;
     int k = 0;
 };
@@ -656,6 +657,7 @@ bool make_gemm(rt_batch* t, int m, int row0, const void* w, int64_t n, int k, bo
     g->n = n;
     g->k = k;
     g->ascale = t->xscale + row0;
+    g->a = t->xa + static_cast<int64_t>(row0) * k;
     g->p = rt::gemm_q4k_plan(m, n, k, t->ctx->num_sms, wbf16, allow_split);
     if (g->p.bm == 0 || g->p.splits > kMaxParts) return false;
     return rt::gemm_q4k_tmaps(t->xa + static_cast<int64_t>(row0) * k, m, w, n, k, g->p, &g->ta, &g->tw);
@@ -700,7 +702,7 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         return e == cudaSuccess;
     };
     auto gemm = [&](const BatchGemm& g, float* c) {
-        return ok(rt::gemm_q4k_launch(g.ta, g.tw, g.ascale, c, g.m, g.n, g.k, g.p, t->ctx->d_err, s));
+        return ok(rt::gemm_q4k_launch(g.ta, g.tw, g.ascale, c, g.m, g.n, g.k, g.p, t->ctx->d_err, s, g.a));
     };
     auto nccl_ok = [&](ncclResult_t r) { return ok(r == ncclSuccess ? cudaSuccess : cudaErrorUnknown); };
     uint32_t ar_call = 0;  // peer all-reduces of this step so far

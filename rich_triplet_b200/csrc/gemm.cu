@@ -552,6 +552,16 @@ __global__ void __launch_bounds__(kThreads, Cfg<NACC, BN, AROWS>::kCtasPerSm)
 GemmPlan gemm_q4k_plan(int64_t m, int64_t n, int k, int num_sms, bool wbf16, bool allow_split) {
     GemmPlan p;
     if (m <= 0 || n <= 0 || k <= 0 || k % 256 != 0 || m > 0x7FFFFFFF || n > 0x7FFFFFFF) return p;
+    // Q4_K at M <= 16: the multi-row GEMV streams the weights several times
+    // faster than the tensor-memory kernel's per-K-block chain.  RT_GEMM_ROWS=0
+    // or a forced tile (RT_GEMM_TILE) keeps the tcgen05 kernel; RT_GEMM_SPLITS
+    // forces either kernel's K split (tests and tuning).
+    const char* rows_env = getenv("RT_GEMM_ROWS");
+    const char* splits_env = getenv("RT_GEMM_SPLITS");
+    if (!wbf16 && m <= kRowsMaxM && !(rows_env && atoi(rows_env) == 0) && !getenv("RT_GEMM_TILE") &&
+        gemm_rows_plan(m, n, k, num_sms > 0 ? num_sms : 148, allow_split ? 8 : 1,
+                       allow_split && splits_env ? atoi(splits_env) : 0, &p))
+        return p;
     // The 256 x 256 tile streams A half as often and dequantises W half as
     // often as the 128 x 128 tile, at about half the cost per FLOP (measured);
     // estimated time: waves of CTAs x per-tile cost (2 units big, 1 small).
@@ -617,6 +627,7 @@ cudaError_t gemm_q4k_prepare() {
     set(gemm_q4k_kernel<1, 128, true, 64>, Cfg<1, 128, 64>::kSmemBytes);
     set(gemm_q4k_kernel<1, 128, true, 16>, Cfg<1, 128, 16>::kSmemBytes);
     set(gemm_q4k_kernel<2, 256, true, 128>, Cfg<2, 256>::kSmemBytes);
+    if (e == cudaSuccess) e = gemm_rows_prepare();
     return e;
 }
 
@@ -645,7 +656,8 @@ bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, c
 }
 
 cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, const float* ascale, float* c, int64_t m,
-                            int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s) {
+                            int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s, const uint16_t* a) {
+    if (p.rows_nt > 0) return gemm_rows_launch(tm_w, a, ascale, c, m, n, k, p, err, s);
     const dim3 g = p.grid;
 #define RT_GEMM_LAUNCH(NA, BNN, WBB, AR) \
     gemm_q4k_kernel<NA, BNN, WBB, AR><<<g, kThreads, p.smem, s>>>(tm_a, tm_w, ascale, c, m, n, k, p.kps, err)

@@ -23,7 +23,14 @@ struct GemmPlan {
     int arows = 128;     // rows of an A stage (16 / 64 for M up to that: a deeper A/B ring)
     dim3 grid;
     size_t smem = 0;
+    // Multi-row GEMV (gemm_rows.cu) instead of the tensor-memory kernel:
+    // n8 tiles of A rows (1, 2 or 4; 0: the tcgen05 kernel), CTAs per K part,
+    // ring slots per warp.
+    int rows_nt = 0, rows_cpp = 0, rows_nb = 0;
 };
+
+// Largest M the multi-row GEMV takes.
+constexpr int kRowsMaxM = 16;
 
 // Tile and split for C[m, n] = A[m, k] . W[n, k]^T.  With splits > 1 the
 // launch writes `splits` partial products [splits][m][n] for the caller to
@@ -37,9 +44,17 @@ cudaError_t gemm_q4k_prepare();
 bool gemm_q4k_tmaps(const void* a, int64_t m, const void* w, int64_t n, int k, const GemmPlan& p, CUtensorMap* tm_a,
                     CUtensorMap* tm_w);
 // c: [p.splits][m][n] f32; row r of every part is multiplied by ascale[r]
-// (null: by 1).
+// (null: by 1).  a: the fp16 rows of A that tm_a maps (read directly by the
+// multi-row GEMV, which plans with p.rows_nt > 0; 16-byte aligned).
 cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, const float* ascale, float* c, int64_t m,
-                            int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s);
+                            int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s, const uint16_t* a);
+// The multi-row GEMV's plan for a Q4_K product with m <= kRowsMaxM (false if
+// the shape does not fit it): at most max_parts K parts (p->splits), exactly
+// force_parts if that is > 0 and fits.
+bool gemm_rows_plan(int64_t m, int64_t n, int k, int num_sms, int max_parts, int force_parts, GemmPlan* p);
+cudaError_t gemm_rows_prepare();
+cudaError_t gemm_rows_launch(const CUtensorMap& tm_w, const uint16_t* a, const float* ascale, float* c, int64_t m,
+                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s);
 // A rows for the GEMM from bf16 rows: out[r] = fp16(a[r] * 2^-e_r), scale[r] = 2^e_r.
 cudaError_t a_to_f16_launch(const uint16_t* a_bf16, int64_t m, int k, uint16_t* out, float* scale, cudaStream_t s);
 // The same from f32 rows.

@@ -17,8 +17,27 @@ def _plan(rtlib, m, n, k, bf16=False):
 
 @pytest.fixture(autouse=True)
 def _no_overrides(monkeypatch):
-    monkeypatch.delenv("RT_GEMM_TILE", raising=False)
-    monkeypatch.delenv("RT_GEMM_SPLITS", raising=False)
+    for v in ("RT_GEMM_TILE", "RT_GEMM_SPLITS", "RT_GEMM_ROWS"):
+        monkeypatch.delenv(v, raising=False)
+
+
+@pytest.mark.parametrize("m,n,k,want", [
+    # Q4_K at M <= 16: the multi-row GEMV (tile 16); one K part while the
+    # part's planes fit, since an extra part costs the pass that adds them
+    (8, 20480, 2560, (16, 1, 16, 2560)),        # 4B gate/up
+    (8, 43008, 5376, (16, 1, 16, 5376)),        # 27B gate/up
+    (1, 43008, 5376, (16, 1, 16, 5376)),
+    (3, 8192, 5376, (16, 1, 16, 5376)),         # 27B qkv, odd M
+    # long K: parts chosen to balance the CTAs' whole tiles (336 tiles over
+    # 7 x 21 CTAs), measured faster than the fewest parts
+    (8, 5376, 21504, (16, 7, 16, 3072)),        # 27B down
+    (16, 43008, 5376, (16, 3, 16, 1792)),       # 16 rows: planes of 7 segments per part
+    # M = 17: the tensor-memory kernel again
+    (17, 20480, 2560, (128, 1, 64, 2560)),
+])
+def test_rows_plan_rules(rtlib, m, n, k, want):
+    rc, got = _plan(rtlib, m, n, k)
+    assert rc == 0 and got == want, (rc, got)
 
 
 @pytest.mark.parametrize("m,n,k,bf16,want", [
@@ -36,7 +55,9 @@ def _no_overrides(monkeypatch):
     # large M: the 256 x 256 tile when it halves the waves, no split
     (2048, 20480, 2560, False, (256, 1, 128, 2560)),
 ])
-def test_plan_rules(rtlib, m, n, k, bf16, want):
+def test_plan_rules(rtlib, monkeypatch, m, n, k, bf16, want):
+    # the tensor-memory kernel's rules (RT_GEMM_ROWS=0 keeps it at M <= 16)
+    monkeypatch.setenv("RT_GEMM_ROWS", "0")
     rc, got = _plan(rtlib, m, n, k, bf16)
     assert rc == 0 and got == want, (rc, got)
 
@@ -49,6 +70,10 @@ def test_plan_rejects_k_off_the_super_block(rtlib):
 
 def test_plan_overrides(rtlib, monkeypatch):
     monkeypatch.setenv("RT_GEMM_SPLITS", "2")
-    assert _plan(rtlib, 8, 43008, 5376)[1][1] == 2
-    monkeypatch.setenv("RT_GEMM_TILE", "256")
-    assert _plan(rtlib, 8, 43008, 5376)[1][0] == 256
+    assert _plan(rtlib, 8, 43008, 5376)[1][:2] == (16, 2)   # the multi-row GEMV, 2 parts
+    monkeypatch.setenv("RT_GEMM_TILE", "256")               # a forced tile: the tcgen05 kernel
+    assert _plan(rtlib, 8, 43008, 5376)[1][:2] == (256, 2)
+    monkeypatch.delenv("RT_GEMM_TILE")
+    monkeypatch.delenv("RT_GEMM_SPLITS")
+    monkeypatch.setenv("RT_GEMM_ROWS", "0")
+    assert _plan(rtlib, 8, 43008, 5376)[1][:2] == (128, 3)
