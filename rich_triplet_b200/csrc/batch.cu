@@ -135,8 +135,8 @@ struct rt_batch {
     PeerBufs peers{};
     void* opened[kMaxRanks] = {};
     int32_t* step_ctr = nullptr;
-    uint32_t* am_send = nullptr;  // [B][kTpWords] this rank's greedy record of each row
-    uint32_t* am_recv = nullptr;  // [nranks][B][kTpWords]
+    uint32_t* am_send = nullptr;  // [slices][rows][kTpWords] this rank's greedy records of each row
+    uint32_t* am_recv = nullptr;  // [nranks][slices][rows][kTpWords]
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
@@ -366,85 +366,37 @@ cudaError_t launch_rows(void (*k)(KArgs...), int rows, int n, cudaStream_t s, Ar
     return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
-// Greedy sampling per row, with sample_token's rule at temperature 0 (the last
-// index of the largest softmax probability; see kGreedyTau in gemv_core.cuh).
-// One CTA of 1024 threads per row: each thread keeps the online state (max,
-// sum of exp(y - max), row of the max) of its strided elements; the CTA
-// combines them in a fixed order into M and S; then only threads whose own
-// maximum is within kGreedyTau of M re-read their elements for candidates.
-struct RowGreedy {
-    float M, S;
-    int best;  // highest candidate index whose probability equals the maximum's
-};
-
-__device__ __forceinline__ RowGreedy row_greedy(const float* r, int V, float* sm, float* ss, long long* si,
-                                                int* sbest) {
-    using rt::gcore::Greedy;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    Greedy g;
-    g.init();
-    for (int i = tid; i < V; i += blockDim.x) g.add(r[i], i);
-    const float my_m = g.m;
-    g.warp_merge();
-    if (lane == 0) {
-        sm[warp] = g.m;
-        ss[warp] = g.s;
-        si[warp] = g.i;
-    }
-    if (tid == 0) *sbest = -1;
-    __syncthreads();
-    Greedy c;
-    c.init();
-    for (int w = 0; w < nw; ++w) c.merge(sm[w], ss[w], si[w], 0, 0);  // every thread, same order
-    RowGreedy out;
-    out.M = c.m;
-    out.S = c.s;
-    const float q = __fdiv_rn(1.0f, c.s), lim = c.m - rt::gcore::kGreedyTau;
-    if (my_m >= lim) {
-        int best = -1;
-        for (int i = tid; i < V; i += blockDim.x) {
-            const float v = r[i];
-            if (v >= lim && rt::gcore::greedy_ties_max(v, c.m, c.s, q)) best = i;
-        }
-        if (best >= 0) atomicMax(sbest, best);
-    }
-    __syncthreads();
-    out.best = *sbest;
-    return out;
-}
-
-// Greedy token of each row, then tokens[b] = it and pos[b] += 1.
-__global__ void argmax_rows_kernel(const float* logits, int V, int32_t* tokens, int32_t* pos) {
-    __shared__ float sm[32], ss[32];
-    __shared__ long long si[32];
-    __shared__ int sbest;
-    const int b = blockIdx.x;
-    const RowGreedy g = row_greedy(logits + static_cast<int64_t>(b) * V, V, sm, ss, si, &sbest);
-    if (threadIdx.x == 0) {
-        tokens[b] = g.best;
-        pos[b] += 1;
-    }
-}
-
-// Tensor-parallel greedy: what each rank sends for a row of its vocab slice
-// [v0, v0 + V).  Words: [0] m (its largest logit, bits), [1] s (sum of
-// exp(y - m) over the slice, bits), [2] the number of its logits within
-// kGreedyTau of m, [3] unused, then up to kTpCand (value bits, vocab index)
-// pairs of those logits, highest indices first.  The merge then has every
-// candidate of the global maximum unless a rank holds more than kTpCand logits
-// within kGreedyTau of its own maximum (counted in word 2): it then decides
+// Greedy sampling (sample_token at temperature 0: the last index of the
+// largest softmax probability, see kGreedyTau in gemv_core.cuh) over rows of
+// logits split into vocab slices, each slice taken by one CTA.  The record of
+// a slice: words [0] m (its largest logit, bits), [1] s (sum of exp(y - m)
+// over the slice, bits), [2] the number of its logits within kGreedyTau of
+// m, [3] unused, then up to kTpCand (value bits, vocab index) pairs of those
+// logits, highest indices first.  The merge (argmax_merge_kernel) combines the
+// records of a row in vocab order: every candidate of the global maximum is
+// in them unless a slice holds more than kTpCand logits within kGreedyTau of
+// its own maximum (word 2).  On one GPU the merge then rescans that slice; a
+// tensor-parallel merge, whose other slices live on other ranks, decides
 // among the kTpCand highest of them.
 constexpr int kTpCand = 4;
 constexpr int kTpWords = 4 + 2 * kTpCand;
+constexpr int kGreedySlices = 32;  // vocab slices per row and rank (CTAs per row)
+constexpr int kGreedyThreads = 256;
 
-__global__ void argmax_local_kernel(const float* logits, int V, int v0, uint32_t* out) {
+// CTA (b, p) of a (rows, slices) grid: the record of columns [p W, (p + 1) W)
+// of row b of `logits` ([rows][V], this rank's vocab rows v0..v0+V).
+__global__ void __launch_bounds__(kGreedyThreads) argmax_local_kernel(const float* logits, int V, int W, int v0,
+                                                                      uint32_t* out) {
     __shared__ float sm[32], ss[32];
     __shared__ long long si[32];
     __shared__ int sbest, ncand;
     __shared__ int cand[kTpCand];
     using rt::gcore::Greedy;
-    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const float* r = logits + static_cast<int64_t>(b) * V;
+    const int b = blockIdx.x, p = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int c0 = p * W;
+    const float* r = logits + static_cast<int64_t>(b) * V + c0;
+    V = max(0, min(W, V - c0));  // this slice's columns
+    v0 += c0;
     Greedy g;
     g.init();
     for (int i = tid; i < V; i += blockDim.x) g.add(r[i], i);
@@ -490,7 +442,7 @@ __global__ void argmax_local_kernel(const float* logits, int V, int v0, uint32_t
         __syncthreads();
     }
     if (tid == 0) {
-        uint32_t* o = out + static_cast<int64_t>(b) * kTpWords;
+        uint32_t* o = out + (static_cast<int64_t>(p) * gridDim.x + b) * kTpWords;
         o[0] = __float_as_uint(c.m);
         o[1] = __float_as_uint(c.s);
         o[2] = static_cast<uint32_t>(ncand);
@@ -503,23 +455,37 @@ __global__ void argmax_local_kernel(const float* logits, int V, int v0, uint32_t
     }
 }
 
-// The greedy token of each row from every rank's record (ranks' slices in
-// vocab order): M = max m_r, S = sum_r s_r exp(m_r - M) in rank order, then
+// The greedy token of each row from its nrec slice records ([nrec][B], in
+// vocab order): M = max m_r, S = sum_r s_r exp(m_r - M) in record order, then
 // the highest candidate index whose probability equals the maximum's; then
-// tokens[b] = it and pos[b] += 1.
-__global__ void argmax_merge_kernel(const uint32_t* recs, int nranks, int B, int32_t* tokens, int32_t* pos) {
+// tokens[b] = it and pos[b] += 1.  logits != null: the records are this GPU's
+// slices of width W of logits ([B][V]), and a slice with more candidates than
+// its record holds is rescanned.
+__global__ void argmax_merge_kernel(const uint32_t* recs, int nrec, int B, int32_t* tokens, int32_t* pos,
+                                    const float* logits, int V, int W) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     auto rec = [&](int r) { return recs + (static_cast<int64_t>(r) * B + b) * kTpWords; };
     float M = -INFINITY;
-    for (int r = 0; r < nranks; ++r) M = fmaxf(M, __uint_as_float(rec(r)[0]));
+    for (int r = 0; r < nrec; ++r) M = fmaxf(M, __uint_as_float(rec(r)[0]));
     float S = 0.f;
-    for (int r = 0; r < nranks; ++r) S += __uint_as_float(rec(r)[1]) * expf(__uint_as_float(rec(r)[0]) - M);
+    for (int r = 0; r < nrec; ++r) {
+        const uint32_t* o = rec(r);
+        if (o[1] != 0u) S += __uint_as_float(o[1]) * expf(__uint_as_float(o[0]) - M);  // empty slice: s = 0, m = -inf
+    }
     const float q = __fdiv_rn(1.0f, S), lim = M - rt::gcore::kGreedyTau;
     int best = -1;
-    for (int r = 0; r < nranks; ++r) {
+    for (int r = 0; r < nrec; ++r) {
         const uint32_t* o = rec(r);
         if (__uint_as_float(o[0]) < lim) continue;
+        if (logits && o[2] > static_cast<uint32_t>(kTpCand)) {
+            const int c1 = min(V, (r + 1) * W);
+            for (int i = r * W; i < c1; ++i) {
+                const float v = logits[static_cast<int64_t>(b) * V + i];
+                if (v >= lim && i > best && rt::gcore::greedy_ties_max(v, M, S, q)) best = i;
+            }
+            continue;
+        }
         for (int k = 0; k < kTpCand; ++k) {
             const float v = __uint_as_float(o[4 + 2 * k]);
             const int i = static_cast<int>(o[5 + 2 * k]);
@@ -863,18 +829,21 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
                            t->resid[p], t->resid[1 - p], rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
                            t->xscale)) &&
             gemm(pl.lm, t->logits) && argmax) {
-            if (t->nranks == 1) {
-                argmax_rows_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->vr, t->tokens, t->pos);
+            const int W = (t->vr + kGreedySlices - 1) / kGreedySlices;
+            argmax_local_kernel<<<dim3(pl.lm_rows, kGreedySlices), kGreedyThreads, 0, s>>>(t->logits, t->vr, W, t->v0,
+                                                                                           t->am_send);
+            const unsigned mb = static_cast<unsigned>((pl.lm_rows + 127) / 128);
+            if (ok(cudaGetLastError()) && t->nranks == 1) {
+                argmax_merge_kernel<<<mb, 128, 0, s>>>(t->am_send, kGreedySlices, pl.lm_rows, t->tokens, t->pos,
+                                                       t->logits, t->vr, W);
                 ok(cudaGetLastError());
-            } else {
-                argmax_local_kernel<<<pl.lm_rows, 1024, 0, s>>>(t->logits, t->vr, t->v0, t->am_send);
-                if (ok(cudaGetLastError()) &&
-                    nccl_ok(t->nccl->all_gather(t->am_send, t->am_recv, kTpWords * static_cast<size_t>(pl.lm_rows), ncclUint32,
-                                                t->comm, s))) {
-                    argmax_merge_kernel<<<(pl.lm_rows + 127) / 128, 128, 0, s>>>(t->am_recv, t->nranks, pl.lm_rows,
-                                                                                 t->tokens, t->pos);
-                    ok(cudaGetLastError());
-                }
+            } else if (e == cudaSuccess &&
+                       nccl_ok(t->nccl->all_gather(t->am_send, t->am_recv,
+                                                   kTpWords * static_cast<size_t>(kGreedySlices) * pl.lm_rows, ncclUint32,
+                                                   t->comm, s))) {
+                argmax_merge_kernel<<<mb, 128, 0, s>>>(t->am_recv, t->nranks * kGreedySlices, pl.lm_rows, t->tokens,
+                                                       t->pos, nullptr, 0, 0);
+                ok(cudaGetLastError());
             }
         }
     }
@@ -1024,14 +993,18 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, const TpInit* tp
     RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->counters, 0, sizeof(uint32_t) * B * t->NKV, ctx->stream));
     RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->tokens, 0, sizeof(int32_t) * B, ctx->stream));
     RT_CHECK_CUDA(ctx, cudaMemsetAsync(t->pos, 0, sizeof(int32_t) * B, ctx->stream));
+    const int64_t rec_rows = std::max<int64_t>(B, t->logit_rows);  // rows a greedy pass covers
+    if ((rc = balloc(t, reinterpret_cast<void**>(&t->am_send), sizeof(uint32_t) * kTpWords * kGreedySlices * rec_rows,
+                     "greedy records")) != RT_OK)
+        return bail(rc);
     if (cudaMallocHost(reinterpret_cast<void**>(&t->h_err), sizeof(int)) != cudaSuccess) return bail(fail(ctx, RT_E_NOMEM, "pinned error word"));
     *t->h_err = 0;
     if (t->nranks > 1) {
         const char* why = nullptr;
         if (!(t->nccl = rt::nccl_api(&why))) return bail(fail(ctx, RT_E_CUDA, "tensor parallel: NCCL unavailable (%s)", why));
         if ((rc = balloc(t, reinterpret_cast<void**>(&t->ar_buf), sizeof(float) * B * t->H, "tp all-reduce buffer")) != RT_OK ||
-            (rc = balloc(t, reinterpret_cast<void**>(&t->am_send), sizeof(uint32_t) * kTpWords * B, "tp greedy records")) != RT_OK ||
-            (rc = balloc(t, reinterpret_cast<void**>(&t->am_recv), sizeof(uint32_t) * kTpWords * B * t->nranks, "tp greedy records")) != RT_OK)
+            (rc = balloc(t, reinterpret_cast<void**>(&t->am_recv), sizeof(uint32_t) * kTpWords * kGreedySlices * rec_rows * t->nranks,
+                         "tp greedy records")) != RT_OK)
             return bail(rc);
         RT_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
         const ncclResult_t nr = t->nccl->comm_init_rank(&t->comm, t->nranks, tp->id, t->rank);

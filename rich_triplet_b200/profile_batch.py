@@ -4,6 +4,10 @@ cache of `--context` positions, a few warm-up steps, then the steps to profile
 (each step is one replay of the engine's CUDA graph).
 
     python -m rich_triplet_b200.profile_batch --seqs 64 --context 4096 --warmup 3 --steps 1
+    python -m rich_triplet_b200.profile_batch --model 27b --seqs 1 --layers 62 --context 8192
+
+`--model 27b` decodes the Gemma 3 27B shapes (config 4 on one GPU: the
+tensor-parallel engine with one rank) instead of the 4B width.
 
 Prints one line with the mean step time (CUDA events) when it is done.
 """
@@ -20,6 +24,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--steps", type=int, default=1)
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--model", default="4b", choices=["4b", "27b"])
     a = ap.parse_args(argv)
 
     import torch
@@ -28,11 +33,18 @@ def main(argv=None):
     from .model import Config4, synth_gemma3
     from .ops import Context
 
-    cfg = Config4.gemma3_4b(vocab_size=262144).with_layers(a.layers)
-    w = synth_gemma3(cfg, seed=a.seed)
     ctx = Context(0)
-    dec = CudaDecodeContext(w, 16, ctx)
-    bat = CudaBatchDecoder(dec, a.seqs, a.context + a.warmup + a.steps + 1)
+    cap = a.context + a.warmup + a.steps + 1
+    if a.model == "27b":
+        from .tp import TpBatchDecoder, synth_shard_weights
+
+        cfg = Config4.gemma3_27b().with_layers(a.layers)
+        dec = CudaDecodeContext(synth_shard_weights(cfg, a.seed, 1, 0), 16, ctx)
+        bat = TpBatchDecoder(dec, a.seqs, cap, 1, 0)
+    else:
+        cfg = Config4.gemma3_4b(vocab_size=262144).with_layers(a.layers)
+        dec = CudaDecodeContext(synth_gemma3(cfg, seed=a.seed), 16, ctx)
+        bat = CudaBatchDecoder(dec, a.seqs, cap)
     bat.synth_kv(a.seed, a.context)
     bat.generate(a.warmup)
     ext = torch.cuda.ExternalStream(ctx.stream_ptr)
@@ -42,7 +54,7 @@ def main(argv=None):
     e1.record(ext)
     e1.synchronize()
     ctx.sync()
-    print(f"profile_batch: seqs={a.seqs} layers={a.layers} context={a.context} steps={a.steps} "
+    print(f"profile_batch: model={a.model} seqs={a.seqs} layers={a.layers} context={a.context} steps={a.steps} "
           f"ms_per_step={e0.elapsed_time(e1) / a.steps:.4f} at {time.strftime('%H:%M:%S')}", flush=True)
     bat.close()
     dec.close()
