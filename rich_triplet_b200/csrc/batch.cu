@@ -63,6 +63,7 @@ struct BatchGemm {
     CUtensorMap ta, tw;
     const float* ascale = nullptr;  // row scales of A
     const uint16_t* a = nullptr;    // fp16 rows of A (the multi-row GEMV reads them directly)
+    const float* a32 = nullptr;     // f32 rows of A for the multi-row GEMV (RowsPlan::f32_rows)
     int64_t m = 0, n = 0;
     int k = 0;
 };
@@ -71,6 +72,10 @@ struct BatchGemm {
 // [lm_row0, lm_row0 + lm_rows) (none if lm_rows == 0).
 struct RowsPlan {
     int m = 0, lm_row0 = 0, lm_rows = 0;
+    // Every projection runs the multi-row GEMV, which reads f32 rows: the row
+    // kernels then write f32 GEMM inputs (no fp16 row scale) and the
+    // attention output feeds the o projection as it is.
+    bool f32_rows = false;
     std::vector<BatchGemm> qkv, o, gu, down;
     BatchGemm lm;
     int64_t part_floats = 0;  // split-K outputs the plan needs
@@ -94,6 +99,7 @@ struct rt_batch {
     float* kv_v0 = nullptr;
     float* rope = nullptr;       // [2 (local, global)][2 (cos, sin)][cap][D/2] (the decoder's in rows mode)
     uint16_t* xa = nullptr;      // fp16 [B][K] input of the next GEMM, row b scaled by 1 / xscale[b]
+    float* xa32 = nullptr;       // f32 [min(B, kRowsMaxM)][K] input of the next multi-row GEMV
     float* xscale = nullptr;     // [B] power-of-two row scales of xa
     float* parts = nullptr;      // GEMM outputs [splits][rows][N]
     int64_t part_cap = 0;        // floats allocated at `parts`
@@ -234,11 +240,12 @@ __device__ __forceinline__ void store_f16_slice(const float* row, RowSlice rs, f
 //   embed != null: r = bf16(embed[tokens[b]]) * embed_scale   (src/transformer4.rs:2360-2364)
 //   else:          s = src parts added in order; r = resid_in + s * rms(s) * (1 + gpost)
 //   resid_out = r;  x = r * rms(r) * (1 + gpre)                 (rms_norm_gemma3, src/autograd2.rs:3477-3496)
-// and x goes out as an fp16 GEMM row with its scale.  Rows of H (a multiple of 4).
+// and x goes out as an fp16 GEMM row with its scale (or, out32 != null, as f32
+// for the multi-row GEMV).  Rows of H (a multiple of 4).
 __global__ void __launch_bounds__(kRowCta) resid_norm_rows_kernel(
     const uint16_t* embed, const int32_t* tokens, float embed_scale, const float* src, int src_parts,
     int64_t part_stride, const float* resid_in, float* resid_out, const float* gpost, const float* gpre, float eps, int H,
-    uint16_t* out, float* oscale) {
+    uint16_t* out, float* oscale, float* out32) {
     extern __shared__ float4 row4[];  // this CTA's slice of the row
     float* row = reinterpret_cast<float*>(row4);
     __shared__ float red[32];
@@ -291,17 +298,26 @@ __global__ void __launch_bounds__(kRowCta) resid_norm_rows_kernel(
                                      __fmul_rn(__fmul_rn(v.y, r2), __fadd_rn(1.0f, g.y)),
                                      __fmul_rn(__fmul_rn(v.z, r2), __fadd_rn(1.0f, g.z)),
                                      __fmul_rn(__fmul_rn(v.w, r2), __fadd_rn(1.0f, g.w)));
-        *reinterpret_cast<float4*>(row + (c - rs.c0)) = x;
-        mx = abs_max4(mx, x);
+        if (out32) {
+            *reinterpret_cast<float4*>(out32 + rs.base + c) = x;
+        } else {
+            *reinterpret_cast<float4*>(row + (c - rs.c0)) = x;
+            mx = abs_max4(mx, x);
+        }
+    }
+    if (out32) {
+        cg::this_cluster().sync();  // no CTA leaves while another still reads its slots
+        return;
     }
     store_f16_slice(row, rs, mx, red, &slot[2], out, oscale + b);
 }
 
 // h[b][j] = gelu_tanh(gate) * up from the interleaved gate/up GEMM output
 // (column 2j gate, 2j + 1 up), its split parts added in order; h goes out as an
-// fp16 GEMM row with its scale.  Rows of F outputs (a multiple of 4).
+// fp16 GEMM row with its scale (or, out32 != null, as f32).  Rows of F outputs
+// (a multiple of 4).
 __global__ void __launch_bounds__(kRowCta) gelu_rows_kernel(const float* c, int parts, int64_t part_stride, int F,
-                                                           uint16_t* out, float* oscale) {
+                                                           uint16_t* out, float* oscale, float* out32) {
     extern __shared__ float4 h4[];
     float* h = reinterpret_cast<float*>(h4);
     __shared__ float red[32];
@@ -317,10 +333,14 @@ __global__ void __launch_bounds__(kRowCta) gelu_rows_kernel(const float* c, int 
                                      __fmul_rn(rt::gcore::gelu_tanh_dev(a.z), a.w),
                                      __fmul_rn(rt::gcore::gelu_tanh_dev(e.x), e.y),
                                      __fmul_rn(rt::gcore::gelu_tanh_dev(e.z), e.w));
-        *reinterpret_cast<float4*>(h + (j - rs.c0)) = v;
-        mx = abs_max4(mx, v);
+        if (out32) {
+            *reinterpret_cast<float4*>(out32 + rs.base + j) = v;
+        } else {
+            *reinterpret_cast<float4*>(h + (j - rs.c0)) = v;
+            mx = abs_max4(mx, v);
+        }
     }
-    store_f16_slice(h, rs, mx, red, &slot[0], out, oscale + b);
+    if (!out32) store_f16_slice(h, rs, mx, red, &slot[0], out, oscale + b);
 }
 
 // Row b of `in` ([B][n] f32, n a multiple of 4) as an fp16 GEMM row with its
@@ -649,6 +669,15 @@ bool build_plan(rt_batch* t, int m, int lm_row0, int lm_rows, RowsPlan* pl) {
         for (const BatchGemm* g : {&pl->qkv[l], &pl->o[l], &pl->gu[l], &pl->down[l]})
             pl->part_floats = std::max<int64_t>(pl->part_floats, static_cast<int64_t>(g->p.splits) * m * g->n);
     }
+    pl->f32_rows = m <= rt::kRowsMaxM && t->xa32 != nullptr;
+    for (int l = 0; l < t->NL; ++l)
+        for (const BatchGemm* g : {&pl->qkv[l], &pl->o[l], &pl->gu[l], &pl->down[l]})
+            pl->f32_rows = pl->f32_rows && g->p.rows_nt > 0;
+    if (pl->f32_rows)
+        for (int l = 0; l < t->NL; ++l) {
+            pl->qkv[l].a32 = pl->gu[l].a32 = pl->down[l].a32 = t->xa32;
+            pl->o[l].a32 = t->attn;
+        }
     return lm_rows == 0 ||
            make_gemm(t, lm_rows, lm_row0, d->embed + static_cast<int64_t>(t->v0) * H, t->vr, H, true, false, &pl->lm);
 }
@@ -668,8 +697,10 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         return e == cudaSuccess;
     };
     auto gemm = [&](const BatchGemm& g, float* c) {
+        if (g.a32) return ok(rt::gemm_rows_launch(g.tw, nullptr, nullptr, c, g.m, g.n, g.k, g.p, t->ctx->d_err, s, g.a32));
         return ok(rt::gemm_q4k_launch(g.ta, g.tw, g.ascale, c, g.m, g.n, g.k, g.p, t->ctx->d_err, s, g.a));
     };
+    float* const x32 = pl.f32_rows ? t->xa32 : nullptr;  // the row kernels' f32 output, if any
     auto nccl_ok = [&](ncclResult_t r) { return ok(r == ncclSuccess ? cudaSuccess : cudaErrorUnknown); };
     uint32_t ar_call = 0;  // peer all-reduces of this step so far
     // A row-split projection's output as a row kernel reads it: (source,
@@ -708,12 +739,12 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         if (l == 0) {
             if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, d->embed, t->tokens, sqrtf(static_cast<float>(H)),
                                 nullptr, 0, int64_t{0}, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0), eps, H,
-                                t->xa, t->xscale)))
+                                t->xa, t->xscale, x32)))
                 break;
         } else {
             if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts,
                                 pdown.stride, t->resid[p], t->resid[1 - p], rt::norm_ptr(d, l - 1, 3),
-                                rt::norm_ptr(d, l, 0), eps, H, t->xa, t->xscale)))
+                                rt::norm_ptr(d, l, 0), eps, H, t->xa, t->xscale, x32)))
                 break;
             p = 1 - p;
         }
@@ -804,20 +835,21 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
             a.seq_out = static_cast<int64_t>(t->NQ) * D;
             if (!ok(rt::attention_launch_batch(a, B, s))) break;
         }
-        if (!ok(launch_rows(f16_rows_kernel, B, t->NQ * D, s, t->attn, t->NQ * D, t->xa, t->xscale))) break;
+        if (!pl.f32_rows && !ok(launch_rows(f16_rows_kernel, B, t->NQ * D, s, t->attn, t->NQ * D, t->xa, t->xscale)))
+            break;
         // o, then residual update + pre-FFN RMSNorm
         const Proj po = project(pl.o[l]);
         if (!po.src) break;
         if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, po.src, po.parts, po.stride,
                             t->resid[p], t->resid[1 - p], rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa,
-                            t->xscale)))
+                            t->xscale, x32)))
             break;
         p = 1 - p;
         // gate/up, GELU gate
         const BatchGemm& gg = pl.gu[l];
         if (!gemm(gg, t->parts)) break;
         if (!ok(launch_rows(gelu_rows_kernel, B, t->F, s, t->parts, gg.p.splits, static_cast<int64_t>(B) * 2 * t->F,
-                            t->F, t->xa, t->xscale)))
+                            t->F, t->xa, t->xscale, x32)))
             break;
         // down
         pdown = project(pl.down[l]);
@@ -827,7 +859,7 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         // final residual update + norm, LM head, greedy tokens
         if (ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts, pdown.stride,
                            t->resid[p], t->resid[1 - p], rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
-                           t->xscale)) &&
+                           t->xscale, static_cast<float*>(nullptr))) &&
             gemm(pl.lm, t->logits) && argmax) {
             const int W = (t->vr + kGreedySlices - 1) / kGreedySlices;
             argmax_local_kernel<<<dim3(pl.lm_rows, kGreedySlices), kGreedyThreads, 0, s>>>(t->logits, t->vr, W, t->v0,
@@ -978,6 +1010,8 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, const TpInit* tp
     const int64_t kmax = std::max<int64_t>({t->H, static_cast<int64_t>(t->NQ) * t->D, t->F});
     if ((rc = balloc(t, reinterpret_cast<void**>(&t->xa), sizeof(uint16_t) * B * kmax + 256, "batch GEMM input")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->xscale), sizeof(float) * B, "batch GEMM row scales")) != RT_OK ||
+        (rc = balloc(t, reinterpret_cast<void**>(&t->xa32), sizeof(float) * std::min<int64_t>(B, rt::kRowsMaxM) * kmax,
+                     "batch GEMM input (f32)")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->qkv), sizeof(float) * B * t->qkv_rows, "batch qkv")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->attn), sizeof(float) * B * t->NQ * t->D, "batch attention")) != RT_OK ||
         (rc = balloc(t, reinterpret_cast<void**>(&t->resid[0]), sizeof(float) * B * t->H, "batch residual")) != RT_OK ||

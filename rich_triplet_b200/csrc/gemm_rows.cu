@@ -1,6 +1,6 @@
 // gemm_rows.cu -- the Q4_K product at small M as a multi-row GEMV:
 // C[M, N] = diag(ascale) . A[M, K] . dequant(W[N, K])^T for M <= 16 rows of A
-// (fp16, a power-of-two scale per row) and a row-major Q4_K weight W, every
+// (fp16 with a power-of-two scale per row, or f32) and a row-major Q4_K weight W, every
 // weight byte streamed once and used for all M rows.  Matmul_q4k_t
 // (src/autograd2.rs:1437-1457) is the product's definition; the reference's
 // batched GEMV (gemv_q4k_t_batch, src/metal_decode.rs:460-524) computes it
@@ -56,7 +56,8 @@ constexpr int kRTilePlane = 2048;     // B-fragment bytes per segment and n8 til
 constexpr size_t kRSmemMax = 227 * 1024;
 
 struct RowsArgs {
-    const uint16_t* a;     // fp16 [m][k]
+    const uint16_t* a;     // fp16 [m][k] (when a32 is null)
+    const float* a32;      // or f32 [m][k], no row scale
     const float* ascale;   // [m] or null
     float* c;              // [parts][m][n]
     int* err;
@@ -280,9 +281,14 @@ __global__ void __launch_bounds__(kRW * 32, 1) gemm_rows_q4k_kernel(const RowsAr
     for (int task = warp; task < 4 * NT * nsp; task += kRW) {
         const int r = task % (4 * NT), s = task / (4 * NT);
         float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (r < m) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.a + static_cast<int64_t>(r) * a.k +
-                                                                 (seg0 + s) * kQ4KSegCols + lane * 8));
+        const int64_t off = static_cast<int64_t>(r) * a.k + (seg0 + s) * kQ4KSegCols + lane * 8;
+        if (r < m && a.a32) {
+            const float4 lo = __ldg(reinterpret_cast<const float4*>(a.a32 + off));
+            const float4 hi = __ldg(reinterpret_cast<const float4*>(a.a32 + off + 4));
+            xv[0] = lo.x, xv[1] = lo.y, xv[2] = lo.z, xv[3] = lo.w;
+            xv[4] = hi.x, xv[5] = hi.y, xv[6] = hi.z, xv[7] = hi.w;
+        } else if (r < m) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.a + off));
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(kRW * 32, 1) gemm_rows_q4k_kernel(const RowsAr
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         const int r = 4 * nt + t;
-        as[nt] = r < m ? (a.ascale ? a.ascale[r] : 1.f) : 0.f;
+        as[nt] = r < m ? (a.ascale && !a.a32 ? a.ascale[r] : 1.f) : 0.f;
     }
     float* cpart = a.c + static_cast<int64_t>(part) * m * n;
     auto store = [&](int r, int64_t row, float v) {
@@ -397,7 +403,7 @@ __global__ void __launch_bounds__(kRW * 32, 1) gemm_rows_q4k_kernel(const RowsAr
                 if (wstart(w + 1) <= s0) continue;  // a warp without units
                 v += S.pieces[((w * 2 + (s0 < a0 ? 1 : 0)) * 4 * NT + r) * kTile + row];
             }
-            store(r, static_cast<int64_t>(T) * kTile + row, v * (a.ascale ? a.ascale[r] : 1.f));
+            store(r, static_cast<int64_t>(T) * kTile + row, v * (a.ascale && !a.a32 ? a.ascale[r] : 1.f));
         }
     }
 }
@@ -468,11 +474,12 @@ cudaError_t gemm_rows_prepare() {
 }
 
 cudaError_t gemm_rows_launch(const CUtensorMap& tm_w, const uint16_t* a, const float* ascale, float* c, int64_t m,
-                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s) {
-    if (!a || p.rows_nt == 0 || m < 1 || m > kRowsMaxM || (reinterpret_cast<uintptr_t>(a) & 15))
-        return cudaErrorInvalidValue;
+                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s, const float* a32) {
+    const uintptr_t src = a32 ? reinterpret_cast<uintptr_t>(a32) : reinterpret_cast<uintptr_t>(a);
+    if (!src || p.rows_nt == 0 || m < 1 || m > kRowsMaxM || (src & 15)) return cudaErrorInvalidValue;
     RowsArgs ra;
     ra.a = a;
+    ra.a32 = a32;
     ra.ascale = ascale;
     ra.c = c;
     ra.err = err;
