@@ -845,12 +845,18 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
                             t->xscale, x32)))
             break;
         p = 1 - p;
-        // gate/up, GELU gate
+        // gate/up, GELU gate (in the multi-row GEMV's epilogue when K is one part)
         const BatchGemm& gg = pl.gu[l];
-        if (!gemm(gg, t->parts)) break;
-        if (!ok(launch_rows(gelu_rows_kernel, B, t->F, s, t->parts, gg.p.splits, static_cast<int64_t>(B) * 2 * t->F,
-                            t->F, t->xa, t->xscale, x32)))
-            break;
+        if (gg.a32 && gg.p.splits == 1) {
+            if (!ok(rt::gemm_rows_launch(gg.tw, nullptr, nullptr, t->xa32, gg.m, gg.n, gg.k, gg.p, t->ctx->d_err, s,
+                                         gg.a32, rt::kRowsEpiGelu)))
+                break;
+        } else {
+            if (!gemm(gg, t->parts)) break;
+            if (!ok(launch_rows(gelu_rows_kernel, B, t->F, s, t->parts, gg.p.splits, static_cast<int64_t>(B) * 2 * t->F,
+                                t->F, t->xa, t->xscale, x32)))
+                break;
+        }
         // down
         pdown = project(pl.down[l]);
         if (!pdown.src) break;

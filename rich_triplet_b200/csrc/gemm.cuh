@@ -53,9 +53,14 @@ cudaError_t gemm_q4k_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_w, co
 // force_parts if that is > 0 and fits.
 bool gemm_rows_plan(int64_t m, int64_t n, int k, int num_sms, int max_parts, int force_parts, GemmPlan* p);
 cudaError_t gemm_rows_prepare();
+// Epilogues of the multi-row GEMV: C as computed, or (one K part, n even) the
+// GELU gate of interleaved gate/up rows, c[r][j] = gelu_tanh(C[r][2j]) * C[r][2j+1]
+// ([m][n / 2]).
+constexpr int kRowsEpiPlain = 0, kRowsEpiGelu = 1;
 // a32 != null: A is f32 rows [m][k] (no row scale; a and ascale unused).
 cudaError_t gemm_rows_launch(const CUtensorMap& tm_w, const uint16_t* a, const float* ascale, float* c, int64_t m,
-                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s, const float* a32 = nullptr);
+                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s, const float* a32 = nullptr,
+                             int epi = kRowsEpiPlain);
 // A rows for the GEMM from bf16 rows: out[r] = fp16(a[r] * 2^-e_r), scale[r] = 2^e_r.
 cudaError_t a_to_f16_launch(const uint16_t* a_bf16, int64_t m, int k, uint16_t* out, float* scale, cudaStream_t s);
 // The same from f32 rows.

@@ -234,7 +234,7 @@ __device__ __forceinline__ void rows_unit(const uint8_t* ub, const uint8_t* pl, 
     }
 }
 
-template <int NT>
+template <int NT, int EPI>
 __global__ void __launch_bounds__(kRW * 32, 1) gemm_rows_q4k_kernel(const RowsArgs a, const __grid_constant__ CUtensorMap tmw) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t{127});
@@ -310,8 +310,14 @@ __global__ void __launch_bounds__(kRW * 32, 1) gemm_rows_q4k_kernel(const RowsAr
         as[nt] = r < m ? (a.ascale && !a.a32 ? a.ascale[r] : 1.f) : 0.f;
     }
     float* cpart = a.c + static_cast<int64_t>(part) * m * n;
+    constexpr bool gelu = EPI == kRowsEpiGelu;
     auto store = [&](int r, int64_t row, float v) {
         if (r < m && row < n) cpart[static_cast<int64_t>(r) * n + row] = v;
+    };
+    // GELU gate: weight rows 2j (gate) and 2j + 1 (up) give output column j
+    // (src/autograd2.rs:3082-3091, the product not contracted into an FMA).
+    auto store_h = [&](int r, int64_t row, float gate, float up) {
+        if (r < m && row + 1 < n) cpart[static_cast<int64_t>(r) * (n >> 1) + (row >> 1)] = __fmul_rn(gelu_tanh_dev(gate), up);
     };
     float acc[NT][2];
 #pragma unroll
@@ -348,8 +354,17 @@ __global__ void __launch_bounds__(kRW * 32, 1) gemm_rows_q4k_kernel(const RowsAr
             if (pu == nsp) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    store(4 * nt + t, row0, acc[nt][0] * as[nt]);
-                    store(4 * nt + t, row0 + 8, acc[nt][1] * as[nt]);
+                    const float v0 = acc[nt][0] * as[nt], v1 = acc[nt][1] * as[nt];
+                    if constexpr (gelu) {  // the up row of a pair sits in lane + 4 (g + 1)
+                        const float u0 = __shfl_down_sync(0xffffffffu, v0, 4), u1 = __shfl_down_sync(0xffffffffu, v1, 4);
+                        if (!(g & 1)) {
+                            store_h(4 * nt + t, row0, v0, u0);
+                            store_h(4 * nt + t, row0 + 8, v1, u1);
+                        }
+                    } else {
+                        store(4 * nt + t, row0, v0);
+                        store(4 * nt + t, row0 + 8, v1);
+                    }
                 }
             } else {
                 float* pc = S.pieces + (warp * 2 + (tl == first_tile ? 0 : 1)) * 4 * NT * kTile;
@@ -393,17 +408,22 @@ __global__ void __launch_bounds__(kRW * 32, 1) gemm_rows_q4k_kernel(const RowsAr
         const uint32_t a0 = (T - tb) * nsp, a1 = a0 + nsp - 1;
         const uint32_t wa = owner(a0), wb = owner(a1);
         if (wa == wb) continue;  // one warp had the whole tile: already stored
-#pragma unroll 1
-        for (int idx = lane; idx < 4 * NT * kTile; idx += 32) {
-            const int r = idx / kTile, row = idx - r * kTile;
-            if (r >= m) continue;
+        auto piece_sum = [&](int r, int row) {
             float v = 0.f;
             for (uint32_t w = wa; w <= wb; ++w) {
                 const uint32_t s0 = wstart(w);
                 if (wstart(w + 1) <= s0) continue;  // a warp without units
                 v += S.pieces[((w * 2 + (s0 < a0 ? 1 : 0)) * 4 * NT + r) * kTile + row];
             }
-            store(r, static_cast<int64_t>(T) * kTile + row, v * (a.ascale && !a.a32 ? a.ascale[r] : 1.f));
+            return v * (a.ascale && !a.a32 ? a.ascale[r] : 1.f);
+        };
+        const int per = gelu ? 2 : 1;  // rows per output
+#pragma unroll 1
+        for (int idx = lane; idx < 4 * NT * kTile / per; idx += 32) {
+            const int r = idx / (kTile / per), row = (idx - r * (kTile / per)) * per;
+            if (r >= m) continue;
+            if constexpr (gelu) store_h(r, static_cast<int64_t>(T) * kTile + row, piece_sum(r, row), piece_sum(r, row + 1));
+            else store(r, static_cast<int64_t>(T) * kTile + row, piece_sum(r, row));
         }
     }
 }
@@ -465,18 +485,24 @@ bool gemm_rows_plan(int64_t m, int64_t n, int k, int num_sms, int max_parts, int
 }
 
 cudaError_t gemm_rows_prepare() {
-    cudaError_t e = cudaFuncSetAttribute(gemm_rows_q4k_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmemMax);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_rows_q4k_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmemMax);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_rows_q4k_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmemMax);
+    cudaError_t e = cudaSuccess;
+    auto set = [&](auto kernel) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmemMax);
+    };
+    set(gemm_rows_q4k_kernel<1, kRowsEpiPlain>);
+    set(gemm_rows_q4k_kernel<2, kRowsEpiPlain>);
+    set(gemm_rows_q4k_kernel<4, kRowsEpiPlain>);
+    set(gemm_rows_q4k_kernel<1, kRowsEpiGelu>);
+    set(gemm_rows_q4k_kernel<2, kRowsEpiGelu>);
+    set(gemm_rows_q4k_kernel<4, kRowsEpiGelu>);
     return e;
 }
 
 cudaError_t gemm_rows_launch(const CUtensorMap& tm_w, const uint16_t* a, const float* ascale, float* c, int64_t m,
-                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s, const float* a32) {
+                             int64_t n, int k, const GemmPlan& p, int* err, cudaStream_t s, const float* a32, int epi) {
     const uintptr_t src = a32 ? reinterpret_cast<uintptr_t>(a32) : reinterpret_cast<uintptr_t>(a);
     if (!src || p.rows_nt == 0 || m < 1 || m > kRowsMaxM || (src & 15)) return cudaErrorInvalidValue;
+    if (epi == kRowsEpiGelu && (p.splits != 1 || (n & 1))) return cudaErrorInvalidValue;
     RowsArgs ra;
     ra.a = a;
     ra.a32 = a32;
@@ -492,10 +518,13 @@ cudaError_t gemm_rows_launch(const CUtensorMap& tm_w, const uint16_t* a, const f
     ra.cpp = p.rows_cpp;
     ra.nb = p.rows_nb;
     const dim3 block(kRW * 32);
-    if (p.rows_nt == 1) gemm_rows_q4k_kernel<1><<<p.grid, block, p.smem, s>>>(ra, tm_w);
-    else if (p.rows_nt == 2) gemm_rows_q4k_kernel<2><<<p.grid, block, p.smem, s>>>(ra, tm_w);
-    else if (p.rows_nt == 4) gemm_rows_q4k_kernel<4><<<p.grid, block, p.smem, s>>>(ra, tm_w);
+#define RT_ROWS_LAUNCH(NTT, EP) gemm_rows_q4k_kernel<NTT, EP><<<p.grid, block, p.smem, s>>>(ra, tm_w)
+    const bool g = epi == kRowsEpiGelu;
+    if (p.rows_nt == 1) g ? RT_ROWS_LAUNCH(1, kRowsEpiGelu) : RT_ROWS_LAUNCH(1, kRowsEpiPlain);
+    else if (p.rows_nt == 2) g ? RT_ROWS_LAUNCH(2, kRowsEpiGelu) : RT_ROWS_LAUNCH(2, kRowsEpiPlain);
+    else if (p.rows_nt == 4) g ? RT_ROWS_LAUNCH(4, kRowsEpiGelu) : RT_ROWS_LAUNCH(4, kRowsEpiPlain);
     else return cudaErrorInvalidValue;
+#undef RT_ROWS_LAUNCH
     return cudaGetLastError();
 }
 
