@@ -405,6 +405,7 @@ constexpr int kGreedyThreads = 256;
 
 // CTA (b, p) of a (rows, slices) grid: the record of columns [p W, (p + 1) W)
 // of row b of `logits` ([rows][V], this rank's vocab rows v0..v0+V).
+// Launched with kGreedyThreads threads.
 __global__ void __launch_bounds__(kGreedyThreads) argmax_local_kernel(const float* logits, int V, int W, int v0,
                                                                       uint32_t* out) {
     __shared__ float sm[32], ss[32];
@@ -419,7 +420,20 @@ __global__ void __launch_bounds__(kGreedyThreads) argmax_local_kernel(const floa
     v0 += c0;
     Greedy g;
     g.init();
-    for (int i = tid; i < V; i += blockDim.x) g.add(r[i], i);
+    // This thread's elements tid, tid + 256, ... in order, loaded 8 at a time
+    // ahead of the (branchy) state updates.
+    constexpr int kBatch = 8;
+    for (int i0 = tid; i0 < V; i0 += kBatch * kGreedyThreads) {
+        float v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int i = i0 + j * kGreedyThreads;
+            v[j] = i < V ? r[i] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j)
+            if (i0 + j * kGreedyThreads < V) g.add(v[j], i0 + j * kGreedyThreads);
+    }
     const float my_m = g.m;
     g.warp_merge();
     if (lane == 0) {
@@ -443,11 +457,22 @@ __global__ void __launch_bounds__(kGreedyThreads) argmax_local_kernel(const floa
     for (int k = 0; k < kTpCand; ++k) {
         int best = -1, cnt = 0;
         if (my_m >= lim)
-            for (int i = tid; i < V; i += blockDim.x)
-                if (r[i] >= lim) {
-                    if (i < below) best = i;
-                    ++cnt;
+            for (int i0 = tid; i0 < V; i0 += kBatch * kGreedyThreads) {
+                float v[kBatch];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int i = i0 + j * kGreedyThreads;
+                    v[j] = i < V ? r[i] : -INFINITY;
                 }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int i = i0 + j * kGreedyThreads;
+                    if (v[j] >= lim) {
+                        if (i < below) best = i;
+                        ++cnt;
+                    }
+                }
+            }
         if (best >= 0) atomicMax(&sbest, best);
         if (k == 0 && cnt) atomicAdd(&ncand, cnt);
         __syncthreads();
