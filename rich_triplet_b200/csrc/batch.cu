@@ -169,6 +169,7 @@ constexpr int kRowCta = 256;
 struct RowSlice {
     int64_t base;  // row start (elements)
     int c0, c1;    // this CTA's columns
+    int chunk;     // columns per CTA (the dynamic shared memory holds multiples of it)
 };
 
 __device__ __forceinline__ RowSlice row_slice(int n) {
@@ -176,7 +177,7 @@ __device__ __forceinline__ RowSlice row_slice(int n) {
     const int q = static_cast<int>(cl.block_rank()), csize = static_cast<int>(cl.num_blocks());
     const int chunk = (n + 4 * csize - 1) / (4 * csize) * 4;
     const int b = blockIdx.x / csize;
-    return RowSlice{static_cast<int64_t>(b) * n, min(n, q * chunk), min(n, (q + 1) * chunk)};
+    return RowSlice{static_cast<int64_t>(b) * n, min(n, q * chunk), min(n, (q + 1) * chunk), chunk};
 }
 
 // Sum (kMax false) or maximum (kMax true) of v over the cluster's threads.
@@ -246,11 +247,16 @@ __global__ void __launch_bounds__(kRowCta) resid_norm_rows_kernel(
     const uint16_t* embed, const int32_t* tokens, float embed_scale, const float* src, int src_parts,
     int64_t part_stride, const float* resid_in, float* resid_out, const float* gpost, const float* gpre, float eps, int H,
     uint16_t* out, float* oscale, float* out32) {
-    extern __shared__ float4 row4[];  // this CTA's slice of the row
+    // This CTA's slice of the row, then of resid_in, gpost and gpre: every
+    // global load is issued in the first pass, before the first reduction.
+    extern __shared__ float4 row4[];
     float* row = reinterpret_cast<float*>(row4);
     __shared__ float red[32];
     __shared__ float slot[4];
     const RowSlice rs = row_slice(H);
+    float* rin = row + rs.chunk;
+    float* gpo = rin + rs.chunk;
+    float* gpr = gpo + rs.chunk;
     const int b = static_cast<int>(rs.base / H), tid = threadIdx.x, step = 4 * blockDim.x;
     const float inv_d = 1.0f / static_cast<float>(H);
     float ss = 0.f;
@@ -263,13 +269,20 @@ __global__ void __launch_bounds__(kRowCta) resid_norm_rows_kernel(
                                          __fmul_rn(rt::bf16_bits_to_f32(raw.y & 0xFFFFu), embed_scale),
                                          __fmul_rn(rt::bf16_bits_to_f32(raw.y >> 16), embed_scale));
             *reinterpret_cast<float4*>(row + (c - rs.c0)) = v;
+            *reinterpret_cast<float4*>(gpr + (c - rs.c0)) = *reinterpret_cast<const float4*>(gpre + c);
             *reinterpret_cast<float4*>(resid_out + rs.base + c) = v;
             ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
     } else {
         for (int c = rs.c0 + 4 * tid; c < rs.c1; c += step) {
             const float4 v = ld_parts4(src, src_parts, part_stride, rs.base + c);
+            const float4 ri = *reinterpret_cast<const float4*>(resid_in + rs.base + c);
+            const float4 g1 = *reinterpret_cast<const float4*>(gpost + c);
+            const float4 g2 = *reinterpret_cast<const float4*>(gpre + c);
             *reinterpret_cast<float4*>(row + (c - rs.c0)) = v;
+            *reinterpret_cast<float4*>(rin + (c - rs.c0)) = ri;
+            *reinterpret_cast<float4*>(gpo + (c - rs.c0)) = g1;
+            *reinterpret_cast<float4*>(gpr + (c - rs.c0)) = g2;
             ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
         ss = cluster_reduce<false>(ss, red, &slot[0]);
@@ -277,8 +290,8 @@ __global__ void __launch_bounds__(kRowCta) resid_norm_rows_kernel(
         ss = 0.f;
         for (int c = rs.c0 + 4 * tid; c < rs.c1; c += step) {
             const float4 v = *reinterpret_cast<const float4*>(row + (c - rs.c0));
-            const float4 ri = *reinterpret_cast<const float4*>(resid_in + rs.base + c);
-            const float4 g = *reinterpret_cast<const float4*>(gpost + c);
+            const float4 ri = *reinterpret_cast<const float4*>(rin + (c - rs.c0));
+            const float4 g = *reinterpret_cast<const float4*>(gpo + (c - rs.c0));
             const float4 nv = make_float4(__fadd_rn(ri.x, __fmul_rn(__fmul_rn(v.x, r1), __fadd_rn(1.0f, g.x))),
                                           __fadd_rn(ri.y, __fmul_rn(__fmul_rn(v.y, r1), __fadd_rn(1.0f, g.y))),
                                           __fadd_rn(ri.z, __fmul_rn(__fmul_rn(v.z, r1), __fadd_rn(1.0f, g.z))),
@@ -293,7 +306,7 @@ __global__ void __launch_bounds__(kRowCta) resid_norm_rows_kernel(
     float mx = 0.f;
     for (int c = rs.c0 + 4 * tid; c < rs.c1; c += step) {
         const float4 v = *reinterpret_cast<const float4*>(row + (c - rs.c0));
-        const float4 g = *reinterpret_cast<const float4*>(gpre + c);
+        const float4 g = *reinterpret_cast<const float4*>(gpr + (c - rs.c0));
         const float4 x = make_float4(__fmul_rn(__fmul_rn(v.x, r2), __fadd_rn(1.0f, g.x)),
                                      __fmul_rn(__fmul_rn(v.y, r2), __fadd_rn(1.0f, g.y)),
                                      __fmul_rn(__fmul_rn(v.z, r2), __fadd_rn(1.0f, g.z)),
@@ -368,13 +381,15 @@ int row_cluster(int rows, int n) {
     return cl;
 }
 
-template <typename... KArgs, typename... Args>
+// kSlices: how many chunk-sized float arrays the kernel keeps in dynamic
+// shared memory.
+template <int kSlices = 1, typename... KArgs, typename... Args>
 cudaError_t launch_rows(void (*k)(KArgs...), int rows, int n, cudaStream_t s, Args... args) {
     const int cl = row_cluster(rows, n);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(rows * cl));
     cfg.blockDim = dim3(kRowCta);
-    cfg.dynamicSmemBytes = sizeof(float) * ((n + 4 * cl - 1) / (4 * cl) * 4);
+    cfg.dynamicSmemBytes = sizeof(float) * kSlices * ((n + 4 * cl - 1) / (4 * cl) * 4);
     cfg.stream = s;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -762,12 +777,12 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
     for (int l = 0; l < t->NL && e == cudaSuccess; ++l) {
         // residual update (or embedding) + attention RMSNorm -> x
         if (l == 0) {
-            if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, d->embed, t->tokens, sqrtf(static_cast<float>(H)),
+            if (!ok(launch_rows<4>(resid_norm_rows_kernel, B, H, s, d->embed, t->tokens, sqrtf(static_cast<float>(H)),
                                 nullptr, 0, int64_t{0}, nullptr, t->resid[0], nullptr, rt::norm_ptr(d, 0, 0), eps, H,
                                 t->xa, t->xscale, x32)))
                 break;
         } else {
-            if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts,
+            if (!ok(launch_rows<4>(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts,
                                 pdown.stride, t->resid[p], t->resid[1 - p], rt::norm_ptr(d, l - 1, 3),
                                 rt::norm_ptr(d, l, 0), eps, H, t->xa, t->xscale, x32)))
                 break;
@@ -865,7 +880,7 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
         // o, then residual update + pre-FFN RMSNorm
         const Proj po = project(pl.o[l]);
         if (!po.src) break;
-        if (!ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, po.src, po.parts, po.stride,
+        if (!ok(launch_rows<4>(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, po.src, po.parts, po.stride,
                             t->resid[p], t->resid[1 - p], rt::norm_ptr(d, l, 1), rt::norm_ptr(d, l, 2), eps, H, t->xa,
                             t->xscale, x32)))
             break;
@@ -888,7 +903,7 @@ cudaError_t enqueue(rt_batch* t, const RowsPlan& pl, cudaStream_t s, bool argmax
     }
     if (e == cudaSuccess && pl.lm_rows > 0) {
         // final residual update + norm, LM head, greedy tokens
-        if (ok(launch_rows(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts, pdown.stride,
+        if (ok(launch_rows<4>(resid_norm_rows_kernel, B, H, s, nullptr, nullptr, 0.f, pdown.src, pdown.parts, pdown.stride,
                            t->resid[p], t->resid[1 - p], rt::norm_ptr(d, t->NL - 1, 3), d->final_norm, eps, H, t->xa,
                            t->xscale, static_cast<float*>(nullptr))) &&
             gemm(pl.lm, t->logits) && argmax) {
@@ -1086,7 +1101,7 @@ int create_engine(rt_dec* d, int rows, int cap, bool rows_mode, const TpInit* tp
                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) == cudaSuccess;
     };
     if (!smem_limit(gelu_rows_kernel, sizeof(float) * t->F) || !smem_limit(f16_rows_kernel, sizeof(float) * t->NQ * t->D) ||
-        !smem_limit(resid_norm_rows_kernel, sizeof(float) * t->H))
+        !smem_limit(resid_norm_rows_kernel, sizeof(float) * 4 * t->H))
         return bail(fail(ctx, RT_E_CUDA, "batch engine: row kernel attributes"));
     if (!rows_mode) {
         // the step's GEMM plans and tensor maps (A is xa, read as [B][K]), then its capture
