@@ -1034,7 +1034,6 @@ __device__ __forceinline__ float q4k_unit_value(const uint8_t* ub, const uint8_t
     int acc[4][4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0;
         uint32_t a0, a1, a2, a3;
         ldsm_x4(ub + ldsm_off + 32 * c, a0, a1, a2, a3);
         const uint32_t l0 = a0 & 0x0F0F0F0Fu, l1 = a1 & 0x0F0F0F0Fu, l2 = a2 & 0x0F0F0F0Fu, l3 = a3 & 0x0F0F0F0Fu;
@@ -1042,7 +1041,7 @@ __device__ __forceinline__ float q4k_unit_value(const uint8_t* ub, const uint8_t
         const uint32_t lw1 = c == 0 ? L0.y : c == 1 ? L0.w : c == 2 ? L1.y : L1.w;
         const uint32_t hw0 = c == 0 ? H0.x : c == 1 ? H0.z : c == 2 ? H1.x : H1.z;
         const uint32_t hw1 = c == 0 ? H0.y : c == 1 ? H0.w : c == 2 ? H1.y : H1.w;
-        mma_u8s8(acc[c], l0, l1, l2, l3, lw0, lw1);
+        mma_u8s8_z(acc[c], l0, l1, l2, l3, lw0, lw1);
         mma_u8s8(acc[c], sub_on_fma(a0, l0), sub_on_fma(a1, l1), sub_on_fma(a2, l2), sub_on_fma(a3, l3), hw0, hw1);
     }
     // Lane t even holds (p0, p1) of rows g and g+8, its odd neighbour (p2, 0).
