@@ -141,10 +141,14 @@ int rt_gemv_bf16_argmax_static(const void* w_dev, int64_t rows, int cols, const 
  * (src/autograd2.rs:1437-1457) and matmul_q4k_t_exact (:1507-1625).  A is bf16
  * row-major [m, K] (uint16 bits), C is f32 row-major [m, N].  flags RT_HOST:
  * host A and C, the call copies and waits; RT_DEVICE: device pointers (16-byte
- * aligned), enqueued on the context stream.  The tensor cores take fp16: each
- * row of A is scaled by a power of two into fp16's range (exact for bf16
- * input), each dequantised weight is rounded to fp16 (relative error <= 2^-11),
- * and the scale is undone on the f32 result. */
+ * aligned), enqueued on the context stream.  For m > 16 the tensor cores take
+ * fp16: each row of A is scaled by a power of two into fp16's range (exact for
+ * bf16 input), each dequantised weight is rounded to fp16 (relative error <=
+ * 2^-11), and the scale is undone on the f32 result.  For m <= 16 a multi-row
+ * GEMV streams W once for all rows: the fp16 rows of A are split into two int8
+ * planes per 256 columns (error <= 1.6e-5 of the segment's largest magnitude)
+ * and multiplied by the exact Q4_K weights (relative L2 about 3e-5 against
+ * the exact product of those fp16 rows). */
 int rt_gemm_q4k(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c, int flags);
 /* The same product for a BF16 weight W [N, K] (K a multiple of 256), such as
  * the tied LM head over several sequences' final hidden states: replaces
@@ -154,19 +158,21 @@ int rt_gemm_bf16(rt_ctx* ctx, const rt_w* w, const void* a, int64_t m, float* c,
  * [out, in]: y[t, out] = x[t, in] . dequant(W)^T + bias (add_bias_rows,
  * src/qlinear.rs:49-61), x and y f32 row-major, bias f32 [out] or NULL.
  * t == 1 runs the GEMV (x split into three int8 planes: f32-level accuracy);
- * t > 1 the tensor-core GEMM of rt_gemm_q4k / rt_gemm_bf16 with fp16 operands
- * (rows of x scaled by powers of two into fp16's range; relative error about
- * 1e-4).  flags RT_HOST: host x, bias and y, the call copies and waits;
+ * t > 1 the product of rt_gemm_q4k / rt_gemm_bf16 over fp16 rows of x (scaled
+ * by powers of two into fp16's range; relative error about 1e-4), on the
+ * multi-row GEMV for Q4_K weights and t <= 16, else on the tensor cores.  flags RT_HOST: host x, bias and y, the call copies and waits;
  * RT_DEVICE: device pointers (x and y 16-byte aligned), enqueued on the
  * context stream.  RT_E_FORMAT for other weight formats. */
 int rt_qlinear_forward(rt_ctx* ctx, const rt_w* w, const float* x, int64_t t, const float* bias, float* y, int flags);
 /* The launch plan rt_gemm_q4k / rt_gemm_bf16 (and the many-sequence engines)
  * choose for an [m, k] x [n, k]^T product on a GPU with num_sms SMs, without
- * a GPU (no counterpart in the reference): out[0] the CTA tile (128: weight
- * rows as the 128-row operand, activations as the narrow one when m <= 64;
- * 256: 256 x 256), out[1] the split-K count, out[2] the activation rows per
- * tile, out[3] the K columns per split.  RT_E_SHAPE when no plan exists.
- * The RT_GEMM_TILE / RT_GEMM_SPLITS tuning overrides apply. */
+ * a GPU (no counterpart in the reference): out[0] the CTA tile (16: the
+ * multi-row GEMV, Q4_K weights at m <= 16; 128: weight rows as the 128-row
+ * operand, activations as the narrow one when m <= 64; 256: 256 x 256),
+ * out[1] the split-K count (the multi-row GEMV's K parts), out[2] the
+ * activation rows per tile, out[3] the K columns per split.  RT_E_SHAPE when
+ * no plan exists.  The RT_GEMM_TILE / RT_GEMM_SPLITS / RT_GEMM_ROWS tuning
+ * overrides apply. */
 int rt_gemm_plan(int64_t m, int64_t n, int32_t k, int32_t num_sms, int32_t bf16_weights, int32_t* out);
 
 /* GEMV throughput measurement (no counterpart in the reference, whose GEMV

@@ -5,8 +5,9 @@ HBM.
 The weight is [out_features, in_features] (PyTorch's Linear.weight layout) in
 one of the formats the reference's QLinear loads; forward is x[T, in] ->
 x . W^T + bias, through rt_qlinear_forward: one row runs the GEMV (f32-level
-accuracy), several rows the tensor-core GEMM (fp16 operands, relative error
-about 1e-4).  Q4_K (matmul_q4k_t_exact) and BF16 (matmul_by_t) weights are
+accuracy), several rows the product over fp16 rows of x (relative error about
+1e-4): the multi-row GEMV for a Q4_K weight and up to 16 rows, else the
+tensor-core GEMM.  Q4_K (matmul_q4k_t_exact) and BF16 (matmul_by_t) weights are
 supported; the f32 format of the reference (its small VAE layers) is not on
 this path and is refused.
 """
