@@ -367,6 +367,70 @@ int rt_test_peer_allreduce_lonely(rt_ctx* ctx, int* err_word, float* first_ms, f
 int rt_batch_synth_kv(rt_batch* batch, uint64_t seed, int32_t seq_len);
 int rt_batch_info(const rt_batch* batch, uint64_t* bytes, int32_t* launches_per_step);
 
+/* ---- Qwen 3.5 decode engine ------------------------------------------- */
+
+typedef struct rt_qwen35 rt_qwen35; /* a Qwen 3.5 hybrid DeltaNet / attention decode engine */
+
+/* ConfigQwen35 (src/transformer_qwen35.rs:32-151).  Layer i is full
+ * attention iff (i + 1) % full_attention_interval == 0 (:133-135), else Gated
+ * DeltaNet.  rope_dim = head_dim * partial_rotary_factor (:144-146). */
+typedef struct {
+    int32_t vocab_size;
+    int32_t hidden_size;             /* multiple of 256 */
+    int32_t num_hidden_layers;
+    int32_t num_attention_heads;     /* full-attention query heads */
+    int32_t num_key_value_heads;
+    int32_t head_dim;                /* <= 512 */
+    int32_t linear_num_key_heads;    /* DeltaNet */
+    int32_t linear_num_value_heads;  /* a multiple of linear_num_key_heads */
+    int32_t linear_key_head_dim;     /* <= 256 */
+    int32_t linear_value_head_dim;   /* divides 256 */
+    int32_t linear_conv_kernel_dim;
+    int32_t intermediate_size;       /* multiple of 256 */
+    int32_t full_attention_interval;
+    int32_t rope_dim;
+    float rms_norm_eps;
+    float rope_theta;
+} rt_qwen35_cfg;
+
+/* One Qwen35Block's weights (src/transformer_qwen35.rs:262-284, 622-634,
+ * 849-853, 881-886).  Projections are Q4_K rt_w handles [out, in] already in
+ * HBM (the engine copies them into its fused layout, so they may be freed
+ * afterwards); vectors are host f32.  input_norm / post_attn_norm / q_norm /
+ * k_norm hold gamma as (1 + gamma) applies it; norm_weight is the DeltaNet
+ * output norm's weight, applied as it is.  The DeltaNet fields are read on
+ * DeltaNet layers, q/k/v/o/q_norm/k_norm on full-attention layers. */
+typedef struct {
+    const rt_w *gate, *up, *down;                                /* [F, H], [F, H], [H, F] */
+    const float *input_norm, *post_attn_norm;                   /* [H] */
+    const rt_w *in_qkv, *in_z, *in_a, *in_b, *out_proj;         /* [2 nk kd + nv vd, H], [nv vd, H], [nv, H] x 2, [H, nv vd] */
+    const float *conv1d_weight;                                 /* [2 nk kd + nv vd][conv_kernel] */
+    const float *a_log, *dt_bias;                               /* [nv] */
+    const float *norm_weight;                                   /* [vd] */
+    const rt_w *q, *k, *v, *o;  /* q: [nq * 2 head_dim, H] (each head's query then its gate), k/v: [nkv head_dim, H], o: [H, nq head_dim] */
+    const float *q_norm, *k_norm;                               /* [head_dim] */
+} rt_qwen35_layer;
+
+/* Build the engine: fuse each layer's projections that share an input into
+ * one Q4_K matrix, upload the vectors, allocate the DeltaNet states (zero),
+ * the conv1d histories and an f32 K/V cache of max_tokens positions per
+ * full-attention layer.  `embed` is the BF16 [vocab, hidden] embedding, tied
+ * with the LM head; the caller keeps it alive while the engine exists.
+ * Replaces MetalDecodeContextQwen35::new (src/metal_decode_qwen35.rs). */
+int rt_qwen35_create(rt_ctx* ctx, const rt_qwen35_cfg* cfg, const rt_qwen35_layer* layers, const rt_w* embed,
+                     const float* final_norm, int32_t max_tokens, rt_qwen35** out);
+void rt_qwen35_destroy(rt_qwen35* eng);
+/* Zero every DeltaNet state and conv1d history (a new sequence; the K/V
+ * caches are overwritten position by position). */
+int rt_qwen35_reset(rt_qwen35* eng);
+/* One token at `position` (the cached sequence length): every layer's
+ * forward_cached, the final norm and the LM head; vocab_size f32 logits to
+ * host `logits` (may be NULL).  The Qwen35Model decode loop's CPU step
+ * (src/transformer_qwen35.rs:1124-1133) and MetalDecodeContextQwen35::decode_step. */
+int rt_qwen35_step(rt_qwen35* eng, int32_t token, int32_t position, float* logits);
+/* The device address of the last step's logits ([vocab_size] f32). */
+int rt_qwen35_logits_device(rt_qwen35* eng, const float** out);
+
 /* ---- synthetic inputs ---------------------------------------------------
  * Deterministic, counter-based (SplitMix64) generators for benchmarks and
  * tests; the same (seed, stream) always gives the same bytes, independent of

@@ -66,6 +66,21 @@ class RtGemma3Layer(ctypes.Structure):
                                                "q_norm", "k_norm")]
 
 
+class RtQwen35Cfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("vocab_size", "hidden_size", "num_hidden_layers", "num_attention_heads",
+                                              "num_key_value_heads", "head_dim", "linear_num_key_heads",
+                                              "linear_num_value_heads", "linear_key_head_dim", "linear_value_head_dim",
+                                              "linear_conv_kernel_dim", "intermediate_size",
+                                              "full_attention_interval", "rope_dim")] + \
+               [("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)]
+
+
+class RtQwen35Layer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("gate", "up", "down", "input_norm", "post_attn_norm", "in_qkv", "in_z",
+                                               "in_a", "in_b", "out_proj", "conv1d_weight", "a_log", "dt_bias",
+                                               "norm_weight", "q", "k", "v", "o", "q_norm", "k_norm")]
+
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -112,6 +127,12 @@ SIGNATURES = {
     "rt_decoder_load_kv": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32]),
     "rt_decoder_read_kv": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32]),
     "rt_decoder_step": (ctypes.c_int, [_vp, _i32, _i32, _vp]),
+    "rt_qwen35_create": (ctypes.c_int, [_vp, ctypes.POINTER(RtQwen35Cfg), ctypes.POINTER(RtQwen35Layer), _vp, _vp, _i32,
+                                        _pp]),
+    "rt_qwen35_destroy": (None, [_vp]),
+    "rt_qwen35_reset": (ctypes.c_int, [_vp]),
+    "rt_qwen35_step": (ctypes.c_int, [_vp, _i32, _i32, _vp]),
+    "rt_qwen35_logits_device": (ctypes.c_int, [_vp, _pp]),
     "rt_decoder_prefill": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
     "rt_decoder_prefill_gemm": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
     "rt_decoder_step_batch": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp]),
