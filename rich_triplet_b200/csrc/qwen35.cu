@@ -52,8 +52,11 @@ __device__ __forceinline__ float qblock_sum(float v, float* red) {
     return v;
 }
 
-// out = embed[token] as f32 (Qwen35Model::embed_token, src/transformer_qwen35.rs:1170-1181).
-__global__ void q_embed_kernel(const uint16_t* __restrict__ embed, int token, int H, float* __restrict__ x) {
+// out = embed[token] as f32 (Qwen35Model::embed_token, src/transformer_qwen35.rs:1170-1181);
+// tokpos = {token, position} of this step.
+__global__ void q_embed_kernel(const uint16_t* __restrict__ embed, const int32_t* __restrict__ tokpos, int H,
+                               float* __restrict__ x) {
+    const int token = tokpos[0];
     for (int c = threadIdx.x; c < H; c += blockDim.x)
         x[c] = rt::bf16_bits_to_f32(embed[static_cast<int64_t>(token) * H + c]);
 }
@@ -196,7 +199,8 @@ struct FaArgs {
     float* vcache;
     float* q_rot;   // [nq][d]
     float* out;     // [nq][d]
-    int nq, nkv, d, rope_dim, pos;
+    const int32_t* tokpos;  // {token, position}: the position is read on the device
+    int nq, nkv, d, rope_dim;
     float eps, scale;
 };
 
@@ -207,7 +211,7 @@ struct FaArgs {
 __global__ void __launch_bounds__(kQThreads) q_fa_prep_kernel(const FaArgs a) {
     __shared__ float red[32];
     __shared__ float row[512];
-    const int hd = blockIdx.x, t = threadIdx.x, d = a.d;
+    const int hd = blockIdx.x, t = threadIdx.x, d = a.d, pos = a.tokpos[1];
     const bool is_q = hd < a.nq;
     const int h = is_q ? hd : hd - a.nq;
     const float* src = is_q ? a.qkv + static_cast<int64_t>(h) * 2 * d : a.qkv + static_cast<int64_t>(a.nq) * 2 * d + h * d;
@@ -220,35 +224,35 @@ __global__ void __launch_bounds__(kQThreads) q_fa_prep_kernel(const FaArgs a) {
     __syncthreads();
     const int half = a.rope_dim / 2;
     float* dst = is_q ? a.q_rot + static_cast<int64_t>(h) * d
-                      : a.kcache + (static_cast<int64_t>(a.pos) * a.nkv + h) * d;
+                      : a.kcache + (static_cast<int64_t>(pos) * a.nkv + h) * d;
     for (int j = t; j < d; j += kQThreads) {
         float v = row[j];
         if (j < half) {
-            const float c = a.rope_cos[static_cast<int64_t>(a.pos) * half + j];
-            const float s = a.rope_sin[static_cast<int64_t>(a.pos) * half + j];
+            const float c = a.rope_cos[static_cast<int64_t>(pos) * half + j];
+            const float s = a.rope_sin[static_cast<int64_t>(pos) * half + j];
             v = row[j] * c - row[j + half] * s;
         } else if (j < 2 * half) {
-            const float c = a.rope_cos[static_cast<int64_t>(a.pos) * half + j - half];
-            const float s = a.rope_sin[static_cast<int64_t>(a.pos) * half + j - half];
+            const float c = a.rope_cos[static_cast<int64_t>(pos) * half + j - half];
+            const float s = a.rope_sin[static_cast<int64_t>(pos) * half + j - half];
             v = row[j] * c + row[j - half] * s;
         }
         dst[j] = v;
     }
     if (!is_q) {
         const float* vs = a.qkv + static_cast<int64_t>(a.nq) * 2 * d + static_cast<int64_t>(a.nkv) * d + h * d;
-        for (int j = t; j < d; j += kQThreads) a.vcache[(static_cast<int64_t>(a.pos) * a.nkv + h) * d + j] = vs[j];
+        for (int j = t; j < d; j += kQThreads) a.vcache[(static_cast<int64_t>(pos) * a.nkv + h) * d + j] = vs[j];
     }
 }
 
 // One CTA per query head: softmax(q . K / sqrt(d)) over positions 0..pos, the
 // weighted sum of V (gqa_attention_cached, src/transformer_qwen35.rs:1814-1869),
-// times sigmoid(gate).  Scores live in dynamic shared memory (pos + 1 floats).
+// times sigmoid(gate).  Scores live in dynamic shared memory (max_tokens floats).
 __global__ void __launch_bounds__(kQThreads) q_fa_attn_kernel(const FaArgs a) {
     extern __shared__ float sc[];
     __shared__ float red[32];
     __shared__ float qv[512];
     const int h = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5, d = a.d;
-    const int kvh = h / (a.nq / a.nkv), L = a.pos + 1;
+    const int kvh = h / (a.nq / a.nkv), L = a.tokpos[1] + 1;
     for (int j = t; j < d; j += kQThreads) qv[j] = a.q_rot[static_cast<int64_t>(h) * d + j];
     __syncthreads();
     for (int p = warp; p < L; p += kQThreads / 32) {
@@ -323,6 +327,12 @@ struct rt_qwen35 {
           *hbuf = nullptr, *logits = nullptr;
     float* part = nullptr;  // LM head split-tile scratch
     uint32_t* cnt = nullptr;
+    // One step as a CUDA graph (captured at the first step); the token and the
+    // position reach it through tokpos, copied in from pinned h_tokpos.
+    int32_t* tokpos = nullptr;
+    int32_t* h_tokpos = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
 };
 
 namespace {
@@ -381,6 +391,91 @@ cudaError_t gemv(rt_qwen35* e, const QProj& p, const float* x, float* y) {
     a.y = y;
     a.err = e->ctx->d_err;
     return rt::gemv_cluster_launch(a, p.tmap, p.plan, e->ctx->stream, false);
+}
+
+}  // namespace
+
+namespace {
+
+// Enqueue one step (every kernel of it) on the context stream; the caller
+// captures it into the engine's graph.
+cudaError_t enqueue_step(rt_qwen35* e) {
+#define QCHECK(call)                      \
+    do {                                  \
+        const cudaError_t r_ = (call);    \
+        if (r_ != cudaSuccess) return r_; \
+    } while (0)
+    const rt_qwen35_cfg& c = e->cfg;
+    cudaStream_t s = e->ctx->stream;
+    const int H = e->H, nv = c.linear_num_value_heads, nq = c.num_attention_heads, D = c.head_dim;
+    const int F = c.intermediate_size;
+    q_embed_kernel<<<1, kQThreads, 0, s>>>(e->embed, e->tokpos, H, e->x);
+    QCHECK(cudaGetLastError());
+    const float* add = nullptr;  // the previous block's MLP output, added before the next norm
+    for (int l = 0; l < e->nl; ++l) {
+        rt_qwen35::Layer& L = e->layers[l];
+        q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, add, L.in_norm, c.rms_norm_eps, H, e->xn);
+        QCHECK(gemv(e, L.in, e->xn, e->big));
+        if (!L.full) {
+            q_dn_conv_kernel<<<(e->qkv_dim + 255) / 256, 256, 0, s>>>(e->big, L.conv_w, L.conv_state, e->qkv_dim,
+                                                                       c.linear_conv_kernel_dim, e->conv);
+            DnHeadArgs a;
+            a.conv = e->conv;
+            a.zab = e->big + e->qkv_dim;
+            a.a_log = L.a_log;
+            a.dt_bias = L.dt_bias;
+            a.norm_w = L.norm_w;
+            a.S = L.S;
+            a.out = e->mix;
+            a.nk = c.linear_num_key_heads;
+            a.nv = nv;
+            a.kd = c.linear_key_head_dim;
+            a.vd = c.linear_value_head_dim;
+            q_dn_heads_kernel<<<nv, kQThreads, 0, s>>>(a);
+        } else {
+            FaArgs a;
+            a.qkv = e->big;
+            a.q_norm = L.q_norm;
+            a.k_norm = L.k_norm;
+            a.rope_cos = e->rope_cos;
+            a.rope_sin = e->rope_sin;
+            a.kcache = L.kcache;
+            a.vcache = L.vcache;
+            a.q_rot = e->q_rot;
+            a.out = e->mix;
+            a.nq = nq;
+            a.nkv = c.num_key_value_heads;
+            a.d = D;
+            a.rope_dim = c.rope_dim;
+            a.tokpos = e->tokpos;
+            a.eps = c.rms_norm_eps;
+            a.scale = 1.0f / sqrtf(static_cast<float>(D));
+            q_fa_prep_kernel<<<nq + a.nkv, kQThreads, 0, s>>>(a);
+            q_fa_attn_kernel<<<nq, kQThreads, sizeof(float) * e->max_tokens, s>>>(a);
+        }
+        QCHECK(cudaGetLastError());
+        QCHECK(gemv(e, L.out, e->mix, e->y));
+        q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, e->y, L.post_norm, c.rms_norm_eps, H, e->xn);
+        QCHECK(gemv(e, L.gu, e->xn, e->big));
+        q_silu_mul_kernel<<<(F + 255) / 256, 256, 0, s>>>(e->big, F, e->hbuf);
+        QCHECK(cudaGetLastError());
+        QCHECK(gemv(e, L.down, e->hbuf, e->y));
+        add = e->y;
+    }
+    q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, add, e->final_norm, c.rms_norm_eps, H, e->xn);
+    QCHECK(cudaGetLastError());
+    rt::GemvArgs a = {};
+    a.w = reinterpret_cast<const uint8_t*>(e->embed);
+    a.rows = c.vocab_size;
+    a.K = H;
+    a.x = e->xn;
+    a.y = e->logits;
+    a.part = e->part;
+    a.tile_cnt = e->cnt;
+    a.err = e->ctx->d_err;
+    QCHECK(rt::gemv_launch(rt::kBF16, rt::kProPlain, rt::kEpiPlain, a, e->lm_tmap, e->lm_plan, s, false));
+    return cudaSuccess;
+#undef QCHECK
 }
 
 }  // namespace
@@ -479,6 +574,7 @@ int rt_qwen35_create(rt_ctx* ctx, const rt_qwen35_cfg* cfg, const rt_qwen35_laye
         (rc = qalloc(e, reinterpret_cast<void**>(&e->q_rot), sizeof(float) * nq * D, "rotated queries")) != RT_OK ||
         (rc = qalloc(e, reinterpret_cast<void**>(&e->hbuf), sizeof(float) * F, "MLP hidden")) != RT_OK ||
         (rc = qalloc(e, reinterpret_cast<void**>(&e->logits), sizeof(float) * c.vocab_size, "logits")) != RT_OK ||
+        (rc = qalloc(e, reinterpret_cast<void**>(&e->tokpos), 2 * sizeof(int32_t), "token and position")) != RT_OK ||
         (rc = qalloc(e, reinterpret_cast<void**>(&e->part), sizeof(float) * std::max<int64_t>(1, e->lm_plan.part_floats),
                      "LM-head scratch")) != RT_OK ||
         (rc = qalloc(e, reinterpret_cast<void**>(&e->cnt), sizeof(uint32_t) * std::max<int64_t>(1, e->lm_plan.cnt_words),
@@ -487,6 +583,8 @@ int rt_qwen35_create(rt_ctx* ctx, const rt_qwen35_cfg* cfg, const rt_qwen35_laye
     if (cudaMemset(e->cnt, 0, sizeof(uint32_t) * std::max<int64_t>(1, e->lm_plan.cnt_words)) != cudaSuccess ||
         cudaFuncSetAttribute(q_fa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) != cudaSuccess)
         return bail(fail(ctx, RT_E_CUDA, "rt_qwen35_create: set-up"));
+    if (cudaMallocHost(reinterpret_cast<void**>(&e->h_tokpos), 2 * sizeof(int32_t)) != cudaSuccess)
+        return bail(fail(ctx, RT_E_NOMEM, "rt_qwen35_create: pinned token buffer"));
     if ((rc = rt_qwen35_reset(e)) != RT_OK) return bail(rc);
     *out = e;
     return RT_OK;
@@ -494,6 +592,9 @@ int rt_qwen35_create(rt_ctx* ctx, const rt_qwen35_cfg* cfg, const rt_qwen35_laye
 
 void rt_qwen35_destroy(rt_qwen35* e) {
     if (!e) return;
+    if (e->exec) cudaGraphExecDestroy(e->exec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    if (e->h_tokpos) cudaFreeHost(e->h_tokpos);
     for (void* p : e->allocs) cudaFree(p);
     delete e;
 }
@@ -525,76 +626,26 @@ int rt_qwen35_step(rt_qwen35* e, int32_t token, int32_t position, float* logits)
         return fail(ctx, RT_E_STATE, "rt_qwen35_step: position %d outside the %d-token cache", position, e->max_tokens);
     RT_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
     cudaStream_t s = ctx->stream;
-    const int H = e->H, nv = c.linear_num_value_heads, nq = c.num_attention_heads, D = c.head_dim;
-    const int F = c.intermediate_size;
-    q_embed_kernel<<<1, kQThreads, 0, s>>>(e->embed, token, H, e->x);
-    RT_CHECK_CUDA(ctx, cudaGetLastError());
-    const float* add = nullptr;  // the previous block's MLP output, added before the next norm
-    for (int l = 0; l < e->nl; ++l) {
-        rt_qwen35::Layer& L = e->layers[l];
-        q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, add, L.in_norm, c.rms_norm_eps, H, e->xn);
-        RT_CHECK_CUDA(ctx, gemv(e, L.in, e->xn, e->big));
-        if (!L.full) {
-            q_dn_conv_kernel<<<(e->qkv_dim + 255) / 256, 256, 0, s>>>(e->big, L.conv_w, L.conv_state, e->qkv_dim,
-                                                                       c.linear_conv_kernel_dim, e->conv);
-            DnHeadArgs a;
-            a.conv = e->conv;
-            a.zab = e->big + e->qkv_dim;
-            a.a_log = L.a_log;
-            a.dt_bias = L.dt_bias;
-            a.norm_w = L.norm_w;
-            a.S = L.S;
-            a.out = e->mix;
-            a.nk = c.linear_num_key_heads;
-            a.nv = nv;
-            a.kd = c.linear_key_head_dim;
-            a.vd = c.linear_value_head_dim;
-            q_dn_heads_kernel<<<nv, kQThreads, 0, s>>>(a);
-        } else {
-            FaArgs a;
-            a.qkv = e->big;
-            a.q_norm = L.q_norm;
-            a.k_norm = L.k_norm;
-            a.rope_cos = e->rope_cos;
-            a.rope_sin = e->rope_sin;
-            a.kcache = L.kcache;
-            a.vcache = L.vcache;
-            a.q_rot = e->q_rot;
-            a.out = e->mix;
-            a.nq = nq;
-            a.nkv = c.num_key_value_heads;
-            a.d = D;
-            a.rope_dim = c.rope_dim;
-            a.pos = position;
-            a.eps = c.rms_norm_eps;
-            a.scale = 1.0f / sqrtf(static_cast<float>(D));
-            q_fa_prep_kernel<<<nq + a.nkv, kQThreads, 0, s>>>(a);
-            q_fa_attn_kernel<<<nq, kQThreads, sizeof(float) * (position + 1), s>>>(a);
+    e->h_tokpos[0] = token;
+    e->h_tokpos[1] = position;
+    RT_CHECK_CUDA(ctx, cudaMemcpyAsync(e->tokpos, e->h_tokpos, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    if (!e->exec) {
+        RT_CHECK_CUDA(ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        const cudaError_t ce = enqueue_step(e);
+        cudaGraph_t g = nullptr;
+        const cudaError_t ee = cudaStreamEndCapture(s, &g);
+        if (ce != cudaSuccess || ee != cudaSuccess || !g) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            return fail(ctx, RT_E_CUDA, "rt_qwen35_step: capture: %s", cudaGetErrorString(ce != cudaSuccess ? ce : ee));
         }
-        RT_CHECK_CUDA(ctx, cudaGetLastError());
-        RT_CHECK_CUDA(ctx, gemv(e, L.out, e->mix, e->y));
-        q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, e->y, L.post_norm, c.rms_norm_eps, H, e->xn);
-        RT_CHECK_CUDA(ctx, gemv(e, L.gu, e->xn, e->big));
-        q_silu_mul_kernel<<<(F + 255) / 256, 256, 0, s>>>(e->big, F, e->hbuf);
-        RT_CHECK_CUDA(ctx, cudaGetLastError());
-        RT_CHECK_CUDA(ctx, gemv(e, L.down, e->hbuf, e->y));
-        add = e->y;
+        e->graph = g;
+        RT_CHECK_CUDA(ctx, cudaGraphInstantiate(&e->exec, g, 0));
     }
-    q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, add, e->final_norm, c.rms_norm_eps, H, e->xn);
-    RT_CHECK_CUDA(ctx, cudaGetLastError());
-    rt::GemvArgs a = {};
-    a.w = reinterpret_cast<const uint8_t*>(e->embed);
-    a.rows = c.vocab_size;
-    a.K = H;
-    a.x = e->xn;
-    a.y = e->logits;
-    a.part = e->part;
-    a.tile_cnt = e->cnt;
-    a.err = ctx->d_err;
-    RT_CHECK_CUDA(ctx, rt::gemv_launch(rt::kBF16, rt::kProPlain, rt::kEpiPlain, a, e->lm_tmap, e->lm_plan, s, false));
+    RT_CHECK_CUDA(ctx, cudaGraphLaunch(e->exec, s));
     if (logits)
         RT_CHECK_CUDA(ctx, cudaMemcpyAsync(logits, e->logits, sizeof(float) * c.vocab_size, cudaMemcpyDeviceToHost, s));
-    return rt_sync(ctx);
+    return rt_sync(ctx);  // also keeps h_tokpos untouched until its copy is done
 }
 
 int rt_qwen35_logits_device(rt_qwen35* e, const float** out) {
