@@ -44,6 +44,7 @@ def parse():
     p.add_argument("--layers", type=int, default=34, help="model depth (34 = Gemma 3 4B)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-config4", action="store_true", help="skip the 27B tensor-parallel section")
+    p.add_argument("--no-qwen35", action="store_true", help="skip the Qwen 3.5 decode section")
     p.add_argument("--tp-allreduce", default="nccl", choices=["peer", "nccl"],
                    help="config 4's per-layer sums: peer all-reduce kernel over NVLink, or NCCL")
     p.add_argument("--cpu-steps", type=int, default=10)
@@ -408,6 +409,47 @@ def tp_decode_config4(args, world, rank, dist, device, hbm_peak):
     return out
 
 
+def qwen35_decode(args, device, hbm_peak):
+    """The Qwen 3.5 decode engine (rt_qwen35_*, the reference's
+    MetalDecodeContextQwen35): the 4B widths (32 layers, 24 Gated DeltaNet +
+    8 full attention, vocabulary 248320) on synthetic weights, greedy-free
+    steps at positions 8..39 after 8 warm-up steps, CUDA events around them.
+    Bytes per step: every Q4_K projection, the BF16 LM head, each DeltaNet
+    state read and written, the K/V rows attended."""
+    import torch
+
+    from rich_triplet_b200.qwen35 import CudaQwen35Decoder, Qwen35Config, synth_qwen35
+
+    cfg = Qwen35Config.qwen35_4b()
+    w = synth_qwen35(cfg, seed=args.seed)
+    dec = CudaQwen35Decoder(w, 1024)
+    try:
+        warm, n = 8, 32
+        for p in range(warm):
+            dec.step_device((p * 7919) % cfg.vocab_size, p)
+        ext = torch.cuda.ExternalStream(dec.ctx.stream_ptr)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        for p in range(warm, warm + n):
+            dec.step_device((p * 7919) % cfg.vocab_size, p)
+        e1.record(ext)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / n
+    finally:
+        dec.close()
+        dec.ctx.close()
+    q4k = sum(b.size for L in w.layers for b in L.proj.values())
+    n_dn = sum(1 for L in w.layers if not L.full)
+    state = n_dn * cfg.linear_num_value_heads * cfg.linear_key_head_dim * cfg.linear_value_head_dim * 4 * 2
+    kv = (cfg.num_hidden_layers - n_dn) * (warm + n / 2) * cfg.num_key_value_heads * cfg.head_dim * 4 * 2
+    step_bytes = q4k + cfg.vocab_size * cfg.hidden_size * 2 + state + kv
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    return {"model": "Qwen 3.5 4B widths (32 layers: 24 Gated DeltaNet, 8 full attention), synthetic Q4_K weights",
+            "value": 1e3 / ms, "unit": "tok/s", "ms_per_step": ms, "positions": [warm, warm + n],
+            "bytes_per_step": step_bytes, "hbm_gbs": gbs, "frac": gbs / hbm_peak,
+            "method": "one CUDA graph launch per step (rt_qwen35_step), host sync per step, CUDA events around 32 steps"}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -518,6 +560,14 @@ def run_ours(args):
 
     # ---- Gemma 3 27B tensor parallel over the ranks ----
     tp4 = tp_decode_config4(args, world, rank, dist, device, hbm_peak) if not args.no_config4 else None
+
+    # ---- the Qwen 3.5 decode engine (one GPU: a single-sequence engine) ----
+    qwen = None
+    if world == 1 and not args.no_qwen35:
+        try:
+            qwen = qwen35_decode(args, device, hbm_peak)
+        except Exception as e:  # reported in the line
+            qwen = {"error": f"{type(e).__name__}: {e}"}
 
     # ---- standalone Q4_K GEMV, CUDA graph of 256 chained
     # launches rotating over 16 weight copies (236 MB > L2) ----
@@ -639,6 +689,7 @@ def run_ours(args):
             "batch_decode_config3": batch3,
             "prefill_config1": prefill,
             "tp_decode_config4": tp4,
+            "qwen35_decode": qwen,
         }
         print(json.dumps(line), flush=True)
     dec.close()
