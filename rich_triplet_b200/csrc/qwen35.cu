@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(kQThreads) q_resid_norm_kernel(float* __restri
                                                                  const float* __restrict__ gamma, float eps, int H,
                                                                  float* __restrict__ xn) {
     __shared__ float red[32];
+    rt::pdl_launch_dependents();  // the next GEMV may start streaming its weights now
     float ss = 0.f;
     for (int c = threadIdx.x; c < H; c += blockDim.x) {
         float v = x[c];
@@ -116,6 +117,7 @@ constexpr int kDnMaxRows = 64;
 
 __global__ void __launch_bounds__(kQThreads) q_dn_heads_kernel(const DnHeadArgs a) {
     __shared__ float red[32];
+    rt::pdl_launch_dependents();
     __shared__ float qs[256], ks[256];  // this head's q (scaled) and k, kd <= 256
     __shared__ float part[kQThreads];
     __shared__ float col[256];          // kv_mem, then the output column values
@@ -250,6 +252,7 @@ __global__ void __launch_bounds__(kQThreads) q_fa_prep_kernel(const FaArgs a) {
 __global__ void __launch_bounds__(kQThreads) q_fa_attn_kernel(const FaArgs a) {
     extern __shared__ float sc[];
     __shared__ float red[32];
+    rt::pdl_launch_dependents();
     __shared__ float qv[512];
     const int h = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5, d = a.d;
     const int kvh = h / (a.nq / a.nkv), L = a.tokpos[1] + 1;
@@ -285,6 +288,7 @@ __global__ void __launch_bounds__(kQThreads) q_fa_attn_kernel(const FaArgs a) {
 
 // h[j] = silu(gate[j]) * up[j] from [gate (F) | up (F)] (Qwen35Mlp::forward, :864-869).
 __global__ void q_silu_mul_kernel(const float* __restrict__ gu, int F, float* __restrict__ out) {
+    rt::pdl_launch_dependents();
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < F; j += gridDim.x * blockDim.x)
         out[j] = silu_f(gu[j]) * gu[F + j];
 }
@@ -390,7 +394,10 @@ cudaError_t gemv(rt_qwen35* e, const QProj& p, const float* x, float* y) {
     a.x = x;
     a.y = y;
     a.err = e->ctx->d_err;
-    return rt::gemv_cluster_launch(a, p.tmap, p.plan, e->ctx->stream, false);
+    // programmatic dependent launch: the GEMV's CTAs start, and copy their
+    // weights, while the kernel before it (which triggers at entry) runs; they
+    // read its output only after griddepcontrol.wait
+    return rt::gemv_cluster_launch(a, p.tmap, p.plan, e->ctx->stream, true);
 }
 
 }  // namespace
@@ -473,7 +480,7 @@ cudaError_t enqueue_step(rt_qwen35* e) {
     a.part = e->part;
     a.tile_cnt = e->cnt;
     a.err = e->ctx->d_err;
-    QCHECK(rt::gemv_launch(rt::kBF16, rt::kProPlain, rt::kEpiPlain, a, e->lm_tmap, e->lm_plan, s, false));
+    QCHECK(rt::gemv_launch(rt::kBF16, rt::kProPlain, rt::kEpiPlain, a, e->lm_tmap, e->lm_plan, s, true));
     return cudaSuccess;
 #undef QCHECK
 }
