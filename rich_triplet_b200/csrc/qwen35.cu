@@ -40,12 +40,13 @@ using rt::fail;
 namespace {
 
 constexpr int kQThreads = 256;
+constexpr int kQWide = 1024;  // threads of the row-norm and DeltaNet head kernels (short per-thread chains)
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : logf(1.0f + expf(x)); }
 
-// Sum of v over the block (kQThreads threads), the same value in every thread.
+// Sum of v over the block (up to 1024 threads), the same value in every thread.
 __device__ __forceinline__ float qblock_sum(float v, float* red) {
     v = rt::block_sum(v, red);
     __syncthreads();  // red is reused by the next reduction
@@ -63,7 +64,7 @@ __global__ void q_embed_kernel(const uint16_t* __restrict__ embed, const int32_t
 
 // x += add (if any); xn = x / sqrt(mean(x^2) + eps) * (1 + gamma)
 // (RmsNorm2::forward_gemma3, the zero-centred variant the blocks use).
-__global__ void __launch_bounds__(kQThreads) q_resid_norm_kernel(float* __restrict__ x, const float* __restrict__ add,
+__global__ void __launch_bounds__(kQWide) q_resid_norm_kernel(float* __restrict__ x, const float* __restrict__ add,
                                                                  const float* __restrict__ gamma, float eps, int H,
                                                                  float* __restrict__ xn) {
     __shared__ float red[32];
@@ -110,26 +111,27 @@ struct DnHeadArgs {
     int nk, nv, kd, vd;
 };
 
-// One CTA per value head h (src/transformer_qwen35.rs:339-453).  Thread t owns
-// column j = t % vd of the head's state and rows i = p, p + P, ... (P = 256 / vd
-// row groups, p = t / vd), at most kMaxRows of them, in registers.
-constexpr int kDnMaxRows = 64;
+// One CTA of kQWide threads per value head h (src/transformer_qwen35.rs:339-453).
+// Thread t owns column j = t % vd of the head's state and rows i = p, p + P,
+// ... (P = kQWide / vd row groups, p = t / vd), at most kDnMaxRows of them, in
+// registers.
+constexpr int kDnMaxRows = 16;
 
-__global__ void __launch_bounds__(kQThreads) q_dn_heads_kernel(const DnHeadArgs a) {
+__global__ void __launch_bounds__(kQWide) q_dn_heads_kernel(const DnHeadArgs a) {
     __shared__ float red[32];
     rt::pdl_launch_dependents();
     __shared__ float qs[256], ks[256];  // this head's q (scaled) and k, kd <= 256
-    __shared__ float part[kQThreads];
+    __shared__ float part[kQWide];
     __shared__ float col[256];          // kv_mem, then the output column values
     const int h = blockIdx.x, t = threadIdx.x;
-    const int kd = a.kd, vd = a.vd, P = kQThreads / vd;
+    const int kd = a.kd, vd = a.vd, P = kQWide / vd;
     const int g = h / (a.nv / a.nk);  // key head of this value head
     const float* q = a.conv + g * kd;
     const float* k = a.conv + a.nk * kd + g * kd;
     const float* v = a.conv + 2 * a.nk * kd + h * vd;
     // l2_normalize_heads (src/transformer_qwen35.rs:1756-1766), then q / sqrt(kd)
     float sq = 0.f, sk = 0.f;
-    for (int i = t; i < kd; i += kQThreads) {
+    for (int i = t; i < kd; i += kQWide) {
         sq += q[i] * q[i];
         sk += k[i] * k[i];
     }
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(kQThreads) q_dn_heads_kernel(const DnHeadArgs 
     sk = qblock_sum(sk, red);
     const float nq = fmaxf(sqrtf(sq), 1e-12f), nk = fmaxf(sqrtf(sk), 1e-12f);
     const float qscale = 1.0f / sqrtf(static_cast<float>(kd));
-    for (int i = t; i < kd; i += kQThreads) {
+    for (int i = t; i < kd; i += kQWide) {
         qs[i] = (q[i] / nq) * qscale;
         ks[i] = k[i] / nk;
     }
@@ -421,7 +423,7 @@ cudaError_t enqueue_step(rt_qwen35* e) {
     const float* add = nullptr;  // the previous block's MLP output, added before the next norm
     for (int l = 0; l < e->nl; ++l) {
         rt_qwen35::Layer& L = e->layers[l];
-        q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, add, L.in_norm, c.rms_norm_eps, H, e->xn);
+        q_resid_norm_kernel<<<1, kQWide, 0, s>>>(e->x, add, L.in_norm, c.rms_norm_eps, H, e->xn);
         QCHECK(gemv(e, L.in, e->xn, e->big));
         if (!L.full) {
             q_dn_conv_kernel<<<(e->qkv_dim + 255) / 256, 256, 0, s>>>(e->big, L.conv_w, L.conv_state, e->qkv_dim,
@@ -438,7 +440,7 @@ cudaError_t enqueue_step(rt_qwen35* e) {
             a.nv = nv;
             a.kd = c.linear_key_head_dim;
             a.vd = c.linear_value_head_dim;
-            q_dn_heads_kernel<<<nv, kQThreads, 0, s>>>(a);
+            q_dn_heads_kernel<<<nv, kQWide, 0, s>>>(a);
         } else {
             FaArgs a;
             a.qkv = e->big;
@@ -462,14 +464,14 @@ cudaError_t enqueue_step(rt_qwen35* e) {
         }
         QCHECK(cudaGetLastError());
         QCHECK(gemv(e, L.out, e->mix, e->y));
-        q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, e->y, L.post_norm, c.rms_norm_eps, H, e->xn);
+        q_resid_norm_kernel<<<1, kQWide, 0, s>>>(e->x, e->y, L.post_norm, c.rms_norm_eps, H, e->xn);
         QCHECK(gemv(e, L.gu, e->xn, e->big));
         q_silu_mul_kernel<<<(F + 255) / 256, 256, 0, s>>>(e->big, F, e->hbuf);
         QCHECK(cudaGetLastError());
         QCHECK(gemv(e, L.down, e->hbuf, e->y));
         add = e->y;
     }
-    q_resid_norm_kernel<<<1, kQThreads, 0, s>>>(e->x, add, e->final_norm, c.rms_norm_eps, H, e->xn);
+    q_resid_norm_kernel<<<1, kQWide, 0, s>>>(e->x, add, e->final_norm, c.rms_norm_eps, H, e->xn);
     QCHECK(cudaGetLastError());
     rt::GemvArgs a = {};
     a.w = reinterpret_cast<const uint8_t*>(e->embed);
@@ -498,7 +500,7 @@ int rt_qwen35_create(rt_ctx* ctx, const rt_qwen35_cfg* cfg, const rt_qwen35_laye
     const int kd = c.linear_key_head_dim, vd = c.linear_value_head_dim, KS = c.linear_conv_kernel_dim;
     const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, D = c.head_dim, F = c.intermediate_size;
     if (H <= 0 || H % 256 || F % 256 || c.num_hidden_layers <= 0 || nk <= 0 || nv % nk || kd > 256 || vd <= 0 ||
-        256 % vd || kd > kDnMaxRows * (256 / vd) || KS < 1 || nq <= 0 || nkv <= 0 || nq % nkv || D > 512 ||
+        vd > 256 || kQWide % vd || kd > kDnMaxRows * (kQWide / vd) || KS < 1 || nq <= 0 || nkv <= 0 || nq % nkv || D > 512 ||
         (nq * D) % 256 || (nv * vd) % 256 || c.rope_dim % 2 || c.rope_dim > D || c.full_attention_interval <= 0 ||
         max_tokens <= 0 || max_tokens > 40000 || c.vocab_size <= 0)
         return fail(ctx, RT_E_SHAPE, "rt_qwen35_create: unsupported configuration");
